@@ -1,0 +1,171 @@
+/*
+ * dwa.h - C ABI of libdwa.so, the B200 (sm_100a) implementation of the DWA
+ * (dynamic weight assembly) retrieval + assembly hot path of theorionic/matrix.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (passed as void*, a cudaStream_t), enqueues its work on that stream and
+ * returns without synchronising.  No entry point allocates device memory:
+ * scratch space is the caller's `workspace`, sized by the matching
+ * *_workspace_bytes() query.  Buffers are owned by the caller and are not
+ * retained after the call returns.
+ *
+ * Return value: DWA_OK (0) or a negative DWA_ERR_* code; dwa_last_error()
+ * gives the message of the last failure on the calling thread.  Errors found
+ * on the device (a row index outside the pool, a wait that ran out) are
+ * recorded in a status word inside the workspace; dwa_workspace_status() reads
+ * it (that call synchronises the stream).
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   dwa_assemble_fwd   src/dwa/assembly_pallas.py:193-222  pallas_assemble (primal)
+ *                      src/dwa/assembly_pallas.py:139-181  _pallas_assemble_forward
+ *                      src/dwa/assembly_pallas.py:42-75    assemble_jax (same values)
+ *                      src/dwa/model.py:184-195            pool gather (row_index form)
+ *   dwa_assemble_bwd   src/dwa/assembly_pallas.py:246-329  _pallas_assemble_bwd
+ *   dwa_retrieve       src/dwa/retrieval.py:48-159         MultiAspectRetrieval.__call__
+ */
+#ifndef DWA_H_
+#define DWA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DWA_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define DWA_API __attribute__((visibility("default")))
+#else
+#define DWA_API
+#endif
+
+/* status codes */
+#define DWA_OK                0
+#define DWA_ERR_INVALID_ARG  -1   /* a size, dtype or pointer argument is invalid */
+#define DWA_ERR_UNSUPPORTED  -2   /* valid but not supported by this build       */
+#define DWA_ERR_CUDA         -3   /* a CUDA runtime / driver call failed          */
+#define DWA_ERR_WORKSPACE    -4   /* workspace missing, too small or misaligned   */
+#define DWA_ERR_DEVICE       -5   /* the device status word reports an error      */
+
+/* element types */
+#define DWA_F32   0
+#define DWA_BF16  1
+
+/* bits of the device status word */
+#define DWA_STATUS_BAD_ROW_INDEX   0x1u  /* a row index outside [0, n_rows)            */
+#define DWA_STATUS_WAIT_TIMEOUT    0x2u  /* a bounded device wait gave up              */
+#define DWA_STATUS_BAD_LIST        0x4u  /* list offsets not monotone / out of range   */
+#define DWA_STATUS_LIST_OVERFLOW   0x8u  /* a probed list longer than max_list         */
+#define DWA_STATUS_FEW_CANDIDATES  0x10u /* fewer candidates than k (tail padded, a=0)  */
+
+/* Shape of one assembly call.  h_A is [B,T,d_A], pool rows are [.., D] with the
+ * reference layout [U (d_B x r) | V (r x d_A) | b (d_B) | pad]
+ * (src/dwa/config.py:159-165).  The reference requires d_A == d_B. */
+typedef struct DwaAssembleDims {
+    int32_t B, T, k, D, d_A, d_B, r;
+    int32_t act_dtype;   /* DWA_F32 or DWA_BF16: h_A, h_mid, g_hmid, g_hA, W_act */
+    int32_t rows_dtype;  /* DWA_F32 or DWA_BF16: element type of `rows`          */
+    int32_t reserved;
+    int64_t n_rows;      /* rows in `rows` when row_index != NULL (bounds check) */
+} DwaAssembleDims;
+
+/* Shape of one retrieval call (src/dwa/retrieval.py:48-159). */
+typedef struct DwaRetrieveDims {
+    int32_t B, S, d_k, d_A;
+    int32_t C;           /* number of lists (centroids); ignored when use_ivf == 0 */
+    int32_t m;           /* lists probed per query (min(m, C) is used)              */
+    int32_t k;           /* k_max: vectors selected per query                       */
+    int32_t max_list;    /* rows in the longest list (bounds candidate scratch)     */
+    int64_t N;           /* pool rows                                               */
+    float   T;           /* temperature                                             */
+    int32_t z_dtype;     /* DWA_F32 or DWA_BF16                                     */
+} DwaRetrieveDims;
+
+DWA_API const char* dwa_version(void);
+DWA_API int         dwa_abi_version(void);
+DWA_API const char* dwa_status_string(int status);
+/* Copies the last error message of this thread into buf (NUL-terminated);
+ * returns the message length. */
+DWA_API int         dwa_last_error(char* buf, size_t buf_bytes);
+
+/* Kernels launched by this library since it was loaded (all threads and
+ * devices): total, and how many GEMMs ran on the tensor cores (tcgen05) or on
+ * the CUDA cores (fp32 path and shapes TMA cannot address).  No reference
+ * counterpart; used to count launches inside a timed region. */
+DWA_API void dwa_launch_counters(uint64_t* total, uint64_t* tensor_core_gemms, uint64_t* simt_gemms);
+
+/* Reads and (if clear != 0) clears the device status word stored in a
+ * workspace used by any entry point.  Synchronises `stream`. */
+DWA_API int dwa_workspace_status(void* stream, void* workspace, uint32_t* status, int clear);
+
+/* ---------------------------------------------------------------------------
+ * Assembly forward.  Replaces pallas_assemble's primal
+ * (src/dwa/assembly_pallas.py:193-222, kernel :85-132, pre-factoring :139-181):
+ *   W[b]     = W_base + sum_k alpha[b,k] * U_k V_k          (fp32, [B,d_B,d_A])
+ *   h_mid[b] = h_A[b] + gamma * h_A[b] W[b]^T + b_base + sum_k alpha[b,k] b_k
+ * `rows`: either the gathered rows [B,k,D] (row_index == NULL, as the reference
+ * receives them) or the whole pool [n_rows, D] with row_index [B,k] int32
+ * selecting each (b,k) row (the gather of src/dwa/model.py:184-195 fused in).
+ * alphas [B,k] f32; W_base [d_B,d_A] f32; b_base [d_B] f32; gamma: 1 f32 on
+ * the device.  Outputs: h_mid [B,T,d_B] (act_dtype); W_out [B,d_B,d_A] f32 or
+ * NULL; W_act [B,d_B,d_A] in act_dtype or NULL (the backward's residual; for
+ * act_dtype == DWA_F32 it may be the same buffer as W_out).
+ * ------------------------------------------------------------------------- */
+DWA_API size_t dwa_assemble_workspace_bytes(const DwaAssembleDims* dims, int with_backward);
+
+DWA_API int dwa_assemble_fwd(void* stream, const DwaAssembleDims* dims,
+                     const void* rows, const int32_t* row_index,
+                     const float* alphas, const void* h_A,
+                     const float* W_base, const float* b_base, const float* gamma,
+                     void* h_mid, float* W_out, void* W_act,
+                     void* workspace, size_t workspace_bytes);
+
+/* ---------------------------------------------------------------------------
+ * Assembly backward.  Replaces _pallas_assemble_bwd
+ * (src/dwa/assembly_pallas.py:246-329) for the residuals
+ * (rows/row_index, alphas, h_A, W, gamma) and cotangents (g_hmid, g_W_out).
+ * W_act: the assembled W in act_dtype (the forward's W_act output).
+ * g_W_out [B,d_B,d_A] f32 may be NULL (zero cotangent of W).
+ * Outputs (all written in full):
+ *   g_rows [B,k,D] f32   gradient of the gathered rows (pad columns zero)
+ *   g_alpha [B,k] f32, g_hA [B,T,d_A] act_dtype, g_W_base [d_B,d_A] f32,
+ *   g_b_base [d_B] f32, g_gamma [1] f32.
+ * ------------------------------------------------------------------------- */
+DWA_API int dwa_assemble_bwd(void* stream, const DwaAssembleDims* dims,
+                     const void* rows, const int32_t* row_index,
+                     const float* alphas, const void* h_A, const void* W_act,
+                     const float* gamma, const void* g_hmid, const float* g_W_out,
+                     float* g_rows, float* g_alpha, void* g_hA, float* g_W_base,
+                     float* g_b_base, float* g_gamma,
+                     void* workspace, size_t workspace_bytes);
+
+/* ---------------------------------------------------------------------------
+ * Retrieval.  Replaces MultiAspectRetrieval.__call__ (src/dwa/retrieval.py:48-159)
+ * on one device.  Parameters: W_Q [S,d_k,d_A] f32, aspect_weights [S] f32,
+ * tau [1] f32, centroids [S,C,d_k] f32 (IVF only); list_offsets [C+1] int64
+ * CSR row ranges of the lists (list c = rows [off[c], off[c+1]); the
+ * reference's equal lists are off[c] = c*N/C); pool_keys [S,N,d_k] f32;
+ * z [B,d_A] (z_dtype); lambda_val [1] f32 on the device.
+ * use_ivf != 0: coarse scoring + top-m lists + fine scoring of the probed
+ * lists (retrieval.py:81-119); use_ivf == 0: full search (:121-138).
+ * is_warmup != 0: top-k of s_i + softmax (:143-147); else sigmoid-gated
+ * selection (:149-156).  Ties between equal scores go to the lower pool row.
+ * Outputs: alphas [B,k] f32, indices [B,k] int32 (pool rows, ordered by
+ * descending score), soft_full [B,N] f32 = softmax(s_full / T) or NULL.
+ * ------------------------------------------------------------------------- */
+DWA_API size_t dwa_retrieve_workspace_bytes(const DwaRetrieveDims* dims, int use_ivf,
+                                    int want_soft_full);
+
+DWA_API int dwa_retrieve(void* stream, const DwaRetrieveDims* dims, int use_ivf, int is_warmup,
+                 const float* lambda_val, const void* z, const float* W_Q,
+                 const float* aspect_weights, const float* tau, const float* centroids,
+                 const int64_t* list_offsets, const float* pool_keys,
+                 float* alphas, int32_t* indices, float* soft_full,
+                 void* workspace, size_t workspace_bytes);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DWA_H_ */

@@ -1,0 +1,112 @@
+"""ctypes binding of libdwa.so (the C ABI declared in include/dwa.h).
+
+The library is built in-tree (``matrix_b200/libdwa.so``, see ``build.py``).
+Loading fails loudly when it is missing: the hot path has no CPU fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libdwa.so")
+
+DWA_OK = 0
+DWA_F32 = 0
+DWA_BF16 = 1
+
+STATUS_BITS = {
+    0x1: "row index outside the pool",
+    0x2: "a bounded device wait ran out",
+    0x4: "list offsets not monotone or out of range",
+    0x8: "a probed list is longer than max_list",
+    0x10: "fewer candidates than k",
+}
+
+
+class DwaError(RuntimeError):
+    """An error returned by libdwa (the message is the library's last error)."""
+
+
+class AssembleDims(C.Structure):
+    _fields_ = [("B", C.c_int32), ("T", C.c_int32), ("k", C.c_int32), ("D", C.c_int32),
+                ("d_A", C.c_int32), ("d_B", C.c_int32), ("r", C.c_int32),
+                ("act_dtype", C.c_int32), ("rows_dtype", C.c_int32), ("reserved", C.c_int32),
+                ("n_rows", C.c_int64)]
+
+
+class RetrieveDims(C.Structure):
+    _fields_ = [("B", C.c_int32), ("S", C.c_int32), ("d_k", C.c_int32), ("d_A", C.c_int32),
+                ("C", C.c_int32), ("m", C.c_int32), ("k", C.c_int32), ("max_list", C.c_int32),
+                ("N", C.c_int64), ("T", C.c_float), ("z_dtype", C.c_int32)]
+
+
+_P = C.c_void_p
+_SIGNATURES = {
+    "dwa_version": (C.c_char_p, []),
+    "dwa_abi_version": (C.c_int, []),
+    "dwa_status_string": (C.c_char_p, [C.c_int]),
+    "dwa_last_error": (C.c_int, [C.c_char_p, C.c_size_t]),
+    "dwa_workspace_status": (C.c_int, [_P, _P, C.POINTER(C.c_uint32), C.c_int]),
+    "dwa_launch_counters": (None, [C.POINTER(C.c_uint64)] * 3),
+    "dwa_assemble_workspace_bytes": (C.c_size_t, [C.POINTER(AssembleDims), C.c_int]),
+    "dwa_assemble_fwd": (C.c_int, [_P, C.POINTER(AssembleDims), _P, _P, _P, _P, _P, _P, _P,
+                                   _P, _P, _P, _P, C.c_size_t]),
+    "dwa_assemble_bwd": (C.c_int, [_P, C.POINTER(AssembleDims), _P, _P, _P, _P, _P, _P, _P, _P,
+                                   _P, _P, _P, _P, _P, _P, _P, C.c_size_t]),
+    "dwa_retrieve_workspace_bytes": (C.c_size_t, [C.POINTER(RetrieveDims), C.c_int, C.c_int]),
+    "dwa_retrieve": (C.c_int, [_P, C.POINTER(RetrieveDims), C.c_int, C.c_int, _P, _P, _P, _P, _P,
+                               _P, _P, _P, _P, _P, _P, _P, C.c_size_t]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGNATURES)
+
+
+def load(path: str = LIB_PATH) -> C.CDLL:
+    """Load libdwa.so once; raise if it is missing or lacks a declared symbol."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(path):
+            raise DwaError(f"{path} is missing: build it with `python -m matrix_b200.build`")
+        lib = C.CDLL(path)
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        if lib.dwa_abi_version() != 1:
+            raise DwaError("libdwa ABI version mismatch")
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    lib = load()
+    buf = C.create_string_buffer(1024)
+    lib.dwa_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def check(rc: int, what: str) -> None:
+    if rc != DWA_OK:
+        lib = load()
+        raise DwaError(f"{what}: {lib.dwa_status_string(rc).decode()} ({rc}): {last_error()}")
+
+
+def launch_counters() -> tuple[int, int, int]:
+    lib = load()
+    t, a, b = C.c_uint64(), C.c_uint64(), C.c_uint64()
+    lib.dwa_launch_counters(C.byref(t), C.byref(a), C.byref(b))
+    return t.value, a.value, b.value
+
+
+def describe_status(bits: int) -> str:
+    return ", ".join(msg for bit, msg in STATUS_BITS.items() if bits & bit) or "ok"

@@ -1,0 +1,130 @@
+// libdwa host plumbing: version, status strings, per-thread last error,
+// device status readback, launch counters and TMA tensor-map encoding.
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "dwa_common.cuh"
+#include "tc_gemm.cuh"
+
+namespace dwa {
+
+std::atomic<uint64_t> g_launches_total{0}, g_launches_tc{0}, g_launches_simt{0};
+
+static thread_local std::string t_last_error;
+
+void set_last_error(const std::string& msg) { t_last_error = msg; }
+
+int fail(int code, const std::string& msg) {
+    set_last_error(msg);
+    return code;
+}
+
+namespace tc {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+bool tc_operand_ok(const Operand& op, int64_t mn_extent, int64_t k_extent, int box_mn) {
+    const int64_t es = 2;
+    if (reinterpret_cast<uintptr_t>(op.ptr) % 16 != 0) return false;
+    if ((op.ld * es) % 16 != 0 || (op.bstride * es) % 16 != 0) return false;
+    if (k_extent < BK) return false;
+    if (op.mn_major) {
+        if (mn_extent < 64 || op.ld < mn_extent) return false;
+    } else {
+        if (mn_extent < box_mn || op.ld < k_extent) return false;
+    }
+    return mn_extent < (int64_t(1) << 31) && k_extent < (int64_t(1) << 31);
+}
+
+bool make_operand_map(CUtensorMap* tm, const Operand& op, int64_t mn_extent, int64_t k_extent,
+                      int batch, int box_mn, std::string* why) {
+    auto enc = tensor_map_encoder();
+    if (!enc) {
+        *why = "cuTensorMapEncodeTiled unavailable";
+        return false;
+    }
+    const int64_t inner = op.mn_major ? mn_extent : k_extent;
+    const int64_t outer = op.mn_major ? k_extent : mn_extent;
+    const bool batched = op.bstride != 0;
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer),
+                          static_cast<cuuint64_t>(batched ? batch : 1)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(op.ld * 2),
+                             static_cast<cuuint64_t>(batched ? op.bstride * 2 : op.ld * 2 * outer)};
+    cuuint32_t box[3] = {64, static_cast<cuuint32_t>(op.mn_major ? 64 : box_mn), 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(op.ptr), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        char buf[160];
+        std::snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled error %d (inner %lld outer %lld ld %lld)",
+                      static_cast<int>(r), static_cast<long long>(inner),
+                      static_cast<long long>(outer), static_cast<long long>(op.ld));
+        *why = buf;
+        return false;
+    }
+    return true;
+}
+
+}  // namespace tc
+}  // namespace dwa
+
+extern "C" const char* dwa_version(void) { return "dwa-b200 0.1 (sm_100a)"; }
+
+extern "C" int dwa_abi_version(void) { return DWA_ABI_VERSION; }
+
+extern "C" const char* dwa_status_string(int status) {
+    switch (status) {
+        case DWA_OK: return "ok";
+        case DWA_ERR_INVALID_ARG: return "invalid argument";
+        case DWA_ERR_UNSUPPORTED: return "unsupported";
+        case DWA_ERR_CUDA: return "CUDA error";
+        case DWA_ERR_WORKSPACE: return "workspace error";
+        case DWA_ERR_DEVICE: return "device status error";
+        default: return "unknown status";
+    }
+}
+
+extern "C" int dwa_last_error(char* buf, size_t buf_bytes) {
+    const std::string& e = dwa::t_last_error;
+    if (buf && buf_bytes) {
+        const size_t n = e.size() < buf_bytes - 1 ? e.size() : buf_bytes - 1;
+        std::memcpy(buf, e.data(), n);
+        buf[n] = '\0';
+    }
+    return static_cast<int>(e.size());
+}
+
+extern "C" int dwa_workspace_status(void* stream, void* workspace, uint32_t* status, int clear) {
+    if (!workspace || !status) return dwa::fail(DWA_ERR_INVALID_ARG, "NULL workspace or status");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    DWA_CUDA_TRY(cudaMemcpyAsync(status, workspace, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+    DWA_CUDA_TRY(cudaStreamSynchronize(st));
+    if (clear) {
+        DWA_CUDA_TRY(cudaMemsetAsync(workspace, 0, sizeof(uint32_t), st));
+        DWA_CUDA_TRY(cudaStreamSynchronize(st));
+    }
+    return *status ? DWA_ERR_DEVICE : DWA_OK;
+}
+
+extern "C" void dwa_launch_counters(uint64_t* total, uint64_t* tensor_core_gemms,
+                                    uint64_t* simt_gemms) {
+    if (total) *total = dwa::g_launches_total.load();
+    if (tensor_core_gemms) *tensor_core_gemms = dwa::g_launches_tc.load();
+    if (simt_gemms) *simt_gemms = dwa::g_launches_simt.load();
+}

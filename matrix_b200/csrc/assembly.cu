@@ -1,0 +1,661 @@
+// DWA assembly forward and backward on B200.
+//
+// Forward (replaces src/dwa/assembly_pallas.py:139-222):
+//   prep    gather each (b,k) pool row (or read the gathered row), split it into
+//           U [d_B,r] | V [r,d_A] | b [d_B] (config.py:159-165) and write
+//             Ug[b] [d_B, k*r]   Ug[b][j][k*r+rho] = U_k[j][rho]     (K-major A)
+//             Vs[b] [k*r, d_A]   Vs[b][k*r+rho][i] = alpha_k V_k[rho][i]
+//             pb[b] [d_B]        b_base + sum_k alpha_k b_k
+//   GEMM W  W[b] = W_base + Ug[b] Vs[b]          M=d_B N=d_A K=k*r  (fp32 + act copy)
+//   GEMM y  h_mid[b] = h_A[b] + gamma h_A[b] W[b]^T + pb[b]     M=T N=d_B K=d_A
+// W is the primal's second output, so forming it costs no extra pass: the
+// apply is one GEMM against the assembled W instead of the reference's three
+// (assembly_pallas.py:113-117), and the [B,k,d_B,d_A] product of :212-221 is
+// never materialised.
+//
+// Backward (replaces assembly_pallas.py:246-329), with G[b] = g[b]^T h_A[b]:
+//   GEMM G    gW[b] = gamma G[b] + g_W_out[b]          -> act copy, += g_W_base,
+//             g_gamma += <G[b], W[b]>  (= sum g * h_A W^T, :275)
+//   GEMM gh   g_hA[b] = g[b] + gamma g[b] W[b]         (:283-285)
+//   GEMM P    g_U[b] = gW[b] Vs[b]^T   (alpha folded into Vs; :303-305)
+//   GEMM Q    Q[b] = Ug[b]^T gW[b]: g_V = alpha Q (:310-312), and
+//             g_alpha += <V_k, Q_k> = <U_k V_k, gW> (:298) without forming U_k V_k
+//   colsum    g_bias[b] = sum_t g[b];  finalize: g_alpha += <b_k, g_bias>,
+//             g_b = alpha g_bias, pad columns zero, g_b_base, g_gamma.
+#include <atomic>
+#include <cstdlib>
+#include <type_traits>
+
+#include "dwa_common.cuh"
+#include "simt_gemm.cuh"
+#include "tc_gemm.cuh"
+
+namespace dwa {
+
+extern std::atomic<uint64_t> g_launches_total, g_launches_tc, g_launches_simt;
+
+// ------------------------------------------------------------ row source ---
+struct RowSrc {
+    const void* rows;
+    const int32_t* row_index;
+    int64_t n_rows;
+    int64_t D;
+    int k;
+    int dtype;
+    // Element offset of row (b, kk), or -1 when its index is outside the pool.
+    __device__ __forceinline__ int64_t offset(int b, int kk) const {
+        int64_t r = static_cast<int64_t>(b) * k + kk;
+        if (row_index) {
+            const int64_t i = row_index[r];
+            if (i < 0 || i >= n_rows) return -1;
+            r = i;
+        }
+        return r * D;
+    }
+};
+
+// ------------------------------------------------------- vector helpers ----
+__device__ __forceinline__ void load32(const float* p, float* v) {
+    const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 t = q[i];
+        v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+    }
+}
+__device__ __forceinline__ void load32(const __nv_bfloat16* p, float* v) {
+    const uint4* q = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint4 t = q[i];
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&t);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 f = __bfloat1622float2(h[j]);
+            v[8 * i + 2 * j] = f.x;
+            v[8 * i + 2 * j + 1] = f.y;
+        }
+    }
+}
+__device__ __forceinline__ void store32(float* p, const float* v) {
+    float4* q = reinterpret_cast<float4*>(p);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+__device__ __forceinline__ void store32(__nv_bfloat16* p, const float* v) {
+    uint4* q = reinterpret_cast<uint4*>(p);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        uint4 t;
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&t);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(v[8 * i + 2 * j], v[8 * i + 2 * j + 1]);
+        q[i] = t;
+    }
+}
+__device__ __forceinline__ void red_add4(float* p, float a, float b, float c, float d) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
+                 "f"(d)
+                 : "memory");
+}
+
+// ------------------------------------------------------------ epilogues ----
+struct NoReduce {
+    static constexpr int kReduce = 0;
+    __device__ void row_done(int, int, float) const {}
+    __device__ void cta_done(int, float) const {}
+};
+
+// W[b](j,i) = W_base(j,i) + acc   -> fp32 W_out and/or act-typed W_act
+template <class ACT>
+struct EpiW : NoReduce {
+    const float* W_base; float* W_out; ACT* W_act; int d_B, d_A; bool vec;
+    __device__ float operator()(int b, int row, int col0, const float* v, int cnt) const {
+        const int64_t o = (static_cast<int64_t>(b) * d_B + row) * d_A + col0;
+        const float* wb = W_base + static_cast<int64_t>(row) * d_A + col0;
+        if (vec && cnt == 32) {
+            float w[32];
+            load32(wb, w);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) w[i] += v[i];
+            if (W_out) store32(W_out + o, w);
+            if (W_act) store32(W_act + o, w);
+        } else {
+            for (int c = 0; c < cnt; ++c) {
+                const float w = wb[c] + v[c];
+                if (W_out) W_out[o + c] = w;
+                if (W_act) W_act[o + c] = Elem<ACT>::from_f(w);
+            }
+        }
+        return 0.f;
+    }
+};
+
+// h_mid[b](t,j) = h_A[b](t,j) + gamma acc + pb[b](j)
+template <class ACT>
+struct EpiApply : NoReduce {
+    const ACT* hA; const float* pb; const float* gamma; ACT* out; int T, d; bool vec;
+    __device__ float operator()(int b, int row, int col0, const float* v, int cnt) const {
+        const int64_t o = (static_cast<int64_t>(b) * T + row) * d + col0;
+        const float* p = pb + static_cast<int64_t>(b) * d + col0;
+        const float g = __ldg(gamma);
+        if (vec && cnt == 32) {
+            float h[32], q[32];
+            load32(hA + o, h);
+            load32(p, q);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) h[i] = h[i] + g * v[i] + q[i];
+            store32(out + o, h);
+        } else {
+            for (int c = 0; c < cnt; ++c)
+                out[o + c] = Elem<ACT>::from_f(Elem<ACT>::to_f(hA[o + c]) + g * v[c] + p[c]);
+        }
+        return 0.f;
+    }
+};
+
+// gW[b](j,i) = gamma G + g_W_out; g_W_base += gW; g_gamma += G * W
+template <class ACT>
+struct EpiG {
+    static constexpr int kReduce = 2;
+    const float* gamma; const float* gWo; ACT* gW; float* gWbase; const ACT* Wact;
+    float* gamma_acc; int d_B, d_A; bool vec;
+    __device__ float operator()(int b, int row, int col0, const float* v, int cnt) const {
+        const int64_t o = (static_cast<int64_t>(b) * d_B + row) * d_A + col0;
+        const int64_t ob = static_cast<int64_t>(row) * d_A + col0;
+        const float g = __ldg(gamma);
+        float part = 0.f;
+        if (vec && cnt == 32) {
+            float w[32], x[32];
+            load32(Wact + o, w);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) part = fmaf(v[i], w[i], part);
+            if (gWo) {
+                load32(gWo + o, x);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) x[i] = fmaf(g, v[i], x[i]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) x[i] = g * v[i];
+            }
+            store32(gW + o, x);
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) red_add4(gWbase + ob + i, x[i], x[i + 1], x[i + 2], x[i + 3]);
+        } else {
+            for (int c = 0; c < cnt; ++c) {
+                part = fmaf(v[c], Elem<ACT>::to_f(Wact[o + c]), part);
+                const float x = gWo ? fmaf(g, v[c], gWo[o + c]) : g * v[c];
+                gW[o + c] = Elem<ACT>::from_f(x);
+                atomicAdd(gWbase + ob + c, x);
+            }
+        }
+        return part;
+    }
+    __device__ void row_done(int, int, float) const {}
+    __device__ void cta_done(int, float acc) const { atomicAdd(gamma_acc, acc); }
+};
+
+// g_hA[b](t,i) = g[b](t,i) + gamma acc
+template <class ACT>
+struct EpiGhA : NoReduce {
+    const ACT* g; const float* gamma; ACT* out; int T, d; bool vec;
+    __device__ float operator()(int b, int row, int col0, const float* v, int cnt) const {
+        const int64_t o = (static_cast<int64_t>(b) * T + row) * d + col0;
+        const float gm = __ldg(gamma);
+        if (vec && cnt == 32) {
+            float x[32];
+            load32(g + o, x);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) x[i] = fmaf(gm, v[i], x[i]);
+            store32(out + o, x);
+        } else {
+            for (int c = 0; c < cnt; ++c)
+                out[o + c] = Elem<ACT>::from_f(fmaf(gm, v[c], Elem<ACT>::to_f(g[o + c])));
+        }
+        return 0.f;
+    }
+};
+
+// g_U: g_rows[b][kk][j*r + rho] = acc(j, kk*r + rho)
+struct EpiP : NoReduce {
+    float* g_rows; int64_t D; int k, r;
+    __device__ float operator()(int b, int row, int col0, const float* v, int cnt) const {
+        for (int c = 0; c < cnt; ++c) {
+            const int n = col0 + c;
+            const int kk = n / r, rho = n - kk * r;
+            g_rows[(static_cast<int64_t>(b) * k + kk) * D + static_cast<int64_t>(row) * r + rho] = v[c];
+        }
+        return 0.f;
+    }
+};
+
+// g_V: g_rows[b][kk][s1 + rho*d_A + i] = alpha[b,kk] acc(kk*r+rho, i);
+// g_alpha[b,kk] += sum_i V_kk[rho][i] acc(kk*r+rho, i)
+template <class RT>
+struct EpiQ {
+    static constexpr int kReduce = 1;
+    RowSrc src; const float* alphas; float* g_rows; float* dW_acc; int64_t s1; int d_A, r; bool vec;
+    __device__ float operator()(int b, int row, int col0, const float* v, int cnt) const {
+        const int kk = row / r, rho = row - kk * r;
+        const float a = __ldg(alphas + static_cast<int64_t>(b) * src.k + kk);
+        const int64_t go = (static_cast<int64_t>(b) * src.k + kk) * src.D + s1 +
+                           static_cast<int64_t>(rho) * d_A + col0;
+        const int64_t ro = src.offset(b, kk);
+        const RT* V = ro < 0 ? nullptr
+                             : static_cast<const RT*>(src.rows) + ro + s1 +
+                                   static_cast<int64_t>(rho) * d_A + col0;
+        float part = 0.f;
+        if (vec && cnt == 32) {
+            float x[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) x[i] = a * v[i];
+            store32(g_rows + go, x);
+            if (V) {
+                load32(V, x);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) part = fmaf(x[i], v[i], part);
+            }
+        } else {
+            for (int c = 0; c < cnt; ++c) {
+                g_rows[go + c] = a * v[c];
+                if (V) part = fmaf(Elem<RT>::to_f(V[c]), v[c], part);
+            }
+        }
+        return part;
+    }
+    __device__ void row_done(int b, int row, float acc) const {
+        atomicAdd(dW_acc + static_cast<int64_t>(b) * src.k + row / r, acc);
+    }
+    __device__ void cta_done(int, float) const {}
+};
+
+// --------------------------------------------------------------- kernels ---
+template <class ACT, class RT>
+__global__ void prep_factors_kernel(RowSrc src, const float* __restrict__ alphas, int d_A, int d_B,
+                                    int r, int64_t ldu, ACT* __restrict__ Ug, ACT* __restrict__ Vs,
+                                    uint32_t* status) {
+    const int kk = blockIdx.x, b = blockIdx.y, k = src.k;
+    const int64_t off = src.offset(b, kk);
+    if (off < 0 && threadIdx.x == 0) raise_status(status, DWA_STATUS_BAD_ROW_INDEX);
+    const RT* row = off < 0 ? nullptr : static_cast<const RT*>(src.rows) + off;
+    const float a = alphas[static_cast<int64_t>(b) * k + kk];
+    ACT* ug = Ug + static_cast<int64_t>(b) * d_B * ldu + static_cast<int64_t>(kk) * r;
+    const int nU = d_B * r;
+    for (int e = threadIdx.x; e < nU; e += blockDim.x) {
+        const int j = e / r, rho = e - j * r;
+        const float u = row ? Elem<RT>::to_f(row[e]) : 0.f;
+        ug[static_cast<int64_t>(j) * ldu + rho] = Elem<ACT>::from_f(u);
+    }
+    const int64_t kr = static_cast<int64_t>(k) * r;
+    ACT* vs = Vs + (static_cast<int64_t>(b) * kr + static_cast<int64_t>(kk) * r) * d_A;
+    const int nV = r * d_A;
+    for (int e = threadIdx.x; e < nV; e += blockDim.x) {
+        const float x = row ? Elem<RT>::to_f(row[nU + e]) : 0.f;
+        vs[e] = Elem<ACT>::from_f(a * x);
+    }
+}
+
+template <class RT>
+__global__ void prep_bias_kernel(RowSrc src, const float* __restrict__ alphas,
+                                 const float* __restrict__ b_base, int64_t s2, int d_B,
+                                 float* __restrict__ pb) {
+    const int b = blockIdx.y;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= d_B) return;
+    float acc = 0.f;
+    for (int kk = 0; kk < src.k; ++kk) {
+        const int64_t off = src.offset(b, kk);
+        if (off < 0) continue;
+        acc = fmaf(alphas[static_cast<int64_t>(b) * src.k + kk],
+                   Elem<RT>::to_f(static_cast<const RT*>(src.rows)[off + s2 + j]), acc);
+    }
+    pb[static_cast<int64_t>(b) * d_B + j] = b_base[j] + acc;
+}
+
+template <class ACT>
+__global__ void colsum_kernel(const ACT* __restrict__ g, int T, int d, float* __restrict__ out) {
+    const int b = blockIdx.y;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= d) return;
+    const ACT* p = g + static_cast<int64_t>(b) * T * d + j;
+    float acc = 0.f;
+    for (int t = 0; t < T; ++t) acc += Elem<ACT>::to_f(p[static_cast<int64_t>(t) * d]);
+    out[static_cast<int64_t>(b) * d + j] = acc;
+}
+
+template <class RT>
+__global__ void finalize_kernel(RowSrc src, const float* __restrict__ alphas,
+                                const float* __restrict__ gbias, const float* __restrict__ dW_acc,
+                                const float* __restrict__ gamma_acc, int64_t s2, int d_B,
+                                float* __restrict__ g_rows, float* __restrict__ g_alpha,
+                                float* __restrict__ g_gamma) {
+    const int kk = blockIdx.x, b = blockIdx.y, k = src.k;
+    __shared__ float s_red[32];
+    const int64_t off = src.offset(b, kk);
+    const RT* bv = off < 0 ? nullptr : static_cast<const RT*>(src.rows) + off + s2;
+    const float a = alphas[static_cast<int64_t>(b) * k + kk];
+    const float* gb = gbias + static_cast<int64_t>(b) * d_B;
+    float* gr = g_rows + (static_cast<int64_t>(b) * k + kk) * src.D;
+    float dot = 0.f;
+    for (int j = threadIdx.x; j < d_B; j += blockDim.x) {
+        const float x = gb[j];
+        if (bv) dot = fmaf(Elem<RT>::to_f(bv[j]), x, dot);
+        gr[s2 + j] = a * x;
+    }
+    for (int64_t c = s2 + d_B + threadIdx.x; c < src.D; c += blockDim.x) gr[c] = 0.f;
+    dot = warp_sum(dot);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = dot;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += s_red[w];
+        g_alpha[static_cast<int64_t>(b) * k + kk] = dW_acc[static_cast<int64_t>(b) * k + kk] + t;
+        if (kk == 0 && b == 0) *g_gamma = *gamma_acc;
+    }
+}
+
+__global__ void bias_grad_kernel(const float* __restrict__ gbias, int B, int d,
+                                 float* __restrict__ g_b_base) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= d) return;
+    float acc = 0.f;
+    for (int b = 0; b < B; ++b) acc += gbias[static_cast<int64_t>(b) * d + j];
+    g_b_base[j] = acc;
+}
+
+// ------------------------------------------------------------------ host ---
+static bool force_simt() {
+    static const bool v = [] {
+        const char* e = std::getenv("DWA_GEMM");
+        return e && std::string(e) == "simt";
+    }();
+    return v;
+}
+
+template <class ACT, bool A_MN, bool B_MN, class Epi>
+static int gemm(const void* a, int64_t lda, int64_t bsa, const void* b, int64_t ldb, int64_t bsb,
+                int M, int N, int K, int batch, const Epi& epi, uint32_t* status, cudaStream_t st) {
+    if constexpr (std::is_same<ACT, __nv_bfloat16>::value) {
+      if (!force_simt()) {
+        const tc::Operand A{a, A_MN, lda, bsa}, B{b, B_MN, ldb, bsb};
+        const int64_t ctas256 = static_cast<int64_t>((M + 127) / 128) * ((N + 255) / 256) * batch;
+        if (N >= 256 && ctas256 >= 120 && tc::tc_operand_ok(A, M, K, 128) &&
+            tc::tc_operand_ok(B, N, K, 256)) {
+            ++g_launches_tc;
+            return tc::launch_gemm_bf16<256, 4, A_MN, B_MN>(A, B, M, N, K, batch, epi, status, st);
+        }
+        if (N >= 128 && tc::tc_operand_ok(A, M, K, 128) && tc::tc_operand_ok(B, N, K, 128)) {
+            ++g_launches_tc;
+            return tc::launch_gemm_bf16<128, 6, A_MN, B_MN>(A, B, M, N, K, batch, epi, status, st);
+        }
+      }
+    }
+    const simt::Operand A{a, A_MN, lda, bsa}, B{b, B_MN, ldb, bsb};
+    ++g_launches_simt;
+    return simt::launch_gemm<ACT, ACT>(A, B, M, N, K, batch, epi, st);
+}
+
+static int check_dims(const DwaAssembleDims* d) {
+    if (!d) return fail(DWA_ERR_INVALID_ARG, "dims is NULL");
+    if (d->B <= 0 || d->T <= 0 || d->k <= 0 || d->r <= 0 || d->d_A <= 0 || d->d_B <= 0)
+        return fail(DWA_ERR_INVALID_ARG, "B, T, k, r, d_A, d_B must be positive");
+    if (d->d_A != d->d_B)
+        return fail(DWA_ERR_INVALID_ARG, "d_A must equal d_B for the residual (config.py:59)");
+    const int64_t need = static_cast<int64_t>(d->d_B) * d->r + static_cast<int64_t>(d->r) * d->d_A + d->d_B;
+    if (d->D < need)
+        return fail(DWA_ERR_INVALID_ARG, "D < d_B*r + r*d_A + d_B (config.py:54-58)");
+    if ((d->act_dtype != DWA_F32 && d->act_dtype != DWA_BF16) ||
+        (d->rows_dtype != DWA_F32 && d->rows_dtype != DWA_BF16))
+        return fail(DWA_ERR_INVALID_ARG, "dtype must be DWA_F32 or DWA_BF16");
+    if (static_cast<int64_t>(d->k) * d->r > (1 << 30) || static_cast<int64_t>(d->T) > (1 << 30))
+        return fail(DWA_ERR_INVALID_ARG, "size out of range");
+    return DWA_OK;
+}
+
+struct AsmWorkspace {
+    uint32_t* status;
+    void* Ug;       // [B, d_B, ldu] act
+    void* Vs;       // [B, kr, d_A]  act
+    float* pb;      // [B, d_B]
+    void* Wact;     // [B, d_B, d_A] act (forward, when the caller passes none)
+    void* gW;       // [B, d_B, d_A] act (backward)
+    float* gbias;   // [B, d_B]
+    float* dW_acc;  // [B, k]
+    float* gamma_acc;
+    int64_t ldu;
+    size_t bytes;
+};
+
+static AsmWorkspace carve(void* base, const DwaAssembleDims& d, bool bwd) {
+    Carver c(base);
+    AsmWorkspace w{};
+    const size_t es = dtype_bytes(d.act_dtype);
+    const int64_t kr = static_cast<int64_t>(d.k) * d.r;
+    w.ldu = static_cast<int64_t>(align_up(static_cast<size_t>(kr), 8));
+    w.status = static_cast<uint32_t*>(base);
+    w.Ug = c.take<char>(static_cast<size_t>(d.B) * d.d_B * w.ldu * es);
+    w.Vs = c.take<char>(static_cast<size_t>(d.B) * kr * d.d_A * es);
+    w.pb = c.take<float>(static_cast<size_t>(d.B) * d.d_B);
+    w.Wact = c.take<char>(static_cast<size_t>(d.B) * d.d_B * d.d_A * es);
+    if (bwd) {
+        w.gW = c.take<char>(static_cast<size_t>(d.B) * d.d_B * d.d_A * es);
+        w.gbias = c.take<float>(static_cast<size_t>(d.B) * d.d_B);
+        w.dW_acc = c.take<float>(static_cast<size_t>(d.B) * d.k);
+        w.gamma_acc = c.take<float>(64);
+    }
+    w.bytes = c.bytes();
+    return w;
+}
+
+static bool vec_ok(const void* p, int64_t ld, size_t es) {
+    return p == nullptr ||
+           ((reinterpret_cast<uintptr_t>(p) % 16 == 0) && ((ld * static_cast<int64_t>(es)) % 16 == 0));
+}
+
+template <class ACT, class RT>
+static int prep(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src, const float* alphas,
+                const float* b_base, const AsmWorkspace& w, bool with_bias) {
+    dim3 g1(d.k, d.B);
+    prep_factors_kernel<ACT, RT><<<g1, 256, 0, st>>>(src, alphas, d.d_A, d.d_B, d.r, w.ldu,
+                                                     static_cast<ACT*>(w.Ug),
+                                                     static_cast<ACT*>(w.Vs), w.status);
+    DWA_LAUNCH_CHECK("prep_factors_kernel");
+    ++g_launches_total;
+    if (with_bias) {
+        const int64_t s2 = static_cast<int64_t>(d.d_B) * d.r + static_cast<int64_t>(d.r) * d.d_A;
+        dim3 g2((d.d_B + 255) / 256, d.B);
+        prep_bias_kernel<RT><<<g2, 256, 0, st>>>(src, alphas, b_base, s2, d.d_B, w.pb);
+        DWA_LAUNCH_CHECK("prep_bias_kernel");
+        ++g_launches_total;
+    }
+    return DWA_OK;
+}
+
+template <class ACT, class RT>
+static int fwd_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src,
+                    const float* alphas, const ACT* hA, const float* W_base, const float* b_base,
+                    const float* gamma, ACT* h_mid, float* W_out, ACT* W_act, const AsmWorkspace& w) {
+    int rc = prep<ACT, RT>(st, d, src, alphas, b_base, w, true);
+    if (rc) return rc;
+    const int64_t kr = static_cast<int64_t>(d.k) * d.r;
+    const size_t es = sizeof(ACT);
+    if (std::is_same<ACT, float>::value && W_act == reinterpret_cast<ACT*>(W_out)) W_act = nullptr;
+    ACT* Wop = W_act ? W_act
+                     : (std::is_same<ACT, float>::value && W_out ? reinterpret_cast<ACT*>(W_out)
+                                                                 : static_cast<ACT*>(w.Wact));
+    ACT* Wact_store = (Wop == reinterpret_cast<ACT*>(W_out)) ? nullptr : Wop;
+    const int64_t dd = static_cast<int64_t>(d.d_B) * d.d_A;
+
+    EpiW<ACT> ew;
+    ew.W_base = W_base; ew.W_out = W_out; ew.W_act = Wact_store; ew.d_B = d.d_B; ew.d_A = d.d_A;
+    ew.vec = vec_ok(W_base, d.d_A, 4) && vec_ok(W_out, d.d_A, 4) && vec_ok(Wact_store, d.d_A, es);
+    // A = Ug (M=d_B, K=kr, K-major); B = Vs (N=d_A, K=kr, MN-major)
+    rc = gemm<ACT, false, true>(w.Ug, w.ldu, static_cast<int64_t>(d.d_B) * w.ldu, w.Vs, d.d_A,
+                                kr * d.d_A, d.d_B, d.d_A, static_cast<int>(kr), d.B, ew, w.status, st);
+    if (rc) return rc;
+    ++g_launches_total;
+
+    EpiApply<ACT> ea;
+    ea.hA = hA; ea.pb = w.pb; ea.gamma = gamma; ea.out = h_mid; ea.T = d.T; ea.d = d.d_B;
+    ea.vec = vec_ok(hA, d.d_A, es) && vec_ok(h_mid, d.d_B, es) && vec_ok(w.pb, d.d_B, 4);
+    // A = h_A (M=T, K=d_A, K-major); B = W (N=d_B, K=d_A, K-major)
+    rc = gemm<ACT, false, false>(hA, d.d_A, static_cast<int64_t>(d.T) * d.d_A, Wop, d.d_A, dd, d.T,
+                                 d.d_B, d.d_A, d.B, ea, w.status, st);
+    if (rc) return rc;
+    ++g_launches_total;
+    return DWA_OK;
+}
+
+template <class ACT, class RT>
+static int bwd_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src,
+                    const float* alphas, const ACT* hA, const ACT* Wact, const float* gamma,
+                    const ACT* g, const float* gWo, float* g_rows, float* g_alpha, ACT* g_hA,
+                    float* g_W_base, float* g_b_base, float* g_gamma, const AsmWorkspace& w) {
+    const int64_t kr = static_cast<int64_t>(d.k) * d.r;
+    const int64_t dd = static_cast<int64_t>(d.d_B) * d.d_A;
+    const int64_t s1 = static_cast<int64_t>(d.d_B) * d.r;
+    const int64_t s2 = s1 + static_cast<int64_t>(d.r) * d.d_A;
+    const size_t es = sizeof(ACT);
+    DWA_CUDA_TRY(cudaMemsetAsync(g_W_base, 0, dd * sizeof(float), st));
+    DWA_CUDA_TRY(cudaMemsetAsync(w.dW_acc, 0, static_cast<size_t>(d.B) * d.k * sizeof(float), st));
+    DWA_CUDA_TRY(cudaMemsetAsync(w.gamma_acc, 0, sizeof(float), st));
+    int rc = prep<ACT, RT>(st, d, src, alphas, nullptr, w, false);
+    if (rc) return rc;
+    ACT* gW = static_cast<ACT*>(w.gW);
+
+    EpiG<ACT> eg;
+    eg.gamma = gamma; eg.gWo = gWo; eg.gW = gW; eg.gWbase = g_W_base; eg.Wact = Wact;
+    eg.gamma_acc = w.gamma_acc; eg.d_B = d.d_B; eg.d_A = d.d_A;
+    eg.vec = vec_ok(gWo, d.d_A, 4) && vec_ok(gW, d.d_A, es) && vec_ok(g_W_base, d.d_A, 4) &&
+             vec_ok(Wact, d.d_A, es);
+    // G = g^T h: A(m=j,k=t) = g[t][j] MN-major; B(n=i,k=t) = h[t][i] MN-major
+    rc = gemm<ACT, true, true>(g, d.d_B, static_cast<int64_t>(d.T) * d.d_B, hA, d.d_A,
+                               static_cast<int64_t>(d.T) * d.d_A, d.d_B, d.d_A, d.T, d.B, eg,
+                               w.status, st);
+    if (rc) return rc;
+    ++g_launches_total;
+
+    EpiGhA<ACT> eh;
+    eh.g = g; eh.gamma = gamma; eh.out = g_hA; eh.T = d.T; eh.d = d.d_A;
+    eh.vec = vec_ok(g, d.d_A, es) && vec_ok(g_hA, d.d_A, es);
+    // g W: A(m=t,k=j) = g[t][j] K-major; B(n=i,k=j) = W[j][i] MN-major
+    rc = gemm<ACT, false, true>(g, d.d_B, static_cast<int64_t>(d.T) * d.d_B, Wact, d.d_A, dd, d.T,
+                                d.d_A, d.d_B, d.B, eh, w.status, st);
+    if (rc) return rc;
+    ++g_launches_total;
+
+    EpiP ep;
+    ep.g_rows = g_rows; ep.D = d.D; ep.k = d.k; ep.r = d.r;
+    // g_U = gW Vs^T: A(m=j,k=i) = gW[j][i] K-major; B(n=kr,k=i) = Vs[n][i] K-major
+    rc = gemm<ACT, false, false>(gW, d.d_A, dd, w.Vs, d.d_A, kr * d.d_A, d.d_B,
+                                 static_cast<int>(kr), d.d_A, d.B, ep, w.status, st);
+    if (rc) return rc;
+    ++g_launches_total;
+
+    EpiQ<RT> eq;
+    eq.src = src; eq.alphas = alphas; eq.g_rows = g_rows; eq.dW_acc = w.dW_acc; eq.s1 = s1;
+    eq.d_A = d.d_A; eq.r = d.r;
+    eq.vec = vec_ok(g_rows, d.D, 4) && (s1 % 8 == 0) && (d.d_A % 8 == 0) &&
+             vec_ok(src.rows, d.D, sizeof(RT));
+    // Q = Ug^T gW: A(m=kr,k=j) = Ug[j][m] MN-major; B(n=i,k=j) = gW[j][i] MN-major
+    rc = gemm<ACT, true, true>(w.Ug, w.ldu, static_cast<int64_t>(d.d_B) * w.ldu, gW, d.d_A, dd,
+                               static_cast<int>(kr), d.d_A, d.d_B, d.B, eq, w.status, st);
+    if (rc) return rc;
+    ++g_launches_total;
+
+    dim3 gc((d.d_B + 255) / 256, d.B);
+    colsum_kernel<ACT><<<gc, 256, 0, st>>>(g, d.T, d.d_B, w.gbias);
+    DWA_LAUNCH_CHECK("colsum_kernel");
+    dim3 gf(d.k, d.B);
+    finalize_kernel<RT><<<gf, 256, 0, st>>>(src, alphas, w.gbias, w.dW_acc, w.gamma_acc, s2, d.d_B,
+                                            g_rows, g_alpha, g_gamma);
+    DWA_LAUNCH_CHECK("finalize_kernel");
+    bias_grad_kernel<<<(d.d_B + 255) / 256, 256, 0, st>>>(w.gbias, d.B, d.d_B, g_b_base);
+    DWA_LAUNCH_CHECK("bias_grad_kernel");
+    g_launches_total += 3;
+    return DWA_OK;
+}
+
+static int check_ws(void* ws, size_t have, size_t need) {
+    if (!ws) return fail(DWA_ERR_WORKSPACE, "workspace is NULL");
+    if (reinterpret_cast<uintptr_t>(ws) % 256 != 0)
+        return fail(DWA_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+    if (have < need)
+        return fail(DWA_ERR_WORKSPACE, "workspace too small: need " + std::to_string(need) +
+                                           " bytes, got " + std::to_string(have));
+    return DWA_OK;
+}
+
+}  // namespace dwa
+
+using namespace dwa;
+
+extern "C" size_t dwa_assemble_workspace_bytes(const DwaAssembleDims* dims, int with_backward) {
+    if (check_dims(dims)) return 0;
+    return carve(nullptr, *dims, with_backward != 0).bytes;
+}
+
+extern "C" int dwa_assemble_fwd(void* stream, const DwaAssembleDims* dims, const void* rows,
+                                const int32_t* row_index, const float* alphas, const void* h_A,
+                                const float* W_base, const float* b_base, const float* gamma,
+                                void* h_mid, float* W_out, void* W_act, void* workspace,
+                                size_t workspace_bytes) {
+    int rc = check_dims(dims);
+    if (rc) return rc;
+    const DwaAssembleDims& d = *dims;
+    if (!rows || !alphas || !h_A || !W_base || !b_base || !gamma || !h_mid)
+        return fail(DWA_ERR_INVALID_ARG, "a required pointer is NULL");
+    const AsmWorkspace w = carve(workspace, d, false);
+    if ((rc = check_ws(workspace, workspace_bytes, w.bytes))) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const RowSrc src{rows, row_index, row_index ? d.n_rows : static_cast<int64_t>(d.B) * d.k, d.D,
+                     d.k, d.rows_dtype};
+    if (d.act_dtype == DWA_BF16) {
+        using A = __nv_bfloat16;
+        if (d.rows_dtype == DWA_BF16)
+            return fwd_impl<A, __nv_bfloat16>(st, d, src, alphas, static_cast<const A*>(h_A), W_base,
+                                              b_base, gamma, static_cast<A*>(h_mid), W_out,
+                                              static_cast<A*>(W_act), w);
+        return fwd_impl<A, float>(st, d, src, alphas, static_cast<const A*>(h_A), W_base, b_base,
+                                  gamma, static_cast<A*>(h_mid), W_out, static_cast<A*>(W_act), w);
+    }
+    if (d.rows_dtype == DWA_BF16)
+        return fwd_impl<float, __nv_bfloat16>(st, d, src, alphas, static_cast<const float*>(h_A),
+                                              W_base, b_base, gamma, static_cast<float*>(h_mid),
+                                              W_out, static_cast<float*>(W_act), w);
+    return fwd_impl<float, float>(st, d, src, alphas, static_cast<const float*>(h_A), W_base, b_base,
+                                  gamma, static_cast<float*>(h_mid), W_out,
+                                  static_cast<float*>(W_act), w);
+}
+
+extern "C" int dwa_assemble_bwd(void* stream, const DwaAssembleDims* dims, const void* rows,
+                                const int32_t* row_index, const float* alphas, const void* h_A,
+                                const void* W_act, const float* gamma, const void* g_hmid,
+                                const float* g_W_out, float* g_rows, float* g_alpha, void* g_hA,
+                                float* g_W_base, float* g_b_base, float* g_gamma, void* workspace,
+                                size_t workspace_bytes) {
+    int rc = check_dims(dims);
+    if (rc) return rc;
+    const DwaAssembleDims& d = *dims;
+    if (!rows || !alphas || !h_A || !W_act || !gamma || !g_hmid || !g_rows || !g_alpha || !g_hA ||
+        !g_W_base || !g_b_base || !g_gamma)
+        return fail(DWA_ERR_INVALID_ARG, "a required pointer is NULL");
+    const AsmWorkspace w = carve(workspace, d, true);
+    if ((rc = check_ws(workspace, workspace_bytes, w.bytes))) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const RowSrc src{rows, row_index, row_index ? d.n_rows : static_cast<int64_t>(d.B) * d.k, d.D,
+                     d.k, d.rows_dtype};
+#define DWA_BWD_ARGS(A, R)                                                                       \
+    st, d, src, alphas, static_cast<const A*>(h_A), static_cast<const A*>(W_act), gamma,         \
+        static_cast<const A*>(g_hmid), g_W_out, g_rows, g_alpha, static_cast<A*>(g_hA), g_W_base, \
+        g_b_base, g_gamma, w
+    if (d.act_dtype == DWA_BF16) {
+        if (d.rows_dtype == DWA_BF16)
+            return bwd_impl<__nv_bfloat16, __nv_bfloat16>(DWA_BWD_ARGS(__nv_bfloat16, __nv_bfloat16));
+        return bwd_impl<__nv_bfloat16, float>(DWA_BWD_ARGS(__nv_bfloat16, float));
+    }
+    if (d.rows_dtype == DWA_BF16)
+        return bwd_impl<float, __nv_bfloat16>(DWA_BWD_ARGS(float, __nv_bfloat16));
+    return bwd_impl<float, float>(DWA_BWD_ARGS(float, float));
+#undef DWA_BWD_ARGS
+}

@@ -1,0 +1,374 @@
+// Batched bf16 GEMM on the sm_100a tensor cores (tcgen05 + TMEM + TMA).
+//
+//   C[b](m, n) = sum_k A[b](m, k) * B[b](n, k)      fp32 accumulation in TMEM
+//
+// followed by a caller-supplied epilogue functor that receives each output row
+// segment in registers.  Either operand may be K-major (k contiguous) or
+// MN-major (m / n contiguous); both are staged by TMA with the 128-byte
+// swizzle and consumed directly by tcgen05.mma through shared-memory matrix
+// descriptors, so no transposes are materialised in HBM.
+//
+// CTA tile 128 x BN x 64, STAGES-deep TMA ring, one CTA per output tile:
+//   warp 0      TMA producer (one elected lane)
+//   warp 1      TMEM allocator + MMA issuer (one elected lane)
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, row = TMEM lane
+// Every mbarrier wait is bounded (kWaitLimitNs); a wait that runs out sets
+// DWA_STATUS_WAIT_TIMEOUT in the status word and the CTA winds down, freeing
+// its TMEM.
+#pragma once
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "dwa_common.cuh"
+
+namespace dwa {
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // bf16 elements per k-block = 128 bytes = one swizzle row
+
+// Host description of one operand.  Element (mn, k) of batch item b lives at
+//   K-major : ptr + b*bstride + mn*ld + k
+//   MN-major: ptr + b*bstride + k*ld + mn
+// (element units).  bstride == 0 means the operand is shared by all items.
+struct Operand {
+    const void* ptr;
+    bool mn_major;
+    int64_t ld;
+    int64_t bstride;
+};
+
+// ------------------------------------------------------------------ PTX ----
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for the phase with the given parity to complete; gives up after
+// kWaitLimitNs and returns false.
+static __device__ __noinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+    }
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* tm) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* tm, uint64_t* bar, int c0,
+                                            int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(slot)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle, sm_100 format:
+// start>>4 [0,14), LBO>>4 [16,30), SBO>>4 [32,46), version=1 [46,48),
+// base offset 0 [49,52), layout SWIZZLE_128B = 2 [61,64).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+    d |= static_cast<uint64_t>(1) << 46;
+    d |= static_cast<uint64_t>(2) << 61;
+    return d;
+}
+
+// Instruction descriptor of tcgen05.mma kind::f16: D fp32, A/B bf16, M=128.
+template <int BN, bool A_MN, bool B_MN>
+__host__ __device__ constexpr uint32_t instr_desc_bf16() {
+    return (1u << 4)                       // D format: f32
+           | (1u << 7)                     // A format: bf16
+           | (1u << 10)                    // B format: bf16
+           | ((A_MN ? 1u : 0u) << 15)      // A major: 0 = K, 1 = MN
+           | ((B_MN ? 1u : 0u) << 16)      // B major
+           | (static_cast<uint32_t>(BN >> 3) << 17)
+           | (static_cast<uint32_t>(BM >> 4) << 24);
+}
+
+// Descriptor of k-step kk (16 elements) inside one staged k-block.
+// K-major: rows of 128 B, 8-row atoms 1024 B apart; advance 32 B per k-step.
+// MN-major: 64-element MN chunks (8 KB each, one TMA box of 64 k-rows) LBO
+// apart; 8 k-rows per 1024 B atom; advance 16 k-rows = 2048 B per k-step.
+template <bool MN>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int kk) {
+    if (MN) return sw128_desc(base + kk * 2048, 8192, 1024);
+    return sw128_desc(base + kk * 32, 16, 1024);
+}
+
+template <int BN, int STAGES>
+struct SmemLayout {
+    static constexpr uint32_t A_STAGE = BM * BK * 2;
+    static constexpr uint32_t B_STAGE = BN * BK * 2;
+    static constexpr uint32_t BAR_OFF = STAGES * (A_STAGE + B_STAGE);
+    static constexpr uint32_t BYTES = 1024 /*align slack*/ + BAR_OFF + (2 * STAGES + 1) * 8 + 16;
+};
+
+// Epilogue protocol.  Epi provides
+//   float operator()(int b, int row, int col0, const float* v, int cnt) const
+//     v[0..cnt) = C[b](row, col0 + i); returns a partial for the reductions;
+//   static constexpr int kReduce;   0 none, 1 per row, 2 per CTA
+//   void row_done(int b, int row, float acc) const   (kReduce == 1)
+//   void cta_done(int b, float acc) const            (kReduce == 2)
+template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
+__global__ void __launch_bounds__(192, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     int M, int N, int K, int a_batched, int b_batched, Epi epi, uint32_t* status) {
+    using L = SmemLayout<BN, STAGES>;
+    constexpr uint32_t TMEM_COLS = BN;
+    extern __shared__ uint8_t dyn_smem[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * L::A_STAGE;
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+    uint64_t* empty_bar = full_bar + STAGES;
+    uint64_t* done_bar = empty_bar + STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+    __shared__ float s_red[4];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, bz = blockIdx.z;
+    const int nkb = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        mbar_init(done_bar, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, TMEM_COLS);
+        tmem_relinquish();
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const int za = a_batched ? bz : 0, zb = b_batched ? bz : 0;
+            int issued = 0;
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = kb % STAGES;
+                if (kb >= STAGES && !mbar_wait_bounded(&empty_bar[s], ((kb / STAGES) - 1) & 1)) {
+                    raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
+                    break;
+                }
+                mbar_arrive_expect_tx(&full_bar[s], L::A_STAGE + L::B_STAGE);
+                const int k0 = kb * BK;
+                uint8_t* a = sA + s * L::A_STAGE;
+                uint8_t* b = sB + s * L::B_STAGE;
+                if (A_MN) {
+#pragma unroll
+                    for (int h = 0; h < BM / 64; ++h)
+                        tma_load_3d(a + h * 8192, &tmA, &full_bar[s], m0 + 64 * h, k0, za);
+                } else {
+                    tma_load_3d(a, &tmA, &full_bar[s], k0, m0, za);
+                }
+                if (B_MN) {
+#pragma unroll
+                    for (int h = 0; h < BN / 64; ++h)
+                        tma_load_3d(b + h * 8192, &tmB, &full_bar[s], n0 + 64 * h, k0, zb);
+                } else {
+                    tma_load_3d(b, &tmB, &full_bar[s], k0, n0, zb);
+                }
+                issued = kb + 1;
+            }
+            // Drain: wait until every issued copy has landed before the CTA may exit.
+            for (int kb = (issued > STAGES ? issued - STAGES : 0); kb < issued; ++kb)
+                if (!mbar_wait_bounded(&full_bar[kb % STAGES], (kb / STAGES) & 1)) {
+                    raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
+                    break;
+                }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = instr_desc_bf16<BN, A_MN, B_MN>();
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = kb % STAGES;
+                if (!mbar_wait_bounded(&full_bar[s], (kb / STAGES) & 1)) {
+                    raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a_base = smem_u32(sA + s * L::A_STAGE);
+                const uint32_t b_base = smem_u32(sB + s * L::B_STAGE);
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; ++kk)
+                    mma_bf16_ss(tmem, operand_desc<A_MN>(a_base, kk), operand_desc<B_MN>(b_base, kk),
+                                idesc, (kb | kk) != 0 ? 1u : 0u);
+                mma_commit(&empty_bar[s]);
+            }
+            mma_commit(done_bar);
+        }
+        __syncwarp();
+    } else {
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const bool ok = mbar_wait_bounded(done_bar, 0);
+        if (!ok && lane == 0) raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
+        tc_fence_after();
+        const int row = m0 + q * 32 + lane;
+        float acc = 0.f;
+        if (ok) {
+            for (int c = 0; c < BN / 32; ++c) {
+                const int col0 = n0 + c * 32;
+                if (col0 >= N) break;
+                float v[32];
+                tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c * 32, v);
+                if (row < M) acc += epi(bz, row, col0, v, min(32, N - col0));
+            }
+        }
+        if (Epi::kReduce == 1) {
+            if (ok && row < M) epi.row_done(bz, row, acc);
+        } else if (Epi::kReduce == 2) {
+            acc = warp_sum(acc);
+            if (lane == 0) s_red[q] = acc;
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (Epi::kReduce == 2 && threadIdx.x == 0)
+        epi.cta_done(bz, s_red[0] + s_red[1] + s_red[2] + s_red[3]);
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------ host ---
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
+
+// Builds the 3-D tensor map {inner, outer, batch} of an operand for the box
+// the kernel loads.  Returns false (with a message) when TMA cannot address it.
+bool make_operand_map(CUtensorMap* tm, const Operand& op, int64_t mn_extent, int64_t k_extent,
+                      int batch, int box_mn, std::string* why);
+
+// True when the operand satisfies the TMA rules (16-byte aligned base and
+// strides) and covers at least one full box in each dimension.
+bool tc_operand_ok(const Operand& op, int64_t mn_extent, int64_t k_extent, int box_mn);
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
+int launch_gemm_bf16(const Operand& A, const Operand& B, int M, int N, int K, int batch,
+                     const Epi& epi, uint32_t* status, cudaStream_t stream) {
+    static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64, 128, 192 or 256");
+    static_assert(BN == 64 || BN == 128 || BN == 256, "TMEM allocation needs a power of two");
+    CUtensorMap ta, tb;
+    std::string why;
+    if (!make_operand_map(&ta, A, M, K, batch, BM, &why) ||
+        !make_operand_map(&tb, B, N, K, batch, BN, &why))
+        return fail(DWA_ERR_INVALID_ARG, "tensor map: " + why);
+    using L = SmemLayout<BN, STAGES>;
+    auto kern = gemm_bf16_kernel<BN, STAGES, A_MN, B_MN, Epi>;
+    static bool attr_set[64] = {};  // per instantiation and device
+    int dev = 0;
+    DWA_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        DWA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(L::BYTES)));
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+    dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, batch);
+    kern<<<grid, 192, L::BYTES, stream>>>(ta, tb, M, N, K, A.bstride != 0, B.bstride != 0, epi,
+                                          status);
+    DWA_LAUNCH_CHECK("gemm_bf16_kernel");
+    return DWA_OK;
+}
+
+}  // namespace tc
+}  // namespace dwa

@@ -1,0 +1,321 @@
+"""CPU oracle for the DWA retrieval + assembly hot path of theorionic/matrix.
+
+TEST INFRASTRUCTURE ONLY.  This module restates, in NumPy, the arithmetic of the
+reference's JAX code so that the CUDA path can be checked against it.  Only the
+tests, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg import it,
+and only as the checker / the timed CPU port.  The product path
+(``matrix_b200``) never imports or calls anything here.
+
+Every function cites the reference file:line it follows (paths relative to the
+reference project root).  Arithmetic is done in the dtype of the inputs (pass
+float64 arrays for a high-precision oracle, float32 arrays for the reference's
+own precision).
+
+Pinning: the outputs of this restatement are checked against golden vectors
+produced by executing the reference's own source files
+(``src/dwa/retrieval.py``, ``src/dwa/assembly_pallas.py``) under a NumPy stand-in
+for ``jax``/``flax`` (``tests/golden/make_golden.py``), and against the
+invariants the reference's tests assert (``tests/test_retrieval.py``,
+``tests/test_assembly.py``).  The reference ships no golden vectors of its own
+and JAX is not installable here, so XLA itself never ran; see
+``tests/golden/make_golden.py`` for what that pin does and does not cover.
+
+Extensions beyond the reference (each reduces exactly to the reference when
+switched off):
+
+* ``list_offsets``: CSR list boundaries so lists may have unequal sizes
+  (the reference only supports ``N % C == 0`` equal lists, config.py:64-67).
+* ``tie_break="index"``: among exactly equal scores, prefer the lower global
+  pool index instead of the lower candidate position (``lax.top_k`` position
+  order, retrieval.py:144-145).  The two agree whenever no two candidate scores
+  are bit-identical.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+EPS = 1e-8  # retrieval.py:66,86,103,115 and assembly_pallas :152,155 use +1e-8
+
+
+# ---------------------------------------------------------------------------
+# jnp / lax primitives with the reference's semantics
+# ---------------------------------------------------------------------------
+
+def l2_normalize(x: np.ndarray) -> np.ndarray:
+    """``x / (||x||_2 + 1e-8)`` over the last axis (retrieval.py:66, 85-87, 102-104)."""
+    return x / (np.linalg.norm(x, axis=-1, keepdims=True) + x.dtype.type(EPS))
+
+
+def softmax(x: np.ndarray, axis: int = -1) -> np.ndarray:
+    """``jax.nn.softmax``: ``exp(x - max) / sum(exp(x - max))``."""
+    m = np.max(x, axis=axis, keepdims=True)
+    e = np.exp(x - m)
+    return e / np.sum(e, axis=axis, keepdims=True)
+
+
+def sigmoid(x: np.ndarray) -> np.ndarray:
+    """``jax.nn.sigmoid`` (retrieval.py:150)."""
+    return 1.0 / (1.0 + np.exp(-x))
+
+
+def top_k(x: np.ndarray, k: int, tie_key: np.ndarray | None = None):
+    """``jax.lax.top_k`` over the last axis: values descending.
+
+    Ties between bit-identical values go to the lower *position* (XLA's rule),
+    or, when ``tie_key`` (same shape as ``x``) is given, to the lower tie key
+    (used for the lower-global-index rule).
+    Returns ``(values, positions)``.
+    """
+    if tie_key is None:
+        order = np.argsort(-x, axis=-1, kind="stable")
+    else:
+        # lexsort sorts by the last key first: primary = -x, secondary = tie_key
+        order = np.lexsort((tie_key, -x), axis=-1)
+    pos = order[..., :k]
+    return np.take_along_axis(x, pos, axis=-1), pos
+
+
+# ---------------------------------------------------------------------------
+# Retrieval: MultiAspectRetrieval.__call__ (retrieval.py:48-159)
+# ---------------------------------------------------------------------------
+
+def equal_list_offsets(N: int, C: int) -> np.ndarray:
+    """List c = rows ``[c*N/C, (c+1)*N/C)`` (retrieval.py:94-98, config.py:64-67)."""
+    assert N % C == 0, "equal lists need N % C == 0 (config.py:64-67)"
+    return (np.arange(C + 1, dtype=np.int64) * (N // C)).astype(np.int64)
+
+
+def aspect_queries(W_Q: np.ndarray, z: np.ndarray) -> np.ndarray:
+    """Normalised aspect queries ``q̂[b,s,:]`` (retrieval.py:64-66)."""
+    queries = np.einsum("ska,ba->bsk", W_Q, z)
+    return l2_normalize(queries)
+
+
+def coarse_scores(q_norm, w, centroids):
+    """``c_score[b,c] = Σ_s w_s q̂[b,s]·ĉ[s,c]`` (retrieval.py:85-89)."""
+    c_norm = l2_normalize(centroids)
+    c_sim = np.einsum("bsk,sck->bsc", q_norm, c_norm)
+    return np.einsum("s,bsc->bc", w, c_sim)
+
+
+def candidate_lists(top_clusters: np.ndarray, list_offsets: np.ndarray):
+    """Candidate pool rows in cluster-rank-major order (retrieval.py:94-98).
+
+    With equal lists this is exactly ``top_clusters[:, :, None] * N_per_C +
+    arange(N_per_C)``.  With CSR offsets each query's candidate count may differ;
+    the result is a list of 1-D int64 arrays, one per query.
+    """
+    out = []
+    for b in range(top_clusters.shape[0]):
+        parts = [np.arange(list_offsets[c], list_offsets[c + 1], dtype=np.int64)
+                 for c in top_clusters[b]]
+        out.append(np.concatenate(parts) if parts else np.zeros(0, np.int64))
+    return out
+
+
+def fine_scores(q_norm, w, pool_keys, cand):
+    """``s_i[n] = Σ_s w_s q̂_s·k̂_s[cand[n]]`` for one query (retrieval.py:100-106).
+
+    ``q_norm`` is ``[S, d_k]`` for that query and ``cand`` the 1-D candidate rows.
+    """
+    keys_refine = pool_keys[:, cand, :]                        # [S, K_ref, d_k]
+    k_norm = l2_normalize(keys_refine)
+    sim_ref = np.einsum("sk,snk->sn", q_norm, k_norm)
+    return np.einsum("s,sn->n", w, sim_ref)
+
+
+def full_scores(q_norm, w, pool_keys):
+    """``s_full[b,n]`` over every pool row (retrieval.py:114-118, 123-125)."""
+    p_norm = l2_normalize(pool_keys)
+    sim_all = np.einsum("bsk,snk->bsn", q_norm, p_norm)
+    return np.einsum("s,bsn->bn", w, sim_all)
+
+
+def select(s_i, cand, k, T, lambda_val, tau, is_warmup, tie_break="position"):
+    """Warmup / gate selection for one query (retrieval.py:143-156).
+
+    Returns ``(alpha [k], global_idx [k])``.  Gate mode ranks ``raw`` exactly as
+    the reference does (``raw`` is monotone in ``s_i`` for ``lambda >= 0``).
+    """
+    tie = cand if tie_break == "index" else None
+    if is_warmup:
+        scores, pos = top_k(s_i, k, tie)                      # :144
+        alpha = softmax(scores / s_i.dtype.type(T))            # :146
+    else:
+        g = sigmoid(s_i.dtype.type(lambda_val) * (s_i - s_i.dtype.type(tau)))   # :150
+        raw = g * np.exp(s_i / s_i.dtype.type(T))              # :151
+        raw = raw / (raw.sum() + s_i.dtype.type(EPS))          # :152
+        top_raw, pos = top_k(raw, k, tie)                      # :153
+        alpha = top_raw / (top_raw.sum() + s_i.dtype.type(EPS))  # :155
+    return alpha, cand[pos]                                    # :145,:154
+
+
+def retrieve(z, W_Q, aspect_weights, tau, centroids, pool_keys, *, k, m, T,
+             lambda_val, is_warmup, use_ivf=True, list_offsets=None,
+             tie_break="position", want_soft_full=True, return_internals=False):
+    """``MultiAspectRetrieval.__call__`` (retrieval.py:48-159), single device.
+
+    Arguments mirror the module's parameters (``W_Q [S,d_k,d_A]``,
+    ``aspect_weights [S]``, ``tau``, ``centroids [S,C,d_k]``) and call arguments
+    (``z [B,d_A]``, ``pool_keys [S,N,d_k]``, ``lambda_val``, ``is_warmup``).
+    Returns ``(alphas [B,k], indices [B,k] int64, soft_full [B,N] or None)``.
+    """
+    B = z.shape[0]
+    S, N, _ = pool_keys.shape
+    q_norm = aspect_queries(W_Q, z)                             # :65-66
+    w = softmax(aspect_weights, axis=0)                         # :69
+    internals = {"q_norm": q_norm, "w": w}
+    soft_full = None
+    if use_ivf:
+        C = centroids.shape[1]
+        if list_offsets is None:
+            list_offsets = equal_list_offsets(N, C)
+        c_score = coarse_scores(q_norm, w, centroids)           # :85-89
+        m_eff = min(m, C)                                       # :90
+        _, top_clusters = top_k(c_score, m_eff)                 # :91
+        cands = candidate_lists(top_clusters, list_offsets)     # :94-98
+        s_list = [fine_scores(q_norm[b], w, pool_keys, cands[b]) for b in range(B)]
+        internals.update(c_score=c_score, top_clusters=top_clusters,
+                         cands=cands, s_i=s_list)
+        if want_soft_full:
+            soft_full = softmax(full_scores(q_norm, w, pool_keys) / q_norm.dtype.type(T))  # :114-119
+    else:
+        s_full = full_scores(q_norm, w, pool_keys)              # :123-125
+        cands = [np.arange(N, dtype=np.int64) for _ in range(B)]   # :135-137
+        s_list = [s_full[b] for b in range(B)]
+        internals.update(cands=cands, s_i=s_list)
+        if want_soft_full:
+            soft_full = softmax(s_full / q_norm.dtype.type(T))  # :138
+    alphas = np.zeros((B, k), dtype=q_norm.dtype)
+    indices = np.zeros((B, k), dtype=np.int64)
+    for b in range(B):
+        alphas[b], indices[b] = select(s_list[b], cands[b], k, T, lambda_val, tau,
+                                       is_warmup, tie_break)
+    if return_internals:
+        return alphas, indices, soft_full, internals
+    return alphas, indices, soft_full
+
+
+# ---------------------------------------------------------------------------
+# Gather (model.py:184-195) and key cache (assembly_pallas.py:392-400)
+# ---------------------------------------------------------------------------
+
+def gather(pool_vectors, indices, out_dtype=np.float32):
+    """``pool_vecs[indices]`` then the cast to float32 (model.py:193-195)."""
+    return pool_vectors[indices].astype(out_dtype)
+
+
+def compute_key_cache(pool_vectors, key_proj):
+    """``einsum("nd,sda->sna")`` (assembly_pallas.py:392-400, pool.py:37-44)."""
+    return np.einsum("nd,sda->sna", pool_vectors, key_proj)
+
+
+# ---------------------------------------------------------------------------
+# Assembly forward: assemble_jax (assembly_pallas.py:42-75)
+# ---------------------------------------------------------------------------
+
+def factor_split(d_B: int, r: int, d_A: int):
+    """``(s1, s2, s3)`` (config.py:159-165)."""
+    s1 = d_B * r
+    s2 = s1 + r * d_A
+    return s1, s2, s2 + d_B
+
+
+def split_factors(gathered, d_B, r, d_A):
+    """U ``[B,k,d_B,r]``, V ``[B,k,r,d_A]``, b ``[B,k,d_B]`` (assembly_pallas.py:54-60)."""
+    B, k, _ = gathered.shape
+    s1, s2, s3 = factor_split(d_B, r, d_A)
+    U = gathered[:, :, :s1].reshape(B, k, d_B, r)
+    V = gathered[:, :, s1:s2].reshape(B, k, r, d_A)
+    b_vec = gathered[:, :, s2:s3]
+    return U, V, b_vec
+
+
+def assemble(gathered, alphas, h_A, W_base, b_base, gamma, d_B, r, d_A):
+    """``assemble_jax`` (assembly_pallas.py:42-75).  Returns ``(h_mid, W)``."""
+    B, k, _ = gathered.shape
+    U, V, b_vec = split_factors(gathered, d_B, r, d_A)
+    aU = alphas[:, :, None, None] * U                                   # :63
+    delta_W = np.matmul(aU.reshape(B * k, d_B, r),
+                        V.reshape(B * k, r, d_A)).reshape(B, k, d_B, d_A).sum(1)  # :64-66
+    W = W_base[None, ...] + delta_W                                     # :67
+    delta_b = (alphas[:, :, None] * b_vec).sum(1)                       # :69
+    bias = b_base[None, :] + delta_b                                    # :70
+    h_res = np.matmul(h_A, W.transpose(0, 2, 1))                        # :73
+    h_mid = h_A + gamma * h_res + bias[:, None, :]                      # :74
+    return h_mid, W
+
+
+# ---------------------------------------------------------------------------
+# Assembly backward: _pallas_assemble_bwd (assembly_pallas.py:246-329)
+# ---------------------------------------------------------------------------
+
+def assemble_bwd(gathered, alphas, h_A, W, gamma, g_hmid, g_W_out, d_B, r, d_A,
+                 batch_chunk: int | None = None):
+    """Analytic VJP of the assembly (assembly_pallas.py:246-329).
+
+    Returns ``(g_gathered [B,k,D], g_alpha [B,k], g_hA [B,T,d_A],
+    g_W_base [d_B,d_A], g_b_base [d_B], g_gamma ())``.  ``g_W_out`` may be
+    ``None`` for a zero cotangent of the ``W`` output.  ``batch_chunk`` only
+    bounds the memory of the ``UV [B,k,d_B,d_A]`` temporary (:293-298); the
+    arithmetic per element is unchanged.
+    """
+    B, k, D = gathered.shape
+    s1, s2, s3 = factor_split(d_B, r, d_A)
+    if g_W_out is None:
+        g_W_out = np.zeros_like(W)
+    U, V, b_vec = split_factors(gathered, d_B, r, d_A)                 # :267-269
+    h_res = np.matmul(h_A, W.transpose(0, 2, 1))                       # :272
+    g_gamma = np.sum(g_hmid * h_res)                                   # :275
+    g_bias = g_hmid.sum(axis=1)                                        # :276
+    g_h_res = gamma * g_hmid                                           # :277
+    g_W_hres = np.einsum("btj,bti->bji", g_h_res, h_A)                 # :281
+    g_hA_hres = np.einsum("btj,bji->bti", g_h_res, W)                  # :283
+    g_hA = g_hmid + g_hA_hres                                          # :285
+    g_W_total = g_W_hres + g_W_out                                     # :288
+    g_W_base = g_W_total.sum(0)                                        # :289
+    g_delta_W = g_W_total                                              # :290
+    step = batch_chunk or B
+    g_alpha_dW = np.zeros((B, k), dtype=g_delta_W.dtype)
+    for b0 in range(0, B, step):
+        b1 = min(B, b0 + step)
+        nb = b1 - b0
+        UV = np.matmul(U[b0:b1].reshape(nb * k, d_B, r),
+                       V[b0:b1].reshape(nb * k, r, d_A)).reshape(nb, k, d_B, d_A)  # :293-295
+        g_alpha_dW[b0:b1] = np.einsum("bkji,bji->bk", UV, g_delta_W[b0:b1])    # :298
+    g_U = alphas[:, :, None, None] * np.matmul(g_delta_W[:, None, :, :],
+                                               V.transpose(0, 1, 3, 2))          # :303-305
+    g_V = alphas[:, :, None, None] * np.matmul(U.transpose(0, 1, 3, 2),
+                                               g_delta_W[:, None, :, :])         # :310-312
+    g_b_base = g_bias.sum(0)                                           # :315
+    g_alpha_bias = (b_vec * g_bias[:, None, :]).sum(-1)                # :316
+    g_b_vec = alphas[:, :, None] * g_bias[:, None, :]                  # :317
+    g_alpha = g_alpha_dW + g_alpha_bias                                # :319
+    g_gathered = np.concatenate([                                      # :322-327
+        g_U.reshape(B, k, s1),
+        g_V.reshape(B, k, s2 - s1),
+        g_b_vec,
+        np.zeros((B, k, D - s3), dtype=gathered.dtype),
+    ], axis=-1)
+    return g_gathered, g_alpha, g_hA, g_W_base, g_b_base, g_gamma
+
+
+def pallas_forward(gathered, alphas, h_A, W_base, b_base, gamma, d_B, r, d_A):
+    """The Pallas kernel's arithmetic (assembly_pallas.py:85-181), in the
+    pre-factored order it uses: ``hA + γ(hA·W_baseᵀ + (hA·V_sᵀ)·U_f) + pb``.
+
+    Equal to :func:`assemble` up to rounding for every B (the reference's Pallas
+    grid leaves rows ``B - B % 8 .. B`` unwritten when ``B > 8`` and
+    ``B % 8 != 0``, :100,131; this restatement computes them).
+    """
+    B, k, _ = gathered.shape
+    kr = k * r
+    U, V, b_vec = split_factors(gathered, d_B, r, d_A)
+    V_scaled = (alphas[:, :, None, None] * V).reshape(B, kr, d_A)     # :168
+    U_flat = U.transpose(0, 1, 3, 2).reshape(B, kr, d_B)              # :169
+    pb = b_base + np.einsum("bk,bkd->bd", alphas, b_vec)              # :170-171
+    h_V = np.matmul(h_A, V_scaled.transpose(0, 2, 1))                  # :113
+    h_res_delta = np.matmul(h_V, U_flat)                               # :114
+    h_base = np.matmul(h_A, W_base.T)                                  # :115
+    return h_A + gamma * (h_base + h_res_delta) + pb[:, None, :]       # :117

@@ -1,0 +1,138 @@
+"""Parity of the CUDA retrieval with golden vectors from the reference's own
+``MultiAspectRetrieval.__call__`` and with the oracle.
+
+Indices must match exactly (the seeds have no near-ties at the top-k boundary,
+checked in the oracle tests); alphas and soft_full within rtol 1e-5.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import assert_close, load_golden
+from matrix_b200.config import DWAConfig
+from matrix_b200.synthetic import make_inputs
+from oracle import dwa_oracle as O
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-5
+
+
+def _dev(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    return t.to(dtype) if dtype is not None else t
+
+
+def _gpu_retrieve(cfg, x, lam, is_warmup, want_sf, use_ivf=True, offsets=None, max_list=None,
+                  z_dtype=None):
+    from matrix_b200.retrieval import retrieve
+    z = _dev(x.z)
+    if z_dtype is not None:
+        z = z.to(z_dtype)
+    a, i, sf = retrieve(z, _dev(x.W_Q), _dev(x.aspect_weights), torch.tensor(x.tau).cuda(),
+                        _dev(x.centroids), _dev(x.keys), lam, is_warmup, k=cfg.k_max, m=cfg.m,
+                        T=cfg.T, use_ivf=use_ivf,
+                        list_offsets=None if offsets is None else _dev(offsets),
+                        max_list=max_list, want_soft_full=want_sf)
+    torch.cuda.synchronize()
+    return a.cpu().numpy(), i.cpu().numpy(), None if sf is None else sf.cpu().numpy()
+
+
+@pytest.mark.parametrize("case", ["smoke", "smoke_rich", "refsmall", "ragged"])
+@pytest.mark.parametrize("want_sf", [True, False])
+def test_retrieval_matches_reference_golden(case, want_sf):
+    from test_oracle_golden import _inputs
+    from matrix_b200.runtime import raise_on_device_status
+    cfg, x, modes, _ = _inputs(case)
+    g = load_golden(case)
+    for is_warmup, lam in modes:
+        tag = "warmup" if is_warmup else "gate"
+        a, i, sf = _gpu_retrieve(cfg, x, lam, is_warmup, want_sf)
+        np.testing.assert_array_equal(i, g[f"{tag}_indices"], err_msg=f"{case}/{tag}")
+        assert_close(a, g[f"{tag}_alphas"], TOL, name=f"{case}/{tag}/alphas")
+        if want_sf:
+            assert_close(sf, g[f"{tag}_soft_full"], TOL, name=f"{case}/{tag}/soft_full")
+    raise_on_device_status()
+
+
+@pytest.mark.parametrize("case", ["smoke_rich", "ragged"])
+def test_fine_scores_equal_full_pass_scores(case):
+    """Selection from the fine kernel and from the full pass are bit-identical."""
+    from test_oracle_golden import _inputs
+    cfg, x, modes, _ = _inputs(case)
+    for is_warmup, lam in modes:
+        a1, i1, _ = _gpu_retrieve(cfg, x, lam, is_warmup, True)
+        a2, i2, _ = _gpu_retrieve(cfg, x, lam, is_warmup, False)
+        np.testing.assert_array_equal(i1, i2)
+        np.testing.assert_array_equal(a1, a2)
+
+
+def _zipf_case(seed=7):
+    cfg = DWAConfig(D=17 * 64, N=20000, use_ivf=True, C=40, m=5, d_A=64, d_B=64, r=8, k_max=24,
+                    S=4, d_k=64, T=1.0, gamma_init=0.1, bf16_pool=False)
+    x = make_inputs(cfg, 6, 16, seed, variant="rich", zipf=1.1)
+    return cfg, x
+
+
+@pytest.mark.parametrize("is_warmup,lam", [(True, 1.0), (False, 5.0), (False, -2.0)])
+def test_zipf_csr_lists_match_oracle(is_warmup, lam):
+    cfg, x = _zipf_case()
+    off = x.list_offsets
+    max_list = int(np.diff(off).max())
+    a, i, sf = _gpu_retrieve(cfg, x, lam, is_warmup, True, offsets=off, max_list=max_list)
+    f = np.float64
+    ra, ri, rsf, internals = O.retrieve(
+        x.z.astype(f), x.W_Q.astype(f), x.aspect_weights.astype(f), f(x.tau),
+        x.centroids.astype(f), x.keys.astype(f), k=cfg.k_max, m=cfg.m, T=cfg.T, lambda_val=lam,
+        is_warmup=is_warmup, list_offsets=off, tie_break="index", return_internals=True)
+    for b in range(i.shape[0]):
+        s = np.sort(internals["s_i"][b])[::-1]
+        assert s[cfg.k_max - 1] - s[cfg.k_max] > 1e-6
+    np.testing.assert_array_equal(i, ri)
+    assert_close(a, ra, TOL, name="alphas")
+    assert_close(sf, rsf, TOL, name="soft_full")
+
+
+@pytest.mark.parametrize("is_warmup,lam", [(True, 1.0), (False, 5.0)])
+def test_full_search_matches_oracle(is_warmup, lam):
+    from test_oracle_golden import _inputs
+    cfg, x, _, _ = _inputs("smoke_rich")
+    a, i, sf = _gpu_retrieve(cfg, x, lam, is_warmup, True, use_ivf=False)
+    f = np.float64
+    ra, ri, rsf = O.retrieve(x.z.astype(f), x.W_Q.astype(f), x.aspect_weights.astype(f), f(x.tau),
+                             None, x.keys.astype(f), k=cfg.k_max, m=cfg.m, T=cfg.T,
+                             lambda_val=lam, is_warmup=is_warmup, use_ivf=False)
+    np.testing.assert_array_equal(i, ri)
+    assert_close(a, ra, TOL, name="alphas")
+    assert_close(sf, rsf, TOL, name="soft_full")
+
+
+def test_bf16_query_input():
+    from test_oracle_golden import _inputs
+    from matrix_b200.synthetic import bf16_round
+    cfg, x, _, _ = _inputs("smoke")
+    x.z = bf16_round(x.z)
+    a1, i1, _ = _gpu_retrieve(cfg, x, 5.0, False, False)
+    a2, i2, _ = _gpu_retrieve(cfg, x, 5.0, False, False, z_dtype=torch.bfloat16)
+    np.testing.assert_array_equal(i1, i2)
+    np.testing.assert_array_equal(a1, a2)
+
+
+def test_module_interface_matches_reference_call():
+    """MultiAspectRetrieval(cfg)(z, keys, lambda, is_warmup) -> (alphas, indices, soft_full)
+    with the reference's invariants (tests/test_retrieval.py:31-70)."""
+    from matrix_b200.retrieval import MultiAspectRetrieval
+    from test_oracle_golden import _inputs
+    cfg, x, _, _ = _inputs("refsmall")
+    mod = MultiAspectRetrieval(cfg, device="cuda", generator=torch.Generator().manual_seed(0))
+    keys = _dev(x.keys)
+    z = _dev(x.z)
+    for lam, wu in ((1.0, True), (5.0, False)):
+        al, ix, sf = mod(z, keys, lam, wu)
+        assert al.shape == (z.shape[0], cfg.k_max) and ix.shape == al.shape
+        assert torch.allclose(al.sum(-1), torch.ones(z.shape[0], device="cuda"), atol=1e-5)
+        assert (al >= 0).all() and (ix >= 0).all() and (ix < cfg.N).all()
+        assert torch.allclose(sf.sum(-1), torch.ones(z.shape[0], device="cuda"), atol=1e-4)
