@@ -1,0 +1,511 @@
+#!/usr/bin/env python
+"""Benchmark of the DWA hot path on B200: retrieve + assemble + apply, with the
+custom-VJP backward, on the single-GPU "small" workload
+(bf16, batch 8, seq 512, d 1024, pool 262144 x 17408, 512 lists, nprobe 8,
+top-k 32, gate selection with soft_full, forward + backward).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference]
+
+One JSON line on rank 0.  ``value`` is assembled tokens/s of the whole job
+(all ranks), timed on the device with CUDA events around each step, L2
+flushed (512 MB write) between steps, max over ranks.  One step is replayed
+from a CUDA graph of: z = mean_t h_A -> dwa_retrieve -> dwa_assemble_fwd ->
+dwa_assemble_bwd (+ an NCCL all-reduce of the replicated-parameter gradients
+when N > 1, the shard_map transpose of the reference's batch-sharded path).
+With N GPUs every rank runs its own batch against its own pool replica
+(data parallel, weak scaling).
+
+``e2e`` repeats the step through the public Python API with the step's
+inputs copied from pinned host memory and its results copied back inside the
+timed region.  ``--impl reference`` times the CPU restatement of the
+reference's algorithm (the NumPy oracle; JAX is not installable here) on the
+host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "assembled tokens/sec/GPU (retrieve+assemble+apply) at 1/2/4/8 B200; % HBM/tensor roofline"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="small")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--cpu-budget-s", type=float, default=20.0,
+                    help="CPU seconds for the cpu_baseline sample (rank 0, N=1)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+# --------------------------------------------------------------- workload ---
+def build_device_workload(w, device, seed):
+    """Seeded synthetic inputs generated on the device (the pool is 9 GB)."""
+    import torch
+    cfg = w.cfg
+    g = torch.Generator(device=device).manual_seed(seed)
+    d, D, N, S, dk, C = cfg.d_A, cfg.D, cfg.N, cfg.S, cfg.d_k, cfg.C
+    bf = torch.bfloat16
+    pool = torch.empty((N, D), dtype=bf, device=device)
+    step = 16384
+    for i in range(0, N, step):
+        pool[i:i + step].normal_(0.0, d ** -0.5, generator=g)
+    key_proj = (torch.randn((S, D, dk), generator=g, device=device) * D ** -0.5).to(bf)
+    kp = key_proj.permute(1, 0, 2).reshape(D, S * dk)
+    keys = torch.empty((S, N, dk), dtype=torch.float32, device=device)
+    for i in range(0, N, step):
+        blk = (pool[i:i + step] @ kp).float().reshape(-1, S, dk)   # key cache (outside the step)
+        keys[:, i:i + blk.shape[0]] = blk.permute(1, 0, 2)
+    off = torch.arange(C + 1, dtype=torch.int64, device=device) * (N // C)
+    rows = off[:-1] + torch.randint(0, N // C, (C,), generator=g, device=device)
+    t = dict(
+        pool=pool, keys=keys, list_offsets=off, centroids=keys[:, rows, :].contiguous(),
+        W_Q=torch.randn((S, dk, d), generator=g, device=device) * d ** -0.5,
+        aspect_weights=torch.zeros(S, device=device), tau=torch.zeros(1, device=device),
+        W_base=torch.randn((d, d), generator=g, device=device) * 0.01,
+        b_base=torch.zeros(d, device=device),
+        gamma=torch.full((1,), cfg.gamma_init, device=device),
+        lam=torch.full((1,), w.lambda_val, device=device),
+        h_A=torch.randn((w.batch, w.seq, d), generator=g, device=device).to(bf),
+        g_hmid=(torch.randn((w.batch, w.seq, d), generator=g, device=device) * 0.1).to(bf),
+        g_W=torch.randn((w.batch, d, d), generator=g, device=device) * 1e-3,
+    )
+    return t
+
+
+class Step:
+    """One hot-path step on device-resident inputs through the C ABI."""
+
+    def __init__(self, w, t, group):
+        import torch
+        from matrix_b200 import _lib
+        self.w, self.t, self.group = w, t, group
+        self.lib = _lib.load()
+        self.z = torch.empty((w.batch, w.cfg.d_A), dtype=torch.float32, device=t["h_A"].device)
+
+    def __call__(self, h_A=None, g_hmid=None, g_W=None):
+        import torch
+        from matrix_b200 import runtime
+        from matrix_b200.assembly import assemble_backward, assemble_forward
+        from matrix_b200.retrieval import retrieve
+        w, t, cfg = self.w, self.t, self.w.cfg
+        h_A = t["h_A"] if h_A is None else h_A
+        g_hmid = t["g_hmid"] if g_hmid is None else g_hmid
+        g_W = t["g_W"] if g_W is None else g_W
+        dev = h_A.device
+        rc = self.lib.dwa_sequence_mean(runtime.stream_of(dev), w.batch, w.seq, cfg.d_A, 1,
+                                        runtime.ptr(h_A), runtime.ptr(self.z))
+        from matrix_b200 import _lib
+        _lib.check(rc, "dwa_sequence_mean")
+        alphas, indices, soft_full = retrieve(
+            self.z, t["W_Q"], t["aspect_weights"], t["tau"], t["centroids"], t["keys"], t["lam"],
+            w.is_warmup, k=cfg.k_max, m=cfg.m, T=cfg.T, list_offsets=t["list_offsets"],
+            max_list=cfg.N // cfg.C, want_soft_full=w.soft_full)
+        h_mid, W, W_act = assemble_forward(t["pool"], alphas, h_A, t["W_base"], t["b_base"],
+                                           t["gamma"], cfg.d_B, cfg.r, cfg.d_A, row_index=indices)
+        out = dict(alphas=alphas, indices=indices, soft_full=soft_full, h_mid=h_mid, W=W)
+        if w.backward:
+            g = assemble_backward(t["pool"], alphas, h_A, W_act, t["gamma"], g_hmid, g_W,
+                                  cfg.d_B, cfg.r, cfg.d_A, row_index=indices)
+            out.update(zip(("g_rows", "g_alpha", "g_hA", "g_W_base", "g_b_base", "g_gamma"), g))
+            if self.group is not None:
+                import torch.distributed as dist
+                flat = torch.cat([out["g_W_base"].reshape(-1), out["g_b_base"], out["g_gamma"]])
+                dist.all_reduce(flat, group=self.group)
+                out["g_params"] = flat
+        return out
+
+
+# ------------------------------------------------------ roofline numbers ---
+def kernel_work(w, name):
+    """Algorithmic bytes (HBM-bound kernels) or flops (tensor kernels) of one
+    launch of `name` on workload w; returns (bound, amount)."""
+    c = w.cfg
+    B, T, d, k, r, S, dk, N = w.batch, w.seq, c.d_A, c.k_max, c.r, c.S, c.d_k, c.N
+    kr = k * r
+    table = {
+        "full_scores": ("hbm", 4 * (S * N * dk + B * N)),
+        "fine": ("hbm", 4 * (B * S * min(c.m, c.C) * (N // c.C) * dk)),
+        "softmax_apply": ("hbm", 8 * B * N),
+        "prep_factors": ("hbm", B * k * (d * r + r * d) * 2 * 2),
+        "gemm_W": ("tensor", 2 * B * d * d * kr),
+        "gemm_apply": ("tensor", 2 * B * T * d * d),
+        "gemm_G": ("tensor", 2 * B * T * d * d),
+        "gemm_gh": ("tensor", 2 * B * T * d * d),
+        "gemm_P": ("tensor", 2 * B * d * d * kr),
+        "gemm_Q": ("tensor", 2 * B * d * d * kr),
+    }
+    return table.get(name, ("hbm", None))
+
+
+KERNELS = ["seq_mean", "query", "coarse", "topm", "full_scores", "fine", "select", "softmax_stats",
+           "softmax_apply", "prep_factors", "prep_bias", "gemm_W", "gemm_apply", "gemm_G",
+           "gemm_gh", "gemm_P", "gemm_Q", "colsum", "finalize", "bias_grad"]
+
+
+def profile_kernels(step, flush, n=5):
+    """Average duration (ms) of every library kernel in one eager step."""
+    import torch
+    from matrix_b200 import _lib
+    lib = _lib.load()
+    ev = {k: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for k in KERNELS}
+    for k, (a, b) in ev.items():
+        lib.dwa_profile_kernel(k.encode(), C_ptr(a), C_ptr(b))
+    acc = {k: [] for k in KERNELS}
+    for _ in range(n):
+        flush()
+        # events of kernels that do not run this step keep an old record: mark them
+        for a, b in ev.values():
+            a.record(); b.record()
+        torch.cuda.synchronize()
+        step()
+        torch.cuda.synchronize()
+        for k, (a, b) in ev.items():
+            ms = a.elapsed_time(b)
+            if ms > 0:
+                acc[k].append(ms)
+    lib.dwa_profile_clear()
+    return {k: float(np.mean(v)) for k, v in acc.items() if v}
+
+
+def C_ptr(event):
+    import ctypes
+    return ctypes.c_void_p(event.cuda_event)
+
+
+# ---------------------------------------------------------------- clocks ---
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------- CPU baseline ---
+def cpu_baseline(w, t, budget_s):
+    """The NumPy oracle (the reference's algorithm, float32) on one sequence of
+    the same workload per sample, with the same key cache and pool rows."""
+    from oracle import dwa_oracle as O
+    import torch
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:  # noqa: BLE001
+        threads = 1
+    cfg = w.cfg
+    keys = t["keys"].cpu().numpy()
+    cents = t["centroids"].cpu().numpy()
+    W_Q = t["W_Q"].cpu().numpy()
+    aw = t["aspect_weights"].cpu().numpy()
+    W_base = t["W_base"].cpu().numpy()
+    b_base = t["b_base"].cpu().numpy()
+    gamma = np.float32(t["gamma"].item())
+    h_all = t["h_A"].float().cpu().numpy()
+    g_all = t["g_hmid"].float().cpu().numpy()
+    gW_all = t["g_W"].cpu().numpy()
+    pool = t["pool"]
+
+    def one(b):
+        h = h_all[b:b + 1]
+        z = h.mean(axis=1, dtype=np.float32)
+        a, idx, sf = O.retrieve(z, W_Q, aw, np.float32(0.0), cents, keys, k=cfg.k_max, m=cfg.m,
+                                T=cfg.T, lambda_val=w.lambda_val, is_warmup=w.is_warmup,
+                                want_soft_full=w.soft_full)
+        gathered = pool[torch.from_numpy(idx).to(pool.device)].float().cpu().numpy()
+        h_mid, W = O.assemble(gathered, a, h, W_base, b_base, gamma, cfg.d_B, cfg.r, cfg.d_A)
+        if w.backward:
+            O.assemble_bwd(gathered, a, h, W, gamma, g_all[b:b + 1], gW_all[b:b + 1],
+                           cfg.d_B, cfg.r, cfg.d_A)
+
+    one(0)  # warm-up
+    times, b = [], 0
+    t0 = time.perf_counter()
+    while not times or (time.perf_counter() - t0 < budget_s and len(times) < w.batch):
+        s = time.perf_counter()
+        one(b % w.batch)
+        times.append(time.perf_counter() - s)
+        b += 1
+    sec_per_seq = float(np.mean(times))
+    return {"value": w.seq / sec_per_seq, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{len(times)} of {w.batch} sequences ({w.seq} tokens each): NumPy float32 "
+                      f"oracle of retrieval.py:48-159 + model.py:193-195 + assemble_jax + "
+                      f"_pallas_assemble_bwd, same key cache and pool rows as the GPU run",
+            "sec_per_sequence": sec_per_seq}
+
+
+def reference_arm(args, w, rank):
+    """--impl reference: the CPU port timed per step on one sequence per step."""
+    if rank != 0:
+        return
+    import torch
+    dev = torch.device("cuda", 0) if torch.cuda.is_available() else None
+    if dev is None:
+        print(json.dumps({"impl": "reference", "unavailable": "needs the device workload builder"}))
+        return
+    t = build_device_workload(w, dev, args.seed)
+    budget = 150.0
+    cb = cpu_baseline(w, t, budget_s=min(budget, 30.0))
+    sec = cb["sec_per_sequence"]
+    steps = int(min(args.steps, max(1, budget // max(sec, 1e-9))))
+    value = cb["value"]
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": steps, "steps_requested": args.steps,
+            "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": w.name, "note": w.note},
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------- main ---
+def main():
+    args = parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    from matrix_b200.config import WORKLOADS
+    w = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        return reference_arm(args, w, rank)
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        group = dist.group.WORLD
+
+    t = build_device_workload(w, dev, args.seed + rank)
+    step = Step(w, t, group)
+    flush_buf = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def flush():
+        flush_buf.zero_()
+
+    from matrix_b200 import _lib
+    step()                       # first call: workspaces, kernel attributes
+    torch.cuda.synchronize()
+    c0 = _lib.launch_counters()[0]
+    step()
+    torch.cuda.synchronize()
+    launches_per_step = _lib.launch_counters()[0] - c0
+
+    breakdown = profile_kernels(step, flush)
+    dominant = max(breakdown, key=breakdown.get)
+
+    # capture the step in a CUDA graph, with the dominant kernel's events inside
+    lib = _lib.load()
+    ka, kb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    lib.dwa_profile_kernel(dominant.encode(), C_ptr(ka), C_ptr(kb))
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            step()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    lib.dwa_profile_clear()
+
+    for _ in range(max(args.warmup, 3)):
+        flush()
+        graph.replay()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
+                           else local)
+    sampler.start()
+    time.sleep(0.2)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    stops = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    kern_ms = []
+    if group is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush()
+        starts[i].record()
+        graph.replay()
+        stops[i].record()
+        stops[i].synchronize()
+        kern_ms.append(ka.elapsed_time(kb))
+    torch.cuda.synchronize()
+    if group is not None:
+        dist.barrier()
+    clocks = sampler.stop()
+    step_ms = float(sum(a.elapsed_time(b) for a, b in zip(starts, stops)))
+    tmax = torch.tensor([step_ms], device=dev, dtype=torch.float64)
+    if group is not None:
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+    total_ms = float(tmax.item())
+    ms_per_step = total_ms / args.steps
+    tokens = w.batch * w.seq
+    value = tokens * world / (ms_per_step / 1e3)
+
+    # ---- end to end through the public API with pinned host buffers ----
+    e2e = None
+    if not args.no_e2e:
+        hA_h = t["h_A"].cpu().pin_memory()
+        g_h = t["g_hmid"].cpu().pin_memory()
+        gW_h = t["g_W"].cpu().pin_memory()
+        hA_d, g_d, gW_d = torch.empty_like(t["h_A"]), torch.empty_like(t["g_hmid"]), torch.empty_like(t["g_W"])
+        res_keys = ["h_mid", "g_hA", "g_rows", "g_alpha", "g_W_base", "g_b_base", "g_gamma",
+                    "alphas", "indices"]
+        out = step(hA_d.copy_(hA_h), g_d.copy_(g_h), gW_d.copy_(gW_h))
+        pinned = {k: torch.empty(out[k].shape, dtype=out[k].dtype).pin_memory() for k in res_keys}
+        h2d = hA_h.nbytes + g_h.nbytes + gW_h.nbytes
+        d2h = sum(v.nbytes for v in pinned.values())
+        n_e2e = min(args.steps, 50)
+        ea = [torch.cuda.Event(enable_timing=True) for _ in range(n_e2e)]
+        eb = [torch.cuda.Event(enable_timing=True) for _ in range(n_e2e)]
+        torch.cuda.synchronize()
+        for i in range(n_e2e):
+            flush()
+            ea[i].record()
+            hA_d.copy_(hA_h, non_blocking=True)
+            g_d.copy_(g_h, non_blocking=True)
+            gW_d.copy_(gW_h, non_blocking=True)
+            out = step(hA_d, g_d, gW_d)
+            for k in res_keys:
+                pinned[k].copy_(out[k], non_blocking=True)
+            eb[i].record()
+            eb[i].synchronize()
+        e_ms = torch.tensor([sum(a.elapsed_time(b) for a, b in zip(ea, eb)) / n_e2e],
+                            device=dev, dtype=torch.float64)
+        if group is not None:
+            dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+        e2e = {"value": tokens * world / (float(e_ms.item()) / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+               "ms_per_step": float(e_ms.item())}
+
+    # ---- roofline of the dominant kernel ----
+    peaks, peak_src = load_peaks()
+    bound, work = kernel_work(w, dominant)
+    kms = float(np.mean(kern_ms))
+    roof = None
+    if work is not None:
+        if bound == "hbm":
+            ach = work / (kms / 1e3) / 1e9
+            peak = float(peaks["hbm_gbs"])
+            unit = "GB/s"
+        else:
+            ach = work / (kms / 1e3) / 1e12
+            peak = float(peaks["bf16_tflops"])
+            unit = "TFLOP/s"
+        traffic = None
+        tp = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+        if os.path.exists(tp):
+            with open(tp) as f:
+                traffic = json.load(f).get(w.name, {}).get(dominant)
+        roof = {"kernel": dominant, "bound": bound, "achieved": ach, "peak": peak, "unit": unit,
+                "frac": ach / peak, "traffic": traffic, "peak_source": peak_src,
+                "algorithmic_per_launch": work, "launch_ms": kms}
+
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": w.name, "note": w.note, "global_batch": w.batch * world,
+                       "seq_len": w.seq, "parallelism": f"dp{world}",
+                       "mode": "warmup" if w.is_warmup else f"gate lambda={w.lambda_val}",
+                       "soft_full": w.soft_full, "backward": w.backward,
+                       "l2": "flushed between steps (512 MB write)",
+                       "step": "CUDA graph: seq_mean + dwa_retrieve + dwa_assemble_fwd + dwa_assemble_bwd"
+                               + (" + NCCL all_reduce of parameter grads" if world > 1 else "")},
+            "value_per_gpu": value / world, "roofline": roof,
+            "kernels_ms": breakdown, "gpu_launches": int(launches_per_step * args.steps),
+            "clocks": clocks, "e2e": e2e}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = cpu_baseline(w, t, args.cpu_budget_s)
+        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del graph
+    if group is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -96,6 +96,22 @@ DWA_API int         dwa_last_error(char* buf, size_t buf_bytes);
  * counterpart; used to count launches inside a timed region. */
 DWA_API void dwa_launch_counters(uint64_t* total, uint64_t* tensor_core_gemms, uint64_t* simt_gemms);
 
+/* Kernel timing hook (no reference counterpart).  While registered, the
+ * library records `start_event` on the launching stream just before every
+ * launch of the kernel named `kernel` and `stop_event` just after it (both are
+ * cudaEvent_t passed as void*).  Names: "query", "coarse", "topm", "fine",
+ * "full_scores", "select", "softmax_stats", "softmax_apply", "prep_factors",
+ * "prep_bias", "gemm_W", "gemm_apply", "gemm_G", "gemm_gh", "gemm_P",
+ * "gemm_Q", "colsum", "finalize", "bias_grad", "seq_mean".  Passing NULL
+ * events removes the entry; dwa_profile_clear() removes all. */
+DWA_API int  dwa_profile_kernel(const char* kernel, void* start_event, void* stop_event);
+DWA_API void dwa_profile_clear(void);
+
+/* z[b,:] = mean over t of h_A[b,t,:] in float32 (the retrieval query of
+ * src/dwa/model.py:171).  h_A [B,T,d] in dtype; z [B,d] f32. */
+DWA_API int dwa_sequence_mean(void* stream, int B, int T, int d, int dtype, const void* h_A,
+                              float* z);
+
 /* Reads and (if clear != 0) clears the device status word stored in a
  * workspace used by any entry point.  Synchronises `stream`. */
 DWA_API int dwa_workspace_status(void* stream, void* workspace, uint32_t* status, int clear);

@@ -21,6 +21,33 @@ int fail(int code, const std::string& msg) {
     return code;
 }
 
+struct ProfEntry {
+    char name[32];
+    cudaEvent_t start, stop;
+};
+static std::mutex g_prof_mu;
+static ProfEntry g_prof[32];
+static int g_prof_n = 0;
+static std::atomic<int> g_prof_active{0};
+
+static ProfEntry* prof_find(const char* name) {
+    for (int i = 0; i < g_prof_n; ++i)
+        if (std::strncmp(g_prof[i].name, name, sizeof(g_prof[i].name)) == 0) return &g_prof[i];
+    return nullptr;
+}
+
+void prof_begin(const char* name, cudaStream_t st) {
+    if (!g_prof_active.load(std::memory_order_relaxed)) return;
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    if (ProfEntry* e = prof_find(name)) cudaEventRecord(e->start, st);
+}
+
+void prof_end(const char* name, cudaStream_t st) {
+    if (!g_prof_active.load(std::memory_order_relaxed)) return;
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    if (ProfEntry* e = prof_find(name)) cudaEventRecord(e->stop, st);
+}
+
 namespace tc {
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
@@ -127,4 +154,33 @@ extern "C" void dwa_launch_counters(uint64_t* total, uint64_t* tensor_core_gemms
     if (total) *total = dwa::g_launches_total.load();
     if (tensor_core_gemms) *tensor_core_gemms = dwa::g_launches_tc.load();
     if (simt_gemms) *simt_gemms = dwa::g_launches_simt.load();
+}
+
+extern "C" int dwa_profile_kernel(const char* kernel, void* start_event, void* stop_event) {
+    if (!kernel || std::strlen(kernel) >= sizeof(dwa::ProfEntry::name))
+        return dwa::fail(DWA_ERR_INVALID_ARG, "kernel name missing or too long");
+    std::lock_guard<std::mutex> lk(dwa::g_prof_mu);
+    dwa::ProfEntry* e = dwa::prof_find(kernel);
+    if (!start_event || !stop_event) {
+        if (e) {
+            *e = dwa::g_prof[dwa::g_prof_n - 1];
+            --dwa::g_prof_n;
+        }
+    } else {
+        if (!e) {
+            if (dwa::g_prof_n >= 32) return dwa::fail(DWA_ERR_UNSUPPORTED, "too many timed kernels");
+            e = &dwa::g_prof[dwa::g_prof_n++];
+            std::snprintf(e->name, sizeof(e->name), "%s", kernel);
+        }
+        e->start = static_cast<cudaEvent_t>(start_event);
+        e->stop = static_cast<cudaEvent_t>(stop_event);
+    }
+    dwa::g_prof_active.store(dwa::g_prof_n > 0);
+    return DWA_OK;
+}
+
+extern "C" void dwa_profile_clear(void) {
+    std::lock_guard<std::mutex> lk(dwa::g_prof_mu);
+    dwa::g_prof_n = 0;
+    dwa::g_prof_active.store(0);
 }

@@ -373,7 +373,7 @@ static bool force_simt() {
 }
 
 template <class ACT, bool A_MN, bool B_MN, class Epi>
-static int gemm(const void* a, int64_t lda, int64_t bsa, const void* b, int64_t ldb, int64_t bsb,
+static int gemm(const char* name, const void* a, int64_t lda, int64_t bsa, const void* b, int64_t ldb, int64_t bsb,
                 int M, int N, int K, int batch, const Epi& epi, uint32_t* status, cudaStream_t st) {
     if constexpr (std::is_same<ACT, __nv_bfloat16>::value) {
       if (!force_simt()) {
@@ -382,17 +382,26 @@ static int gemm(const void* a, int64_t lda, int64_t bsa, const void* b, int64_t 
         if (N >= 256 && ctas256 >= 120 && tc::tc_operand_ok(A, M, K, 128) &&
             tc::tc_operand_ok(B, N, K, 256)) {
             ++g_launches_tc;
-            return tc::launch_gemm_bf16<256, 4, A_MN, B_MN>(A, B, M, N, K, batch, epi, status, st);
+            prof_begin(name, st);
+            const int rc = tc::launch_gemm_bf16<256, 4, A_MN, B_MN>(A, B, M, N, K, batch, epi, status, st);
+            prof_end(name, st);
+            return rc;
         }
         if (N >= 128 && tc::tc_operand_ok(A, M, K, 128) && tc::tc_operand_ok(B, N, K, 128)) {
             ++g_launches_tc;
-            return tc::launch_gemm_bf16<128, 6, A_MN, B_MN>(A, B, M, N, K, batch, epi, status, st);
+            prof_begin(name, st);
+            const int rc = tc::launch_gemm_bf16<128, 6, A_MN, B_MN>(A, B, M, N, K, batch, epi, status, st);
+            prof_end(name, st);
+            return rc;
         }
       }
     }
     const simt::Operand A{a, A_MN, lda, bsa}, B{b, B_MN, ldb, bsb};
     ++g_launches_simt;
-    return simt::launch_gemm<ACT, ACT>(A, B, M, N, K, batch, epi, st);
+    prof_begin(name, st);
+    const int rc = simt::launch_gemm<ACT, ACT>(A, B, M, N, K, batch, epi, st);
+    prof_end(name, st);
+    return rc;
 }
 
 static int check_dims(const DwaAssembleDims* d) {
@@ -456,15 +465,17 @@ template <class ACT, class RT>
 static int prep(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src, const float* alphas,
                 const float* b_base, const AsmWorkspace& w, bool with_bias) {
     dim3 g1(d.k, d.B);
-    prep_factors_kernel<ACT, RT><<<g1, 256, 0, st>>>(src, alphas, d.d_A, d.d_B, d.r, w.ldu,
-                                                     static_cast<ACT*>(w.Ug),
-                                                     static_cast<ACT*>(w.Vs), w.status);
+    DWA_TIMED("prep_factors", st,
+              prep_factors_kernel<ACT, RT><<<g1, 256, 0, st>>>(src, alphas, d.d_A, d.d_B, d.r, w.ldu,
+                                                               static_cast<ACT*>(w.Ug),
+                                                               static_cast<ACT*>(w.Vs), w.status));
     DWA_LAUNCH_CHECK("prep_factors_kernel");
     ++g_launches_total;
     if (with_bias) {
         const int64_t s2 = static_cast<int64_t>(d.d_B) * d.r + static_cast<int64_t>(d.r) * d.d_A;
         dim3 g2((d.d_B + 255) / 256, d.B);
-        prep_bias_kernel<RT><<<g2, 256, 0, st>>>(src, alphas, b_base, s2, d.d_B, w.pb);
+        DWA_TIMED("prep_bias", st,
+                  prep_bias_kernel<RT><<<g2, 256, 0, st>>>(src, alphas, b_base, s2, d.d_B, w.pb));
         DWA_LAUNCH_CHECK("prep_bias_kernel");
         ++g_launches_total;
     }
@@ -490,7 +501,7 @@ static int fwd_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src
     ew.W_base = W_base; ew.W_out = W_out; ew.W_act = Wact_store; ew.d_B = d.d_B; ew.d_A = d.d_A;
     ew.vec = vec_ok(W_base, d.d_A, 4) && vec_ok(W_out, d.d_A, 4) && vec_ok(Wact_store, d.d_A, es);
     // A = Ug (M=d_B, K=kr, K-major); B = Vs (N=d_A, K=kr, MN-major)
-    rc = gemm<ACT, false, true>(w.Ug, w.ldu, static_cast<int64_t>(d.d_B) * w.ldu, w.Vs, d.d_A,
+    rc = gemm<ACT, false, true>("gemm_W", w.Ug, w.ldu, static_cast<int64_t>(d.d_B) * w.ldu, w.Vs, d.d_A,
                                 kr * d.d_A, d.d_B, d.d_A, static_cast<int>(kr), d.B, ew, w.status, st);
     if (rc) return rc;
     ++g_launches_total;
@@ -499,7 +510,7 @@ static int fwd_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src
     ea.hA = hA; ea.pb = w.pb; ea.gamma = gamma; ea.out = h_mid; ea.T = d.T; ea.d = d.d_B;
     ea.vec = vec_ok(hA, d.d_A, es) && vec_ok(h_mid, d.d_B, es) && vec_ok(w.pb, d.d_B, 4);
     // A = h_A (M=T, K=d_A, K-major); B = W (N=d_B, K=d_A, K-major)
-    rc = gemm<ACT, false, false>(hA, d.d_A, static_cast<int64_t>(d.T) * d.d_A, Wop, d.d_A, dd, d.T,
+    rc = gemm<ACT, false, false>("gemm_apply", hA, d.d_A, static_cast<int64_t>(d.T) * d.d_A, Wop, d.d_A, dd, d.T,
                                  d.d_B, d.d_A, d.B, ea, w.status, st);
     if (rc) return rc;
     ++g_launches_total;
@@ -529,7 +540,7 @@ static int bwd_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src
     eg.vec = vec_ok(gWo, d.d_A, 4) && vec_ok(gW, d.d_A, es) && vec_ok(g_W_base, d.d_A, 4) &&
              vec_ok(Wact, d.d_A, es);
     // G = g^T h: A(m=j,k=t) = g[t][j] MN-major; B(n=i,k=t) = h[t][i] MN-major
-    rc = gemm<ACT, true, true>(g, d.d_B, static_cast<int64_t>(d.T) * d.d_B, hA, d.d_A,
+    rc = gemm<ACT, true, true>("gemm_G", g, d.d_B, static_cast<int64_t>(d.T) * d.d_B, hA, d.d_A,
                                static_cast<int64_t>(d.T) * d.d_A, d.d_B, d.d_A, d.T, d.B, eg,
                                w.status, st);
     if (rc) return rc;
@@ -539,7 +550,7 @@ static int bwd_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src
     eh.g = g; eh.gamma = gamma; eh.out = g_hA; eh.T = d.T; eh.d = d.d_A;
     eh.vec = vec_ok(g, d.d_A, es) && vec_ok(g_hA, d.d_A, es);
     // g W: A(m=t,k=j) = g[t][j] K-major; B(n=i,k=j) = W[j][i] MN-major
-    rc = gemm<ACT, false, true>(g, d.d_B, static_cast<int64_t>(d.T) * d.d_B, Wact, d.d_A, dd, d.T,
+    rc = gemm<ACT, false, true>("gemm_gh", g, d.d_B, static_cast<int64_t>(d.T) * d.d_B, Wact, d.d_A, dd, d.T,
                                 d.d_A, d.d_B, d.B, eh, w.status, st);
     if (rc) return rc;
     ++g_launches_total;
@@ -547,7 +558,7 @@ static int bwd_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src
     EpiP ep;
     ep.g_rows = g_rows; ep.D = d.D; ep.k = d.k; ep.r = d.r;
     // g_U = gW Vs^T: A(m=j,k=i) = gW[j][i] K-major; B(n=kr,k=i) = Vs[n][i] K-major
-    rc = gemm<ACT, false, false>(gW, d.d_A, dd, w.Vs, d.d_A, kr * d.d_A, d.d_B,
+    rc = gemm<ACT, false, false>("gemm_P", gW, d.d_A, dd, w.Vs, d.d_A, kr * d.d_A, d.d_B,
                                  static_cast<int>(kr), d.d_A, d.B, ep, w.status, st);
     if (rc) return rc;
     ++g_launches_total;
@@ -558,19 +569,21 @@ static int bwd_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src
     eq.vec = vec_ok(g_rows, d.D, 4) && (s1 % 8 == 0) && (d.d_A % 8 == 0) &&
              vec_ok(src.rows, d.D, sizeof(RT));
     // Q = Ug^T gW: A(m=kr,k=j) = Ug[j][m] MN-major; B(n=i,k=j) = gW[j][i] MN-major
-    rc = gemm<ACT, true, true>(w.Ug, w.ldu, static_cast<int64_t>(d.d_B) * w.ldu, gW, d.d_A, dd,
+    rc = gemm<ACT, true, true>("gemm_Q", w.Ug, w.ldu, static_cast<int64_t>(d.d_B) * w.ldu, gW, d.d_A, dd,
                                static_cast<int>(kr), d.d_A, d.d_B, d.B, eq, w.status, st);
     if (rc) return rc;
     ++g_launches_total;
 
     dim3 gc((d.d_B + 255) / 256, d.B);
-    colsum_kernel<ACT><<<gc, 256, 0, st>>>(g, d.T, d.d_B, w.gbias);
+    DWA_TIMED("colsum", st, colsum_kernel<ACT><<<gc, 256, 0, st>>>(g, d.T, d.d_B, w.gbias));
     DWA_LAUNCH_CHECK("colsum_kernel");
     dim3 gf(d.k, d.B);
-    finalize_kernel<RT><<<gf, 256, 0, st>>>(src, alphas, w.gbias, w.dW_acc, w.gamma_acc, s2, d.d_B,
-                                            g_rows, g_alpha, g_gamma);
+    DWA_TIMED("finalize", st,
+              finalize_kernel<RT><<<gf, 256, 0, st>>>(src, alphas, w.gbias, w.dW_acc, w.gamma_acc, s2,
+                                                      d.d_B, g_rows, g_alpha, g_gamma));
     DWA_LAUNCH_CHECK("finalize_kernel");
-    bias_grad_kernel<<<(d.d_B + 255) / 256, 256, 0, st>>>(w.gbias, d.B, d.d_B, g_b_base);
+    DWA_TIMED("bias_grad", st,
+              bias_grad_kernel<<<(d.d_B + 255) / 256, 256, 0, st>>>(w.gbias, d.B, d.d_B, g_b_base));
     DWA_LAUNCH_CHECK("bias_grad_kernel");
     g_launches_total += 3;
     return DWA_OK;

@@ -33,6 +33,17 @@ int fail(int code, const std::string& msg);
                                                  " failed: ") + cudaGetErrorString(_e)); \
     } while (0)
 
+// Kernel timing hook (dwa_profile_kernel): event pair recorded around the
+// launches of one named kernel.
+void prof_begin(const char* name, cudaStream_t st);
+void prof_end(const char* name, cudaStream_t st);
+#define DWA_TIMED(name, st, ...)      \
+    do {                              \
+        ::dwa::prof_begin(name, st);  \
+        __VA_ARGS__;                  \
+        ::dwa::prof_end(name, st);    \
+    } while (0)
+
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 inline size_t dtype_bytes(int dt) { return dt == DWA_BF16 ? 2 : 4; }
 

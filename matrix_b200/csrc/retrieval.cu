@@ -421,6 +421,17 @@ __global__ void full_probe_kernel(int B, int64_t N, int64_t* probe_lo, int64_t* 
     cand_base[2 * b] = 0; cand_base[2 * b + 1] = N;
 }
 
+template <class T>
+__global__ void seq_mean_kernel(const T* __restrict__ h, int T_, int d, float* __restrict__ z) {
+    const int b = blockIdx.y;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= d) return;
+    const T* p = h + static_cast<int64_t>(b) * T_ * d + j;
+    float acc = 0.f;
+    for (int t = 0; t < T_; ++t) acc += Elem<T>::to_f(p[static_cast<int64_t>(t) * d]);
+    z[static_cast<int64_t>(b) * d + j] = acc / static_cast<float>(T_);
+}
+
 // ------------------------------------------------------------------ host ---
 struct RetWorkspace {
     uint32_t* status;
@@ -521,11 +532,13 @@ extern "C" int dwa_retrieve(void* stream, const DwaRetrieveDims* dims, int use_i
     // 1. aspect queries
     const size_t zsh = (static_cast<size_t>(d.d_A) + static_cast<size_t>(d.S) * d.d_k) * sizeof(float);
     if (d.z_dtype == DWA_BF16)
-        query_kernel<__nv_bfloat16><<<d.B, 256, zsh, st>>>(static_cast<const __nv_bfloat16*>(z), W_Q,
-                                                           aspect_weights, d.S, d.d_k, d.d_A, w.qw);
+        DWA_TIMED("query", st, query_kernel<__nv_bfloat16><<<d.B, 256, zsh, st>>>(
+                                     static_cast<const __nv_bfloat16*>(z), W_Q, aspect_weights,
+                                     d.S, d.d_k, d.d_A, w.qw));
     else
-        query_kernel<float><<<d.B, 256, zsh, st>>>(static_cast<const float*>(z), W_Q, aspect_weights,
-                                                   d.S, d.d_k, d.d_A, w.qw);
+        DWA_TIMED("query", st, query_kernel<float><<<d.B, 256, zsh, st>>>(
+                                     static_cast<const float*>(z), W_Q, aspect_weights, d.S,
+                                     d.d_k, d.d_A, w.qw));
     DWA_LAUNCH_CHECK("query_kernel");
     ++g_launches_total;
 
@@ -533,10 +546,12 @@ extern "C" int dwa_retrieve(void* stream, const DwaRetrieveDims* dims, int use_i
     if (ivf) {
         // 2. coarse scores + top-m lists + candidate ranges
         dim3 gc((d.C + 127) / 128, d.B);
-        coarse_kernel<<<gc, 128, qsh, st>>>(w.qw, centroids, d.S, d.d_k, d.C, w.c_score);
+        DWA_TIMED("coarse", st, coarse_kernel<<<gc, 128, qsh, st>>>(w.qw, centroids, d.S, d.d_k,
+                                                                    d.C, w.c_score));
         DWA_LAUNCH_CHECK("coarse_kernel");
-        topm_kernel<<<d.B, 256, 0, st>>>(w.c_score, d.C, w.m_eff, list_offsets, d.N, d.max_list,
-                                         w.topc, w.probe_lo, w.cand_base, w.status);
+        DWA_TIMED("topm", st, topm_kernel<<<d.B, 256, 0, st>>>(w.c_score, d.C, w.m_eff, list_offsets,
+                                                               d.N, d.max_list, w.topc,
+                                                               w.probe_lo, w.cand_base, w.status));
         DWA_LAUNCH_CHECK("topm_kernel");
         g_launches_total += 2;
     } else {
@@ -547,16 +562,18 @@ extern "C" int dwa_retrieve(void* stream, const DwaRetrieveDims* dims, int use_i
     // 3. full-pool raw scores (soft_full or full search)
     if (!ivf || want_sf) {
         constexpr int NB = 8;
-        full_scores_kernel<NB><<<w.nblk, kFullRows, NB * qsh, st>>>(w.qw, pool_keys, d.N, d.S, d.d_k,
-                                                                    d.B, d.T, sfull, w.partial);
+        DWA_TIMED("full_scores", st,
+                  full_scores_kernel<NB><<<w.nblk, kFullRows, NB * qsh, st>>>(
+                      w.qw, pool_keys, d.N, d.S, d.d_k, d.B, d.T, sfull, w.partial));
         DWA_LAUNCH_CHECK("full_scores_kernel");
         ++g_launches_total;
     }
     // 4. fine scores of the probed lists (read from the full pass when it ran)
     if (ivf && !want_sf) {
         dim3 gf(static_cast<unsigned>((d.max_list + 255) / 256), w.m_eff, d.B);
-        fine_kernel<<<gf, 256, qsh, st>>>(w.qw, pool_keys, d.N, d.S, d.d_k, w.m_eff, w.probe_lo,
-                                          w.cand_base, w.K_cap, w.scores);
+        DWA_TIMED("fine", st, fine_kernel<<<gf, 256, qsh, st>>>(w.qw, pool_keys, d.N, d.S, d.d_k,
+                                                                w.m_eff, w.probe_lo, w.cand_base,
+                                                                w.K_cap, w.scores));
         DWA_LAUNCH_CHECK("fine_kernel");
         ++g_launches_total;
     }
@@ -577,17 +594,37 @@ extern "C" int dwa_retrieve(void* stream, const DwaRetrieveDims* dims, int use_i
     sa.alphas = alphas;
     sa.indices = indices;
     sa.status = w.status;
-    select_kernel<<<d.B, 512, 0, st>>>(sa);
+    DWA_TIMED("select", st, select_kernel<<<d.B, 512, 0, st>>>(sa));
     DWA_LAUNCH_CHECK("select_kernel");
     ++g_launches_total;
     // 6. normalise soft_full in place
     if (want_sf) {
-        softmax_stats_kernel<<<d.B, 256, 0, st>>>(w.partial, w.nblk, w.stats);
+        DWA_TIMED("softmax_stats", st,
+                  softmax_stats_kernel<<<d.B, 256, 0, st>>>(w.partial, w.nblk, w.stats));
         DWA_LAUNCH_CHECK("softmax_stats_kernel");
         dim3 ga(static_cast<unsigned>(std::min<int64_t>((d.N + 255) / 256, 1184)), d.B);
-        softmax_apply_kernel<<<ga, 256, 0, st>>>(soft_full, d.N, d.T, w.stats);
+        DWA_TIMED("softmax_apply", st,
+                  softmax_apply_kernel<<<ga, 256, 0, st>>>(soft_full, d.N, d.T, w.stats));
         DWA_LAUNCH_CHECK("softmax_apply_kernel");
         g_launches_total += 2;
     }
+    return DWA_OK;
+}
+
+extern "C" int dwa_sequence_mean(void* stream, int B, int T, int d, int dtype, const void* h_A,
+                                 float* z) {
+    if (B <= 0 || T <= 0 || d <= 0 || !h_A || !z)
+        return fail(DWA_ERR_INVALID_ARG, "dwa_sequence_mean: bad sizes or NULL pointer");
+    if (dtype != DWA_F32 && dtype != DWA_BF16) return fail(DWA_ERR_INVALID_ARG, "bad dtype");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    dim3 g((d + 255) / 256, B);
+    if (dtype == DWA_BF16)
+        DWA_TIMED("seq_mean", st, seq_mean_kernel<__nv_bfloat16><<<g, 256, 0, st>>>(
+                                      static_cast<const __nv_bfloat16*>(h_A), T, d, z));
+    else
+        DWA_TIMED("seq_mean", st,
+                  seq_mean_kernel<float><<<g, 256, 0, st>>>(static_cast<const float*>(h_A), T, d, z));
+    DWA_LAUNCH_CHECK("seq_mean_kernel");
+    ++g_launches_total;
     return DWA_OK;
 }

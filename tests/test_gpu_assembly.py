@@ -112,9 +112,12 @@ def test_fused_gather_equals_gathered_rows(name):
     cfg, x, idx, alphas = _setup(name, seed=3)
     a = _run(cfg, x, idx, alphas, fused=False)
     b = _run(cfg, x, idx, alphas, fused=True)
-    for u, v in zip((a[0], a[1], *a[2]), (b[0], b[1], *b[2])):
-        if u is not None:
-            assert torch.equal(u, v)
+    # h_mid, W, g_rows, g_hA have a fixed summation order: bit-identical.
+    for u, v in zip((a[0], a[1], a[2][0], a[2][2]), (b[0], b[1], b[2][0], b[2][2])):
+        assert torch.equal(u, v)
+    # g_alpha, g_W_base, g_b_base, g_gamma are accumulated with float atomics
+    for u, v in zip((a[2][1], *a[2][3:]), (b[2][1], *b[2][3:])):
+        assert_close(_np(u), _np(v), 1e-6)
 
 
 @pytest.mark.parametrize("name", ["bf16_tc", "f32_refsmall"])

@@ -70,14 +70,14 @@ def test_fine_scores_equal_full_pass_scores(case):
         np.testing.assert_array_equal(a1, a2)
 
 
-def _zipf_case(seed=7):
+def _zipf_case(seed=8):
     cfg = DWAConfig(D=17 * 64, N=20000, use_ivf=True, C=40, m=5, d_A=64, d_B=64, r=8, k_max=24,
                     S=4, d_k=64, T=1.0, gamma_init=0.1, bf16_pool=False)
     x = make_inputs(cfg, 6, 16, seed, variant="rich", zipf=1.1)
     return cfg, x
 
 
-@pytest.mark.parametrize("is_warmup,lam", [(True, 1.0), (False, 5.0), (False, -2.0)])
+@pytest.mark.parametrize("is_warmup,lam", [(True, 1.0), (False, 5.0)])
 def test_zipf_csr_lists_match_oracle(is_warmup, lam):
     cfg, x = _zipf_case()
     off = x.list_offsets
@@ -88,9 +88,12 @@ def test_zipf_csr_lists_match_oracle(is_warmup, lam):
         x.z.astype(f), x.W_Q.astype(f), x.aspect_weights.astype(f), f(x.tau),
         x.centroids.astype(f), x.keys.astype(f), k=cfg.k_max, m=cfg.m, T=cfg.T, lambda_val=lam,
         is_warmup=is_warmup, list_offsets=off, tie_break="index", return_internals=True)
+    c = np.sort(internals["c_score"], axis=1)[:, ::-1]
+    assert (c[:, cfg.m - 1] - c[:, cfg.m] > 1e-6).all(), "seed has a near-tie among lists"
     for b in range(i.shape[0]):
         s = np.sort(internals["s_i"][b])[::-1]
-        assert s[cfg.k_max - 1] - s[cfg.k_max] > 1e-6
+        assert s[cfg.k_max - 1] - s[cfg.k_max] > 1e-6, "seed has a near-tie at top-k"
+
     np.testing.assert_array_equal(i, ri)
     assert_close(a, ra, TOL, name="alphas")
     assert_close(sf, rsf, TOL, name="soft_full")
@@ -136,3 +139,29 @@ def test_module_interface_matches_reference_call():
         assert torch.allclose(al.sum(-1), torch.ones(z.shape[0], device="cuda"), atol=1e-5)
         assert (al >= 0).all() and (ix >= 0).all() and (ix < cfg.N).all()
         assert torch.allclose(sf.sum(-1), torch.ones(z.shape[0], device="cuda"), atol=1e-4)
+
+
+def test_negative_lambda_selects_a_valid_top_k_of_raw():
+    """For lambda < 0 the gate ``raw`` (retrieval.py:150-152) is not monotone in
+    s and is flat near its maximum, so fp32 and fp64 can order near-equal raw
+    values differently.  Check the selection is a top-k of raw up to 1e-5
+    relative rounding and that alphas follow retrieval.py:155 for that set."""
+    cfg, x = _zipf_case()
+    off = x.list_offsets
+    lam = -2.0
+    a, i, _ = _gpu_retrieve(cfg, x, lam, False, False, offsets=off, max_list=int(np.diff(off).max()))
+    f = np.float64
+    _, _, _, it = O.retrieve(x.z.astype(f), x.W_Q.astype(f), x.aspect_weights.astype(f), f(x.tau),
+                             x.centroids.astype(f), x.keys.astype(f), k=cfg.k_max, m=cfg.m, T=cfg.T,
+                             lambda_val=lam, is_warmup=False, list_offsets=off,
+                             return_internals=True)
+    for b in range(i.shape[0]):
+        s, cand = it["s_i"][b], it["cands"][b]
+        raw = O.sigmoid(lam * (s - x.tau)) * np.exp(s / cfg.T)
+        raw = raw / (raw.sum() + 1e-8)
+        kth = np.sort(raw)[::-1][cfg.k_max - 1]
+        # candidates of one query are distinct rows: look up raw by row
+        sel = raw[np.argsort(cand)][np.searchsorted(np.sort(cand), i[b])]
+        assert len(set(i[b].tolist())) == cfg.k_max
+        assert (sel >= kth * (1 - 1e-5)).all()
+        assert_close(a[b], sel / (sel.sum() + 1e-8), TOL, name="alphas")
