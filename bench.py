@@ -177,21 +177,23 @@ def profile_kernels(step, flush, n=5):
     lib = _lib.load()
     ev = {k: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for k in KERNELS}
+    for a, b in ev.values():     # torch creates the CUDA event on its first record
+        a.record(); b.record()
+    torch.cuda.synchronize()
     for k, (a, b) in ev.items():
         lib.dwa_profile_kernel(k.encode(), C_ptr(a), C_ptr(b))
     acc = {k: [] for k in KERNELS}
     for _ in range(n):
         flush()
-        # events of kernels that do not run this step keep an old record: mark them
-        for a, b in ev.values():
-            a.record(); b.record()
         torch.cuda.synchronize()
+        t_step = torch.cuda.Event(enable_timing=True)
+        t_step.record()
         step()
         torch.cuda.synchronize()
         for k, (a, b) in ev.items():
-            ms = a.elapsed_time(b)
-            if ms > 0:
-                acc[k].append(ms)
+            # a kernel that did not run this step still holds an earlier record
+            if t_step.elapsed_time(a) >= 0:
+                acc[k].append(a.elapsed_time(b))
     lib.dwa_profile_clear()
     return {k: float(np.mean(v)) for k, v in acc.items() if v}
 
@@ -376,6 +378,8 @@ def main():
     # capture the step in a CUDA graph, with the dominant kernel's events inside
     lib = _lib.load()
     ka, kb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ka.record(); kb.record()     # the library re-records both inside every graph replay
+    torch.cuda.synchronize()
     lib.dwa_profile_kernel(dominant.encode(), C_ptr(ka), C_ptr(kb))
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
@@ -400,6 +404,7 @@ def main():
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     stops = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     kern_ms = []
+    kern_src = "graph replay (external event nodes)"
     if group is not None:
         dist.barrier()
     torch.cuda.synchronize()
@@ -409,11 +414,27 @@ def main():
         graph.replay()
         stops[i].record()
         stops[i].synchronize()
-        kern_ms.append(ka.elapsed_time(kb))
+        if kern_src is not None:
+            try:
+                kern_ms.append(ka.elapsed_time(kb))
+            except Exception:  # noqa: BLE001  (no timing on graph-recorded events)
+                kern_src, kern_ms = None, []
     torch.cuda.synchronize()
     if group is not None:
         dist.barrier()
     clocks = sampler.stop()
+    if kern_src is None:
+        # time the dominant kernel's launches in eager steps, same flush discipline
+        kern_src = "eager steps"
+        ka, kb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ka.record(); kb.record()
+        lib.dwa_profile_kernel(dominant.encode(), C_ptr(ka), C_ptr(kb))
+        for i in range(min(args.steps, 50)):
+            flush()
+            step()
+            torch.cuda.synchronize()
+            kern_ms.append(ka.elapsed_time(kb))
+        lib.dwa_profile_clear()
     step_ms = float(sum(a.elapsed_time(b) for a, b in zip(starts, stops)))
     tmax = torch.tensor([step_ms], device=dev, dtype=torch.float64)
     if group is not None:
@@ -480,7 +501,7 @@ def main():
                 traffic = json.load(f).get(w.name, {}).get(dominant)
         roof = {"kernel": dominant, "bound": bound, "achieved": ach, "peak": peak, "unit": unit,
                 "frac": ach / peak, "traffic": traffic, "peak_source": peak_src,
-                "algorithmic_per_launch": work, "launch_ms": kms}
+                "algorithmic_per_launch": work, "launch_ms": kms, "timed_in": kern_src}
 
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,

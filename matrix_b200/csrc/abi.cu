@@ -36,16 +36,26 @@ static ProfEntry* prof_find(const char* name) {
     return nullptr;
 }
 
+// Inside a stream capture the record becomes an external event node of the
+// graph, so every replay records the event again.
+static void prof_record(cudaEvent_t ev, cudaStream_t st) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusActive)
+        cudaEventRecordWithFlags(ev, st, cudaEventRecordExternal);
+    else
+        cudaEventRecord(ev, st);
+}
+
 void prof_begin(const char* name, cudaStream_t st) {
     if (!g_prof_active.load(std::memory_order_relaxed)) return;
     std::lock_guard<std::mutex> lk(g_prof_mu);
-    if (ProfEntry* e = prof_find(name)) cudaEventRecord(e->start, st);
+    if (ProfEntry* e = prof_find(name)) prof_record(e->start, st);
 }
 
 void prof_end(const char* name, cudaStream_t st) {
     if (!g_prof_active.load(std::memory_order_relaxed)) return;
     std::lock_guard<std::mutex> lk(g_prof_mu);
-    if (ProfEntry* e = prof_find(name)) cudaEventRecord(e->stop, st);
+    if (ProfEntry* e = prof_find(name)) prof_record(e->stop, st);
 }
 
 namespace tc {
