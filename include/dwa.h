@@ -181,6 +181,32 @@ DWA_API int dwa_retrieve(void* stream, const DwaRetrieveDims* dims, int use_ivf,
                  float* alphas, int32_t* indices, float* soft_full,
                  void* workspace, size_t workspace_bytes);
 
+/* ---------------------------------------------------------------------------
+ * Retrieval without a workspace.  No counterpart in the reference: it exists for
+ * callers that cannot hand this library scratch memory or let it allocate, such
+ * as a legacy XLA custom-call target that receives only its operand and result
+ * buffers, or code that runs while a CUDA stream is being captured, where
+ * cudaMalloc is not allowed.  Same arguments and results as dwa_retrieve minus
+ * the workspace; the scratch is a fixed 8 MiB device array inside libdwa that
+ * every GPU loading the library keeps until the process exits.
+ *  - Shapes whose scratch need (dwa_retrieve_workspace_bytes) exceeds 8 MiB are
+ *    rejected with DWA_ERR_UNSUPPORTED and a message; nothing is launched.
+ *  - The first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress) and caches it; make that first call before any
+ *    stream capture.
+ *  - Allocates nothing (no cudaMalloc / cudaFree, no allocating library call).
+ *  - All calls share the one array: calls that overlap on the GPU (other
+ *    streams, other threads) race and must be serialised by the caller.
+ *  - The device status word lives in that shared scratch and cannot be read
+ *    back; use dwa_retrieve for runs that check it.
+ * ------------------------------------------------------------------------- */
+DWA_API int dwa_retrieve_noalloc(void* stream, const DwaRetrieveDims* dims, int use_ivf,
+                                 int is_warmup, const float* lambda_val, const void* z,
+                                 const float* W_Q, const float* aspect_weights, const float* tau,
+                                 const float* centroids, const int64_t* list_offsets,
+                                 const float* pool_keys, float* alphas, int32_t* indices,
+                                 float* soft_full);
+
 #ifdef __cplusplus
 }
 #endif

@@ -62,6 +62,8 @@ _SIGNATURES = {
     "dwa_retrieve_workspace_bytes": (C.c_size_t, [C.POINTER(RetrieveDims), C.c_int, C.c_int]),
     "dwa_retrieve": (C.c_int, [_P, C.POINTER(RetrieveDims), C.c_int, C.c_int, _P, _P, _P, _P, _P,
                                _P, _P, _P, _P, _P, _P, _P, C.c_size_t]),
+    "dwa_retrieve_noalloc": (C.c_int, [_P, C.POINTER(RetrieveDims), C.c_int, C.c_int, _P, _P, _P,
+                                       _P, _P, _P, _P, _P, _P, _P, _P]),
 }
 
 _lib = None

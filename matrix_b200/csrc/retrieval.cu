@@ -16,6 +16,7 @@
 // All scoring is bound by HBM reads of the fp32 key cache.
 #include <algorithm>
 #include <atomic>
+#include <mutex>
 
 #include "dwa_common.cuh"
 
@@ -627,4 +628,62 @@ extern "C" int dwa_sequence_mean(void* stream, int B, int T, int d, int dtype, c
     DWA_LAUNCH_CHECK("seq_mean_kernel");
     ++g_launches_total;
     return DWA_OK;
+}
+
+// ---------------------------------------------------- allocation-free ---
+// dwa_retrieve_noalloc runs the retrieval above with its scratch taken from
+// this file-scope device array instead of a caller workspace.  Every GPU that
+// loads libdwa keeps these 8 MiB until the process exits.  In host code the
+// name g_retrieve_scratch is only a stand-in for the symbol, not a device
+// address: the address a kernel may use comes from cudaGetSymbolAddress, once
+// per device, with that device current.
+namespace dwa {
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
+static __device__ __align__(256) unsigned char g_retrieve_scratch[kNoAllocScratchBytes];
+
+static std::mutex g_scratch_mu;
+static void* g_scratch_addr[64];
+
+static int scratch_address(void** out) {
+    int dev = 0;
+    DWA_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(DWA_ERR_UNSUPPORTED, "device ordinal above 63");
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (!g_scratch_addr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_retrieve_scratch);
+        if (e != cudaSuccess || p == nullptr)
+            return fail(DWA_ERR_CUDA, std::string("cudaGetSymbolAddress(g_retrieve_scratch): ") +
+                                          cudaGetErrorString(e));
+        g_scratch_addr[dev] = p;
+    }
+    *out = g_scratch_addr[dev];
+    return DWA_OK;
+}
+}  // namespace dwa
+
+extern "C" int dwa_retrieve_noalloc(void* stream, const DwaRetrieveDims* dims, int use_ivf,
+                                    int is_warmup, const float* lambda_val, const void* z,
+                                    const float* W_Q, const float* aspect_weights,
+                                    const float* tau, const float* centroids,
+                                    const int64_t* list_offsets, const float* pool_keys,
+                                    float* alphas, int32_t* indices, float* soft_full) {
+    int rc = check_ret(dims, use_ivf);
+    if (rc) return rc;
+    const size_t need = carve_ret(nullptr, *dims, use_ivf != 0, soft_full != nullptr).bytes;
+    if (need > kNoAllocScratchBytes)
+        return fail(DWA_ERR_UNSUPPORTED,
+                    "dwa_retrieve_noalloc: this shape needs " + std::to_string(need) +
+                        " bytes of scratch but the built-in scratch holds " +
+                        std::to_string(kNoAllocScratchBytes) +
+                        " bytes; call dwa_retrieve with a caller workspace");
+    void* scratch = nullptr;
+    if ((rc = scratch_address(&scratch))) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // The scratch keeps the previous call's bytes; only the status word must
+    // start at zero (every other byte is written before it is read).
+    DWA_CUDA_TRY(cudaMemsetAsync(scratch, 0, 256, st));
+    return dwa_retrieve(stream, dims, use_ivf, is_warmup, lambda_val, z, W_Q, aspect_weights, tau,
+                        centroids, list_offsets, pool_keys, alphas, indices, soft_full, scratch,
+                        kNoAllocScratchBytes);
 }
