@@ -96,6 +96,11 @@ WORKLOADS: dict[str, Workload] = {
                       note="bf16, batch 32, seq 2048, d 2048, pool 4M, 4096 Zipf(1.1) lists, nprobe 32, top-k 64"),
     "decode": Workload("decode", _cfg(4096, 1 << 21, 2048, 16, 64, "bfloat16"), 64, 1, False,
                        note="bf16, batch 1-256, seq 1, d 4096, pool 2M, 2048 lists, nprobe 16, top-k 16-128"),
+    # reduced cases for detailed ncu captures (a few GB on the device)
+    "profile_keys": Workload("profile_keys", _cfg(512, 131072, 256, 8, 32, "bfloat16"), 8, 512, True,
+                             note="ncu case: key cache 134 MB (> L2), pool 2.3 GB; small shapes otherwise"),
+    "profile_gemm": Workload("profile_gemm", _cfg(1024, 16384, 32, 8, 32, "bfloat16"), 8, 512, True,
+                             note="ncu case: the small workload's GEMM shapes with a 0.57 GB pool"),
 }
 
 

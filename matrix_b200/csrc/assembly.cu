@@ -55,43 +55,33 @@ struct RowSrc {
 };
 
 // ------------------------------------------------------- vector helpers ----
-__device__ __forceinline__ void load32(const float* p, float* v) {
-    const float4* q = reinterpret_cast<const float4*>(p);
+// 8 consecutive elements through 16-byte accesses (the pointer must be 16-byte
+// aligned for bf16, 16-byte aligned for fp32 pairs of float4).
+__device__ __forceinline__ void load8(const float* p, float* v) {
+    const float4 a = reinterpret_cast<const float4*>(p)[0];
+    const float4 b = reinterpret_cast<const float4*>(p)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float* v) {
+    const uint4 t = *reinterpret_cast<const uint4*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&t);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const float4 t = q[i];
-        v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+    for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        v[2 * j] = f.x;
+        v[2 * j + 1] = f.y;
     }
 }
-__device__ __forceinline__ void load32(const __nv_bfloat16* p, float* v) {
-    const uint4* q = reinterpret_cast<const uint4*>(p);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint4 t = q[i];
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&t);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float2 f = __bfloat1622float2(h[j]);
-            v[8 * i + 2 * j] = f.x;
-            v[8 * i + 2 * j + 1] = f.y;
-        }
-    }
+__device__ __forceinline__ void store8(float* p, const float* v) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
 }
-__device__ __forceinline__ void store32(float* p, const float* v) {
-    float4* q = reinterpret_cast<float4*>(p);
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float* v) {
+    uint4 t;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&t);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) q[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-}
-__device__ __forceinline__ void store32(__nv_bfloat16* p, const float* v) {
-    uint4* q = reinterpret_cast<uint4*>(p);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        uint4 t;
-        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&t);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(v[8 * i + 2 * j], v[8 * i + 2 * j + 1]);
-        q[i] = t;
-    }
+    for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+    *reinterpret_cast<uint4*>(p) = t;
 }
 __device__ __forceinline__ void red_add4(float* p, float a, float b, float c, float d) {
     asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
@@ -113,13 +103,13 @@ struct EpiW : NoReduce {
     __device__ float operator()(int b, int row, int col0, const float* v, int cnt) const {
         const int64_t o = (static_cast<int64_t>(b) * d_B + row) * d_A + col0;
         const float* wb = W_base + static_cast<int64_t>(row) * d_A + col0;
-        if (vec && cnt == 32) {
-            float w[32];
-            load32(wb, w);
+        if (vec && cnt == 8) {
+            float w[8];
+            load8(wb, w);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) w[i] += v[i];
-            if (W_out) store32(W_out + o, w);
-            if (W_act) store32(W_act + o, w);
+            for (int i = 0; i < 8; ++i) w[i] += v[i];
+            if (W_out) store8(W_out + o, w);
+            if (W_act) store8(W_act + o, w);
         } else {
             for (int c = 0; c < cnt; ++c) {
                 const float w = wb[c] + v[c];
@@ -139,13 +129,13 @@ struct EpiApply : NoReduce {
         const int64_t o = (static_cast<int64_t>(b) * T + row) * d + col0;
         const float* p = pb + static_cast<int64_t>(b) * d + col0;
         const float g = __ldg(gamma);
-        if (vec && cnt == 32) {
-            float h[32], q[32];
-            load32(hA + o, h);
-            load32(p, q);
+        if (vec && cnt == 8) {
+            float h[8], q[8];
+            load8(hA + o, h);
+            load8(p, q);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) h[i] = h[i] + g * v[i] + q[i];
-            store32(out + o, h);
+            for (int i = 0; i < 8; ++i) h[i] = h[i] + g * v[i] + q[i];
+            store8(out + o, h);
         } else {
             for (int c = 0; c < cnt; ++c)
                 out[o + c] = Elem<ACT>::from_f(Elem<ACT>::to_f(hA[o + c]) + g * v[c] + p[c]);
@@ -165,22 +155,23 @@ struct EpiG {
         const int64_t ob = static_cast<int64_t>(row) * d_A + col0;
         const float g = __ldg(gamma);
         float part = 0.f;
-        if (vec && cnt == 32) {
-            float w[32], x[32];
-            load32(Wact + o, w);
+        if (vec && cnt == 8) {
+            float w[8], x[8];
+            load8(Wact + o, w);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) part = fmaf(v[i], w[i], part);
+            for (int i = 0; i < 8; ++i) part = fmaf(v[i], w[i], part);
             if (gWo) {
-                load32(gWo + o, x);
+                load8(gWo + o, x);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) x[i] = fmaf(g, v[i], x[i]);
+                for (int i = 0; i < 8; ++i) x[i] = fmaf(g, v[i], x[i]);
             } else {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) x[i] = g * v[i];
+                for (int i = 0; i < 8; ++i) x[i] = g * v[i];
             }
-            store32(gW + o, x);
+            store8(gW + o, x);
 #pragma unroll
-            for (int i = 0; i < 32; i += 4) red_add4(gWbase + ob + i, x[i], x[i + 1], x[i + 2], x[i + 3]);
+            red_add4(gWbase + ob, x[0], x[1], x[2], x[3]);
+            red_add4(gWbase + ob + 4, x[4], x[5], x[6], x[7]);
         } else {
             for (int c = 0; c < cnt; ++c) {
                 part = fmaf(v[c], Elem<ACT>::to_f(Wact[o + c]), part);
@@ -202,12 +193,12 @@ struct EpiGhA : NoReduce {
     __device__ float operator()(int b, int row, int col0, const float* v, int cnt) const {
         const int64_t o = (static_cast<int64_t>(b) * T + row) * d + col0;
         const float gm = __ldg(gamma);
-        if (vec && cnt == 32) {
-            float x[32];
-            load32(g + o, x);
+        if (vec && cnt == 8) {
+            float x[8];
+            load8(g + o, x);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) x[i] = fmaf(gm, v[i], x[i]);
-            store32(out + o, x);
+            for (int i = 0; i < 8; ++i) x[i] = fmaf(gm, v[i], x[i]);
+            store8(out + o, x);
         } else {
             for (int c = 0; c < cnt; ++c)
                 out[o + c] = Elem<ACT>::from_f(fmaf(gm, v[c], Elem<ACT>::to_f(g[o + c])));
@@ -218,8 +209,12 @@ struct EpiGhA : NoReduce {
 
 // g_U: g_rows[b][kk][j*r + rho] = acc(j, kk*r + rho)
 struct EpiP : NoReduce {
-    float* g_rows; int64_t D; int k, r;
+    float* g_rows; int64_t D; int k, r; bool vec;
     __device__ float operator()(int b, int row, int col0, const float* v, int cnt) const {
+        if (vec && cnt == 8 && r == 8) {   // the 8 columns are the 8 factors of one pool row
+            store8(g_rows + (static_cast<int64_t>(b) * k + col0 / 8) * D + static_cast<int64_t>(row) * 8, v);
+            return 0.f;
+        }
         for (int c = 0; c < cnt; ++c) {
             const int n = col0 + c;
             const int kk = n / r, rho = n - kk * r;
@@ -245,15 +240,15 @@ struct EpiQ {
                              : static_cast<const RT*>(src.rows) + ro + s1 +
                                    static_cast<int64_t>(rho) * d_A + col0;
         float part = 0.f;
-        if (vec && cnt == 32) {
-            float x[32];
+        if (vec && cnt == 8) {
+            float x[8];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) x[i] = a * v[i];
-            store32(g_rows + go, x);
+            for (int i = 0; i < 8; ++i) x[i] = a * v[i];
+            store8(g_rows + go, x);
             if (V) {
-                load32(V, x);
+                load8(V, x);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) part = fmaf(x[i], v[i], part);
+                for (int i = 0; i < 8; ++i) part = fmaf(x[i], v[i], part);
             }
         } else {
             for (int c = 0; c < cnt; ++c) {
@@ -295,32 +290,58 @@ __global__ void prep_factors_kernel(RowSrc src, const float* __restrict__ alphas
     }
 }
 
-template <class RT>
-__global__ void prep_bias_kernel(RowSrc src, const float* __restrict__ alphas,
-                                 const float* __restrict__ b_base, int64_t s2, int d_B,
-                                 float* __restrict__ pb) {
-    const int b = blockIdx.y;
-    const int j = blockIdx.x * blockDim.x + threadIdx.x;
-    if (j >= d_B) return;
-    float acc = 0.f;
-    for (int kk = 0; kk < src.k; ++kk) {
-        const int64_t off = src.offset(b, kk);
-        if (off < 0) continue;
-        acc = fmaf(alphas[static_cast<int64_t>(b) * src.k + kk],
-                   Elem<RT>::to_f(static_cast<const RT*>(src.rows)[off + s2 + j]), acc);
+// bf16 rows, bf16 activations, r == 8: one 16-byte vector per (row j, k) of U
+// (its 8 factors) and per 8 elements of V.
+__global__ void __launch_bounds__(256) prep_factors_bf16_r8_kernel(
+    RowSrc src, const float* __restrict__ alphas, int d_A, int d_B, int64_t ldu,
+    __nv_bfloat16* __restrict__ Ug, __nv_bfloat16* __restrict__ Vs, uint32_t* status) {
+    const int kk = blockIdx.x, b = blockIdx.y, k = src.k;
+    const int64_t off = src.offset(b, kk);
+    if (off < 0 && threadIdx.x == 0) raise_status(status, DWA_STATUS_BAD_ROW_INDEX);
+    const uint4* row = off < 0 ? nullptr
+                               : reinterpret_cast<const uint4*>(
+                                     static_cast<const __nv_bfloat16*>(src.rows) + off);
+    const float a = alphas[static_cast<int64_t>(b) * k + kk];
+    const uint4 zero = make_uint4(0, 0, 0, 0);
+    __nv_bfloat16* ug = Ug + static_cast<int64_t>(b) * d_B * ldu + static_cast<int64_t>(kk) * 8;
+    for (int j = threadIdx.x; j < d_B; j += blockDim.x)
+        *reinterpret_cast<uint4*>(ug + static_cast<int64_t>(j) * ldu) = row ? __ldg(row + j) : zero;
+    const int64_t kr = static_cast<int64_t>(k) * 8;
+    uint4* vs = reinterpret_cast<uint4*>(Vs + (static_cast<int64_t>(b) * kr + static_cast<int64_t>(kk) * 8) * d_A);
+    const int nv = d_A;  // 8 rows of d_A elements = d_A vectors of 8
+    for (int e = threadIdx.x; e < nv; e += blockDim.x) {
+        uint4 v = row ? __ldg(row + d_B + e) : zero;
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h[i]);
+            h[i] = __floats2bfloat162_rn(a * f.x, a * f.y);
+        }
+        vs[e] = v;
     }
-    pb[static_cast<int64_t>(b) * d_B + j] = b_base[j] + acc;
 }
 
-template <class ACT>
-__global__ void colsum_kernel(const ACT* __restrict__ g, int T, int d, float* __restrict__ out) {
+// pb[b][j] = b_base[j] + sum_k alpha[b,k] b_k[j]: the k row offsets are read
+// once into shared memory so the k loads of a column are independent.
+template <class RT>
+__global__ void __launch_bounds__(256) prep_bias_kernel(RowSrc src, const float* __restrict__ alphas,
+                                                        const float* __restrict__ b_base, int64_t s2,
+                                                        int d_B, float* __restrict__ pb) {
+    extern __shared__ int64_t offs[];   // [k]
     const int b = blockIdx.y;
+    for (int kk = threadIdx.x; kk < src.k; kk += blockDim.x) offs[kk] = src.offset(b, kk);
+    __syncthreads();
     const int j = blockIdx.x * blockDim.x + threadIdx.x;
-    if (j >= d) return;
-    const ACT* p = g + static_cast<int64_t>(b) * T * d + j;
+    if (j >= d_B) return;
+    const RT* rows = static_cast<const RT*>(src.rows);
+    const float* a = alphas + static_cast<int64_t>(b) * src.k;
     float acc = 0.f;
-    for (int t = 0; t < T; ++t) acc += Elem<ACT>::to_f(p[static_cast<int64_t>(t) * d]);
-    out[static_cast<int64_t>(b) * d + j] = acc;
+#pragma unroll 8
+    for (int kk = 0; kk < src.k; ++kk) {
+        const int64_t off = offs[kk];
+        if (off >= 0) acc = fmaf(a[kk], Elem<RT>::to_f(rows[off + s2 + j]), acc);
+    }
+    pb[static_cast<int64_t>(b) * d_B + j] = b_base[j] + acc;
 }
 
 template <class RT>
@@ -465,17 +486,27 @@ template <class ACT, class RT>
 static int prep(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src, const float* alphas,
                 const float* b_base, const AsmWorkspace& w, bool with_bias) {
     dim3 g1(d.k, d.B);
-    DWA_TIMED("prep_factors", st,
-              prep_factors_kernel<ACT, RT><<<g1, 256, 0, st>>>(src, alphas, d.d_A, d.d_B, d.r, w.ldu,
-                                                               static_cast<ACT*>(w.Ug),
-                                                               static_cast<ACT*>(w.Vs), w.status));
+    const bool vec8 = std::is_same<ACT, __nv_bfloat16>::value && std::is_same<RT, __nv_bfloat16>::value &&
+                      d.r == 8 && d.D % 8 == 0 && d.d_A % 8 == 0 && w.ldu % 8 == 0 &&
+                      reinterpret_cast<uintptr_t>(src.rows) % 16 == 0;
+    if (vec8)
+        DWA_TIMED("prep_factors", st,
+                  prep_factors_bf16_r8_kernel<<<g1, 256, 0, st>>>(
+                      src, alphas, d.d_A, d.d_B, w.ldu, static_cast<__nv_bfloat16*>(w.Ug),
+                      static_cast<__nv_bfloat16*>(w.Vs), w.status));
+    else
+        DWA_TIMED("prep_factors", st,
+                  prep_factors_kernel<ACT, RT><<<g1, 256, 0, st>>>(src, alphas, d.d_A, d.d_B, d.r,
+                                                                   w.ldu, static_cast<ACT*>(w.Ug),
+                                                                   static_cast<ACT*>(w.Vs), w.status));
     DWA_LAUNCH_CHECK("prep_factors_kernel");
     ++g_launches_total;
     if (with_bias) {
         const int64_t s2 = static_cast<int64_t>(d.d_B) * d.r + static_cast<int64_t>(d.r) * d.d_A;
         dim3 g2((d.d_B + 255) / 256, d.B);
         DWA_TIMED("prep_bias", st,
-                  prep_bias_kernel<RT><<<g2, 256, 0, st>>>(src, alphas, b_base, s2, d.d_B, w.pb));
+                  prep_bias_kernel<RT><<<g2, 256, d.k * sizeof(int64_t), st>>>(src, alphas, b_base, s2,
+                                                                              d.d_B, w.pb));
         DWA_LAUNCH_CHECK("prep_bias_kernel");
         ++g_launches_total;
     }
@@ -557,6 +588,7 @@ static int bwd_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src
 
     EpiP ep;
     ep.g_rows = g_rows; ep.D = d.D; ep.k = d.k; ep.r = d.r;
+    ep.vec = vec_ok(g_rows, d.D, 4);
     // g_U = gW Vs^T: A(m=j,k=i) = gW[j][i] K-major; B(n=kr,k=i) = Vs[n][i] K-major
     rc = gemm<ACT, false, false>("gemm_P", gW, d.d_A, dd, w.Vs, d.d_A, kr * d.d_A, d.d_B,
                                  static_cast<int>(kr), d.d_A, d.B, ep, w.status, st);
@@ -574,8 +606,8 @@ static int bwd_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src
     if (rc) return rc;
     ++g_launches_total;
 
-    dim3 gc((d.d_B + 255) / 256, d.B);
-    DWA_TIMED("colsum", st, colsum_kernel<ACT><<<gc, 256, 0, st>>>(g, d.T, d.d_B, w.gbias));
+    dim3 gc((d.d_B + 63) / 64, d.B);
+    DWA_TIMED("colsum", st, column_sum_kernel<ACT><<<gc, 1024, 0, st>>>(g, d.T, d.d_B, 0, w.gbias));
     DWA_LAUNCH_CHECK("colsum_kernel");
     dim3 gf(d.k, d.B);
     DWA_TIMED("finalize", st,

@@ -115,4 +115,41 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// out[b][j] = sum_t x[b][t][j]   (divided by T when `mean`), x [B, T, d].
+// Grid (ceil(d/64), B), 1024 threads: lane l of warp w sums columns c0+2l,
+// c0+2l+1 over rows t = w, w+32, ... (16 loads in flight per thread); the 32
+// warp partials are then added in a fixed order, so the result is
+// deterministic.
+template <class T>
+__global__ void __launch_bounds__(1024) column_sum_kernel(const T* __restrict__ x, int T_, int d,
+                                                          int mean, float* __restrict__ out) {
+    __shared__ float part[32][65];
+    const int b = blockIdx.y, lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int c = blockIdx.x * 64 + 2 * lane;
+    const T* p = x + static_cast<int64_t>(b) * T_ * d;
+    float a0 = 0.f, a1 = 0.f;
+    for (int t0 = w; t0 < T_; t0 += 32 * 16) {
+        float v0[16], v1[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+            const int t = t0 + 32 * u;
+            const T* q = p + static_cast<int64_t>(t) * d;
+            v0[u] = (t < T_ && c < d) ? Elem<T>::to_f(q[c]) : 0.f;
+            v1[u] = (t < T_ && c + 1 < d) ? Elem<T>::to_f(q[c + 1]) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 16; ++u) { a0 += v0[u]; a1 += v1[u]; }
+    }
+    part[w][2 * lane] = a0;
+    part[w][2 * lane + 1] = a1;
+    __syncthreads();
+    if (threadIdx.x < 64) {
+        const int j = blockIdx.x * 64 + threadIdx.x;
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s += part[i][threadIdx.x];
+        if (j < d) out[static_cast<int64_t>(b) * d + j] = mean ? s / static_cast<float>(T_) : s;
+    }
+}
+
 }  // namespace dwa

@@ -19,6 +19,7 @@
 #include <mutex>
 
 #include "dwa_common.cuh"
+#include "tc_gemm.cuh"
 
 namespace dwa {
 
@@ -28,37 +29,55 @@ constexpr int kMaxK = 256;  // top-k / top-m capacity of the block selection
 
 // ------------------------------------------------------------- scoring -----
 // sc[q] = sum_s (qw[q][s] . key_s) / (sqrt(|key_s|^2) + 1e-8)   for one row.
-template <int NB>
+// DK > 0: d_k is the compile-time DK (fully unrolled, all loads of an aspect in
+// flight at once); DK == 0: runtime d_k.  For a given row and query the
+// operations and their order do not depend on NB, so the fine pass (NB = 1)
+// and the full pass (NB > 1) give bit-identical scores.
+template <int NB, int DK>
 __device__ __forceinline__ void row_scores(const float* __restrict__ keys, int64_t N, int S,
                                            int d_k, int64_t row, const float* qw, int nb,
                                            float* sc) {
 #pragma unroll
     for (int q = 0; q < NB; ++q) sc[q] = 0.f;
-    for (int s = 0; s < S; ++s) {
-        const float* kp = keys + (static_cast<int64_t>(s) * N + row) * d_k;
-        float dot[NB];
+    if constexpr (DK > 0) {
+        for (int s = 0; s < S; ++s) {
+            const float4* kp = reinterpret_cast<const float4*>(keys + (static_cast<int64_t>(s) * N + row) * DK);
+            float4 kv[DK / 4];
 #pragma unroll
-        for (int q = 0; q < NB; ++q) dot[q] = 0.f;
-        float nrm = 0.f;
-        if ((d_k & 3) == 0) {
-            for (int d = 0; d < d_k; d += 4) {
-                const float4 kv = __ldg(reinterpret_cast<const float4*>(kp + d));
-                nrm = fmaf(kv.x, kv.x, nrm);
-                nrm = fmaf(kv.y, kv.y, nrm);
-                nrm = fmaf(kv.z, kv.z, nrm);
-                nrm = fmaf(kv.w, kv.w, nrm);
+            for (int c = 0; c < DK / 4; ++c) kv[c] = __ldg(kp + c);
+            float nrm = 0.f;
 #pragma unroll
-                for (int q = 0; q < NB; ++q) {
-                    if (q < nb) {
-                        const float* qq = qw + (q * S + s) * d_k + d;
-                        dot[q] = fmaf(kv.x, qq[0], dot[q]);
-                        dot[q] = fmaf(kv.y, qq[1], dot[q]);
-                        dot[q] = fmaf(kv.z, qq[2], dot[q]);
-                        dot[q] = fmaf(kv.w, qq[3], dot[q]);
+            for (int c = 0; c < DK / 4; ++c) {
+                nrm = fmaf(kv[c].x, kv[c].x, nrm);
+                nrm = fmaf(kv[c].y, kv[c].y, nrm);
+                nrm = fmaf(kv[c].z, kv[c].z, nrm);
+                nrm = fmaf(kv[c].w, kv[c].w, nrm);
+            }
+            const float den = sqrtf(nrm) + 1e-8f;
+#pragma unroll
+            for (int q = 0; q < NB; ++q) {
+                if (q < nb) {
+                    const float4* qq = reinterpret_cast<const float4*>(qw + (q * S + s) * DK);
+                    float dot = 0.f;
+#pragma unroll
+                    for (int c = 0; c < DK / 4; ++c) {
+                        const float4 qv = qq[c];
+                        dot = fmaf(kv[c].x, qv.x, dot);
+                        dot = fmaf(kv[c].y, qv.y, dot);
+                        dot = fmaf(kv[c].z, qv.z, dot);
+                        dot = fmaf(kv[c].w, qv.w, dot);
                     }
+                    sc[q] += dot / den;
                 }
             }
-        } else {
+        }
+    } else {
+        for (int s = 0; s < S; ++s) {
+            const float* kp = keys + (static_cast<int64_t>(s) * N + row) * d_k;
+            float dot[NB];
+#pragma unroll
+            for (int q = 0; q < NB; ++q) dot[q] = 0.f;
+            float nrm = 0.f;
             for (int d = 0; d < d_k; ++d) {
                 const float x = __ldg(kp + d);
                 nrm = fmaf(x, x, nrm);
@@ -66,11 +85,20 @@ __device__ __forceinline__ void row_scores(const float* __restrict__ keys, int64
                 for (int q = 0; q < NB; ++q)
                     if (q < nb) dot[q] = fmaf(x, qw[(q * S + s) * d_k + d], dot[q]);
             }
-        }
-        const float den = sqrtf(nrm) + 1e-8f;
+            const float den = sqrtf(nrm) + 1e-8f;
 #pragma unroll
-        for (int q = 0; q < NB; ++q) sc[q] += dot[q] / den;
+            for (int q = 0; q < NB; ++q) sc[q] += dot[q] / den;
+        }
     }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, uint64_t* bar, int c0,
+                                            int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(tc::smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(tc::smem_u32(bar)), "r"(c0), "r"(c1)
+        : "memory");
 }
 
 __device__ __forceinline__ uint32_t float_ord(float f) {
@@ -121,15 +149,33 @@ __device__ int block_topk(int64_t n, int k, const KeyAt& key_at, uint64_t* sel_k
             if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 0xFF], 1u);
         }
         __syncthreads();
-        if (tid == 0) {
-            int acc = 0, dsel = 0;
-            for (int dg = 255; dg >= 0; --dg) {
-                if (acc + static_cast<int>(hist[dg]) >= kleft) { dsel = dg; break; }
-                acc += static_cast<int>(hist[dg]);
+        if (tid < 32) {
+            // warp 0 scans the 256 buckets from the top: 8 buckets per lane
+            unsigned c8[8], tot = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) { c8[i] = hist[255 - (tid * 8 + i)]; tot += c8[i]; }
+            unsigned incl = tot;  // inclusive prefix over lanes (lane 0 = highest buckets)
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (tid >= o) incl += v;
             }
-            s_kleft = kleft - acc;
-            s_done = (static_cast<int>(hist[dsel]) == kleft - acc);
-            s_prefix = prefix | (static_cast<uint64_t>(dsel) << shift);
+            const unsigned before = incl - tot;
+            const bool mine = before < static_cast<unsigned>(kleft) &&
+                              incl >= static_cast<unsigned>(kleft);
+            if (mine) {
+                unsigned acc = before;
+                for (int i = 0; i < 8; ++i) {
+                    if (acc + c8[i] >= static_cast<unsigned>(kleft)) {
+                        const int dsel = 255 - (tid * 8 + i);
+                        s_kleft = kleft - static_cast<int>(acc);
+                        s_done = (c8[i] == static_cast<unsigned>(kleft) - acc);
+                        s_prefix = prefix | (static_cast<uint64_t>(dsel) << shift);
+                        break;
+                    }
+                    acc += c8[i];
+                }
+            }
         }
         __syncthreads();
         prefix = s_prefix;
@@ -173,88 +219,197 @@ __device__ int block_topk(int64_t n, int k, const KeyAt& key_at, uint64_t* sel_k
 }
 
 // --------------------------------------------------------------- kernels ---
+// Raw aspect queries q[b, o] = W_Q[o, :] . z[b, :] for o = s*d_k + kk
+// (retrieval.py:65).  One warp per row o of W_Q for all queries of a tile of
+// up to QB queries held in shared memory, so W_Q is read once per tile.
+constexpr int QB = 16;
 template <class ZT>
-__global__ void query_kernel(const ZT* __restrict__ z, const float* __restrict__ W_Q,
-                             const float* __restrict__ aspect_w, int S, int d_k, int d_A,
-                             float* __restrict__ qw) {
-    extern __shared__ float sh[];
-    float* zs = sh;        // [d_A]
-    float* q = sh + d_A;   // [S*d_k]
-    const int b = blockIdx.x;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    for (int i = threadIdx.x; i < d_A; i += blockDim.x)
-        zs[i] = Elem<ZT>::to_f(z[static_cast<int64_t>(b) * d_A + i]);
-    __syncthreads();
-    for (int o = warp; o < S * d_k; o += nw) {
-        const float* w = W_Q + static_cast<int64_t>(o) * d_A;
-        float acc = 0.f;
-        for (int i = lane; i < d_A; i += 32) acc = fmaf(w[i], zs[i], acc);
-        acc = warp_sum(acc);
-        if (lane == 0) q[o] = acc;
-    }
-    __syncthreads();
-    for (int s = warp; s < S; s += nw) {
-        float ss = 0.f;
-        for (int d = lane; d < d_k; d += 32) ss = fmaf(q[s * d_k + d], q[s * d_k + d], ss);
-        ss = warp_sum(ss);
-        const float inv_den = 1.f / (sqrtf(ss) + 1e-8f);
-        float mx = -INFINITY;
-        for (int t = 0; t < S; ++t) mx = fmaxf(mx, aspect_w[t]);
-        float den = 0.f;
-        for (int t = 0; t < S; ++t) den += expf(aspect_w[t] - mx);
-        const float ws = expf(aspect_w[s] - mx) / den;
-        for (int d = lane; d < d_k; d += 32)
-            qw[(static_cast<int64_t>(b) * S + s) * d_k + d] = (q[s * d_k + d] * inv_den) * ws;
+__global__ void __launch_bounds__(256) query_proj_kernel(const ZT* __restrict__ z,
+                                                         const float* __restrict__ W_Q, int B,
+                                                         int rows, int d_A, int btile,
+                                                         float* __restrict__ q) {
+    extern __shared__ float zs[];  // [btile][d_A]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int o = blockIdx.x * (blockDim.x >> 5) + warp;
+    for (int b0 = 0; b0 < B; b0 += btile) {
+        const int nb = min(btile, B - b0);
+        __syncthreads();
+        {
+            const ZT* zb = z + static_cast<int64_t>(b0) * d_A;
+            const int n = nb * d_A;
+            for (int i0 = threadIdx.x; i0 < n; i0 += blockDim.x * 8) {
+                float t[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int i = i0 + u * blockDim.x;
+                    t[u] = i < n ? Elem<ZT>::to_f(zb[i]) : 0.f;
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int i = i0 + u * blockDim.x;
+                    if (i < n) zs[i] = t[u];
+                }
+            }
+        }
+        __syncthreads();
+        if (o < rows) {
+            const float* w = W_Q + static_cast<int64_t>(o) * d_A;
+            float acc[QB];
+#pragma unroll
+            for (int j = 0; j < QB; ++j) acc[j] = 0.f;
+            // up to 32 loads of the W_Q row in flight per batch, then the FMAs
+            for (int i0 = lane; i0 < d_A; i0 += 32 * 32) {
+                float wv[32];
+#pragma unroll
+                for (int u = 0; u < 32; ++u) {
+                    const int i = i0 + 32 * u;
+                    wv[u] = i < d_A ? __ldg(w + i) : 0.f;
+                }
+#pragma unroll
+                for (int u = 0; u < 32; ++u) {
+                    const int i = i0 + 32 * u;
+                    if (i < d_A) {
+#pragma unroll
+                        for (int j = 0; j < QB; ++j)
+                            if (j < nb) acc[j] = fmaf(wv[u], zs[j * d_A + i], acc[j]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < QB; ++j) {
+                if (j < nb) {
+                    const float v = warp_sum(acc[j]);
+                    if (lane == 0) q[static_cast<int64_t>(b0 + j) * rows + o] = v;
+                }
+            }
+        }
     }
 }
 
-__global__ void coarse_kernel(const float* __restrict__ qw, const float* __restrict__ centroids,
-                              int S, int d_k, int C, float* __restrict__ c_score) {
-    extern __shared__ float qs[];
+// qw[b,s,:] = softmax(aspect_weights)_s * q[b,s,:] / (|q[b,s,:]| + 1e-8)   (:66, :69)
+__global__ void query_norm_kernel(float* __restrict__ qw, const float* __restrict__ aspect_w,
+                                  int S, int d_k) {
+    const int b = blockIdx.x, s = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (s >= S) return;
+    float* q = qw + (static_cast<int64_t>(b) * S + s) * d_k;
+    float ss = 0.f;
+    for (int d = lane; d < d_k; d += 32) ss = fmaf(q[d], q[d], ss);
+    ss = warp_sum(ss);
+    const float inv_den = 1.f / (sqrtf(ss) + 1e-8f);
+    float mx = -INFINITY;
+    for (int t = 0; t < S; ++t) mx = fmaxf(mx, aspect_w[t]);
+    float den = 0.f;
+    for (int t = 0; t < S; ++t) den += expf(aspect_w[t] - mx);
+    const float ws = expf(aspect_w[s] - mx) / den;
+    for (int d = lane; d < d_k; d += 32) q[d] = (q[d] * inv_den) * ws;
+}
+
+// One thread per (centroid, aspect): t = (qw[b,s] . c[s,c]) / (|c[s,c]| + 1e-8)
+// with row_scores' operation order; the S terms of a centroid are then added
+// in aspect order (the same sum row_scores forms).
+template <int DK>
+__global__ void __launch_bounds__(1024) coarse_kernel(const float* __restrict__ qw,
+                                                      const float* __restrict__ centroids, int S,
+                                                      int d_k, int C, float* __restrict__ c_score) {
+    extern __shared__ __align__(16) float qs[];   // [S*d_k] then terms [S][64]
+    float* terms = qs + S * d_k;
     const int b = blockIdx.y;
     for (int i = threadIdx.x; i < S * d_k; i += blockDim.x)
         qs[i] = qw[static_cast<int64_t>(b) * S * d_k + i];
     __syncthreads();
-    const int c = blockIdx.x * blockDim.x + threadIdx.x;
-    if (c >= C) return;
-    float sc;
-    row_scores<1>(centroids, C, S, d_k, c, qs, 1, &sc);
-    c_score[static_cast<int64_t>(b) * C + c] = sc;
+    const int cl = threadIdx.x & 63, s = threadIdx.x >> 6;
+    const int c = blockIdx.x * 64 + cl;
+    if (c < C && s < S) {
+        const float* kp = centroids + (static_cast<int64_t>(s) * C + c) * d_k;
+        const float* qq = qs + s * d_k;
+        float dot = 0.f, nrm = 0.f;
+        if constexpr (DK > 0) {
+            float4 kv[DK / 4];
+#pragma unroll
+            for (int i = 0; i < DK / 4; ++i) kv[i] = __ldg(reinterpret_cast<const float4*>(kp) + i);
+#pragma unroll
+            for (int i = 0; i < DK / 4; ++i) {
+                nrm = fmaf(kv[i].x, kv[i].x, nrm);
+                nrm = fmaf(kv[i].y, kv[i].y, nrm);
+                nrm = fmaf(kv[i].z, kv[i].z, nrm);
+                nrm = fmaf(kv[i].w, kv[i].w, nrm);
+            }
+#pragma unroll
+            for (int i = 0; i < DK / 4; ++i) {
+                const float4 qv = reinterpret_cast<const float4*>(qq)[i];
+                dot = fmaf(kv[i].x, qv.x, dot);
+                dot = fmaf(kv[i].y, qv.y, dot);
+                dot = fmaf(kv[i].z, qv.z, dot);
+                dot = fmaf(kv[i].w, qv.w, dot);
+            }
+        } else {
+            for (int d = 0; d < d_k; ++d) {
+                const float x = __ldg(kp + d);
+                nrm = fmaf(x, x, nrm);
+                dot = fmaf(x, qq[d], dot);
+            }
+        }
+        terms[s * 64 + cl] = dot / (sqrtf(nrm) + 1e-8f);
+    }
+    __syncthreads();
+    if (s == 0 && c < C) {
+        float sc = 0.f;
+        for (int t = 0; t < S; ++t) sc += terms[t * 64 + cl];
+        c_score[static_cast<int64_t>(b) * C + c] = sc;
+    }
 }
 
-__global__ void topm_kernel(const float* __restrict__ c_score, int C, int m,
-                            const int64_t* __restrict__ list_off, int64_t N, int max_list,
-                            int32_t* __restrict__ top_clusters, int64_t* __restrict__ probe_lo,
-                            int64_t* __restrict__ cand_base, uint32_t* status) {
+constexpr int kStageKeys = 6144;  // candidates staged in shared memory (48 KB of keys)
+
+__global__ void __launch_bounds__(512) topm_kernel(
+    const float* __restrict__ c_score, int C, int m, const int64_t* __restrict__ list_off,
+    int64_t N, int max_list, int32_t* __restrict__ top_clusters, int64_t* __restrict__ probe_lo,
+    int64_t* __restrict__ cand_base, uint32_t* status) {
     __shared__ uint64_t sel_key[kMaxK];
     __shared__ int64_t sel_pos[kMaxK];
+    extern __shared__ uint64_t skeys[];
     const int b = blockIdx.x;
     const float* cs = c_score + static_cast<int64_t>(b) * C;
-    auto key_at = [&](int64_t i) { return make_key(cs[i], static_cast<uint32_t>(i)); };
-    const int got = block_topk(C, m, key_at, sel_key, sel_pos);
+    int got;
+    if (C <= kStageKeys) {
+        for (int i = threadIdx.x; i < C; i += blockDim.x) skeys[i] = make_key(cs[i], static_cast<uint32_t>(i));
+        __syncthreads();
+        auto key_at = [&](int64_t i) { return skeys[i]; };
+        got = block_topk(C, m, key_at, sel_key, sel_pos);
+    } else {
+        auto key_at = [&](int64_t i) { return make_key(cs[i], static_cast<uint32_t>(i)); };
+        got = block_topk(C, m, key_at, sel_key, sel_pos);
+    }
+    // list ranges of the m winners, one thread each, then a prefix sum over them
+    __shared__ int64_t s_sz[kMaxK + 1];
+    for (int j = threadIdx.x; j < m; j += blockDim.x) {
+        const int c = j < got ? static_cast<int>(sel_pos[j]) : 0;
+        int64_t lo = list_off[c], hi = list_off[c + 1];
+        if (lo < 0 || hi < lo || hi > N) { raise_status(status, DWA_STATUS_BAD_LIST); lo = hi = 0; }
+        int64_t sz = hi - lo;
+        if (sz > max_list) { raise_status(status, DWA_STATUS_LIST_OVERFLOW); sz = max_list; }
+        top_clusters[static_cast<int64_t>(b) * m + j] = c;
+        probe_lo[static_cast<int64_t>(b) * (m + 1) + j] = lo;
+        s_sz[j] = sz;
+    }
+    __syncthreads();
     if (threadIdx.x == 0) {
         int64_t acc = 0;
         for (int j = 0; j < m; ++j) {
-            const int c = j < got ? static_cast<int>(sel_pos[j]) : 0;
-            int64_t lo = list_off[c], hi = list_off[c + 1];
-            if (lo < 0 || hi < lo || hi > N) { raise_status(status, DWA_STATUS_BAD_LIST); lo = hi = 0; }
-            int64_t sz = hi - lo;
-            if (sz > max_list) { raise_status(status, DWA_STATUS_LIST_OVERFLOW); sz = max_list; }
-            top_clusters[static_cast<int64_t>(b) * m + j] = c;
-            probe_lo[static_cast<int64_t>(b) * (m + 1) + j] = lo;
             cand_base[static_cast<int64_t>(b) * (m + 1) + j] = acc;
-            acc += sz;
+            acc += s_sz[j];
         }
         probe_lo[static_cast<int64_t>(b) * (m + 1) + m] = 0;
         cand_base[static_cast<int64_t>(b) * (m + 1) + m] = acc;
     }
 }
 
+template <int DK>
 __global__ void fine_kernel(const float* __restrict__ qw, const float* __restrict__ keys, int64_t N,
                             int S, int d_k, int m, const int64_t* __restrict__ probe_lo,
                             const int64_t* __restrict__ cand_base, int64_t K_cap,
                             float* __restrict__ scores) {
-    extern __shared__ float qs[];
+    extern __shared__ __align__(16) float qs[];
     const int b = blockIdx.z, j = blockIdx.y;
     for (int i = threadIdx.x; i < S * d_k; i += blockDim.x)
         qs[i] = qw[static_cast<int64_t>(b) * S * d_k + i];
@@ -265,17 +420,17 @@ __global__ void fine_kernel(const float* __restrict__ qw, const float* __restric
     if (r >= sz) return;
     const int64_t row = probe_lo[static_cast<int64_t>(b) * (m + 1) + j] + r;
     float sc;
-    row_scores<1>(keys, N, S, d_k, row, qs, 1, &sc);
+    row_scores<1, DK>(keys, N, S, d_k, row, qs, 1, &sc);
     scores[static_cast<int64_t>(b) * K_cap + base + r] = sc;
 }
 
 // Full-pool scores for up to NB queries at a time; writes raw s_full and per
 // block (max, sum exp) of s/T for the softmax.
-template <int NB>
-__global__ void full_scores_kernel(const float* __restrict__ qw, const float* __restrict__ keys,
-                                   int64_t N, int S, int d_k, int B, float T,
-                                   float* __restrict__ sfull, float* __restrict__ partial) {
-    extern __shared__ float qs[];  // [NB][S][d_k]
+template <int NB, int DK>
+__global__ void __launch_bounds__(256) full_scores_kernel(
+    const float* __restrict__ qw, const float* __restrict__ keys, int64_t N, int S, int d_k, int B,
+    float T, float* __restrict__ sfull, float* __restrict__ partial) {
+    extern __shared__ __align__(16) float qs[];  // [NB][S][d_k]
     __shared__ float red[33];
     const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const int nblk = gridDim.x;
@@ -286,7 +441,7 @@ __global__ void full_scores_kernel(const float* __restrict__ qw, const float* __
             qs[i] = qw[static_cast<int64_t>(b0) * S * d_k + i];
         __syncthreads();
         float sc[NB];
-        if (row < N) row_scores<NB>(keys, N, S, d_k, row, qs, nb, sc);
+        if (row < N) row_scores<NB, DK>(keys, N, S, d_k, row, qs, nb, sc);
         for (int q = 0; q < nb; ++q) {
             float x = -INFINITY;
             if (row < N) {
@@ -301,6 +456,171 @@ __global__ void full_scores_kernel(const float* __restrict__ qw, const float* __
                 partial[(static_cast<int64_t>(b0 + q) * nblk + blockIdx.x) * 2 + 1] = zs;
             }
         }
+    }
+}
+
+// Full-pool scores with the key cache streamed through shared memory by TMA.
+// Persistent CTAs; a work item is (tile of 256 rows, aspect s).  Warp 8 is the
+// producer: one lane issues two 2-D TMA loads per item (floats 0-31 and 32-63
+// of the 256 rows, 128-byte swizzle) into a 3-slot ring.  Warps 0-7 consume:
+// thread t scores row t of the tile for all queries, reading its row through
+// the swizzle (conflict-free).  The arithmetic per (row, aspect, query) is
+// row_scores' (bit-identical scores).  Per query each thread keeps an online
+// (max, sum exp) of s/T; one reduction per CTA at the end.
+constexpr int kFsRows = 256, kFsStages = 3, kFsMaxB = 16;
+constexpr uint32_t kFsHalf = kFsRows * 128, kFsSlot = 2 * kFsHalf;  // 32 KB, 64 KB
+
+__global__ void __launch_bounds__(288, 1) full_scores_tma_kernel(
+    const __grid_constant__ CUtensorMap tm_keys, const float* __restrict__ qw, int64_t N, int S,
+    int B, float T, int ntiles, float* __restrict__ sfull, float* __restrict__ partial,
+    uint32_t* status) {
+    extern __shared__ uint8_t dyn[];
+    uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn) + 1023) & ~uintptr_t(1023));
+    float* qs = reinterpret_cast<float*>(ring + kFsStages * kFsSlot);  // [B][S][64]
+    uint64_t* full = reinterpret_cast<uint64_t*>(qs + B * S * 64);
+    uint64_t* empty = full + kFsStages;
+    __shared__ float red_m[8][kFsMaxB], red_z[8][kFsMaxB];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    {
+        const int n4 = B * S * 16;  // float4s
+        float4 t[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = threadIdx.x + u * blockDim.x;
+            if (i < n4) t[u] = reinterpret_cast<const float4*>(qw)[i];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = threadIdx.x + u * blockDim.x;
+            if (i < n4) reinterpret_cast<float4*>(qs)[i] = t[u];
+        }
+    }
+    if (threadIdx.x == 0) {
+        tc::prefetch_tmap(&tm_keys);
+        for (int i = 0; i < kFsStages; ++i) { tc::mbar_init(&full[i], 1); tc::mbar_init(&empty[i], 8); }
+        tc::fence_barrier_init();
+    }
+    __syncthreads();
+    const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int items = my_tiles * S;
+
+    if (warp == 8) {  // producer
+        if (lane == 0) {
+            int issued = 0;
+            for (int it = 0; it < items; ++it) {
+                const int slot = it % kFsStages;
+                if (it >= kFsStages &&
+                    !tc::mbar_wait_bounded(&empty[slot], ((it / kFsStages) - 1) & 1)) {
+                    raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
+                    break;
+                }
+                const int tile = blockIdx.x + (it / S) * gridDim.x, s = it % S;
+                const int y = static_cast<int>(static_cast<int64_t>(s) * N + static_cast<int64_t>(tile) * kFsRows);
+                uint8_t* dst = ring + slot * kFsSlot;
+                tc::mbar_arrive_expect_tx(&full[slot], kFsSlot);
+                tma_load_2d(dst, &tm_keys, &full[slot], 0, y);
+                tma_load_2d(dst + kFsHalf, &tm_keys, &full[slot], 32, y);
+                issued = it + 1;
+            }
+            for (int it = (issued > kFsStages ? issued - kFsStages : 0); it < issued; ++it)
+                if (!tc::mbar_wait_bounded(&full[it % kFsStages], (it / kFsStages) & 1)) {
+                    raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
+                    break;
+                }
+        }
+        __syncwarp();
+        return;
+    }
+
+    const int r = threadIdx.x;  // row within the tile
+    float mrun[kFsMaxB], zrun[kFsMaxB], sc[kFsMaxB];
+#pragma unroll
+    for (int q = 0; q < kFsMaxB; ++q) { mrun[q] = -INFINITY; zrun[q] = 0.f; }
+    bool ok = true;
+    for (int it = 0; it < items && ok; ++it) {
+        const int slot = it % kFsStages, s = it % S;
+        const int tile = blockIdx.x + (it / S) * gridDim.x;
+        if (s == 0) {
+#pragma unroll
+            for (int q = 0; q < kFsMaxB; ++q) sc[q] = 0.f;
+        }
+        if (!tc::mbar_wait_bounded(&full[slot], (it / kFsStages) & 1)) {
+            if (lane == 0) raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
+            ok = false;
+            break;
+        }
+        const uint8_t* base = ring + slot * kFsSlot + r * 128;
+        float4 kv[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c)
+            kv[c] = *reinterpret_cast<const float4*>(base + (c >> 3) * kFsHalf +
+                                                     (((c & 7) ^ (r & 7)) << 4));
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(&empty[slot])) : "memory");
+        float nrm = 0.f;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+            nrm = fmaf(kv[c].x, kv[c].x, nrm);
+            nrm = fmaf(kv[c].y, kv[c].y, nrm);
+            nrm = fmaf(kv[c].z, kv[c].z, nrm);
+            nrm = fmaf(kv[c].w, kv[c].w, nrm);
+        }
+        const float den = sqrtf(nrm) + 1e-8f;
+#pragma unroll
+        for (int q = 0; q < kFsMaxB; ++q) {
+            if (q < B) {
+                const float4* qq = reinterpret_cast<const float4*>(qs + (q * S + s) * 64);
+                float dot = 0.f;
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    const float4 qv = qq[c];
+                    dot = fmaf(kv[c].x, qv.x, dot);
+                    dot = fmaf(kv[c].y, qv.y, dot);
+                    dot = fmaf(kv[c].z, qv.z, dot);
+                    dot = fmaf(kv[c].w, qv.w, dot);
+                }
+                sc[q] += dot / den;
+            }
+        }
+        if (s == S - 1) {
+            const int64_t n = static_cast<int64_t>(tile) * kFsRows + r;
+            if (n < N) {
+#pragma unroll
+                for (int q = 0; q < kFsMaxB; ++q) {
+                    if (q < B) {
+                        sfull[static_cast<int64_t>(q) * N + n] = sc[q];
+                        const float x = sc[q] / T;
+                        if (x > mrun[q]) {
+                            zrun[q] = zrun[q] * expf(mrun[q] - x) + 1.f;
+                            mrun[q] = x;
+                        } else {
+                            zrun[q] += expf(x - mrun[q]);
+                        }
+                    }
+                }
+            }
+        }
+    }
+    // CTA reduction of the online statistics (consumer warps only)
+#pragma unroll
+    for (int q = 0; q < kFsMaxB; ++q) {
+        if (q < B) {
+            const float m = warp_max(mrun[q]);
+            float z = (mrun[q] == -INFINITY) ? 0.f : zrun[q] * expf(mrun[q] - m);
+            z = warp_sum(z);
+            if (lane == 0) { red_m[warp][q] = m; red_z[warp][q] = z; }
+        }
+    }
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    if (threadIdx.x < B) {
+        const int q = threadIdx.x;
+        float M = -INFINITY;
+        for (int w = 0; w < 8; ++w) M = fmaxf(M, red_m[w][q]);
+        float Z = 0.f;
+        for (int w = 0; w < 8; ++w)
+            if (red_m[w][q] != -INFINITY) Z += red_z[w][q] * expf(red_m[w][q] - M);
+        partial[(static_cast<int64_t>(q) * gridDim.x + blockIdx.x) * 2] = M;
+        partial[(static_cast<int64_t>(q) * gridDim.x + blockIdx.x) * 2 + 1] = Z;
     }
 }
 
@@ -350,11 +670,15 @@ __device__ __forceinline__ float gate_raw(float s, float lam, float tau, float T
     return g * expf(s / T);
 }
 
-__global__ void select_kernel(SelectArgs a) {
+// One block per query.  STAGED: the candidate keys (and the gate sum) are
+// computed once into shared memory and every radix pass reads them there.
+template <bool STAGED>
+__global__ void __launch_bounds__(1024) select_kernel(SelectArgs a) {
     __shared__ uint64_t sel_key[kMaxK];
     __shared__ int64_t sel_pos[kMaxK];
     __shared__ int64_t s_lo[kMaxK + 1], s_base[kMaxK + 1];
     __shared__ float red[33];
+    extern __shared__ uint64_t skeys[];
     const int b = blockIdx.x;
     for (int j = threadIdx.x; j <= a.m; j += blockDim.x) {
         s_lo[j] = a.probe_lo[static_cast<int64_t>(b) * (a.m + 1) + j];
@@ -375,43 +699,81 @@ __global__ void select_kernel(SelectArgs a) {
         return a.sfull ? a.sfull[static_cast<int64_t>(b) * a.N + *row]
                        : a.scores[static_cast<int64_t>(b) * a.K_cap + pos];
     };
-    auto key_at = [&](int64_t pos) {
+    auto key_of = [&](int64_t pos, float* raw_out) {
         int64_t row;
         const float s = locate(pos, &row);
-        return make_key(rank_raw ? gate_raw(s, lam, tau, T) : s, static_cast<uint32_t>(row));
+        const float raw = gate ? gate_raw(s, lam, tau, T) : 0.f;
+        *raw_out = raw;
+        return make_key(rank_raw ? raw : s, static_cast<uint32_t>(row));
     };
     float Z = 0.f;
-    if (gate) {
+    int got;
+    if (STAGED) {
+        // candidate order within a probed list is the row order, so walking the
+        // probes keeps global reads coalesced
         float acc = 0.f;
-        for (int64_t p = threadIdx.x; p < n; p += blockDim.x) {
-            int64_t row;
-            acc += gate_raw(locate(p, &row), lam, tau, T);
+        for (int j = 0; j < a.m; ++j) {
+            const int64_t lo = s_lo[j], base = s_base[j], sz = s_base[j + 1] - s_base[j];
+            for (int64_t r = threadIdx.x; r < sz; r += blockDim.x) {
+                const int64_t row = lo + r;
+                const float s = a.sfull ? a.sfull[static_cast<int64_t>(b) * a.N + row]
+                                        : a.scores[static_cast<int64_t>(b) * a.K_cap + base + r];
+                const float raw = gate ? gate_raw(s, lam, tau, T) : 0.f;
+                acc += raw;
+                skeys[base + r] = make_key(rank_raw ? raw : s, static_cast<uint32_t>(row));
+            }
         }
-        Z = block_reduce(acc, false, red);
+        if (gate) Z = block_reduce(acc, false, red);
+        __syncthreads();
+        auto key_at = [&](int64_t i) { return skeys[i]; };
+        got = block_topk(n, a.k, key_at, sel_key, sel_pos);
+    } else {
+        if (gate) {
+            float acc = 0.f;
+            for (int64_t p = threadIdx.x; p < n; p += blockDim.x) {
+                float raw;
+                key_of(p, &raw);
+                acc += raw;
+            }
+            Z = block_reduce(acc, false, red);
+        }
+        auto key_at = [&](int64_t pos) { float raw; return key_of(pos, &raw); };
+        got = block_topk(n, a.k, key_at, sel_key, sel_pos);
     }
-    const int got = block_topk(n, a.k, key_at, sel_key, sel_pos);
-    if (threadIdx.x == 0) {
-        if (got < a.k) raise_status(a.status, DWA_STATUS_FEW_CANDIDATES);
-        float sv[kMaxK];
-        int64_t rows[kMaxK];
-        for (int i = 0; i < got; ++i) sv[i] = locate(sel_pos[i], &rows[i]);
+    // winners' scores and rows, one thread each
+    __shared__ float s_sv[kMaxK];
+    for (int i = threadIdx.x; i < got; i += blockDim.x) {
+        int64_t row;
+        s_sv[i] = locate(sel_pos[i], &row);
+        sel_pos[i] = row;
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        const int l = threadIdx.x;
+        if (l == 0 && got < a.k) raise_status(a.status, DWA_STATUS_FEW_CANDIDATES);
         float* al = a.alphas + static_cast<int64_t>(b) * a.k;
         int32_t* ix = a.indices + static_cast<int64_t>(b) * a.k;
         if (!gate) {
-            const float mx = got > 0 ? sv[0] / T : 0.f;
+            // softmax(top / T) (retrieval.py:146); s_sv[0] is the maximum
+            const float mx = got > 0 ? s_sv[0] / T : 0.f;
             float den = 0.f;
-            for (int i = 0; i < got; ++i) den += expf(sv[i] / T - mx);
-            for (int i = 0; i < got; ++i) al[i] = expf(sv[i] / T - mx) / den;
+            for (int i = l; i < got; i += 32) den += expf(s_sv[i] / T - mx);
+            den = warp_sum(den);
+            for (int i = l; i < got; i += 32) al[i] = expf(s_sv[i] / T - mx) / den;
         } else {
+            // raw / (sum raw + 1e-8), then / (sum top + 1e-8) (retrieval.py:150-155)
             float tot = 0.f;
-            for (int i = 0; i < got; ++i) {
-                sv[i] = gate_raw(sv[i], lam, tau, T) / (Z + 1e-8f);
-                tot += sv[i];
+            for (int i = l; i < got; i += 32) {
+                const float v = gate_raw(s_sv[i], lam, tau, T) / (Z + 1e-8f);
+                s_sv[i] = v;
+                tot += v;
             }
-            for (int i = 0; i < got; ++i) al[i] = sv[i] / (tot + 1e-8f);
+            tot = warp_sum(tot);
+            for (int i = l; i < got; i += 32) al[i] = s_sv[i] / (tot + 1e-8f);
         }
-        for (int i = 0; i < got; ++i) ix[i] = static_cast<int32_t>(rows[i]);
-        for (int i = got; i < a.k; ++i) { al[i] = 0.f; ix[i] = got > 0 ? ix[0] : 0; }
+        for (int i = l; i < got; i += 32) ix[i] = static_cast<int32_t>(sel_pos[i]);
+        __syncwarp();
+        for (int i = got + l; i < a.k; i += 32) { al[i] = 0.f; ix[i] = got > 0 ? static_cast<int32_t>(sel_pos[0]) : 0; }
     }
 }
 
@@ -420,17 +782,6 @@ __global__ void full_probe_kernel(int B, int64_t N, int64_t* probe_lo, int64_t* 
     if (b >= B) return;
     probe_lo[2 * b] = 0; probe_lo[2 * b + 1] = 0;
     cand_base[2 * b] = 0; cand_base[2 * b + 1] = N;
-}
-
-template <class T>
-__global__ void seq_mean_kernel(const T* __restrict__ h, int T_, int d, float* __restrict__ z) {
-    const int b = blockIdx.y;
-    const int j = blockIdx.x * blockDim.x + threadIdx.x;
-    if (j >= d) return;
-    const T* p = h + static_cast<int64_t>(b) * T_ * d + j;
-    float acc = 0.f;
-    for (int t = 0; t < T_; ++t) acc += Elem<T>::to_f(p[static_cast<int64_t>(t) * d]);
-    z[static_cast<int64_t>(b) * d + j] = acc / static_cast<float>(T_);
 }
 
 // ------------------------------------------------------------------ host ---
@@ -452,6 +803,7 @@ struct RetWorkspace {
 };
 
 constexpr int kFullRows = 256;
+constexpr int64_t kSelectStageKeys = 25600;  // 200 KB of staged keys
 
 static RetWorkspace carve_ret(void* base, const DwaRetrieveDims& d, bool ivf, bool want_sf) {
     Carver c(base);
@@ -493,8 +845,9 @@ static int check_ret(const DwaRetrieveDims* d, int use_ivf) {
         if ((d->m < d->C ? d->m : d->C) > kMaxK) return fail(DWA_ERR_UNSUPPORTED, "m > 256");
     }
     const size_t qbytes = static_cast<size_t>(d->S) * d->d_k * sizeof(float);
-    if (qbytes * 8 > 48 * 1024 || (d->d_A + d->S * d->d_k) * sizeof(float) > 48 * 1024)
+    if (qbytes * 8 > 48 * 1024 || static_cast<size_t>(d->d_A) * sizeof(float) > 48 * 1024)
         return fail(DWA_ERR_UNSUPPORTED, "S*d_k or d_A too large for shared memory staging");
+    if (d->S > 16) return fail(DWA_ERR_UNSUPPORTED, "S > 16");
     return DWA_OK;
 }
 
@@ -529,30 +882,46 @@ extern "C" int dwa_retrieve(void* stream, const DwaRetrieveDims* dims, int use_i
         return fail(DWA_ERR_WORKSPACE, "workspace too small: need " + std::to_string(w.bytes));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const size_t qsh = static_cast<size_t>(d.S) * d.d_k * sizeof(float);
+    // d_k = 64 with 16-byte aligned keys takes the unrolled scoring; the fine
+    // and the full pass always take the same variant (bit-identical scores).
+    const bool dk64 = d.d_k == 64 && reinterpret_cast<uintptr_t>(pool_keys) % 16 == 0 &&
+                      (!ivf || reinterpret_cast<uintptr_t>(centroids) % 16 == 0);
 
-    // 1. aspect queries
-    const size_t zsh = (static_cast<size_t>(d.d_A) + static_cast<size_t>(d.S) * d.d_k) * sizeof(float);
+    // 1. aspect queries: projection over many CTAs, then normalisation
+    const int rows = d.S * d.d_k;
+    const int btile = std::max(1, std::min({QB, d.B, static_cast<int>((48 * 1024) / (4 * d.d_A))}));
+    const size_t zsh = static_cast<size_t>(btile) * d.d_A * sizeof(float);
     if (d.z_dtype == DWA_BF16)
-        DWA_TIMED("query", st, query_kernel<__nv_bfloat16><<<d.B, 256, zsh, st>>>(
-                                     static_cast<const __nv_bfloat16*>(z), W_Q, aspect_weights,
-                                     d.S, d.d_k, d.d_A, w.qw));
+        DWA_TIMED("query", st, query_proj_kernel<__nv_bfloat16><<<(rows + 3) / 4, 128, zsh, st>>>(
+                                     static_cast<const __nv_bfloat16*>(z), W_Q, d.B, rows, d.d_A,
+                                     btile, w.qw));
     else
-        DWA_TIMED("query", st, query_kernel<float><<<d.B, 256, zsh, st>>>(
-                                     static_cast<const float*>(z), W_Q, aspect_weights, d.S,
-                                     d.d_k, d.d_A, w.qw));
-    DWA_LAUNCH_CHECK("query_kernel");
-    ++g_launches_total;
+        DWA_TIMED("query", st, query_proj_kernel<float><<<(rows + 3) / 4, 128, zsh, st>>>(
+                                     static_cast<const float*>(z), W_Q, d.B, rows, d.d_A, btile,
+                                     w.qw));
+    DWA_LAUNCH_CHECK("query_proj_kernel");
+    DWA_TIMED("query_norm", st,
+              query_norm_kernel<<<d.B, 32 * d.S, 0, st>>>(w.qw, aspect_weights, d.S, d.d_k));
+    DWA_LAUNCH_CHECK("query_norm_kernel");
+    g_launches_total += 2;
 
     float* sfull = want_sf ? soft_full : w.sfull;
     if (ivf) {
         // 2. coarse scores + top-m lists + candidate ranges
-        dim3 gc((d.C + 127) / 128, d.B);
-        DWA_TIMED("coarse", st, coarse_kernel<<<gc, 128, qsh, st>>>(w.qw, centroids, d.S, d.d_k,
-                                                                    d.C, w.c_score));
+        dim3 gc((d.C + 63) / 64, d.B);
+        const int cth = 64 * d.S;                       // S <= 16 (checked on entry)
+        const size_t csh = qsh + static_cast<size_t>(d.S) * 64 * sizeof(float);
+        if (dk64)
+            DWA_TIMED("coarse", st, coarse_kernel<64><<<gc, cth, csh, st>>>(
+                                        w.qw, centroids, d.S, d.d_k, d.C, w.c_score));
+        else
+            DWA_TIMED("coarse", st, coarse_kernel<0><<<gc, cth, csh, st>>>(
+                                        w.qw, centroids, d.S, d.d_k, d.C, w.c_score));
         DWA_LAUNCH_CHECK("coarse_kernel");
-        DWA_TIMED("topm", st, topm_kernel<<<d.B, 256, 0, st>>>(w.c_score, d.C, w.m_eff, list_offsets,
-                                                               d.N, d.max_list, w.topc,
-                                                               w.probe_lo, w.cand_base, w.status));
+        const size_t tsh = d.C <= kStageKeys ? static_cast<size_t>(d.C) * 8 : 0;
+        DWA_TIMED("topm", st, topm_kernel<<<d.B, 512, tsh, st>>>(w.c_score, d.C, w.m_eff, list_offsets,
+                                                                 d.N, d.max_list, w.topc,
+                                                                 w.probe_lo, w.cand_base, w.status));
         DWA_LAUNCH_CHECK("topm_kernel");
         g_launches_total += 2;
     } else {
@@ -561,20 +930,66 @@ extern "C" int dwa_retrieve(void* stream, const DwaRetrieveDims* dims, int use_i
         ++g_launches_total;
     }
     // 3. full-pool raw scores (soft_full or full search)
-    if (!ivf || want_sf) {
-        constexpr int NB = 8;
+    int sf_blocks = w.nblk;
+    const size_t fs_smem = 1024 + static_cast<size_t>(kFsStages) * kFsSlot +
+                           static_cast<size_t>(d.B) * d.S * 64 * sizeof(float) + 2 * kFsStages * 8;
+    CUtensorMap tm_keys;
+    constexpr size_t kFsSmemLimit = 227 * 1024 - 2048;  // leaves room for static shared memory
+    bool use_tma = dk64 && d.B <= kFsMaxB && fs_smem <= kFsSmemLimit &&
+                   static_cast<int64_t>(d.S) * d.N < (int64_t(1) << 31);
+    if (use_tma && (!ivf || want_sf)) {
+        auto enc = tc::tensor_map_encoder();
+        cuuint64_t dims2[2] = {64, static_cast<cuuint64_t>(d.S) * static_cast<cuuint64_t>(d.N)};
+        cuuint64_t strides2[1] = {64 * sizeof(float)};
+        cuuint32_t box2[2] = {32, static_cast<cuuint32_t>(kFsRows)};
+        cuuint32_t es2[2] = {1, 1};
+        use_tma = enc && enc(&tm_keys, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(pool_keys),
+                             dims2, strides2, box2, es2, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    }
+    if ((!ivf || want_sf) && use_tma) {
+        int dev = 0, sms = 148;
+        DWA_CUDA_TRY(cudaGetDevice(&dev));
+        DWA_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        static bool attr_set[64] = {};
+        if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+            DWA_CUDA_TRY(cudaFuncSetAttribute(full_scores_tma_kernel,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              static_cast<int>(kFsSmemLimit)));
+            if (dev >= 0 && dev < 64) attr_set[dev] = true;
+        }
+        const int ntiles = static_cast<int>((d.N + kFsRows - 1) / kFsRows);
+        sf_blocks = std::min(ntiles, sms);
         DWA_TIMED("full_scores", st,
-                  full_scores_kernel<NB><<<w.nblk, kFullRows, NB * qsh, st>>>(
-                      w.qw, pool_keys, d.N, d.S, d.d_k, d.B, d.T, sfull, w.partial));
+                  full_scores_tma_kernel<<<sf_blocks, 288, fs_smem, st>>>(
+                      tm_keys, w.qw, d.N, d.S, d.B, d.T, ntiles, sfull, w.partial, w.status));
+        DWA_LAUNCH_CHECK("full_scores_tma_kernel");
+        ++g_launches_total;
+    } else if (!ivf || want_sf) {
+        constexpr int NB = 8;
+        if (dk64)
+            DWA_TIMED("full_scores", st,
+                      full_scores_kernel<NB, 64><<<w.nblk, kFullRows, NB * qsh, st>>>(
+                          w.qw, pool_keys, d.N, d.S, d.d_k, d.B, d.T, sfull, w.partial));
+        else
+            DWA_TIMED("full_scores", st,
+                      full_scores_kernel<NB, 0><<<w.nblk, kFullRows, NB * qsh, st>>>(
+                          w.qw, pool_keys, d.N, d.S, d.d_k, d.B, d.T, sfull, w.partial));
         DWA_LAUNCH_CHECK("full_scores_kernel");
         ++g_launches_total;
     }
     // 4. fine scores of the probed lists (read from the full pass when it ran)
     if (ivf && !want_sf) {
         dim3 gf(static_cast<unsigned>((d.max_list + 255) / 256), w.m_eff, d.B);
-        DWA_TIMED("fine", st, fine_kernel<<<gf, 256, qsh, st>>>(w.qw, pool_keys, d.N, d.S, d.d_k,
-                                                                w.m_eff, w.probe_lo, w.cand_base,
-                                                                w.K_cap, w.scores));
+        if (dk64)
+            DWA_TIMED("fine", st, fine_kernel<64><<<gf, 256, qsh, st>>>(
+                                      w.qw, pool_keys, d.N, d.S, d.d_k, w.m_eff, w.probe_lo,
+                                      w.cand_base, w.K_cap, w.scores));
+        else
+            DWA_TIMED("fine", st, fine_kernel<0><<<gf, 256, qsh, st>>>(
+                                      w.qw, pool_keys, d.N, d.S, d.d_k, w.m_eff, w.probe_lo,
+                                      w.cand_base, w.K_cap, w.scores));
         DWA_LAUNCH_CHECK("fine_kernel");
         ++g_launches_total;
     }
@@ -595,13 +1010,29 @@ extern "C" int dwa_retrieve(void* stream, const DwaRetrieveDims* dims, int use_i
     sa.alphas = alphas;
     sa.indices = indices;
     sa.status = w.status;
-    DWA_TIMED("select", st, select_kernel<<<d.B, 512, 0, st>>>(sa));
+    if (w.K_cap <= kSelectStageKeys) {
+        const size_t ssh = static_cast<size_t>(w.K_cap) * 8;
+        if (ssh > 48 * 1024) {
+            int dev = 0;
+            DWA_CUDA_TRY(cudaGetDevice(&dev));
+            static bool attr_set[64] = {};
+            if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+                DWA_CUDA_TRY(cudaFuncSetAttribute(select_kernel<true>,
+                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  static_cast<int>(kSelectStageKeys * 8)));
+                if (dev >= 0 && dev < 64) attr_set[dev] = true;
+            }
+        }
+        DWA_TIMED("select", st, select_kernel<true><<<d.B, 1024, ssh, st>>>(sa));
+    } else {
+        DWA_TIMED("select", st, select_kernel<false><<<d.B, 1024, 0, st>>>(sa));
+    }
     DWA_LAUNCH_CHECK("select_kernel");
     ++g_launches_total;
     // 6. normalise soft_full in place
     if (want_sf) {
         DWA_TIMED("softmax_stats", st,
-                  softmax_stats_kernel<<<d.B, 256, 0, st>>>(w.partial, w.nblk, w.stats));
+                  softmax_stats_kernel<<<d.B, 256, 0, st>>>(w.partial, sf_blocks, w.stats));
         DWA_LAUNCH_CHECK("softmax_stats_kernel");
         dim3 ga(static_cast<unsigned>(std::min<int64_t>((d.N + 255) / 256, 1184)), d.B);
         DWA_TIMED("softmax_apply", st,
@@ -618,14 +1049,14 @@ extern "C" int dwa_sequence_mean(void* stream, int B, int T, int d, int dtype, c
         return fail(DWA_ERR_INVALID_ARG, "dwa_sequence_mean: bad sizes or NULL pointer");
     if (dtype != DWA_F32 && dtype != DWA_BF16) return fail(DWA_ERR_INVALID_ARG, "bad dtype");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    dim3 g((d + 255) / 256, B);
+    dim3 g((d + 63) / 64, B);
     if (dtype == DWA_BF16)
-        DWA_TIMED("seq_mean", st, seq_mean_kernel<__nv_bfloat16><<<g, 256, 0, st>>>(
-                                      static_cast<const __nv_bfloat16*>(h_A), T, d, z));
+        DWA_TIMED("seq_mean", st, column_sum_kernel<__nv_bfloat16><<<g, 1024, 0, st>>>(
+                                      static_cast<const __nv_bfloat16*>(h_A), T, d, 1, z));
     else
-        DWA_TIMED("seq_mean", st,
-                  seq_mean_kernel<float><<<g, 256, 0, st>>>(static_cast<const float*>(h_A), T, d, z));
-    DWA_LAUNCH_CHECK("seq_mean_kernel");
+        DWA_TIMED("seq_mean", st, column_sum_kernel<float><<<g, 1024, 0, st>>>(
+                                      static_cast<const float*>(h_A), T, d, 1, z));
+    DWA_LAUNCH_CHECK("column_sum_kernel");
     ++g_launches_total;
     return DWA_OK;
 }

@@ -11,7 +11,8 @@
 // CTA tile 128 x BN x 64, STAGES-deep TMA ring, one CTA per output tile:
 //   warp 0      TMA producer (one elected lane)
 //   warp 1      TMEM allocator + MMA issuer (one elected lane)
-//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, row = TMEM lane
+//   warps 2..17 epilogue: tcgen05.ld into a shared fp32 tile, then a coalesced
+//               pass (8 columns per lane) through the epilogue functor
 // Every mbarrier wait is bounded (kWaitLimitNs); a wait that runs out sets
 // DWA_STATUS_WAIT_TIMEOUT in the status word and the CTA winds down, freeing
 // its TMEM.
@@ -190,17 +191,23 @@ struct SmemLayout {
     static constexpr uint32_t A_STAGE = BM * BK * 2;
     static constexpr uint32_t B_STAGE = BN * BK * 2;
     static constexpr uint32_t BAR_OFF = STAGES * (A_STAGE + B_STAGE);
+    // the epilogue reuses the stage buffers for the fp32 accumulator tile
+    static_assert(BM * (BN + 4) * 4 <= BAR_OFF, "epilogue tile must fit in the stage buffers");
     static constexpr uint32_t BYTES = 1024 /*align slack*/ + BAR_OFF + (2 * STAGES + 1) * 8 + 16;
 };
 
 // Epilogue protocol.  Epi provides
 //   float operator()(int b, int row, int col0, const float* v, int cnt) const
-//     v[0..cnt) = C[b](row, col0 + i); returns a partial for the reductions;
+//     v[0..cnt) = C[b](row, col0 + i), cnt <= 8 (col0 a multiple of 8 when
+//     cnt == 8); returns a partial for the reductions;
 //   static constexpr int kReduce;   0 none, 1 per row, 2 per CTA
 //   void row_done(int b, int row, float acc) const   (kReduce == 1)
 //   void cta_done(int b, float acc) const            (kReduce == 2)
+constexpr int kEpiWarps = 16;                       // epilogue warps (2..17)
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;   // + TMA warp + MMA warp
+
 template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      int M, int N, int K, int a_batched, int b_batched, Epi epi, uint32_t* status) {
     using L = SmemLayout<BN, STAGES>;
@@ -214,7 +221,7 @@ __global__ void __launch_bounds__(192, 1)
     uint64_t* empty_bar = full_bar + STAGES;
     uint64_t* done_bar = empty_bar + STAGES;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
-    __shared__ float s_red[4];
+    __shared__ float s_red[kEpiWarps];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, bz = blockIdx.z;
@@ -299,32 +306,68 @@ __global__ void __launch_bounds__(192, 1)
         }
         __syncwarp();
     } else {
-        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        // Epilogue.  Phase 1: TMEM -> shared tile (fp32, row stride BN+4 floats),
+        // thread = row; warp w may only read TMEM lanes 32*(w%4).., so the 16
+        // warps form 4 column groups of one warp per lane quarter.  The stage
+        // buffers are free: every TMA load was consumed by an MMA and done_bar
+        // fires after the last MMA completes.
+        const int q = warp & 3;
+        const int e = warp - 2;        // epilogue warp 0..15
+        const int grp = e >> 2;        // column group 0..3
         const bool ok = mbar_wait_bounded(done_bar, 0);
         if (!ok && lane == 0) raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
         tc_fence_after();
-        const int row = m0 + q * 32 + lane;
-        float acc = 0.f;
+        constexpr int LD = BN + 4;
+        float* tile = reinterpret_cast<float*>(smem);
         if (ok) {
-            for (int c = 0; c < BN / 32; ++c) {
-                const int col0 = n0 + c * 32;
-                if (col0 >= N) break;
+            const int r_local = q * 32 + lane;
+            for (int c = grp; c < BN / 32; c += 4) {
+                if (n0 + c * 32 >= N) break;
                 float v[32];
                 tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c * 32, v);
-                if (row < M) acc += epi(bz, row, col0, v, min(32, N - col0));
+                float4* dst = reinterpret_cast<float4*>(tile + r_local * LD + c * 32);
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
             }
         }
-        if (Epi::kReduce == 1) {
-            if (ok && row < M) epi.row_done(bz, row, acc);
-        } else if (Epi::kReduce == 2) {
-            acc = warp_sum(acc);
-            if (lane == 0) s_red[q] = acc;
-        }
         tc_fence_before();
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");
+        // Phase 2: coalesced.  LPR lanes cover one row (8 columns each).
+        constexpr int LPR = BN / 8, RPW = 32 / LPR;
+        const int sub = lane / LPR, li = lane % LPR;
+        float cta_acc = 0.f;
+        if (ok) {
+            for (int rr = e * RPW + sub; rr < BM; rr += kEpiWarps * RPW) {
+                const int row = m0 + rr, col0 = n0 + li * 8;
+                const int cnt = min(8, N - col0);
+                float part = 0.f;
+                if (row < M && cnt > 0) {
+                    const float4* src = reinterpret_cast<const float4*>(tile + rr * LD + li * 8);
+                    const float4 a = src[0], b = src[1];
+                    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+                    part = epi(bz, row, col0, v, cnt);
+                }
+                if (Epi::kReduce == 1) {
+#pragma unroll
+                    for (int o = LPR / 2; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+                    if (li == 0 && row < M) epi.row_done(bz, row, part);
+                } else if (Epi::kReduce == 2) {
+                    cta_acc += part;
+                }
+            }
+        }
+        if (Epi::kReduce == 2) {
+            cta_acc = warp_sum(cta_acc);
+            if (lane == 0) s_red[e] = cta_acc;
+        }
     }
     __syncthreads();
-    if (Epi::kReduce == 2 && threadIdx.x == 0)
-        epi.cta_done(bz, s_red[0] + s_red[1] + s_red[2] + s_red[3]);
+    if (Epi::kReduce == 2 && threadIdx.x == 0) {
+        float t = 0.f;
+        for (int i = 0; i < kEpiWarps; ++i) t += s_red[i];
+        epi.cta_done(bz, t);
+    }
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, TMEM_COLS);
@@ -364,8 +407,8 @@ int launch_gemm_bf16(const Operand& A, const Operand& B, int M, int N, int K, in
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
     dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, batch);
-    kern<<<grid, 192, L::BYTES, stream>>>(ta, tb, M, N, K, A.bstride != 0, B.bstride != 0, epi,
-                                          status);
+    kern<<<grid, kGemmThreads, L::BYTES, stream>>>(ta, tb, M, N, K, A.bstride != 0, B.bstride != 0,
+                                                   epi, status);
     DWA_LAUNCH_CHECK("gemm_bf16_kernel");
     return DWA_OK;
 }
