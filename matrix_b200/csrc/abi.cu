@@ -58,6 +58,54 @@ void prof_end(const char* name, cudaStream_t st) {
     if (ProfEntry* e = prof_find(name)) prof_record(e->stop, st);
 }
 
+struct LaneState {
+    std::mutex mu;
+    bool ready = false;
+    cudaStream_t aux[2];
+    cudaEvent_t ev[8];
+};
+static LaneState g_lanes[64];
+
+Lanes::Lanes(cudaStream_t st) : main(st) {
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        rc = fail(DWA_ERR_CUDA, "Lanes: no current device");
+        dev = -1;
+        return;
+    }
+    LaneState& L = g_lanes[dev];
+    L.mu.lock();
+    if (!L.ready) {
+        bool ok = true;
+        for (auto& a : L.aux) ok = ok && cudaStreamCreateWithFlags(&a, cudaStreamNonBlocking) == cudaSuccess;
+        for (auto& e : L.ev) ok = ok && cudaEventCreateWithFlags(&e, cudaEventDisableTiming) == cudaSuccess;
+        if (!ok) {
+            rc = fail(DWA_ERR_CUDA, "Lanes: stream/event creation failed");
+            return;
+        }
+        L.ready = true;
+    }
+    aux[0] = L.aux[0];
+    aux[1] = L.aux[1];
+    for (int i = 0; i < 8; ++i) ev[i] = L.ev[i];
+    if ((rc = depend(aux[0], main, 0))) return;
+    rc = depend(aux[1], main, 0);
+}
+
+Lanes::~Lanes() {
+    if (dev >= 0) g_lanes[dev].mu.unlock();
+}
+
+int Lanes::depend(cudaStream_t to, cudaStream_t from, int slot) {
+    if (cudaEventRecord(ev[slot], from) != cudaSuccess || cudaStreamWaitEvent(to, ev[slot], 0) != cudaSuccess)
+        return fail(DWA_ERR_CUDA, "Lanes: event record/wait failed");
+    return DWA_OK;
+}
+
+int Lanes::join() {
+    int r = depend(main, aux[0], 6);
+    return r ? r : depend(main, aux[1], 7);
+}
+
 namespace tc {
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {

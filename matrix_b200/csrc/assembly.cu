@@ -90,27 +90,42 @@ __device__ __forceinline__ void red_add4(float* p, float a, float b, float c, fl
 }
 
 // ------------------------------------------------------------ epilogues ----
+// Epilogue functors.  The tensor-core GEMM calls load() for several rows first
+// (global operands into a register fragment) and finish() afterwards, so the
+// loads of those rows are in flight together; the CUDA-core GEMM calls
+// operator(), i.e. both back to back.  The vector path covers 8 columns
+// starting at a multiple of 8; other segments take the scalar path in finish().
 struct NoReduce {
     static constexpr int kReduce = 0;
     __device__ void row_done(int, int, float) const {}
     __device__ void cta_done(int, float) const {}
 };
 
+#define DWA_EPI_CALL                                                                    \
+    __device__ float operator()(int b, int row, int col0, const float* v, int cnt) const { \
+        Frag f;                                                                           \
+        load(b, row, col0, cnt, f);                                                       \
+        return finish(b, row, col0, v, cnt, f);                                           \
+    }
+
 // W[b](j,i) = W_base(j,i) + acc   -> fp32 W_out and/or act-typed W_act
 template <class ACT>
 struct EpiW : NoReduce {
     const float* W_base; float* W_out; ACT* W_act; int d_B, d_A; bool vec;
-    __device__ float operator()(int b, int row, int col0, const float* v, int cnt) const {
+    struct Frag { float wb[8]; };
+    __device__ void load(int, int row, int col0, int cnt, Frag& f) const {
+        if (vec && cnt == 8) load8(W_base + static_cast<int64_t>(row) * d_A + col0, f.wb);
+    }
+    __device__ float finish(int b, int row, int col0, const float* v, int cnt, const Frag& f) const {
         const int64_t o = (static_cast<int64_t>(b) * d_B + row) * d_A + col0;
-        const float* wb = W_base + static_cast<int64_t>(row) * d_A + col0;
         if (vec && cnt == 8) {
             float w[8];
-            load8(wb, w);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) w[i] += v[i];
+            for (int i = 0; i < 8; ++i) w[i] = f.wb[i] + v[i];
             if (W_out) store8(W_out + o, w);
             if (W_act) store8(W_act + o, w);
         } else {
+            const float* wb = W_base + static_cast<int64_t>(row) * d_A + col0;
             for (int c = 0; c < cnt; ++c) {
                 const float w = wb[c] + v[c];
                 if (W_out) W_out[o + c] = w;
@@ -119,29 +134,36 @@ struct EpiW : NoReduce {
         }
         return 0.f;
     }
+    DWA_EPI_CALL
 };
 
 // h_mid[b](t,j) = h_A[b](t,j) + gamma acc + pb[b](j)
 template <class ACT>
 struct EpiApply : NoReduce {
     const ACT* hA; const float* pb; const float* gamma; ACT* out; int T, d; bool vec;
-    __device__ float operator()(int b, int row, int col0, const float* v, int cnt) const {
+    struct Frag { float h[8], q[8]; };
+    __device__ void load(int b, int row, int col0, int cnt, Frag& f) const {
+        if (vec && cnt == 8) {
+            load8(hA + (static_cast<int64_t>(b) * T + row) * d + col0, f.h);
+            load8(pb + static_cast<int64_t>(b) * d + col0, f.q);
+        }
+    }
+    __device__ float finish(int b, int row, int col0, const float* v, int cnt, const Frag& f) const {
         const int64_t o = (static_cast<int64_t>(b) * T + row) * d + col0;
-        const float* p = pb + static_cast<int64_t>(b) * d + col0;
         const float g = __ldg(gamma);
         if (vec && cnt == 8) {
-            float h[8], q[8];
-            load8(hA + o, h);
-            load8(p, q);
+            float h[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) h[i] = h[i] + g * v[i] + q[i];
+            for (int i = 0; i < 8; ++i) h[i] = f.h[i] + g * v[i] + f.q[i];
             store8(out + o, h);
         } else {
+            const float* p = pb + static_cast<int64_t>(b) * d + col0;
             for (int c = 0; c < cnt; ++c)
                 out[o + c] = Elem<ACT>::from_f(Elem<ACT>::to_f(hA[o + c]) + g * v[c] + p[c]);
         }
         return 0.f;
     }
+    DWA_EPI_CALL
 };
 
 // gW[b](j,i) = gamma G + g_W_out; g_W_base += gW; g_gamma += G * W
@@ -150,26 +172,27 @@ struct EpiG {
     static constexpr int kReduce = 2;
     const float* gamma; const float* gWo; ACT* gW; float* gWbase; const ACT* Wact;
     float* gamma_acc; int d_B, d_A; bool vec;
-    __device__ float operator()(int b, int row, int col0, const float* v, int cnt) const {
+    struct Frag { float w[8], x[8]; };
+    __device__ void load(int b, int row, int col0, int cnt, Frag& f) const {
+        if (vec && cnt == 8) {
+            const int64_t o = (static_cast<int64_t>(b) * d_B + row) * d_A + col0;
+            load8(Wact + o, f.w);
+            if (gWo) load8(gWo + o, f.x);
+        }
+    }
+    __device__ float finish(int b, int row, int col0, const float* v, int cnt, const Frag& f) const {
         const int64_t o = (static_cast<int64_t>(b) * d_B + row) * d_A + col0;
         const int64_t ob = static_cast<int64_t>(row) * d_A + col0;
         const float g = __ldg(gamma);
         float part = 0.f;
         if (vec && cnt == 8) {
-            float w[8], x[8];
-            load8(Wact + o, w);
+            float x[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) part = fmaf(v[i], w[i], part);
-            if (gWo) {
-                load8(gWo + o, x);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) x[i] = fmaf(g, v[i], x[i]);
-            } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) x[i] = g * v[i];
+            for (int i = 0; i < 8; ++i) {
+                part = fmaf(v[i], f.w[i], part);
+                x[i] = gWo ? fmaf(g, v[i], f.x[i]) : g * v[i];
             }
             store8(gW + o, x);
-#pragma unroll
             red_add4(gWbase + ob, x[0], x[1], x[2], x[3]);
             red_add4(gWbase + ob + 4, x[4], x[5], x[6], x[7]);
         } else {
@@ -182,6 +205,7 @@ struct EpiG {
         }
         return part;
     }
+    DWA_EPI_CALL
     __device__ void row_done(int, int, float) const {}
     __device__ void cta_done(int, float acc) const { atomicAdd(gamma_acc, acc); }
 };
@@ -190,14 +214,17 @@ struct EpiG {
 template <class ACT>
 struct EpiGhA : NoReduce {
     const ACT* g; const float* gamma; ACT* out; int T, d; bool vec;
-    __device__ float operator()(int b, int row, int col0, const float* v, int cnt) const {
+    struct Frag { float x[8]; };
+    __device__ void load(int b, int row, int col0, int cnt, Frag& f) const {
+        if (vec && cnt == 8) load8(g + (static_cast<int64_t>(b) * T + row) * d + col0, f.x);
+    }
+    __device__ float finish(int b, int row, int col0, const float* v, int cnt, const Frag& f) const {
         const int64_t o = (static_cast<int64_t>(b) * T + row) * d + col0;
         const float gm = __ldg(gamma);
         if (vec && cnt == 8) {
             float x[8];
-            load8(g + o, x);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) x[i] = fmaf(gm, v[i], x[i]);
+            for (int i = 0; i < 8; ++i) x[i] = fmaf(gm, v[i], f.x[i]);
             store8(out + o, x);
         } else {
             for (int c = 0; c < cnt; ++c)
@@ -205,12 +232,15 @@ struct EpiGhA : NoReduce {
         }
         return 0.f;
     }
+    DWA_EPI_CALL
 };
 
 // g_U: g_rows[b][kk][j*r + rho] = acc(j, kk*r + rho)
 struct EpiP : NoReduce {
     float* g_rows; int64_t D; int k, r; bool vec;
-    __device__ float operator()(int b, int row, int col0, const float* v, int cnt) const {
+    struct Frag {};
+    __device__ void load(int, int, int, int, Frag&) const {}
+    __device__ float finish(int b, int row, int col0, const float* v, int cnt, const Frag&) const {
         if (vec && cnt == 8 && r == 8) {   // the 8 columns are the 8 factors of one pool row
             store8(g_rows + (static_cast<int64_t>(b) * k + col0 / 8) * D + static_cast<int64_t>(row) * 8, v);
             return 0.f;
@@ -222,6 +252,7 @@ struct EpiP : NoReduce {
         }
         return 0.f;
     }
+    DWA_EPI_CALL
 };
 
 // g_V: g_rows[b][kk][s1 + rho*d_A + i] = alpha[b,kk] acc(kk*r+rho, i);
@@ -230,34 +261,41 @@ template <class RT>
 struct EpiQ {
     static constexpr int kReduce = 1;
     RowSrc src; const float* alphas; float* g_rows; float* dW_acc; int64_t s1; int d_A, r; bool vec;
-    __device__ float operator()(int b, int row, int col0, const float* v, int cnt) const {
+    struct Frag { float vv[8]; float a; bool has; };
+    __device__ void load(int b, int row, int col0, int cnt, Frag& f) const {
         const int kk = row / r, rho = row - kk * r;
-        const float a = __ldg(alphas + static_cast<int64_t>(b) * src.k + kk);
+        f.a = __ldg(alphas + static_cast<int64_t>(b) * src.k + kk);
+        const int64_t ro = src.offset(b, kk);
+        f.has = ro >= 0;
+        if (vec && cnt == 8 && f.has)
+            load8(static_cast<const RT*>(src.rows) + ro + s1 + static_cast<int64_t>(rho) * d_A + col0, f.vv);
+    }
+    __device__ float finish(int b, int row, int col0, const float* v, int cnt, const Frag& f) const {
+        const int kk = row / r, rho = row - kk * r;
         const int64_t go = (static_cast<int64_t>(b) * src.k + kk) * src.D + s1 +
                            static_cast<int64_t>(rho) * d_A + col0;
-        const int64_t ro = src.offset(b, kk);
-        const RT* V = ro < 0 ? nullptr
-                             : static_cast<const RT*>(src.rows) + ro + s1 +
-                                   static_cast<int64_t>(rho) * d_A + col0;
         float part = 0.f;
         if (vec && cnt == 8) {
             float x[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) x[i] = a * v[i];
-            store8(g_rows + go, x);
-            if (V) {
-                load8(V, x);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) part = fmaf(x[i], v[i], part);
+            for (int i = 0; i < 8; ++i) {
+                x[i] = f.a * v[i];
+                if (f.has) part = fmaf(f.vv[i], v[i], part);
             }
+            store8(g_rows + go, x);
         } else {
+            const int64_t ro = src.offset(b, kk);
+            const RT* V = ro < 0 ? nullptr
+                                 : static_cast<const RT*>(src.rows) + ro + s1 +
+                                       static_cast<int64_t>(rho) * d_A + col0;
             for (int c = 0; c < cnt; ++c) {
-                g_rows[go + c] = a * v[c];
+                g_rows[go + c] = f.a * v[c];
                 if (V) part = fmaf(Elem<RT>::to_f(V[c]), v[c], part);
             }
         }
         return part;
     }
+    DWA_EPI_CALL
     __device__ void row_done(int b, int row, float acc) const {
         atomicAdd(dW_acc + static_cast<int64_t>(b) * src.k + row / r, acc);
     }
@@ -304,20 +342,31 @@ __global__ void __launch_bounds__(256) prep_factors_bf16_r8_kernel(
     const float a = alphas[static_cast<int64_t>(b) * k + kk];
     const uint4 zero = make_uint4(0, 0, 0, 0);
     __nv_bfloat16* ug = Ug + static_cast<int64_t>(b) * d_B * ldu + static_cast<int64_t>(kk) * 8;
-    for (int j = threadIdx.x; j < d_B; j += blockDim.x)
-        *reinterpret_cast<uint4*>(ug + static_cast<int64_t>(j) * ldu) = row ? __ldg(row + j) : zero;
     const int64_t kr = static_cast<int64_t>(k) * 8;
     uint4* vs = reinterpret_cast<uint4*>(Vs + (static_cast<int64_t>(b) * kr + static_cast<int64_t>(kk) * 8) * d_A);
-    const int nv = d_A;  // 8 rows of d_A elements = d_A vectors of 8
-    for (int e = threadIdx.x; e < nv; e += blockDim.x) {
-        uint4 v = row ? __ldg(row + d_B + e) : zero;
-        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+    // U: d_B vectors, V: d_A vectors (8 rows of d_A); up to 8 of each in flight
+    for (int j0 = threadIdx.x; j0 < d_B || j0 < d_A; j0 += blockDim.x * 8) {
+        uint4 u[8], v[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float2 f = __bfloat1622float2(h[i]);
-            h[i] = __floats2bfloat162_rn(a * f.x, a * f.y);
+        for (int t = 0; t < 8; ++t) {
+            const int j = j0 + t * blockDim.x;
+            u[t] = (row && j < d_B) ? __ldg(row + j) : zero;
+            v[t] = (row && j < d_A) ? __ldg(row + d_B + j) : zero;
         }
-        vs[e] = v;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const int j = j0 + t * blockDim.x;
+            if (j < d_B) *reinterpret_cast<uint4*>(ug + static_cast<int64_t>(j) * ldu) = u[t];
+            if (j < d_A) {
+                __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v[t]);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float2 f = __bfloat1622float2(h[i]);
+                    h[i] = __floats2bfloat162_rn(a * f.x, a * f.y);
+                }
+                vs[j] = v[t];
+            }
+        }
     }
 }
 
@@ -336,7 +385,7 @@ __global__ void __launch_bounds__(256) prep_bias_kernel(RowSrc src, const float*
     const RT* rows = static_cast<const RT*>(src.rows);
     const float* a = alphas + static_cast<int64_t>(b) * src.k;
     float acc = 0.f;
-#pragma unroll 8
+#pragma unroll 16
     for (int kk = 0; kk < src.k; ++kk) {
         const int64_t off = offs[kk];
         if (off >= 0) acc = fmaf(a[kk], Elem<RT>::to_f(rows[off + s2 + j]), acc);
@@ -484,12 +533,13 @@ static bool vec_ok(const void* p, int64_t ld, size_t es) {
 
 template <class ACT, class RT>
 static int prep(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src, const float* alphas,
-                const float* b_base, const AsmWorkspace& w, bool with_bias) {
+                const float* b_base, const AsmWorkspace& w, bool with_factors, bool with_bias) {
     dim3 g1(d.k, d.B);
     const bool vec8 = std::is_same<ACT, __nv_bfloat16>::value && std::is_same<RT, __nv_bfloat16>::value &&
                       d.r == 8 && d.D % 8 == 0 && d.d_A % 8 == 0 && w.ldu % 8 == 0 &&
                       reinterpret_cast<uintptr_t>(src.rows) % 16 == 0;
-    if (vec8)
+    if (!with_factors) {
+    } else if (vec8)
         DWA_TIMED("prep_factors", st,
                   prep_factors_bf16_r8_kernel<<<g1, 256, 0, st>>>(
                       src, alphas, d.d_A, d.d_B, w.ldu, static_cast<__nv_bfloat16*>(w.Ug),
@@ -500,7 +550,7 @@ static int prep(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src, co
                                                                    w.ldu, static_cast<ACT*>(w.Ug),
                                                                    static_cast<ACT*>(w.Vs), w.status));
     DWA_LAUNCH_CHECK("prep_factors_kernel");
-    ++g_launches_total;
+    if (with_factors) ++g_launches_total;
     if (with_bias) {
         const int64_t s2 = static_cast<int64_t>(d.d_B) * d.r + static_cast<int64_t>(d.r) * d.d_A;
         dim3 g2((d.d_B + 255) / 256, d.B);
@@ -517,8 +567,12 @@ template <class ACT, class RT>
 static int fwd_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src,
                     const float* alphas, const ACT* hA, const float* W_base, const float* b_base,
                     const float* gamma, ACT* h_mid, float* W_out, ACT* W_act, const AsmWorkspace& w) {
-    int rc = prep<ACT, RT>(st, d, src, alphas, b_base, w, true);
+    Lanes lanes(st);
+    int rc = lanes.rc;
     if (rc) return rc;
+    // aux0: the bias pb (needed only by the apply epilogue); main: factors + W
+    if ((rc = prep<ACT, RT>(lanes.aux[0], d, src, alphas, b_base, w, false, true))) return rc;
+    if ((rc = prep<ACT, RT>(st, d, src, alphas, b_base, w, true, false))) return rc;
     const int64_t kr = static_cast<int64_t>(d.k) * d.r;
     const size_t es = sizeof(ACT);
     if (std::is_same<ACT, float>::value && W_act == reinterpret_cast<ACT*>(W_out)) W_act = nullptr;
@@ -537,6 +591,7 @@ static int fwd_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src
     if (rc) return rc;
     ++g_launches_total;
 
+    if ((rc = lanes.join())) return rc;
     EpiApply<ACT> ea;
     ea.hA = hA; ea.pb = w.pb; ea.gamma = gamma; ea.out = h_mid; ea.T = d.T; ea.d = d.d_B;
     ea.vec = vec_ok(hA, d.d_A, es) && vec_ok(h_mid, d.d_B, es) && vec_ok(w.pb, d.d_B, 4);
@@ -561,8 +616,11 @@ static int bwd_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src
     DWA_CUDA_TRY(cudaMemsetAsync(g_W_base, 0, dd * sizeof(float), st));
     DWA_CUDA_TRY(cudaMemsetAsync(w.dW_acc, 0, static_cast<size_t>(d.B) * d.k * sizeof(float), st));
     DWA_CUDA_TRY(cudaMemsetAsync(w.gamma_acc, 0, sizeof(float), st));
-    int rc = prep<ACT, RT>(st, d, src, alphas, nullptr, w, false);
+    // Three lanes:  main: G -> P      aux0: prep -> gh -> Q      aux1: colsum
+    Lanes lanes(st);
+    int rc = lanes.rc;
     if (rc) return rc;
+    cudaStream_t a0 = lanes.aux[0], a1 = lanes.aux[1];
     ACT* gW = static_cast<ACT*>(w.gW);
 
     EpiG<ACT> eg;
@@ -577,15 +635,31 @@ static int bwd_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src
     if (rc) return rc;
     ++g_launches_total;
 
+    if (d.d_B % 8 == 0 && reinterpret_cast<uintptr_t>(g) % 16 == 0) {
+        dim3 gc((d.d_B + 255) / 256, d.B);
+        DWA_TIMED("colsum", a1, column_sum8_kernel<ACT><<<gc, 512, 0, a1>>>(g, d.T, d.d_B, 0, w.gbias));
+    } else {
+        dim3 gc((d.d_B + 63) / 64, d.B);
+        DWA_TIMED("colsum", a1, column_sum_kernel<ACT><<<gc, 1024, 0, a1>>>(g, d.T, d.d_B, 0, w.gbias));
+    }
+    DWA_LAUNCH_CHECK("colsum_kernel");
+    DWA_TIMED("bias_grad", a1,
+              bias_grad_kernel<<<(d.d_B + 255) / 256, 256, 0, a1>>>(w.gbias, d.B, d.d_B, g_b_base));
+    DWA_LAUNCH_CHECK("bias_grad_kernel");
+    g_launches_total += 2;
+
+    if ((rc = prep<ACT, RT>(a0, d, src, alphas, nullptr, w, true, false))) return rc;
     EpiGhA<ACT> eh;
     eh.g = g; eh.gamma = gamma; eh.out = g_hA; eh.T = d.T; eh.d = d.d_A;
     eh.vec = vec_ok(g, d.d_A, es) && vec_ok(g_hA, d.d_A, es);
     // g W: A(m=t,k=j) = g[t][j] K-major; B(n=i,k=j) = W[j][i] MN-major
     rc = gemm<ACT, false, true>("gemm_gh", g, d.d_B, static_cast<int64_t>(d.T) * d.d_B, Wact, d.d_A, dd, d.T,
-                                d.d_A, d.d_B, d.B, eh, w.status, st);
+                                d.d_A, d.d_B, d.B, eh, w.status, a0);
     if (rc) return rc;
     ++g_launches_total;
 
+    // main: P needs gW (main) and Vs (aux0's prep)
+    if ((rc = lanes.depend(st, a0, 1))) return rc;
     EpiP ep;
     ep.g_rows = g_rows; ep.D = d.D; ep.k = d.k; ep.r = d.r;
     ep.vec = vec_ok(g_rows, d.D, 4);
@@ -595,6 +669,8 @@ static int bwd_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src
     if (rc) return rc;
     ++g_launches_total;
 
+    // aux0: Q needs gW (main's G) and Ug (its own prep)
+    if ((rc = lanes.depend(a0, st, 2))) return rc;
     EpiQ<RT> eq;
     eq.src = src; eq.alphas = alphas; eq.g_rows = g_rows; eq.dW_acc = w.dW_acc; eq.s1 = s1;
     eq.d_A = d.d_A; eq.r = d.r;
@@ -602,22 +678,17 @@ static int bwd_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src
              vec_ok(src.rows, d.D, sizeof(RT));
     // Q = Ug^T gW: A(m=kr,k=j) = Ug[j][m] MN-major; B(n=i,k=j) = gW[j][i] MN-major
     rc = gemm<ACT, true, true>("gemm_Q", w.Ug, w.ldu, static_cast<int64_t>(d.d_B) * w.ldu, gW, d.d_A, dd,
-                               static_cast<int>(kr), d.d_A, d.d_B, d.B, eq, w.status, st);
+                               static_cast<int>(kr), d.d_A, d.d_B, d.B, eq, w.status, a0);
     if (rc) return rc;
     ++g_launches_total;
 
-    dim3 gc((d.d_B + 63) / 64, d.B);
-    DWA_TIMED("colsum", st, column_sum_kernel<ACT><<<gc, 1024, 0, st>>>(g, d.T, d.d_B, 0, w.gbias));
-    DWA_LAUNCH_CHECK("colsum_kernel");
+    if ((rc = lanes.join())) return rc;
     dim3 gf(d.k, d.B);
     DWA_TIMED("finalize", st,
               finalize_kernel<RT><<<gf, 256, 0, st>>>(src, alphas, w.gbias, w.dW_acc, w.gamma_acc, s2,
                                                       d.d_B, g_rows, g_alpha, g_gamma));
     DWA_LAUNCH_CHECK("finalize_kernel");
-    DWA_TIMED("bias_grad", st,
-              bias_grad_kernel<<<(d.d_B + 255) / 256, 256, 0, st>>>(w.gbias, d.B, d.d_B, g_b_base));
-    DWA_LAUNCH_CHECK("bias_grad_kernel");
-    g_launches_total += 3;
+    ++g_launches_total;
     return DWA_OK;
 }
 

@@ -44,6 +44,23 @@ void prof_end(const char* name, cudaStream_t st);
         ::dwa::prof_end(name, st);    \
     } while (0)
 
+// Intra-call concurrency: per-device auxiliary streams and events, created on
+// first use.  A Lanes object holds the device's lock from construction to
+// destruction, so the record/wait pairs of one call are not interleaved with
+// another host thread's.  Everything is stream-ordered (capturable in a graph).
+struct Lanes {
+    cudaStream_t main = nullptr;
+    cudaStream_t aux[2] = {nullptr, nullptr};
+    cudaEvent_t ev[8] = {};
+    int dev = -1;
+    int rc = 0;
+    explicit Lanes(cudaStream_t st);   // forks aux[0], aux[1] off `main`
+    ~Lanes();
+    // `to` waits for everything enqueued so far on `from` (event slot `slot`)
+    int depend(cudaStream_t to, cudaStream_t from, int slot);
+    int join();                         // main waits for both aux streams
+};
+
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 inline size_t dtype_bytes(int dt) { return dt == DWA_BF16 ? 2 : 4; }
 
@@ -149,6 +166,64 @@ __global__ void __launch_bounds__(1024) column_sum_kernel(const T* __restrict__ 
 #pragma unroll
         for (int i = 0; i < 32; ++i) s += part[i][threadIdx.x];
         if (j < d) out[static_cast<int64_t>(b) * d + j] = mean ? s / static_cast<float>(T_) : s;
+    }
+}
+
+// Same sums with 8 consecutive columns per lane (16-byte loads for bf16, two
+// for fp32): grid (ceil(d/256), B), 512 threads; warp w takes rows w, w+16, ...
+// (16 loads in flight per lane); partials added in warp order.  d % 8 == 0 and
+// a 16-byte aligned x required.
+template <class T>
+__global__ void __launch_bounds__(512) column_sum8_kernel(const T* __restrict__ x, int T_, int d,
+                                                          int mean, float* __restrict__ out) {
+    __shared__ float part[16][257];
+    const int b = blockIdx.y, lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int c = blockIdx.x * 256 + 8 * lane;
+    const T* p = x + static_cast<int64_t>(b) * T_ * d;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (c < d) {
+        for (int t0 = w; t0 < T_; t0 += 16 * 16) {
+            float v[16][8];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                const int t = t0 + 16 * u;
+                const T* q = p + static_cast<int64_t>(t) * d + c;
+                if (t < T_) {
+                    if constexpr (sizeof(T) == 2) {
+                        const uint4 r = *reinterpret_cast<const uint4*>(q);
+                        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const float2 f = __bfloat1622float2(h[j]);
+                            v[u][2 * j] = f.x;
+                            v[u][2 * j + 1] = f.y;
+                        }
+                    } else {
+                        const float4 a = reinterpret_cast<const float4*>(q)[0];
+                        const float4 e = reinterpret_cast<const float4*>(q)[1];
+                        v[u][0] = a.x; v[u][1] = a.y; v[u][2] = a.z; v[u][3] = a.w;
+                        v[u][4] = e.x; v[u][5] = e.y; v[u][6] = e.z; v[u][7] = e.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) v[u][j] = 0.f;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 16; ++u)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[j] += v[u][j];
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) part[w][8 * lane + j] = acc[j];
+    __syncthreads();
+    if (threadIdx.x < 256) {
+        const int col = blockIdx.x * 256 + threadIdx.x;
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) s += part[i][threadIdx.x];
+        if (col < d) out[static_cast<int64_t>(b) * d + col] = mean ? s / static_cast<float>(T_) : s;
     }
 }
 

@@ -237,15 +237,15 @@ __global__ void __launch_bounds__(256) query_proj_kernel(const ZT* __restrict__ 
         {
             const ZT* zb = z + static_cast<int64_t>(b0) * d_A;
             const int n = nb * d_A;
-            for (int i0 = threadIdx.x; i0 < n; i0 += blockDim.x * 8) {
-                float t[8];
+            for (int i0 = threadIdx.x; i0 < n; i0 += blockDim.x * 32) {
+                float t[32];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
+                for (int u = 0; u < 32; ++u) {
                     const int i = i0 + u * blockDim.x;
                     t[u] = i < n ? Elem<ZT>::to_f(zb[i]) : 0.f;
                 }
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
+                for (int u = 0; u < 32; ++u) {
                     const int i = i0 + u * blockDim.x;
                     if (i < n) zs[i] = t[u];
                 }
@@ -638,14 +638,25 @@ __global__ void softmax_stats_kernel(const float* __restrict__ partial, int nblk
     if (threadIdx.x == 0) { stats[2 * b] = mx; stats[2 * b + 1] = z; }
 }
 
-__global__ void softmax_apply_kernel(float* __restrict__ sfull, int64_t N, float T,
-                                     const float* __restrict__ stats) {
+// soft_full[b, n] = exp(s/T - M_b) / Z_b in place; 8 elements per thread.
+__global__ void __launch_bounds__(256) softmax_apply_kernel(float* __restrict__ sfull, int64_t N,
+                                                            float T, const float* __restrict__ stats) {
     const int b = blockIdx.y;
     const float mx = stats[2 * b], z = stats[2 * b + 1];
     float* p = sfull + static_cast<int64_t>(b) * N;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < N;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-        p[i] = expf(p[i] / T - mx) / z;
+    const int64_t i0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
+    if (i0 + 8 <= N && (reinterpret_cast<uintptr_t>(p) & 15) == 0 && (N & 3) == 0) {
+        float4 a = reinterpret_cast<const float4*>(p + i0)[0];
+        float4 c = reinterpret_cast<const float4*>(p + i0)[1];
+        a.x = expf(a.x / T - mx) / z; a.y = expf(a.y / T - mx) / z;
+        a.z = expf(a.z / T - mx) / z; a.w = expf(a.w / T - mx) / z;
+        c.x = expf(c.x / T - mx) / z; c.y = expf(c.y / T - mx) / z;
+        c.z = expf(c.z / T - mx) / z; c.w = expf(c.w / T - mx) / z;
+        reinterpret_cast<float4*>(p + i0)[0] = a;
+        reinterpret_cast<float4*>(p + i0)[1] = c;
+    } else {
+        for (int64_t i = i0; i < i0 + 8 && i < N; ++i) p[i] = expf(p[i] / T - mx) / z;
+    }
 }
 
 struct SelectArgs {
@@ -1034,7 +1045,7 @@ extern "C" int dwa_retrieve(void* stream, const DwaRetrieveDims* dims, int use_i
         DWA_TIMED("softmax_stats", st,
                   softmax_stats_kernel<<<d.B, 256, 0, st>>>(w.partial, sf_blocks, w.stats));
         DWA_LAUNCH_CHECK("softmax_stats_kernel");
-        dim3 ga(static_cast<unsigned>(std::min<int64_t>((d.N + 255) / 256, 1184)), d.B);
+        dim3 ga(static_cast<unsigned>((d.N + 2047) / 2048), d.B);
         DWA_TIMED("softmax_apply", st,
                   softmax_apply_kernel<<<ga, 256, 0, st>>>(soft_full, d.N, d.T, w.stats));
         DWA_LAUNCH_CHECK("softmax_apply_kernel");
@@ -1049,13 +1060,25 @@ extern "C" int dwa_sequence_mean(void* stream, int B, int T, int d, int dtype, c
         return fail(DWA_ERR_INVALID_ARG, "dwa_sequence_mean: bad sizes or NULL pointer");
     if (dtype != DWA_F32 && dtype != DWA_BF16) return fail(DWA_ERR_INVALID_ARG, "bad dtype");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    dim3 g((d + 63) / 64, B);
-    if (dtype == DWA_BF16)
-        DWA_TIMED("seq_mean", st, column_sum_kernel<__nv_bfloat16><<<g, 1024, 0, st>>>(
-                                      static_cast<const __nv_bfloat16*>(h_A), T, d, 1, z));
-    else
-        DWA_TIMED("seq_mean", st, column_sum_kernel<float><<<g, 1024, 0, st>>>(
-                                      static_cast<const float*>(h_A), T, d, 1, z));
+    const int es = dtype == DWA_BF16 ? 2 : 4;
+    if (d % 8 == 0 && reinterpret_cast<uintptr_t>(h_A) % 16 == 0) {
+        dim3 g((d + 255) / 256, B);
+        if (dtype == DWA_BF16)
+            DWA_TIMED("seq_mean", st, column_sum8_kernel<__nv_bfloat16><<<g, 512, 0, st>>>(
+                                          static_cast<const __nv_bfloat16*>(h_A), T, d, 1, z));
+        else
+            DWA_TIMED("seq_mean", st, column_sum8_kernel<float><<<g, 512, 0, st>>>(
+                                          static_cast<const float*>(h_A), T, d, 1, z));
+    } else {
+        dim3 g((d + 63) / 64, B);
+        if (dtype == DWA_BF16)
+            DWA_TIMED("seq_mean", st, column_sum_kernel<__nv_bfloat16><<<g, 1024, 0, st>>>(
+                                          static_cast<const __nv_bfloat16*>(h_A), T, d, 1, z));
+        else
+            DWA_TIMED("seq_mean", st, column_sum_kernel<float><<<g, 1024, 0, st>>>(
+                                          static_cast<const float*>(h_A), T, d, 1, z));
+    }
+    (void)es;
     DWA_LAUNCH_CHECK("column_sum_kernel");
     ++g_launches_total;
     return DWA_OK;

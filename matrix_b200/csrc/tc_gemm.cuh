@@ -197,7 +197,8 @@ struct SmemLayout {
 };
 
 // Epilogue protocol.  Epi provides
-//   float operator()(int b, int row, int col0, const float* v, int cnt) const
+//   struct Frag;  void load(int b, int row, int col0, int cnt, Frag&) const
+//   float finish(int b, int row, int col0, const float* v, int cnt, const Frag&) const
 //     v[0..cnt) = C[b](row, col0 + i), cnt <= 8 (col0 a multiple of 8 when
 //     cnt == 8); returns a partial for the reductions;
 //   static constexpr int kReduce;   0 none, 1 per row, 2 per CTA
@@ -333,27 +334,39 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         tc_fence_before();
         asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");
-        // Phase 2: coalesced.  LPR lanes cover one row (8 columns each).
-        constexpr int LPR = BN / 8, RPW = 32 / LPR;
+        // Phase 2: coalesced.  LPR lanes cover one row (8 columns each); each
+        // warp first loads the epilogue operands of PF rows, then finishes them.
+        constexpr int LPR = BN / 8, RPW = 32 / LPR, PF = 4;
+        constexpr int STEP = kEpiWarps * RPW;
         const int sub = lane / LPR, li = lane % LPR;
+        const int col0 = n0 + li * 8;
+        const int cnt = min(8, N - col0);
         float cta_acc = 0.f;
         if (ok) {
-            for (int rr = e * RPW + sub; rr < BM; rr += kEpiWarps * RPW) {
-                const int row = m0 + rr, col0 = n0 + li * 8;
-                const int cnt = min(8, N - col0);
-                float part = 0.f;
-                if (row < M && cnt > 0) {
-                    const float4* src = reinterpret_cast<const float4*>(tile + rr * LD + li * 8);
-                    const float4 a = src[0], b = src[1];
-                    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-                    part = epi(bz, row, col0, v, cnt);
-                }
-                if (Epi::kReduce == 1) {
+            for (int base = e * RPW + sub; base < BM; base += STEP * PF) {
+                typename Epi::Frag frag[PF];
 #pragma unroll
-                    for (int o = LPR / 2; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-                    if (li == 0 && row < M) epi.row_done(bz, row, part);
-                } else if (Epi::kReduce == 2) {
-                    cta_acc += part;
+                for (int u = 0; u < PF; ++u) {
+                    const int rr = base + u * STEP, row = m0 + rr;
+                    if (rr < BM && row < M && cnt > 0) epi.load(bz, row, col0, cnt, frag[u]);
+                }
+#pragma unroll
+                for (int u = 0; u < PF; ++u) {
+                    const int rr = base + u * STEP, row = m0 + rr;
+                    float part = 0.f;
+                    if (rr < BM && row < M && cnt > 0) {
+                        const float4* src = reinterpret_cast<const float4*>(tile + rr * LD + li * 8);
+                        const float4 a = src[0], b = src[1];
+                        const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+                        part = epi.finish(bz, row, col0, v, cnt, frag[u]);
+                    }
+                    if (Epi::kReduce == 1) {
+#pragma unroll
+                        for (int o = LPR / 2; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+                        if (li == 0 && rr < BM && row < M) epi.row_done(bz, row, part);
+                    } else if (Epi::kReduce == 2) {
+                        cta_acc += part;
+                    }
                 }
             }
         }
