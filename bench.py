@@ -8,7 +8,7 @@ top-k 32, gate selection with soft_full, forward + backward).
 
 One JSON line on rank 0.  ``value`` is assembled tokens/s of the whole job
 (all ranks), timed on the device with CUDA events around each step, L2
-flushed (512 MB write) between steps, max over ranks.  One step is replayed
+flushed (512 MB write, then a 256 MB read) between steps, max over ranks.  One step is replayed
 from a CUDA graph of: z = mean_t h_A -> dwa_retrieve -> dwa_assemble_fwd ->
 dwa_assemble_bwd (+ an NCCL all-reduce of the replicated-parameter gradients
 when N > 1, the shard_map transpose of the reference's batch-sharded path).
@@ -144,6 +144,29 @@ class Step:
 
 
 # ------------------------------------------------------ roofline numbers ---
+def profiled_traffic(kernel, w):
+    """DRAM bytes (read + write) per launch of `kernel` at workload `w`, from
+    the `traffic:` lines of the ncu summaries under profiles/.  A summary
+    captured on a smaller case is scaled by the queries x pool rows it
+    processed (the key stream and the s_full writes both grow with them)."""
+    d = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(d):
+        return None
+    for fn in sorted(os.listdir(d)):
+        if not fn.endswith(".txt"):
+            continue
+        with open(os.path.join(d, fn)) as f:
+            for line in f:
+                if not line.startswith("traffic:"):
+                    continue
+                kv = dict(tok.split("=", 1) for tok in line.split()[1:] if "=" in tok)
+                if kv.get("kernel") != kernel:
+                    continue
+                scale = (w.cfg.N * w.batch) / (float(kv["rows"]) * float(kv["queries"]))
+                return int((int(kv["dram_read_bytes"]) + int(kv["dram_write_bytes"])) * scale)
+    return None
+
+
 def kernel_work(w, name):
     """Algorithmic bytes (HBM-bound kernels) or flops (tensor kernels) of one
     launch of `name` on workload w; returns (bound, amount)."""
@@ -371,9 +394,14 @@ def main():
     t = build_device_workload(w, dev, args.seed + rank)
     step = Step(w, t, group)
     flush_buf = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    flush_sink = torch.empty((), dtype=torch.float32, device=dev)
 
     def flush():
+        # write 512 MB (> 126 MB L2), then read back 256 MB of it: the write
+        # evicts the step's data, the read makes the flush's dirty lines be
+        # written back here rather than inside the next timed step
         flush_buf.zero_()
+        flush_sink.copy_(flush_buf[: flush_buf.numel() // 2].sum())
 
     from matrix_b200 import _lib
     step()                       # first call: workspaces, kernel attributes
@@ -505,11 +533,7 @@ def main():
             ach = work / (kms / 1e3) / 1e12
             peak = float(peaks["bf16_tflops"])
             unit = "TFLOP/s"
-        traffic = None
-        tp = os.path.join(ROOT, "profiles", "ncu_traffic.json")
-        if os.path.exists(tp):
-            with open(tp) as f:
-                traffic = json.load(f).get(w.name, {}).get(dominant)
+        traffic = profiled_traffic(dominant, w)
         roof = {"kernel": dominant, "bound": bound, "achieved": ach, "peak": peak, "unit": unit,
                 "frac": ach / peak, "traffic": traffic, "peak_source": peak_src,
                 "algorithmic_per_launch": work, "launch_ms": kms, "timed_in": kern_src}
@@ -522,7 +546,7 @@ def main():
                        "seq_len": w.seq, "parallelism": f"dp{world}",
                        "mode": "warmup" if w.is_warmup else f"gate lambda={w.lambda_val}",
                        "soft_full": w.soft_full, "backward": w.backward,
-                       "l2": "flushed between steps (512 MB write)",
+                       "l2": "flushed between steps (512 MB write, then 256 MB read)",
                        "step": "CUDA graph: seq_mean + dwa_retrieve + dwa_assemble_fwd + dwa_assemble_bwd"
                                + (" + NCCL all_reduce of parameter grads" if world > 1 else "")},
             "value_per_gpu": value / world, "roofline": roof,

@@ -15,11 +15,15 @@
 // and the selection may read them from the full pass when soft_full is on.
 // All scoring is bound by HBM reads of the fp32 key cache.
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 #include <atomic>
 #include <mutex>
 
 #include "dwa_common.cuh"
 #include "tc_gemm.cuh"
+#include "scores_scan.cuh"
+#include "scores_tc.cuh"
 
 namespace dwa {
 
@@ -425,11 +429,11 @@ __global__ void fine_kernel(const float* __restrict__ qw, const float* __restric
 }
 
 // Full-pool scores for up to NB queries at a time; writes raw s_full and per
-// block (max, sum exp) of s/T for the softmax.
+// block (max, sum exp) of s*invT (invT = 1/T) for the softmax.
 template <int NB, int DK>
 __global__ void __launch_bounds__(256) full_scores_kernel(
     const float* __restrict__ qw, const float* __restrict__ keys, int64_t N, int S, int d_k, int B,
-    float T, float* __restrict__ sfull, float* __restrict__ partial) {
+    float invT, float* __restrict__ sfull, float* __restrict__ partial) {
     extern __shared__ __align__(16) float qs[];  // [NB][S][d_k]
     __shared__ float red[33];
     const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -446,7 +450,7 @@ __global__ void __launch_bounds__(256) full_scores_kernel(
             float x = -INFINITY;
             if (row < N) {
                 sfull[static_cast<int64_t>(b0 + q) * N + row] = sc[q];
-                x = sc[q] / T;
+                x = sc[q] * invT;
             }
             const float mx = block_reduce(x, true, red);
             const float e = row < N ? expf(x - mx) : 0.f;
@@ -456,171 +460,6 @@ __global__ void __launch_bounds__(256) full_scores_kernel(
                 partial[(static_cast<int64_t>(b0 + q) * nblk + blockIdx.x) * 2 + 1] = zs;
             }
         }
-    }
-}
-
-// Full-pool scores with the key cache streamed through shared memory by TMA.
-// Persistent CTAs; a work item is (tile of 256 rows, aspect s).  Warp 8 is the
-// producer: one lane issues two 2-D TMA loads per item (floats 0-31 and 32-63
-// of the 256 rows, 128-byte swizzle) into a 3-slot ring.  Warps 0-7 consume:
-// thread t scores row t of the tile for all queries, reading its row through
-// the swizzle (conflict-free).  The arithmetic per (row, aspect, query) is
-// row_scores' (bit-identical scores).  Per query each thread keeps an online
-// (max, sum exp) of s/T; one reduction per CTA at the end.
-constexpr int kFsRows = 256, kFsStages = 3, kFsMaxB = 16;
-constexpr uint32_t kFsHalf = kFsRows * 128, kFsSlot = 2 * kFsHalf;  // 32 KB, 64 KB
-
-__global__ void __launch_bounds__(288, 1) full_scores_tma_kernel(
-    const __grid_constant__ CUtensorMap tm_keys, const float* __restrict__ qw, int64_t N, int S,
-    int B, float T, int ntiles, float* __restrict__ sfull, float* __restrict__ partial,
-    uint32_t* status) {
-    extern __shared__ uint8_t dyn[];
-    uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn) + 1023) & ~uintptr_t(1023));
-    float* qs = reinterpret_cast<float*>(ring + kFsStages * kFsSlot);  // [B][S][64]
-    uint64_t* full = reinterpret_cast<uint64_t*>(qs + B * S * 64);
-    uint64_t* empty = full + kFsStages;
-    __shared__ float red_m[8][kFsMaxB], red_z[8][kFsMaxB];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    {
-        const int n4 = B * S * 16;  // float4s
-        float4 t[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int i = threadIdx.x + u * blockDim.x;
-            if (i < n4) t[u] = reinterpret_cast<const float4*>(qw)[i];
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int i = threadIdx.x + u * blockDim.x;
-            if (i < n4) reinterpret_cast<float4*>(qs)[i] = t[u];
-        }
-    }
-    if (threadIdx.x == 0) {
-        tc::prefetch_tmap(&tm_keys);
-        for (int i = 0; i < kFsStages; ++i) { tc::mbar_init(&full[i], 1); tc::mbar_init(&empty[i], 8); }
-        tc::fence_barrier_init();
-    }
-    __syncthreads();
-    const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-    const int items = my_tiles * S;
-
-    if (warp == 8) {  // producer
-        if (lane == 0) {
-            int issued = 0;
-            for (int it = 0; it < items; ++it) {
-                const int slot = it % kFsStages;
-                if (it >= kFsStages &&
-                    !tc::mbar_wait_bounded(&empty[slot], ((it / kFsStages) - 1) & 1)) {
-                    raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
-                    break;
-                }
-                const int tile = blockIdx.x + (it / S) * gridDim.x, s = it % S;
-                const int y = static_cast<int>(static_cast<int64_t>(s) * N + static_cast<int64_t>(tile) * kFsRows);
-                uint8_t* dst = ring + slot * kFsSlot;
-                tc::mbar_arrive_expect_tx(&full[slot], kFsSlot);
-                tma_load_2d(dst, &tm_keys, &full[slot], 0, y);
-                tma_load_2d(dst + kFsHalf, &tm_keys, &full[slot], 32, y);
-                issued = it + 1;
-            }
-            for (int it = (issued > kFsStages ? issued - kFsStages : 0); it < issued; ++it)
-                if (!tc::mbar_wait_bounded(&full[it % kFsStages], (it / kFsStages) & 1)) {
-                    raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
-                    break;
-                }
-        }
-        __syncwarp();
-        return;
-    }
-
-    const int r = threadIdx.x;  // row within the tile
-    float mrun[kFsMaxB], zrun[kFsMaxB], sc[kFsMaxB];
-#pragma unroll
-    for (int q = 0; q < kFsMaxB; ++q) { mrun[q] = -INFINITY; zrun[q] = 0.f; }
-    bool ok = true;
-    for (int it = 0; it < items && ok; ++it) {
-        const int slot = it % kFsStages, s = it % S;
-        const int tile = blockIdx.x + (it / S) * gridDim.x;
-        if (s == 0) {
-#pragma unroll
-            for (int q = 0; q < kFsMaxB; ++q) sc[q] = 0.f;
-        }
-        if (!tc::mbar_wait_bounded(&full[slot], (it / kFsStages) & 1)) {
-            if (lane == 0) raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
-            ok = false;
-            break;
-        }
-        const uint8_t* base = ring + slot * kFsSlot + r * 128;
-        float4 kv[16];
-#pragma unroll
-        for (int c = 0; c < 16; ++c)
-            kv[c] = *reinterpret_cast<const float4*>(base + (c >> 3) * kFsHalf +
-                                                     (((c & 7) ^ (r & 7)) << 4));
-        __syncwarp();
-        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(&empty[slot])) : "memory");
-        float nrm = 0.f;
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-            nrm = fmaf(kv[c].x, kv[c].x, nrm);
-            nrm = fmaf(kv[c].y, kv[c].y, nrm);
-            nrm = fmaf(kv[c].z, kv[c].z, nrm);
-            nrm = fmaf(kv[c].w, kv[c].w, nrm);
-        }
-        const float den = sqrtf(nrm) + 1e-8f;
-#pragma unroll
-        for (int q = 0; q < kFsMaxB; ++q) {
-            if (q < B) {
-                const float4* qq = reinterpret_cast<const float4*>(qs + (q * S + s) * 64);
-                float dot = 0.f;
-#pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    const float4 qv = qq[c];
-                    dot = fmaf(kv[c].x, qv.x, dot);
-                    dot = fmaf(kv[c].y, qv.y, dot);
-                    dot = fmaf(kv[c].z, qv.z, dot);
-                    dot = fmaf(kv[c].w, qv.w, dot);
-                }
-                sc[q] += dot / den;
-            }
-        }
-        if (s == S - 1) {
-            const int64_t n = static_cast<int64_t>(tile) * kFsRows + r;
-            if (n < N) {
-#pragma unroll
-                for (int q = 0; q < kFsMaxB; ++q) {
-                    if (q < B) {
-                        sfull[static_cast<int64_t>(q) * N + n] = sc[q];
-                        const float x = sc[q] / T;
-                        if (x > mrun[q]) {
-                            zrun[q] = zrun[q] * expf(mrun[q] - x) + 1.f;
-                            mrun[q] = x;
-                        } else {
-                            zrun[q] += expf(x - mrun[q]);
-                        }
-                    }
-                }
-            }
-        }
-    }
-    // CTA reduction of the online statistics (consumer warps only)
-#pragma unroll
-    for (int q = 0; q < kFsMaxB; ++q) {
-        if (q < B) {
-            const float m = warp_max(mrun[q]);
-            float z = (mrun[q] == -INFINITY) ? 0.f : zrun[q] * expf(mrun[q] - m);
-            z = warp_sum(z);
-            if (lane == 0) { red_m[warp][q] = m; red_z[warp][q] = z; }
-        }
-    }
-    asm volatile("bar.sync 1, 256;" ::: "memory");
-    if (threadIdx.x < B) {
-        const int q = threadIdx.x;
-        float M = -INFINITY;
-        for (int w = 0; w < 8; ++w) M = fmaxf(M, red_m[w][q]);
-        float Z = 0.f;
-        for (int w = 0; w < 8; ++w)
-            if (red_m[w][q] != -INFINITY) Z += red_z[w][q] * expf(red_m[w][q] - M);
-        partial[(static_cast<int64_t>(q) * gridDim.x + blockIdx.x) * 2] = M;
-        partial[(static_cast<int64_t>(q) * gridDim.x + blockIdx.x) * 2 + 1] = Z;
     }
 }
 
@@ -638,9 +477,10 @@ __global__ void softmax_stats_kernel(const float* __restrict__ partial, int nblk
     if (threadIdx.x == 0) { stats[2 * b] = mx; stats[2 * b + 1] = z; }
 }
 
-// soft_full[b, n] = exp(s/T - M_b) / Z_b in place; 8 elements per thread.
+// soft_full[b, n] = exp(s*invT - M_b) / Z_b in place (invT = 1/T, the factor the
+// full pass used for M and Z); 8 elements per thread.
 __global__ void __launch_bounds__(256) softmax_apply_kernel(float* __restrict__ sfull, int64_t N,
-                                                            float T, const float* __restrict__ stats) {
+                                                            float invT, const float* __restrict__ stats) {
     const int b = blockIdx.y;
     const float mx = stats[2 * b], z = stats[2 * b + 1];
     float* p = sfull + static_cast<int64_t>(b) * N;
@@ -648,14 +488,14 @@ __global__ void __launch_bounds__(256) softmax_apply_kernel(float* __restrict__ 
     if (i0 + 8 <= N && (reinterpret_cast<uintptr_t>(p) & 15) == 0 && (N & 3) == 0) {
         float4 a = reinterpret_cast<const float4*>(p + i0)[0];
         float4 c = reinterpret_cast<const float4*>(p + i0)[1];
-        a.x = expf(a.x / T - mx) / z; a.y = expf(a.y / T - mx) / z;
-        a.z = expf(a.z / T - mx) / z; a.w = expf(a.w / T - mx) / z;
-        c.x = expf(c.x / T - mx) / z; c.y = expf(c.y / T - mx) / z;
-        c.z = expf(c.z / T - mx) / z; c.w = expf(c.w / T - mx) / z;
+        a.x = expf(a.x * invT - mx) / z; a.y = expf(a.y * invT - mx) / z;
+        a.z = expf(a.z * invT - mx) / z; a.w = expf(a.w * invT - mx) / z;
+        c.x = expf(c.x * invT - mx) / z; c.y = expf(c.y * invT - mx) / z;
+        c.z = expf(c.z * invT - mx) / z; c.w = expf(c.w * invT - mx) / z;
         reinterpret_cast<float4*>(p + i0)[0] = a;
         reinterpret_cast<float4*>(p + i0)[1] = c;
     } else {
-        for (int64_t i = i0; i < i0 + 8 && i < N; ++i) p[i] = expf(p[i] / T - mx) / z;
+        for (int64_t i = i0; i < i0 + 8 && i < N; ++i) p[i] = expf(p[i] * invT - mx) / z;
     }
 }
 
@@ -814,6 +654,7 @@ struct RetWorkspace {
 };
 
 constexpr int kFullRows = 256;
+constexpr int kMaxScanGrid = 1024;            // CTAs of a key scan
 constexpr int64_t kSelectStageKeys = 25600;  // 200 KB of staged keys
 
 static RetWorkspace carve_ret(void* base, const DwaRetrieveDims& d, bool ivf, bool want_sf) {
@@ -834,7 +675,12 @@ static RetWorkspace carve_ret(void* base, const DwaRetrieveDims& d, bool ivf, bo
     const bool full_pass = !ivf || want_sf;
     if (!ivf && !want_sf) w.sfull = c.take<float>(static_cast<size_t>(d.B) * d.N);
     if (full_pass) {
-        w.partial = c.take<float>(static_cast<size_t>(d.B) * w.nblk * 2);
+        // the key scans launch at most min(ceil(N/32), kMaxScanGrid) CTAs (32- or
+        // 64-row blocks), the generic pass ceil(N/256)
+        const size_t part_blocks = std::max<size_t>(
+            static_cast<size_t>(w.nblk),
+            std::min<size_t>(static_cast<size_t>((d.N + 31) / 32), kMaxScanGrid));
+        w.partial = c.take<float>(static_cast<size_t>(d.B) * part_blocks * 2);
         w.stats = c.take<float>(static_cast<size_t>(d.B) * 2);
     }
     w.bytes = c.bytes();
@@ -940,58 +786,142 @@ extern "C" int dwa_retrieve(void* stream, const DwaRetrieveDims* dims, int use_i
         DWA_LAUNCH_CHECK("full_probe_kernel");
         ++g_launches_total;
     }
-    // 3. full-pool raw scores (soft_full or full search)
-    int sf_blocks = w.nblk;
-    const size_t fs_smem = 1024 + static_cast<size_t>(kFsStages) * kFsSlot +
-                           static_cast<size_t>(d.B) * d.S * 64 * sizeof(float) + 2 * kFsStages * 8;
-    CUtensorMap tm_keys;
-    constexpr size_t kFsSmemLimit = 227 * 1024 - 2048;  // leaves room for static shared memory
-    bool use_tma = dk64 && d.B <= kFsMaxB && fs_smem <= kFsSmemLimit &&
-                   static_cast<int64_t>(d.S) * d.N < (int64_t(1) << 31);
-    if (use_tma && (!ivf || want_sf)) {
+    // Scoring variant, the same for the full and the fine pass so both give
+    // bit-identical scores (d_k = 64): the CUDA-core key scan for B <= 16, the
+    // tensor-core key scan for 16 < B <= 32 with S <= 4, else the generic
+    // kernels.  DWA_SCORES=tc (tensor-core scan wherever B <= 32) or
+    // DWA_SCORES=generic select another variant, for comparisons.
+    int dev = 0, dev_sms = 148;
+    DWA_CUDA_TRY(cudaGetDevice(&dev));
+    DWA_CUDA_TRY(cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, dev));
+    dev_sms = std::min(dev_sms, kMaxScanGrid);
+    const char* variant = std::getenv("DWA_SCORES");
+    const bool ask_tc = variant && std::strcmp(variant, "tc") == 0;
+    const bool ask_generic = variant && std::strcmp(variant, "generic") == 0;
+    const bool scan_shape = dk64 && !ask_generic && static_cast<int64_t>(d.S) * d.N < (int64_t(1) << 31);
+    // tensor-core scan
+    const int nq = d.B <= 16 ? 16 : 32;
+    const int tc_stages = sc::ring_stages(nq, d.S);
+    const size_t tc_smem = sc::smem_bytes(tc_stages, nq, d.S);
+    bool use_tc = scan_shape && d.B <= 32 && (ask_tc || d.B > 16) && d.S <= sc::MAXS &&
+                  d.S * nq <= 128 && tc_smem <= sc::kSmemLimit;
+    // CUDA-core scan: full pass with QB query chains, fine pass <8, true>
+    const int qb = d.B <= 4 ? 4 : d.B <= 8 ? 8 : 16;
+    auto scan_full_smem = [&](int st) {
+        return qb == 16 ? ks::smem_bytes<16>(st, 16, d.S) : ks::smem_bytes<8>(st, qb, d.S);
+    };
+    int scan_stages = 0, fine_stages = 0;
+    for (int st = 3; st >= 2 && !scan_stages; --st)
+        if (scan_full_smem(st) <= ks::kSmemLimit) scan_stages = st;
+    for (int st = 3; st >= 2 && !fine_stages; --st)
+        if (ks::smem_bytes<8>(st, d.B, d.S) <= ks::kSmemLimit) fine_stages = st;
+    bool use_scan = scan_shape && !use_tc && d.B <= ks::MAX_QB && scan_stages && fine_stages;
+    CUtensorMap tm_scores;
+    if (use_tc || use_scan) {
         auto enc = tc::tensor_map_encoder();
         cuuint64_t dims2[2] = {64, static_cast<cuuint64_t>(d.S) * static_cast<cuuint64_t>(d.N)};
         cuuint64_t strides2[1] = {64 * sizeof(float)};
-        cuuint32_t box2[2] = {32, static_cast<cuuint32_t>(kFsRows)};
+        cuuint32_t box2[2] = {use_tc ? 32u : static_cast<cuuint32_t>(ks::KQ),
+                              static_cast<cuuint32_t>(use_tc ? sc::BOX : ks::BOX)};
         cuuint32_t es2[2] = {1, 1};
-        use_tma = enc && enc(&tm_keys, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(pool_keys),
-                             dims2, strides2, box2, es2, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+        const bool ok = enc && enc(&tm_scores, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(pool_keys),
+                                   dims2, strides2, box2, es2, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                   use_tc ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+        if (!ok) use_tc = use_scan = false;
     }
-    if ((!ivf || want_sf) && use_tma) {
-        int dev = 0, sms = 148;
-        DWA_CUDA_TRY(cudaGetDevice(&dev));
-        DWA_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-        static bool attr_set[64] = {};
-        if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-            DWA_CUDA_TRY(cudaFuncSetAttribute(full_scores_tma_kernel,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              static_cast<int>(kFsSmemLimit)));
-            if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    static bool tc_attr[2][64] = {}, scan_attr[4][64] = {};
+    const int ti = nq == 16 ? 0 : 1;
+    if (use_tc && (dev < 0 || dev >= 64 || !tc_attr[ti][dev])) {
+        const void* fn = nq == 16 ? reinterpret_cast<const void*>(sc::key_scan_tc_kernel<16>)
+                                  : reinterpret_cast<const void*>(sc::key_scan_tc_kernel<32>);
+        DWA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(sc::kSmemLimit)));
+        if (dev >= 0 && dev < 64) tc_attr[ti][dev] = true;
+    }
+    const int qi = qb == 4 ? 0 : qb == 8 ? 1 : 2;
+    if (use_scan && (dev < 0 || dev >= 64 || !scan_attr[qi][dev] || !scan_attr[3][dev])) {
+        const void* fns[2] = {
+            qb == 4   ? reinterpret_cast<const void*>(ks::key_scan_kernel<4, false>)
+            : qb == 8 ? reinterpret_cast<const void*>(ks::key_scan_kernel<8, false>)
+                      : reinterpret_cast<const void*>(ks::key_scan_kernel<16, false>),
+            reinterpret_cast<const void*>(ks::key_scan_kernel<8, true>)};
+        for (const void* fn : fns)
+            DWA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              static_cast<int>(ks::kSmemLimit)));
+        if (dev >= 0 && dev < 64) scan_attr[qi][dev] = scan_attr[3][dev] = true;
+    }
+    // mode 0: full pass into `out` = s_full [B, N]; mode 1: fine pass into scores [B, K_cap]
+    auto launch_scores = [&](int mode, float* out, int* blocks_out) -> int {
+        kt::Args ka{};
+        ka.N = d.N; ka.S = d.S; ka.B = d.B; ka.invT = 1.f / d.T; ka.mode = mode;
+        ka.qw = w.qw; ka.out = out; ka.partial = w.partial; ka.status = w.status;
+        int rows, box;
+        if (use_tc) {
+            rows = sc::ROWS; box = sc::BOX; ka.stages = tc_stages;
+        } else {
+            rows = mode == 1 ? ks::tile_rows<8>() : qb == 16 ? ks::tile_rows<16>() : ks::tile_rows<8>();
+            box = ks::BOX;
+            ka.stages = mode == 1 ? fine_stages : scan_stages;
         }
-        const int ntiles = static_cast<int>((d.N + kFsRows - 1) / kFsRows);
-        sf_blocks = std::min(ntiles, sms);
-        DWA_TIMED("full_scores", st,
-                  full_scores_tma_kernel<<<sf_blocks, 288, fs_smem, st>>>(
-                      tm_keys, w.qw, d.N, d.S, d.B, d.T, ntiles, sfull, w.partial, w.status));
-        DWA_LAUNCH_CHECK("full_scores_tma_kernel");
+        int64_t work;
+        if (mode == 0) {
+            ka.nblk = (d.N + box - 1) / box;
+            work = ka.nblk;
+        } else {
+            ka.tiles_per_list = (d.max_list + rows - 1) / rows;
+            ka.m = w.m_eff;
+            ka.ntiles = d.B * w.m_eff * ka.tiles_per_list;
+            ka.probe_lo = w.probe_lo; ka.cand_base = w.cand_base; ka.K_cap = w.K_cap;
+            work = ka.ntiles;
+        }
+        const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(work, dev_sms)));
+        const char* name = mode == 0 ? "full_scores" : "fine";
+        if (use_tc) {
+            if (nq == 16)
+                DWA_TIMED(name, st, sc::key_scan_tc_kernel<16><<<blocks, sc::THREADS, tc_smem, st>>>(tm_scores, ka));
+            else
+                DWA_TIMED(name, st, sc::key_scan_tc_kernel<32><<<blocks, sc::THREADS, tc_smem, st>>>(tm_scores, ka));
+            DWA_LAUNCH_CHECK("key_scan_tc_kernel");
+        } else {
+            const size_t smem = mode == 1 ? ks::smem_bytes<8>(fine_stages, d.B, d.S) : scan_full_smem(scan_stages);
+            if (mode == 1)
+                DWA_TIMED(name, st, (ks::key_scan_kernel<8, true><<<blocks, ks::THREADS, smem, st>>>(tm_scores, ka)));
+            else if (qb == 4)
+                DWA_TIMED(name, st, (ks::key_scan_kernel<4, false><<<blocks, ks::THREADS, smem, st>>>(tm_scores, ka)));
+            else if (qb == 8)
+                DWA_TIMED(name, st, (ks::key_scan_kernel<8, false><<<blocks, ks::THREADS, smem, st>>>(tm_scores, ka)));
+            else
+                DWA_TIMED(name, st, (ks::key_scan_kernel<16, false><<<blocks, ks::THREADS, smem, st>>>(tm_scores, ka)));
+            DWA_LAUNCH_CHECK("key_scan_kernel");
+        }
         ++g_launches_total;
+        if (blocks_out) *blocks_out = blocks;
+        return DWA_OK;
+    };
+
+    // 3. full-pool raw scores (soft_full or full search)
+    int sf_blocks = w.nblk;
+    if ((!ivf || want_sf) && (use_tc || use_scan)) {
+        if ((rc = launch_scores(0, sfull, &sf_blocks))) return rc;
     } else if (!ivf || want_sf) {
         constexpr int NB = 8;
         if (dk64)
             DWA_TIMED("full_scores", st,
                       full_scores_kernel<NB, 64><<<w.nblk, kFullRows, NB * qsh, st>>>(
-                          w.qw, pool_keys, d.N, d.S, d.d_k, d.B, d.T, sfull, w.partial));
+                          w.qw, pool_keys, d.N, d.S, d.d_k, d.B, 1.f / d.T, sfull, w.partial));
         else
             DWA_TIMED("full_scores", st,
                       full_scores_kernel<NB, 0><<<w.nblk, kFullRows, NB * qsh, st>>>(
-                          w.qw, pool_keys, d.N, d.S, d.d_k, d.B, d.T, sfull, w.partial));
+                          w.qw, pool_keys, d.N, d.S, d.d_k, d.B, 1.f / d.T, sfull, w.partial));
         DWA_LAUNCH_CHECK("full_scores_kernel");
         ++g_launches_total;
     }
     // 4. fine scores of the probed lists (read from the full pass when it ran)
-    if (ivf && !want_sf) {
+    if (ivf && !want_sf && (use_tc || use_scan)) {
+        if ((rc = launch_scores(1, w.scores, nullptr))) return rc;
+    } else if (ivf && !want_sf) {
         dim3 gf(static_cast<unsigned>((d.max_list + 255) / 256), w.m_eff, d.B);
         if (dk64)
             DWA_TIMED("fine", st, fine_kernel<64><<<gf, 256, qsh, st>>>(
@@ -1047,7 +977,7 @@ extern "C" int dwa_retrieve(void* stream, const DwaRetrieveDims* dims, int use_i
         DWA_LAUNCH_CHECK("softmax_stats_kernel");
         dim3 ga(static_cast<unsigned>((d.N + 2047) / 2048), d.B);
         DWA_TIMED("softmax_apply", st,
-                  softmax_apply_kernel<<<ga, 256, 0, st>>>(soft_full, d.N, d.T, w.stats));
+                  softmax_apply_kernel<<<ga, 256, 0, st>>>(soft_full, d.N, 1.f / d.T, w.stats));
         DWA_LAUNCH_CHECK("softmax_apply_kernel");
         g_launches_total += 2;
     }

@@ -1,0 +1,270 @@
+// Key-cache scan on the CUDA cores: scores of key rows against the queries.
+//
+//   score(row, b) = sum_s  (q[b,s] . k[s,row]) * inv(row, s),
+//   inv(row, s)   = 1 / (sqrt(|k[s,row]|^2) + 1e-8)
+//
+// (src/dwa/retrieval.py:100-118, aspect weights folded into q).  With B <= 16
+// queries there are at most 17 FMAs per key float, so the scan can be bound by
+// HBM; what limits a CUDA-core version is shared memory: every query value a
+// thread multiplies is a broadcast load that costs one wavefront per float per
+// warp.  A thread therefore scores R rows at once (R = 4 for B <= 8), so each
+// query load feeds R rows: per 56 KB of keys about 1.3K wavefront-cycles of
+// shared memory and 1K cycles of FMA issue per SM against 2.5K cycles of HBM.
+//
+// Persistent CTAs of 256 threads (one per SM, ~180 KB shared memory):
+//   warp 0      TMA producer: per item one quarter-aspect (16 floats) of a
+//               tile of ROWS = 224*R rows, as 64-row boxes with 64-byte
+//               swizzle, into a ring of `stages` 56 KB slots; partial tiles
+//               load only the boxes they need
+//   warps 1-7   consumers: thread t of consumer warp w scores rows
+//               w*32R + 32i + lane (i < R).  Per item, 4R conflict-free
+//               16-byte loads take its rows' 16 floats into registers and the
+//               slot is released at once; per 4 floats one broadcast load per
+//               query feeds 4R FMAs, with the |k|^2 chains alongside.  After the last
+//               quarter of an aspect: one IEEE reciprocal per row and
+//               score += dot * inv per (row, query).
+// Full pass: rows split over the CTAs as in key_tiles.cuh; writes s_full
+// [B, N] (coalesced per query) and the online softmax statistics of s/T per
+// query (per warp and tile: max and sum of exp over its rows, merged into lane
+// j's running pair for query j) -> partial [B, grid, 2].  Fine pass: tiles of
+// the probed lists of each query (query b only), written to scores [B, K_cap].
+// A (row, query) score is the same FMA chain in the same order in both passes,
+// so the two passes give bit-identical scores.  Every wait is bounded
+// (DWA_STATUS_WAIT_TIMEOUT).
+#pragma once
+
+#include "key_tiles.cuh"
+
+namespace dwa {
+namespace ks {
+
+// 8 warps: every SM sub-partition holds 2, so a thread may use 255 registers
+// (R*16 key floats and 2*R*QB accumulators live at once).
+constexpr int CONSUMER_WARPS = 7;
+constexpr int THREADS = 32 + 32 * CONSUMER_WARPS;   // 256
+constexpr int BOX = 64;                  // rows per TMA box (4 KB)
+constexpr int KQ = 16;                   // floats per row per item (a quarter of d_k = 64)
+constexpr int MAX_QB = 16;
+constexpr size_t kSmemLimit = 227 * 1024 - 4096;   // leaves room for static shared memory
+
+// Rows per thread for a query block of QB queries (registers: R*16 key floats,
+// R*QB dot and score accumulators).
+template <int QB> constexpr int rows_per_thread() { return QB <= 8 ? 4 : 2; }
+template <int QB> constexpr int tile_rows() { return 32 * rows_per_thread<QB>() * CONSUMER_WARPS; }
+template <int QB> constexpr uint32_t slot_bytes() { return tile_rows<QB>() * KQ * 4; }
+
+// Dynamic shared memory for `stages` slots and nq x S query vectors.
+template <int QB>
+inline size_t smem_bytes(int stages, int nq, int S) {
+    return 1024 + static_cast<size_t>(stages) * slot_bytes<QB>() +
+           static_cast<size_t>(nq) * S * 64 * sizeof(float) + 2 * static_cast<size_t>(stages) * 8;
+}
+
+// QB: queries scored per row (full pass, B <= QB, padded with zero queries);
+// FINE: the fine pass (one query per tile, chains of query t.b only).
+template <int QB, bool FINE>
+__global__ void __launch_bounds__(THREADS, 1) key_scan_kernel(const __grid_constant__ CUtensorMap tm,
+                                                              kt::Args a) {
+    constexpr int R = rows_per_thread<QB>();
+    constexpr int ROWS = tile_rows<QB>();
+    constexpr uint32_t SLOT = slot_bytes<QB>();
+    constexpr int J = FINE ? 1 : QB;   // query chains per row
+    extern __shared__ uint8_t dyn[];
+    const int stages = a.stages, S = a.S;
+    uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn) + 1023) & ~uintptr_t(1023));
+    const int nq = FINE ? a.B : QB;    // query vectors staged
+    float* qs = reinterpret_cast<float*>(ring + static_cast<size_t>(stages) * SLOT);   // [nq][S][64]
+    uint64_t* full = reinterpret_cast<uint64_t*>(qs + nq * S * 64);
+    uint64_t* empty = full + stages;
+    __shared__ float red_m[CONSUMER_WARPS][32], red_z[CONSUMER_WARPS][32];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        tc::prefetch_tmap(&tm);
+        for (int i = 0; i < stages; ++i) {
+            tc::mbar_init(&full[i], 1);
+            tc::mbar_init(&empty[i], CONSUMER_WARPS);
+        }
+        tc::fence_barrier_init();
+    }
+    __syncthreads();
+
+    int64_t row_lo, row_hi;
+    const int ntile = kt::tile_count<ROWS, BOX>(a, blockIdx.x, gridDim.x, row_lo, row_hi);
+
+    if (warp == 0) {
+        // ------------------------------------------------------- producer
+        if (lane == 0) {
+            int it = 0;
+            bool ok = true;
+            for (int i = 0; i < ntile && ok; ++i) {
+                const kt::Tile t = kt::tile_at<ROWS>(a, i, blockIdx.x, gridDim.x, row_lo, row_hi);
+                if (!t.valid) continue;
+                const int nbox = (t.rows + BOX - 1) / BOX;
+                for (int s = 0; s < S && ok; ++s) {
+                    for (int kq = 0; kq < 4; ++kq, ++it) {
+                        const int slot = it % stages;
+                        if (it >= stages && !tc::mbar_wait_bounded(&empty[slot], ((it / stages) - 1) & 1)) {
+                            raise_status(a.status, DWA_STATUS_WAIT_TIMEOUT);
+                            ok = false;
+                            break;
+                        }
+                        const int y = static_cast<int>(static_cast<int64_t>(s) * a.N + t.row0);
+                        uint8_t* dst = ring + static_cast<size_t>(slot) * SLOT;
+                        tc::mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(nbox) * BOX * KQ * 4);
+                        for (int bx = 0; bx < nbox; ++bx)
+                            kt::tma_load_2d(dst + bx * BOX * KQ * 4, &tm, &full[slot], kq * KQ, y + bx * BOX);
+                    }
+                }
+            }
+            // drain: the last issued loads must have landed before exit
+            for (int i = (it > stages ? it - stages : 0); i < it; ++i)
+                if (!tc::mbar_wait_bounded(&full[i % stages], (i / stages) & 1)) {
+                    raise_status(a.status, DWA_STATUS_WAIT_TIMEOUT);
+                    break;
+                }
+        }
+        __syncwarp();
+        return;
+    }
+
+    // ----------------------------------------------------------- consumers
+    // the queries are staged while the producer's first loads are in flight
+    for (int i = threadIdx.x - 32; i < nq * S * 16; i += 32 * CONSUMER_WARPS) {
+        const int qb = i / (S * 16);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (qb < a.B) v = reinterpret_cast<const float4*>(a.qw)[i];
+        reinterpret_cast<float4*>(qs)[i] = v;
+    }
+    asm volatile("bar.sync 2, %0;" ::"r"(CONSUMER_WARPS * 32) : "memory");
+    const int cw = warp - 1;
+    const int rbase = cw * 32 * R + lane;   // tile row of chain i: rbase + 32*i
+    const float invT = a.invT;
+    float m_run = -INFINITY, z_run = 0.f;   // lane j: statistics of query j over this warp's rows
+    int it = 0;
+    bool ok = true;
+    for (int ti = 0; ti < ntile && ok; ++ti) {
+        const kt::Tile t = kt::tile_at<ROWS>(a, ti, blockIdx.x, gridDim.x, row_lo, row_hi);
+        if (!t.valid) continue;
+        const bool warp_active = cw * 32 * R < t.rows;
+        const float* qt = FINE ? qs + t.b * S * 64 : qs;
+        float sc[R][J], dot[R][J], nrm[R];
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+            nrm[i] = 0.f;
+#pragma unroll
+            for (int j = 0; j < J; ++j) { sc[i][j] = 0.f; dot[i][j] = 0.f; }
+        }
+        for (int s = 0; s < S && ok; ++s) {
+            for (int kq = 0; kq < 4; ++kq, ++it) {
+                const int slot = it % stages;
+                if (!tc::mbar_wait_bounded(&full[slot], (it / stages) & 1)) {
+                    if (lane == 0) raise_status(a.status, DWA_STATUS_WAIT_TIMEOUT);
+                    ok = false;
+                    break;
+                }
+                if (!warp_active) {
+                    __syncwarp();
+                    if (lane == 0) kt::mbar_arrive(&empty[slot]);
+                    continue;
+                }
+                const uint8_t* sp = ring + static_cast<size_t>(slot) * SLOT;
+                const float* qa = qt + s * 64 + kq * KQ;   // query j of this quarter: qa + j*S*64
+                float4 kv[R][4];
+#pragma unroll
+                for (int i = 0; i < R; ++i) {
+                    const int rr = rbase + 32 * i;
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+                        kv[i][c] = *reinterpret_cast<const float4*>(sp + rr * (KQ * 4) + ((c ^ ((rr >> 1) & 3)) << 4));
+                }
+                __syncwarp();
+                if (lane == 0) kt::mbar_arrive(&empty[slot]);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+#pragma unroll
+                    for (int i = 0; i < R; ++i) {
+                        nrm[i] = fmaf(kv[i][c].x, kv[i][c].x, nrm[i]);
+                        nrm[i] = fmaf(kv[i][c].y, kv[i][c].y, nrm[i]);
+                        nrm[i] = fmaf(kv[i][c].z, kv[i][c].z, nrm[i]);
+                        nrm[i] = fmaf(kv[i][c].w, kv[i][c].w, nrm[i]);
+                    }
+#pragma unroll
+                    for (int j = 0; j < J; ++j) {
+                        const float4 qv = *reinterpret_cast<const float4*>(qa + j * S * 64 + c * 4);
+#pragma unroll
+                        for (int i = 0; i < R; ++i) {
+                            dot[i][j] = fmaf(kv[i][c].x, qv.x, dot[i][j]);
+                            dot[i][j] = fmaf(kv[i][c].y, qv.y, dot[i][j]);
+                            dot[i][j] = fmaf(kv[i][c].z, qv.z, dot[i][j]);
+                            dot[i][j] = fmaf(kv[i][c].w, qv.w, dot[i][j]);
+                        }
+                    }
+                }
+                if (kq == 3) {
+#pragma unroll
+                    for (int i = 0; i < R; ++i) {
+                        const float inv = 1.f / (sqrtf(nrm[i]) + 1e-8f);
+#pragma unroll
+                        for (int j = 0; j < J; ++j) { sc[i][j] = fmaf(dot[i][j], inv, sc[i][j]); dot[i][j] = 0.f; }
+                        nrm[i] = 0.f;
+                    }
+                }
+            }
+        }
+        if (!ok || !warp_active) continue;
+        if (!FINE) {
+#pragma unroll
+            for (int j = 0; j < QB; ++j) {
+                if (j < a.B) {
+                    float x[R], mt = -INFINITY;
+#pragma unroll
+                    for (int i = 0; i < R; ++i) {
+                        const int rr = rbase + 32 * i;
+                        const bool valid = rr < t.rows;
+                        if (valid) a.out[static_cast<int64_t>(j) * a.N + t.row0 + rr] = sc[i][j];
+                        x[i] = valid ? sc[i][j] * invT : -INFINITY;
+                        mt = fmaxf(mt, x[i]);
+                    }
+                    mt = warp_max(mt);
+                    if (mt != -INFINITY) {
+                        float e = 0.f;
+#pragma unroll
+                        for (int i = 0; i < R; ++i) e += __expf(x[i] - mt);
+                        const float zt = warp_sum(e);
+                        if (lane == j) {
+                            const float mn = fmaxf(m_run, mt);
+                            z_run = z_run * __expf(m_run - mn) + zt * __expf(mt - mn);
+                            m_run = mn;
+                        }
+                    }
+                }
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < R; ++i) {
+                const int rr = rbase + 32 * i;
+                if (rr < t.rows) a.out[static_cast<int64_t>(t.b) * a.K_cap + t.obase + rr] = sc[i][0];
+            }
+        }
+    }
+    if (!FINE) {
+        // CTA reduction of the online statistics (consumer warps only)
+        red_m[cw][lane] = m_run;
+        red_z[cw][lane] = z_run;
+        asm volatile("bar.sync 1, %0;" ::"r"(CONSUMER_WARPS * 32) : "memory");
+        if (cw == 0 && lane < a.B && lane < QB) {
+            const int j = lane;
+            float M = -INFINITY;
+            for (int w = 0; w < CONSUMER_WARPS; ++w) M = fmaxf(M, red_m[w][j]);
+            float Z = 0.f;
+            for (int w = 0; w < CONSUMER_WARPS; ++w)
+                if (red_m[w][j] != -INFINITY) Z += red_z[w][j] * expf(red_m[w][j] - M);
+            a.partial[(static_cast<int64_t>(j) * gridDim.x + blockIdx.x) * 2] = M;
+            a.partial[(static_cast<int64_t>(j) * gridDim.x + blockIdx.x) * 2 + 1] = Z;
+        }
+    }
+}
+
+}  // namespace ks
+}  // namespace dwa

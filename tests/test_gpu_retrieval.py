@@ -99,6 +99,42 @@ def test_zipf_csr_lists_match_oracle(is_warmup, lam):
     assert_close(sf, rsf, TOL, name="soft_full")
 
 
+@pytest.mark.parametrize("variant", ["default", "tc", "generic"])
+@pytest.mark.parametrize("B,seed", [(3, 30), (8, 31), (13, 31), (20, 31)])
+def test_batch_sizes_across_scoring_variants_match_oracle(B, seed, variant, monkeypatch):
+    """Every scoring kernel on batches that take each of its code paths.
+
+    default: the CUDA-core key scan with 4, 8 and 16 query chains (batch 3, 8,
+    13) and the tensor-core scan with N = 32 (batch 20); tc (DWA_SCORES=tc): the
+    tensor-core scan with N = 16 (batch 3, 8, 13) and N = 32; generic
+    (DWA_SCORES=generic): the generic kernels.  N = 19967 is not a multiple of
+    the TMA boxes and the largest Zipf(1.1) list (5416 rows) spans several
+    fine-pass tiles.  Indices equal the oracle's (seeds checked for a 1e-5 gap
+    at the list and top-k boundaries), and the fine pass selects
+    bit-identically to the full pass."""
+    if variant != "default":
+        monkeypatch.setenv("DWA_SCORES", variant)
+    cfg = DWAConfig(D=17 * 64, N=41 * 487, use_ivf=True, C=41, m=5, d_A=64, d_B=64, r=8, k_max=24,
+                    S=4, d_k=64, T=1.0, gamma_init=0.1, bf16_pool=False)
+    x = make_inputs(cfg, B, 8, seed, variant="rich", zipf=1.1)
+    off = x.list_offsets
+    max_list = int(np.diff(off).max())
+    f = np.float64
+    for is_warmup, lam in ((True, 1.0), (False, 5.0)):
+        a, i, sf = _gpu_retrieve(cfg, x, lam, is_warmup, True, offsets=off, max_list=max_list)
+        a2, i2, _ = _gpu_retrieve(cfg, x, lam, is_warmup, False, offsets=off, max_list=max_list)
+        ra, ri, rsf = O.retrieve(
+            x.z.astype(f), x.W_Q.astype(f), x.aspect_weights.astype(f), f(x.tau),
+            x.centroids.astype(f), x.keys.astype(f), k=cfg.k_max, m=cfg.m, T=cfg.T,
+            lambda_val=lam, is_warmup=is_warmup, list_offsets=off, tie_break="index")
+        tag = f"{variant} B={B} warmup={is_warmup}"
+        np.testing.assert_array_equal(i, ri, err_msg=tag)
+        assert_close(a, ra, TOL, name=f"alphas {tag}")
+        assert_close(sf, rsf, TOL, name=f"soft_full {tag}")
+        np.testing.assert_array_equal(i2, i, err_msg=f"fine pass {tag}")
+        np.testing.assert_array_equal(a2, a, err_msg=f"fine pass {tag}")
+
+
 @pytest.mark.parametrize("is_warmup,lam", [(True, 1.0), (False, 5.0)])
 def test_full_search_matches_oracle(is_warmup, lam):
     from test_oracle_golden import _inputs
