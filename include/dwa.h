@@ -182,6 +182,48 @@ DWA_API int dwa_retrieve(void* stream, const DwaRetrieveDims* dims, int use_ivf,
                  void* workspace, size_t workspace_bytes);
 
 /* ---------------------------------------------------------------------------
+ * Row-sharded retrieval over P ranks.  Replaces the model-sharded branch of
+ * MultiAspectRetrieval.__call__ (src/dwa/retrieval.py:74-79, 121-138: IVF off,
+ * every rank scores its pool rows, scores all-gathered) and the masked-psum
+ * gather of the winners (src/dwa/model.py:16-47), keeping IVF on: rank p
+ * holds the keys of pool rows [row_lo, row_lo + N) (whole lists, or any
+ * contiguous slice); centroids, W_Q, aspect weights, tau and the global
+ * list_offsets are replicated.  Per call:
+ *   1. dwa_retrieve_local on every rank: the same coarse top-m lists, the
+ *      rank's part of them scored, its top-k written as a summary
+ *      [B, 2k+3] f32 (k scores best first, k global rows as int32 bits, the
+ *      partial gate sum, the soft_full max and sum of exp(s/T - max)), and
+ *      soft_full (if given) [B, N] left as raw scores of the rank's rows.
+ *   2. an all-gather of the summaries into [P, B, 2k+3] (NCCL, by the caller).
+ *   3. dwa_retrieve_merge on every rank: the global top-k (ties to the lower
+ *      pool row), alphas and indices exactly as dwa_retrieve defines them,
+ *      and the rank's soft_full slice normalised with the merged statistics.
+ * The result equals dwa_retrieve on the whole pool (indices bit-exact; alphas
+ * and soft_full up to the order of the partial sums).
+ * dims: the local call's N is the rank's row count (workspace from
+ * dwa_retrieve_workspace_bytes with those dims); the merge's N is the row
+ * count of the soft_full slice it normalises (0 without soft_full).
+ * ------------------------------------------------------------------------- */
+typedef struct DwaShard {
+    int64_t row_lo;    /* global pool row of the rank's first key row */
+    int64_t n_global;  /* rows of the whole pool (< 2^31) */
+} DwaShard;
+
+DWA_API int dwa_retrieve_local(void* stream, const DwaRetrieveDims* dims, const DwaShard* shard,
+                               int use_ivf, int is_warmup, const float* lambda_val, const void* z,
+                               const float* W_Q, const float* aspect_weights, const float* tau,
+                               const float* centroids, const int64_t* list_offsets,
+                               const float* pool_keys, float* summary, float* soft_full,
+                               void* workspace, size_t workspace_bytes);
+
+DWA_API size_t dwa_retrieve_merge_workspace_bytes(const DwaRetrieveDims* dims);
+
+DWA_API int dwa_retrieve_merge(void* stream, const DwaRetrieveDims* dims, int world,
+                               const float* summaries, int is_warmup, const float* lambda_val,
+                               const float* tau, float* alphas, int32_t* indices, float* soft_full,
+                               void* workspace, size_t workspace_bytes);
+
+/* ---------------------------------------------------------------------------
  * Retrieval without a workspace.  No counterpart in the reference: it exists for
  * callers that cannot hand this library scratch memory or let it allocate, such
  * as a legacy XLA custom-call target that receives only its operand and result

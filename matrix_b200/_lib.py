@@ -43,6 +43,10 @@ class RetrieveDims(C.Structure):
                 ("N", C.c_int64), ("T", C.c_float), ("z_dtype", C.c_int32)]
 
 
+class Shard(C.Structure):
+    _fields_ = [("row_lo", C.c_int64), ("n_global", C.c_int64)]
+
+
 _P = C.c_void_p
 _SIGNATURES = {
     "dwa_version": (C.c_char_p, []),
@@ -64,6 +68,11 @@ _SIGNATURES = {
                                _P, _P, _P, _P, _P, _P, _P, C.c_size_t]),
     "dwa_retrieve_noalloc": (C.c_int, [_P, C.POINTER(RetrieveDims), C.c_int, C.c_int, _P, _P, _P,
                                        _P, _P, _P, _P, _P, _P, _P, _P]),
+    "dwa_retrieve_local": (C.c_int, [_P, C.POINTER(RetrieveDims), C.POINTER(Shard), C.c_int, C.c_int,
+                                     _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t]),
+    "dwa_retrieve_merge_workspace_bytes": (C.c_size_t, [C.POINTER(RetrieveDims)]),
+    "dwa_retrieve_merge": (C.c_int, [_P, C.POINTER(RetrieveDims), C.c_int, _P, C.c_int, _P, _P, _P,
+                                     _P, _P, _P, C.c_size_t]),
 }
 
 _lib = None

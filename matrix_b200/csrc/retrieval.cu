@@ -31,6 +31,14 @@ extern std::atomic<uint64_t> g_launches_total;
 
 constexpr int kMaxK = 256;  // top-k / top-m capacity of the block selection
 
+// Summary of one query on one rank of a sharded call, 2k+3 floats:
+//   [0, k)    scores s of the rank's top-k candidates, best first (-inf: none)
+//   [k, 2k)   their global pool rows as int32 bits (-1: none)
+//   [2k]      sum of raw over the rank's candidates (gate mode; 0 in warmup)
+//   [2k+1]    max of s/T over the rank's rows (soft_full), [2k+2] sum exp(s/T - max)
+__host__ __device__ constexpr int summary_width(int k) { return 2 * k + 3; }
+
+
 // ------------------------------------------------------------- scoring -----
 // sc[q] = sum_s (qw[q][s] . key_s) / (sqrt(|key_s|^2) + 1e-8)   for one row.
 // DK > 0: d_k is the compile-time DK (fully unrolled, all loads of an aspect in
@@ -365,10 +373,14 @@ __global__ void __launch_bounds__(1024) coarse_kernel(const float* __restrict__ 
 
 constexpr int kStageKeys = 6144;  // candidates staged in shared memory (48 KB of keys)
 
+// Top-m lists per query (ties to the lower list) and each probed list's
+// candidate range.  [row_lo, row_hi) is the window of pool rows whose keys this
+// call holds (the whole pool, or one rank's slice): a list's candidates are its
+// rows inside the window, as local key rows; n_global bounds the list offsets.
 __global__ void __launch_bounds__(512) topm_kernel(
     const float* __restrict__ c_score, int C, int m, const int64_t* __restrict__ list_off,
-    int64_t N, int max_list, int32_t* __restrict__ top_clusters, int64_t* __restrict__ probe_lo,
-    int64_t* __restrict__ cand_base, uint32_t* status) {
+    int64_t n_global, int64_t row_lo, int64_t row_hi, int max_list, int32_t* __restrict__ top_clusters,
+    int64_t* __restrict__ probe_lo, int64_t* __restrict__ cand_base, uint32_t* status) {
     __shared__ uint64_t sel_key[kMaxK];
     __shared__ int64_t sel_pos[kMaxK];
     extern __shared__ uint64_t skeys[];
@@ -389,11 +401,14 @@ __global__ void __launch_bounds__(512) topm_kernel(
     for (int j = threadIdx.x; j < m; j += blockDim.x) {
         const int c = j < got ? static_cast<int>(sel_pos[j]) : 0;
         int64_t lo = list_off[c], hi = list_off[c + 1];
-        if (lo < 0 || hi < lo || hi > N) { raise_status(status, DWA_STATUS_BAD_LIST); lo = hi = 0; }
-        int64_t sz = hi - lo;
-        if (sz > max_list) { raise_status(status, DWA_STATUS_LIST_OVERFLOW); sz = max_list; }
+        if (lo < 0 || hi < lo || hi > n_global) { raise_status(status, DWA_STATUS_BAD_LIST); lo = hi = 0; }
+        if (hi - lo > max_list) raise_status(status, DWA_STATUS_LIST_OVERFLOW);
+        lo = lo > row_lo ? lo : row_lo;
+        hi = hi < row_hi ? hi : row_hi;
+        int64_t sz = hi > lo ? hi - lo : 0;
+        if (sz > max_list) sz = max_list;
         top_clusters[static_cast<int64_t>(b) * m + j] = c;
-        probe_lo[static_cast<int64_t>(b) * (m + 1) + j] = lo;
+        probe_lo[static_cast<int64_t>(b) * (m + 1) + j] = sz > 0 ? lo - row_lo : 0;
         s_sz[j] = sz;
     }
     __syncthreads();
@@ -463,8 +478,28 @@ __global__ void __launch_bounds__(256) full_scores_kernel(
     }
 }
 
+// The summary of a rank that holds no rows: no candidates, no soft_full mass.
+__global__ void empty_summary_kernel(float* summary, int k) {
+    float* sm = summary + static_cast<int64_t>(blockIdx.x) * summary_width(k);
+    for (int i = threadIdx.x; i < k; i += blockDim.x) {
+        sm[i] = -INFINITY;
+        sm[k + i] = __int_as_float(-1);
+    }
+    if (threadIdx.x == 0) { sm[2 * k] = 0.f; sm[2 * k + 1] = -INFINITY; sm[2 * k + 2] = 0.f; }
+}
+
+// A rank without soft_full: statistics that contribute nothing to the merge.
+__global__ void fill_stats_kernel(float* stats, int B, int stride) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    stats[static_cast<int64_t>(b) * stride] = -INFINITY;
+    stats[static_cast<int64_t>(b) * stride + 1] = 0.f;
+}
+
+// (max, sum exp) of s/T per query from the per-CTA pairs of the full pass,
+// written to stats[b * stride + {0, 1}].
 __global__ void softmax_stats_kernel(const float* __restrict__ partial, int nblk,
-                                     float* __restrict__ stats) {
+                                     float* __restrict__ stats, int stride) {
     __shared__ float red[33];
     const int b = blockIdx.x;
     const float* p = partial + static_cast<int64_t>(b) * nblk * 2;
@@ -474,7 +509,7 @@ __global__ void softmax_stats_kernel(const float* __restrict__ partial, int nblk
     float z = 0.f;
     for (int i = threadIdx.x; i < nblk; i += blockDim.x) z += p[2 * i + 1] * expf(p[2 * i] - mx);
     z = block_reduce(z, false, red);
-    if (threadIdx.x == 0) { stats[2 * b] = mx; stats[2 * b + 1] = z; }
+    if (threadIdx.x == 0) { stats[static_cast<int64_t>(b) * stride] = mx; stats[static_cast<int64_t>(b) * stride + 1] = z; }
 }
 
 // soft_full[b, n] = exp(s*invT - M_b) / Z_b in place (invT = 1/T, the factor the
@@ -514,11 +549,43 @@ struct SelectArgs {
     float* alphas;
     int32_t* indices;
     uint32_t* status;
+    int64_t row_lo;     // global pool row of local key row 0
+    float* summary;     // non-null: a rank's part of a sharded call, [B, 2k+3] (see below)
 };
 
 __device__ __forceinline__ float gate_raw(float s, float lam, float tau, float T) {
     const float g = 1.f / (1.f + expf(-(lam * (s - tau))));
     return g * expf(s / T);
+}
+
+// alphas and indices of one query from its got <= k winners (scores s_sv, global
+// rows rows_sv, best first), run by one warp (retrieval.py:143-158): warmup
+// softmax(top / T); gate raw / (Z + 1e-8), then / (sum top + 1e-8).  Shared by
+// the single-call selection and the merge of a sharded call.
+__device__ void write_alphas(int got, int k, bool gate, float lam, float tau, float T, float Z,
+                             float* s_sv, const int64_t* rows_sv, float* al, int32_t* ix) {
+    const int l = threadIdx.x & 31;
+    if (!gate) {
+        // softmax(top / T) (retrieval.py:146); s_sv[0] is the maximum
+        const float mx = got > 0 ? s_sv[0] / T : 0.f;
+        float den = 0.f;
+        for (int i = l; i < got; i += 32) den += expf(s_sv[i] / T - mx);
+        den = warp_sum(den);
+        for (int i = l; i < got; i += 32) al[i] = expf(s_sv[i] / T - mx) / den;
+    } else {
+        // raw / (sum raw + 1e-8), then / (sum top + 1e-8) (retrieval.py:150-155)
+        float tot = 0.f;
+        for (int i = l; i < got; i += 32) {
+            const float v = gate_raw(s_sv[i], lam, tau, T) / (Z + 1e-8f);
+            s_sv[i] = v;
+            tot += v;
+        }
+        tot = warp_sum(tot);
+        for (int i = l; i < got; i += 32) al[i] = s_sv[i] / (tot + 1e-8f);
+    }
+    for (int i = l; i < got; i += 32) ix[i] = static_cast<int32_t>(rows_sv[i]);
+    __syncwarp();
+    for (int i = got + l; i < k; i += 32) { al[i] = 0.f; ix[i] = got > 0 ? static_cast<int32_t>(rows_sv[0]) : 0; }
 }
 
 // One block per query.  STAGED: the candidate keys (and the gate sum) are
@@ -555,7 +622,7 @@ __global__ void __launch_bounds__(1024) select_kernel(SelectArgs a) {
         const float s = locate(pos, &row);
         const float raw = gate ? gate_raw(s, lam, tau, T) : 0.f;
         *raw_out = raw;
-        return make_key(rank_raw ? raw : s, static_cast<uint32_t>(row));
+        return make_key(rank_raw ? raw : s, static_cast<uint32_t>(row + a.row_lo));
     };
     float Z = 0.f;
     int got;
@@ -571,7 +638,7 @@ __global__ void __launch_bounds__(1024) select_kernel(SelectArgs a) {
                                         : a.scores[static_cast<int64_t>(b) * a.K_cap + base + r];
                 const float raw = gate ? gate_raw(s, lam, tau, T) : 0.f;
                 acc += raw;
-                skeys[base + r] = make_key(rank_raw ? raw : s, static_cast<uint32_t>(row));
+                skeys[base + r] = make_key(rank_raw ? raw : s, static_cast<uint32_t>(row + a.row_lo));
             }
         }
         if (gate) Z = block_reduce(acc, false, red);
@@ -591,40 +658,106 @@ __global__ void __launch_bounds__(1024) select_kernel(SelectArgs a) {
         auto key_at = [&](int64_t pos) { float raw; return key_of(pos, &raw); };
         got = block_topk(n, a.k, key_at, sel_key, sel_pos);
     }
-    // winners' scores and rows, one thread each
+    // winners' scores and global rows, one thread each
     __shared__ float s_sv[kMaxK];
     for (int i = threadIdx.x; i < got; i += blockDim.x) {
         int64_t row;
         s_sv[i] = locate(sel_pos[i], &row);
-        sel_pos[i] = row;
+        sel_pos[i] = row + a.row_lo;
+    }
+    __syncthreads();
+    if (a.summary) {
+        float* sm = a.summary + static_cast<int64_t>(b) * summary_width(a.k);
+        for (int i = threadIdx.x; i < a.k; i += blockDim.x) {
+            sm[i] = i < got ? s_sv[i] : -INFINITY;
+            sm[a.k + i] = __int_as_float(i < got ? static_cast<int32_t>(sel_pos[i]) : -1);
+        }
+        if (threadIdx.x == 0) sm[2 * a.k] = gate ? Z : 0.f;
+        return;
+    }
+    if (threadIdx.x < 32) {
+        if (threadIdx.x == 0 && got < a.k) raise_status(a.status, DWA_STATUS_FEW_CANDIDATES);
+        write_alphas(got, a.k, gate, lam, tau, T, Z, s_sv, sel_pos, a.alphas + static_cast<int64_t>(b) * a.k,
+                     a.indices + static_cast<int64_t>(b) * a.k);
+    }
+}
+
+// Merge of a sharded call: per query, the global top-k of the world ranks'
+// summaries (ties to the lower global row), Z = sum of the ranks' partial
+// sums in rank order, alphas as in the single call; and the soft_full
+// statistics (max, sum exp) of s/T combined over the ranks into stats[b].
+struct MergeArgs {
+    const float* summaries;   // [world, B, 2k+3]
+    int world, B, k;
+    float T;
+    int is_warmup;
+    const float* lambda_val;
+    const float* tau;
+    float* alphas;
+    int32_t* indices;
+    float* stats;             // [B, 2] or null
+    uint32_t* status;
+};
+
+__global__ void __launch_bounds__(1024) merge_kernel(MergeArgs a) {
+    __shared__ uint64_t sel_key[kMaxK];
+    __shared__ int64_t sel_pos[kMaxK];
+    __shared__ float s_sv[kMaxK];
+    __shared__ int s_valid;
+    extern __shared__ uint64_t mkeys[];
+    const int b = blockIdx.x, W = summary_width(a.k);
+    const float lam = __ldg(a.lambda_val), tau = __ldg(a.tau), T = a.T;
+    const bool gate = !a.is_warmup;
+    const bool rank_raw = gate && lam < 0.f;
+    const int n = a.world * a.k;
+    if (threadIdx.x == 0) s_valid = 0;
+    __syncthreads();
+    int valid = 0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float* sm = a.summaries + (static_cast<int64_t>(i / a.k) * a.B + b) * W;
+        const int j = i % a.k;
+        const int32_t row = __float_as_int(sm[a.k + j]);
+        const float sv = sm[j];
+        // a missing candidate gets its position as key: distinct, and below
+        // every real key (whose top 32 bits are an ordered float >= 2^23)
+        mkeys[i] = row >= 0 ? make_key(rank_raw ? gate_raw(sv, lam, tau, T) : sv, static_cast<uint32_t>(row))
+                            : static_cast<uint64_t>(i);
+        valid += row >= 0;
+    }
+    atomicAdd(&s_valid, valid);
+    __syncthreads();
+    auto key_at = [&](int64_t i) { return mkeys[i]; };
+    int got = block_topk(n, a.k, key_at, sel_key, sel_pos);
+    got = got < s_valid ? got : s_valid;
+    for (int i = threadIdx.x; i < got; i += blockDim.x) {
+        const int64_t pos = sel_pos[i];
+        const float* sm = a.summaries + ((pos / a.k) * a.B + b) * W;
+        s_sv[i] = sm[pos % a.k];
+        sel_pos[i] = __float_as_int(sm[a.k + pos % a.k]);
     }
     __syncthreads();
     if (threadIdx.x < 32) {
-        const int l = threadIdx.x;
-        if (l == 0 && got < a.k) raise_status(a.status, DWA_STATUS_FEW_CANDIDATES);
-        float* al = a.alphas + static_cast<int64_t>(b) * a.k;
-        int32_t* ix = a.indices + static_cast<int64_t>(b) * a.k;
-        if (!gate) {
-            // softmax(top / T) (retrieval.py:146); s_sv[0] is the maximum
-            const float mx = got > 0 ? s_sv[0] / T : 0.f;
-            float den = 0.f;
-            for (int i = l; i < got; i += 32) den += expf(s_sv[i] / T - mx);
-            den = warp_sum(den);
-            for (int i = l; i < got; i += 32) al[i] = expf(s_sv[i] / T - mx) / den;
-        } else {
-            // raw / (sum raw + 1e-8), then / (sum top + 1e-8) (retrieval.py:150-155)
-            float tot = 0.f;
-            for (int i = l; i < got; i += 32) {
-                const float v = gate_raw(s_sv[i], lam, tau, T) / (Z + 1e-8f);
-                s_sv[i] = v;
-                tot += v;
+        float Z = 0.f, M = -INFINITY;
+        if (threadIdx.x == 0) {
+            if (got < a.k) raise_status(a.status, DWA_STATUS_FEW_CANDIDATES);
+            for (int p = 0; p < a.world; ++p) {
+                const float* sm = a.summaries + (static_cast<int64_t>(p) * a.B + b) * W;
+                Z += sm[2 * a.k];
+                M = fmaxf(M, sm[2 * a.k + 1]);
             }
-            tot = warp_sum(tot);
-            for (int i = l; i < got; i += 32) al[i] = s_sv[i] / (tot + 1e-8f);
+            if (a.stats) {
+                float zs = 0.f;
+                for (int p = 0; p < a.world; ++p) {
+                    const float* sm = a.summaries + (static_cast<int64_t>(p) * a.B + b) * W;
+                    if (sm[2 * a.k + 1] != -INFINITY) zs += sm[2 * a.k + 2] * expf(sm[2 * a.k + 1] - M);
+                }
+                a.stats[2 * b] = M;
+                a.stats[2 * b + 1] = zs;
+            }
         }
-        for (int i = l; i < got; i += 32) ix[i] = static_cast<int32_t>(sel_pos[i]);
-        __syncwarp();
-        for (int i = got + l; i < a.k; i += 32) { al[i] = 0.f; ix[i] = got > 0 ? static_cast<int32_t>(sel_pos[0]) : 0; }
+        Z = __shfl_sync(0xffffffffu, Z, 0);
+        write_alphas(got, a.k, gate, lam, tau, T, Z, s_sv, sel_pos, a.alphas + static_cast<int64_t>(b) * a.k,
+                     a.indices + static_cast<int64_t>(b) * a.k);
     }
 }
 
@@ -718,18 +851,24 @@ extern "C" size_t dwa_retrieve_workspace_bytes(const DwaRetrieveDims* dims, int 
     return carve_ret(nullptr, *dims, use_ivf != 0, want_soft_full != 0).bytes;
 }
 
-extern "C" int dwa_retrieve(void* stream, const DwaRetrieveDims* dims, int use_ivf, int is_warmup,
-                            const float* lambda_val, const void* z, const float* W_Q,
-                            const float* aspect_weights, const float* tau, const float* centroids,
-                            const int64_t* list_offsets, const float* pool_keys, float* alphas,
-                            int32_t* indices, float* soft_full, void* workspace,
-                            size_t workspace_bytes) {
+// One retrieval call.  shard == nullptr: the whole pool (dwa_retrieve).
+// Otherwise pool_keys holds the rows [row_lo, row_lo + N) of an n_global-row
+// pool and, instead of alphas / indices, the call writes this rank's summary
+// [B, 2k+3] (see summary_width) and leaves soft_full as raw scores.
+static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaShard* shard, int use_ivf,
+                         int is_warmup, const float* lambda_val, const void* z, const float* W_Q,
+                         const float* aspect_weights, const float* tau, const float* centroids,
+                         const int64_t* list_offsets, const float* pool_keys, float* alphas,
+                         int32_t* indices, float* soft_full, float* summary, void* workspace,
+                         size_t workspace_bytes) {
     int rc = check_ret(dims, use_ivf);
     if (rc) return rc;
     const DwaRetrieveDims& d = *dims;
     const bool ivf = use_ivf != 0, want_sf = soft_full != nullptr;
-    if (!lambda_val || !z || !W_Q || !aspect_weights || !tau || !pool_keys || !alphas || !indices)
+    if (!lambda_val || !z || !W_Q || !aspect_weights || !tau || !pool_keys ||
+        (shard ? !summary : (!alphas || !indices)))
         return fail(DWA_ERR_INVALID_ARG, "a required pointer is NULL");
+    const int64_t row_lo = shard ? shard->row_lo : 0, n_global = shard ? shard->n_global : d.N;
     if (ivf && (!centroids || !list_offsets))
         return fail(DWA_ERR_INVALID_ARG, "IVF needs centroids and list_offsets");
     const RetWorkspace w = carve_ret(workspace, d, ivf, want_sf);
@@ -777,8 +916,9 @@ extern "C" int dwa_retrieve(void* stream, const DwaRetrieveDims* dims, int use_i
         DWA_LAUNCH_CHECK("coarse_kernel");
         const size_t tsh = d.C <= kStageKeys ? static_cast<size_t>(d.C) * 8 : 0;
         DWA_TIMED("topm", st, topm_kernel<<<d.B, 512, tsh, st>>>(w.c_score, d.C, w.m_eff, list_offsets,
-                                                                 d.N, d.max_list, w.topc,
-                                                                 w.probe_lo, w.cand_base, w.status));
+                                                                 n_global, row_lo, row_lo + d.N,
+                                                                 d.max_list, w.topc, w.probe_lo,
+                                                                 w.cand_base, w.status));
         DWA_LAUNCH_CHECK("topm_kernel");
         g_launches_total += 2;
     } else {
@@ -951,6 +1091,8 @@ extern "C" int dwa_retrieve(void* stream, const DwaRetrieveDims* dims, int use_i
     sa.alphas = alphas;
     sa.indices = indices;
     sa.status = w.status;
+    sa.row_lo = row_lo;
+    sa.summary = shard ? summary : nullptr;
     if (w.K_cap <= kSelectStageKeys) {
         const size_t ssh = static_cast<size_t>(w.K_cap) * 8;
         if (ssh > 48 * 1024) {
@@ -970,16 +1112,104 @@ extern "C" int dwa_retrieve(void* stream, const DwaRetrieveDims* dims, int use_i
     }
     DWA_LAUNCH_CHECK("select_kernel");
     ++g_launches_total;
-    // 6. normalise soft_full in place
-    if (want_sf) {
+    // 6. normalise soft_full in place (a rank of a sharded call only writes its
+    //    statistics into the summary; the merge normalises)
+    if (want_sf && shard) {
         DWA_TIMED("softmax_stats", st,
-                  softmax_stats_kernel<<<d.B, 256, 0, st>>>(w.partial, sf_blocks, w.stats));
+                  softmax_stats_kernel<<<d.B, 256, 0, st>>>(w.partial, sf_blocks, summary + 2 * d.k + 1,
+                                                            summary_width(d.k)));
+        DWA_LAUNCH_CHECK("softmax_stats_kernel");
+        ++g_launches_total;
+    } else if (shard) {
+        fill_stats_kernel<<<(d.B + 127) / 128, 128, 0, st>>>(summary + 2 * d.k + 1, d.B, summary_width(d.k));
+        DWA_LAUNCH_CHECK("fill_stats_kernel");
+        ++g_launches_total;
+    } else if (want_sf) {
+        DWA_TIMED("softmax_stats", st,
+                  softmax_stats_kernel<<<d.B, 256, 0, st>>>(w.partial, sf_blocks, w.stats, 2));
         DWA_LAUNCH_CHECK("softmax_stats_kernel");
         dim3 ga(static_cast<unsigned>((d.N + 2047) / 2048), d.B);
         DWA_TIMED("softmax_apply", st,
                   softmax_apply_kernel<<<ga, 256, 0, st>>>(soft_full, d.N, 1.f / d.T, w.stats));
         DWA_LAUNCH_CHECK("softmax_apply_kernel");
         g_launches_total += 2;
+    }
+    return DWA_OK;
+}
+
+extern "C" int dwa_retrieve(void* stream, const DwaRetrieveDims* dims, int use_ivf, int is_warmup,
+                            const float* lambda_val, const void* z, const float* W_Q,
+                            const float* aspect_weights, const float* tau, const float* centroids,
+                            const int64_t* list_offsets, const float* pool_keys, float* alphas,
+                            int32_t* indices, float* soft_full, void* workspace,
+                            size_t workspace_bytes) {
+    return retrieve_impl(stream, dims, nullptr, use_ivf, is_warmup, lambda_val, z, W_Q, aspect_weights,
+                         tau, centroids, list_offsets, pool_keys, alphas, indices, soft_full, nullptr,
+                         workspace, workspace_bytes);
+}
+
+extern "C" int dwa_retrieve_local(void* stream, const DwaRetrieveDims* dims, const DwaShard* shard,
+                                  int use_ivf, int is_warmup, const float* lambda_val, const void* z,
+                                  const float* W_Q, const float* aspect_weights, const float* tau,
+                                  const float* centroids, const int64_t* list_offsets,
+                                  const float* pool_keys, float* summary, float* soft_full,
+                                  void* workspace, size_t workspace_bytes) {
+    if (!shard || !dims) return fail(DWA_ERR_INVALID_ARG, "dims and shard are required");
+    if (dims->N == 0) {
+        // a rank that holds no rows contributes an empty summary
+        if (!summary || dims->B <= 0 || dims->k <= 0 || dims->k > kMaxK)
+            return fail(DWA_ERR_INVALID_ARG, "summary, B and k (<= 256) are required");
+        empty_summary_kernel<<<dims->B, 128, 0, static_cast<cudaStream_t>(stream)>>>(summary, dims->k);
+        DWA_LAUNCH_CHECK("empty_summary_kernel");
+        ++g_launches_total;
+        return DWA_OK;
+    }
+    if (shard->row_lo < 0 || shard->n_global <= 0 || shard->row_lo + dims->N > shard->n_global ||
+        shard->n_global >= (int64_t(1) << 31))
+        return fail(DWA_ERR_INVALID_ARG, "shard rows [row_lo, row_lo + N) must lie in [0, n_global < 2^31)");
+    return retrieve_impl(stream, dims, shard, use_ivf, is_warmup, lambda_val, z, W_Q, aspect_weights, tau,
+                         centroids, list_offsets, pool_keys, nullptr, nullptr, soft_full, summary, workspace,
+                         workspace_bytes);
+}
+
+extern "C" size_t dwa_retrieve_merge_workspace_bytes(const DwaRetrieveDims* dims) {
+    if (!dims || dims->B <= 0) return 0;
+    return 256 + ((static_cast<size_t>(dims->B) * 2 * sizeof(float) + 255) / 256) * 256;
+}
+
+extern "C" int dwa_retrieve_merge(void* stream, const DwaRetrieveDims* dims, int world,
+                                  const float* summaries, int is_warmup, const float* lambda_val,
+                                  const float* tau, float* alphas, int32_t* indices, float* soft_full,
+                                  void* workspace, size_t workspace_bytes) {
+    if (!dims) return fail(DWA_ERR_INVALID_ARG, "dims is NULL");
+    const DwaRetrieveDims& d = *dims;
+    if (world < 1 || d.B <= 0 || d.k <= 0 || d.N < 0) return fail(DWA_ERR_INVALID_ARG, "bad world / B / k / N");
+    if (d.k > kMaxK) return fail(DWA_ERR_UNSUPPORTED, "k > 256");
+    if (static_cast<int64_t>(world) * d.k > 4096) return fail(DWA_ERR_UNSUPPORTED, "world * k > 4096");
+    if (!(d.T > 0.f)) return fail(DWA_ERR_INVALID_ARG, "T must be > 0");
+    if (!summaries || !lambda_val || !tau || !alphas || !indices)
+        return fail(DWA_ERR_INVALID_ARG, "a required pointer is NULL");
+    if (!workspace || reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
+        return fail(DWA_ERR_WORKSPACE, "workspace must be non-NULL and 256-byte aligned");
+    if (workspace_bytes < dwa_retrieve_merge_workspace_bytes(dims))
+        return fail(DWA_ERR_WORKSPACE, "workspace too small");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    MergeArgs ma;
+    ma.summaries = summaries; ma.world = world; ma.B = d.B; ma.k = d.k; ma.T = d.T;
+    ma.is_warmup = is_warmup; ma.lambda_val = lambda_val; ma.tau = tau;
+    ma.alphas = alphas; ma.indices = indices;
+    ma.status = static_cast<uint32_t*>(workspace);
+    float* stats = reinterpret_cast<float*>(static_cast<char*>(workspace) + 256);
+    ma.stats = soft_full ? stats : nullptr;
+    const size_t msh = static_cast<size_t>(world) * d.k * sizeof(uint64_t);
+    DWA_TIMED("merge", st, merge_kernel<<<d.B, 1024, msh, st>>>(ma));
+    DWA_LAUNCH_CHECK("merge_kernel");
+    ++g_launches_total;
+    if (soft_full && d.N > 0) {
+        dim3 ga(static_cast<unsigned>((d.N + 2047) / 2048), d.B);
+        DWA_TIMED("softmax_apply", st, softmax_apply_kernel<<<ga, 256, 0, st>>>(soft_full, d.N, 1.f / d.T, stats));
+        DWA_LAUNCH_CHECK("softmax_apply_kernel");
+        ++g_launches_total;
     }
     return DWA_OK;
 }

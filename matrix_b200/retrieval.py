@@ -110,10 +110,21 @@ class MultiAspectRetrieval:
 
     def __call__(self, z, pool_keys, lambda_val, is_warmup: bool, mesh=None, *,
                  want_soft_full: bool = True):
-        if mesh is not None:
-            raise NotImplementedError(
-                "model-sharded retrieval uses matrix_b200.sharded.sharded_retrieve")
+        """``mesh``: ``None`` (one device) or a ``matrix_b200.sharded.RowShard``,
+        in which case ``pool_keys`` holds this rank's rows and soft_full is its
+        slice (the reference's ``mesh`` branch, retrieval.py:74-79)."""
         cfg = self.cfg
+        if mesh is not None:
+            from .sharded import RowShard, sharded_retrieve
+            if not isinstance(mesh, RowShard):
+                raise TypeError("mesh must be a matrix_b200.sharded.RowShard")
+            offs = self.list_offsets
+            if cfg.use_ivf and offs is None:
+                offs = equal_list_offsets(mesh.n_global, cfg.C, z.device)
+            return sharded_retrieve(z, self.W_Q, self.aspect_weights, self.tau, self.centroids,
+                                    pool_keys, offs, lambda_val, is_warmup, mesh, k=cfg.k_max,
+                                    m=cfg.m, T=cfg.T, max_list=self.max_list, use_ivf=cfg.use_ivf,
+                                    want_soft_full=want_soft_full)
         return retrieve(z, self.W_Q, self.aspect_weights, self.tau, self.centroids, pool_keys,
                         lambda_val, is_warmup, k=cfg.k_max, m=cfg.m, T=cfg.T, use_ivf=cfg.use_ivf,
                         list_offsets=self.list_offsets, max_list=self.max_list,

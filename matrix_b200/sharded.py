@@ -1,0 +1,186 @@
+"""Row-sharded IVF retrieval over P ranks (one process per GPU).
+
+Replaces the reference's model-sharded retrieval, which turns IVF off and
+all-gathers every rank's full-pool scores (src/dwa/retrieval.py:74-79, 121-138)
+and then fetches the winners with a masked psum (src/dwa/model.py:16-47).  Here
+IVF stays on and only k candidates per query cross the interconnect:
+
+1. ``retrieve_local`` on every rank (``dwa_retrieve_local``): rank p holds the
+   keys of pool rows ``[row_lo, row_hi)``; centroids, ``W_Q``, aspect weights,
+   ``tau`` and the global CSR ``list_offsets`` are replicated, so every rank
+   picks the same top-m lists and scores the part of them it holds.  Output:
+   a summary ``[B, 2k+3]`` per rank (see ``summary_width``) and, with
+   soft_full, the raw scores of the rank's rows.
+2. ``gather_summaries``: one all-gather of ``B*(2k+3)*4`` bytes per rank.
+3. ``retrieve_merge`` on every rank (``dwa_retrieve_merge``): the global top-k
+   (ties to the lower pool row), alphas as the single-device call defines
+   them, and the rank's soft_full slice normalised with the merged softmax
+   statistics.
+
+The result equals ``retrieve`` on the whole pool: indices bit-exact, alphas
+and soft_full up to the order in which partial sums are added.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from .runtime import dtype_code, ptr, require_cuda, stream_of, workspace
+
+
+def summary_width(k: int) -> int:
+    """Floats per query in a rank's summary: k scores, k global rows (int32
+    bits), the partial gate sum, the soft_full max and sum of exp."""
+    return 2 * k + 3
+
+
+@dataclass(frozen=True)
+class RowShard:
+    """This rank's rows ``[row_lo, row_hi)`` of an ``n_global``-row pool and the
+    process group of the ranks that hold the other rows (``None``: one rank)."""
+
+    row_lo: int
+    row_hi: int
+    n_global: int
+    group: object = None
+
+
+def shard_rows(list_offsets, world: int) -> list[tuple[int, int]]:
+    """Contiguous row ranges ``[(row_lo, row_hi)] * world`` made of whole lists,
+    balanced by rows: rank p's range ends at the list boundary nearest to
+    ``(p+1) * N / world``.  ``list_offsets`` is the CSR ``[C+1]`` (any array
+    type).  A rank may get no rows when there are fewer lists than ranks."""
+    off = np.asarray(list_offsets.cpu() if isinstance(list_offsets, torch.Tensor) else list_offsets,
+                     dtype=np.int64)
+    if off.ndim != 1 or off.size < 2 or off[0] != 0 or np.any(np.diff(off) < 0):
+        raise ValueError("list_offsets must be a non-decreasing CSR array starting at 0")
+    if world < 1:
+        raise ValueError("world must be >= 1")
+    n = int(off[-1])
+    bounds = [0]
+    for p in range(1, world):
+        target = p * n / world
+        j = int(np.argmin(np.abs(off - target)))
+        bounds.append(max(bounds[-1], int(off[j])))
+    bounds.append(n)
+    return [(bounds[p], bounds[p + 1]) for p in range(world)]
+
+
+def gather_summaries(summary: torch.Tensor, group=None) -> torch.Tensor:
+    """All-gather every rank's ``[B, 2k+3]`` summary into ``[P, B, 2k+3]`` (rank
+    order).  One collective; with no process group, the summary alone."""
+    import torch.distributed as dist
+    if group is None and not (dist.is_available() and dist.is_initialized()):
+        return summary.unsqueeze(0)
+    world = dist.get_world_size(group)
+    if world == 1:
+        return summary.unsqueeze(0)
+    out = torch.empty((world,) + tuple(summary.shape), dtype=summary.dtype, device=summary.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, summary.contiguous(), group=group)
+    else:
+        dist.all_gather(list(out.unbind(0)), summary.contiguous(), group=group)
+    return out
+
+
+def _dims(B, S, d_k, d_A, C, m, k, max_list, N, T, zdt):
+    return _lib.RetrieveDims(B, S, d_k, d_A, C, m, k, int(max_list), int(N), float(T), zdt)
+
+
+def retrieve_local(z, W_Q, aspect_weights, tau, centroids, local_keys, list_offsets, lambda_val,
+                   is_warmup, *, k, m, T, row_lo, n_global, max_list, use_ivf=True,
+                   want_soft_full=True):
+    """``dwa_retrieve_local``: this rank's summary ``[B, 2k+3]`` and, with
+    ``want_soft_full``, the raw scores ``[B, N_local]`` of its rows."""
+    require_cuda("z", z)
+    dev = z.device
+    require_cuda("local_keys", local_keys, dev)
+    if local_keys.dtype != torch.float32 or local_keys.dim() != 3:
+        raise ValueError("local_keys must be float32 [S, N_local, d_k]")
+    S, n_loc, d_k = local_keys.shape
+    B, d_A = z.shape
+    C = centroids.shape[1] if use_ivf else 1
+    if use_ivf:
+        require_cuda("centroids", centroids, dev)
+        require_cuda("list_offsets", list_offsets, dev)
+        if list_offsets.dtype != torch.int64 or list_offsets.numel() != C + 1:
+            raise ValueError("list_offsets must be int64 [C+1] (global rows)")
+    lam = lambda_val if isinstance(lambda_val, torch.Tensor) else torch.tensor(
+        [float(lambda_val)], dtype=torch.float32, device=dev)
+    lam = lam.reshape(1).float().contiguous()
+    tau_t = tau.reshape(1).float().contiguous()
+    W_Q = W_Q.float().contiguous()
+    aw = aspect_weights.float().contiguous()
+    dims = _dims(B, S, d_k, d_A, C, m, k, max_list or 0, n_loc, T, dtype_code(z.dtype, "z"))
+    shard = _lib.Shard(int(row_lo), int(n_global))
+    summary = torch.empty((B, summary_width(k)), dtype=torch.float32, device=dev)
+    soft = torch.empty((B, n_loc), dtype=torch.float32, device=dev) if want_soft_full else None
+    lib = _lib.load()
+    ws, ws_bytes = None, 0
+    if n_loc > 0:          # a rank without rows only writes an empty summary
+        ws_bytes = lib.dwa_retrieve_workspace_bytes(dims, int(use_ivf), int(want_soft_full))
+        if ws_bytes == 0:
+            raise _lib.DwaError(f"dwa_retrieve_workspace_bytes: {_lib.last_error()}")
+        ws = workspace(dev, "retrieve_local", ws_bytes)
+    with torch.cuda.device(dev):
+        rc = lib.dwa_retrieve_local(stream_of(dev), dims, shard, int(use_ivf), int(bool(is_warmup)),
+                                    ptr(lam), ptr(z), ptr(W_Q), ptr(aw), ptr(tau_t),
+                                    ptr(centroids) if use_ivf else None,
+                                    ptr(list_offsets) if use_ivf else None, ptr(local_keys),
+                                    ptr(summary), ptr(soft), ptr(ws), ws_bytes)
+    _lib.check(rc, "dwa_retrieve_local")
+    return summary, soft
+
+
+def retrieve_merge(summaries, lambda_val, tau, is_warmup, *, k, T, soft_full=None):
+    """``dwa_retrieve_merge``: ``(alphas [B,k], indices [B,k] int32)`` from the
+    gathered ``[P, B, 2k+3]`` summaries; ``soft_full`` (this rank's raw slice,
+    if given) is normalised in place."""
+    require_cuda("summaries", summaries)
+    dev = summaries.device
+    P, B, W = summaries.shape
+    if W != summary_width(k):
+        raise ValueError(f"summaries must be [P, B, {summary_width(k)}]")
+    lam = lambda_val if isinstance(lambda_val, torch.Tensor) else torch.tensor(
+        [float(lambda_val)], dtype=torch.float32, device=dev)
+    lam = lam.reshape(1).float().contiguous()
+    tau_t = tau.reshape(1).float().contiguous()
+    n_soft = 0 if soft_full is None else soft_full.shape[1]
+    if soft_full is not None:
+        require_cuda("soft_full", soft_full, dev)
+        if soft_full.dtype != torch.float32 or soft_full.shape[0] != B or not soft_full.is_contiguous():
+            raise ValueError("soft_full must be contiguous float32 [B, N_local]")
+    dims = _dims(B, 1, 1, 1, 1, 1, k, 0, n_soft, T, _lib.DWA_F32)
+    alphas = torch.empty((B, k), dtype=torch.float32, device=dev)
+    indices = torch.empty((B, k), dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    ws = workspace(dev, "retrieve_merge", lib.dwa_retrieve_merge_workspace_bytes(dims))
+    with torch.cuda.device(dev):
+        rc = lib.dwa_retrieve_merge(stream_of(dev), dims, P, ptr(summaries.contiguous()),
+                                    int(bool(is_warmup)), ptr(lam), ptr(tau_t), ptr(alphas),
+                                    ptr(indices), ptr(soft_full), ptr(ws), ws.numel())
+    _lib.check(rc, "dwa_retrieve_merge")
+    return alphas, indices
+
+
+def sharded_retrieve(z, W_Q, aspect_weights, tau, centroids, local_keys, list_offsets, lambda_val,
+                     is_warmup, shard: RowShard, *, k, m, T, max_list=None, use_ivf=True,
+                     want_soft_full=True):
+    """The three steps on this rank: ``(alphas [B,k], indices [B,k] int32,
+    soft_full [B, N_local] or None)``; every rank gets the same alphas and
+    indices and its own normalised slice of soft_full."""
+    if local_keys.shape[1] != shard.row_hi - shard.row_lo:
+        raise ValueError("local_keys must hold exactly the rows [row_lo, row_hi)")
+    if use_ivf and max_list is None:
+        max_list = int((list_offsets[1:] - list_offsets[:-1]).max().item())
+    summary, soft = retrieve_local(z, W_Q, aspect_weights, tau, centroids, local_keys, list_offsets,
+                                   lambda_val, is_warmup, k=k, m=m, T=T, row_lo=shard.row_lo,
+                                   n_global=shard.n_global, max_list=max_list or 0, use_ivf=use_ivf,
+                                   want_soft_full=want_soft_full)
+    gathered = gather_summaries(summary, shard.group)
+    alphas, indices = retrieve_merge(gathered, lambda_val, tau, is_warmup, k=k, T=T, soft_full=soft)
+    return alphas, indices, soft

@@ -198,6 +198,98 @@ def retrieve(z, W_Q, aspect_weights, tau, centroids, pool_keys, *, k, m, T,
 
 
 # ---------------------------------------------------------------------------
+# Row-sharded retrieval: one rank's summary and the merge (extension; with one
+# rank it reduces to ``retrieve`` with tie_break="index")
+# ---------------------------------------------------------------------------
+
+def summary_width(k: int) -> int:
+    return 2 * k + 3
+
+
+def retrieve_local(z, W_Q, aspect_weights, tau, centroids, local_keys, *, row_lo, k, m, T,
+                   lambda_val, is_warmup, use_ivf=True, list_offsets=None, n_global=None,
+                   want_soft_full=True):
+    """One rank's part of a row-sharded call: the rank holds the keys of pool rows
+    ``[row_lo, row_lo + N_local)``; the top-m lists are chosen exactly as in
+    ``retrieve`` (retrieval.py:85-98) and only their rows held here are scored
+    (:100-106).  Returns ``(summary [B, 2k+3], s_full_local [B, N_local] or None)``:
+    the rank's top-k (scores best first, global rows as floats), the partial sum of
+    the unnormalised gate ``raw`` (:150-151), and the max / sum of exp of s/T over
+    its rows (:114-119)."""
+    B = z.shape[0]
+    S, n_loc, _ = local_keys.shape
+    f = local_keys.dtype.type
+    q_norm = aspect_queries(W_Q, z)
+    w = softmax(aspect_weights, axis=0)
+    row_hi = row_lo + n_loc
+    if use_ivf:
+        C = centroids.shape[1]
+        if list_offsets is None:
+            list_offsets = equal_list_offsets(n_global, C)
+        _, top_clusters = top_k(coarse_scores(q_norm, w, centroids), min(m, C))
+        cands = [c[(c >= row_lo) & (c < row_hi)] for c in candidate_lists(top_clusters, list_offsets)]
+    else:
+        cands = [np.arange(row_lo, row_hi, dtype=np.int64) for _ in range(B)]
+    W = summary_width(k)
+    summary = np.zeros((B, W), dtype=np.float64)
+    for b in range(B):
+        c = cands[b]
+        s = fine_scores(q_norm[b], w, local_keys, c - row_lo) if c.size else np.zeros(0, f)
+        if is_warmup:
+            rank, zpart = s, 0.0
+        else:
+            raw = sigmoid(f(lambda_val) * (s - f(tau))) * np.exp(s / f(T))
+            rank, zpart = raw, float(raw.sum())
+        _, pos = top_k(rank, min(k, c.size), c)
+        got = pos.size
+        summary[b, :k] = -np.inf
+        summary[b, k:2 * k] = -1
+        summary[b, :got] = s[pos]
+        summary[b, k:k + got] = c[pos]
+        summary[b, 2 * k] = zpart
+    s_loc = None
+    if want_soft_full:
+        s_loc = full_scores(q_norm, w, local_keys)
+        x = s_loc / f(T)
+        mx = x.max(axis=1) if n_loc else np.full(B, -np.inf)
+        summary[:, 2 * k + 1] = mx
+        summary[:, 2 * k + 2] = np.exp(x - mx[:, None]).sum(axis=1) if n_loc else 0.0
+    else:
+        summary[:, 2 * k + 1] = -np.inf
+        summary[:, 2 * k + 2] = 0.0
+    return summary, s_loc
+
+
+def merge_summaries(summaries, *, k, T, lambda_val, tau, is_warmup):
+    """Merge of the ranks' summaries ``[P, B, 2k+3]``: the global top-k (ties to the
+    lower pool row), alphas by retrieval.py:146 (warmup) or :152-155 (gate, with
+    the gate sum added over ranks), and the combined soft_full statistics.
+    Returns ``(alphas [B,k], indices [B,k], stats [B,2] = (max, sum exp))``."""
+    P, B, _ = summaries.shape
+    alphas = np.zeros((B, k))
+    indices = np.zeros((B, k), dtype=np.int64)
+    stats = np.zeros((B, 2))
+    for b in range(B):
+        s = summaries[:, b, :k].reshape(-1)
+        rows = summaries[:, b, k:2 * k].reshape(-1).astype(np.int64)
+        ok = rows >= 0
+        s, rows = s[ok], rows[ok]
+        Z = summaries[:, b, 2 * k].sum()
+        if is_warmup:
+            top, pos = top_k(s, k, rows)
+            alphas[b] = softmax(top / T)
+        else:
+            raw = sigmoid(lambda_val * (s - tau)) * np.exp(s / T) / (Z + EPS)
+            top_raw, pos = top_k(raw, k, rows)
+            alphas[b] = top_raw / (top_raw.sum() + EPS)
+        indices[b] = rows[pos]
+        mx = summaries[:, b, 2 * k + 1]
+        M = mx.max()
+        stats[b] = M, (summaries[:, b, 2 * k + 2] * np.exp(np.where(np.isfinite(mx), mx - M, -np.inf))).sum()
+    return alphas, indices, stats
+
+
+# ---------------------------------------------------------------------------
 # Gather (model.py:184-195) and key cache (assembly_pallas.py:392-400)
 # ---------------------------------------------------------------------------
 

@@ -1,0 +1,180 @@
+"""Row-sharded retrieval on the GPU through the C ABI.
+
+Ranks are emulated on one GPU: each rank's ``dwa_retrieve_local`` runs on its
+own slice of the key cache, the summaries are stacked as an all-gather would
+stack them, and every rank's ``dwa_retrieve_merge`` must give the indices of
+``dwa_retrieve`` on the whole pool bit-exactly (and the oracle's), alphas and
+the concatenated soft_full slices within rtol 1e-5.  Cases: 2 and 3 ranks,
+warmup and both gate signs, Zipf lists, an empty rank, a split through the
+middle of a list, full search (IVF off).  With two or more GPUs visible, two
+NCCL ranks also run ``sharded_retrieve`` for real.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from conftest import assert_close
+from matrix_b200.config import DWAConfig
+from matrix_b200.synthetic import make_inputs
+from oracle import dwa_oracle as O
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-5
+MODES = [(True, 1.0), (False, 5.0), (False, -2.0)]
+
+
+def _case(B=6, seed=31):
+    cfg = DWAConfig(D=17 * 64, N=41 * 487, use_ivf=True, C=41, m=5, d_A=64, d_B=64, r=8, k_max=24,
+                    S=4, d_k=64, T=1.0, gamma_init=0.1, bf16_pool=False)
+    return cfg, make_inputs(cfg, B, 8, seed, variant="rich", zipf=1.1)
+
+
+def _dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _emulated(cfg, x, shards, is_warmup, lam, use_ivf=True, want_sf=True):
+    from matrix_b200.sharded import retrieve_local, retrieve_merge
+    z, W_Q, aw = _dev(x.z), _dev(x.W_Q), _dev(x.aspect_weights)
+    tau, cents, off = torch.tensor(x.tau).cuda(), _dev(x.centroids), _dev(x.list_offsets)
+    keys = _dev(x.keys)
+    max_list = int(np.diff(x.list_offsets).max())
+    sums, softs = [], []
+    for lo, hi in shards:
+        local = keys[:, lo:hi].contiguous()
+        sm, sf = retrieve_local(z, W_Q, aw, tau, cents, local, off, lam, is_warmup, k=cfg.k_max,
+                                m=cfg.m, T=cfg.T, row_lo=lo, n_global=cfg.N, max_list=max_list,
+                                use_ivf=use_ivf, want_soft_full=want_sf)
+        sums.append(sm)
+        softs.append(sf)
+    gathered = torch.stack(sums)
+    outs = []
+    for p in range(len(shards)):
+        a, i = retrieve_merge(gathered, lam, tau, is_warmup, k=cfg.k_max, T=cfg.T, soft_full=softs[p])
+        outs.append((a, i))
+    torch.cuda.synchronize()
+    sf = torch.cat(softs, dim=1).cpu().numpy() if want_sf else None
+    return [(a.cpu().numpy(), i.cpu().numpy()) for a, i in outs], sf
+
+
+def _single(cfg, x, is_warmup, lam, use_ivf=True, want_sf=True):
+    from matrix_b200.retrieval import retrieve
+    a, i, sf = retrieve(_dev(x.z), _dev(x.W_Q), _dev(x.aspect_weights), torch.tensor(x.tau).cuda(),
+                        _dev(x.centroids), _dev(x.keys), lam, is_warmup, k=cfg.k_max, m=cfg.m, T=cfg.T,
+                        use_ivf=use_ivf, list_offsets=_dev(x.list_offsets),
+                        max_list=int(np.diff(x.list_offsets).max()), want_soft_full=want_sf)
+    torch.cuda.synchronize()
+    return a.cpu().numpy(), i.cpu().numpy(), None if sf is None else sf.cpu().numpy()
+
+
+def _check(cfg, x, shards, is_warmup, lam, use_ivf=True, want_sf=True):
+    from matrix_b200.runtime import raise_on_device_status
+    outs, sf = _emulated(cfg, x, shards, is_warmup, lam, use_ivf, want_sf)
+    ra, ri, rsf = _single(cfg, x, is_warmup, lam, use_ivf, want_sf)
+    f = np.float64
+    oa, oi, _ = O.retrieve(x.z.astype(f), x.W_Q.astype(f), x.aspect_weights.astype(f), f(x.tau),
+                           x.centroids.astype(f), x.keys.astype(f), k=cfg.k_max, m=cfg.m, T=cfg.T,
+                           lambda_val=lam, is_warmup=is_warmup, use_ivf=use_ivf,
+                           list_offsets=x.list_offsets, tie_break="index", want_soft_full=False)
+    tag = f"shards={shards} warmup={is_warmup} lam={lam} ivf={use_ivf}"
+    for p, (a, i) in enumerate(outs):
+        np.testing.assert_array_equal(i, ri, err_msg=f"rank {p} vs single call, {tag}")
+        assert_close(a, ra, TOL, name=f"alphas rank {p} {tag}")
+        if is_warmup or lam >= 0:
+            np.testing.assert_array_equal(i, oi, err_msg=f"rank {p} vs oracle, {tag}")
+            assert_close(a, oa, TOL, name=f"alphas rank {p} vs oracle {tag}")
+    if want_sf:
+        assert_close(sf, rsf, TOL, name=f"soft_full {tag}")
+    raise_on_device_status()
+
+
+@pytest.mark.parametrize("is_warmup,lam", MODES)
+@pytest.mark.parametrize("world", [2, 3])
+def test_emulated_ranks_equal_single_call(world, is_warmup, lam):
+    from matrix_b200.sharded import shard_rows
+    cfg, x = _case()
+    _check(cfg, x, shard_rows(x.list_offsets, world), is_warmup, lam)
+
+
+@pytest.mark.parametrize("is_warmup,lam", MODES)
+def test_empty_rank_and_split_list(is_warmup, lam):
+    cfg, x = _case()
+    off = x.list_offsets
+    mid = int((off[10] + off[11]) // 2)
+    _check(cfg, x, [(0, 0), (0, mid), (mid, int(off[-1]))], is_warmup, lam)
+
+
+def test_without_soft_full_and_full_search():
+    from matrix_b200.sharded import shard_rows
+    cfg, x = _case()
+    shards = shard_rows(x.list_offsets, 2)
+    _check(cfg, x, shards, False, 5.0, want_sf=False)
+    _check(cfg, x, shards, True, 1.0, use_ivf=False)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _nccl_rank(rank, world, port, out_dir):
+    import torch.distributed as dist
+    from datetime import timedelta
+    from matrix_b200.sharded import RowShard, shard_rows, sharded_retrieve
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        cfg, x = _case()
+        lo, hi = shard_rows(x.list_offsets, world)[rank]
+
+        def d(a):
+            return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+        res = {}
+        for is_warmup, lam in MODES:
+            a, i, sf = sharded_retrieve(d(x.z), d(x.W_Q), d(x.aspect_weights), torch.tensor(x.tau).to(dev),
+                                        d(x.centroids), d(x.keys[:, lo:hi]), d(x.list_offsets), lam,
+                                        is_warmup, RowShard(lo, hi, cfg.N, None), k=cfg.k_max, m=cfg.m,
+                                        T=cfg.T)
+            torch.cuda.synchronize(dev)
+            res[f"a_{is_warmup}_{lam}"] = a.cpu().numpy()
+            res[f"i_{is_warmup}_{lam}"] = i.cpu().numpy()
+            res[f"sf_{is_warmup}_{lam}"] = sf.cpu().numpy()
+        np.savez(os.path.join(out_dir, f"rank{rank}.npz"), **res)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_two_nccl_ranks(tmp_path):
+    import torch.multiprocessing as mp
+    from matrix_b200.sharded import shard_rows
+    world = 2
+    mp.start_processes(_nccl_rank, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    cfg, x = _case()
+    shards = shard_rows(x.list_offsets, world)
+    for is_warmup, lam in MODES:
+        ra, ri, rsf = _single(cfg, x, is_warmup, lam)
+        sfs = []
+        for rank in range(world):
+            got = np.load(tmp_path / f"rank{rank}.npz")
+            np.testing.assert_array_equal(got[f"i_{is_warmup}_{lam}"], ri)
+            assert_close(got[f"a_{is_warmup}_{lam}"], ra, TOL, name="alphas")
+            sfs.append(got[f"sf_{is_warmup}_{lam}"])
+        assert_close(np.concatenate(sfs, axis=1), rsf, TOL, name="soft_full")
+        assert sum(hi - lo for lo, hi in shards) == cfg.N
