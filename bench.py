@@ -53,6 +53,8 @@ def parse_args():
                     help="CPU seconds for the cpu_baseline sample (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-key-cache", action="store_true",
+                    help="skip timing compute_key_cache (once per window, not part of the step)")
     return ap.parse_args()
 
 
@@ -78,15 +80,12 @@ def build_device_workload(w, device, seed):
     for i in range(0, N, step):
         pool[i:i + step].normal_(0.0, d ** -0.5, generator=g)
     key_proj = (torch.randn((S, D, dk), generator=g, device=device) * D ** -0.5).to(bf)
-    kp = key_proj.permute(1, 0, 2).reshape(D, S * dk)
-    keys = torch.empty((S, N, dk), dtype=torch.float32, device=device)
-    for i in range(0, N, step):
-        blk = (pool[i:i + step] @ kp).float().reshape(-1, S, dk)   # key cache (outside the step)
-        keys[:, i:i + blk.shape[0]] = blk.permute(1, 0, 2)
+    from matrix_b200.assembly import compute_key_cache
+    keys = compute_key_cache(pool, key_proj)        # once per window in training (outside the step)
     off = torch.arange(C + 1, dtype=torch.int64, device=device) * (N // C)
     rows = off[:-1] + torch.randint(0, N // C, (C,), generator=g, device=device)
     t = dict(
-        pool=pool, keys=keys, list_offsets=off, centroids=keys[:, rows, :].contiguous(),
+        pool=pool, key_proj=key_proj, keys=keys, list_offsets=off, centroids=keys[:, rows, :].contiguous(),
         W_Q=torch.randn((S, dk, d), generator=g, device=device) * d ** -0.5,
         aspect_weights=torch.zeros(S, device=device), tau=torch.zeros(1, device=device),
         W_base=torch.randn((d, d), generator=g, device=device) * 0.01,
@@ -230,6 +229,44 @@ def profile_kernels(step, flush, n=5):
                 acc[k].append(ms)
     del g
     return {k: float(np.mean(v)) for k, v in acc.items() if v and np.mean(v) > 1e-4}
+
+
+def time_key_cache(t, flush, peaks, reps=3):
+    """``compute_key_cache`` on the workload's pool (once per training window,
+    not part of the step), timed with CUDA events after a flush, against its
+    HBM and bf16 rooflines; cuBLAS's bf16 GEMM of the same product
+    (``pool @ key_proj`` into ``[N, S*d_k]``, no re-layout) as a library reference."""
+    import torch
+    from matrix_b200.assembly import compute_key_cache
+    pool, kp = t["pool"], t["key_proj"]
+    N, D = pool.shape
+    S, _, dk = kp.shape
+    kp2 = kp.permute(1, 0, 2).reshape(D, S * dk).contiguous()
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize()
+        ms = []
+        for _ in range(reps):
+            flush()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            ms.append(a.elapsed_time(b))
+        return float(min(ms))
+
+    ours = timed(lambda: compute_key_cache(pool, kp))
+    lib = timed(lambda: torch.matmul(pool, kp2))
+    flops = 2.0 * N * D * S * dk
+    hbm = float(N * D * 2 + S * N * dk * 4 + S * D * dk * 2)
+    t_hbm = hbm / (float(peaks["hbm_gbs"]) * 1e9) * 1e3
+    t_tc = flops / (float(peaks["bf16_tflops"]) * 1e12) * 1e3
+    return {"ms": ours, "tflops": flops / (ours * 1e-3) / 1e12, "hbm_gbs": hbm / (ours * 1e-3) / 1e9,
+            "roofline_ms": max(t_hbm, t_tc), "frac": max(t_hbm, t_tc) / ours,
+            "bound": "hbm" if t_hbm >= t_tc else "tensor", "algorithmic_bytes": hbm, "flops": flops,
+            "cublas_gemm_ms": lib, "shape": f"pool [{N}, {D}] bf16 x key_proj [{S}, {D}, {dk}] bf16"}
 
 
 def C_ptr(event):
@@ -552,6 +589,8 @@ def main():
             "value_per_gpu": value / world, "roofline": roof,
             "kernels_ms": breakdown, "gpu_launches": int(launches_per_step * args.steps),
             "clocks": clocks, "e2e": e2e}
+    if world == 1 and not args.no_key_cache:
+        line["key_cache"] = time_key_cache(t, flush, peaks)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_baseline(w, t, args.cpu_budget_s)
         line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}

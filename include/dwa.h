@@ -22,6 +22,11 @@
  *                      src/dwa/model.py:184-195            pool gather (row_index form)
  *   dwa_assemble_bwd   src/dwa/assembly_pallas.py:246-329  _pallas_assemble_bwd
  *   dwa_retrieve       src/dwa/retrieval.py:48-159         MultiAspectRetrieval.__call__
+ *   dwa_retrieve_local src/dwa/retrieval.py:74-79, 121-138 model-sharded retrieval
+ *   dwa_retrieve_merge src/dwa/model.py:16-47              _distributed_gather of the winners
+ *   dwa_key_cache      src/dwa/assembly_pallas.py:392-400  compute_key_cache
+ *                      src/dwa/pool.py:37-44               VectorPool.compute_keys
+ *   dwa_centroid_ema   train.py:318-328                    centroid EMA of the IVF lists
  */
 #ifndef DWA_H_
 #define DWA_H_
@@ -102,7 +107,8 @@ DWA_API void dwa_launch_counters(uint64_t* total, uint64_t* tensor_core_gemms, u
  * cudaEvent_t passed as void*).  Names: "query", "coarse", "topm", "fine",
  * "full_scores", "select", "softmax_stats", "softmax_apply", "prep_factors",
  * "prep_bias", "gemm_W", "gemm_apply", "gemm_G", "gemm_gh", "gemm_P",
- * "gemm_Q", "colsum", "finalize", "bias_grad", "seq_mean".  Passing NULL
+ * "gemm_Q", "colsum", "finalize", "bias_grad", "seq_mean", "merge",
+ * "key_cache", "centroid_ema".  Passing NULL
  * events removes the entry; dwa_profile_clear() removes all. */
 DWA_API int  dwa_profile_kernel(const char* kernel, void* start_event, void* stop_event);
 DWA_API void dwa_profile_clear(void);
@@ -222,6 +228,37 @@ DWA_API int dwa_retrieve_merge(void* stream, const DwaRetrieveDims* dims, int wo
                                const float* summaries, int is_warmup, const float* lambda_val,
                                const float* tau, float* alphas, int32_t* indices, float* soft_full,
                                void* workspace, size_t workspace_bytes);
+
+/* ---------------------------------------------------------------------------
+ * Key cache.  Replaces compute_key_cache (src/dwa/assembly_pallas.py:392-400) and
+ * VectorPool.compute_keys (src/dwa/pool.py:37-44): keys [S,N,d_k] f32 =
+ * einsum("nd,sda->sna", pool_vectors [N,D], key_proj [S,D,d_k]) in fp32, both
+ * inputs of `dtype` (DWA_BF16: tcgen05 GEMM, DWA_F32: CUDA-core GEMM).  Called
+ * once per training window (train.py:253-256).
+ * ------------------------------------------------------------------------- */
+typedef struct DwaKeyCacheDims {
+    int64_t N;       /* pool rows */
+    int32_t D;       /* pool row width */
+    int32_t S;       /* aspects */
+    int32_t d_k;     /* key dim per aspect */
+    int32_t dtype;   /* DWA_F32 or DWA_BF16: pool_vectors and key_proj */
+} DwaKeyCacheDims;
+
+DWA_API size_t dwa_key_cache_workspace_bytes(const DwaKeyCacheDims* dims);
+
+DWA_API int dwa_key_cache(void* stream, const DwaKeyCacheDims* dims, const void* pool_vectors,
+                          const void* key_proj, float* keys, void* workspace, size_t workspace_bytes);
+
+/* ---------------------------------------------------------------------------
+ * Centroid EMA.  Replaces train.py:318-328: centroids [S,C,d_k] f32 (in place)
+ * = decay * centroids + (1 - decay) * mean of the keys of each list (CSR
+ * list_offsets [C+1] into keys [S,N,d_k]); the reference uses decay 0.9 with
+ * equal lists.  Empty lists keep their centroid.  workspace: >= 256 bytes,
+ * 256-byte aligned, its first word the device status.
+ * ------------------------------------------------------------------------- */
+DWA_API int dwa_centroid_ema(void* stream, int S, int C, int d_k, int64_t N, const float* keys,
+                             const int64_t* list_offsets, float decay, float* centroids,
+                             void* workspace, size_t workspace_bytes);
 
 /* ---------------------------------------------------------------------------
  * Retrieval without a workspace.  No counterpart in the reference: it exists for

@@ -43,6 +43,11 @@ class RetrieveDims(C.Structure):
                 ("N", C.c_int64), ("T", C.c_float), ("z_dtype", C.c_int32)]
 
 
+class KeyCacheDims(C.Structure):
+    _fields_ = [("N", C.c_int64), ("D", C.c_int32), ("S", C.c_int32), ("d_k", C.c_int32),
+                ("dtype", C.c_int32)]
+
+
 class Shard(C.Structure):
     _fields_ = [("row_lo", C.c_int64), ("n_global", C.c_int64)]
 
@@ -71,6 +76,10 @@ _SIGNATURES = {
     "dwa_retrieve_local": (C.c_int, [_P, C.POINTER(RetrieveDims), C.POINTER(Shard), C.c_int, C.c_int,
                                      _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t]),
     "dwa_retrieve_merge_workspace_bytes": (C.c_size_t, [C.POINTER(RetrieveDims)]),
+    "dwa_key_cache_workspace_bytes": (C.c_size_t, [C.POINTER(KeyCacheDims)]),
+    "dwa_key_cache": (C.c_int, [_P, C.POINTER(KeyCacheDims), _P, _P, _P, _P, C.c_size_t]),
+    "dwa_centroid_ema": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int64, _P, _P, C.c_float, _P, _P,
+                                   C.c_size_t]),
     "dwa_retrieve_merge": (C.c_int, [_P, C.POINTER(RetrieveDims), C.c_int, _P, C.c_int, _P, _P, _P,
                                      _P, _P, _P, C.c_size_t]),
 }

@@ -186,3 +186,60 @@ def shard_pallas_assemble(gathered, alphas, h_A, W_base, b_base, gamma, d_B: int
     of the replicated parameters, as ``shard_map``'s transpose does.
     """
     return _Assemble.apply(gathered, alphas, h_A, W_base, b_base, gamma, d_B, r, d_A, mesh)
+
+
+def compute_key_cache(pool_vectors: torch.Tensor, key_proj: torch.Tensor) -> torch.Tensor:
+    """``compute_key_cache`` (src/dwa/assembly_pallas.py:392-400, pool.py:37-44):
+    keys ``[S, N, d_k]`` f32 = einsum("nd,sda->sna") of the pool ``[N, D]`` and the
+    key projections ``[S, D, d_k]`` (both bf16 or both f32), one ``dwa_key_cache``
+    GEMM (tcgen05 for bf16)."""
+    require_cuda("pool_vectors", pool_vectors)
+    dev = pool_vectors.device
+    require_cuda("key_proj", key_proj, dev)
+    if pool_vectors.dim() != 2 or key_proj.dim() != 3 or key_proj.shape[1] != pool_vectors.shape[1]:
+        raise ValueError("pool_vectors must be [N, D] and key_proj [S, D, d_k]")
+    if pool_vectors.dtype != key_proj.dtype:
+        raise ValueError("pool_vectors and key_proj must have the same dtype")
+    N, D = pool_vectors.shape
+    S, _, d_k = key_proj.shape
+    dims = _lib.KeyCacheDims(N, D, S, d_k, dtype_code(pool_vectors.dtype, "pool_vectors"))
+    pool_vectors = pool_vectors.contiguous()
+    key_proj = key_proj.contiguous()
+    keys = torch.empty((S, N, d_k), dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    nbytes = lib.dwa_key_cache_workspace_bytes(dims)
+    if nbytes == 0:
+        raise _lib.DwaError(f"dwa_key_cache_workspace_bytes: {_lib.last_error()}")
+    ws = workspace(dev, "key_cache", nbytes)
+    with torch.cuda.device(dev):
+        rc = lib.dwa_key_cache(stream_of(dev), dims, ptr(pool_vectors), ptr(key_proj), ptr(keys),
+                               ptr(ws), ws.numel())
+    _lib.check(rc, "dwa_key_cache")
+    return keys
+
+
+def centroid_ema(centroids: torch.Tensor, keys: torch.Tensor, list_offsets: torch.Tensor,
+                 decay: float = 0.9) -> torch.Tensor:
+    """The centroid update of train.py:318-328 in place: ``centroids [S, C, d_k]
+    = decay * centroids + (1 - decay) * mean of each list's keys`` (CSR
+    ``list_offsets [C+1]`` into ``keys [S, N, d_k]``).  Returns ``centroids``."""
+    require_cuda("centroids", centroids)
+    dev = centroids.device
+    require_cuda("keys", keys, dev)
+    require_cuda("list_offsets", list_offsets, dev)
+    S, C, d_k = centroids.shape
+    if centroids.dtype != torch.float32 or not centroids.is_contiguous():
+        raise ValueError("centroids must be contiguous float32 [S, C, d_k]")
+    if keys.dtype != torch.float32 or keys.shape[0] != S or keys.shape[2] != d_k:
+        raise ValueError("keys must be float32 [S, N, d_k]")
+    if list_offsets.dtype != torch.int64 or list_offsets.numel() != C + 1:
+        raise ValueError("list_offsets must be int64 [C+1]")
+    keys = keys.contiguous()
+    lib = _lib.load()
+    ws = workspace(dev, "centroid_ema", 256)
+    with torch.cuda.device(dev):
+        rc = lib.dwa_centroid_ema(stream_of(dev), S, C, d_k, keys.shape[1], ptr(keys),
+                                  ptr(list_offsets.contiguous()), float(decay), ptr(centroids),
+                                  ptr(ws), ws.numel())
+    _lib.check(rc, "dwa_centroid_ema")
+    return centroids

@@ -75,6 +75,7 @@ class HotPathInputs:
     z: np.ndarray             # [B, d_A] float32
     g_hmid: np.ndarray        # [B, seq, d_B]
     g_W: np.ndarray           # [B, d_B, d_A]
+    key_proj: np.ndarray | None = None   # [S, D, d_k], keys = pool @ key_proj (not in the digest)
 
     def digest(self) -> str:
         h = hashlib.sha256()
@@ -142,4 +143,4 @@ def make_inputs(cfg: DWAConfig, batch: int, seq: int, seed: int = 0, *,
     return HotPathInputs(pool=pool, keys=keys, list_offsets=offsets.astype(np.int64),
                          centroids=centroids, W_Q=W_Q, aspect_weights=aspect_weights,
                          tau=tau, W_base=W_base, b_base=b_base, gamma=gamma, h_A=h_A, z=z,
-                         g_hmid=g_hmid, g_W=g_W)
+                         g_hmid=g_hmid, g_W=g_W, key_proj=key_proj)

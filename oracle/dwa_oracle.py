@@ -303,6 +303,19 @@ def compute_key_cache(pool_vectors, key_proj):
     return np.einsum("nd,sda->sna", pool_vectors, key_proj)
 
 
+def centroid_ema(centroids, keys, list_offsets, decay=0.9):
+    """Centroid update of train.py:318-328: ``decay * c + (1 - decay) * mean`` of
+    each list's keys (the reference reshapes equal lists ``[S, C, N/C, d_k]`` and
+    takes the mean over axis 2; CSR lists are the extension).  Empty lists keep
+    their centroid."""
+    out = centroids.copy()
+    for c in range(centroids.shape[1]):
+        lo, hi = int(list_offsets[c]), int(list_offsets[c + 1])
+        if hi > lo:
+            out[:, c] = decay * centroids[:, c] + (1 - decay) * keys[:, lo:hi].mean(axis=1)
+    return out
+
+
 # ---------------------------------------------------------------------------
 # Assembly forward: assemble_jax (assembly_pallas.py:42-75)
 # ---------------------------------------------------------------------------
