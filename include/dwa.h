@@ -27,6 +27,8 @@
  *   dwa_key_cache      src/dwa/assembly_pallas.py:392-400  compute_key_cache
  *                      src/dwa/pool.py:37-44               VectorPool.compute_keys
  *   dwa_centroid_ema   train.py:318-328                    centroid EMA of the IVF lists
+ *   dwa_rmsnorm_fwd/bwd src/dwa/assembly.py:29, model.py:207 nnx.RMSNorm after the assembly
+ *   dwa_pool_grad_scatter src/dwa/model.py:193-195        VJP of the pool gather
  */
 #ifndef DWA_H_
 #define DWA_H_
@@ -108,7 +110,8 @@ DWA_API void dwa_launch_counters(uint64_t* total, uint64_t* tensor_core_gemms, u
  * "full_scores", "select", "softmax_stats", "softmax_apply", "prep_factors",
  * "prep_bias", "gemm_W", "gemm_apply", "gemm_G", "gemm_gh", "gemm_P",
  * "gemm_Q", "colsum", "finalize", "bias_grad", "seq_mean", "merge",
- * "key_cache", "centroid_ema".  Passing NULL
+ * "key_cache", "centroid_ema", "rmsnorm_fwd", "rmsnorm_bwd", "scatter_sort",
+ * "scatter_add".  Passing NULL
  * events removes the entry; dwa_profile_clear() removes all. */
 DWA_API int  dwa_profile_kernel(const char* kernel, void* start_event, void* stop_event);
 DWA_API void dwa_profile_clear(void);
@@ -259,6 +262,44 @@ DWA_API int dwa_key_cache(void* stream, const DwaKeyCacheDims* dims, const void*
 DWA_API int dwa_centroid_ema(void* stream, int S, int C, int d_k, int64_t N, const float* keys,
                              const int64_t* list_offsets, float decay, float* centroids,
                              void* workspace, size_t workspace_bytes);
+
+/* ---------------------------------------------------------------------------
+ * RMSNorm of the assembly output.  Replaces the assembler's layer_norm
+ * (flax nnx.RMSNorm(d_B), src/dwa/assembly.py:29, applied at
+ * src/dwa/model.py:207-219): over rows of x [rows, d] (x_dtype),
+ *   y = x * (rsqrt(mean(x^2) + eps) * scale),  scale [d] f32, eps 1e-6 in flax,
+ * statistics in fp32, y [rows, d] in y_dtype (flax promotes bf16 x with its fp32
+ * scale to fp32), rstd [rows] f32 saved for the backward.  The backward takes
+ * g_y [rows, d] (g_dtype) and writes g_x [rows, d] (x_dtype) and g_scale [d]
+ * f32 (overwritten; deterministic).  d % 8 == 0, 16-byte aligned rows.
+ * ------------------------------------------------------------------------- */
+DWA_API int dwa_rmsnorm_fwd(void* stream, int64_t rows, int d, int x_dtype, int y_dtype, const void* x,
+                            const float* scale, float eps, void* y, float* rstd);
+
+DWA_API size_t dwa_rmsnorm_bwd_workspace_bytes(int64_t rows, int d);
+
+DWA_API int dwa_rmsnorm_bwd(void* stream, int64_t rows, int d, int x_dtype, int g_dtype, const void* x,
+                            const float* scale, const float* rstd, const void* g_y, void* g_x,
+                            float* g_scale, void* workspace, size_t workspace_bytes);
+
+/* ---------------------------------------------------------------------------
+ * Pool-row gradient scatter: the VJP of the gather pool[indices]
+ * (src/dwa/model.py:193-195; of _distributed_gather, model.py:16-47, with the
+ * pool row-sharded).  For the n contributions g_rows [n, D] f32 of pool rows
+ * indices [n] int32 (the backward's g_rows [B,k,D] and the retrieval indices),
+ *   g_pool[row - row_lo, :] += sum of the g_rows of that row
+ * over the rows inside [row_lo, row_hi) of an n_global-row pool; g_pool is
+ * [row_hi - row_lo, D] in g_dtype (DWA_F32 or DWA_BF16, rounded once per row).
+ * Rows of other windows are skipped; rows outside [0, n_global) set
+ * DWA_STATUS_BAD_ROW_INDEX.  Deterministic (no atomics); n <= 8192 per call.
+ * Rows not selected are left as they are: pass a zeroed g_pool for the dense
+ * gradient the reference's autodiff forms.
+ * ------------------------------------------------------------------------- */
+DWA_API size_t dwa_pool_grad_scatter_workspace_bytes(int n);
+
+DWA_API int dwa_pool_grad_scatter(void* stream, int n, int D, const int32_t* indices, const float* g_rows,
+                                  int64_t n_global, int64_t row_lo, int64_t row_hi, int g_dtype,
+                                  void* g_pool, void* workspace, size_t workspace_bytes);
 
 /* ---------------------------------------------------------------------------
  * Retrieval without a workspace.  No counterpart in the reference: it exists for

@@ -77,6 +77,13 @@ _SIGNATURES = {
                                      _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t]),
     "dwa_retrieve_merge_workspace_bytes": (C.c_size_t, [C.POINTER(RetrieveDims)]),
     "dwa_key_cache_workspace_bytes": (C.c_size_t, [C.POINTER(KeyCacheDims)]),
+    "dwa_rmsnorm_fwd": (C.c_int, [_P, C.c_int64, C.c_int, C.c_int, C.c_int, _P, _P, C.c_float, _P, _P]),
+    "dwa_rmsnorm_bwd_workspace_bytes": (C.c_size_t, [C.c_int64, C.c_int]),
+    "dwa_pool_grad_scatter_workspace_bytes": (C.c_size_t, [C.c_int]),
+    "dwa_pool_grad_scatter": (C.c_int, [_P, C.c_int, C.c_int, _P, _P, C.c_int64, C.c_int64, C.c_int64,
+                                        C.c_int, _P, _P, C.c_size_t]),
+    "dwa_rmsnorm_bwd": (C.c_int, [_P, C.c_int64, C.c_int, C.c_int, C.c_int, _P, _P, _P, _P, _P, _P, _P,
+                                  C.c_size_t]),
     "dwa_key_cache": (C.c_int, [_P, C.POINTER(KeyCacheDims), _P, _P, _P, _P, C.c_size_t]),
     "dwa_centroid_ema": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int64, _P, _P, C.c_float, _P, _P,
                                    C.c_size_t]),

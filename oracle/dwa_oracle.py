@@ -317,6 +317,30 @@ def centroid_ema(centroids, keys, list_offsets, decay=0.9):
 
 
 # ---------------------------------------------------------------------------
+# RMSNorm after the assembly (assembly.py:29, model.py:207-219)
+# ---------------------------------------------------------------------------
+# The reference calls flax's ``nnx.RMSNorm(d_B)``; flax is not vendored and its
+# version is not pinned (pyproject.toml:7 lists no dependencies).  Restated from
+# flax's published algorithm: statistics ``mean(x^2)`` over the feature axis in
+# at least float32, ``mul = rsqrt(var + epsilon) * scale`` (epsilon = 1e-6 by
+# default, scale initialised to ones), ``y = x * mul``.
+
+def rms_norm(x, scale, eps=1e-6):
+    var = np.mean(np.square(x), axis=-1, keepdims=True)
+    return x * (1.0 / np.sqrt(var + eps) * scale)
+
+
+def rms_norm_bwd(x, scale, g, eps=1e-6):
+    """VJP of ``rms_norm`` w.r.t. ``x`` and ``scale`` (``g`` = dL/dy)."""
+    d = x.shape[-1]
+    r = 1.0 / np.sqrt(np.mean(np.square(x), axis=-1, keepdims=True) + eps)
+    dot = np.sum(g * scale * x, axis=-1, keepdims=True)
+    g_x = r * scale * g - (r ** 3 / d) * x * dot
+    g_scale = np.sum((g * x * r).reshape(-1, d), axis=0)
+    return g_x, g_scale
+
+
+# ---------------------------------------------------------------------------
 # Assembly forward: assemble_jax (assembly_pallas.py:42-75)
 # ---------------------------------------------------------------------------
 
