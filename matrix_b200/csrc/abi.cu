@@ -2,6 +2,7 @@
 // device status readback, launch counters and TMA tensor-map encoding.
 #include <atomic>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -11,6 +12,14 @@
 namespace dwa {
 
 std::atomic<uint64_t> g_launches_total{0}, g_launches_tc{0}, g_launches_simt{0};
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("DWA_PDL");
+        return !(v && std::strcmp(v, "0") == 0);
+    }();
+    return on;
+}
 
 static thread_local std::string t_last_error;
 

@@ -257,6 +257,7 @@ template <class ACT, class RT>
 __global__ void prep_factors_kernel(RowSrc src, const float* __restrict__ alphas, int d_A, int d_B,
                                     int r, int64_t ldu, ACT* __restrict__ Ug, ACT* __restrict__ Vs,
                                     uint32_t* status) {
+    pdl_enter();
     const int kk = blockIdx.x, b = blockIdx.y, k = src.k;
     const int64_t off = src.offset(b, kk);
     if (off < 0 && threadIdx.x == 0) raise_status(status, DWA_STATUS_BAD_ROW_INDEX);
@@ -283,6 +284,7 @@ __global__ void prep_factors_kernel(RowSrc src, const float* __restrict__ alphas
 __global__ void __launch_bounds__(256) prep_factors_bf16_r8_kernel(
     RowSrc src, const float* __restrict__ alphas, int d_A, int d_B, int64_t ldu,
     __nv_bfloat16* __restrict__ Ug, __nv_bfloat16* __restrict__ Vs, uint32_t* status) {
+    pdl_enter();
     const int kk = blockIdx.x, b = blockIdx.y, k = src.k;
     const int64_t off = src.offset(b, kk);
     if (off < 0 && threadIdx.x == 0) raise_status(status, DWA_STATUS_BAD_ROW_INDEX);
@@ -326,6 +328,7 @@ template <class RT>
 __global__ void __launch_bounds__(256) prep_bias_kernel(RowSrc src, const float* __restrict__ alphas,
                                                         const float* __restrict__ b_base, int64_t s2,
                                                         int d_B, float* __restrict__ pb) {
+    pdl_enter();
     extern __shared__ int64_t offs[];   // [k]
     const int b = blockIdx.y;
     for (int kk = threadIdx.x; kk < src.k; kk += blockDim.x) offs[kk] = src.offset(b, kk);
@@ -349,6 +352,7 @@ __global__ void finalize_kernel(RowSrc src, const float* __restrict__ alphas,
                                 const float* __restrict__ gamma_acc, int64_t s2, int d_B,
                                 float* __restrict__ g_rows, float* __restrict__ g_alpha,
                                 float* __restrict__ g_gamma) {
+    pdl_enter();
     const int kk = blockIdx.x, b = blockIdx.y, k = src.k;
     __shared__ float s_red[32];
     const int64_t off = src.offset(b, kk);
@@ -376,6 +380,7 @@ __global__ void finalize_kernel(RowSrc src, const float* __restrict__ alphas,
 
 __global__ void bias_grad_kernel(const float* __restrict__ gbias, int B, int d,
                                  float* __restrict__ g_b_base) {
+    pdl_enter();
     const int j = blockIdx.x * blockDim.x + threadIdx.x;
     if (j >= d) return;
     float acc = 0.f;
@@ -491,12 +496,12 @@ static int prep(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src, co
     if (!with_factors) {
     } else if (vec8)
         DWA_TIMED("prep_factors", st,
-                  prep_factors_bf16_r8_kernel<<<g1, 256, 0, st>>>(
+                  launch_pdl(prep_factors_bf16_r8_kernel, g1, 256, 0, st, 
                       src, alphas, d.d_A, d.d_B, w.ldu, static_cast<__nv_bfloat16*>(w.Ug),
                       static_cast<__nv_bfloat16*>(w.Vs), w.status));
     else
         DWA_TIMED("prep_factors", st,
-                  prep_factors_kernel<ACT, RT><<<g1, 256, 0, st>>>(src, alphas, d.d_A, d.d_B, d.r,
+                  launch_pdl(prep_factors_kernel<ACT, RT>, g1, 256, 0, st, src, alphas, d.d_A, d.d_B, d.r,
                                                                    w.ldu, static_cast<ACT*>(w.Ug),
                                                                    static_cast<ACT*>(w.Vs), w.status));
     DWA_LAUNCH_CHECK("prep_factors_kernel");
@@ -505,7 +510,7 @@ static int prep(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src, co
         const int64_t s2 = static_cast<int64_t>(d.d_B) * d.r + static_cast<int64_t>(d.r) * d.d_A;
         dim3 g2((d.d_B + 255) / 256, d.B);
         DWA_TIMED("prep_bias", st,
-                  prep_bias_kernel<RT><<<g2, 256, d.k * sizeof(int64_t), st>>>(src, alphas, b_base, s2,
+                  launch_pdl(prep_bias_kernel<RT>, g2, 256, d.k * sizeof(int64_t), st, src, alphas, b_base, s2,
                                                                               d.d_B, w.pb));
         DWA_LAUNCH_CHECK("prep_bias_kernel");
         ++g_launches_total;
@@ -587,14 +592,14 @@ static int bwd_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src
 
     if (d.d_B % 8 == 0 && reinterpret_cast<uintptr_t>(g) % 16 == 0) {
         dim3 gc((d.d_B + 255) / 256, d.B);
-        DWA_TIMED("colsum", a1, column_sum8_kernel<ACT><<<gc, 512, 0, a1>>>(g, d.T, d.d_B, 0, w.gbias));
+        DWA_TIMED("colsum", a1, launch_pdl(column_sum8_kernel<ACT>, gc, 512, 0, a1, g, d.T, d.d_B, 0, w.gbias));
     } else {
         dim3 gc((d.d_B + 63) / 64, d.B);
-        DWA_TIMED("colsum", a1, column_sum_kernel<ACT><<<gc, 1024, 0, a1>>>(g, d.T, d.d_B, 0, w.gbias));
+        DWA_TIMED("colsum", a1, launch_pdl(column_sum_kernel<ACT>, gc, 1024, 0, a1, g, d.T, d.d_B, 0, w.gbias));
     }
     DWA_LAUNCH_CHECK("colsum_kernel");
     DWA_TIMED("bias_grad", a1,
-              bias_grad_kernel<<<(d.d_B + 255) / 256, 256, 0, a1>>>(w.gbias, d.B, d.d_B, g_b_base));
+              launch_pdl(bias_grad_kernel, (d.d_B + 255) / 256, 256, 0, a1, w.gbias, d.B, d.d_B, g_b_base));
     DWA_LAUNCH_CHECK("bias_grad_kernel");
     g_launches_total += 2;
 
@@ -635,7 +640,7 @@ static int bwd_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src
     if ((rc = lanes.join())) return rc;
     dim3 gf(d.k, d.B);
     DWA_TIMED("finalize", st,
-              finalize_kernel<RT><<<gf, 256, 0, st>>>(src, alphas, w.gbias, w.dW_acc, w.gamma_acc, s2,
+              launch_pdl(finalize_kernel<RT>, gf, 256, 0, st, src, alphas, w.gbias, w.dW_acc, w.gamma_acc, s2,
                                                       d.d_B, g_rows, g_alpha, g_gamma));
     DWA_LAUNCH_CHECK("finalize_kernel");
     ++g_launches_total;

@@ -6,6 +6,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 #include <string>
+#include <utility>
 
 #include "../../include/dwa.h"
 
@@ -32,6 +33,36 @@ int fail(int code, const std::string& msg);
             return ::dwa::fail(DWA_ERR_CUDA, std::string("launch of " what        \
                                                  " failed: ") + cudaGetErrorString(_e)); \
     } while (0)
+
+// Programmatic dependent launch.  Every kernel of the library is launched with
+// launch_pdl, which lets the next kernel of the same stream (or CUDA graph) be
+// scheduled while this one drains, and every kernel calls pdl_enter() before it
+// touches global memory that an earlier kernel wrote: griddepcontrol.wait returns
+// once the preceding kernel has completed and its writes are visible; then
+// launch_dependents allows the following kernel to start its prologue.  Both are
+// no-ops for a kernel launched without the attribute.  DWA_PDL=0 disables it.
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+bool pdl_enabled();
+
+template <class... KArgs, class... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Kernel timing hook (dwa_profile_kernel): event pair recorded around the
 // launches of one named kernel.
@@ -140,6 +171,7 @@ __device__ __forceinline__ float warp_max(float v) {
 template <class T>
 __global__ void __launch_bounds__(1024) column_sum_kernel(const T* __restrict__ x, int T_, int d,
                                                           int mean, float* __restrict__ out) {
+    pdl_enter();
     __shared__ float part[32][65];
     const int b = blockIdx.y, lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int c = blockIdx.x * 64 + 2 * lane;
@@ -176,6 +208,7 @@ __global__ void __launch_bounds__(1024) column_sum_kernel(const T* __restrict__ 
 template <class T>
 __global__ void __launch_bounds__(512) column_sum8_kernel(const T* __restrict__ x, int T_, int d,
                                                           int mean, float* __restrict__ out) {
+    pdl_enter();
     __shared__ float part[16][257];
     const int b = blockIdx.y, lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int c = blockIdx.x * 256 + 8 * lane;

@@ -34,6 +34,7 @@ extern std::atomic<uint64_t> g_launches_total, g_launches_tc, g_launches_simt;
 // bt[s*d_k + a, d] = kp[s, d, a]: 32 x 32 tiles through shared memory.
 template <class T>
 __global__ void proj_relayout_kernel(const T* __restrict__ kp, T* __restrict__ bt, int S, int D, int d_k) {
+    pdl_enter();
     __shared__ T tile[32][33];
     const int s = blockIdx.z, d0 = blockIdx.x * 32, a0 = blockIdx.y * 32;
     for (int i = threadIdx.y; i < 32; i += blockDim.y) {
@@ -71,6 +72,7 @@ struct EpiKeys : NoReduce {
 __global__ void centroid_ema_kernel(const float* __restrict__ keys, const int64_t* __restrict__ off,
                                     int64_t N, int C, int d_k, float decay, float* __restrict__ cent,
                                     uint32_t* status) {
+    pdl_enter();
     extern __shared__ float part[];   // [blockDim.y][d_k]
     const int c = blockIdx.x, s = blockIdx.y;
     const int64_t lo = off[c], hi = off[c + 1];
@@ -132,10 +134,10 @@ extern "C" int dwa_key_cache(void* stream, const DwaKeyCacheDims* dims, const vo
     void* bt = static_cast<char*>(workspace) + 256;
     const dim3 gr((d.D + 31) / 32, (d.d_k + 31) / 32, d.S), br(32, 8);
     if (d.dtype == DWA_BF16)
-        proj_relayout_kernel<__nv_bfloat16><<<gr, br, 0, st>>>(static_cast<const __nv_bfloat16*>(key_proj),
+        launch_pdl(proj_relayout_kernel<__nv_bfloat16>, gr, br, 0, st, static_cast<const __nv_bfloat16*>(key_proj),
                                                               static_cast<__nv_bfloat16*>(bt), d.S, d.D, d.d_k);
     else
-        proj_relayout_kernel<float><<<gr, br, 0, st>>>(static_cast<const float*>(key_proj),
+        launch_pdl(proj_relayout_kernel<float>, gr, br, 0, st, static_cast<const float*>(key_proj),
                                                       static_cast<float*>(bt), d.S, d.D, d.d_k);
     DWA_LAUNCH_CHECK("proj_relayout_kernel");
     ++g_launches_total;
@@ -191,7 +193,7 @@ extern "C" int dwa_centroid_ema(void* stream, int S, int C, int d_k, int64_t N, 
     const int ty = 1024 / tx < 16 ? 1024 / tx : 16;
     const size_t sh = static_cast<size_t>(ty) * d_k * sizeof(float);
     if (sh > 48 * 1024) return fail(DWA_ERR_UNSUPPORTED, "d_k too large for the EMA reduction");
-    DWA_TIMED("centroid_ema", st, centroid_ema_kernel<<<dim3(C, S), dim3(tx, ty), sh, st>>>(
+    DWA_TIMED("centroid_ema", st, launch_pdl(centroid_ema_kernel, dim3(C, S), dim3(tx, ty), sh, st, 
                                       keys, list_offsets, N, C, d_k, decay, centroids,
                                       static_cast<uint32_t*>(workspace)));
     DWA_LAUNCH_CHECK("centroid_ema_kernel");

@@ -47,6 +47,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(const TI* __r
                                                                   const float* __restrict__ scale, int d,
                                                                   float eps, TO* __restrict__ y,
                                                                   float* __restrict__ rstd) {
+    pdl_enter();
     __shared__ float red[33];
     const int64_t r = blockIdx.x;
     const TI* xr = x + r * d;
@@ -78,6 +79,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(const TI* __r
                                                                   const TG* __restrict__ gy, int64_t rows,
                                                                   int d, TI* __restrict__ gx,
                                                                   float* __restrict__ part) {
+    pdl_enter();
     __shared__ float red[33];
     extern __shared__ float gs[];   // [d] partial g_scale of this CTA
     for (int c = threadIdx.x; c < d; c += blockDim.x) gs[c] = 0.f;
@@ -141,7 +143,7 @@ extern "C" int dwa_rmsnorm_fwd(void* stream, int64_t rows, int d, int x_dtype, i
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const unsigned g = static_cast<unsigned>(rows);
 #define DWA_NORM_FWD(TI, TO)                                                                             \
-    DWA_TIMED("rmsnorm_fwd", st, (rmsnorm_fwd_kernel<TI, TO><<<g, kNormThreads, 0, st>>>(                 \
+    DWA_TIMED("rmsnorm_fwd", st, (launch_pdl(rmsnorm_fwd_kernel<TI, TO>, g, kNormThreads, 0, st,                  \
                                       static_cast<const TI*>(x), scale, d, eps, static_cast<TO*>(y), rstd)))
     if (x_dtype == DWA_BF16 && y_dtype == DWA_BF16) DWA_NORM_FWD(__nv_bfloat16, __nv_bfloat16);
     else if (x_dtype == DWA_BF16) DWA_NORM_FWD(__nv_bfloat16, float);
@@ -175,7 +177,7 @@ extern "C" int dwa_rmsnorm_bwd(void* stream, int64_t rows, int d, int x_dtype, i
     const int nblk = static_cast<int>((rows + kNormRowsPerBlock - 1) / kNormRowsPerBlock);
     const size_t sh = static_cast<size_t>(d) * sizeof(float);
 #define DWA_NORM_BWD(TI, TG)                                                                              \
-    DWA_TIMED("rmsnorm_bwd", st, (rmsnorm_bwd_kernel<TI, TG><<<nblk, kNormThreads, sh, st>>>(              \
+    DWA_TIMED("rmsnorm_bwd", st, (launch_pdl(rmsnorm_bwd_kernel<TI, TG>, nblk, kNormThreads, sh, st,               \
                                       static_cast<const TI*>(x), scale, rstd, static_cast<const TG*>(g_y),  \
                                       rows, d, static_cast<TI*>(g_x), part)))
     if (x_dtype == DWA_BF16 && g_dtype == DWA_BF16) DWA_NORM_BWD(__nv_bfloat16, __nv_bfloat16);
@@ -184,7 +186,7 @@ extern "C" int dwa_rmsnorm_bwd(void* stream, int64_t rows, int d, int x_dtype, i
     else DWA_NORM_BWD(float, float);
 #undef DWA_NORM_BWD
     DWA_LAUNCH_CHECK("rmsnorm_bwd_kernel");
-    column_sum_kernel<float><<<dim3((d + 63) / 64, 1), 1024, 0, st>>>(part, nblk, d, 0, g_scale);
+    launch_pdl(column_sum_kernel<float>, dim3((d + 63) / 64, 1), 1024, 0, st, part, nblk, d, 0, g_scale);
     DWA_LAUNCH_CHECK("column_sum_kernel");
     g_launches_total += 2;
     return DWA_OK;

@@ -25,6 +25,7 @@ __global__ void __launch_bounds__(1024) scatter_sort_kernel(const int32_t* __res
                                                            int64_t n_global, int64_t row_lo, int64_t row_hi,
                                                            int32_t* __restrict__ order, int32_t* __restrict__ seg,
                                                            uint32_t* status) {
+    pdl_enter();
     extern __shared__ uint64_t key[];   // [np2]
     int np2 = 1;
     while (np2 < n) np2 <<= 1;
@@ -79,6 +80,7 @@ __global__ void __launch_bounds__(256) scatter_add_kernel(const int32_t* __restr
                                                           const int32_t* __restrict__ order,
                                                           const int32_t* __restrict__ seg, int64_t row_lo,
                                                           TG* __restrict__ g_pool) {
+    pdl_enter();
     const int s = blockIdx.x;
     if (s >= seg[kScatterMaxN + 1]) return;
     const int j0 = seg[s], j1 = seg[s + 1];
@@ -132,15 +134,15 @@ extern "C" int dwa_pool_grad_scatter(void* stream, int n, int D, const int32_t* 
             if (dev >= 0 && dev < 64) attr_set[dev] = true;
         }
     }
-    DWA_TIMED("scatter_sort", st, scatter_sort_kernel<<<1, 1024, sh, st>>>(indices, n, n_global, row_lo, row_hi,
+    DWA_TIMED("scatter_sort", st, launch_pdl(scatter_sort_kernel, 1, 1024, sh, st, indices, n, n_global, row_lo, row_hi,
                                                                          order, seg, status));
     DWA_LAUNCH_CHECK("scatter_sort_kernel");
     const dim3 g(static_cast<unsigned>(n), static_cast<unsigned>((D + kScatterCols - 1) / kScatterCols));
     if (g_dtype == DWA_BF16)
-        DWA_TIMED("scatter_add", st, scatter_add_kernel<__nv_bfloat16><<<g, 256, 0, st>>>(
+        DWA_TIMED("scatter_add", st, launch_pdl(scatter_add_kernel<__nv_bfloat16>, g, 256, 0, st, 
                                          indices, g_rows, D, order, seg, row_lo, static_cast<__nv_bfloat16*>(g_pool)));
     else
-        DWA_TIMED("scatter_add", st, scatter_add_kernel<float><<<g, 256, 0, st>>>(
+        DWA_TIMED("scatter_add", st, launch_pdl(scatter_add_kernel<float>, g, 256, 0, st, 
                                          indices, g_rows, D, order, seg, row_lo, static_cast<float*>(g_pool)));
     DWA_LAUNCH_CHECK("scatter_add_kernel");
     g_launches_total += 2;

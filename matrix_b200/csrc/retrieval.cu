@@ -240,6 +240,7 @@ __global__ void __launch_bounds__(256) query_proj_kernel(const ZT* __restrict__ 
                                                          const float* __restrict__ W_Q, int B,
                                                          int rows, int d_A, int btile,
                                                          float* __restrict__ q) {
+    pdl_enter();
     extern __shared__ float zs[];  // [btile][d_A]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int o = blockIdx.x * (blockDim.x >> 5) + warp;
@@ -301,6 +302,7 @@ __global__ void __launch_bounds__(256) query_proj_kernel(const ZT* __restrict__ 
 // qw[b,s,:] = softmax(aspect_weights)_s * q[b,s,:] / (|q[b,s,:]| + 1e-8)   (:66, :69)
 __global__ void query_norm_kernel(float* __restrict__ qw, const float* __restrict__ aspect_w,
                                   int S, int d_k) {
+    pdl_enter();
     const int b = blockIdx.x, s = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (s >= S) return;
     float* q = qw + (static_cast<int64_t>(b) * S + s) * d_k;
@@ -323,6 +325,7 @@ template <int DK>
 __global__ void __launch_bounds__(1024) coarse_kernel(const float* __restrict__ qw,
                                                       const float* __restrict__ centroids, int S,
                                                       int d_k, int C, float* __restrict__ c_score) {
+    pdl_enter();
     extern __shared__ __align__(16) float qs[];   // [S*d_k] then terms [S][64]
     float* terms = qs + S * d_k;
     const int b = blockIdx.y;
@@ -381,6 +384,7 @@ __global__ void __launch_bounds__(512) topm_kernel(
     const float* __restrict__ c_score, int C, int m, const int64_t* __restrict__ list_off,
     int64_t n_global, int64_t row_lo, int64_t row_hi, int max_list, int32_t* __restrict__ top_clusters,
     int64_t* __restrict__ probe_lo, int64_t* __restrict__ cand_base, uint32_t* status) {
+    pdl_enter();
     __shared__ uint64_t sel_key[kMaxK];
     __shared__ int64_t sel_pos[kMaxK];
     extern __shared__ uint64_t skeys[];
@@ -428,6 +432,7 @@ __global__ void fine_kernel(const float* __restrict__ qw, const float* __restric
                             int S, int d_k, int m, const int64_t* __restrict__ probe_lo,
                             const int64_t* __restrict__ cand_base, int64_t K_cap,
                             float* __restrict__ scores) {
+    pdl_enter();
     extern __shared__ __align__(16) float qs[];
     const int b = blockIdx.z, j = blockIdx.y;
     for (int i = threadIdx.x; i < S * d_k; i += blockDim.x)
@@ -449,6 +454,7 @@ template <int NB, int DK>
 __global__ void __launch_bounds__(256) full_scores_kernel(
     const float* __restrict__ qw, const float* __restrict__ keys, int64_t N, int S, int d_k, int B,
     float invT, float* __restrict__ sfull, float* __restrict__ partial) {
+    pdl_enter();
     extern __shared__ __align__(16) float qs[];  // [NB][S][d_k]
     __shared__ float red[33];
     const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -480,6 +486,7 @@ __global__ void __launch_bounds__(256) full_scores_kernel(
 
 // The summary of a rank that holds no rows: no candidates, no soft_full mass.
 __global__ void empty_summary_kernel(float* summary, int k) {
+    pdl_enter();
     float* sm = summary + static_cast<int64_t>(blockIdx.x) * summary_width(k);
     for (int i = threadIdx.x; i < k; i += blockDim.x) {
         sm[i] = -INFINITY;
@@ -490,6 +497,7 @@ __global__ void empty_summary_kernel(float* summary, int k) {
 
 // A rank without soft_full: statistics that contribute nothing to the merge.
 __global__ void fill_stats_kernel(float* stats, int B, int stride) {
+    pdl_enter();
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
     stats[static_cast<int64_t>(b) * stride] = -INFINITY;
@@ -500,6 +508,7 @@ __global__ void fill_stats_kernel(float* stats, int B, int stride) {
 // written to stats[b * stride + {0, 1}].
 __global__ void softmax_stats_kernel(const float* __restrict__ partial, int nblk,
                                      float* __restrict__ stats, int stride) {
+    pdl_enter();
     __shared__ float red[33];
     const int b = blockIdx.x;
     const float* p = partial + static_cast<int64_t>(b) * nblk * 2;
@@ -516,6 +525,7 @@ __global__ void softmax_stats_kernel(const float* __restrict__ partial, int nblk
 // full pass used for M and Z); 8 elements per thread.
 __global__ void __launch_bounds__(256) softmax_apply_kernel(float* __restrict__ sfull, int64_t N,
                                                             float invT, const float* __restrict__ stats) {
+    pdl_enter();
     const int b = blockIdx.y;
     const float mx = stats[2 * b], z = stats[2 * b + 1];
     float* p = sfull + static_cast<int64_t>(b) * N;
@@ -592,6 +602,7 @@ __device__ void write_alphas(int got, int k, bool gate, float lam, float tau, fl
 // computed once into shared memory and every radix pass reads them there.
 template <bool STAGED>
 __global__ void __launch_bounds__(1024) select_kernel(SelectArgs a) {
+    pdl_enter();
     __shared__ uint64_t sel_key[kMaxK];
     __shared__ int64_t sel_pos[kMaxK];
     __shared__ int64_t s_lo[kMaxK + 1], s_base[kMaxK + 1];
@@ -700,6 +711,7 @@ struct MergeArgs {
 };
 
 __global__ void __launch_bounds__(1024) merge_kernel(MergeArgs a) {
+    pdl_enter();
     __shared__ uint64_t sel_key[kMaxK];
     __shared__ int64_t sel_pos[kMaxK];
     __shared__ float s_sv[kMaxK];
@@ -762,6 +774,7 @@ __global__ void __launch_bounds__(1024) merge_kernel(MergeArgs a) {
 }
 
 __global__ void full_probe_kernel(int B, int64_t N, int64_t* probe_lo, int64_t* cand_base) {
+    pdl_enter();
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
     probe_lo[2 * b] = 0; probe_lo[2 * b + 1] = 0;
@@ -888,16 +901,16 @@ static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaSha
     const int btile = std::max(1, std::min({QB, d.B, static_cast<int>((48 * 1024) / (4 * d.d_A))}));
     const size_t zsh = static_cast<size_t>(btile) * d.d_A * sizeof(float);
     if (d.z_dtype == DWA_BF16)
-        DWA_TIMED("query", st, query_proj_kernel<__nv_bfloat16><<<(rows + 3) / 4, 128, zsh, st>>>(
+        DWA_TIMED("query", st, launch_pdl(query_proj_kernel<__nv_bfloat16>, (rows + 3) / 4, 128, zsh, st, 
                                      static_cast<const __nv_bfloat16*>(z), W_Q, d.B, rows, d.d_A,
                                      btile, w.qw));
     else
-        DWA_TIMED("query", st, query_proj_kernel<float><<<(rows + 3) / 4, 128, zsh, st>>>(
+        DWA_TIMED("query", st, launch_pdl(query_proj_kernel<float>, (rows + 3) / 4, 128, zsh, st, 
                                      static_cast<const float*>(z), W_Q, d.B, rows, d.d_A, btile,
                                      w.qw));
     DWA_LAUNCH_CHECK("query_proj_kernel");
     DWA_TIMED("query_norm", st,
-              query_norm_kernel<<<d.B, 32 * d.S, 0, st>>>(w.qw, aspect_weights, d.S, d.d_k));
+              launch_pdl(query_norm_kernel, d.B, 32 * d.S, 0, st, w.qw, aspect_weights, d.S, d.d_k));
     DWA_LAUNCH_CHECK("query_norm_kernel");
     g_launches_total += 2;
 
@@ -908,21 +921,21 @@ static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaSha
         const int cth = 64 * d.S;                       // S <= 16 (checked on entry)
         const size_t csh = qsh + static_cast<size_t>(d.S) * 64 * sizeof(float);
         if (dk64)
-            DWA_TIMED("coarse", st, coarse_kernel<64><<<gc, cth, csh, st>>>(
+            DWA_TIMED("coarse", st, launch_pdl(coarse_kernel<64>, gc, cth, csh, st, 
                                         w.qw, centroids, d.S, d.d_k, d.C, w.c_score));
         else
-            DWA_TIMED("coarse", st, coarse_kernel<0><<<gc, cth, csh, st>>>(
+            DWA_TIMED("coarse", st, launch_pdl(coarse_kernel<0>, gc, cth, csh, st, 
                                         w.qw, centroids, d.S, d.d_k, d.C, w.c_score));
         DWA_LAUNCH_CHECK("coarse_kernel");
         const size_t tsh = d.C <= kStageKeys ? static_cast<size_t>(d.C) * 8 : 0;
-        DWA_TIMED("topm", st, topm_kernel<<<d.B, 512, tsh, st>>>(w.c_score, d.C, w.m_eff, list_offsets,
+        DWA_TIMED("topm", st, launch_pdl(topm_kernel, d.B, 512, tsh, st, w.c_score, d.C, w.m_eff, list_offsets,
                                                                  n_global, row_lo, row_lo + d.N,
                                                                  d.max_list, w.topc, w.probe_lo,
                                                                  w.cand_base, w.status));
         DWA_LAUNCH_CHECK("topm_kernel");
         g_launches_total += 2;
     } else {
-        full_probe_kernel<<<(d.B + 127) / 128, 128, 0, st>>>(d.B, d.N, w.probe_lo, w.cand_base);
+        launch_pdl(full_probe_kernel, (d.B + 127) / 128, 128, 0, st, d.B, d.N, w.probe_lo, w.cand_base);
         DWA_LAUNCH_CHECK("full_probe_kernel");
         ++g_launches_total;
     }
@@ -1020,20 +1033,20 @@ static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaSha
         const char* name = mode == 0 ? "full_scores" : "fine";
         if (use_tc) {
             if (nq == 16)
-                DWA_TIMED(name, st, sc::key_scan_tc_kernel<16><<<blocks, sc::THREADS, tc_smem, st>>>(tm_scores, ka));
+                DWA_TIMED(name, st, launch_pdl(sc::key_scan_tc_kernel<16>, blocks, sc::THREADS, tc_smem, st, tm_scores, ka));
             else
-                DWA_TIMED(name, st, sc::key_scan_tc_kernel<32><<<blocks, sc::THREADS, tc_smem, st>>>(tm_scores, ka));
+                DWA_TIMED(name, st, launch_pdl(sc::key_scan_tc_kernel<32>, blocks, sc::THREADS, tc_smem, st, tm_scores, ka));
             DWA_LAUNCH_CHECK("key_scan_tc_kernel");
         } else {
             const size_t smem = mode == 1 ? ks::smem_bytes<8>(fine_stages, d.B, d.S) : scan_full_smem(scan_stages);
             if (mode == 1)
-                DWA_TIMED(name, st, (ks::key_scan_kernel<8, true><<<blocks, ks::THREADS, smem, st>>>(tm_scores, ka)));
+                DWA_TIMED(name, st, (launch_pdl(ks::key_scan_kernel<8, true>, blocks, ks::THREADS, smem, st, tm_scores, ka)));
             else if (qb == 4)
-                DWA_TIMED(name, st, (ks::key_scan_kernel<4, false><<<blocks, ks::THREADS, smem, st>>>(tm_scores, ka)));
+                DWA_TIMED(name, st, (launch_pdl(ks::key_scan_kernel<4, false>, blocks, ks::THREADS, smem, st, tm_scores, ka)));
             else if (qb == 8)
-                DWA_TIMED(name, st, (ks::key_scan_kernel<8, false><<<blocks, ks::THREADS, smem, st>>>(tm_scores, ka)));
+                DWA_TIMED(name, st, (launch_pdl(ks::key_scan_kernel<8, false>, blocks, ks::THREADS, smem, st, tm_scores, ka)));
             else
-                DWA_TIMED(name, st, (ks::key_scan_kernel<16, false><<<blocks, ks::THREADS, smem, st>>>(tm_scores, ka)));
+                DWA_TIMED(name, st, (launch_pdl(ks::key_scan_kernel<16, false>, blocks, ks::THREADS, smem, st, tm_scores, ka)));
             DWA_LAUNCH_CHECK("key_scan_kernel");
         }
         ++g_launches_total;
@@ -1049,11 +1062,11 @@ static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaSha
         constexpr int NB = 8;
         if (dk64)
             DWA_TIMED("full_scores", st,
-                      full_scores_kernel<NB, 64><<<w.nblk, kFullRows, NB * qsh, st>>>(
+                      launch_pdl(full_scores_kernel<NB, 64>, w.nblk, kFullRows, NB * qsh, st, 
                           w.qw, pool_keys, d.N, d.S, d.d_k, d.B, 1.f / d.T, sfull, w.partial));
         else
             DWA_TIMED("full_scores", st,
-                      full_scores_kernel<NB, 0><<<w.nblk, kFullRows, NB * qsh, st>>>(
+                      launch_pdl(full_scores_kernel<NB, 0>, w.nblk, kFullRows, NB * qsh, st, 
                           w.qw, pool_keys, d.N, d.S, d.d_k, d.B, 1.f / d.T, sfull, w.partial));
         DWA_LAUNCH_CHECK("full_scores_kernel");
         ++g_launches_total;
@@ -1064,11 +1077,11 @@ static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaSha
     } else if (ivf && !want_sf) {
         dim3 gf(static_cast<unsigned>((d.max_list + 255) / 256), w.m_eff, d.B);
         if (dk64)
-            DWA_TIMED("fine", st, fine_kernel<64><<<gf, 256, qsh, st>>>(
+            DWA_TIMED("fine", st, launch_pdl(fine_kernel<64>, gf, 256, qsh, st, 
                                       w.qw, pool_keys, d.N, d.S, d.d_k, w.m_eff, w.probe_lo,
                                       w.cand_base, w.K_cap, w.scores));
         else
-            DWA_TIMED("fine", st, fine_kernel<0><<<gf, 256, qsh, st>>>(
+            DWA_TIMED("fine", st, launch_pdl(fine_kernel<0>, gf, 256, qsh, st, 
                                       w.qw, pool_keys, d.N, d.S, d.d_k, w.m_eff, w.probe_lo,
                                       w.cand_base, w.K_cap, w.scores));
         DWA_LAUNCH_CHECK("fine_kernel");
@@ -1106,9 +1119,9 @@ static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaSha
                 if (dev >= 0 && dev < 64) attr_set[dev] = true;
             }
         }
-        DWA_TIMED("select", st, select_kernel<true><<<d.B, 1024, ssh, st>>>(sa));
+        DWA_TIMED("select", st, launch_pdl(select_kernel<true>, d.B, 1024, ssh, st, sa));
     } else {
-        DWA_TIMED("select", st, select_kernel<false><<<d.B, 1024, 0, st>>>(sa));
+        DWA_TIMED("select", st, launch_pdl(select_kernel<false>, d.B, 1024, 0, st, sa));
     }
     DWA_LAUNCH_CHECK("select_kernel");
     ++g_launches_total;
@@ -1116,21 +1129,21 @@ static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaSha
     //    statistics into the summary; the merge normalises)
     if (want_sf && shard) {
         DWA_TIMED("softmax_stats", st,
-                  softmax_stats_kernel<<<d.B, 256, 0, st>>>(w.partial, sf_blocks, summary + 2 * d.k + 1,
+                  launch_pdl(softmax_stats_kernel, d.B, 256, 0, st, w.partial, sf_blocks, summary + 2 * d.k + 1,
                                                             summary_width(d.k)));
         DWA_LAUNCH_CHECK("softmax_stats_kernel");
         ++g_launches_total;
     } else if (shard) {
-        fill_stats_kernel<<<(d.B + 127) / 128, 128, 0, st>>>(summary + 2 * d.k + 1, d.B, summary_width(d.k));
+        launch_pdl(fill_stats_kernel, (d.B + 127) / 128, 128, 0, st, summary + 2 * d.k + 1, d.B, summary_width(d.k));
         DWA_LAUNCH_CHECK("fill_stats_kernel");
         ++g_launches_total;
     } else if (want_sf) {
         DWA_TIMED("softmax_stats", st,
-                  softmax_stats_kernel<<<d.B, 256, 0, st>>>(w.partial, sf_blocks, w.stats, 2));
+                  launch_pdl(softmax_stats_kernel, d.B, 256, 0, st, w.partial, sf_blocks, w.stats, 2));
         DWA_LAUNCH_CHECK("softmax_stats_kernel");
         dim3 ga(static_cast<unsigned>((d.N + 2047) / 2048), d.B);
         DWA_TIMED("softmax_apply", st,
-                  softmax_apply_kernel<<<ga, 256, 0, st>>>(soft_full, d.N, 1.f / d.T, w.stats));
+                  launch_pdl(softmax_apply_kernel, ga, 256, 0, st, soft_full, d.N, 1.f / d.T, w.stats));
         DWA_LAUNCH_CHECK("softmax_apply_kernel");
         g_launches_total += 2;
     }
@@ -1159,7 +1172,7 @@ extern "C" int dwa_retrieve_local(void* stream, const DwaRetrieveDims* dims, con
         // a rank that holds no rows contributes an empty summary
         if (!summary || dims->B <= 0 || dims->k <= 0 || dims->k > kMaxK)
             return fail(DWA_ERR_INVALID_ARG, "summary, B and k (<= 256) are required");
-        empty_summary_kernel<<<dims->B, 128, 0, static_cast<cudaStream_t>(stream)>>>(summary, dims->k);
+        launch_pdl(empty_summary_kernel, dims->B, 128, 0, static_cast<cudaStream_t>(stream), summary, dims->k);
         DWA_LAUNCH_CHECK("empty_summary_kernel");
         ++g_launches_total;
         return DWA_OK;
@@ -1202,12 +1215,12 @@ extern "C" int dwa_retrieve_merge(void* stream, const DwaRetrieveDims* dims, int
     float* stats = reinterpret_cast<float*>(static_cast<char*>(workspace) + 256);
     ma.stats = soft_full ? stats : nullptr;
     const size_t msh = static_cast<size_t>(world) * d.k * sizeof(uint64_t);
-    DWA_TIMED("merge", st, merge_kernel<<<d.B, 1024, msh, st>>>(ma));
+    DWA_TIMED("merge", st, launch_pdl(merge_kernel, d.B, 1024, msh, st, ma));
     DWA_LAUNCH_CHECK("merge_kernel");
     ++g_launches_total;
     if (soft_full && d.N > 0) {
         dim3 ga(static_cast<unsigned>((d.N + 2047) / 2048), d.B);
-        DWA_TIMED("softmax_apply", st, softmax_apply_kernel<<<ga, 256, 0, st>>>(soft_full, d.N, 1.f / d.T, stats));
+        DWA_TIMED("softmax_apply", st, launch_pdl(softmax_apply_kernel, ga, 256, 0, st, soft_full, d.N, 1.f / d.T, stats));
         DWA_LAUNCH_CHECK("softmax_apply_kernel");
         ++g_launches_total;
     }
@@ -1224,18 +1237,18 @@ extern "C" int dwa_sequence_mean(void* stream, int B, int T, int d, int dtype, c
     if (d % 8 == 0 && reinterpret_cast<uintptr_t>(h_A) % 16 == 0) {
         dim3 g((d + 255) / 256, B);
         if (dtype == DWA_BF16)
-            DWA_TIMED("seq_mean", st, column_sum8_kernel<__nv_bfloat16><<<g, 512, 0, st>>>(
+            DWA_TIMED("seq_mean", st, launch_pdl(column_sum8_kernel<__nv_bfloat16>, g, 512, 0, st, 
                                           static_cast<const __nv_bfloat16*>(h_A), T, d, 1, z));
         else
-            DWA_TIMED("seq_mean", st, column_sum8_kernel<float><<<g, 512, 0, st>>>(
+            DWA_TIMED("seq_mean", st, launch_pdl(column_sum8_kernel<float>, g, 512, 0, st, 
                                           static_cast<const float*>(h_A), T, d, 1, z));
     } else {
         dim3 g((d + 63) / 64, B);
         if (dtype == DWA_BF16)
-            DWA_TIMED("seq_mean", st, column_sum_kernel<__nv_bfloat16><<<g, 1024, 0, st>>>(
+            DWA_TIMED("seq_mean", st, launch_pdl(column_sum_kernel<__nv_bfloat16>, g, 1024, 0, st, 
                                           static_cast<const __nv_bfloat16*>(h_A), T, d, 1, z));
         else
-            DWA_TIMED("seq_mean", st, column_sum_kernel<float><<<g, 1024, 0, st>>>(
+            DWA_TIMED("seq_mean", st, launch_pdl(column_sum_kernel<float>, g, 1024, 0, st, 
                                           static_cast<const float*>(h_A), T, d, 1, z));
     }
     (void)es;

@@ -88,6 +88,7 @@ __global__ void __launch_bounds__(THREADS, 1) key_scan_kernel(const __grid_const
         tc::fence_barrier_init();
     }
     __syncthreads();
+    pdl_enter();   // the queries come from the previous kernel
 
     int64_t row_lo, row_hi;
     const int ntile = kt::tile_count<ROWS, BOX>(a, blockIdx.x, gridDim.x, row_lo, row_hi);

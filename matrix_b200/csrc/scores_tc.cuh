@@ -125,6 +125,7 @@ __global__ void __launch_bounds__(THREADS, 1) key_scan_tc_kernel(const __grid_co
     __shared__ float red_m[WORKER_WARPS][32], red_z[WORKER_WARPS][32];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_enter();   // the queries come from the previous kernel
     // role: warps 0-1 producers, 2-3 MMA issuers, 4-7 / 8-11 workers of group 0 / 1
     const int g = warp < 4 ? (warp & 1) : ((warp - 4) >> 2);
     uint8_t* ring = rings + static_cast<size_t>(g * stages) * SLOT;

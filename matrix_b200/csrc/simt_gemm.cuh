@@ -31,6 +31,7 @@ __device__ __forceinline__ float ld_op(const Operand& op, int b, int mn, int k) 
 template <class TA, class TB, class Epi>
 __global__ void __launch_bounds__(256)
     gemm_kernel(Operand A, Operand B, int M, int N, int K, Epi epi) {
+    pdl_enter();
     __shared__ float As[TK][TM + 4];
     __shared__ float Bs[TK][TN + 4];
     __shared__ float s_red[8];
@@ -101,7 +102,7 @@ template <class TA, class TB, class Epi>
 int launch_gemm(const Operand& A, const Operand& B, int M, int N, int K, int batch, const Epi& epi,
                 cudaStream_t stream) {
     dim3 grid((N + TN - 1) / TN, (M + TM - 1) / TM, batch);
-    gemm_kernel<TA, TB, Epi><<<grid, 256, 0, stream>>>(A, B, M, N, K, epi);
+    launch_pdl(gemm_kernel<TA, TB, Epi>, grid, 256, 0, stream, A, B, M, N, K, epi);
     DWA_LAUNCH_CHECK("simt::gemm_kernel");
     return DWA_OK;
 }

@@ -248,6 +248,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_enter();   // operands and epilogue inputs come from earlier kernels
 
     if (warp == 0) {
         if (lane == 0) {
@@ -422,7 +423,7 @@ int launch_gemm_bf16(const Operand& A, const Operand& B, int M, int N, int K, in
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
     dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, batch);
-    kern<<<grid, kGemmThreads, L::BYTES, stream>>>(ta, tb, M, N, K, A.bstride != 0, B.bstride != 0,
+    launch_pdl(kern, grid, kGemmThreads, L::BYTES, stream, ta, tb, M, N, K, A.bstride != 0, B.bstride != 0,
                                                    epi, status);
     DWA_LAUNCH_CHECK("gemm_bf16_kernel");
     return DWA_OK;
