@@ -534,27 +534,56 @@ def main():
         h2d = hA_h.nbytes + g_h.nbytes + gW_h.nbytes
         d2h = sum(v.nbytes for v in pinned.values())
         n_e2e = min(args.steps, 50)
-        ea = [torch.cuda.Event(enable_timing=True) for _ in range(n_e2e)]
-        eb = [torch.cuda.Event(enable_timing=True) for _ in range(n_e2e)]
+        # A training loop's input pipeline: step i+1's inputs go up on a copy
+        # stream while step i computes and step i-1's results come down on
+        # another; device inputs and pinned host outputs are double-buffered.
+        # Every step's H2D and D2H is inside the timed region; L2 is not flushed
+        # (the pool and key cache are larger than L2).
+        s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+        main = torch.cuda.current_stream()
+        bufs = [(hA_d, g_d, gW_d), (torch.empty_like(hA_d), torch.empty_like(g_d), torch.empty_like(gW_d))]
+        pins = [pinned, {k: torch.empty_like(v).pin_memory() for k, v in pinned.items()}]
+        ev_in = [torch.cuda.Event() for _ in range(n_e2e)]
+        ev_used = [torch.cuda.Event() for _ in range(n_e2e)]
+        ev_out = [torch.cuda.Event() for _ in range(n_e2e)]
+        t_start, t_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
+        ring = [None, None]     # step outputs alive until their copy to the host is done
+        t_start.record(main)
+        s_in.wait_event(t_start)
         for i in range(n_e2e):
-            flush()
-            ea[i].record()
-            hA_d.copy_(hA_h, non_blocking=True)
-            g_d.copy_(g_h, non_blocking=True)
-            gW_d.copy_(gW_h, non_blocking=True)
-            out = step(hA_d, g_d, gW_d)
-            for k in res_keys:
-                pinned[k].copy_(out[k], non_blocking=True)
-            eb[i].record()
-            eb[i].synchronize()
-        e_ms = torch.tensor([sum(a.elapsed_time(b) for a, b in zip(ea, eb)) / n_e2e],
-                            device=dev, dtype=torch.float64)
+            bh, bg, bw = bufs[i % 2]
+            with torch.cuda.stream(s_in):
+                if i >= 2:
+                    s_in.wait_event(ev_used[i - 2])      # step i-2 has read this buffer
+                bh.copy_(hA_h, non_blocking=True)
+                bg.copy_(g_h, non_blocking=True)
+                bw.copy_(gW_h, non_blocking=True)
+                ev_in[i].record(s_in)
+            main.wait_event(ev_in[i])
+            if i >= 2:
+                # step i-2's outputs reached the host: release them in stream order
+                main.wait_event(ev_out[i - 2])
+                ring[i % 2] = None
+            out = step(bh, bg, bw)
+            ev_used[i].record(main)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_used[i])
+                for k in res_keys:
+                    pins[i % 2][k].copy_(out[k], non_blocking=True)
+                ev_out[i].record(s_out)
+            ring[i % 2] = out
+        main.wait_event(ev_out[n_e2e - 1])
+        t_stop.record(main)
+        t_stop.synchronize()
+        e_ms = torch.tensor([t_start.elapsed_time(t_stop) / n_e2e], device=dev, dtype=torch.float64)
         if group is not None:
             dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
         e2e = {"value": tokens * world / (float(e_ms.item()) / 1e3), "unit": "tokens/s",
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-               "ms_per_step": float(e_ms.item())}
+               "ms_per_step": float(e_ms.item()), "steps": n_e2e,
+               "mode": "copies overlapped with compute on two copy streams, double-buffered; "
+                       "no L2 flush (inputs larger than L2)"}
 
     # ---- roofline of the dominant kernel ----
     peaks, peak_src = load_peaks()

@@ -24,6 +24,7 @@
 //             g_b = alpha g_bias, pad columns zero, g_b_base, g_gamma.
 #include <atomic>
 #include <cstdlib>
+#include <cstring>
 #include <type_traits>
 
 #include "dwa_common.cuh"
@@ -397,12 +398,36 @@ static bool force_simt() {
     return v;
 }
 
+// GEMMs (by name) that run two 128-column CTAs per SM (DWA_GEMM_PAIR: "all" or a
+// comma-separated list of names).
+static bool pair_config(const char* name) {
+    const char* v = std::getenv("DWA_GEMM_PAIR");
+    if (!v || !*v) return false;
+    if (std::strcmp(v, "all") == 0) return true;
+    const size_t n = std::strlen(name);
+    for (const char* p = v; *p;) {
+        const char* q = std::strchr(p, ',');
+        const size_t len = q ? static_cast<size_t>(q - p) : std::strlen(p);
+        if (len == n && std::strncmp(p, name, n) == 0) return true;
+        if (!q) break;
+        p = q + 1;
+    }
+    return false;
+}
+
 template <class ACT, bool A_MN, bool B_MN, class Epi>
 static int gemm(const char* name, const void* a, int64_t lda, int64_t bsa, const void* b, int64_t ldb, int64_t bsb,
                 int M, int N, int K, int batch, const Epi& epi, uint32_t* status, cudaStream_t st) {
     if constexpr (std::is_same<ACT, __nv_bfloat16>::value) {
       if (!force_simt()) {
         const tc::Operand A{a, A_MN, lda, bsa}, B{b, B_MN, ldb, bsb};
+        if (pair_config(name) && N >= 128 && tc::tc_operand_ok(A, M, K, 128) && tc::tc_operand_ok(B, N, K, 128)) {
+            ++g_launches_tc;
+            prof_begin(name, st);
+            const int rc = tc::launch_gemm_bf16<128, 3, A_MN, B_MN, Epi, 8>(A, B, M, N, K, batch, epi, status, st);
+            prof_end(name, st);
+            return rc;
+        }
         const int64_t ctas256 = static_cast<int64_t>((M + 127) / 128) * ((N + 255) / 256) * batch;
         if (N >= 256 && ctas256 >= 120 && tc::tc_operand_ok(A, M, K, 128) &&
             tc::tc_operand_ok(B, N, K, 256)) {

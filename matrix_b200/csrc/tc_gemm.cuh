@@ -206,11 +206,14 @@ struct SmemLayout {
 //   static constexpr int kReduce;   0 none, 1 per row, 2 per CTA
 //   void row_done(int b, int row, float acc) const   (kReduce == 1)
 //   void cta_done(int b, float acc) const            (kReduce == 2)
-constexpr int kEpiWarps = 16;                       // epilogue warps (2..17)
-constexpr int kGemmThreads = 64 + 32 * kEpiWarps;   // + TMA warp + MMA warp
+// EW epilogue warps (16: one CTA per SM; 8: with BN = 128 and 3 stages two CTAs
+// fit on an SM, so one CTA's epilogue overlaps the other's mainloop).
+constexpr int kEpiWarps = 16;
+template <int EW> constexpr int gemm_threads() { return 64 + 32 * EW; }   // + TMA warp + MMA warp
+constexpr int kGemmThreads = gemm_threads<kEpiWarps>();
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EW = kEpiWarps>
+__global__ void __launch_bounds__(gemm_threads<EW>(), EW == 8 ? 2 : 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      int M, int N, int K, int a_batched, int b_batched, Epi epi, uint32_t* status) {
     using L = SmemLayout<BN, STAGES>;
@@ -224,7 +227,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t* empty_bar = full_bar + STAGES;
     uint64_t* done_bar = empty_bar + STAGES;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
-    __shared__ float s_red[kEpiWarps];
+    __shared__ float s_red[EW];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, bz = blockIdx.z;
@@ -311,13 +314,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         __syncwarp();
     } else {
         // Epilogue.  Phase 1: TMEM -> shared tile (fp32, row stride BN+4 floats),
-        // thread = row; warp w may only read TMEM lanes 32*(w%4).., so the 16
-        // warps form 4 column groups of one warp per lane quarter.  The stage
+        // thread = row; warp w may only read TMEM lanes 32*(w%4).., so the EW
+        // warps form EW/4 column groups of one warp per lane quarter.  The stage
         // buffers are free: every TMA load was consumed by an MMA and done_bar
         // fires after the last MMA completes.
         const int q = warp & 3;
-        const int e = warp - 2;        // epilogue warp 0..15
-        const int grp = e >> 2;        // column group 0..3
+        const int e = warp - 2;        // epilogue warp 0..EW-1
+        const int grp = e >> 2;        // column group 0..EW/4-1
         const bool ok = mbar_wait_bounded(done_bar, 0);
         if (!ok && lane == 0) raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
         tc_fence_after();
@@ -325,7 +328,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         float* tile = reinterpret_cast<float*>(smem);
         if (ok) {
             const int r_local = q * 32 + lane;
-            for (int c = grp; c < BN / 32; c += 4) {
+            for (int c = grp; c < BN / 32; c += EW / 4) {
                 if (n0 + c * 32 >= N) break;
                 float v[32];
                 tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c * 32, v);
@@ -336,11 +339,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
         }
         tc_fence_before();
-        asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory");
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * EW) : "memory");
         // Phase 2: coalesced.  LPR lanes cover one row (8 columns each); each
         // warp first loads the epilogue operands of PF rows, then finishes them.
         constexpr int LPR = BN / 8, RPW = 32 / LPR, PF = 4;
-        constexpr int STEP = kEpiWarps * RPW;
+        constexpr int STEP = EW * RPW;
         const int sub = lane / LPR, li = lane % LPR;
         const int col0 = n0 + li * 8;
         const int cnt = min(8, N - col0);
@@ -381,7 +384,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncthreads();
     if (Epi::kReduce == 2 && threadIdx.x == 0) {
         float t = 0.f;
-        for (int i = 0; i < kEpiWarps; ++i) t += s_red[i];
+        for (int i = 0; i < EW; ++i) t += s_red[i];
         epi.cta_done(bz, t);
     }
     if (warp == 1) {
@@ -402,7 +405,7 @@ bool make_operand_map(CUtensorMap* tm, const Operand& op, int64_t mn_extent, int
 // strides) and covers at least one full box in each dimension.
 bool tc_operand_ok(const Operand& op, int64_t mn_extent, int64_t k_extent, int box_mn);
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
+template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EW = kEpiWarps>
 int launch_gemm_bf16(const Operand& A, const Operand& B, int M, int N, int K, int batch,
                      const Epi& epi, uint32_t* status, cudaStream_t stream) {
     static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64, 128, 192 or 256");
@@ -413,7 +416,7 @@ int launch_gemm_bf16(const Operand& A, const Operand& B, int M, int N, int K, in
         !make_operand_map(&tb, B, N, K, batch, BN, &why))
         return fail(DWA_ERR_INVALID_ARG, "tensor map: " + why);
     using L = SmemLayout<BN, STAGES>;
-    auto kern = gemm_bf16_kernel<BN, STAGES, A_MN, B_MN, Epi>;
+    auto kern = gemm_bf16_kernel<BN, STAGES, A_MN, B_MN, Epi, EW>;
     static bool attr_set[64] = {};  // per instantiation and device
     int dev = 0;
     DWA_CUDA_TRY(cudaGetDevice(&dev));
@@ -423,7 +426,7 @@ int launch_gemm_bf16(const Operand& A, const Operand& B, int M, int N, int K, in
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
     dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, batch);
-    launch_pdl(kern, grid, kGemmThreads, L::BYTES, stream, ta, tb, M, N, K, A.bstride != 0, B.bstride != 0,
+    launch_pdl(kern, grid, gemm_threads<EW>(), L::BYTES, stream, ta, tb, M, N, K, A.bstride != 0, B.bstride != 0,
                                                    epi, status);
     DWA_LAUNCH_CHECK("gemm_bf16_kernel");
     return DWA_OK;
