@@ -194,9 +194,11 @@ KERNELS = ["seq_mean", "query", "query_norm", "coarse", "topm", "full_scores", "
 
 
 def profile_kernels(step, flush, n=5):
-    """Average duration (ms) of every library kernel of one step, from replays
-    of a CUDA graph of the step in which the library records an event pair
-    around each kernel (no host launch gaps inside the measurement)."""
+    """Average duration (ms) of every library kernel of one step, and its start
+    relative to the step's first kernel (the sequence mean), from replays of a
+    CUDA graph of the step in which the library records an event pair around
+    each kernel (no host launch gaps inside the measurement).  A kernel the
+    step does not launch keeps its setup record, which precedes the replay."""
     import torch
     from matrix_b200 import _lib
     lib = _lib.load()
@@ -216,19 +218,21 @@ def profile_kernels(step, flush, n=5):
     with torch.cuda.graph(g):
         step()
     lib.dwa_profile_clear()
-    # kernels that are not part of the step keep their first (back-to-back) record
-    stale = {k for k, (a, b) in ev.items() if a.elapsed_time(b) < 1e-4}
+    first = ev[KERNELS[0]][0]
     acc = {k: [] for k in KERNELS}
+    start = {k: [] for k in KERNELS}
     for _ in range(n):
         flush()
         g.replay()
         torch.cuda.synchronize()
         for k, (a, b) in ev.items():
-            ms = a.elapsed_time(b)
-            if ms > 1e-4 or k not in stale:
-                acc[k].append(ms)
+            t0 = first.elapsed_time(a)
+            if t0 >= 0.0:
+                acc[k].append(a.elapsed_time(b))
+                start[k].append(t0)
     del g
-    return {k: float(np.mean(v)) for k, v in acc.items() if v and np.mean(v) > 1e-4}
+    dur = {k: float(np.mean(v)) for k, v in acc.items() if v}
+    return dur, {k: float(np.mean(start[k])) for k in dur}
 
 
 def time_key_cache(t, flush, peaks, reps=3):
@@ -448,7 +452,7 @@ def main():
     torch.cuda.synchronize()
     launches_per_step = _lib.launch_counters()[0] - c0
 
-    breakdown = profile_kernels(step, flush)
+    breakdown, kstarts = profile_kernels(step, flush)
     dominant = max(breakdown, key=breakdown.get)
 
     # capture the step in a CUDA graph, with the dominant kernel's events inside
@@ -616,7 +620,7 @@ def main():
                        "step": "CUDA graph: seq_mean + dwa_retrieve + dwa_assemble_fwd + dwa_assemble_bwd"
                                + (" + NCCL all_reduce of parameter grads" if world > 1 else "")},
             "value_per_gpu": value / world, "roofline": roof,
-            "kernels_ms": breakdown, "gpu_launches": int(launches_per_step * args.steps),
+            "kernels_ms": breakdown, "kernels_start_ms": kstarts, "gpu_launches": int(launches_per_step * args.steps),
             "clocks": clocks, "e2e": e2e}
     if world == 1 and not args.no_key_cache:
         line["key_cache"] = time_key_cache(t, flush, peaks)

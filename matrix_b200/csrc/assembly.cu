@@ -616,8 +616,7 @@ static int bwd_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src
     ++g_launches_total;
 
     if (d.d_B % 8 == 0 && reinterpret_cast<uintptr_t>(g) % 16 == 0) {
-        dim3 gc((d.d_B + 255) / 256, d.B);
-        DWA_TIMED("colsum", a1, launch_pdl(column_sum8_kernel<ACT>, gc, 512, 0, a1, g, d.T, d.d_B, 0, w.gbias));
+        DWA_TIMED("colsum", a1, launch_column_sum8<ACT>(a1, g, d.B, d.T, d.d_B, 0, w.gbias));
     } else {
         dim3 gc((d.d_B + 63) / 64, d.B);
         DWA_TIMED("colsum", a1, launch_pdl(column_sum_kernel<ACT>, gc, 1024, 0, a1, g, d.T, d.d_B, 0, w.gbias));

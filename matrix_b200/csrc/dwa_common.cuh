@@ -2,6 +2,7 @@
 // waits, last-error plumbing.
 #pragma once
 
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -48,6 +49,13 @@ __device__ __forceinline__ void pdl_enter() {
 
 bool pdl_enabled();
 
+// Split cluster barrier: arrive early, wait just before the first access to
+// another CTA's shared memory (every CTA of the cluster has then started).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+
 template <class... KArgs, class... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                               Args&&... args) {
@@ -61,6 +69,28 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
     attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// launch_pdl for a kernel run as thread-block clusters of `cluster` CTAs
+// (each grid dimension a multiple of the cluster's).
+template <class... KArgs, class... Args>
+inline cudaError_t launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                      cudaStream_t st, dim3 cluster, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster.x;
+    attr[1].val.clusterDim.y = cluster.y;
+    attr[1].val.clusterDim.z = cluster.z;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
@@ -202,26 +232,33 @@ __global__ void __launch_bounds__(1024) column_sum_kernel(const T* __restrict__ 
 }
 
 // Same sums with 8 consecutive columns per lane (16-byte loads for bf16, two
-// for fp32): grid (ceil(d/256), B), 512 threads; warp w takes rows w, w+16, ...
-// (16 loads in flight per lane); partials added in warp order.  d % 8 == 0 and
-// a 16-byte aligned x required.
+// for fp32): grid (ceil(d/256), B, split) launched as clusters of (1, 1, split)
+// CTAs, 512 threads.  CTA z of a cluster sums the rows
+// [T*z/split, T*(z+1)/split) (warp w takes rows w, w+16, ..., 4 loads in flight
+// per lane), adds its 16 warp partials in warp order, and cluster rank 0 adds
+// the split CTAs' sums in rank order out of their shared memory: deterministic
+// for a given split.  d % 8 == 0 and a 16-byte aligned x required.
 template <class T>
-__global__ void __launch_bounds__(512) column_sum8_kernel(const T* __restrict__ x, int T_, int d,
+__global__ void __launch_bounds__(512, 2) column_sum8_kernel(const T* __restrict__ x, int T_, int d,
                                                           int mean, float* __restrict__ out) {
     pdl_enter();
     __shared__ float part[16][257];
+    __shared__ float tot[256];
     const int b = blockIdx.y, lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int split = gridDim.z, z = blockIdx.z;
+    const int t_lo = static_cast<int>(static_cast<int64_t>(T_) * z / split);
+    const int t_hi = static_cast<int>(static_cast<int64_t>(T_) * (z + 1) / split);
     const int c = blockIdx.x * 256 + 8 * lane;
     const T* p = x + static_cast<int64_t>(b) * T_ * d;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (c < d) {
-        for (int t0 = w; t0 < T_; t0 += 16 * 16) {
-            float v[16][8];
+        for (int t0 = t_lo + w; t0 < t_hi; t0 += 16 * 4) {
+            float v[4][8];
 #pragma unroll
-            for (int u = 0; u < 16; ++u) {
+            for (int u = 0; u < 4; ++u) {
                 const int t = t0 + 16 * u;
                 const T* q = p + static_cast<int64_t>(t) * d + c;
-                if (t < T_) {
+                if (t < t_hi) {
                     if constexpr (sizeof(T) == 2) {
                         const uint4 r = *reinterpret_cast<const uint4*>(q);
                         const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r);
@@ -243,7 +280,7 @@ __global__ void __launch_bounds__(512) column_sum8_kernel(const T* __restrict__ 
                 }
             }
 #pragma unroll
-            for (int u = 0; u < 16; ++u)
+            for (int u = 0; u < 4; ++u)
 #pragma unroll
                 for (int j = 0; j < 8; ++j) acc[j] += v[u][j];
         }
@@ -252,12 +289,35 @@ __global__ void __launch_bounds__(512) column_sum8_kernel(const T* __restrict__ 
     for (int j = 0; j < 8; ++j) part[w][8 * lane + j] = acc[j];
     __syncthreads();
     if (threadIdx.x < 256) {
-        const int col = blockIdx.x * 256 + threadIdx.x;
         float s = 0.f;
 #pragma unroll
         for (int i = 0; i < 16; ++i) s += part[i][threadIdx.x];
-        if (col < d) out[static_cast<int64_t>(b) * d + col] = mean ? s / static_cast<float>(T_) : s;
+        tot[threadIdx.x] = s;
     }
+    if (split > 1) {
+        cooperative_groups::cluster_group cl = cooperative_groups::this_cluster();
+        cl.sync();
+        if (cl.block_rank() == 0 && threadIdx.x < 256) {
+            float s = 0.f;
+            for (int r = 0; r < split; ++r) s += cl.map_shared_rank(tot, r)[threadIdx.x];
+            const int col = blockIdx.x * 256 + threadIdx.x;
+            if (col < d) out[static_cast<int64_t>(b) * d + col] = mean ? s / static_cast<float>(T_) : s;
+        }
+        cl.sync();   // every CTA's sums stay in place until rank 0 has read them
+    } else if (threadIdx.x < 256) {
+        const int col = blockIdx.x * 256 + threadIdx.x;
+        if (col < d) out[static_cast<int64_t>(b) * d + col] = mean ? tot[threadIdx.x] / static_cast<float>(T_) : tot[threadIdx.x];
+    }
+}
+
+// Launch of column_sum8_kernel over x [B, T, d]: about 64 rows per CTA, at most
+// 8 CTAs (one cluster) per (column block, b).
+template <class T>
+inline cudaError_t launch_column_sum8(cudaStream_t st, const T* x, int B, int T_, int d, int mean, float* out) {
+    int split = (T_ + 63) / 64;
+    split = split < 1 ? 1 : split > 8 ? 8 : split;
+    return launch_pdl_cluster(column_sum8_kernel<T>, dim3((d + 255) / 256, B, split), dim3(512), 0, st,
+                              dim3(1, 1, split), x, T_, d, mean, out);
 }
 
 }  // namespace dwa

@@ -138,184 +138,228 @@ __device__ __forceinline__ float block_reduce(float v, bool is_max, float* sh) {
 }
 
 // Selects the min(k, n) largest keys of key_at(0..n) into sel_key/sel_pos,
-// sorted descending.  MSB-first radix select (8 bits per pass) on the 64-bit
-// keys, stopping as soon as the boundary bucket is taken whole, then a
-// bitonic sort of the winners.  Keys must be distinct.
+// sorted descending; keys must be distinct.  A few block-wide steps, each
+// short, since the cost here is the length of the dependent chain:
+//   1. the bits every key shares (block OR / AND) are known, so the radix
+//      passes start at the highest bit on which keys differ;
+//   2. MSB-first radix passes of 8 bits histogram the keys that still match
+//      the prefix (shared-memory atomics); warp 0 finds the bucket holding the
+//      k-th key.  The passes stop as soon as at most cap = max(64, kk) keys lie
+//      at or above that bucket (usually after one pass);
+//   3. those keys are gathered and each one's rank among them (the number of
+//      larger keys) puts the top kk in order.
+// With n <= cap the passes are skipped.
 template <class KeyAt>
 __device__ int block_topk(int64_t n, int k, const KeyAt& key_at, uint64_t* sel_key,
                           int64_t* sel_pos) {
-    __shared__ unsigned hist[256];
-    __shared__ uint64_t s_prefix;
-    __shared__ int s_kleft, s_done, s_count;
-    const int tid = threadIdx.x, nt = blockDim.x;
+    __shared__ unsigned hist[2][256];
+    __shared__ uint64_t s_or[32], s_and[32];
+    __shared__ uint64_t s_prefix[2];
+    __shared__ int s_kleft[2], s_stop[2], s_count;
+    __shared__ uint64_t t_key[kMaxK];
+    __shared__ int64_t t_pos[kMaxK];
+    const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
     const int kk = static_cast<int>(n < k ? n : k);
     if (kk <= 0) return 0;
+    const int cap = kk > 64 ? kk : 64;
     uint64_t prefix = 0, mask = 0;
-    int kleft = kk;
-    for (int pass = 0; pass < 8; ++pass) {
-        const int shift = 56 - 8 * pass;
-        for (int i = tid; i < 256; i += nt) hist[i] = 0;
-        __syncthreads();
+    if (n > cap) {
+        // 1. common bits
+        uint64_t o = 0, a = ~0ull;
         for (int64_t i = tid; i < n; i += nt) {
             const uint64_t key = key_at(i);
-            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 0xFF], 1u);
+            o |= key;
+            a &= key;
         }
+        const uint32_t o_lo = __reduce_or_sync(0xffffffffu, static_cast<uint32_t>(o));
+        const uint32_t o_hi = __reduce_or_sync(0xffffffffu, static_cast<uint32_t>(o >> 32));
+        const uint32_t a_lo = __reduce_and_sync(0xffffffffu, static_cast<uint32_t>(a));
+        const uint32_t a_hi = __reduce_and_sync(0xffffffffu, static_cast<uint32_t>(a >> 32));
+        if (lane == 0) {
+            s_or[warp] = (static_cast<uint64_t>(o_hi) << 32) | o_lo;
+            s_and[warp] = (static_cast<uint64_t>(a_hi) << 32) | a_lo;
+        }
+        for (int i = tid; i < 512; i += nt) (&hist[0][0])[i] = 0;
         __syncthreads();
-        if (tid < 32) {
-            // warp 0 scans the 256 buckets from the top: 8 buckets per lane
-            unsigned c8[8], tot = 0;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) { c8[i] = hist[255 - (tid * 8 + i)]; tot += c8[i]; }
-            unsigned incl = tot;  // inclusive prefix over lanes (lane 0 = highest buckets)
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
-                if (tid >= o) incl += v;
+        o = 0;
+        a = ~0ull;
+        for (int w = 0; w < (nt >> 5); ++w) {
+            o |= s_or[w];
+            a &= s_and[w];
+        }
+        // distinct keys differ somewhere (o != a); equal keys leave nothing to resolve
+        int hi = o == a ? -1 : 63 - __clzll(static_cast<long long>(o ^ a));
+        mask = hi < 0 ? ~0ull : hi == 63 ? 0ull : ~((2ull << hi) - 1);
+        prefix = a & mask;
+        int kleft = kk;
+        // 2. radix passes over bits [lo, hi]; keys above the prefix: kk - kleft
+        for (int pass = 0; hi >= 0; ++pass) {
+            const int buf = pass & 1;
+            const int lo = hi >= 7 ? hi - 7 : 0;
+            const unsigned dmask = (1u << (hi - lo + 1)) - 1;
+            for (int64_t i = tid; i < n; i += nt) {
+                const uint64_t key = key_at(i);
+                if ((key & mask) == prefix) atomicAdd(&hist[buf][static_cast<unsigned>(key >> lo) & dmask], 1u);
             }
-            const unsigned before = incl - tot;
-            const bool mine = before < static_cast<unsigned>(kleft) &&
-                              incl >= static_cast<unsigned>(kleft);
-            if (mine) {
-                unsigned acc = before;
-                for (int i = 0; i < 8; ++i) {
-                    if (acc + c8[i] >= static_cast<unsigned>(kleft)) {
-                        const int dsel = 255 - (tid * 8 + i);
-                        s_kleft = kleft - static_cast<int>(acc);
-                        s_done = (c8[i] == static_cast<unsigned>(kleft) - acc);
-                        s_prefix = prefix | (static_cast<uint64_t>(dsel) << shift);
-                        break;
+            __syncthreads();
+            for (int i = tid; i < 256; i += nt) hist[buf ^ 1][i] = 0;
+            if (tid < 32) {
+                // warp 0 scans the 256 buckets from the top: 8 buckets per lane
+                unsigned c8[8], tot = 0;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) { c8[i] = hist[buf][255 - (tid * 8 + i)]; tot += c8[i]; }
+                unsigned incl = tot;  // inclusive prefix over lanes (lane 0 = highest buckets)
+#pragma unroll
+                for (int o2 = 1; o2 < 32; o2 <<= 1) {
+                    const unsigned v = __shfl_up_sync(0xffffffffu, incl, o2);
+                    if (tid >= o2) incl += v;
+                }
+                const unsigned before = incl - tot;
+                const bool mine = before < static_cast<unsigned>(kleft) && incl >= static_cast<unsigned>(kleft);
+                if (mine) {
+                    unsigned acc = before;
+                    for (int i = 0; i < 8; ++i) {
+                        if (acc + c8[i] >= static_cast<unsigned>(kleft)) {
+                            const int dsel = 255 - (tid * 8 + i);
+                            // keys at or above the boundary bucket: (kk - kleft) + acc + c8[i]
+                            s_kleft[buf] = kleft - static_cast<int>(acc);
+                            s_stop[buf] = (kk - kleft) + static_cast<int>(acc + c8[i]) <= cap;
+                            s_prefix[buf] = prefix | (static_cast<uint64_t>(dsel) << lo);
+                            break;
+                        }
+                        acc += c8[i];
                     }
-                    acc += c8[i];
                 }
             }
+            __syncthreads();
+            prefix = s_prefix[buf];
+            mask |= static_cast<uint64_t>(dmask) << lo;
+            kleft = s_kleft[buf];
+            if (s_stop[buf]) break;
+            hi = lo - 1;
         }
-        __syncthreads();
-        prefix = s_prefix;
-        mask |= 0xFFull << shift;
-        kleft = s_kleft;
-        const int done = s_done;
-        __syncthreads();
-        if (done) break;
     }
+    // 3. gather the keys at or above the threshold (at most cap of them) ...
     if (tid == 0) s_count = 0;
     __syncthreads();
     for (int64_t i = tid; i < n; i += nt) {
         const uint64_t key = key_at(i);
         if ((key & mask) >= prefix) {
             const int slot = atomicAdd(&s_count, 1);
-            if (slot < kMaxK) { sel_key[slot] = key; sel_pos[slot] = i; }
+            if (slot < kMaxK) { t_key[slot] = key; t_pos[slot] = i; }
         }
     }
     __syncthreads();
-    int P = 1;
-    while (P < kk) P <<= 1;
-    for (int i = kk + tid; i < P; i += nt) { sel_key[i] = 0; sel_pos[i] = -1; }
-    __syncthreads();
-    for (int size = 2; size <= P; size <<= 1) {
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            for (int i = tid; i < P; i += nt) {
-                const int j = i ^ stride;
-                if (j > i) {
-                    const bool desc = (i & size) == 0;
-                    const uint64_t a = sel_key[i], c = sel_key[j];
-                    if ((a < c) == desc) {
-                        sel_key[i] = c; sel_key[j] = a;
-                        const int64_t t = sel_pos[i]; sel_pos[i] = sel_pos[j]; sel_pos[j] = t;
-                    }
-                }
-            }
-            __syncthreads();
+    // ... and place each by its rank among them
+    const int cnt = s_count < kMaxK ? s_count : kMaxK;
+    for (int t = tid; t < cnt; t += nt) {
+        const uint64_t key = t_key[t];
+        int r0 = 0, r1 = 0, r2 = 0, r3 = 0;
+        int j = 0;
+        for (; j + 4 <= cnt; j += 4) {
+            r0 += t_key[j] > key;
+            r1 += t_key[j + 1] > key;
+            r2 += t_key[j + 2] > key;
+            r3 += t_key[j + 3] > key;
         }
+        for (; j < cnt; ++j) r0 += t_key[j] > key;
+        const int rank = r0 + r1 + r2 + r3;
+        if (rank < kk) { sel_key[rank] = key; sel_pos[rank] = t_pos[t]; }
     }
+    __syncthreads();
     return kk;
 }
 
 // --------------------------------------------------------------- kernels ---
 // Raw aspect queries q[b, o] = W_Q[o, :] . z[b, :] for o = s*d_k + kk
-// (retrieval.py:65).  One warp per row o of W_Q for all queries of a tile of
-// up to QB queries held in shared memory, so W_Q is read once per tile.
-constexpr int QB = 16;
+// (retrieval.py:65).  CTA (x, y) computes the kProjRows rows o of W_Q from
+// x * kProjRows for the kProjQ queries from y * kProjQ: thread t takes columns
+// t, t + 256, ... (kProjCols of them per batch of loads in flight), the 256
+// partial dot products of an output are added by warp shuffles, then over the
+// 8 warps in warp order.
+constexpr int kProjRows = 2, kProjQ = 8, kProjThreads = 256, kProjCols = 4;
 template <class ZT>
-__global__ void __launch_bounds__(256) query_proj_kernel(const ZT* __restrict__ z,
-                                                         const float* __restrict__ W_Q, int B,
-                                                         int rows, int d_A, int btile,
-                                                         float* __restrict__ q) {
+__global__ void __launch_bounds__(kProjThreads) query_proj_kernel(const ZT* __restrict__ z,
+                                                                  const float* __restrict__ W_Q, int B,
+                                                                  int rows, int d_A, float* __restrict__ q) {
     pdl_enter();
-    extern __shared__ float zs[];  // [btile][d_A]
+    constexpr int NO = kProjRows * kProjQ;
+    __shared__ float red[kProjThreads / 32][NO];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int o = blockIdx.x * (blockDim.x >> 5) + warp;
-    for (int b0 = 0; b0 < B; b0 += btile) {
-        const int nb = min(btile, B - b0);
-        __syncthreads();
-        {
-            const ZT* zb = z + static_cast<int64_t>(b0) * d_A;
-            const int n = nb * d_A;
-            for (int i0 = threadIdx.x; i0 < n; i0 += blockDim.x * 32) {
-                float t[32];
+    const int o0 = blockIdx.x * kProjRows, b0 = blockIdx.y * kProjQ;
+    const int nr = min(kProjRows, rows - o0), nb = min(kProjQ, B - b0);
+    float acc[kProjRows][kProjQ];
 #pragma unroll
-                for (int u = 0; u < 32; ++u) {
-                    const int i = i0 + u * blockDim.x;
-                    t[u] = i < n ? Elem<ZT>::to_f(zb[i]) : 0.f;
-                }
+    for (int r = 0; r < kProjRows; ++r)
 #pragma unroll
-                for (int u = 0; u < 32; ++u) {
-                    const int i = i0 + u * blockDim.x;
-                    if (i < n) zs[i] = t[u];
-                }
-            }
+        for (int j = 0; j < kProjQ; ++j) acc[r][j] = 0.f;
+    for (int c0 = threadIdx.x; c0 < d_A; c0 += kProjThreads * kProjCols) {
+        float wv[kProjCols][kProjRows], zv[kProjCols][kProjQ];
+#pragma unroll
+        for (int u = 0; u < kProjCols; ++u) {
+            const int c = c0 + u * kProjThreads;
+#pragma unroll
+            for (int r = 0; r < kProjRows; ++r)
+                wv[u][r] = (c < d_A && r < nr) ? __ldg(W_Q + static_cast<int64_t>(o0 + r) * d_A + c) : 0.f;
+#pragma unroll
+            for (int j = 0; j < kProjQ; ++j)
+                zv[u][j] = (c < d_A && j < nb) ? Elem<ZT>::to_f(z[static_cast<int64_t>(b0 + j) * d_A + c]) : 0.f;
         }
-        __syncthreads();
-        if (o < rows) {
-            const float* w = W_Q + static_cast<int64_t>(o) * d_A;
-            float acc[QB];
 #pragma unroll
-            for (int j = 0; j < QB; ++j) acc[j] = 0.f;
-            // up to 32 loads of the W_Q row in flight per batch, then the FMAs
-            for (int i0 = lane; i0 < d_A; i0 += 32 * 32) {
-                float wv[32];
+        for (int u = 0; u < kProjCols; ++u)
 #pragma unroll
-                for (int u = 0; u < 32; ++u) {
-                    const int i = i0 + 32 * u;
-                    wv[u] = i < d_A ? __ldg(w + i) : 0.f;
-                }
+            for (int r = 0; r < kProjRows; ++r)
 #pragma unroll
-                for (int u = 0; u < 32; ++u) {
-                    const int i = i0 + 32 * u;
-                    if (i < d_A) {
+                for (int j = 0; j < kProjQ; ++j) acc[r][j] = fmaf(wv[u][r], zv[u][j], acc[r][j]);
+    }
 #pragma unroll
-                        for (int j = 0; j < QB; ++j)
-                            if (j < nb) acc[j] = fmaf(wv[u], zs[j * d_A + i], acc[j]);
-                    }
-                }
-            }
+    for (int r = 0; r < kProjRows; ++r)
 #pragma unroll
-            for (int j = 0; j < QB; ++j) {
-                if (j < nb) {
-                    const float v = warp_sum(acc[j]);
-                    if (lane == 0) q[static_cast<int64_t>(b0 + j) * rows + o] = v;
-                }
-            }
+        for (int j = 0; j < kProjQ; ++j) {
+            const float v = warp_sum(acc[r][j]);
+            if (lane == 0) red[warp][r * kProjQ + j] = v;
         }
+    __syncthreads();
+    if (threadIdx.x < NO) {
+        const int r = threadIdx.x / kProjQ, j = threadIdx.x % kProjQ;
+        float v = 0.f;
+#pragma unroll
+        for (int i = 0; i < kProjThreads / 32; ++i) v += red[i][threadIdx.x];
+        if (r < nr && j < nb) q[static_cast<int64_t>(b0 + j) * rows + o0 + r] = v;
     }
 }
 
-// qw[b,s,:] = softmax(aspect_weights)_s * q[b,s,:] / (|q[b,s,:]| + 1e-8)   (:66, :69)
-__global__ void query_norm_kernel(float* __restrict__ qw, const float* __restrict__ aspect_w,
-                                  int S, int d_k) {
-    pdl_enter();
-    const int b = blockIdx.x, s = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (s >= S) return;
-    float* q = qw + (static_cast<int64_t>(b) * S + s) * d_k;
+// One aspect of one query, in place, by one warp:
+// q <- softmax(aspect_weights)_s * q / (|q| + 1e-8)   (retrieval.py:66, :69).
+// Shared by query_norm_kernel and the coarse top-m kernel, so both give the
+// same bits.
+__device__ __forceinline__ void normalize_aspect(float* q, const float* __restrict__ aspect_w, int S, int s,
+                                                 int d_k) {
+    const int lane = threadIdx.x & 31;
     float ss = 0.f;
     for (int d = lane; d < d_k; d += 32) ss = fmaf(q[d], q[d], ss);
     ss = warp_sum(ss);
     const float inv_den = 1.f / (sqrtf(ss) + 1e-8f);
+    // the S <= 16 weights: one load per lane, then the sequential max and sum
+    const float wl = lane < S ? aspect_w[lane] : 0.f;
     float mx = -INFINITY;
-    for (int t = 0; t < S; ++t) mx = fmaxf(mx, aspect_w[t]);
+    for (int t = 0; t < S; ++t) mx = fmaxf(mx, __shfl_sync(0xffffffffu, wl, t));
     float den = 0.f;
-    for (int t = 0; t < S; ++t) den += expf(aspect_w[t] - mx);
-    const float ws = expf(aspect_w[s] - mx) / den;
+    for (int t = 0; t < S; ++t) den += expf(__shfl_sync(0xffffffffu, wl, t) - mx);
+    const float ws = expf(__shfl_sync(0xffffffffu, wl, s) - mx) / den;
     for (int d = lane; d < d_k; d += 32) q[d] = (q[d] * inv_den) * ws;
+}
+
+// qw[b,s,:] from the raw q[b,s,:]: one warp per aspect.
+__global__ void query_norm_kernel(const float* __restrict__ q, const float* __restrict__ aspect_w, int S,
+                                  int d_k, float* __restrict__ qw) {
+    pdl_enter();
+    const int b = blockIdx.x, s = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (s >= S) return;
+    const int64_t off = (static_cast<int64_t>(b) * S + s) * d_k;
+    for (int d = lane; d < d_k; d += 32) qw[off + d] = q[off + d];
+    __syncwarp();
+    normalize_aspect(qw + off, aspect_w, S, s, d_k);
 }
 
 // One thread per (centroid, aspect): t = (qw[b,s] . c[s,c]) / (|c[s,c]| + 1e-8)
@@ -374,6 +418,39 @@ __global__ void __launch_bounds__(1024) coarse_kernel(const float* __restrict__ 
     }
 }
 
+// Candidate ranges of query b's m chosen lists (sel_pos[0..got), best first):
+// each list clipped to the key rows [row_lo, row_hi) this call holds and to
+// max_list rows, as local key rows, and the prefix sum of their sizes.
+__device__ void select_list_ranges(int got, int m, int b, const int64_t* sel_pos,
+                                   const int64_t* __restrict__ list_off, int64_t n_global, int64_t row_lo,
+                                   int64_t row_hi, int max_list, int32_t* __restrict__ top_clusters,
+                                   int64_t* __restrict__ probe_lo, int64_t* __restrict__ cand_base,
+                                   uint32_t* status, int64_t* s_sz) {
+    for (int j = threadIdx.x; j < m; j += blockDim.x) {
+        const int c = j < got ? static_cast<int>(sel_pos[j]) : 0;
+        int64_t lo = list_off[c], hi = list_off[c + 1];
+        if (lo < 0 || hi < lo || hi > n_global) { raise_status(status, DWA_STATUS_BAD_LIST); lo = hi = 0; }
+        if (hi - lo > max_list) raise_status(status, DWA_STATUS_LIST_OVERFLOW);
+        lo = lo > row_lo ? lo : row_lo;
+        hi = hi < row_hi ? hi : row_hi;
+        int64_t sz = hi > lo ? hi - lo : 0;
+        if (sz > max_list) sz = max_list;
+        top_clusters[static_cast<int64_t>(b) * m + j] = c;
+        probe_lo[static_cast<int64_t>(b) * (m + 1) + j] = sz > 0 ? lo - row_lo : 0;
+        s_sz[j] = sz;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int64_t acc = 0;
+        for (int j = 0; j < m; ++j) {
+            cand_base[static_cast<int64_t>(b) * (m + 1) + j] = acc;
+            acc += s_sz[j];
+        }
+        probe_lo[static_cast<int64_t>(b) * (m + 1) + m] = 0;
+        cand_base[static_cast<int64_t>(b) * (m + 1) + m] = acc;
+    }
+}
+
 constexpr int kStageKeys = 6144;  // candidates staged in shared memory (48 KB of keys)
 
 // Top-m lists per query (ties to the lower list) and each probed list's
@@ -400,31 +477,140 @@ __global__ void __launch_bounds__(512) topm_kernel(
         auto key_at = [&](int64_t i) { return make_key(cs[i], static_cast<uint32_t>(i)); };
         got = block_topk(C, m, key_at, sel_key, sel_pos);
     }
-    // list ranges of the m winners, one thread each, then a prefix sum over them
     __shared__ int64_t s_sz[kMaxK + 1];
-    for (int j = threadIdx.x; j < m; j += blockDim.x) {
-        const int c = j < got ? static_cast<int>(sel_pos[j]) : 0;
-        int64_t lo = list_off[c], hi = list_off[c + 1];
-        if (lo < 0 || hi < lo || hi > n_global) { raise_status(status, DWA_STATUS_BAD_LIST); lo = hi = 0; }
-        if (hi - lo > max_list) raise_status(status, DWA_STATUS_LIST_OVERFLOW);
-        lo = lo > row_lo ? lo : row_lo;
-        hi = hi < row_hi ? hi : row_hi;
-        int64_t sz = hi > lo ? hi - lo : 0;
-        if (sz > max_list) sz = max_list;
-        top_clusters[static_cast<int64_t>(b) * m + j] = c;
-        probe_lo[static_cast<int64_t>(b) * (m + 1) + j] = sz > 0 ? lo - row_lo : 0;
-        s_sz[j] = sz;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        int64_t acc = 0;
-        for (int j = 0; j < m; ++j) {
-            cand_base[static_cast<int64_t>(b) * (m + 1) + j] = acc;
-            acc += s_sz[j];
+    select_list_ranges(got, m, b, sel_pos, list_off, n_global, row_lo, row_hi, max_list, top_clusters,
+                       probe_lo, cand_base, status, s_sz);
+}
+
+// Coarse scores and top-m lists of one query by one cluster of CL CTAs
+// (grid (CL, B), clusters (CL, 1, 1), 64*S threads): every CTA normalises the
+// query's raw aspects in shared memory (normalize_aspect), scores its chunk of
+// ceil(C / CL) centroids with coarse_kernel's operations and order, and stores
+// their selection keys straight into cluster rank 0's key array (distributed
+// shared memory); after one cluster barrier rank 0 writes the normalised qw[b]
+// and picks the lists as topm_kernel does.  Replaces query_norm + coarse + topm
+// when the C keys fit in shared memory.
+struct CoarseTopmArgs {
+    const float* q;          // [B, S, d_k] raw aspect queries
+    const float* aspect_w;   // [S]
+    const float* centroids;  // [S, C, d_k]
+    int S, d_k, C, m;
+    const int64_t* list_off;
+    int64_t n_global, row_lo, row_hi;
+    int max_list;
+    float* qw;               // [B, S, d_k] out: normalised queries
+    int32_t* top_clusters;
+    int64_t* probe_lo;
+    int64_t* cand_base;
+    uint32_t* status;
+};
+
+constexpr int kCoarseCluster = 8;
+
+__host__ __device__ inline size_t coarse_topm_keys_bytes(int C) { return (static_cast<size_t>(C) * 8 + 15) / 16 * 16; }
+__host__ __device__ inline int coarse_topm_chunk(int C, int CL) { return (C + CL - 1) / CL; }
+__host__ __device__ inline size_t coarse_topm_smem(int C, int S, int d_k) {
+    return coarse_topm_keys_bytes(C) + (static_cast<size_t>(S) * d_k + static_cast<size_t>(S) * 64) * sizeof(float);
+}
+
+template <int DK>
+__global__ void __launch_bounds__(1024) coarse_topm_kernel(CoarseTopmArgs a) {
+    __shared__ uint64_t sel_key[kMaxK];
+    __shared__ int64_t sel_pos[kMaxK];
+    __shared__ int64_t s_sz[kMaxK + 1];
+    extern __shared__ __align__(16) unsigned char ctm[];
+    cooperative_groups::cluster_group cl = cooperative_groups::this_cluster();
+    cluster_arrive_relaxed();
+    const int S = a.S, d_k = a.d_k, C = a.C;
+    const int CL = static_cast<int>(cl.num_blocks()), rank = static_cast<int>(cl.block_rank());
+    const int b = blockIdx.y, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int cpc = coarse_topm_chunk(C, CL), c_lo = rank * cpc, c_hi = min(C, c_lo + cpc);
+    const int cl_i = threadIdx.x & 63, s = threadIdx.x >> 6;
+    // The preceding kernel (the query projection) does not write the
+    // centroids: the first chunk's rows and their squared norms are read
+    // before waiting for it.
+    float4 kv0[DK > 0 ? DK / 4 : 1];
+    float nrm0 = 0.f;
+    if constexpr (DK > 0) {
+        if (c_lo + cl_i < c_hi) {
+            const float4* kp = reinterpret_cast<const float4*>(a.centroids + (static_cast<int64_t>(s) * C + c_lo + cl_i) * d_k);
+#pragma unroll
+            for (int i = 0; i < DK / 4; ++i) kv0[i] = __ldg(kp + i);
+#pragma unroll
+            for (int i = 0; i < DK / 4; ++i) {
+                nrm0 = fmaf(kv0[i].x, kv0[i].x, nrm0);
+                nrm0 = fmaf(kv0[i].y, kv0[i].y, nrm0);
+                nrm0 = fmaf(kv0[i].z, kv0[i].z, nrm0);
+                nrm0 = fmaf(kv0[i].w, kv0[i].w, nrm0);
+            }
         }
-        probe_lo[static_cast<int64_t>(b) * (m + 1) + m] = 0;
-        cand_base[static_cast<int64_t>(b) * (m + 1) + m] = acc;
     }
+    pdl_enter();
+    uint64_t* keys = reinterpret_cast<uint64_t*>(ctm);
+    float* qs = reinterpret_cast<float*>(ctm + coarse_topm_keys_bytes(C));
+    float* terms = qs + S * d_k;
+    uint64_t* keys0 = cl.map_shared_rank(keys, 0);
+    for (int i = threadIdx.x; i < S * d_k; i += blockDim.x) qs[i] = a.q[static_cast<int64_t>(b) * S * d_k + i];
+    __syncthreads();
+    for (int t = warp; t < S; t += nwarps) normalize_aspect(qs + t * d_k, a.aspect_w, S, t, d_k);
+    __syncthreads();
+    if (rank == 0)
+        for (int i = threadIdx.x; i < S * d_k; i += blockDim.x) a.qw[static_cast<int64_t>(b) * S * d_k + i] = qs[i];
+    cluster_wait();   // rank 0 is running: its key array takes remote stores
+    for (int cb = c_lo; cb < c_hi; cb += 64) {
+        const int c = cb + cl_i;
+        if (c < c_hi) {
+            const float* kp = a.centroids + (static_cast<int64_t>(s) * C + c) * d_k;
+            const float* qq = qs + s * d_k;
+            float dot = 0.f, nrm = 0.f;
+            if constexpr (DK > 0) {
+                float4 kv[DK / 4];
+                if (cb == c_lo) {
+#pragma unroll
+                    for (int i = 0; i < DK / 4; ++i) kv[i] = kv0[i];
+                    nrm = nrm0;
+                } else {
+#pragma unroll
+                    for (int i = 0; i < DK / 4; ++i) kv[i] = __ldg(reinterpret_cast<const float4*>(kp) + i);
+#pragma unroll
+                    for (int i = 0; i < DK / 4; ++i) {
+                        nrm = fmaf(kv[i].x, kv[i].x, nrm);
+                        nrm = fmaf(kv[i].y, kv[i].y, nrm);
+                        nrm = fmaf(kv[i].z, kv[i].z, nrm);
+                        nrm = fmaf(kv[i].w, kv[i].w, nrm);
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < DK / 4; ++i) {
+                    const float4 qv = reinterpret_cast<const float4*>(qq)[i];
+                    dot = fmaf(kv[i].x, qv.x, dot);
+                    dot = fmaf(kv[i].y, qv.y, dot);
+                    dot = fmaf(kv[i].z, qv.z, dot);
+                    dot = fmaf(kv[i].w, qv.w, dot);
+                }
+            } else {
+                for (int d = 0; d < d_k; ++d) {
+                    const float x = __ldg(kp + d);
+                    nrm = fmaf(x, x, nrm);
+                    dot = fmaf(x, qq[d], dot);
+                }
+            }
+            terms[s * 64 + cl_i] = dot / (sqrtf(nrm) + 1e-8f);
+        }
+        __syncthreads();
+        if (s == 0 && c < c_hi) {
+            float sc = 0.f;
+            for (int t = 0; t < S; ++t) sc += terms[t * 64 + cl_i];
+            keys0[c] = make_key(sc, static_cast<uint32_t>(c));
+        }
+        __syncthreads();
+    }
+    cl.sync();   // every rank's keys are in rank 0's shared memory
+    if (rank != 0) return;
+    auto key_at = [&](int64_t i) { return keys[i]; };
+    const int got = block_topk(C, a.m, key_at, sel_key, sel_pos);
+    select_list_ranges(got, a.m, b, sel_pos, a.list_off, a.n_global, a.row_lo, a.row_hi, a.max_list,
+                       a.top_clusters, a.probe_lo, a.cand_base, a.status, s_sz);
 }
 
 template <int DK>
@@ -495,52 +681,26 @@ __global__ void empty_summary_kernel(float* summary, int k) {
     if (threadIdx.x == 0) { sm[2 * k] = 0.f; sm[2 * k + 1] = -INFINITY; sm[2 * k + 2] = 0.f; }
 }
 
-// A rank without soft_full: statistics that contribute nothing to the merge.
-__global__ void fill_stats_kernel(float* stats, int B, int stride) {
-    pdl_enter();
-    const int b = blockIdx.x * blockDim.x + threadIdx.x;
-    if (b >= B) return;
-    stats[static_cast<int64_t>(b) * stride] = -INFINITY;
-    stats[static_cast<int64_t>(b) * stride + 1] = 0.f;
-}
-
-// (max, sum exp) of s/T per query from the per-CTA pairs of the full pass,
-// written to stats[b * stride + {0, 1}].
-__global__ void softmax_stats_kernel(const float* __restrict__ partial, int nblk,
-                                     float* __restrict__ stats, int stride) {
-    pdl_enter();
-    __shared__ float red[33];
-    const int b = blockIdx.x;
-    const float* p = partial + static_cast<int64_t>(b) * nblk * 2;
-    float mx = -INFINITY;
-    for (int i = threadIdx.x; i < nblk; i += blockDim.x) mx = fmaxf(mx, p[2 * i]);
-    mx = block_reduce(mx, true, red);
-    float z = 0.f;
-    for (int i = threadIdx.x; i < nblk; i += blockDim.x) z += p[2 * i + 1] * expf(p[2 * i] - mx);
-    z = block_reduce(z, false, red);
-    if (threadIdx.x == 0) { stats[static_cast<int64_t>(b) * stride] = mx; stats[static_cast<int64_t>(b) * stride + 1] = z; }
-}
-
-// soft_full[b, n] = exp(s*invT - M_b) / Z_b in place (invT = 1/T, the factor the
-// full pass used for M and Z); 8 elements per thread.
+// soft_full[b, n] = exp(s*invT - M_b) * (1 / Z_b) in place (invT = 1/T, the
+// factor the full pass used for M and Z); 8 elements per thread.
 __global__ void __launch_bounds__(256) softmax_apply_kernel(float* __restrict__ sfull, int64_t N,
                                                             float invT, const float* __restrict__ stats) {
     pdl_enter();
     const int b = blockIdx.y;
-    const float mx = stats[2 * b], z = stats[2 * b + 1];
+    const float mx = stats[2 * b], rz = 1.f / stats[2 * b + 1];
     float* p = sfull + static_cast<int64_t>(b) * N;
     const int64_t i0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
     if (i0 + 8 <= N && (reinterpret_cast<uintptr_t>(p) & 15) == 0 && (N & 3) == 0) {
         float4 a = reinterpret_cast<const float4*>(p + i0)[0];
         float4 c = reinterpret_cast<const float4*>(p + i0)[1];
-        a.x = expf(a.x * invT - mx) / z; a.y = expf(a.y * invT - mx) / z;
-        a.z = expf(a.z * invT - mx) / z; a.w = expf(a.w * invT - mx) / z;
-        c.x = expf(c.x * invT - mx) / z; c.y = expf(c.y * invT - mx) / z;
-        c.z = expf(c.z * invT - mx) / z; c.w = expf(c.w * invT - mx) / z;
+        a.x = expf(a.x * invT - mx) * rz; a.y = expf(a.y * invT - mx) * rz;
+        a.z = expf(a.z * invT - mx) * rz; a.w = expf(a.w * invT - mx) * rz;
+        c.x = expf(c.x * invT - mx) * rz; c.y = expf(c.y * invT - mx) * rz;
+        c.z = expf(c.z * invT - mx) * rz; c.w = expf(c.w * invT - mx) * rz;
         reinterpret_cast<float4*>(p + i0)[0] = a;
         reinterpret_cast<float4*>(p + i0)[1] = c;
     } else {
-        for (int64_t i = i0; i < i0 + 8 && i < N; ++i) p[i] = expf(p[i] * invT - mx) / z;
+        for (int64_t i = i0; i < i0 + 8 && i < N; ++i) p[i] = expf(p[i] * invT - mx) * rz;
     }
 }
 
@@ -561,6 +721,13 @@ struct SelectArgs {
     uint32_t* status;
     int64_t row_lo;     // global pool row of local key row 0
     float* summary;     // non-null: a rank's part of a sharded call, [B, 2k+3] (see below)
+    // soft_full statistics (max, sum exp) of s/T into sf_stats[b * sf_stride + {0, 1}]
+    // when sf_stats is non-null: from the full pass's per-CTA pairs
+    // sf_partial [B, sf_nblk, 2], or (-inf, 0) when sf_partial is null
+    const float* sf_partial;
+    int sf_nblk;
+    float* sf_stats;
+    int sf_stride;
 };
 
 __device__ __forceinline__ float gate_raw(float s, float lam, float tau, float T) {
@@ -598,21 +765,57 @@ __device__ void write_alphas(int got, int k, bool gate, float lam, float tau, fl
     for (int i = got + l; i < k; i += 32) { al[i] = 0.f; ix[i] = got > 0 ? static_cast<int32_t>(rows_sv[0]) : 0; }
 }
 
-// One block per query.  STAGED: the candidate keys (and the gate sum) are
-// computed once into shared memory and every radix pass reads them there.
-template <bool STAGED>
+// soft_full statistics of query b (see SelectArgs), by the whole block.
+__device__ void write_softmax_stats(const SelectArgs& a, int b, float* red) {
+    float mx = -INFINITY, zs = 0.f;
+    if (a.sf_partial) {
+        const float* p = a.sf_partial + static_cast<int64_t>(b) * a.sf_nblk * 2;
+        for (int i = threadIdx.x; i < a.sf_nblk; i += blockDim.x) mx = fmaxf(mx, p[2 * i]);
+        mx = block_reduce(mx, true, red);
+        for (int i = threadIdx.x; i < a.sf_nblk; i += blockDim.x) zs += p[2 * i + 1] * expf(p[2 * i] - mx);
+        zs = block_reduce(zs, false, red);
+    }
+    if (threadIdx.x == 0) {
+        a.sf_stats[static_cast<int64_t>(b) * a.sf_stride] = mx;
+        a.sf_stats[static_cast<int64_t>(b) * a.sf_stride + 1] = zs;
+    }
+}
+
+// The result of query b's selection from its got <= k winners (scores s_sv,
+// global rows rows_sv, best first) and the gate sum Z: the rank's summary in a
+// sharded call, else alphas and indices.
+__device__ void emit_selection(const SelectArgs& a, int b, int got, bool gate, float lam, float tau, float Z,
+                               float* s_sv, int64_t* rows_sv) {
+    if (a.summary) {
+        float* sm = a.summary + static_cast<int64_t>(b) * summary_width(a.k);
+        for (int i = threadIdx.x; i < a.k; i += blockDim.x) {
+            sm[i] = i < got ? s_sv[i] : -INFINITY;
+            sm[a.k + i] = __int_as_float(i < got ? static_cast<int32_t>(rows_sv[i]) : -1);
+        }
+        if (threadIdx.x == 0) sm[2 * a.k] = gate ? Z : 0.f;
+        return;
+    }
+    if (threadIdx.x < 32) {
+        if (threadIdx.x == 0 && got < a.k) raise_status(a.status, DWA_STATUS_FEW_CANDIDATES);
+        write_alphas(got, a.k, gate, lam, tau, a.T, Z, s_sv, rows_sv, a.alphas + static_cast<int64_t>(b) * a.k,
+                     a.indices + static_cast<int64_t>(b) * a.k);
+    }
+}
+
+// One block per query, for candidate sets larger than a cluster stages: every
+// radix pass recomputes the keys from the scores in global memory.
 __global__ void __launch_bounds__(1024) select_kernel(SelectArgs a) {
     pdl_enter();
     __shared__ uint64_t sel_key[kMaxK];
     __shared__ int64_t sel_pos[kMaxK];
     __shared__ int64_t s_lo[kMaxK + 1], s_base[kMaxK + 1];
     __shared__ float red[33];
-    extern __shared__ uint64_t skeys[];
     const int b = blockIdx.x;
     for (int j = threadIdx.x; j <= a.m; j += blockDim.x) {
         s_lo[j] = a.probe_lo[static_cast<int64_t>(b) * (a.m + 1) + j];
         s_base[j] = a.cand_base[static_cast<int64_t>(b) * (a.m + 1) + j];
     }
+    if (a.sf_stats) write_softmax_stats(a, b, red);
     __syncthreads();
     const int64_t n = s_base[a.m];
     const float lam = __ldg(a.lambda_val), tau = __ldg(a.tau), T = a.T;
@@ -637,26 +840,7 @@ __global__ void __launch_bounds__(1024) select_kernel(SelectArgs a) {
     };
     float Z = 0.f;
     int got;
-    if (STAGED) {
-        // candidate order within a probed list is the row order, so walking the
-        // probes keeps global reads coalesced
-        float acc = 0.f;
-        for (int j = 0; j < a.m; ++j) {
-            const int64_t lo = s_lo[j], base = s_base[j], sz = s_base[j + 1] - s_base[j];
-            for (int64_t r = threadIdx.x; r < sz; r += blockDim.x) {
-                const int64_t row = lo + r;
-                const float s = a.sfull ? a.sfull[static_cast<int64_t>(b) * a.N + row]
-                                        : a.scores[static_cast<int64_t>(b) * a.K_cap + base + r];
-                const float raw = gate ? gate_raw(s, lam, tau, T) : 0.f;
-                acc += raw;
-                skeys[base + r] = make_key(rank_raw ? raw : s, static_cast<uint32_t>(row + a.row_lo));
-            }
-        }
-        if (gate) Z = block_reduce(acc, false, red);
-        __syncthreads();
-        auto key_at = [&](int64_t i) { return skeys[i]; };
-        got = block_topk(n, a.k, key_at, sel_key, sel_pos);
-    } else {
+    {
         if (gate) {
             float acc = 0.f;
             for (int64_t p = threadIdx.x; p < n; p += blockDim.x) {
@@ -677,20 +861,130 @@ __global__ void __launch_bounds__(1024) select_kernel(SelectArgs a) {
         sel_pos[i] = row + a.row_lo;
     }
     __syncthreads();
-    if (a.summary) {
-        float* sm = a.summary + static_cast<int64_t>(b) * summary_width(a.k);
-        for (int i = threadIdx.x; i < a.k; i += blockDim.x) {
-            sm[i] = i < got ? s_sv[i] : -INFINITY;
-            sm[a.k + i] = __int_as_float(i < got ? static_cast<int32_t>(sel_pos[i]) : -1);
+    emit_selection(a, b, got, gate, lam, tau, Z, s_sv, sel_pos);
+}
+
+// Selection of one query by a cluster of CL CTAs (grid (CL, B), clusters
+// (CL, 1, 1), kSelThreads threads), for candidate sets that fit in the
+// cluster's shared memory.  CTA r stages the candidate positions
+// [n*r/CL, n*(r+1)/CL): score, gate term and key, adds its share of the gate
+// sum Z, selects its local top k and stores it, with its Z share, into cluster
+// rank 0's shared memory.  After one cluster barrier rank 0 adds the Z shares
+// in rank order and selects the top k of the CL*k pushed slots; the keys order
+// (score or gate term, then pool row) is the single-block selection's, so the
+// winners are the same.  The last rank also writes the soft_full statistics.
+constexpr int kSelThreads = 256;
+constexpr int kSelCluster = 8;
+constexpr int kSelLocalKeys = 14336;   // candidates a CTA stages (168 KB of keys and scores)
+
+// Dynamic shared memory: keys [cap], pushed keys [CL*k], scores [cap], pushed
+// scores [CL*k], cap = max(local_cap, CL*k).
+__host__ __device__ inline size_t select_cluster_smem(int64_t local_cap, int CL, int k) {
+    const int64_t ck = static_cast<int64_t>(CL) * k;
+    const int64_t cap = local_cap > ck ? local_cap : ck;
+    return static_cast<size_t>(cap + ck) * (sizeof(uint64_t) + sizeof(float));
+}
+
+__global__ void __launch_bounds__(kSelThreads) select_cluster_kernel(SelectArgs a, int local_cap) {
+    pdl_enter();
+    __shared__ uint64_t sel_key[kMaxK];
+    __shared__ int64_t sel_pos[kMaxK];
+    __shared__ int64_t s_lo[kMaxK + 1], s_base[kMaxK + 1];
+    __shared__ float red[33];
+    __shared__ int m_got[kSelCluster];     // rank 0: each rank's number of winners
+    __shared__ float m_z[kSelCluster];     // rank 0: each rank's share of Z
+    __shared__ float s_sv[kMaxK];
+    extern __shared__ __align__(16) unsigned char sel_sm[];
+    cooperative_groups::cluster_group cl = cooperative_groups::this_cluster();
+    cluster_arrive_relaxed();
+    const int CL = static_cast<int>(cl.num_blocks()), r = static_cast<int>(cl.block_rank());
+    const int b = blockIdx.y, tid = threadIdx.x, k = a.k;
+    const int ck = CL * k, cap = local_cap > ck ? local_cap : ck;
+    uint64_t* skeys = reinterpret_cast<uint64_t*>(sel_sm);
+    uint64_t* mkeys = skeys + cap;
+    float* sscore = reinterpret_cast<float*>(mkeys + ck);
+    float* mscore = sscore + cap;
+    for (int j = tid; j <= a.m; j += blockDim.x) {
+        s_lo[j] = a.probe_lo[static_cast<int64_t>(b) * (a.m + 1) + j];
+        s_base[j] = a.cand_base[static_cast<int64_t>(b) * (a.m + 1) + j];
+    }
+    if (a.sf_stats && r == CL - 1) write_softmax_stats(a, b, red);
+    __syncthreads();
+    const int64_t n = s_base[a.m];
+    const int64_t p_lo = n * r / CL, p_hi = n * (r + 1) / CL;
+    const float lam = __ldg(a.lambda_val), tau = __ldg(a.tau), T = a.T;
+    const bool gate = !a.is_warmup;
+    const bool rank_raw = gate && lam < 0.f;
+    float zacc = 0.f;
+    if (p_hi - p_lo > local_cap) raise_status(a.status, DWA_STATUS_LIST_OVERFLOW);
+    const int64_t p_end = p_hi - p_lo > local_cap ? p_lo + local_cap : p_hi;
+    constexpr int U = 4;
+    for (int64_t p0 = p_lo; p0 < p_end; p0 += kSelThreads * U) {
+        float sv[U];
+        int64_t rowv[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t p = p0 + u * kSelThreads + tid;
+            sv[u] = 0.f;
+            rowv[u] = 0;
+            if (p < p_end) {
+                int lo = 0, hi = a.m - 1;
+                while (lo < hi) {
+                    const int mid = (lo + hi + 1) >> 1;
+                    if (s_base[mid] <= p) lo = mid; else hi = mid - 1;
+                }
+                rowv[u] = s_lo[lo] + (p - s_base[lo]);
+                sv[u] = a.sfull ? a.sfull[static_cast<int64_t>(b) * a.N + rowv[u]]
+                                : a.scores[static_cast<int64_t>(b) * a.K_cap + p];
+            }
         }
-        if (threadIdx.x == 0) sm[2 * a.k] = gate ? Z : 0.f;
-        return;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t p = p0 + u * kSelThreads + tid;
+            if (p < p_end) {
+                const float raw = gate ? gate_raw(sv[u], lam, tau, T) : 0.f;
+                zacc += raw;
+                skeys[p - p_lo] = make_key(rank_raw ? raw : sv[u], static_cast<uint32_t>(rowv[u] + a.row_lo));
+                sscore[p - p_lo] = sv[u];
+            }
+        }
     }
-    if (threadIdx.x < 32) {
-        if (threadIdx.x == 0 && got < a.k) raise_status(a.status, DWA_STATUS_FEW_CANDIDATES);
-        write_alphas(got, a.k, gate, lam, tau, T, Z, s_sv, sel_pos, a.alphas + static_cast<int64_t>(b) * a.k,
-                     a.indices + static_cast<int64_t>(b) * a.k);
+    const float zshare = gate ? block_reduce(zacc, false, red) : 0.f;
+    __syncthreads();
+    auto key_at = [&](int64_t i) { return skeys[i]; };
+    const int got = block_topk(p_end - p_lo, k, key_at, sel_key, sel_pos);
+    // push the local winners (slots past got: key 0, below every real key)
+    // and the Z share into rank 0
+    cluster_wait();
+    {
+        uint64_t* mk = cl.map_shared_rank(mkeys, 0);
+        float* ms = cl.map_shared_rank(mscore, 0);
+        for (int i = tid; i < k; i += blockDim.x) {
+            mk[r * k + i] = i < got ? sel_key[i] : 0ull;
+            ms[r * k + i] = i < got ? sscore[sel_pos[i]] : 0.f;
+        }
+        if (tid == 0) {
+            cl.map_shared_rank(m_got, 0)[r] = got;
+            cl.map_shared_rank(m_z, 0)[r] = zshare;
+        }
     }
+    cl.sync();
+    if (r != 0) return;
+    // rank 0: the top k of the CL*k slots (Z shares added in rank order)
+    int total = 0;
+    float Z = 0.f;
+    for (int src = 0; src < CL; ++src) {
+        total += m_got[src];
+        Z += m_z[src];
+    }
+    auto mkey_at = [&](int64_t i) { return mkeys[i]; };
+    const int fin = block_topk(ck, total < k ? total : k, mkey_at, sel_key, sel_pos);
+    for (int i = tid; i < fin; i += blockDim.x) {
+        s_sv[i] = mscore[sel_pos[i]];
+        sel_pos[i] = static_cast<int64_t>(0xFFFFFFFFu - static_cast<uint32_t>(sel_key[i] & 0xFFFFFFFFu));
+    }
+    __syncthreads();
+    emit_selection(a, b, fin, gate, lam, tau, Z, s_sv, sel_pos);
 }
 
 // Merge of a sharded call: per query, the global top-k of the world ranks'
@@ -784,6 +1078,7 @@ __global__ void full_probe_kernel(int B, int64_t N, int64_t* probe_lo, int64_t* 
 // ------------------------------------------------------------------ host ---
 struct RetWorkspace {
     uint32_t* status;
+    float* q;
     float* qw;
     float* c_score;
     int32_t* topc;
@@ -801,7 +1096,6 @@ struct RetWorkspace {
 
 constexpr int kFullRows = 256;
 constexpr int kMaxScanGrid = 1024;            // CTAs of a key scan
-constexpr int64_t kSelectStageKeys = 25600;  // 200 KB of staged keys
 
 static RetWorkspace carve_ret(void* base, const DwaRetrieveDims& d, bool ivf, bool want_sf) {
     Carver c(base);
@@ -810,6 +1104,7 @@ static RetWorkspace carve_ret(void* base, const DwaRetrieveDims& d, bool ivf, bo
     w.m_eff = ivf ? (d.m < d.C ? d.m : d.C) : 1;
     w.K_cap = ivf ? static_cast<int64_t>(w.m_eff) * d.max_list : d.N;
     w.nblk = static_cast<int>((d.N + kFullRows - 1) / kFullRows);
+    w.q = c.take<float>(static_cast<size_t>(d.B) * d.S * d.d_k);
     w.qw = c.take<float>(static_cast<size_t>(d.B) * d.S * d.d_k);
     w.probe_lo = c.take<int64_t>(static_cast<size_t>(d.B) * (w.m_eff + 1));
     w.cand_base = c.take<int64_t>(static_cast<size_t>(d.B) * (w.m_eff + 1));
@@ -896,27 +1191,53 @@ static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaSha
     const bool dk64 = d.d_k == 64 && reinterpret_cast<uintptr_t>(pool_keys) % 16 == 0 &&
                       (!ivf || reinterpret_cast<uintptr_t>(centroids) % 16 == 0);
 
-    // 1. aspect queries: projection over many CTAs, then normalisation
+    // 1. raw aspect queries q = W_Q z
     const int rows = d.S * d.d_k;
-    const int btile = std::max(1, std::min({QB, d.B, static_cast<int>((48 * 1024) / (4 * d.d_A))}));
-    const size_t zsh = static_cast<size_t>(btile) * d.d_A * sizeof(float);
+    const dim3 gq((rows + kProjRows - 1) / kProjRows, (d.B + kProjQ - 1) / kProjQ);
     if (d.z_dtype == DWA_BF16)
-        DWA_TIMED("query", st, launch_pdl(query_proj_kernel<__nv_bfloat16>, (rows + 3) / 4, 128, zsh, st, 
-                                     static_cast<const __nv_bfloat16*>(z), W_Q, d.B, rows, d.d_A,
-                                     btile, w.qw));
+        DWA_TIMED("query", st, launch_pdl(query_proj_kernel<__nv_bfloat16>, gq, kProjThreads, 0, st,
+                                          static_cast<const __nv_bfloat16*>(z), W_Q, d.B, rows, d.d_A, w.q));
     else
-        DWA_TIMED("query", st, launch_pdl(query_proj_kernel<float>, (rows + 3) / 4, 128, zsh, st, 
-                                     static_cast<const float*>(z), W_Q, d.B, rows, d.d_A, btile,
-                                     w.qw));
+        DWA_TIMED("query", st, launch_pdl(query_proj_kernel<float>, gq, kProjThreads, 0, st,
+                                          static_cast<const float*>(z), W_Q, d.B, rows, d.d_A, w.q));
     DWA_LAUNCH_CHECK("query_proj_kernel");
-    DWA_TIMED("query_norm", st,
-              launch_pdl(query_norm_kernel, d.B, 32 * d.S, 0, st, w.qw, aspect_weights, d.S, d.d_k));
-    DWA_LAUNCH_CHECK("query_norm_kernel");
-    g_launches_total += 2;
+    ++g_launches_total;
 
+    // 2. normalised queries qw; with IVF also the coarse scores, the top-m lists
+    //    and their candidate ranges: one cluster per query when the C list keys
+    //    fit in shared memory, else three kernels
+    const int CL = ivf ? std::min(kCoarseCluster, (d.C + 63) / 64) : 1;
+    const size_t ct_smem = coarse_topm_smem(d.C, d.S, d.d_k);
+    const bool fused_coarse = ivf && d.C <= kStageKeys && ct_smem <= 200 * 1024;
+    if (!fused_coarse) {
+        DWA_TIMED("query_norm", st, launch_pdl(query_norm_kernel, d.B, 32 * d.S, 0, st, w.q, aspect_weights,
+                                               d.S, d.d_k, w.qw));
+        DWA_LAUNCH_CHECK("query_norm_kernel");
+        ++g_launches_total;
+    }
     float* sfull = want_sf ? soft_full : w.sfull;
-    if (ivf) {
-        // 2. coarse scores + top-m lists + candidate ranges
+    if (fused_coarse) {
+        const size_t sm = ct_smem;
+        CoarseTopmArgs ca;
+        ca.q = w.q; ca.aspect_w = aspect_weights; ca.centroids = centroids;
+        ca.S = d.S; ca.d_k = d.d_k; ca.C = d.C; ca.m = w.m_eff;
+        ca.list_off = list_offsets; ca.n_global = n_global; ca.row_lo = row_lo; ca.row_hi = row_lo + d.N;
+        ca.max_list = d.max_list; ca.qw = w.qw; ca.top_clusters = w.topc; ca.probe_lo = w.probe_lo;
+        ca.cand_base = w.cand_base; ca.status = w.status;
+        auto fn = dk64 ? coarse_topm_kernel<64> : coarse_topm_kernel<0>;
+        {   // static + dynamic shared memory may pass 48 KB at any size
+            int dv = 0;
+            DWA_CUDA_TRY(cudaGetDevice(&dv));
+            static bool ct_attr[2][64] = {};
+            if (dv < 0 || dv >= 64 || !ct_attr[dk64][dv]) {
+                DWA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+                if (dv >= 0 && dv < 64) ct_attr[dk64][dv] = true;
+            }
+        }
+        DWA_TIMED("coarse", st, launch_pdl_cluster(fn, dim3(CL, d.B), dim3(64 * d.S), sm, st, dim3(CL, 1, 1), ca));
+        DWA_LAUNCH_CHECK("coarse_topm_kernel");
+        ++g_launches_total;
+    } else if (ivf) {
         dim3 gc((d.C + 63) / 64, d.B);
         const int cth = 64 * d.S;                       // S <= 16 (checked on entry)
         const size_t csh = qsh + static_cast<size_t>(d.S) * 64 * sizeof(float);
@@ -928,6 +1249,16 @@ static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaSha
                                         w.qw, centroids, d.S, d.d_k, d.C, w.c_score));
         DWA_LAUNCH_CHECK("coarse_kernel");
         const size_t tsh = d.C <= kStageKeys ? static_cast<size_t>(d.C) * 8 : 0;
+        {
+            int dv = 0;
+            DWA_CUDA_TRY(cudaGetDevice(&dv));
+            static bool tm_attr[64] = {};
+            if (dv < 0 || dv >= 64 || !tm_attr[dv]) {
+                DWA_CUDA_TRY(cudaFuncSetAttribute(topm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  static_cast<int>(kStageKeys * 8)));
+                if (dv >= 0 && dv < 64) tm_attr[dv] = true;
+            }
+        }
         DWA_TIMED("topm", st, launch_pdl(topm_kernel, d.B, 512, tsh, st, w.c_score, d.C, w.m_eff, list_offsets,
                                                                  n_global, row_lo, row_lo + d.N,
                                                                  d.max_list, w.topc, w.probe_lo,
@@ -1106,46 +1437,43 @@ static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaSha
     sa.status = w.status;
     sa.row_lo = row_lo;
     sa.summary = shard ? summary : nullptr;
-    if (w.K_cap <= kSelectStageKeys) {
-        const size_t ssh = static_cast<size_t>(w.K_cap) * 8;
-        if (ssh > 48 * 1024) {
-            int dev = 0;
-            DWA_CUDA_TRY(cudaGetDevice(&dev));
+    sa.sf_partial = want_sf ? w.partial : nullptr;
+    sa.sf_nblk = sf_blocks;
+    sa.sf_stats = shard ? summary + 2 * d.k + 1 : want_sf ? w.stats : nullptr;
+    sa.sf_stride = shard ? summary_width(d.k) : 2;
+    // one cluster of CL CTAs per query stages the candidates (about 512 per
+    // CTA) when they fit, else one block per query re-reads them every pass
+    int sel_cl = static_cast<int>(std::min<int64_t>(kSelCluster, std::max<int64_t>(1, (w.K_cap + 511) / 512)));
+    int64_t local_cap = (w.K_cap + sel_cl - 1) / sel_cl;
+    if (local_cap <= kSelLocalKeys) {
+        const size_t ssh = select_cluster_smem(local_cap, sel_cl, d.k);
+        {
+            // static + dynamic shared memory may pass 48 KB at any size
+            int dv = 0;
+            DWA_CUDA_TRY(cudaGetDevice(&dv));
             static bool attr_set[64] = {};
-            if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-                DWA_CUDA_TRY(cudaFuncSetAttribute(select_kernel<true>,
-                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                  static_cast<int>(kSelectStageKeys * 8)));
-                if (dev >= 0 && dev < 64) attr_set[dev] = true;
+            if (dv < 0 || dv >= 64 || !attr_set[dv]) {
+                DWA_CUDA_TRY(cudaFuncSetAttribute(select_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  static_cast<int>(select_cluster_smem(kSelLocalKeys, kSelCluster, kMaxK))));
+                if (dv >= 0 && dv < 64) attr_set[dv] = true;
             }
         }
-        DWA_TIMED("select", st, launch_pdl(select_kernel<true>, d.B, 1024, ssh, st, sa));
+        DWA_TIMED("select", st, launch_pdl_cluster(select_cluster_kernel, dim3(sel_cl, d.B), dim3(kSelThreads), ssh, st,
+                                                   dim3(sel_cl, 1, 1), sa, static_cast<int>(local_cap)));
     } else {
-        DWA_TIMED("select", st, launch_pdl(select_kernel<false>, d.B, 1024, 0, st, sa));
+        DWA_TIMED("select", st, launch_pdl(select_kernel, d.B, 1024, 0, st, sa));
     }
     DWA_LAUNCH_CHECK("select_kernel");
     ++g_launches_total;
-    // 6. normalise soft_full in place (a rank of a sharded call only writes its
-    //    statistics into the summary; the merge normalises)
-    if (want_sf && shard) {
-        DWA_TIMED("softmax_stats", st,
-                  launch_pdl(softmax_stats_kernel, d.B, 256, 0, st, w.partial, sf_blocks, summary + 2 * d.k + 1,
-                                                            summary_width(d.k)));
-        DWA_LAUNCH_CHECK("softmax_stats_kernel");
-        ++g_launches_total;
-    } else if (shard) {
-        launch_pdl(fill_stats_kernel, (d.B + 127) / 128, 128, 0, st, summary + 2 * d.k + 1, d.B, summary_width(d.k));
-        DWA_LAUNCH_CHECK("fill_stats_kernel");
-        ++g_launches_total;
-    } else if (want_sf) {
-        DWA_TIMED("softmax_stats", st,
-                  launch_pdl(softmax_stats_kernel, d.B, 256, 0, st, w.partial, sf_blocks, w.stats, 2));
-        DWA_LAUNCH_CHECK("softmax_stats_kernel");
+    // 6. normalise soft_full in place with the statistics the selection wrote
+    //    (a rank of a sharded call only writes them into its summary; the merge
+    //    normalises)
+    if (want_sf && !shard) {
         dim3 ga(static_cast<unsigned>((d.N + 2047) / 2048), d.B);
         DWA_TIMED("softmax_apply", st,
                   launch_pdl(softmax_apply_kernel, ga, 256, 0, st, soft_full, d.N, 1.f / d.T, w.stats));
         DWA_LAUNCH_CHECK("softmax_apply_kernel");
-        g_launches_total += 2;
+        ++g_launches_total;
     }
     return DWA_OK;
 }
@@ -1235,13 +1563,10 @@ extern "C" int dwa_sequence_mean(void* stream, int B, int T, int d, int dtype, c
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int es = dtype == DWA_BF16 ? 2 : 4;
     if (d % 8 == 0 && reinterpret_cast<uintptr_t>(h_A) % 16 == 0) {
-        dim3 g((d + 255) / 256, B);
         if (dtype == DWA_BF16)
-            DWA_TIMED("seq_mean", st, launch_pdl(column_sum8_kernel<__nv_bfloat16>, g, 512, 0, st, 
-                                          static_cast<const __nv_bfloat16*>(h_A), T, d, 1, z));
+            DWA_TIMED("seq_mean", st, launch_column_sum8(st, static_cast<const __nv_bfloat16*>(h_A), B, T, d, 1, z));
         else
-            DWA_TIMED("seq_mean", st, launch_pdl(column_sum8_kernel<float>, g, 512, 0, st, 
-                                          static_cast<const float*>(h_A), T, d, 1, z));
+            DWA_TIMED("seq_mean", st, launch_column_sum8(st, static_cast<const float*>(h_A), B, T, d, 1, z));
     } else {
         dim3 g((d + 63) / 64, B);
         if (dtype == DWA_BF16)

@@ -32,6 +32,23 @@ def equal_list_offsets(N: int, C: int, device) -> torch.Tensor:
     return (torch.arange(C + 1, dtype=torch.int64, device=device) * (N // C)).contiguous()
 
 
+def sequence_mean(h_A: torch.Tensor) -> torch.Tensor:
+    """The retrieval query input ``z = h_A.mean(axis=1)`` (model.py:171):
+    ``h_A [B, T, d_A]`` f32 or bf16 -> ``z [B, d_A]`` f32, summed in fp32 in a
+    fixed order (``dwa_sequence_mean``)."""
+    require_cuda("h_A", h_A)
+    if h_A.dim() != 3:
+        raise ValueError("h_A must be [B, T, d_A]")
+    h_A = h_A.contiguous()
+    B, T, d = h_A.shape
+    z = torch.empty((B, d), dtype=torch.float32, device=h_A.device)
+    with torch.cuda.device(h_A.device):
+        rc = _lib.load().dwa_sequence_mean(stream_of(h_A.device), B, T, d, dtype_code(h_A.dtype, "h_A"),
+                                           ptr(h_A), ptr(z))
+    _lib.check(rc, "dwa_sequence_mean")
+    return z
+
+
 def retrieve(z, W_Q, aspect_weights, tau, centroids, pool_keys, lambda_val, is_warmup, *, k, m, T,
              use_ivf=True, list_offsets=None, max_list=None, want_soft_full=True):
     """One ``dwa_retrieve`` call.  Returns ``(alphas [B,k] f32, indices [B,k]
