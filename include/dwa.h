@@ -233,6 +233,30 @@ DWA_API int dwa_retrieve_merge(void* stream, const DwaRetrieveDims* dims, int wo
                                void* workspace, size_t workspace_bytes);
 
 /* ---------------------------------------------------------------------------
+ * Retrieval VJP.  The backward that jax.vjp derives for
+ * MultiAspectRetrieval.__call__ (src/dwa/retrieval.py:64-158): the cotangents
+ * g_alphas [B,k] and g_soft_full [B,N] (f32; either may be NULL) of the
+ * forward's outputs back to
+ *   g_z [B,d_A] f32, g_W_Q [S,d_k,d_A], g_aspect_weights [S], g_tau [1]
+ * and, when g_pool_keys is non-NULL, the key cache g_pool_keys [S,N,d_k]
+ * (B <= 32).  The forward's alphas and indices (with g_alphas) and its
+ * normalised soft_full (with g_soft_full) are inputs; the queries, the probed
+ * lists and the candidate scores are recomputed from the same arguments as
+ * dwa_retrieve's.  indices and the coarse top-m carry no gradient (integer /
+ * piecewise constant), so centroids get none.  Every output is overwritten;
+ * reductions run in a fixed order.  Needs d_k % 4 == 0 and S*d_k <= 1024.
+ * ------------------------------------------------------------------------- */
+DWA_API size_t dwa_retrieve_bwd_workspace_bytes(const DwaRetrieveDims* dims, int use_ivf);
+DWA_API int dwa_retrieve_bwd(void* stream, const DwaRetrieveDims* dims, int use_ivf, int is_warmup,
+                             const float* lambda_val, const void* z, const float* W_Q,
+                             const float* aspect_weights, const float* tau, const float* centroids,
+                             const int64_t* list_offsets, const float* pool_keys, const float* alphas,
+                             const int32_t* indices, const float* soft_full, const float* g_alphas,
+                             const float* g_soft_full, float* g_z, float* g_W_Q,
+                             float* g_aspect_weights, float* g_tau, float* g_pool_keys,
+                             void* workspace, size_t workspace_bytes);
+
+/* ---------------------------------------------------------------------------
  * Key cache.  Replaces compute_key_cache (src/dwa/assembly_pallas.py:392-400) and
  * VectorPool.compute_keys (src/dwa/pool.py:37-44): keys [S,N,d_k] f32 =
  * einsum("nd,sda->sna", pool_vectors [N,D], key_proj [S,D,d_k]) in fp32, both

@@ -87,6 +87,9 @@ _SIGNATURES = {
     "dwa_key_cache": (C.c_int, [_P, C.POINTER(KeyCacheDims), _P, _P, _P, _P, C.c_size_t]),
     "dwa_centroid_ema": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int64, _P, _P, C.c_float, _P, _P,
                                    C.c_size_t]),
+    "dwa_retrieve_bwd_workspace_bytes": (C.c_size_t, [C.POINTER(RetrieveDims), C.c_int]),
+    "dwa_retrieve_bwd": (C.c_int, [_P, C.POINTER(RetrieveDims), C.c_int, C.c_int, _P, _P, _P, _P, _P, _P,
+                                   _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t]),
     "dwa_retrieve_merge": (C.c_int, [_P, C.POINTER(RetrieveDims), C.c_int, _P, C.c_int, _P, _P, _P,
                                      _P, _P, _P, C.c_size_t]),
 }

@@ -1159,38 +1159,15 @@ extern "C" size_t dwa_retrieve_workspace_bytes(const DwaRetrieveDims* dims, int 
     return carve_ret(nullptr, *dims, use_ivf != 0, want_soft_full != 0).bytes;
 }
 
-// One retrieval call.  shard == nullptr: the whole pool (dwa_retrieve).
-// Otherwise pool_keys holds the rows [row_lo, row_lo + N) of an n_global-row
-// pool and, instead of alphas / indices, the call writes this rank's summary
-// [B, 2k+3] (see summary_width) and leaves soft_full as raw scores.
-static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaShard* shard, int use_ivf,
-                         int is_warmup, const float* lambda_val, const void* z, const float* W_Q,
-                         const float* aspect_weights, const float* tau, const float* centroids,
-                         const int64_t* list_offsets, const float* pool_keys, float* alphas,
-                         int32_t* indices, float* soft_full, float* summary, void* workspace,
-                         size_t workspace_bytes) {
-    int rc = check_ret(dims, use_ivf);
-    if (rc) return rc;
-    const DwaRetrieveDims& d = *dims;
-    const bool ivf = use_ivf != 0, want_sf = soft_full != nullptr;
-    if (!lambda_val || !z || !W_Q || !aspect_weights || !tau || !pool_keys ||
-        (shard ? !summary : (!alphas || !indices)))
-        return fail(DWA_ERR_INVALID_ARG, "a required pointer is NULL");
-    const int64_t row_lo = shard ? shard->row_lo : 0, n_global = shard ? shard->n_global : d.N;
-    if (ivf && (!centroids || !list_offsets))
-        return fail(DWA_ERR_INVALID_ARG, "IVF needs centroids and list_offsets");
-    const RetWorkspace w = carve_ret(workspace, d, ivf, want_sf);
-    if (!workspace || reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
-        return fail(DWA_ERR_WORKSPACE, "workspace must be non-NULL and 256-byte aligned");
-    if (workspace_bytes < w.bytes)
-        return fail(DWA_ERR_WORKSPACE, "workspace too small: need " + std::to_string(w.bytes));
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
+// Steps 1-2 of a retrieval call, shared by the forward and the VJP: raw
+// queries q = W_Q z into w.q; normalised queries into w.qw; with IVF the top-m
+// lists of every query and their candidate ranges (probe_lo, cand_base) clipped
+// to the key rows [row_lo, row_lo + N); without IVF one range of all N rows.
+static int launch_queries_and_probes(cudaStream_t st, const DwaRetrieveDims& d, bool ivf, bool dk64,
+                                     const void* z, const float* W_Q, const float* aspect_weights,
+                                     const float* centroids, const int64_t* list_offsets, int64_t row_lo,
+                                     int64_t n_global, const RetWorkspace& w) {
     const size_t qsh = static_cast<size_t>(d.S) * d.d_k * sizeof(float);
-    // d_k = 64 with 16-byte aligned keys takes the unrolled scoring; the fine
-    // and the full pass always take the same variant (bit-identical scores).
-    const bool dk64 = d.d_k == 64 && reinterpret_cast<uintptr_t>(pool_keys) % 16 == 0 &&
-                      (!ivf || reinterpret_cast<uintptr_t>(centroids) % 16 == 0);
-
     // 1. raw aspect queries q = W_Q z
     const int rows = d.S * d.d_k;
     const dim3 gq((rows + kProjRows - 1) / kProjRows, (d.B + kProjQ - 1) / kProjQ);
@@ -1215,7 +1192,6 @@ static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaSha
         DWA_LAUNCH_CHECK("query_norm_kernel");
         ++g_launches_total;
     }
-    float* sfull = want_sf ? soft_full : w.sfull;
     if (fused_coarse) {
         const size_t sm = ct_smem;
         CoarseTopmArgs ca;
@@ -1270,6 +1246,45 @@ static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaSha
         DWA_LAUNCH_CHECK("full_probe_kernel");
         ++g_launches_total;
     }
+    return DWA_OK;
+}
+
+// One retrieval call.  shard == nullptr: the whole pool (dwa_retrieve).
+// Otherwise pool_keys holds the rows [row_lo, row_lo + N) of an n_global-row
+// pool and, instead of alphas / indices, the call writes this rank's summary
+// [B, 2k+3] (see summary_width) and leaves soft_full as raw scores.
+static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaShard* shard, int use_ivf,
+                         int is_warmup, const float* lambda_val, const void* z, const float* W_Q,
+                         const float* aspect_weights, const float* tau, const float* centroids,
+                         const int64_t* list_offsets, const float* pool_keys, float* alphas,
+                         int32_t* indices, float* soft_full, float* summary, void* workspace,
+                         size_t workspace_bytes) {
+    int rc = check_ret(dims, use_ivf);
+    if (rc) return rc;
+    const DwaRetrieveDims& d = *dims;
+    const bool ivf = use_ivf != 0, want_sf = soft_full != nullptr;
+    if (!lambda_val || !z || !W_Q || !aspect_weights || !tau || !pool_keys ||
+        (shard ? !summary : (!alphas || !indices)))
+        return fail(DWA_ERR_INVALID_ARG, "a required pointer is NULL");
+    const int64_t row_lo = shard ? shard->row_lo : 0, n_global = shard ? shard->n_global : d.N;
+    if (ivf && (!centroids || !list_offsets))
+        return fail(DWA_ERR_INVALID_ARG, "IVF needs centroids and list_offsets");
+    const RetWorkspace w = carve_ret(workspace, d, ivf, want_sf);
+    if (!workspace || reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
+        return fail(DWA_ERR_WORKSPACE, "workspace must be non-NULL and 256-byte aligned");
+    if (workspace_bytes < w.bytes)
+        return fail(DWA_ERR_WORKSPACE, "workspace too small: need " + std::to_string(w.bytes));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t qsh = static_cast<size_t>(d.S) * d.d_k * sizeof(float);
+    // d_k = 64 with 16-byte aligned keys takes the unrolled scoring; the fine
+    // and the full pass always take the same variant (bit-identical scores).
+    const bool dk64 = d.d_k == 64 && reinterpret_cast<uintptr_t>(pool_keys) % 16 == 0 &&
+                      (!ivf || reinterpret_cast<uintptr_t>(centroids) % 16 == 0);
+
+    if ((rc = launch_queries_and_probes(st, d, ivf, dk64, z, W_Q, aspect_weights, centroids, list_offsets,
+                                        row_lo, n_global, w)))
+        return rc;
+    float* sfull = want_sf ? soft_full : w.sfull;
     // Scoring variant, the same for the full and the fine pass so both give
     // bit-identical scores (d_k = 64): the CUDA-core key scan for B <= 16, the
     // tensor-core key scan for 16 < B <= 32 with S <= 4, else the generic
@@ -1639,3 +1654,4 @@ extern "C" int dwa_retrieve_noalloc(void* stream, const DwaRetrieveDims* dims, i
                         centroids, list_offsets, pool_keys, alphas, indices, soft_full, scratch,
                         kNoAllocScratchBytes);
 }
+#include "retrieval_bwd.cuh"

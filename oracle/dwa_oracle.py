@@ -197,6 +197,105 @@ def retrieve(z, W_Q, aspect_weights, tau, centroids, pool_keys, *, k, m, T,
     return alphas, indices, soft_full
 
 
+def _normalize_bwd(x, g_y):
+    """VJP of ``x / (||x|| + 1e-8)`` over the last axis (the gradient of
+    ``jnp.linalg.norm`` is ``x / ||x||``)."""
+    n = np.linalg.norm(x, axis=-1, keepdims=True)
+    d = n + x.dtype.type(EPS)
+    return g_y / d - x * np.sum(x * g_y, axis=-1, keepdims=True) / (n * d * d)
+
+
+def retrieve_bwd(z, W_Q, aspect_weights, tau, centroids, pool_keys, *, k, m, T, lambda_val,
+                 is_warmup, g_alphas=None, g_soft_full=None, use_ivf=True, list_offsets=None,
+                 tie_break="index"):
+    """VJP of ``retrieve`` (retrieval.py:64-158): the cotangents of ``alphas``
+    and ``soft_full`` back to ``z``, ``W_Q``, ``aspect_weights``, ``tau`` and
+    ``pool_keys``, as ``jax.vjp`` of ``MultiAspectRetrieval.__call__`` gives
+    them.  ``indices`` are integers and the coarse top-m and the top-k are
+    piecewise constant, so no gradient reaches the centroids; ``lambda_val`` is
+    a schedule value, not a parameter.
+
+    Every score the selection or soft_full reads is ``s[b, n] = Σ_s w_s
+    q̂[b,s]·k̂[s,n]`` (:100-106, :114-118), so the cotangents are first collected
+    per (query, pool row) in ``G [B, N]``:
+
+    * warmup (:144-146): ``α = softmax(top/T)`` puts ``α(g_α - Σ α g_α)/T`` on
+      the winners' rows;
+    * gate (:150-155): ``raw = σ(λ(s-τ)) e^{s/T}``, ``rn = raw/(Σ raw + 1e-8)``,
+      ``α = top(rn)/(Σ top + 1e-8)``: every candidate's row gets
+      ``g_raw · raw · (λ(1-σ) + 1/T)`` through the sum over all candidates,
+      and ``τ`` gets ``-Σ g_raw · raw · λ(1-σ)``;
+    * soft_full (:118-119): ``soft (g_soft - Σ g_soft soft) / T`` on every row.
+
+    Then ``A[b,s] = Σ_n G[b,n] k̂[s,n]`` gives ``g_q̂ = w_s A``, ``g_w[s] =
+    Σ_b q̂[b,s]·A[b,s]`` and ``g_k̂[s,n] = w_s Σ_b G[b,n] q̂[b,s]``, followed by
+    the normalisation, projection (:65) and softmax (:69) backward.
+
+    Returns ``dict(g_z, g_W_Q, g_aspect_weights, g_tau, g_pool_keys, G)``.
+    """
+    dt = z.dtype.type
+    B = z.shape[0]
+    S, N, _ = pool_keys.shape
+    queries = np.einsum("ska,ba->bsk", W_Q, z)                  # :65
+    q_norm = l2_normalize(queries)                               # :66
+    w = softmax(aspect_weights, axis=0)                          # :69
+    T_ = dt(T)
+    if use_ivf:
+        C = centroids.shape[1]
+        if list_offsets is None:
+            list_offsets = equal_list_offsets(N, C)
+        _, top_clusters = top_k(coarse_scores(q_norm, w, centroids), min(m, C))
+        cands = candidate_lists(top_clusters, list_offsets)
+        s_list = [fine_scores(q_norm[b], w, pool_keys, cands[b]) for b in range(B)]
+    else:
+        s_full = full_scores(q_norm, w, pool_keys)
+        cands = [np.arange(N, dtype=np.int64) for _ in range(B)]
+        s_list = [s_full[b] for b in range(B)]
+    G = np.zeros((B, N), dtype=z.dtype)
+    g_tau = dt(0)
+    if g_alphas is not None:
+        lam, tau_ = dt(lambda_val), dt(tau)
+        for b in range(B):
+            s, cand = s_list[b], cands[b]
+            tie = cand if tie_break == "index" else None
+            if is_warmup:
+                top, pos = top_k(s, k, tie)
+                alpha = softmax(top / T_)
+                ga = g_alphas[b, :len(pos)]
+                G[b, cand[pos]] += alpha * (ga - np.sum(alpha * ga)) / T_
+            else:
+                sg = sigmoid(lam * (s - tau_))
+                raw = sg * np.exp(s / T_)
+                Zr = raw.sum() + dt(EPS)
+                rn = raw / Zr
+                top_raw, pos = top_k(rn, k, tie)
+                St = top_raw.sum() + dt(EPS)
+                ga = g_alphas[b, :len(pos)]
+                g_t = ga / St - np.sum(ga * top_raw) / (St * St)
+                g_rn = np.zeros_like(s)
+                g_rn[pos] = g_t
+                g_raw = g_rn / Zr - np.sum(g_rn * raw) / (Zr * Zr)
+                G[b, cand] += g_raw * raw * (lam * (1 - sg) + 1 / T_)
+                g_tau += np.sum(g_raw * raw * (-lam * (1 - sg)))
+    if g_soft_full is not None:
+        soft = softmax(full_scores(q_norm, w, pool_keys) / T_)
+        G += soft * (g_soft_full - np.sum(g_soft_full * soft, axis=-1, keepdims=True)) / T_
+    k_norm = l2_normalize(pool_keys)
+    A = np.einsum("bn,snk->bsk", G, k_norm)
+    g_qn = w[None, :, None] * A
+    g_w = np.einsum("bsk,bsk->s", q_norm, A)
+    g_kn = np.einsum("bn,s,bsk->snk", G, w, q_norm)
+    g_queries = _normalize_bwd(queries, g_qn)
+    return dict(
+        g_z=np.einsum("bsk,ska->ba", g_queries, W_Q),
+        g_W_Q=np.einsum("bsk,ba->ska", g_queries, z),
+        g_aspect_weights=w * (g_w - np.sum(w * g_w)),
+        g_tau=g_tau,
+        g_pool_keys=_normalize_bwd(pool_keys, g_kn),
+        G=G,
+    )
+
+
 # ---------------------------------------------------------------------------
 # Row-sharded retrieval: one rank's summary and the merge (extension; with one
 # rank it reduces to ``retrieve`` with tie_break="index")
