@@ -257,6 +257,34 @@ DWA_API int dwa_retrieve_bwd(void* stream, const DwaRetrieveDims* dims, int use_
                              void* workspace, size_t workspace_bytes);
 
 /* ---------------------------------------------------------------------------
+ * Auxiliary losses.  Replaces aux_losses (src/dwa/losses.py:9-73) and its
+ * jax.grad: from the forward's alphas [B,k], indices [B,k], the key cache
+ * [S,N,d_k], the assembled W [B,d_B,d_A] f32, W_base [d_B,d_A] and the
+ * normalised soft_full [B,N],
+ *   losses[5] = {l_util, l_div, l_norm, l_sparse, total_aux}
+ * with total_aux = Σ lambda * loss (TrainConfig.lambda_*, config.py:181-184),
+ * and the gradients of total_aux (each output may be NULL):
+ *   g_alphas [B,k], g_soft_full [B,N], g_W [B,d_B,d_A], g_W_base [d_B,d_A]
+ *   (overwritten), g_pool_keys [S,N,d_k] (ADDED into, at the retrieved rows,
+ *   so it composes with dwa_retrieve_bwd's key gradient).
+ * B*k <= 8192; reductions in a fixed order.
+ * ------------------------------------------------------------------------- */
+typedef struct DwaAuxDims {
+    int32_t B, k, S, d_k, d_B, d_A;
+    int64_t N;
+} DwaAuxDims;
+typedef struct DwaAuxWeights {
+    float util, div, norm, sparse;   /* lambda_util, lambda_div, lambda_norm, lambda_sparse */
+} DwaAuxWeights;
+DWA_API size_t dwa_aux_losses_workspace_bytes(const DwaAuxDims* dims);
+DWA_API int dwa_aux_losses(void* stream, const DwaAuxDims* dims, const DwaAuxWeights* lambdas,
+                           const float* alphas, const int32_t* indices, const float* pool_keys,
+                           const float* W, const float* W_base, const float* soft_full,
+                           float* losses, float* g_alphas, float* g_soft_full, float* g_W,
+                           float* g_W_base, float* g_pool_keys, void* workspace,
+                           size_t workspace_bytes);
+
+/* ---------------------------------------------------------------------------
  * Key cache.  Replaces compute_key_cache (src/dwa/assembly_pallas.py:392-400) and
  * VectorPool.compute_keys (src/dwa/pool.py:37-44): keys [S,N,d_k] f32 =
  * einsum("nd,sda->sna", pool_vectors [N,D], key_proj [S,D,d_k]) in fp32, both

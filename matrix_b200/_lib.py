@@ -52,6 +52,15 @@ class Shard(C.Structure):
     _fields_ = [("row_lo", C.c_int64), ("n_global", C.c_int64)]
 
 
+class AuxDims(C.Structure):
+    _fields_ = [("B", C.c_int32), ("k", C.c_int32), ("S", C.c_int32), ("d_k", C.c_int32),
+                ("d_B", C.c_int32), ("d_A", C.c_int32), ("N", C.c_int64)]
+
+
+class AuxWeights(C.Structure):
+    _fields_ = [("util", C.c_float), ("div", C.c_float), ("norm", C.c_float), ("sparse", C.c_float)]
+
+
 _P = C.c_void_p
 _SIGNATURES = {
     "dwa_version": (C.c_char_p, []),
@@ -87,6 +96,9 @@ _SIGNATURES = {
     "dwa_key_cache": (C.c_int, [_P, C.POINTER(KeyCacheDims), _P, _P, _P, _P, C.c_size_t]),
     "dwa_centroid_ema": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int64, _P, _P, C.c_float, _P, _P,
                                    C.c_size_t]),
+    "dwa_aux_losses_workspace_bytes": (C.c_size_t, [C.POINTER(AuxDims)]),
+    "dwa_aux_losses": (C.c_int, [_P, C.POINTER(AuxDims), C.POINTER(AuxWeights), _P, _P, _P, _P, _P, _P, _P,
+                                 _P, _P, _P, _P, _P, _P, C.c_size_t]),
     "dwa_retrieve_bwd_workspace_bytes": (C.c_size_t, [C.POINTER(RetrieveDims), C.c_int]),
     "dwa_retrieve_bwd": (C.c_int, [_P, C.POINTER(RetrieveDims), C.c_int, C.c_int, _P, _P, _P, _P, _P, _P,
                                    _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t]),

@@ -297,6 +297,75 @@ def retrieve_bwd(z, W_Q, aspect_weights, tau, centroids, pool_keys, *, k, m, T, 
 
 
 # ---------------------------------------------------------------------------
+# Auxiliary losses: aux_losses (losses.py:9-73) and their VJP
+# ---------------------------------------------------------------------------
+
+def aux_losses(alphas, indices, pool_keys, W, W_base, soft_full, *, lambda_util, lambda_div,
+               lambda_norm, lambda_sparse):
+    """``aux_losses`` (losses.py:9-73), literally: ``l_util = N Σ f P``
+    (:35-38), ``l_div`` the mean upper-triangle cosine of the aspect-mean
+    retrieved keys (:42-50), ``l_norm = mean_b ||W_b - W_base||²`` (:53-54),
+    ``l_sparse`` the mean entropy of the clipped alphas (:57-58) and the
+    weighted total (:66-71)."""
+    B, k = alphas.shape
+    N = soft_full.shape[-1]
+    dt = alphas.dtype.type
+    f = np.zeros(N, dtype=alphas.dtype)
+    np.add.at(f, indices.reshape(-1), dt(1))
+    f = f / dt(B * k)
+    P = soft_full.mean(axis=0)
+    l_util = dt(N) * np.dot(f, P)
+    rk = pool_keys[:, indices, :].transpose(1, 2, 0, 3).mean(axis=2)        # [B, k, d_k]
+    rkn = l2_normalize(rk)
+    cos = np.einsum("bkd,bld->bkl", rkn, rkn)
+    mask = np.triu(np.ones((k, k), dtype=bool), k=1)
+    l_div = (cos * mask[None]).sum() / (mask.sum() * B + dt(EPS))
+    l_norm = ((W - W_base[None]) ** 2).sum(axis=(-1, -2)).mean()
+    a = np.clip(alphas, dt(1e-8), dt(1.0))
+    l_sparse = -(a * np.log(a)).sum(axis=-1).mean()
+    total = (dt(lambda_util) * l_util + dt(lambda_div) * l_div + dt(lambda_norm) * l_norm
+             + dt(lambda_sparse) * l_sparse)
+    return dict(l_util=l_util, l_div=l_div, l_norm=l_norm, l_sparse=l_sparse, total_aux=total)
+
+
+def aux_losses_bwd(alphas, indices, pool_keys, W, W_base, soft_full, *, lambda_util, lambda_div,
+                   lambda_norm, lambda_sparse):
+    """Gradients of ``total_aux`` (losses.py:66-71) w.r.t. alphas, soft_full, W,
+    W_base and pool_keys, as ``jax.grad`` gives them:
+
+    * ``g_soft[b, n] = λ_util N f_n / B`` (:38);
+    * ``l_div``: ``g_r̂_i = c (U - r̂_i)`` with ``U = Σ_j r̂_j`` and
+      ``c = λ_div / (B k(k-1)/2 + 1e-8)``, then the normalisation VJP and
+      ``1/S`` into every aspect's row ``indices[b, i]`` (duplicates add);
+    * ``g_W = 2 λ_norm (W - W_base) / B``, ``g_W_base = -Σ_b g_W``;
+    * ``g_α = -λ_sparse (log a + 1) / B`` times the gradient of
+      ``jnp.clip`` (1 inside (1e-8, 1), 1/2 on a bound, 0 outside).
+    """
+    B, k = alphas.shape
+    S, N, d_k = pool_keys.shape
+    dt = alphas.dtype.type
+    f = np.zeros(N, dtype=alphas.dtype)
+    np.add.at(f, indices.reshape(-1), dt(1))
+    f = f / dt(B * k)
+    g_soft = np.broadcast_to(dt(lambda_util) * dt(N) * f / dt(B), (B, N)).copy()
+    rk = pool_keys[:, indices, :].transpose(1, 2, 0, 3).mean(axis=2)        # [B, k, d_k]
+    rkn = l2_normalize(rk)
+    c = dt(lambda_div) / (dt(k * (k - 1) // 2 * B) + dt(EPS))
+    g_rkn = c * (rkn.sum(axis=1, keepdims=True) - rkn)
+    g_rk = _normalize_bwd(rk, g_rkn)
+    g_keys = np.zeros_like(pool_keys)
+    for s in range(S):
+        np.add.at(g_keys[s], indices.reshape(-1), g_rk.reshape(-1, d_k) / dt(S))
+    g_W = dt(2 * lambda_norm / B) * (W - W_base[None])
+    lo, hi = dt(1e-8), dt(1.0)
+    a = np.clip(alphas, lo, hi)
+    clip_grad = np.where((alphas > lo) & (alphas < hi), dt(1), np.where((alphas == lo) | (alphas == hi), dt(0.5), dt(0)))
+    g_alphas = -dt(lambda_sparse) * (np.log(a) + 1) / dt(B) * clip_grad
+    return dict(g_alphas=g_alphas, g_soft_full=g_soft, g_W=g_W, g_W_base=-g_W.sum(axis=0),
+                g_pool_keys=g_keys)
+
+
+# ---------------------------------------------------------------------------
 # Row-sharded retrieval: one rank's summary and the merge (extension; with one
 # rank it reduces to ``retrieve`` with tie_break="index")
 # ---------------------------------------------------------------------------
