@@ -53,6 +53,8 @@ def parse_args():
                     help="CPU seconds for the cpu_baseline sample (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip timing the retrieval VJP and the auxiliary losses")
     ap.add_argument("--no-key-cache", action="store_true",
                     help="skip timing compute_key_cache (once per window, not part of the step)")
     return ap.parse_args()
@@ -271,6 +273,76 @@ def time_key_cache(t, flush, peaks, reps=3):
             "roofline_ms": max(t_hbm, t_tc), "frac": max(t_hbm, t_tc) / ours,
             "bound": "hbm" if t_hbm >= t_tc else "tensor", "algorithmic_bytes": hbm, "flops": flops,
             "cublas_gemm_ms": lib, "shape": f"pool [{N}, {D}] bf16 x key_proj [{S}, {D}, {dk}] bf16"}
+
+
+def time_training_extras(w, t, flush, peaks, reps=5):
+    """The training-time parts next to the step, on the workload's inputs, timed
+    with CUDA events after a flush (best of ``reps``):
+
+    * ``retrieve_bwd``: the retrieval VJP for the alphas' cotangent alone (the
+      key pass visits only the probed lists' tiles), with the soft_full
+      cotangent as well (the key pass reads every key row), and with the
+      key-cache gradient; the key pass of the full case against the HBM
+      roofline (keys + G read once: 4 (S N d_k + B N) bytes);
+    * ``aux_losses``: the four losses and their gradients.
+    The cotangents are seeded synthetic values of the right shapes."""
+    import torch
+    from matrix_b200 import _lib
+    from matrix_b200.losses import aux_losses_and_grads
+    from matrix_b200.retrieval import retrieve, retrieve_backward
+    lib = _lib.load()
+    cfg = w.cfg
+    g = torch.Generator(device=t["keys"].device).manual_seed(7)
+    z = t["h_A"].float().mean(dim=1)
+    kw = dict(k=cfg.k_max, m=cfg.m, T=cfg.T, list_offsets=t["list_offsets"], max_list=cfg.N // cfg.C)
+    args = (z, t["W_Q"], t["aspect_weights"], t["tau"], t["centroids"], t["keys"], t["lam"], w.is_warmup)
+    alphas, indices, soft_full = retrieve(*args, **kw, want_soft_full=True)
+    g_al = torch.randn(alphas.shape, generator=g, device=z.device)
+    g_sf = torch.randn(soft_full.shape, generator=g, device=z.device)
+
+    def timed(fn, name=None):
+        fn()
+        torch.cuda.synchronize()
+        ms, kms = [], []
+        ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        if name:
+            for e in ev:
+                e.record()
+            torch.cuda.synchronize()
+            lib.dwa_profile_kernel(name.encode(), C_ptr(ev[0]), C_ptr(ev[1]))
+        for _ in range(reps):
+            flush()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            ms.append(a.elapsed_time(b))
+            if name:
+                kms.append(ev[0].elapsed_time(ev[1]))
+        if name:
+            lib.dwa_profile_clear()
+        return float(min(ms)), (float(min(kms)) if kms else None)
+
+    def bwd(gs, keys):
+        return retrieve_backward(*args, alphas, indices, soft_full, g_al, gs, **kw, want_key_grad=keys)
+
+    probed_ms, _ = timed(lambda: bwd(None, False))
+    full_ms, kp_ms = timed(lambda: bwd(g_sf, False), name="key_grad")
+    keys_ms, _ = timed(lambda: bwd(g_sf, True))
+    S, N, dk = t["keys"].shape
+    B = z.shape[0]
+    kp_bytes = 4.0 * (S * N * dk + B * N)
+    out = {"retrieve_bwd": {
+        "alphas_only_ms": probed_ms, "alphas_and_soft_full_ms": full_ms, "with_key_grad_ms": keys_ms,
+        "key_pass": {"kernel": "key_grad", "ms": kp_ms, "algorithmic_bytes": kp_bytes,
+                     "hbm_gbs": kp_bytes / (kp_ms * 1e-3) / 1e9 if kp_ms else None,
+                     "frac": (kp_bytes / (kp_ms * 1e-3) / 1e9) / float(peaks["hbm_gbs"]) if kp_ms else None},
+        "shape": f"B {B}, keys [{S}, {N}, {dk}] f32, {cfg.m} probes of {cfg.N // cfg.C} rows, top-k {cfg.k_max}"}}
+    W = torch.randn((B, cfg.d_B, cfg.d_A), generator=g, device=z.device) * 0.01
+    aux_ms, _ = timed(lambda: aux_losses_and_grads(alphas, indices, t["keys"], W, t["W_base"], soft_full))
+    out["aux_losses"] = {"ms": aux_ms, "shape": f"B {B}, k {cfg.k_max}, N {N}, W [{B}, {cfg.d_B}, {cfg.d_A}] f32"}
+    return out
 
 
 def C_ptr(event):
@@ -624,6 +696,8 @@ def main():
             "clocks": clocks, "e2e": e2e}
     if world == 1 and not args.no_key_cache:
         line["key_cache"] = time_key_cache(t, flush, peaks)
+    if world == 1 and not args.no_extras:
+        line.update(time_training_extras(w, t, flush, peaks))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_baseline(w, t, args.cpu_budget_s)
         line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}

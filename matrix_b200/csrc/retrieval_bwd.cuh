@@ -41,20 +41,34 @@ struct KeyGradArgs {
     float* g_keys;          // [S, N, d_k] or null
 };
 
-// One persistent CTA walks key tiles t = blockIdx.x, +gridDim.x, ...: stages
-// the tile's S x 32 rows (keys) and the G values of its rows, computes the
-// row norms, and accumulates A += G k̂ per (query, column) in registers
-// (thread t owns columns t, t + 256, ...); with g_keys, also writes the key
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(tc::smem_u32(dst)), "l"(src) : "memory");
+}
+// 4 bytes, or zeros when n == 0 (nothing is read then)
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, int n) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(tc::smem_u32(dst)), "l"(src), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// One persistent CTA walks the active key tiles t = blockIdx.x, +gridDim.x,
+// ... with two shared-memory buffers: the next tile's keys (S x 32 rows) and G
+// values ([row][QB], zero for queries past nb) stream in by cp.async while the
+// current tile is reduced.  Per tile: the row norms (one thread per (row,
+// aspect)), then A += G k̂ per (query, column) in registers: thread t owns
+// columns t, t + 256, ..., reads G four queries at a time (broadcast float4)
+// and issues QB FMAs per column and row.  With g_keys, also writes the key
 // gradient of its rows.  Partial sums per CTA; added in CTA order afterwards.
+// Needs d_k % 4 == 0 and d_k dividing 1024.
 template <int CPT, int QB>
 __global__ void __launch_bounds__(kKeyThreads) key_grad_pass_kernel(KeyGradArgs a) {
     pdl_enter();
     extern __shared__ __align__(16) float kg_sm[];
     const int S = a.S, d_k = a.d_k, cols = S * d_k;
-    float* kt = kg_sm;                                // [kKeyTile][cols]
-    float* gk = kt + kKeyTile * cols;                 // [kKeyTile][cols] (g_keys only)
-    float* gt = gk + (a.g_keys ? kKeyTile * cols : 0);// [QB][kKeyTile]
-    float* nrm = gt + QB * kKeyTile;                  // [kKeyTile][S]
+    float* ktb = kg_sm;                               // [2][kKeyTile][cols]
+    float* gtb = ktb + 2 * kKeyTile * cols;           // [2][kKeyTile][QB]
+    float* gk = gtb + 2 * QB * kKeyTile;              // [kKeyTile][cols] (g_keys only)
+    float* nrm = gk + (a.g_keys ? kKeyTile * cols : 0);// [kKeyTile][S]
     float* inv = nrm + kKeyTile * S;                  // [kKeyTile][S]
     float* dotk = inv + kKeyTile * S;                 // [kKeyTile][S]
     float* qs = dotk + kKeyTile * S;                  // [QB][cols] (g_keys only)
@@ -62,50 +76,84 @@ __global__ void __launch_bounds__(kKeyThreads) key_grad_pass_kernel(KeyGradArgs 
     if (a.g_keys)
         for (int i = tid; i < a.nb * cols; i += blockDim.x)
             qs[i] = a.qh[static_cast<int64_t>(a.b0) * cols + i] * a.w[(i % cols) / d_k];
+    // this thread's part of a tile load: float4 c4 of rows r0, r0 + rstep, ...
+    const int q4 = d_k / 4;
+    const int c4 = tid % q4, r0 = tid / q4, rstep = kKeyThreads / q4;
+    int col_s[CPT];
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) col_s[c] = (tid + c * kKeyThreads) / d_k;
+    auto next_active = [&](int64_t t) {
+        while (t < a.ntiles && a.tile_on && !a.tile_on[t]) t += gridDim.x;
+        return t;
+    };
+    auto issue = [&](int64_t t, int buf) {
+        const int64_t row0 = t * kKeyTile;
+        const int rows = static_cast<int>(a.N - row0 < kKeyTile ? a.N - row0 : kKeyTile);
+        float* kt = ktb + buf * kKeyTile * cols;
+        for (int s = 0; s < S; ++s) {
+            const float4* src = reinterpret_cast<const float4*>(a.keys + (static_cast<int64_t>(s) * a.N + row0) * d_k);
+            for (int r = r0; r < rows; r += rstep) cp_async16(kt + r * cols + s * d_k + 4 * c4, src + r * q4 + c4);
+        }
+        float* gt = gtb + buf * QB * kKeyTile;
+        for (int i = tid; i < QB * kKeyTile; i += blockDim.x) {
+            const int b = i / kKeyTile, r = i - b * kKeyTile;
+            const bool in = r < rows && b < a.nb;
+            cp_async4(gt + r * QB + b, in ? a.G + static_cast<int64_t>(a.b0 + b) * a.N + row0 + r : a.G, in ? 4 : 0);
+        }
+    };
     float acc[CPT][QB];
 #pragma unroll
     for (int c = 0; c < CPT; ++c)
 #pragma unroll
         for (int b = 0; b < QB; ++b) acc[c][b] = 0.f;
-    for (int64_t t = blockIdx.x; t < a.ntiles; t += gridDim.x) {
-        if (a.tile_on && !a.tile_on[t]) continue;
+    int64_t t = next_active(blockIdx.x);
+    if (t < a.ntiles) issue(t, 0);
+    cp_async_commit();
+    int cur = 0;
+    while (t < a.ntiles) {
+        const int64_t tn = next_active(t + gridDim.x);
+        if (tn < a.ntiles) issue(tn, cur ^ 1);
+        cp_async_commit();
+        cp_async_wait1();          // this thread's copies of tile t are done
+        __syncthreads();           // everyone's are
         const int64_t row0 = t * kKeyTile;
         const int rows = static_cast<int>(a.N - row0 < kKeyTile ? a.N - row0 : kKeyTile);
-        __syncthreads();   // the previous tile is consumed
-        // keys: per aspect a contiguous block of rows * d_k floats (d_k % 4 == 0)
-        const int q4 = d_k / 4;
-        for (int i = tid; i < S * rows * q4; i += blockDim.x) {
-            const int s = i / (rows * q4), rem = i - s * rows * q4, r = rem / q4, c4 = rem - r * q4;
-            const float4 v = __ldg(reinterpret_cast<const float4*>(a.keys + (static_cast<int64_t>(s) * a.N + row0 + r) * d_k) + c4);
-            *reinterpret_cast<float4*>(kt + r * cols + s * d_k + 4 * c4) = v;
-        }
-        for (int i = tid; i < a.nb * kKeyTile; i += blockDim.x) {
-            const int b = i / kKeyTile, r = i - b * kKeyTile;
-            gt[b * kKeyTile + r] = r < rows ? a.G[static_cast<int64_t>(a.b0 + b) * a.N + row0 + r] : 0.f;
-        }
-        __syncthreads();
-        for (int p = warp; p < rows * S; p += nwarps) {
+        const float* kt = ktb + cur * kKeyTile * cols;
+        const float* gt = gtb + cur * QB * kKeyTile;
+        // norms: one thread per (row, aspect); each starts at a different float4
+        // of the row so that the threads of a warp spread over the banks
+        for (int p = tid; p < rows * S; p += blockDim.x) {
             const int r = p / S, s = p - r * S;
-            const float* kr = kt + r * cols + s * d_k;
-            float ss = 0.f;
-            for (int d = lane; d < d_k; d += 32) ss = fmaf(kr[d], kr[d], ss);
-            ss = warp_sum(ss);
-            if (lane == 0) {
-                const float n = sqrtf(ss);
-                nrm[r * S + s] = n;
-                inv[r * S + s] = 1.f / (n + 1e-8f);
+            const float4* kr = reinterpret_cast<const float4*>(kt + r * cols + s * d_k);
+            float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+            for (int i = 0; i < q4; ++i) {
+                const float4 v = kr[(i + p) % q4];
+                s0 = fmaf(v.x, v.x, s0);
+                s1 = fmaf(v.y, v.y, s1);
+                s2 = fmaf(v.z, v.z, s2);
+                s3 = fmaf(v.w, v.w, s3);
             }
+            const float n = sqrtf((s0 + s1) + (s2 + s3));
+            nrm[r * S + s] = n;
+            inv[r * S + s] = 1.f / (n + 1e-8f);
         }
         __syncthreads();
+#pragma unroll 4
         for (int r = 0; r < rows; ++r) {
+            const float4* gr = reinterpret_cast<const float4*>(gt + r * QB);
 #pragma unroll
             for (int c = 0; c < CPT; ++c) {
                 const int col = tid + c * kKeyThreads;
-                if (col < cols) {
-                    const float kh = kt[r * cols + col] * inv[r * S + col / d_k];
+                if (CPT == 1 || col < cols) {
+                    const float kh = kt[r * cols + col] * inv[r * S + col_s[c]];
 #pragma unroll
-                    for (int b = 0; b < QB; ++b)
-                        if (b < a.nb) acc[c][b] = fmaf(gt[b * kKeyTile + r], kh, acc[c][b]);
+                    for (int q = 0; q < QB / 4; ++q) {
+                        const float4 g = gr[q];
+                        acc[c][4 * q] = fmaf(g.x, kh, acc[c][4 * q]);
+                        acc[c][4 * q + 1] = fmaf(g.y, kh, acc[c][4 * q + 1]);
+                        acc[c][4 * q + 2] = fmaf(g.z, kh, acc[c][4 * q + 2]);
+                        acc[c][4 * q + 3] = fmaf(g.w, kh, acc[c][4 * q + 3]);
+                    }
                 }
             }
         }
@@ -114,7 +162,7 @@ __global__ void __launch_bounds__(kKeyThreads) key_grad_pass_kernel(KeyGradArgs 
             for (int i = tid; i < rows * cols; i += blockDim.x) {
                 const int r = i / cols, col = i - r * cols;
                 float g = 0.f;
-                for (int b = 0; b < a.nb; ++b) g = fmaf(gt[b * kKeyTile + r], qs[b * cols + col], g);
+                for (int b = 0; b < a.nb; ++b) g = fmaf(gt[r * QB + b], qs[b * cols + col], g);
                 gk[i] = g;
             }
             __syncthreads();
@@ -134,6 +182,9 @@ __global__ void __launch_bounds__(kKeyThreads) key_grad_pass_kernel(KeyGradArgs 
                 a.g_keys[(static_cast<int64_t>(s) * a.N + row0 + r) * d_k + d] = gk[i] * iv - kt[i] * coef;
             }
         }
+        __syncthreads();           // buffer cur is free for the tile after next
+        t = tn;
+        cur ^= 1;
     }
     float* out = a.partial + static_cast<int64_t>(blockIdx.x) * a.nb * cols;
 #pragma unroll
@@ -148,7 +199,7 @@ __global__ void __launch_bounds__(kKeyThreads) key_grad_pass_kernel(KeyGradArgs 
 
 __host__ inline size_t key_grad_smem(int S, int d_k, int QB, bool g_keys) {
     const size_t cols = static_cast<size_t>(S) * d_k;
-    return (kKeyTile * cols * (g_keys ? 2 : 1) + static_cast<size_t>(QB) * kKeyTile + 3 * kKeyTile * S +
+    return (kKeyTile * cols * (g_keys ? 3 : 2) + 2 * static_cast<size_t>(QB) * kKeyTile + 3 * kKeyTile * S +
             (g_keys ? static_cast<size_t>(QB) * cols : 0)) * sizeof(float);
 }
 
@@ -177,9 +228,23 @@ __global__ void __launch_bounds__(256) soft_dot_kernel(const float* __restrict__
     __shared__ float red[33];
     const int b = blockIdx.y;
     const int64_t n0 = static_cast<int64_t>(blockIdx.x) * kSoftChunk;
+    const int64_t n1 = n0 + kSoftChunk < N ? n0 + kSoftChunk : N;
     float acc = 0.f;
-    for (int64_t n = n0 + threadIdx.x; n < N && n < n0 + kSoftChunk; n += blockDim.x)
-        acc = fmaf(g_soft[static_cast<int64_t>(b) * N + n], soft[static_cast<int64_t>(b) * N + n], acc);
+    if ((N & 3) == 0) {
+        // 16-byte rows (N % 4 == 0): float4 loads
+        const float4* s4 = reinterpret_cast<const float4*>(soft + static_cast<int64_t>(b) * N);
+        const float4* g4 = reinterpret_cast<const float4*>(g_soft + static_cast<int64_t>(b) * N);
+        for (int64_t n = n0 / 4 + threadIdx.x; n < n1 / 4; n += blockDim.x) {
+            const float4 sv = s4[n], gv = g4[n];
+            acc = fmaf(gv.x, sv.x, acc);
+            acc = fmaf(gv.y, sv.y, acc);
+            acc = fmaf(gv.z, sv.z, acc);
+            acc = fmaf(gv.w, sv.w, acc);
+        }
+    } else {
+        for (int64_t n = n0 + threadIdx.x; n < n1; n += blockDim.x)
+            acc = fmaf(g_soft[static_cast<int64_t>(b) * N + n], soft[static_cast<int64_t>(b) * N + n], acc);
+    }
     acc = block_reduce(acc, false, red);
     if (threadIdx.x == 0) part[static_cast<int64_t>(b) * gridDim.x + blockIdx.x] = acc;
 }
@@ -199,9 +264,21 @@ __global__ void __launch_bounds__(256) soft_grad_kernel(const float* __restrict_
     __syncthreads();
     const float dot = s_dot;
     const int64_t n0 = static_cast<int64_t>(blockIdx.x) * kSoftChunk;
-    for (int64_t n = n0 + threadIdx.x; n < N && n < n0 + kSoftChunk; n += blockDim.x) {
-        const int64_t i = static_cast<int64_t>(b) * N + n;
-        G[i] = soft[i] * (g_soft[i] - dot) * invT;
+    const int64_t n1 = n0 + kSoftChunk < N ? n0 + kSoftChunk : N;
+    if ((N & 3) == 0) {
+        const float4* s4 = reinterpret_cast<const float4*>(soft + static_cast<int64_t>(b) * N);
+        const float4* g4 = reinterpret_cast<const float4*>(g_soft + static_cast<int64_t>(b) * N);
+        float4* G4 = reinterpret_cast<float4*>(G + static_cast<int64_t>(b) * N);
+        for (int64_t n = n0 / 4 + threadIdx.x; n < n1 / 4; n += blockDim.x) {
+            const float4 sv = s4[n], gv = g4[n];
+            G4[n] = make_float4(sv.x * (gv.x - dot) * invT, sv.y * (gv.y - dot) * invT,
+                                sv.z * (gv.z - dot) * invT, sv.w * (gv.w - dot) * invT);
+        }
+    } else {
+        for (int64_t n = n0 + threadIdx.x; n < n1; n += blockDim.x) {
+            const int64_t i = static_cast<int64_t>(b) * N + n;
+            G[i] = soft[i] * (g_soft[i] - dot) * invT;
+        }
     }
 }
 
@@ -227,7 +304,7 @@ struct SelGradArgs {
     uint32_t* status;
 };
 
-__global__ void __launch_bounds__(256) sel_grad_kernel(SelGradArgs a) {
+__global__ void __launch_bounds__(1024) sel_grad_kernel(SelGradArgs a) {
     pdl_enter();
     __shared__ int64_t s_lo[kMaxK + 1], s_base[kMaxK + 1];
     __shared__ float red[33];
@@ -348,6 +425,31 @@ __global__ void unweighted_queries_kernel(const float* __restrict__ q, const flo
     }
 }
 
+// First level of A = Σ_CTA partial: group g of kPartGroups adds the partials
+// [P*g/G, P*(g+1)/G) of every (query, column) in CTA order, 4 loads in flight
+// per thread.  Grid (ceil(nb*cols/256), kPartGroups).
+constexpr int kPartGroups = 16;
+__global__ void __launch_bounds__(256) partial_reduce_kernel(const float* __restrict__ partial, int nparts,
+                                                            int64_t width, float* __restrict__ out) {
+    pdl_enter();
+    const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (e >= width) return;
+    const int g = blockIdx.y;
+    const int p0 = static_cast<int>(static_cast<int64_t>(nparts) * g / kPartGroups);
+    const int p1 = static_cast<int>(static_cast<int64_t>(nparts) * (g + 1) / kPartGroups);
+    float acc = 0.f;
+    int p = p0;
+    for (; p + 4 <= p1; p += 4) {
+        const float v0 = partial[static_cast<int64_t>(p) * width + e];
+        const float v1 = partial[static_cast<int64_t>(p + 1) * width + e];
+        const float v2 = partial[static_cast<int64_t>(p + 2) * width + e];
+        const float v3 = partial[static_cast<int64_t>(p + 3) * width + e];
+        acc = (((acc + v0) + v1) + v2) + v3;
+    }
+    for (; p < p1; ++p) acc += partial[static_cast<int64_t>(p) * width + e];
+    out[static_cast<int64_t>(g) * width + e] = acc;
+}
+
 // A = Σ_CTA partial (in CTA order), then per (query, aspect): g_q̂ = w_s A,
 // g_w partial q̂·A, and g_q = normalize-VJP(g_q̂) into gq [B, S*d_k].
 // One CTA per (query, aspect), d_k threads rounded up to a warp multiple.
@@ -449,6 +551,7 @@ struct BwdWorkspace {
     float* G;            // [B, N]
     float* partial;      // [grid, min(B, 32), S*d_k]
     float* gq;           // [B, S*d_k]
+    float* part2;        // [kPartGroups, min(B, 32), S*d_k]
     float* qh;           // [B, S*d_k] normalised queries, unweighted (key gradient)
     float* ws;           // [S] softmax(aspect_weights) (key gradient)
     float* gw_part;      // [B, S]
@@ -478,6 +581,7 @@ static BwdWorkspace carve_bwd(void* base, const DwaRetrieveDims& d, bool ivf) {
     w.G = c.take<float>(static_cast<size_t>(d.B) * d.N);
     w.partial = c.take<float>(static_cast<size_t>(w.grid) * std::min(d.B, kBwdMaxQ) * cols);
     w.gq = c.take<float>(static_cast<size_t>(d.B) * cols);
+    w.part2 = c.take<float>(static_cast<size_t>(kPartGroups) * std::min(d.B, kBwdMaxQ) * cols);
     w.qh = c.take<float>(static_cast<size_t>(d.B) * cols);
     w.ws = c.take<float>(static_cast<size_t>(d.S));
     w.gw_part = c.take<float>(static_cast<size_t>(d.B) * d.S);
@@ -492,7 +596,8 @@ static BwdWorkspace carve_bwd(void* base, const DwaRetrieveDims& d, bool ivf) {
 static int check_bwd(const DwaRetrieveDims* d, int use_ivf) {
     int rc = check_ret(d, use_ivf);
     if (rc) return rc;
-    if (d->d_k % 4 != 0) return fail(DWA_ERR_UNSUPPORTED, "retrieval VJP needs d_k % 4 == 0");
+    if (d->d_k % 4 != 0 || 1024 % d->d_k != 0)
+        return fail(DWA_ERR_UNSUPPORTED, "retrieval VJP needs d_k % 4 == 0 and d_k dividing 1024");
     if (d->S * d->d_k > 4 * kKeyThreads) return fail(DWA_ERR_UNSUPPORTED, "retrieval VJP needs S*d_k <= 1024");
     return DWA_OK;
 }
@@ -569,7 +674,7 @@ extern "C" int dwa_retrieve_bwd(void* stream, const DwaRetrieveDims* dims, int u
         sa.K_cap = f.K_cap; sa.N = d.N; sa.k = d.k; sa.T = d.T; sa.is_warmup = is_warmup;
         sa.lambda_val = lambda_val; sa.tau = tau; sa.alphas = alphas; sa.indices = indices;
         sa.g_alphas = g_alphas; sa.row_lo = 0; sa.G = w.G; sa.gtau = w.gtau; sa.status = f.status;
-        DWA_TIMED("sel_grad", st, launch_pdl(sel_grad_kernel, d.B, 256, 0, st, sa));
+        DWA_TIMED("sel_grad", st, launch_pdl(sel_grad_kernel, d.B, 1024, 0, st, sa));
         DWA_LAUNCH_CHECK("sel_grad_kernel");
         ++g_launches_total;
     } else {
@@ -609,12 +714,24 @@ extern "C" int dwa_retrieve_bwd(void* stream, const DwaRetrieveDims* dims, int u
         else if (cpt == 2) fn = qb == 8 ? key_grad_pass_kernel<2, 8> : qb == 16 ? key_grad_pass_kernel<2, 16> : key_grad_pass_kernel<2, 32>;
         else fn = qb == 8 ? key_grad_pass_kernel<4, 8> : key_grad_pass_kernel<4, 16>;
         DWA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm)));
-        DWA_TIMED("key_grad", st, launch_pdl(fn, w.grid, kKeyThreads, sm, st, ka));
+        // one wave of persistent CTAs (at most the grid the partials were sized for)
+        int occ = 1, dv = 0, sms = 148;
+        DWA_CUDA_TRY(cudaGetDevice(&dv));
+        DWA_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dv));
+        DWA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kKeyThreads, sm));
+        const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(
+            {static_cast<int64_t>(w.grid), static_cast<int64_t>(std::max(occ, 1)) * sms, ntiles})));
+        DWA_TIMED("key_grad", st, launch_pdl(fn, grid, kKeyThreads, sm, st, ka));
         DWA_LAUNCH_CHECK("key_grad_pass_kernel");
         ++g_launches_total;
         // 5. the queries' gradients of this pass
+        const int64_t width = static_cast<int64_t>(nb) * cols;
+        launch_pdl(partial_reduce_kernel, dim3(static_cast<unsigned>((width + 255) / 256), kPartGroups), 256, 0, st,
+                   w.partial, grid, width, w.part2);
+        DWA_LAUNCH_CHECK("partial_reduce_kernel");
+        ++g_launches_total;
         const int qthreads = (d.d_k + 31) / 32 * 32;
-        launch_pdl(query_grad_kernel, dim3(nb, d.S), qthreads, 0, st, w.partial, w.grid, nb, b0, f.q,
+        launch_pdl(query_grad_kernel, dim3(nb, d.S), qthreads, 0, st, w.part2, kPartGroups, nb, b0, f.q,
                    aspect_weights, d.S, d.d_k, w.gq, w.gw_part);
         DWA_LAUNCH_CHECK("query_grad_kernel");
         ++g_launches_total;
