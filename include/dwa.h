@@ -257,6 +257,33 @@ DWA_API int dwa_retrieve_bwd(void* stream, const DwaRetrieveDims* dims, int use_
                              void* workspace, size_t workspace_bytes);
 
 /* ---------------------------------------------------------------------------
+ * Peer access to a row-sharded pool (one process per GPU, one node).  Replaces
+ * _distributed_gather (src/dwa/model.py:16-47), which all-reduces B*k*D values
+ * over the model axis, by direct reads of the owning rank's rows.
+ *   dwa_ipc_handle: the CUDA IPC handle (dwa_ipc_handle_bytes() bytes) of the
+ *     allocation holding ptr, and ptr's byte offset in it;
+ *   dwa_ipc_open / dwa_ipc_close: map / unmap a peer's handle (+ offset);
+ *   dwa_gather_rows: out[i, :] = pool row indices[i] for i < n, read from the
+ *     shard that holds it (plain 16-byte loads, NVLink for peers' rows); rows
+ *     outside [row_lo[0], row_lo[world]) set DWA_STATUS_BAD_ROW_INDEX in the
+ *     workspace's status word and come out as zeros.  D * element size must be
+ *     a multiple of 16 bytes.
+ * ------------------------------------------------------------------------- */
+typedef struct DwaPoolShards {
+    int32_t world;               /* <= 16 */
+    const void* const* bases;    /* host array [world]: device pointer of rank r's first row */
+    const int64_t* row_lo;       /* host array [world + 1]: rank r holds global rows [row_lo[r], row_lo[r+1]) */
+} DwaPoolShards;
+DWA_API size_t dwa_ipc_handle_bytes(void);
+DWA_API int dwa_ipc_handle(const void* ptr, void* handle, int64_t* offset);
+DWA_API int dwa_ipc_open(const void* handle, int64_t offset, void** ptr);
+DWA_API int dwa_ipc_close(void* ptr, int64_t offset);
+DWA_API size_t dwa_gather_rows_workspace_bytes(void);
+DWA_API int dwa_gather_rows(void* stream, int n, int64_t D, int dtype, const int32_t* indices,
+                            const DwaPoolShards* shards, void* out, void* workspace,
+                            size_t workspace_bytes);
+
+/* ---------------------------------------------------------------------------
  * Auxiliary losses.  Replaces aux_losses (src/dwa/losses.py:9-73) and its
  * jax.grad: from the forward's alphas [B,k], indices [B,k], the key cache
  * [S,N,d_k], the assembled W [B,d_B,d_A] f32, W_base [d_B,d_A] and the

@@ -52,6 +52,10 @@ class Shard(C.Structure):
     _fields_ = [("row_lo", C.c_int64), ("n_global", C.c_int64)]
 
 
+class PoolShards(C.Structure):
+    _fields_ = [("world", C.c_int32), ("bases", C.POINTER(C.c_void_p)), ("row_lo", C.POINTER(C.c_int64))]
+
+
 class AuxDims(C.Structure):
     _fields_ = [("B", C.c_int32), ("k", C.c_int32), ("S", C.c_int32), ("d_k", C.c_int32),
                 ("d_B", C.c_int32), ("d_A", C.c_int32), ("N", C.c_int64)]
@@ -96,6 +100,12 @@ _SIGNATURES = {
     "dwa_key_cache": (C.c_int, [_P, C.POINTER(KeyCacheDims), _P, _P, _P, _P, C.c_size_t]),
     "dwa_centroid_ema": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int64, _P, _P, C.c_float, _P, _P,
                                    C.c_size_t]),
+    "dwa_ipc_handle_bytes": (C.c_size_t, []),
+    "dwa_ipc_handle": (C.c_int, [_P, _P, C.POINTER(C.c_int64)]),
+    "dwa_ipc_open": (C.c_int, [_P, C.c_int64, C.POINTER(C.c_void_p)]),
+    "dwa_ipc_close": (C.c_int, [_P, C.c_int64]),
+    "dwa_gather_rows_workspace_bytes": (C.c_size_t, []),
+    "dwa_gather_rows": (C.c_int, [_P, C.c_int, C.c_int64, C.c_int, _P, C.POINTER(PoolShards), _P, _P, C.c_size_t]),
     "dwa_aux_losses_workspace_bytes": (C.c_size_t, [C.POINTER(AuxDims)]),
     "dwa_aux_losses": (C.c_int, [_P, C.POINTER(AuxDims), C.POINTER(AuxWeights), _P, _P, _P, _P, _P, _P, _P,
                                  _P, _P, _P, _P, _P, _P, C.c_size_t]),

@@ -178,3 +178,86 @@ def test_two_nccl_ranks(tmp_path):
             sfs.append(got[f"sf_{is_warmup}_{lam}"])
         assert_close(np.concatenate(sfs, axis=1), rsf, TOL, name="soft_full")
         assert sum(hi - lo for lo, hi in shards) == cfg.N
+
+
+def _peer_rank(rank, world, port, out_dir):
+    """One rank of a row-sharded pool: map the peer's shard by IPC, gather the
+    winning rows of this rank's sequences from both shards, assemble them, and
+    return the rows' gradients to their owners (all-gather + sorted scatter)."""
+    import torch.distributed as dist
+    from datetime import timedelta
+    from matrix_b200.assembly import assemble_backward, assemble_forward
+    from matrix_b200.peer import PeerPool
+    from matrix_b200.pool_grad import scatter_pool_grad_gathered
+    from test_gpu_assembly import _setup
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=dev)
+    pp = None
+    try:
+        cfg, x, idx, alphas = _setup("bf16_small_like")
+        N, B = x.pool.shape[0], idx.shape[0]
+        bounds = [N * r // world for r in range(world + 1)]
+        lo, hi = bounds[rank], bounds[rank + 1]
+
+        def d(a, dt=None):
+            t = torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+            return t.to(dt) if dt is not None else t
+
+        local = d(x.pool[lo:hi], torch.bfloat16)
+        pp = PeerPool(local, bounds)
+        b0, b1 = B * rank // world, B * (rank + 1) // world      # this rank's sequences
+        rows = pp.gather(d(idx[b0:b1]))
+        h_A = d(x.h_A[b0:b1], torch.bfloat16)
+        args = (d(alphas[b0:b1]), h_A, d(x.W_base), d(x.b_base), torch.tensor(x.gamma).to(dev))
+        h_mid, W, W_act = assemble_forward(rows, *args, cfg.d_B, cfg.r, cfg.d_A)
+        g_rows = assemble_backward(rows, args[0], h_A, W_act, args[4], d(x.g_hmid[b0:b1], torch.bfloat16),
+                                   d(x.g_W[b0:b1]), cfg.d_B, cfg.r, cfg.d_A)[0]
+        g_pool = torch.zeros((hi - lo, x.pool.shape[1]), dtype=torch.float32, device=dev)
+        scatter_pool_grad_gathered(g_rows, d(idx[b0:b1]), g_pool, row_lo=lo, n_global=N)
+        torch.cuda.synchronize(dev)
+        np.savez(os.path.join(out_dir, f"peer{rank}.npz"), rows=rows.float().cpu().numpy(),
+                 h_mid=h_mid.float().cpu().numpy(), W=W.cpu().numpy(), g_pool=g_pool.cpu().numpy())
+        dist.barrier()
+    finally:
+        if pp is not None:
+            pp.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_two_ranks_peer_gather_and_sharded_assembly(tmp_path):
+    """Rows read over NVLink from the owning rank equal the single-device
+    gather; each rank's assembly of its sequences equals the single-device
+    assembly; the owners' scattered row gradients equal the single-device
+    pool gradient."""
+    import torch.multiprocessing as mp
+    from matrix_b200.assembly import assemble_backward, assemble_forward
+    from matrix_b200.pool_grad import scatter_pool_grad
+    from test_gpu_assembly import _setup
+    world = 2
+    mp.start_processes(_peer_rank, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    cfg, x, idx, alphas = _setup("bf16_small_like")
+    pool = _dev(x.pool).to(torch.bfloat16)
+    idx_t = _dev(idx)
+    h_A = _dev(x.h_A).to(torch.bfloat16)
+    args = (_dev(alphas), h_A, _dev(x.W_base), _dev(x.b_base), torch.tensor(x.gamma).cuda())
+    h_mid, W, W_act = assemble_forward(pool, *args, cfg.d_B, cfg.r, cfg.d_A, row_index=idx_t)
+    g_rows = assemble_backward(pool, args[0], h_A, W_act, args[4], _dev(x.g_hmid).to(torch.bfloat16),
+                               _dev(x.g_W), cfg.d_B, cfg.r, cfg.d_A, row_index=idx_t)[0]
+    g_pool = torch.zeros(pool.shape, dtype=torch.float32, device="cuda")
+    scatter_pool_grad(g_rows, idx_t, g_pool)
+    torch.cuda.synchronize()
+    B, N = idx.shape[0], x.pool.shape[0]
+    got = [np.load(tmp_path / f"peer{r}.npz") for r in range(world)]
+    np.testing.assert_array_equal(np.concatenate([g["rows"] for g in got]),
+                                  pool[idx_t.long()].float().cpu().numpy())
+    np.testing.assert_array_equal(np.concatenate([g["h_mid"] for g in got]), h_mid.float().cpu().numpy())
+    np.testing.assert_array_equal(np.concatenate([g["W"] for g in got]), W.cpu().numpy())
+    assert_close(np.concatenate([g["g_pool"] for g in got]), g_pool.cpu().numpy(), TOL, name="g_pool")
