@@ -52,6 +52,9 @@ def parse_args():
     ap.add_argument("--cpu-budget-s", type=float, default=20.0,
                     help="CPU seconds for the cpu_baseline sample (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sharded", action="store_true",
+                    help="row-shard the pool over the ranks (the medium / large configs): the "
+                         "workload's batch is the global batch, each rank holds 1/N of the rows")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip timing the retrieval VJP and the auxiliary losses")
@@ -144,6 +147,129 @@ class Step:
         return out
 
 
+# ------------------------------------------------- row-sharded workload ---
+def build_sharded_workload(w, device, rank, world, group, seed):
+    """Rank ``rank``'s part of a row-sharded pool: the rows ``[lo, hi)`` (whole
+    lists, balanced by rows) and their keys; the replicated parameters (same
+    seed on every rank, centroids = key rows at random indices, combined by an
+    all-reduce); this rank's ``w.batch / world`` sequences."""
+    import torch
+    from matrix_b200.assembly import compute_key_cache
+    from matrix_b200.sharded import shard_rows
+    from matrix_b200.synthetic import zipf_list_offsets
+    cfg = w.cfg
+    d, D, N, S, dk, C = cfg.d_A, cfg.D, cfg.N, cfg.S, cfg.d_k, cfg.C
+    if w.batch % world:
+        raise ValueError("the global batch must split evenly over the ranks")
+    rng = np.random.default_rng(seed)
+    off_np = (zipf_list_offsets(N, C, w.zipf, rng) if w.zipf else np.arange(C + 1, dtype=np.int64) * (N // C))
+    lo, hi = shard_rows(off_np, world)[rank]
+    bf = torch.bfloat16
+    g_rows = torch.Generator(device=device).manual_seed(seed + 1 + rank)     # this rank's pool rows
+    pool = torch.empty((hi - lo, D), dtype=bf, device=device)
+    for i in range(0, hi - lo, 16384):
+        pool[i:i + 16384].normal_(0.0, d ** -0.5, generator=g_rows)
+    g = torch.Generator(device=device).manual_seed(seed)                    # replicated parameters
+    key_proj = (torch.randn((S, D, dk), generator=g, device=device) * D ** -0.5).to(bf)
+    keys = compute_key_cache(pool, key_proj)
+    sizes = np.diff(off_np)
+    rows_c = off_np[:-1] + (rng.random(C) * sizes).astype(np.int64)
+    cent = torch.zeros((S, C, dk), device=device)
+    mine = np.nonzero((rows_c >= lo) & (rows_c < hi))[0]
+    if mine.size:
+        cent[:, torch.from_numpy(mine).to(device)] = keys[:, torch.from_numpy(rows_c[mine] - lo).to(device)]
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(cent, group=group)
+    Bp = w.batch // world
+    gs = torch.Generator(device=device).manual_seed(seed + 7919 * (rank + 1))  # this rank's sequences
+    t = dict(
+        pool=pool, keys=keys, row_lo=lo, row_hi=hi, list_offsets=torch.from_numpy(off_np).to(device),
+        max_list=int(sizes.max()), centroids=cent.contiguous(),
+        W_Q=torch.randn((S, dk, d), generator=g, device=device) * d ** -0.5,
+        aspect_weights=torch.zeros(S, device=device), tau=torch.zeros(1, device=device),
+        W_base=torch.randn((d, d), generator=g, device=device) * 0.01,
+        b_base=torch.zeros(d, device=device),
+        gamma=torch.full((1,), cfg.gamma_init, device=device),
+        lam=torch.full((1,), w.lambda_val, device=device),
+        h_A=torch.randn((Bp, w.seq, d), generator=gs, device=device).to(bf),
+    )
+    if w.backward:
+        t["g_hmid"] = (torch.randn((Bp, w.seq, d), generator=gs, device=device) * 0.1).to(bf)
+        t["g_W"] = torch.randn((Bp, d, d), generator=gs, device=device) * 1e-3
+        t["g_pool"] = torch.zeros((hi - lo, D), dtype=bf, device=device)
+    return t
+
+
+class ShardedStep:
+    """One step of a row-sharded pool on this rank: the sequence means of its
+    sequences, one all-gather of z, row-sharded retrieval (local top-k, one
+    all-gather of the summaries, merge), the winning rows of its sequences read
+    from the ranks that hold them (peer loads), their assembly and, with the
+    backward, the rows' gradients returned to their owners and the parameter
+    gradients all-reduced."""
+
+    def __init__(self, w, t, group, rank, world):
+        import torch
+        from matrix_b200 import _lib
+        from matrix_b200.peer import PeerPool
+        self.w, self.t, self.group, self.rank, self.world = w, t, group, rank, world
+        self.lib = _lib.load()
+        dev = t["h_A"].device
+        Bp = w.batch // world
+        self.b0, self.b1 = rank * Bp, (rank + 1) * Bp
+        self.z_local = torch.empty((Bp, w.cfg.d_A), dtype=torch.float32, device=dev)
+        self.z = torch.empty((w.batch, w.cfg.d_A), dtype=torch.float32, device=dev)
+        bounds = None
+        if world > 1:
+            import torch.distributed as dist
+            lohi = [None] * world
+            dist.all_gather_object(lohi, (t["row_lo"], t["row_hi"]), group=group)
+            bounds = [lohi[0][0]] + [h for _, h in lohi]
+            self.peers = PeerPool(t["pool"], bounds, group)
+        else:
+            self.peers = PeerPool.from_shards([t["pool"]], [0, t["row_hi"]])
+
+    def __call__(self):
+        import torch
+        from matrix_b200 import _lib, runtime
+        from matrix_b200.assembly import assemble_backward, assemble_forward
+        from matrix_b200.pool_grad import scatter_pool_grad_gathered
+        from matrix_b200.sharded import RowShard, sharded_retrieve
+        w, t, cfg = self.w, self.t, self.w.cfg
+        dev = t["h_A"].device
+        rc = self.lib.dwa_sequence_mean(runtime.stream_of(dev), self.z_local.shape[0], w.seq, cfg.d_A, 1,
+                                        runtime.ptr(t["h_A"]), runtime.ptr(self.z_local))
+        _lib.check(rc, "dwa_sequence_mean")
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_gather_into_tensor(self.z, self.z_local, group=self.group)
+            z = self.z
+        else:
+            z = self.z_local
+        alphas, indices, soft = sharded_retrieve(
+            z, t["W_Q"], t["aspect_weights"], t["tau"], t["centroids"], t["keys"], t["list_offsets"], t["lam"],
+            w.is_warmup, RowShard(t["row_lo"], t["row_hi"], cfg.N, self.group), k=cfg.k_max, m=cfg.m, T=cfg.T,
+            max_list=t["max_list"], want_soft_full=w.soft_full)
+        idx_mine = indices[self.b0:self.b1]
+        rows = self.peers.gather(idx_mine)
+        h_mid, W, W_act = assemble_forward(rows, alphas[self.b0:self.b1], t["h_A"], t["W_base"], t["b_base"],
+                                           t["gamma"], cfg.d_B, cfg.r, cfg.d_A)
+        out = dict(alphas=alphas, indices=indices, soft_full=soft, h_mid=h_mid, W=W)
+        if w.backward:
+            g = assemble_backward(rows, alphas[self.b0:self.b1], t["h_A"], W_act, t["gamma"], t["g_hmid"],
+                                  t["g_W"], cfg.d_B, cfg.r, cfg.d_A)
+            out.update(zip(("g_rows", "g_alpha", "g_hA", "g_W_base", "g_b_base", "g_gamma"), g))
+            scatter_pool_grad_gathered(g[0], idx_mine, t["g_pool"], row_lo=t["row_lo"], n_global=cfg.N,
+                                       group=self.group)
+            if self.world > 1:
+                import torch.distributed as dist
+                flat = torch.cat([out["g_W_base"].reshape(-1), out["g_b_base"], out["g_gamma"]])
+                dist.all_reduce(flat, group=self.group)
+                out["g_params"] = flat
+        return out
+
+
 # ------------------------------------------------------ roofline numbers ---
 def profiled_traffic(kernel, w):
     """DRAM bytes (read + write) per launch of `kernel` at workload `w`, from
@@ -168,23 +294,28 @@ def profiled_traffic(kernel, w):
     return None
 
 
-def kernel_work(w, name):
+def kernel_work(w, name, n_rows=None, seqs=None):
     """Algorithmic bytes (HBM-bound kernels) or flops (tensor kernels) of one
-    launch of `name` on workload w; returns (bound, amount)."""
+    launch of `name` on workload w; returns (bound, amount).  A rank of a
+    row-sharded pool scores ``n_rows`` rows for all ``w.batch`` queries and
+    assembles ``seqs`` sequences."""
     c = w.cfg
     B, T, d, k, r, S, dk, N = w.batch, w.seq, c.d_A, c.k_max, c.r, c.S, c.d_k, c.N
+    N = N if n_rows is None else n_rows
+    Ba = B if seqs is None else seqs
     kr = k * r
     table = {
         "full_scores": ("hbm", 4 * (S * N * dk + B * N)),
-        "fine": ("hbm", 4 * (B * S * min(c.m, c.C) * (N // c.C) * dk)),
+        "fine": ("hbm", 4 * (B * S * min(c.m, c.C) * (c.N // c.C) * dk)),
         "softmax_apply": ("hbm", 8 * B * N),
-        "prep_factors": ("hbm", B * k * (d * r + r * d) * 2 * 2),
-        "gemm_W": ("tensor", 2 * B * d * d * kr),
-        "gemm_apply": ("tensor", 2 * B * T * d * d),
-        "gemm_G": ("tensor", 2 * B * T * d * d),
-        "gemm_gh": ("tensor", 2 * B * T * d * d),
-        "gemm_P": ("tensor", 2 * B * d * d * kr),
-        "gemm_Q": ("tensor", 2 * B * d * d * kr),
+        "prep_factors": ("hbm", Ba * k * (d * r + r * d) * 2 * 2),
+        "gemm_W": ("tensor", 2 * Ba * d * d * kr),
+        "gemm_apply": ("tensor", 2 * Ba * T * d * d),
+        "gemm_G": ("tensor", 2 * Ba * T * d * d),
+        "gemm_gh": ("tensor", 2 * Ba * T * d * d),
+        "gemm_P": ("tensor", 2 * Ba * d * d * kr),
+        "gemm_Q": ("tensor", 2 * Ba * d * d * kr),
+        "gather_rows": ("hbm", 2 * Ba * k * c.D * (2 if c.bf16_pool else 4)),
     }
     return table.get(name, ("hbm", None))
 
@@ -192,7 +323,7 @@ def kernel_work(w, name):
 KERNELS = ["seq_mean", "query", "query_norm", "coarse", "topm", "full_scores", "fine", "select",
            "softmax_stats",
            "softmax_apply", "prep_factors", "prep_bias", "gemm_W", "gemm_apply", "gemm_G",
-           "gemm_gh", "gemm_P", "gemm_Q", "colsum", "finalize", "bias_grad"]
+           "gemm_gh", "gemm_P", "gemm_Q", "colsum", "finalize", "bias_grad", "merge", "gather_rows"]
 
 
 def profile_kernels(step, flush, n=5):
@@ -504,8 +635,15 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
         group = dist.group.WORLD
 
-    t = build_device_workload(w, dev, args.seed + rank)
-    step = Step(w, t, group)
+    if args.sharded:
+        # a manual mode for the configs whose pool is row-sharded; the driver's
+        # runs use the data-parallel default
+        args.no_e2e = args.no_extras = args.no_key_cache = args.no_cpu_baseline = True
+        t = build_sharded_workload(w, dev, rank, world, group, args.seed)
+        step = ShardedStep(w, t, group, rank, world)
+    else:
+        t = build_device_workload(w, dev, args.seed + rank)
+        step = Step(w, t, group)
     flush_buf = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     flush_sink = torch.empty((), dtype=torch.float32, device=dev)
 
@@ -594,7 +732,8 @@ def main():
     total_ms = float(tmax.item())
     ms_per_step = total_ms / args.steps
     tokens = w.batch * w.seq
-    value = tokens * world / (ms_per_step / 1e3)
+    # data parallel: w.batch sequences per rank; row-sharded: w.batch in all
+    value = tokens * (1 if args.sharded else world) / (ms_per_step / 1e3)
 
     # ---- end to end through the public API with pinned host buffers ----
     e2e = None
@@ -663,7 +802,10 @@ def main():
 
     # ---- roofline of the dominant kernel ----
     peaks, peak_src = load_peaks()
-    bound, work = kernel_work(w, dominant)
+    if args.sharded:
+        bound, work = kernel_work(w, dominant, n_rows=t["row_hi"] - t["row_lo"], seqs=w.batch // world)
+    else:
+        bound, work = kernel_work(w, dominant)
     kms = float(np.mean(kern_ms))
     roof = None
     if work is not None:
@@ -675,22 +817,30 @@ def main():
             ach = work / (kms / 1e3) / 1e12
             peak = float(peaks["bf16_tflops"])
             unit = "TFLOP/s"
-        traffic = profiled_traffic(dominant, w)
+        traffic = None if args.sharded else profiled_traffic(dominant, w)
         roof = {"kernel": dominant, "bound": bound, "achieved": ach, "peak": peak, "unit": unit,
                 "frac": ach / peak, "traffic": traffic, "peak_source": peak_src,
                 "algorithmic_per_launch": work, "launch_ms": kms, "timed_in": kern_src}
 
+    if args.sharded:
+        step_desc = ("CUDA graph: seq_mean + all-gather of z + dwa_retrieve_local + all-gather of summaries + "
+                     "dwa_retrieve_merge + dwa_gather_rows (peer loads) + dwa_assemble_fwd"
+                     + (" + dwa_assemble_bwd + pool-row gradient all-gather and scatter + NCCL all_reduce of "
+                        "parameter grads" if w.backward else ""))
+    else:
+        step_desc = ("CUDA graph: seq_mean + dwa_retrieve + dwa_assemble_fwd + dwa_assemble_bwd"
+                     + (" + NCCL all_reduce of parameter grads" if world > 1 else ""))
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic",
-            "config": {"workload": w.name, "note": w.note, "global_batch": w.batch * world,
-                       "seq_len": w.seq, "parallelism": f"dp{world}",
+            "higher_is_better": True, "scaling": "strong" if args.sharded else "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": w.name, "note": w.note,
+                       "global_batch": w.batch if args.sharded else w.batch * world,
+                       "seq_len": w.seq, "parallelism": f"rows{world}" if args.sharded else f"dp{world}",
                        "mode": "warmup" if w.is_warmup else f"gate lambda={w.lambda_val}",
                        "soft_full": w.soft_full, "backward": w.backward,
                        "l2": "flushed between steps (512 MB write, then 256 MB read)",
-                       "step": "CUDA graph: seq_mean + dwa_retrieve + dwa_assemble_fwd + dwa_assemble_bwd"
-                               + (" + NCCL all_reduce of parameter grads" if world > 1 else "")},
+                       "step": step_desc},
             "value_per_gpu": value / world, "roofline": roof,
             "kernels_ms": breakdown, "kernels_start_ms": kstarts, "gpu_launches": int(launches_per_step * args.steps),
             "clocks": clocks, "e2e": e2e}
