@@ -49,7 +49,7 @@ constexpr size_t kSmemLimit = 227 * 1024 - 4096;   // leaves room for static sha
 
 // Rows per thread for a query block of QB queries (registers: R*16 key floats,
 // R*QB dot and score accumulators).
-template <int QB> constexpr int rows_per_thread() { return QB <= 8 ? 4 : 2; }
+template <int QB> constexpr int rows_per_thread() { return 4; }
 template <int QB> constexpr int tile_rows() { return 32 * rows_per_thread<QB>() * CONSUMER_WARPS; }
 template <int QB> constexpr uint32_t slot_bytes() { return tile_rows<QB>() * KQ * 4; }
 
@@ -171,6 +171,40 @@ __global__ void __launch_bounds__(THREADS, 1) key_scan_kernel(const __grid_const
                 }
                 const uint8_t* sp = ring + static_cast<size_t>(slot) * SLOT;
                 const float* qa = qt + s * 64 + kq * KQ;   // query j of this quarter: qa + j*S*64
+                if constexpr (J > 8) {
+                    // 16 query chains: the key registers hold one float4 chunk of
+                    // the R rows at a time (the accumulators take the rest), and
+                    // the slot is released after the last chunk
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        float4 kc[R];
+#pragma unroll
+                        for (int i = 0; i < R; ++i) {
+                            const int rr = rbase + 32 * i;
+                            kc[i] = *reinterpret_cast<const float4*>(sp + rr * (KQ * 4) + ((c ^ ((rr >> 1) & 3)) << 4));
+                        }
+#pragma unroll
+                        for (int i = 0; i < R; ++i) {
+                            nrm[i] = fmaf(kc[i].x, kc[i].x, nrm[i]);
+                            nrm[i] = fmaf(kc[i].y, kc[i].y, nrm[i]);
+                            nrm[i] = fmaf(kc[i].z, kc[i].z, nrm[i]);
+                            nrm[i] = fmaf(kc[i].w, kc[i].w, nrm[i]);
+                        }
+#pragma unroll
+                        for (int j = 0; j < J; ++j) {
+                            const float4 qv = *reinterpret_cast<const float4*>(qa + j * S * 64 + c * 4);
+#pragma unroll
+                            for (int i = 0; i < R; ++i) {
+                                dot[i][j] = fmaf(kc[i].x, qv.x, dot[i][j]);
+                                dot[i][j] = fmaf(kc[i].y, qv.y, dot[i][j]);
+                                dot[i][j] = fmaf(kc[i].z, qv.z, dot[i][j]);
+                                dot[i][j] = fmaf(kc[i].w, qv.w, dot[i][j]);
+                            }
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) kt::mbar_arrive(&empty[slot]);
+                } else {
                 float4 kv[R][4];
 #pragma unroll
                 for (int i = 0; i < R; ++i) {
@@ -201,6 +235,7 @@ __global__ void __launch_bounds__(THREADS, 1) key_scan_kernel(const __grid_const
                             dot[i][j] = fmaf(kv[i][c].w, qv.w, dot[i][j]);
                         }
                     }
+                }
                 }
                 if (kq == 3) {
 #pragma unroll
