@@ -257,6 +257,46 @@ DWA_API int dwa_retrieve_bwd(void* stream, const DwaRetrieveDims* dims, int use_
                              void* workspace, size_t workspace_bytes);
 
 /* ---------------------------------------------------------------------------
+ * Retrieval VJP over a row-sharded pool (the backward of dwa_retrieve_local +
+ * dwa_retrieve_merge): dims->N = the rank's rows, shard->row_lo its first
+ * global row; the same workspace (dwa_retrieve_bwd_local_workspace_bytes) goes
+ * to the three phases of one call.
+ *   phase 1 (dwa_retrieve_bwd_local1): part1 [B, k+3] = the scores of the
+ *     winners this rank holds (0 for the others), Σ raw over its candidates,
+ *     Σ g_soft·soft over its rows, its candidate count;
+ *   the caller sums part1 over the ranks (one all-reduce);
+ *   phase 2 (dwa_retrieve_bwd_local2): dL/ds on this rank's rows from the sums,
+ *     the key pass over them; part2 [B, S*d_k+1] = this rank's A and g_tau
+ *     share; its key gradient when g_pool_keys is non-NULL (B <= 32);
+ *   the caller sums part2 over the ranks (one all-reduce);
+ *   phase 3 (dwa_retrieve_bwd_finish): g_z, g_W_Q, g_aspect_weights, g_tau
+ *     (needs no rows: a rank that holds none passes zero partials to the sums
+ *     and runs only this phase, with dims->N = 1 and its own workspace).
+ * soft_full / g_soft_full are the rank's [B, N] slices; alphas, indices,
+ * g_alphas are the merged [B, k] values every rank holds.
+ * ------------------------------------------------------------------------- */
+DWA_API size_t dwa_retrieve_bwd_local_workspace_bytes(const DwaRetrieveDims* dims, int use_ivf);
+DWA_API int dwa_retrieve_bwd_local1(void* stream, const DwaRetrieveDims* dims, const DwaShard* shard,
+                                    int use_ivf, int is_warmup, const float* lambda_val, const void* z,
+                                    const float* W_Q, const float* aspect_weights, const float* tau,
+                                    const float* centroids, const int64_t* list_offsets,
+                                    const float* local_keys, const int32_t* indices,
+                                    const float* soft_full, const float* g_soft_full, float* part1,
+                                    void* workspace, size_t workspace_bytes);
+DWA_API int dwa_retrieve_bwd_local2(void* stream, const DwaRetrieveDims* dims, const DwaShard* shard,
+                                    int use_ivf, int is_warmup, const float* lambda_val, const float* tau,
+                                    const float* aspect_weights, const int64_t* list_offsets,
+                                    const float* local_keys, const float* alphas, const int32_t* indices,
+                                    const float* soft_full, const float* g_alphas,
+                                    const float* g_soft_full, const float* part1_sum, float* part2,
+                                    float* g_pool_keys, void* workspace, size_t workspace_bytes);
+DWA_API int dwa_retrieve_bwd_finish(void* stream, const DwaRetrieveDims* dims, int use_ivf, const void* z,
+                                    const float* W_Q, const float* aspect_weights,
+                                    const float* part2_sum, float* g_z, float* g_W_Q,
+                                    float* g_aspect_weights, float* g_tau, void* workspace,
+                                    size_t workspace_bytes);
+
+/* ---------------------------------------------------------------------------
  * Peer access to a row-sharded pool (one process per GPU, one node).  Replaces
  * _distributed_gather (src/dwa/model.py:16-47), which all-reduces B*k*D values
  * over the model axis, by direct reads of the owning rank's rows.

@@ -100,6 +100,13 @@ _SIGNATURES = {
     "dwa_key_cache": (C.c_int, [_P, C.POINTER(KeyCacheDims), _P, _P, _P, _P, C.c_size_t]),
     "dwa_centroid_ema": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int64, _P, _P, C.c_float, _P, _P,
                                    C.c_size_t]),
+    "dwa_retrieve_bwd_local_workspace_bytes": (C.c_size_t, [C.POINTER(RetrieveDims), C.c_int]),
+    "dwa_retrieve_bwd_local1": (C.c_int, [_P, C.POINTER(RetrieveDims), C.POINTER(Shard), C.c_int, C.c_int,
+                                          _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t]),
+    "dwa_retrieve_bwd_local2": (C.c_int, [_P, C.POINTER(RetrieveDims), C.POINTER(Shard), C.c_int, C.c_int,
+                                          _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t]),
+    "dwa_retrieve_bwd_finish": (C.c_int, [_P, C.POINTER(RetrieveDims), C.c_int, _P, _P, _P, _P, _P, _P, _P, _P,
+                                          _P, C.c_size_t]),
     "dwa_ipc_handle_bytes": (C.c_size_t, []),
     "dwa_ipc_handle": (C.c_int, [_P, _P, C.POINTER(C.c_int64)]),
     "dwa_ipc_open": (C.c_int, [_P, C.c_int64, C.POINTER(C.c_void_p)]),

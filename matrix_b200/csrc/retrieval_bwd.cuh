@@ -251,14 +251,14 @@ __global__ void __launch_bounds__(256) soft_dot_kernel(const float* __restrict__
 
 __global__ void __launch_bounds__(256) soft_grad_kernel(const float* __restrict__ soft,
                                                        const float* __restrict__ g_soft, int64_t N,
-                                                       const float* __restrict__ part, int nchunks,
+                                                       const float* __restrict__ part, int nchunks, int pstride,
                                                        float invT, float* __restrict__ G) {
     pdl_enter();
     __shared__ float s_dot;
     const int b = blockIdx.y;
     if (threadIdx.x == 0) {
         float d = 0.f;
-        for (int i = 0; i < nchunks; ++i) d += part[static_cast<int64_t>(b) * nchunks + i];
+        for (int i = 0; i < nchunks; ++i) d += part[static_cast<int64_t>(b) * pstride + i];
         s_dot = d;
     }
     __syncthreads();
@@ -453,7 +453,7 @@ __global__ void __launch_bounds__(256) partial_reduce_kernel(const float* __rest
 // A = Σ_CTA partial (in CTA order), then per (query, aspect): g_q̂ = w_s A,
 // g_w partial q̂·A, and g_q = normalize-VJP(g_q̂) into gq [B, S*d_k].
 // One CTA per (query, aspect), d_k threads rounded up to a warp multiple.
-__global__ void query_grad_kernel(const float* __restrict__ partial, int nparts, int nb, int b0,
+__global__ void query_grad_kernel(const float* __restrict__ partial, int nparts, int nb, int b0, int rstride,
                                   const float* __restrict__ q, const float* __restrict__ aspect_w, int S,
                                   int d_k, float* __restrict__ gq, float* __restrict__ gw_part) {
     pdl_enter();
@@ -462,7 +462,7 @@ __global__ void query_grad_kernel(const float* __restrict__ partial, int nparts,
     const int cols = S * d_k;
     float A = 0.f, qv = 0.f;
     if (d < d_k) {
-        for (int p = 0; p < nparts; ++p) A += partial[(static_cast<int64_t>(p) * nb + bl) * cols + s * d_k + d];
+        for (int p = 0; p < nparts; ++p) A += partial[(static_cast<int64_t>(p) * nb + bl) * rstride + s * d_k + d];
         qv = q[(static_cast<int64_t>(b) * S + s) * d_k + d];
     }
     float mx = -INFINITY;
@@ -515,7 +515,7 @@ __global__ void __launch_bounds__(128) wq_grad_kernel(const float* __restrict__ 
 // (softmax VJP of g_w = Σ_b gw_part) and g_tau = Σ_b gtau.
 __global__ void query_grad_finish_kernel(const float* __restrict__ gz_part, int nchunks, int B, int d_A,
                                          const float* __restrict__ gw_part, const float* __restrict__ aspect_w,
-                                         int S, const float* __restrict__ gtau, float* __restrict__ g_z,
+                                         int S, const float* __restrict__ gtau, int gtau_stride, float* __restrict__ g_z,
                                          float* __restrict__ g_aw, float* __restrict__ g_tau) {
     pdl_enter();
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -541,7 +541,7 @@ __global__ void query_grad_finish_kernel(const float* __restrict__ gz_part, int 
             g_aw[t] = (expf(aspect_w[t] - mx) / den) * (gw - wg);
         }
         float gt = 0.f;
-        for (int b = 0; b < B; ++b) gt += gtau[b];
+        for (int b = 0; b < B; ++b) gt += gtau[static_cast<int64_t>(b) * gtau_stride];
         g_tau[0] = gt;
     }
 }
@@ -662,7 +662,7 @@ extern "C" int dwa_retrieve_bwd(void* stream, const DwaRetrieveDims* dims, int u
         launch_pdl(soft_dot_kernel, dim3(nchunks, d.B), 256, 0, st, soft_full, g_soft_full, d.N, w.soft_part);
         DWA_LAUNCH_CHECK("soft_dot_kernel");
         launch_pdl(soft_grad_kernel, dim3(nchunks, d.B), 256, 0, st, soft_full, g_soft_full, d.N, w.soft_part,
-                   nchunks, 1.f / d.T, w.G);
+                   nchunks, nchunks, 1.f / d.T, w.G);
         DWA_LAUNCH_CHECK("soft_grad_kernel");
         g_launches_total += 2;
     } else {
@@ -731,7 +731,7 @@ extern "C" int dwa_retrieve_bwd(void* stream, const DwaRetrieveDims* dims, int u
         DWA_LAUNCH_CHECK("partial_reduce_kernel");
         ++g_launches_total;
         const int qthreads = (d.d_k + 31) / 32 * 32;
-        launch_pdl(query_grad_kernel, dim3(nb, d.S), qthreads, 0, st, w.part2, kPartGroups, nb, b0, f.q,
+        launch_pdl(query_grad_kernel, dim3(nb, d.S), qthreads, 0, st, w.part2, kPartGroups, nb, b0, cols, f.q,
                    aspect_weights, d.S, d.d_k, w.gq, w.gw_part);
         DWA_LAUNCH_CHECK("query_grad_kernel");
         ++g_launches_total;
@@ -749,8 +749,398 @@ extern "C" int dwa_retrieve_bwd(void* stream, const DwaRetrieveDims* dims, int u
     DWA_LAUNCH_CHECK("wq_grad_kernel");
     const int64_t nz = static_cast<int64_t>(d.B) * d.d_A;
     launch_pdl(query_grad_finish_kernel, static_cast<unsigned>((nz + 255) / 256), 256, 0, st, w.gz_part, nchunk_o, d.B,
-               d.d_A, w.gw_part, aspect_weights, d.S, w.gtau, g_z, g_aspect_weights, g_tau);
+               d.d_A, w.gw_part, aspect_weights, d.S, w.gtau, 1, g_z, g_aspect_weights, g_tau);
     DWA_LAUNCH_CHECK("query_grad_finish_kernel");
     g_launches_total += 2;
+    return DWA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// The VJP over a row-sharded pool: every rank runs phase 1 on its rows, the
+// caller sums the [B, k+3] partials over the ranks, every rank runs phase 2,
+// the caller sums the [B, S*d_k+1] partials, and every rank runs phase 3.
+// The same workspace goes to all three phases of one call.
+// ---------------------------------------------------------------------------
+namespace dwa {
+
+// Phase-1 partials of query b, [k+3]: the scores of the winners this rank
+// holds (0 for the others), Σ raw over this rank's candidates (gate mode),
+// Σ g_soft·soft over its rows (added in chunk order), its candidate count.
+struct Part1Args {
+    const float* scores;       // [B, K_cap] (gate) or null
+    const int64_t* probe_lo;
+    const int64_t* cand_base;
+    int m;
+    int64_t K_cap, N, row_lo;
+    int k;
+    float T;
+    int gate;
+    const float* lambda_val;
+    const float* tau;
+    const int32_t* indices;    // [B, k] global rows
+    const float* soft_part;    // [B, nchunks] or null
+    int nchunks;
+    float* part1;              // [B, k+3]
+};
+
+__global__ void __launch_bounds__(256) bwd_part1_kernel(Part1Args a) {
+    pdl_enter();
+    __shared__ int64_t s_lo[kMaxK + 1], s_base[kMaxK + 1];
+    __shared__ float red[33];
+    const int b = blockIdx.x, tid = threadIdx.x, W = a.k + 3;
+    for (int j = tid; j <= a.m; j += blockDim.x) {
+        s_lo[j] = a.probe_lo[static_cast<int64_t>(b) * (a.m + 1) + j];
+        s_base[j] = a.cand_base[static_cast<int64_t>(b) * (a.m + 1) + j];
+    }
+    __syncthreads();
+    float* out = a.part1 + static_cast<int64_t>(b) * W;
+    const float* sc = a.gate ? a.scores + static_cast<int64_t>(b) * a.K_cap : nullptr;
+    for (int i = tid; i < a.k; i += blockDim.x) {
+        float v = 0.f;
+        if (sc) {
+            const int64_t row = static_cast<int64_t>(a.indices[static_cast<int64_t>(b) * a.k + i]) - a.row_lo;
+            for (int j = 0; j < a.m; ++j)
+                if (row >= s_lo[j] && row < s_lo[j] + (s_base[j + 1] - s_base[j])) v = sc[s_base[j] + (row - s_lo[j])];
+        }
+        out[i] = v;
+    }
+    float z = 0.f;
+    if (sc) {
+        const float lam = __ldg(a.lambda_val), tau = __ldg(a.tau);
+        for (int j = 0; j < a.m; ++j) {
+            const int64_t base = s_base[j], sz = s_base[j + 1] - s_base[j];
+            for (int64_t r = tid; r < sz; r += blockDim.x) z += gate_raw(sc[base + r], lam, tau, a.T);
+        }
+    }
+    z = block_reduce(z, false, red);
+    if (tid == 0) {
+        float dt = 0.f;
+        if (a.soft_part)
+            for (int c = 0; c < a.nchunks; ++c) dt += a.soft_part[static_cast<int64_t>(b) * a.nchunks + c];
+        out[a.k] = z;
+        out[a.k + 1] = dt;
+        out[a.k + 2] = static_cast<float>(s_base[a.m]);
+    }
+}
+
+// Selection backward of query b on this rank's rows from the summed phase-1
+// values: the same quantities as sel_grad_kernel (the gate sum Z, the winners'
+// gate terms, the top-k backward of α), added to G for this rank's candidates
+// and winners only; this rank's share of g_tau.
+struct SelGradGlobalArgs {
+    SelGradArgs s;             // scores / probes / N / row_lo of this rank
+    const float* part1;        // [B, k+3] summed over the ranks
+};
+
+__global__ void __launch_bounds__(1024) sel_grad_global_kernel(SelGradGlobalArgs g) {
+    pdl_enter();
+    const SelGradArgs& a = g.s;
+    __shared__ int64_t s_lo[kMaxK + 1], s_base[kMaxK + 1];
+    __shared__ float red[33];
+    __shared__ float w_raw[kMaxK], w_fac[kMaxK], w_gt[kMaxK];
+    const int b = blockIdx.x, tid = threadIdx.x, W = a.k + 3;
+    for (int j = tid; j <= a.m; j += blockDim.x) {
+        s_lo[j] = a.probe_lo[static_cast<int64_t>(b) * (a.m + 1) + j];
+        s_base[j] = a.cand_base[static_cast<int64_t>(b) * (a.m + 1) + j];
+    }
+    __syncthreads();
+    const float* p1 = g.part1 + static_cast<int64_t>(b) * W;
+    const float n_all = p1[a.k + 2];
+    const int got = n_all < static_cast<float>(a.k) ? static_cast<int>(n_all) : a.k;
+    const float* ga = a.g_alphas + static_cast<int64_t>(b) * a.k;
+    const float* al = a.alphas + static_cast<int64_t>(b) * a.k;
+    float* Gb = a.G + static_cast<int64_t>(b) * a.N;
+    const float T = a.T, invT = 1.f / a.T;
+    auto local_row = [&](int i) {
+        const int64_t row = static_cast<int64_t>(a.indices[static_cast<int64_t>(b) * a.k + i]) - a.row_lo;
+        return (row >= 0 && row < a.N) ? row : int64_t(-1);
+    };
+    if (a.is_warmup) {
+        float d = 0.f;
+        for (int i = tid; i < got; i += blockDim.x) d = fmaf(al[i], ga[i], d);
+        d = block_reduce(d, false, red);
+        for (int i = tid; i < got; i += blockDim.x) {
+            const int64_t row = local_row(i);
+            if (row >= 0) Gb[row] += al[i] * (ga[i] - d) * invT;
+        }
+        if (tid == 0) a.gtau[b] = 0.f;
+        return;
+    }
+    const float lam = __ldg(a.lambda_val), tau = __ldg(a.tau);
+    const float Zp = p1[a.k] + 1e-8f;
+    for (int i = tid; i < got; i += blockDim.x) {
+        const float s = p1[i];
+        const float sg = 1.f / (1.f + expf(-(lam * (s - tau))));
+        w_raw[i] = sg * expf(s / T);
+        w_fac[i] = lam * (1.f - sg) + invT;
+    }
+    __syncthreads();
+    float st = 0.f, gt_dot = 0.f;
+    for (int i = tid; i < got; i += blockDim.x) {
+        const float t = w_raw[i] / Zp;
+        st += t;
+        gt_dot = fmaf(ga[i], t, gt_dot);
+    }
+    const float St = block_reduce(st, false, red) + 1e-8f;
+    const float GD = block_reduce(gt_dot, false, red);
+    float graw_dot = 0.f;
+    for (int i = tid; i < got; i += blockDim.x) {
+        const float g_t = ga[i] / St - GD / (St * St);
+        w_gt[i] = g_t;
+        graw_dot = fmaf(g_t, w_raw[i], graw_dot);
+    }
+    const float cz = -block_reduce(graw_dot, false, red) / (Zp * Zp);
+    const float* sc = a.scores + static_cast<int64_t>(b) * a.K_cap;
+    float tacc = 0.f;
+    for (int j = 0; j < a.m; ++j) {
+        const int64_t lo = s_lo[j], base = s_base[j], sz = s_base[j + 1] - s_base[j];
+        for (int64_t r = tid; r < sz; r += blockDim.x) {
+            const float s = sc[base + r];
+            const float sg = 1.f / (1.f + expf(-(lam * (s - tau))));
+            const float raw = sg * expf(s / T);
+            Gb[lo + r] += cz * raw * (lam * (1.f - sg) + invT);
+            tacc += cz * raw * (-lam * (1.f - sg));
+        }
+    }
+    __syncthreads();
+    for (int i = tid; i < got; i += blockDim.x) {
+        const int64_t row = local_row(i);
+        if (row < 0) continue;
+        const float graw = w_gt[i] / Zp;
+        Gb[row] += graw * w_raw[i] * w_fac[i];
+        tacc -= graw * w_raw[i] * (w_fac[i] - invT);
+    }
+    tacc = block_reduce(tacc, false, red);
+    if (tid == 0) a.gtau[b] = tacc;
+}
+
+// This rank's A of queries [b0, b0+nb) = Σ of the kPartGroups partial groups,
+// into part2 [B, cols+1] (row stride cols+1), with its g_tau share in column cols.
+__global__ void a_final_kernel(const float* __restrict__ part, int nb, int b0, int cols,
+                               const float* __restrict__ gtau, float* __restrict__ part2) {
+    pdl_enter();
+    const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t width = static_cast<int64_t>(nb) * cols;
+    if (e < width) {
+        float acc = 0.f;
+        for (int g = 0; g < kPartGroups; ++g) acc += part[static_cast<int64_t>(g) * width + e];
+        const int bl = static_cast<int>(e / cols), col = static_cast<int>(e % cols);
+        part2[static_cast<int64_t>(b0 + bl) * (cols + 1) + col] = acc;
+    } else if (e < width + nb) {
+        const int bl = static_cast<int>(e - width);
+        part2[static_cast<int64_t>(b0 + bl) * (cols + 1) + cols] = gtau[b0 + bl];
+    }
+}
+
+}  // namespace dwa
+
+extern "C" size_t dwa_retrieve_bwd_local_workspace_bytes(const DwaRetrieveDims* dims, int use_ivf) {
+    return dwa_retrieve_bwd_workspace_bytes(dims, use_ivf);
+}
+
+extern "C" int dwa_retrieve_bwd_local1(void* stream, const DwaRetrieveDims* dims, const DwaShard* shard, int use_ivf,
+                                       int is_warmup, const float* lambda_val, const void* z, const float* W_Q,
+                                       const float* aspect_weights, const float* tau, const float* centroids,
+                                       const int64_t* list_offsets, const float* local_keys, const int32_t* indices,
+                                       const float* soft_full, const float* g_soft_full, float* part1,
+                                       void* workspace, size_t workspace_bytes) {
+    using namespace dwa;
+    int rc = check_bwd(dims, use_ivf);
+    if (rc) return rc;
+    const DwaRetrieveDims& d = *dims;
+    const bool ivf = use_ivf != 0;
+    if (!shard || shard->row_lo < 0 || shard->n_global < shard->row_lo + d.N || shard->n_global >= (int64_t(1) << 31))
+        return fail(DWA_ERR_INVALID_ARG, "shard: need 0 <= row_lo and row_lo + N <= n_global < 2^31");
+    if (!lambda_val || !z || !W_Q || !aspect_weights || !tau || !local_keys || !indices || !part1)
+        return fail(DWA_ERR_INVALID_ARG, "a required pointer is NULL");
+    if (g_soft_full && !soft_full) return fail(DWA_ERR_INVALID_ARG, "g_soft_full needs soft_full");
+    if (ivf && (!centroids || !list_offsets)) return fail(DWA_ERR_INVALID_ARG, "IVF needs centroids and list_offsets");
+    const BwdWorkspace w = carve_bwd(workspace, d, ivf);
+    if (!workspace || reinterpret_cast<uintptr_t>(workspace) % 256 != 0 || workspace_bytes < w.bytes)
+        return fail(DWA_ERR_WORKSPACE, "workspace: dwa_retrieve_bwd_local_workspace_bytes, 256-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const bool dk64 = d.d_k == 64 && reinterpret_cast<uintptr_t>(local_keys) % 16 == 0 &&
+                      (!ivf || reinterpret_cast<uintptr_t>(centroids) % 16 == 0);
+    const RetWorkspace& f = w.f;
+    const size_t qsh = static_cast<size_t>(d.S) * d.d_k * sizeof(float);
+    if ((rc = launch_queries_and_probes(st, d, ivf, dk64, z, W_Q, aspect_weights, centroids, list_offsets,
+                                        shard->row_lo, shard->n_global, f)))
+        return rc;
+    const bool gate = !is_warmup;
+    float* scores = ivf ? f.scores : f.sfull;
+    if (gate) {
+        dim3 gf(static_cast<unsigned>(((ivf ? d.max_list : d.N) + 255) / 256), f.m_eff, d.B);
+        if (dk64)
+            launch_pdl(fine_kernel<64>, gf, 256, qsh, st, f.qw, local_keys, d.N, d.S, d.d_k, f.m_eff, f.probe_lo,
+                       f.cand_base, f.K_cap, scores);
+        else
+            launch_pdl(fine_kernel<0>, gf, 256, qsh, st, f.qw, local_keys, d.N, d.S, d.d_k, f.m_eff, f.probe_lo,
+                       f.cand_base, f.K_cap, scores);
+        DWA_LAUNCH_CHECK("fine_kernel");
+        ++g_launches_total;
+    }
+    const int nchunks = static_cast<int>((d.N + kSoftChunk - 1) / kSoftChunk);
+    if (g_soft_full) {
+        launch_pdl(soft_dot_kernel, dim3(nchunks, d.B), 256, 0, st, soft_full, g_soft_full, d.N, w.soft_part);
+        DWA_LAUNCH_CHECK("soft_dot_kernel");
+        ++g_launches_total;
+    }
+    Part1Args pa{};
+    pa.scores = gate ? scores : nullptr; pa.probe_lo = f.probe_lo; pa.cand_base = f.cand_base; pa.m = f.m_eff;
+    pa.K_cap = f.K_cap; pa.N = d.N; pa.row_lo = shard->row_lo; pa.k = d.k; pa.T = d.T; pa.gate = gate;
+    pa.lambda_val = lambda_val; pa.tau = tau; pa.indices = indices;
+    pa.soft_part = g_soft_full ? w.soft_part : nullptr; pa.nchunks = nchunks; pa.part1 = part1;
+    launch_pdl(bwd_part1_kernel, d.B, 256, 0, st, pa);
+    DWA_LAUNCH_CHECK("bwd_part1_kernel");
+    ++g_launches_total;
+    return DWA_OK;
+}
+
+extern "C" int dwa_retrieve_bwd_local2(void* stream, const DwaRetrieveDims* dims, const DwaShard* shard, int use_ivf,
+                                       int is_warmup, const float* lambda_val, const float* tau,
+                                       const float* aspect_weights, const int64_t* list_offsets,
+                                       const float* local_keys, const float* alphas, const int32_t* indices,
+                                       const float* soft_full, const float* g_alphas, const float* g_soft_full,
+                                       const float* part1_sum, float* part2, float* g_pool_keys, void* workspace,
+                                       size_t workspace_bytes) {
+    using namespace dwa;
+    int rc = check_bwd(dims, use_ivf);
+    if (rc) return rc;
+    const DwaRetrieveDims& d = *dims;
+    const bool ivf = use_ivf != 0;
+    if (!shard || shard->row_lo < 0) return fail(DWA_ERR_INVALID_ARG, "shard is NULL or row_lo < 0");
+    if (!lambda_val || !tau || !aspect_weights || !local_keys || !part1_sum || !part2 || (ivf && !list_offsets))
+        return fail(DWA_ERR_INVALID_ARG, "a required pointer is NULL");
+    if (g_alphas && (!alphas || !indices)) return fail(DWA_ERR_INVALID_ARG, "g_alphas needs alphas and indices");
+    if (g_soft_full && !soft_full) return fail(DWA_ERR_INVALID_ARG, "g_soft_full needs soft_full");
+    if (reinterpret_cast<uintptr_t>(local_keys) % 16 != 0) return fail(DWA_ERR_INVALID_ARG, "keys must be 16-byte aligned");
+    if (g_pool_keys && d.B > kBwdMaxQ) return fail(DWA_ERR_UNSUPPORTED, "retrieval VJP: the key gradient needs B <= 32");
+    const BwdWorkspace w = carve_bwd(workspace, d, ivf);
+    if (!workspace || reinterpret_cast<uintptr_t>(workspace) % 256 != 0 || workspace_bytes < w.bytes)
+        return fail(DWA_ERR_WORKSPACE, "workspace: dwa_retrieve_bwd_local_workspace_bytes, 256-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const RetWorkspace& f = w.f;
+    float* scores = ivf ? f.scores : f.sfull;
+    const int nchunks = static_cast<int>((d.N + kSoftChunk - 1) / kSoftChunk);
+    (void)nchunks;
+    if (g_soft_full) {
+        const int nc = static_cast<int>((d.N + kSoftChunk - 1) / kSoftChunk);
+        launch_pdl(soft_grad_kernel, dim3(nc, d.B), 256, 0, st, soft_full, g_soft_full, d.N, part1_sum + d.k + 1, 1,
+                   d.k + 3, 1.f / d.T, w.G);
+        DWA_LAUNCH_CHECK("soft_grad_kernel");
+        ++g_launches_total;
+    } else {
+        DWA_CUDA_TRY(cudaMemsetAsync(w.G, 0, static_cast<size_t>(d.B) * d.N * sizeof(float), st));
+    }
+    if (g_alphas) {
+        SelGradGlobalArgs ga{};
+        SelGradArgs& sa = ga.s;
+        sa.scores = scores; sa.probe_lo = f.probe_lo; sa.cand_base = f.cand_base; sa.m = f.m_eff;
+        sa.K_cap = f.K_cap; sa.N = d.N; sa.k = d.k; sa.T = d.T; sa.is_warmup = is_warmup;
+        sa.lambda_val = lambda_val; sa.tau = tau; sa.alphas = alphas; sa.indices = indices;
+        sa.g_alphas = g_alphas; sa.row_lo = shard->row_lo; sa.G = w.G; sa.gtau = w.gtau; sa.status = f.status;
+        ga.part1 = part1_sum;
+        launch_pdl(sel_grad_global_kernel, d.B, 1024, 0, st, ga);
+        DWA_LAUNCH_CHECK("sel_grad_global_kernel");
+        ++g_launches_total;
+    } else {
+        DWA_CUDA_TRY(cudaMemsetAsync(w.gtau, 0, static_cast<size_t>(d.B) * sizeof(float), st));
+    }
+    const int64_t ntiles = (d.N + kKeyTile - 1) / kKeyTile;
+    const bool probed_only = ivf && !g_soft_full && !g_pool_keys;
+    if (probed_only) {
+        DWA_CUDA_TRY(cudaMemsetAsync(w.tile_on, 0, static_cast<size_t>(ntiles), st));
+        launch_pdl(key_tile_flags_kernel, (d.B * f.m_eff + 127) / 128, 128, 0, st, f.topc, d.B, f.m_eff,
+                   list_offsets, shard->row_lo, d.N, w.tile_on);
+        DWA_LAUNCH_CHECK("key_tile_flags_kernel");
+        ++g_launches_total;
+    }
+    const int cols = d.S * d.d_k;
+    const int cpt = (cols + kKeyThreads - 1) / kKeyThreads;
+    if (g_pool_keys) {
+        launch_pdl(unweighted_queries_kernel, d.B, 32 * d.S, 0, st, f.q, aspect_weights, d.S, d.d_k, w.qh, w.ws);
+        DWA_LAUNCH_CHECK("unweighted_queries_kernel");
+        ++g_launches_total;
+    }
+    for (int b0 = 0; b0 < d.B; b0 += kBwdMaxQ) {
+        const int nb = std::min(kBwdMaxQ, d.B - b0);
+        const int qb = nb <= 8 ? 8 : nb <= 16 ? 16 : 32;
+        KeyGradArgs ka{};
+        ka.keys = local_keys; ka.N = d.N; ka.S = d.S; ka.d_k = d.d_k; ka.B = d.B; ka.b0 = b0; ka.nb = nb;
+        ka.G = w.G; ka.qh = w.qh; ka.w = w.ws; ka.tile_on = probed_only ? w.tile_on : nullptr;
+        ka.ntiles = ntiles; ka.partial = w.partial; ka.g_keys = g_pool_keys;
+        if (cpt > 2 && qb > 16) return fail(DWA_ERR_UNSUPPORTED, "retrieval VJP: S*d_k > 512 needs B <= 16 per pass");
+        const size_t sm = key_grad_smem(d.S, d.d_k, qb, g_pool_keys != nullptr);
+        if (sm > 200 * 1024) return fail(DWA_ERR_UNSUPPORTED, "retrieval VJP: S*d_k too large for the key tile");
+        void (*fn)(KeyGradArgs) = nullptr;
+        if (cpt == 1) fn = qb == 8 ? key_grad_pass_kernel<1, 8> : qb == 16 ? key_grad_pass_kernel<1, 16> : key_grad_pass_kernel<1, 32>;
+        else if (cpt == 2) fn = qb == 8 ? key_grad_pass_kernel<2, 8> : qb == 16 ? key_grad_pass_kernel<2, 16> : key_grad_pass_kernel<2, 32>;
+        else fn = qb == 8 ? key_grad_pass_kernel<4, 8> : key_grad_pass_kernel<4, 16>;
+        DWA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm)));
+        int occ = 1, dv = 0, sms = 148;
+        DWA_CUDA_TRY(cudaGetDevice(&dv));
+        DWA_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dv));
+        DWA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kKeyThreads, sm));
+        const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(
+            {static_cast<int64_t>(w.grid), static_cast<int64_t>(std::max(occ, 1)) * sms, ntiles})));
+        launch_pdl(fn, grid, kKeyThreads, sm, st, ka);
+        DWA_LAUNCH_CHECK("key_grad_pass_kernel");
+        const int64_t width = static_cast<int64_t>(nb) * cols;
+        launch_pdl(partial_reduce_kernel, dim3(static_cast<unsigned>((width + 255) / 256), kPartGroups), 256, 0, st,
+                   w.partial, grid, width, w.part2);
+        DWA_LAUNCH_CHECK("partial_reduce_kernel");
+        launch_pdl(a_final_kernel, static_cast<unsigned>((width + nb + 255) / 256), 256, 0, st, w.part2, nb, b0, cols,
+                   w.gtau, part2);
+        DWA_LAUNCH_CHECK("a_final_kernel");
+        g_launches_total += 3;
+    }
+    return DWA_OK;
+}
+
+extern "C" int dwa_retrieve_bwd_finish(void* stream, const DwaRetrieveDims* dims, int use_ivf, const void* z,
+                                       const float* W_Q, const float* aspect_weights, const float* part2_sum,
+                                       float* g_z, float* g_W_Q, float* g_aspect_weights, float* g_tau,
+                                       void* workspace, size_t workspace_bytes) {
+    using namespace dwa;
+    int rc = check_bwd(dims, use_ivf);
+    if (rc) return rc;
+    const DwaRetrieveDims& d = *dims;
+    if (!z || !W_Q || !aspect_weights || !part2_sum || !g_z || !g_W_Q || !g_aspect_weights || !g_tau)
+        return fail(DWA_ERR_INVALID_ARG, "a required pointer is NULL");
+    const BwdWorkspace w = carve_bwd(workspace, d, use_ivf != 0);
+    if (!workspace || reinterpret_cast<uintptr_t>(workspace) % 256 != 0 || workspace_bytes < w.bytes)
+        return fail(DWA_ERR_WORKSPACE, "workspace: dwa_retrieve_bwd_local_workspace_bytes, 256-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int cols = d.S * d.d_k;
+    // the raw queries again (this phase needs no rows, so an empty rank runs it too)
+    const dim3 gq((cols + kProjRows - 1) / kProjRows, (d.B + kProjQ - 1) / kProjQ);
+    if (d.z_dtype == DWA_BF16)
+        launch_pdl(query_proj_kernel<__nv_bfloat16>, gq, kProjThreads, 0, st, static_cast<const __nv_bfloat16*>(z),
+                   W_Q, d.B, cols, d.d_A, w.f.q);
+    else
+        launch_pdl(query_proj_kernel<float>, gq, kProjThreads, 0, st, static_cast<const float*>(z), W_Q, d.B, cols,
+                   d.d_A, w.f.q);
+    DWA_LAUNCH_CHECK("query_proj_kernel");
+    ++g_launches_total;
+    const int qthreads = (d.d_k + 31) / 32 * 32;
+    launch_pdl(query_grad_kernel, dim3(d.B, d.S), qthreads, 0, st, part2_sum, 1, d.B, 0, cols + 1, w.f.q,
+               aspect_weights, d.S, d.d_k, w.gq, w.gw_part);
+    DWA_LAUNCH_CHECK("query_grad_kernel");
+    const int nchunk_o = (cols + kGradRowsPerCta - 1) / kGradRowsPerCta;
+    const size_t gsh = static_cast<size_t>(d.B) * kGradRowsPerCta * sizeof(float);
+    if (gsh > 48 * 1024) return fail(DWA_ERR_UNSUPPORTED, "retrieval VJP: B too large for the W_Q gradient");
+    const dim3 gw((d.d_A + 127) / 128, nchunk_o);
+    if (d.z_dtype == DWA_BF16)
+        launch_pdl(wq_grad_kernel<__nv_bfloat16>, gw, 128, gsh, st, w.gq, static_cast<const __nv_bfloat16*>(z), W_Q,
+                   d.B, cols, d.d_A, g_W_Q, w.gz_part);
+    else
+        launch_pdl(wq_grad_kernel<float>, gw, 128, gsh, st, w.gq, static_cast<const float*>(z), W_Q, d.B, cols,
+                   d.d_A, g_W_Q, w.gz_part);
+    DWA_LAUNCH_CHECK("wq_grad_kernel");
+    const int64_t nz = static_cast<int64_t>(d.B) * d.d_A;
+    launch_pdl(query_grad_finish_kernel, static_cast<unsigned>((nz + 255) / 256), 256, 0, st, w.gz_part, nchunk_o, d.B,
+               d.d_A, w.gw_part, aspect_weights, d.S, part2_sum + cols, cols + 1, g_z, g_aspect_weights, g_tau);
+    DWA_LAUNCH_CHECK("query_grad_finish_kernel");
+    g_launches_total += 3;
     return DWA_OK;
 }

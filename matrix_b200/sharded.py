@@ -184,3 +184,133 @@ def sharded_retrieve(z, W_Q, aspect_weights, tau, centroids, local_keys, list_of
     gathered = gather_summaries(summary, shard.group)
     alphas, indices = retrieve_merge(gathered, lambda_val, tau, is_warmup, k=k, T=T, soft_full=soft)
     return alphas, indices, soft
+
+
+# ---------------------------------------------------------------------------
+# The retrieval VJP over a row-sharded pool (dwa_retrieve_bwd_local1/2, finish)
+# ---------------------------------------------------------------------------
+
+def _bwd_args(z, W_Q, aspect_weights, tau, lambda_val, n_rows, *, k, m, T, C, max_list):
+    dev = z.device
+    lam = lambda_val if isinstance(lambda_val, torch.Tensor) else torch.tensor(
+        [float(lambda_val)], dtype=torch.float32, device=dev)
+    B, d_A = z.shape
+    S, d_k, _ = W_Q.shape
+    dims = _dims(B, S, d_k, d_A, C, m, k, max_list or 0, max(int(n_rows), 1), T, dtype_code(z.dtype, "z"))
+    return dims, lam.reshape(1).float().contiguous(), tau.reshape(1).float().contiguous(), \
+        W_Q.float().contiguous(), aspect_weights.float().contiguous()
+
+
+def _bwd_ws_bytes(z, W_Q, n_rows, *, k, m, T, C, max_list, use_ivf):
+    dims = _dims(z.shape[0], W_Q.shape[0], W_Q.shape[1], z.shape[1], C, m, k, max_list or 0,
+                 max(int(n_rows), 1), T, dtype_code(z.dtype, "z"))
+    nbytes = _lib.load().dwa_retrieve_bwd_local_workspace_bytes(dims, int(use_ivf))
+    if nbytes == 0:
+        raise _lib.DwaError(f"dwa_retrieve_bwd_local_workspace_bytes: {_lib.last_error()}")
+    return nbytes
+
+
+def bwd_workspace(z, W_Q, n_rows, *, k, m, T, C, max_list, use_ivf=True):
+    """A workspace for the three phases of one rank's call (one per emulated
+    rank when several share a GPU)."""
+    return torch.zeros(_bwd_ws_bytes(z, W_Q, n_rows, k=k, m=m, T=T, C=C, max_list=max_list, use_ivf=use_ivf),
+                       dtype=torch.uint8, device=z.device)
+
+
+def retrieve_bwd_local1(ws, z, W_Q, aspect_weights, tau, centroids, local_keys, list_offsets, lambda_val,
+                        is_warmup, indices, soft_local, g_soft_local, *, k, m, T, row_lo, n_global, max_list,
+                        use_ivf=True):
+    """Phase 1 on this rank's rows: ``part1 [B, k+3]`` (zeros for a rank without rows)."""
+    B = z.shape[0]
+    n_loc = local_keys.shape[1]
+    part1 = torch.zeros((B, k + 3), dtype=torch.float32, device=z.device)
+    if n_loc == 0:
+        return part1
+    C = centroids.shape[1] if use_ivf else 1
+    dims, lam, tau_t, W_Q, aw = _bwd_args(z, W_Q, aspect_weights, tau, lambda_val, n_loc, k=k, m=m, T=T, C=C,
+                                          max_list=max_list)
+    lib = _lib.load()
+    with torch.cuda.device(z.device):
+        rc = lib.dwa_retrieve_bwd_local1(
+            stream_of(z.device), dims, _lib.Shard(int(row_lo), int(n_global)), int(use_ivf), int(bool(is_warmup)),
+            ptr(lam), ptr(z), ptr(W_Q), ptr(aw), ptr(tau_t), ptr(centroids) if use_ivf else None,
+            ptr(list_offsets) if use_ivf else None, ptr(local_keys), ptr(indices.int().contiguous()),
+            ptr(soft_local), ptr(g_soft_local), ptr(part1), ptr(ws), ws.numel())
+    _lib.check(rc, "dwa_retrieve_bwd_local1")
+    return part1
+
+
+def retrieve_bwd_local2(ws, z, W_Q, aspect_weights, tau, centroids, local_keys, list_offsets, lambda_val,
+                        is_warmup, alphas, indices, soft_local, g_alphas, g_soft_local, part1_sum, *, k, m, T,
+                        row_lo, max_list, use_ivf=True, want_key_grad=False):
+    """Phase 2: ``(part2 [B, S*d_k+1], key gradient of this rank's rows or None)``."""
+    B = z.shape[0]
+    S, n_loc, d_k = local_keys.shape
+    part2 = torch.zeros((B, S * d_k + 1), dtype=torch.float32, device=z.device)
+    g_keys = torch.zeros(tuple(local_keys.shape), dtype=torch.float32, device=z.device) if want_key_grad else None
+    if n_loc == 0:
+        return part2, g_keys
+    C = centroids.shape[1] if use_ivf else 1
+    dims, lam, tau_t, W_Q, aw = _bwd_args(z, W_Q, aspect_weights, tau, lambda_val, n_loc, k=k, m=m, T=T, C=C,
+                                          max_list=max_list)
+    lib = _lib.load()
+    with torch.cuda.device(z.device):
+        rc = lib.dwa_retrieve_bwd_local2(
+            stream_of(z.device), dims, _lib.Shard(int(row_lo), 0), int(use_ivf), int(bool(is_warmup)), ptr(lam),
+            ptr(tau_t), ptr(aw), ptr(list_offsets) if use_ivf else None, ptr(local_keys),
+            ptr(alphas.float().contiguous()) if alphas is not None else None,
+            ptr(indices.int().contiguous()) if indices is not None else None, ptr(soft_local),
+            ptr(g_alphas.float().contiguous()) if g_alphas is not None else None, ptr(g_soft_local),
+            ptr(part1_sum.contiguous()), ptr(part2), ptr(g_keys), ptr(ws), ws.numel())
+    _lib.check(rc, "dwa_retrieve_bwd_local2")
+    return part2, g_keys
+
+
+def retrieve_bwd_finish(ws, z, W_Q, aspect_weights, part2_sum, *, k, m, T, C, max_list, use_ivf=True):
+    """Phase 3: ``dict(g_z, g_W_Q, g_aspect_weights, g_tau)`` from the summed part2."""
+    dev = z.device
+    f32 = dict(dtype=torch.float32, device=dev)
+    dims, _, _, W_Qc, aw = _bwd_args(z, W_Q, aspect_weights, torch.zeros(1, device=dev), 0.0, 1, k=k, m=m, T=T, C=C,
+                                     max_list=max_list)
+    out = dict(g_z=torch.empty((z.shape[0], z.shape[1]), **f32), g_W_Q=torch.empty(tuple(W_Q.shape), **f32),
+               g_aspect_weights=torch.empty((W_Q.shape[0],), **f32), g_tau=torch.empty((), **f32))
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.dwa_retrieve_bwd_finish(stream_of(dev), dims, int(use_ivf), ptr(z), ptr(W_Qc), ptr(aw),
+                                         ptr(part2_sum.contiguous()), ptr(out["g_z"]), ptr(out["g_W_Q"]),
+                                         ptr(out["g_aspect_weights"]), ptr(out["g_tau"]), ptr(ws), ws.numel())
+    _lib.check(rc, "dwa_retrieve_bwd_finish")
+    return out
+
+
+def sharded_retrieve_backward(z, W_Q, aspect_weights, tau, centroids, local_keys, list_offsets, lambda_val,
+                              is_warmup, shard: RowShard, alphas, indices, soft_local, g_alphas, g_soft_local, *,
+                              k, m, T, max_list=None, use_ivf=True, want_key_grad=False):
+    """The VJP of ``sharded_retrieve`` on this rank: the three phases with one
+    all-reduce of ``[B, k+3]`` and one of ``[B, S*d_k+1]`` floats between them.
+    Returns ``dict(g_z, g_W_Q, g_aspect_weights, g_tau, g_pool_keys)`` with the
+    key gradient of this rank's rows (or None); every rank gets the same
+    parameter gradients."""
+    import torch.distributed as dist
+    if use_ivf and max_list is None:
+        max_list = int((list_offsets[1:] - list_offsets[:-1]).max().item())
+    C = centroids.shape[1] if use_ivf else 1
+    n_loc = local_keys.shape[1]
+    ws = workspace(z.device, "retrieve_bwd_local",
+                   _bwd_ws_bytes(z, W_Q, n_loc, k=k, m=m, T=T, C=C, max_list=max_list, use_ivf=use_ivf))
+    world = dist.get_world_size(shard.group) if dist.is_available() and dist.is_initialized() else 1
+    part1 = retrieve_bwd_local1(ws, z, W_Q, aspect_weights, tau, centroids, local_keys, list_offsets, lambda_val,
+                                is_warmup, indices, soft_local, g_soft_local, k=k, m=m, T=T, row_lo=shard.row_lo,
+                                n_global=shard.n_global, max_list=max_list, use_ivf=use_ivf)
+    if world > 1:
+        dist.all_reduce(part1, group=shard.group)
+    part2, g_keys = retrieve_bwd_local2(ws, z, W_Q, aspect_weights, tau, centroids, local_keys, list_offsets,
+                                        lambda_val, is_warmup, alphas, indices, soft_local, g_alphas, g_soft_local,
+                                        part1, k=k, m=m, T=T, row_lo=shard.row_lo, max_list=max_list,
+                                        use_ivf=use_ivf, want_key_grad=want_key_grad)
+    if world > 1:
+        dist.all_reduce(part2, group=shard.group)
+    out = retrieve_bwd_finish(ws, z, W_Q, aspect_weights, part2, k=k, m=m, T=T, C=C, max_list=max_list,
+                              use_ivf=use_ivf)
+    out["g_pool_keys"] = g_keys
+    return out

@@ -261,3 +261,106 @@ def test_two_ranks_peer_gather_and_sharded_assembly(tmp_path):
     np.testing.assert_array_equal(np.concatenate([g["h_mid"] for g in got]), h_mid.float().cpu().numpy())
     np.testing.assert_array_equal(np.concatenate([g["W"] for g in got]), W.cpu().numpy())
     assert_close(np.concatenate([g["g_pool"] for g in got]), g_pool.cpu().numpy(), TOL, name="g_pool")
+
+
+# ---------------------------------------------------------------------------
+# The retrieval VJP over the same emulated ranks
+# ---------------------------------------------------------------------------
+
+def _emulated_bwd(cfg, x, shards, is_warmup, lam, g_alphas, g_soft, use_ivf=True, want_keys=True):
+    """Every rank's phase 1, the sum over the ranks (the all-reduce), every
+    rank's phase 2, the sum, and phase 3; the ranks' key gradients stacked."""
+    from matrix_b200.retrieval import retrieve
+    from matrix_b200.sharded import (bwd_workspace, retrieve_bwd_finish, retrieve_bwd_local1,
+                                     retrieve_bwd_local2)
+    z, W_Q, aw = _dev(x.z), _dev(x.W_Q), _dev(x.aspect_weights)
+    tau, cents, off = torch.tensor(x.tau).cuda(), _dev(x.centroids), _dev(x.list_offsets)
+    keys = _dev(x.keys)
+    max_list = int(np.diff(x.list_offsets).max())
+    kw = dict(k=cfg.k_max, m=cfg.m, T=cfg.T, max_list=max_list, use_ivf=use_ivf)
+    a, i, sf = retrieve(z, W_Q, aw, tau, cents, keys, lam, is_warmup, k=cfg.k_max, m=cfg.m, T=cfg.T,
+                        use_ivf=use_ivf, list_offsets=off if use_ivf else None,
+                        max_list=max_list if use_ivf else None, want_soft_full=True)
+    ga, gs = _dev(g_alphas), _dev(g_soft)
+    C = cfg.C if use_ivf else 1
+    wss, locs = [], []
+    for lo, hi in shards:
+        wss.append(bwd_workspace(z, W_Q, hi - lo, k=cfg.k_max, m=cfg.m, T=cfg.T, C=C, max_list=max_list,
+                                 use_ivf=use_ivf))
+        locs.append(keys[:, lo:hi].contiguous())
+    p1 = sum(retrieve_bwd_local1(wss[r], z, W_Q, aw, tau, cents, locs[r], off, lam, is_warmup, i,
+                                 sf[:, lo:hi].contiguous(), gs[:, lo:hi].contiguous(), row_lo=lo, n_global=cfg.N,
+                                 **kw)
+             for r, (lo, hi) in enumerate(shards))
+    parts, gks = [], []
+    for r, (lo, hi) in enumerate(shards):
+        p2, gk = retrieve_bwd_local2(wss[r], z, W_Q, aw, tau, cents, locs[r], off, lam, is_warmup, a, i,
+                                     sf[:, lo:hi].contiguous(), ga, gs[:, lo:hi].contiguous(), p1, row_lo=lo,
+                                     want_key_grad=want_keys, **kw)
+        parts.append(p2)
+        gks.append(gk)
+    out = retrieve_bwd_finish(wss[0], z, W_Q, aw, sum(parts), k=cfg.k_max, m=cfg.m, T=cfg.T, C=C,
+                              max_list=max_list, use_ivf=use_ivf)
+    torch.cuda.synchronize()
+    res = {k_: v.cpu().numpy() for k_, v in out.items()}
+    if want_keys:
+        res["g_pool_keys"] = torch.cat(gks, dim=1).cpu().numpy()
+    return res, (a, i, sf)
+
+
+@pytest.mark.parametrize("is_warmup,lam", [(True, 1.0), (False, 5.0)])
+@pytest.mark.parametrize("world", [2, 3])
+def test_emulated_ranks_vjp_equals_single_call(world, is_warmup, lam):
+    """The three-phase VJP over emulated ranks equals dwa_retrieve_bwd on the
+    whole pool (rtol 1e-5), key gradients included."""
+    from matrix_b200.retrieval import retrieve_backward
+    from matrix_b200.sharded import shard_rows
+    cfg, x = _case()
+    rng = np.random.default_rng(5)
+    g_alphas = rng.standard_normal((x.z.shape[0], cfg.k_max)).astype(np.float32)
+    g_soft = (rng.standard_normal((x.z.shape[0], cfg.N)) * 50).astype(np.float32)
+    shards = shard_rows(x.list_offsets, world)
+    got, (a, i, sf) = _emulated_bwd(cfg, x, shards, is_warmup, lam, g_alphas, g_soft)
+    max_list = int(np.diff(x.list_offsets).max())
+    ref = retrieve_backward(_dev(x.z), _dev(x.W_Q), _dev(x.aspect_weights), torch.tensor(x.tau).cuda(),
+                            _dev(x.centroids), _dev(x.keys), lam, is_warmup, a, i, sf, _dev(g_alphas),
+                            _dev(g_soft), k=cfg.k_max, m=cfg.m, T=cfg.T, list_offsets=_dev(x.list_offsets),
+                            max_list=max_list, want_key_grad=True)
+    for name in ("g_z", "g_W_Q", "g_aspect_weights", "g_pool_keys"):
+        assert_close(got[name], ref[name].cpu().numpy(), TOL, name=f"{name} world={world}")
+    r = float(ref["g_tau"])
+    assert abs(float(got["g_tau"]) - r) <= TOL * max(abs(r), 1e-3)
+
+
+def test_emulated_vjp_with_empty_rank_and_alphas_only():
+    """An empty middle rank (zero partials, phase 3 only) and the alphas'
+    cotangent alone (phase 2 visits only probed tiles)."""
+    from matrix_b200.retrieval import retrieve_backward
+    cfg, x = _case(seed=33)
+    rng = np.random.default_rng(6)
+    g_alphas = rng.standard_normal((x.z.shape[0], cfg.k_max)).astype(np.float32)
+    off = x.list_offsets
+    mid = int(off[len(off) // 2])
+    shards = [(0, mid), (mid, mid), (mid, cfg.N)]
+    from matrix_b200.sharded import (bwd_workspace, retrieve_bwd_finish, retrieve_bwd_local1,
+                                     retrieve_bwd_local2)
+    from matrix_b200.retrieval import retrieve
+    z, W_Q, aw = _dev(x.z), _dev(x.W_Q), _dev(x.aspect_weights)
+    tau, cents, offd, keys = torch.tensor(x.tau).cuda(), _dev(x.centroids), _dev(off), _dev(x.keys)
+    max_list = int(np.diff(off).max())
+    kw = dict(k=cfg.k_max, m=cfg.m, T=cfg.T, max_list=max_list)
+    a, i, _ = retrieve(z, W_Q, aw, tau, cents, keys, 5.0, False, k=cfg.k_max, m=cfg.m, T=cfg.T,
+                       list_offsets=offd, max_list=max_list, want_soft_full=False)
+    ga = _dev(g_alphas)
+    wss = [bwd_workspace(z, W_Q, hi - lo, C=cfg.C, **kw) for lo, hi in shards]
+    locs = [keys[:, lo:hi].contiguous() for lo, hi in shards]
+    p1 = sum(retrieve_bwd_local1(wss[r], z, W_Q, aw, tau, cents, locs[r], offd, 5.0, False, i, None, None,
+                                 row_lo=lo, n_global=cfg.N, **kw) for r, (lo, hi) in enumerate(shards))
+    p2 = sum(retrieve_bwd_local2(wss[r], z, W_Q, aw, tau, cents, locs[r], offd, 5.0, False, a, i, None, ga, None,
+                                 p1, row_lo=lo, **kw)[0] for r, (lo, hi) in enumerate(shards))
+    got = retrieve_bwd_finish(wss[1], z, W_Q, aw, p2, C=cfg.C, **kw)
+    ref = retrieve_backward(z, W_Q, aw, tau, cents, keys, 5.0, False, a, i, None, ga, None, k=cfg.k_max, m=cfg.m,
+                            T=cfg.T, list_offsets=offd, max_list=max_list)
+    torch.cuda.synchronize()
+    for name in ("g_z", "g_W_Q", "g_aspect_weights"):
+        assert_close(got[name].cpu().numpy(), ref[name].cpu().numpy(), TOL, name=name)
