@@ -602,6 +602,66 @@ static int check_bwd(const DwaRetrieveDims* d, int use_ivf) {
     return DWA_OK;
 }
 
+// The key pass of a VJP call over the key rows [0, d.N) of `keys`: the probed
+// lists' tiles only when `probed_only`, the key gradient when g_pool_keys is
+// non-NULL; `per_pass(b0, nb, grid)` runs after each pass of <= kBwdMaxQ
+// queries on its per-CTA partials.
+template <class PerPass>
+static int run_key_pass(cudaStream_t st, const DwaRetrieveDims& d, const BwdWorkspace& w, const float* keys,
+                        const float* aspect_weights, const int64_t* list_offsets, int64_t row_lo,
+                        bool probed_only, float* g_pool_keys, const PerPass& per_pass) {
+    const RetWorkspace& f = w.f;
+    const int64_t ntiles = (d.N + kKeyTile - 1) / kKeyTile;
+    if (probed_only) {
+        DWA_CUDA_TRY(cudaMemsetAsync(w.tile_on, 0, static_cast<size_t>(ntiles), st));
+        launch_pdl(key_tile_flags_kernel, (d.B * f.m_eff + 127) / 128, 128, 0, st, f.topc, d.B, f.m_eff,
+                   list_offsets, row_lo, d.N, w.tile_on);
+        DWA_LAUNCH_CHECK("key_tile_flags_kernel");
+        ++g_launches_total;
+    }
+    const int cols = d.S * d.d_k;
+    const int cpt = (cols + kKeyThreads - 1) / kKeyThreads;
+    if (g_pool_keys) {
+        // the key gradient needs the normalised queries unweighted and the aspect weights
+        launch_pdl(unweighted_queries_kernel, d.B, 32 * d.S, 0, st, f.q, aspect_weights, d.S, d.d_k, w.qh, w.ws);
+        DWA_LAUNCH_CHECK("unweighted_queries_kernel");
+        ++g_launches_total;
+    }
+    for (int b0 = 0; b0 < d.B; b0 += kBwdMaxQ) {
+        const int nb = std::min(kBwdMaxQ, d.B - b0);
+        const int qb = nb <= 8 ? 8 : nb <= 16 ? 16 : 32;
+        KeyGradArgs ka{};
+        ka.keys = keys; ka.N = d.N; ka.S = d.S; ka.d_k = d.d_k; ka.B = d.B; ka.b0 = b0; ka.nb = nb;
+        ka.G = w.G; ka.qh = w.qh; ka.w = w.ws; ka.tile_on = probed_only ? w.tile_on : nullptr;
+        ka.ntiles = ntiles; ka.partial = w.partial; ka.g_keys = g_pool_keys;
+        if (cpt > 2 && qb > 16) return fail(DWA_ERR_UNSUPPORTED, "retrieval VJP: S*d_k > 512 needs B <= 16 per pass");
+        const size_t sm = key_grad_smem(d.S, d.d_k, qb, g_pool_keys != nullptr);
+        if (sm > 200 * 1024) return fail(DWA_ERR_UNSUPPORTED, "retrieval VJP: S*d_k too large for the key tile");
+        void (*fn)(KeyGradArgs) = nullptr;
+        if (cpt == 1) fn = qb == 8 ? key_grad_pass_kernel<1, 8> : qb == 16 ? key_grad_pass_kernel<1, 16> : key_grad_pass_kernel<1, 32>;
+        else if (cpt == 2) fn = qb == 8 ? key_grad_pass_kernel<2, 8> : qb == 16 ? key_grad_pass_kernel<2, 16> : key_grad_pass_kernel<2, 32>;
+        else fn = qb == 8 ? key_grad_pass_kernel<4, 8> : key_grad_pass_kernel<4, 16>;
+        DWA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm)));
+        // one wave of persistent CTAs (at most the grid the partials were sized for)
+        int occ = 1, dv = 0, sms = 148;
+        DWA_CUDA_TRY(cudaGetDevice(&dv));
+        DWA_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dv));
+        DWA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kKeyThreads, sm));
+        const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(
+            {static_cast<int64_t>(w.grid), static_cast<int64_t>(std::max(occ, 1)) * sms, ntiles})));
+        DWA_TIMED("key_grad", st, launch_pdl(fn, grid, kKeyThreads, sm, st, ka));
+        DWA_LAUNCH_CHECK("key_grad_pass_kernel");
+        const int64_t width = static_cast<int64_t>(nb) * cols;
+        launch_pdl(partial_reduce_kernel, dim3(static_cast<unsigned>((width + 255) / 256), kPartGroups), 256, 0, st,
+                   w.partial, grid, width, w.part2);
+        DWA_LAUNCH_CHECK("partial_reduce_kernel");
+        g_launches_total += 2;
+        int rc = per_pass(b0, nb);
+        if (rc) return rc;
+    }
+    return DWA_OK;
+}
+
 }  // namespace dwa
 
 extern "C" size_t dwa_retrieve_bwd_workspace_bytes(const DwaRetrieveDims* dims, int use_ivf) {
@@ -681,61 +741,19 @@ extern "C" int dwa_retrieve_bwd(void* stream, const DwaRetrieveDims* dims, int u
         DWA_CUDA_TRY(cudaMemsetAsync(w.gtau, 0, static_cast<size_t>(d.B) * sizeof(float), st));
     }
     // 4. key pass: every row, or the tiles of probed lists when only the
-    //    selection has a cotangent and no key gradient is asked for
-    const int64_t ntiles = (d.N + kKeyTile - 1) / kKeyTile;
-    const bool probed_only = ivf && !g_soft_full && !g_pool_keys;
-    if (probed_only) {
-        DWA_CUDA_TRY(cudaMemsetAsync(w.tile_on, 0, static_cast<size_t>(ntiles), st));
-        launch_pdl(key_tile_flags_kernel, (d.B * f.m_eff + 127) / 128, 128, 0, st, f.topc, d.B, f.m_eff,
-                   list_offsets, int64_t(0), d.N, w.tile_on);
-        DWA_LAUNCH_CHECK("key_tile_flags_kernel");
-        ++g_launches_total;
-    }
+    //    selection has a cotangent and no key gradient is asked for;
+    // 5. the queries' gradients of each pass
     const int cols = d.S * d.d_k;
-    const int cpt = (cols + kKeyThreads - 1) / kKeyThreads;
-    if (g_pool_keys) {
-        // the key gradient needs the normalised queries unweighted and the aspect weights
-        launch_pdl(unweighted_queries_kernel, d.B, 32 * d.S, 0, st, f.q, aspect_weights, d.S, d.d_k, w.qh, w.ws);
-        DWA_LAUNCH_CHECK("unweighted_queries_kernel");
-        ++g_launches_total;
-    }
-    for (int b0 = 0; b0 < d.B; b0 += kBwdMaxQ) {
-        const int nb = std::min(kBwdMaxQ, d.B - b0);
-        const int qb = nb <= 8 ? 8 : nb <= 16 ? 16 : 32;
-        KeyGradArgs ka{};
-        ka.keys = pool_keys; ka.N = d.N; ka.S = d.S; ka.d_k = d.d_k; ka.B = d.B; ka.b0 = b0; ka.nb = nb;
-        ka.G = w.G; ka.qh = w.qh; ka.w = w.ws; ka.tile_on = probed_only ? w.tile_on : nullptr;
-        ka.ntiles = ntiles; ka.partial = w.partial; ka.g_keys = g_pool_keys;
-        if (cpt > 2 && qb > 16) return fail(DWA_ERR_UNSUPPORTED, "retrieval VJP: S*d_k > 512 needs B <= 16 per pass");
-        const size_t sm = key_grad_smem(d.S, d.d_k, qb, g_pool_keys != nullptr);
-        if (sm > 200 * 1024) return fail(DWA_ERR_UNSUPPORTED, "retrieval VJP: S*d_k too large for the key tile");
-        void (*fn)(KeyGradArgs) = nullptr;
-        if (cpt == 1) fn = qb == 8 ? key_grad_pass_kernel<1, 8> : qb == 16 ? key_grad_pass_kernel<1, 16> : key_grad_pass_kernel<1, 32>;
-        else if (cpt == 2) fn = qb == 8 ? key_grad_pass_kernel<2, 8> : qb == 16 ? key_grad_pass_kernel<2, 16> : key_grad_pass_kernel<2, 32>;
-        else fn = qb == 8 ? key_grad_pass_kernel<4, 8> : key_grad_pass_kernel<4, 16>;
-        DWA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm)));
-        // one wave of persistent CTAs (at most the grid the partials were sized for)
-        int occ = 1, dv = 0, sms = 148;
-        DWA_CUDA_TRY(cudaGetDevice(&dv));
-        DWA_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dv));
-        DWA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kKeyThreads, sm));
-        const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(
-            {static_cast<int64_t>(w.grid), static_cast<int64_t>(std::max(occ, 1)) * sms, ntiles})));
-        DWA_TIMED("key_grad", st, launch_pdl(fn, grid, kKeyThreads, sm, st, ka));
-        DWA_LAUNCH_CHECK("key_grad_pass_kernel");
-        ++g_launches_total;
-        // 5. the queries' gradients of this pass
-        const int64_t width = static_cast<int64_t>(nb) * cols;
-        launch_pdl(partial_reduce_kernel, dim3(static_cast<unsigned>((width + 255) / 256), kPartGroups), 256, 0, st,
-                   w.partial, grid, width, w.part2);
-        DWA_LAUNCH_CHECK("partial_reduce_kernel");
-        ++g_launches_total;
-        const int qthreads = (d.d_k + 31) / 32 * 32;
-        launch_pdl(query_grad_kernel, dim3(nb, d.S), qthreads, 0, st, w.part2, kPartGroups, nb, b0, cols, f.q,
-                   aspect_weights, d.S, d.d_k, w.gq, w.gw_part);
-        DWA_LAUNCH_CHECK("query_grad_kernel");
-        ++g_launches_total;
-    }
+    const int qthreads = (d.d_k + 31) / 32 * 32;
+    rc = run_key_pass(st, d, w, pool_keys, aspect_weights, list_offsets, 0, ivf && !g_soft_full && !g_pool_keys,
+                      g_pool_keys, [&](int b0, int nb) {
+                          launch_pdl(query_grad_kernel, dim3(nb, d.S), qthreads, 0, st, w.part2, kPartGroups, nb, b0,
+                                     cols, f.q, aspect_weights, d.S, d.d_k, w.gq, w.gw_part);
+                          DWA_LAUNCH_CHECK("query_grad_kernel");
+                          ++g_launches_total;
+                          return DWA_OK;
+                      });
+    if (rc) return rc;
     const int nchunk_o = (cols + kGradRowsPerCta - 1) / kGradRowsPerCta;
     const size_t gsh = static_cast<size_t>(d.B) * kGradRowsPerCta * sizeof(float);
     if (gsh > 48 * 1024) return fail(DWA_ERR_UNSUPPORTED, "retrieval VJP: B too large for the W_Q gradient");
@@ -1021,8 +1039,6 @@ extern "C" int dwa_retrieve_bwd_local2(void* stream, const DwaRetrieveDims* dims
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const RetWorkspace& f = w.f;
     float* scores = ivf ? f.scores : f.sfull;
-    const int nchunks = static_cast<int>((d.N + kSoftChunk - 1) / kSoftChunk);
-    (void)nchunks;
     if (g_soft_full) {
         const int nc = static_cast<int>((d.N + kSoftChunk - 1) / kSoftChunk);
         launch_pdl(soft_grad_kernel, dim3(nc, d.B), 256, 0, st, soft_full, g_soft_full, d.N, part1_sum + d.k + 1, 1,
@@ -1046,54 +1062,17 @@ extern "C" int dwa_retrieve_bwd_local2(void* stream, const DwaRetrieveDims* dims
     } else {
         DWA_CUDA_TRY(cudaMemsetAsync(w.gtau, 0, static_cast<size_t>(d.B) * sizeof(float), st));
     }
-    const int64_t ntiles = (d.N + kKeyTile - 1) / kKeyTile;
-    const bool probed_only = ivf && !g_soft_full && !g_pool_keys;
-    if (probed_only) {
-        DWA_CUDA_TRY(cudaMemsetAsync(w.tile_on, 0, static_cast<size_t>(ntiles), st));
-        launch_pdl(key_tile_flags_kernel, (d.B * f.m_eff + 127) / 128, 128, 0, st, f.topc, d.B, f.m_eff,
-                   list_offsets, shard->row_lo, d.N, w.tile_on);
-        DWA_LAUNCH_CHECK("key_tile_flags_kernel");
-        ++g_launches_total;
-    }
     const int cols = d.S * d.d_k;
-    const int cpt = (cols + kKeyThreads - 1) / kKeyThreads;
-    if (g_pool_keys) {
-        launch_pdl(unweighted_queries_kernel, d.B, 32 * d.S, 0, st, f.q, aspect_weights, d.S, d.d_k, w.qh, w.ws);
-        DWA_LAUNCH_CHECK("unweighted_queries_kernel");
-        ++g_launches_total;
-    }
-    for (int b0 = 0; b0 < d.B; b0 += kBwdMaxQ) {
-        const int nb = std::min(kBwdMaxQ, d.B - b0);
-        const int qb = nb <= 8 ? 8 : nb <= 16 ? 16 : 32;
-        KeyGradArgs ka{};
-        ka.keys = local_keys; ka.N = d.N; ka.S = d.S; ka.d_k = d.d_k; ka.B = d.B; ka.b0 = b0; ka.nb = nb;
-        ka.G = w.G; ka.qh = w.qh; ka.w = w.ws; ka.tile_on = probed_only ? w.tile_on : nullptr;
-        ka.ntiles = ntiles; ka.partial = w.partial; ka.g_keys = g_pool_keys;
-        if (cpt > 2 && qb > 16) return fail(DWA_ERR_UNSUPPORTED, "retrieval VJP: S*d_k > 512 needs B <= 16 per pass");
-        const size_t sm = key_grad_smem(d.S, d.d_k, qb, g_pool_keys != nullptr);
-        if (sm > 200 * 1024) return fail(DWA_ERR_UNSUPPORTED, "retrieval VJP: S*d_k too large for the key tile");
-        void (*fn)(KeyGradArgs) = nullptr;
-        if (cpt == 1) fn = qb == 8 ? key_grad_pass_kernel<1, 8> : qb == 16 ? key_grad_pass_kernel<1, 16> : key_grad_pass_kernel<1, 32>;
-        else if (cpt == 2) fn = qb == 8 ? key_grad_pass_kernel<2, 8> : qb == 16 ? key_grad_pass_kernel<2, 16> : key_grad_pass_kernel<2, 32>;
-        else fn = qb == 8 ? key_grad_pass_kernel<4, 8> : key_grad_pass_kernel<4, 16>;
-        DWA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm)));
-        int occ = 1, dv = 0, sms = 148;
-        DWA_CUDA_TRY(cudaGetDevice(&dv));
-        DWA_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dv));
-        DWA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kKeyThreads, sm));
-        const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(
-            {static_cast<int64_t>(w.grid), static_cast<int64_t>(std::max(occ, 1)) * sms, ntiles})));
-        launch_pdl(fn, grid, kKeyThreads, sm, st, ka);
-        DWA_LAUNCH_CHECK("key_grad_pass_kernel");
-        const int64_t width = static_cast<int64_t>(nb) * cols;
-        launch_pdl(partial_reduce_kernel, dim3(static_cast<unsigned>((width + 255) / 256), kPartGroups), 256, 0, st,
-                   w.partial, grid, width, w.part2);
-        DWA_LAUNCH_CHECK("partial_reduce_kernel");
-        launch_pdl(a_final_kernel, static_cast<unsigned>((width + nb + 255) / 256), 256, 0, st, w.part2, nb, b0, cols,
-                   w.gtau, part2);
-        DWA_LAUNCH_CHECK("a_final_kernel");
-        g_launches_total += 3;
-    }
+    rc = run_key_pass(st, d, w, local_keys, aspect_weights, list_offsets, shard->row_lo,
+                      ivf && !g_soft_full && !g_pool_keys, g_pool_keys, [&](int b0, int nb) {
+                          const int64_t width = static_cast<int64_t>(nb) * cols;
+                          launch_pdl(a_final_kernel, static_cast<unsigned>((width + nb + 255) / 256), 256, 0, st,
+                                     w.part2, nb, b0, cols, w.gtau, part2);
+                          DWA_LAUNCH_CHECK("a_final_kernel");
+                          ++g_launches_total;
+                          return DWA_OK;
+                      });
+    if (rc) return rc;
     return DWA_OK;
 }
 
