@@ -343,6 +343,19 @@ typedef struct DwaAuxDims {
 typedef struct DwaAuxWeights {
     float util, div, norm, sparse;   /* lambda_util, lambda_div, lambda_norm, lambda_sparse */
 } DwaAuxWeights;
+/* Over a row-sharded pool: this rank holds pool / key / soft_full rows
+ * [row_lo, row_lo + dims->N) of n_global and the assembled W of w_batch of the
+ * dims->B sequences (its own).  Phase 1 (dwa_aux_losses_local): part [2] =
+ * this rank's shares of l_util's and l_norm's sums, rk_part [B, k, d_k] = the
+ * aspect-mean keys of the winners it holds (zeros elsewhere), g_soft_full of
+ * its rows, g_W of its sequences, its share of g_W_base.  The caller sums
+ * part, rk_part and g_W_base over the ranks.  Phase 2 (dwa_aux_losses_finish,
+ * the same workspace size): losses[5], g_alphas, and l_div's key gradient
+ * added into this rank's rows of g_pool_keys. */
+typedef struct DwaAuxShard {
+    int64_t row_lo, n_global;
+    int32_t w_batch;
+} DwaAuxShard;
 DWA_API size_t dwa_aux_losses_workspace_bytes(const DwaAuxDims* dims);
 DWA_API int dwa_aux_losses(void* stream, const DwaAuxDims* dims, const DwaAuxWeights* lambdas,
                            const float* alphas, const int32_t* indices, const float* pool_keys,
@@ -350,6 +363,17 @@ DWA_API int dwa_aux_losses(void* stream, const DwaAuxDims* dims, const DwaAuxWei
                            float* losses, float* g_alphas, float* g_soft_full, float* g_W,
                            float* g_W_base, float* g_pool_keys, void* workspace,
                            size_t workspace_bytes);
+DWA_API int dwa_aux_losses_local(void* stream, const DwaAuxDims* dims, const DwaAuxShard* shard,
+                                 const DwaAuxWeights* lambdas, const int32_t* indices,
+                                 const float* local_keys, const float* W, const float* W_base,
+                                 const float* soft_full, float* part, float* rk_part,
+                                 float* g_soft_full, float* g_W, float* g_W_base_part,
+                                 void* workspace, size_t workspace_bytes);
+DWA_API int dwa_aux_losses_finish(void* stream, const DwaAuxDims* dims, const DwaAuxShard* shard,
+                                  const DwaAuxWeights* lambdas, const float* alphas,
+                                  const int32_t* indices, const float* part_sum, const float* rk_sum,
+                                  float* losses, float* g_alphas, float* g_pool_keys, void* workspace,
+                                  size_t workspace_bytes);
 
 /* ---------------------------------------------------------------------------
  * Key cache.  Replaces compute_key_cache (src/dwa/assembly_pallas.py:392-400) and

@@ -61,6 +61,10 @@ class AuxDims(C.Structure):
                 ("d_B", C.c_int32), ("d_A", C.c_int32), ("N", C.c_int64)]
 
 
+class AuxShard(C.Structure):
+    _fields_ = [("row_lo", C.c_int64), ("n_global", C.c_int64), ("w_batch", C.c_int32)]
+
+
 class AuxWeights(C.Structure):
     _fields_ = [("util", C.c_float), ("div", C.c_float), ("norm", C.c_float), ("sparse", C.c_float)]
 
@@ -113,6 +117,10 @@ _SIGNATURES = {
     "dwa_ipc_close": (C.c_int, [_P, C.c_int64]),
     "dwa_gather_rows_workspace_bytes": (C.c_size_t, []),
     "dwa_gather_rows": (C.c_int, [_P, C.c_int, C.c_int64, C.c_int, _P, C.POINTER(PoolShards), _P, _P, C.c_size_t]),
+    "dwa_aux_losses_local": (C.c_int, [_P, C.POINTER(AuxDims), C.POINTER(AuxShard), C.POINTER(AuxWeights),
+                                       _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t]),
+    "dwa_aux_losses_finish": (C.c_int, [_P, C.POINTER(AuxDims), C.POINTER(AuxShard), C.POINTER(AuxWeights),
+                                        _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t]),
     "dwa_aux_losses_workspace_bytes": (C.c_size_t, [C.POINTER(AuxDims)]),
     "dwa_aux_losses": (C.c_int, [_P, C.POINTER(AuxDims), C.POINTER(AuxWeights), _P, _P, _P, _P, _P, _P, _P,
                                  _P, _P, _P, _P, _P, _P, C.c_size_t]),

@@ -56,6 +56,7 @@ struct AuxQueryArgs {
     float* g_alphas;           // [B, k] or null
     float* g_rk;               // [B, k, d_k] (already / S) or null
     uint32_t* status;
+    const float* rk_in;        // [B, k, d_k] aspect-mean keys given (a sharded pool's finish) or null
 };
 
 // One CTA per query: l_sparse and its gradient, the query's l_util share and
@@ -84,9 +85,9 @@ __global__ void __launch_bounds__(kAuxThreads) aux_query_kernel(AuxQueryArgs a) 
         }
     }
     sp = aux_block_sum(sp, red);
-    // l_util share: Σ_j Σ_b' soft[b', idx[b, j]]
+    // l_util share: Σ_j Σ_b' soft[b', idx[b, j]] (none without soft_full: a sharded finish)
     float ut = 0.f;
-    for (int i = tid; i < k; i += blockDim.x) {
+    for (int i = tid; i < k && a.soft; i += blockDim.x) {
         const int64_t n = ix[i];
         if (n < 0 || n >= a.N) { raise_status(a.status, DWA_STATUS_BAD_ROW_INDEX); continue; }
         float c = 0.f;
@@ -96,6 +97,10 @@ __global__ void __launch_bounds__(kAuxThreads) aux_query_kernel(AuxQueryArgs a) 
     ut = aux_block_sum(ut, red);
     // aspect-mean keys of the k retrieved rows
     for (int e = tid; e < k * d_k; e += blockDim.x) {
+        if (a.rk_in) {
+            rk[e] = a.rk_in[static_cast<int64_t>(b) * k * d_k + e];
+            continue;
+        }
         const int i = e / d_k, d = e - i * d_k;
         int64_t n = ix[i];
         n = n < 0 ? 0 : n >= a.N ? a.N - 1 : n;
@@ -188,18 +193,21 @@ __global__ void __launch_bounds__(kAuxThreads) aux_norm_kernel(const float* __re
 
 // Selection counts of the pool rows, then g_soft[b, n] = scale * cnt[n] on the
 // selected columns (the rest of g_soft is zeroed before).
-__global__ void aux_count_kernel(const int32_t* __restrict__ idx, int n, int64_t N, int* __restrict__ cnt) {
+__global__ void aux_count_kernel(const int32_t* __restrict__ idx, int n, int64_t row_lo, int64_t N,
+                                 int* __restrict__ cnt) {
     pdl_enter();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n && idx[i] >= 0 && idx[i] < N) atomicAdd(&cnt[idx[i]], 1);
+    if (i >= n) return;
+    const int64_t r = static_cast<int64_t>(idx[i]) - row_lo;
+    if (r >= 0 && r < N) atomicAdd(&cnt[r], 1);
 }
 
-__global__ void aux_soft_grad_kernel(const int32_t* __restrict__ idx, int n, int B, int64_t N,
+__global__ void aux_soft_grad_kernel(const int32_t* __restrict__ idx, int n, int B, int64_t row_lo, int64_t N,
                                      const int* __restrict__ cnt, float scale, float* __restrict__ g_soft) {
     pdl_enter();
     const int i = blockIdx.x;
     if (i >= n) return;
-    const int64_t c = idx[i];
+    const int64_t c = static_cast<int64_t>(idx[i]) - row_lo;
     if (c < 0 || c >= N) return;
     const float v = scale * static_cast<float>(cnt[c]);
     for (int b = threadIdx.x; b < B; b += blockDim.x) g_soft[static_cast<int64_t>(b) * N + c] = v;
@@ -222,6 +230,77 @@ __global__ void aux_finish_kernel(const float* __restrict__ qpart, int B, int k,
     const float l_util = static_cast<float>(N) / (fB * fB * static_cast<float>(k)) * u;
     const float l_div = dv / (static_cast<float>(static_cast<int64_t>(k) * (k - 1) / 2) * fB + 1e-8f);
     const float l_norm = nm / fB;
+    const float l_sparse = sp / fB;
+    losses[0] = l_util;
+    losses[1] = l_div;
+    losses[2] = l_norm;
+    losses[3] = l_sparse;
+    losses[4] = lu * l_util + ld * l_div + ln * l_norm + ls * l_sparse;
+}
+
+// A rank of a row-sharded pool, per query: its share of l_util's sum (the
+// selected columns it holds) and the aspect-mean keys of the winners it holds
+// (zeros for the others), so that a sum over the ranks gives every winner's.
+__global__ void __launch_bounds__(kAuxThreads) aux_local_kernel(const int32_t* __restrict__ indices, int k,
+                                                               int B, int S, int d_k, int64_t row_lo,
+                                                               int64_t n_loc, const float* __restrict__ keys,
+                                                               const float* __restrict__ soft,
+                                                               float* __restrict__ ushare,
+                                                               float* __restrict__ rk_out) {
+    pdl_enter();
+    __shared__ float red[33];
+    const int b = blockIdx.x, tid = threadIdx.x;
+    const int32_t* ix = indices + static_cast<int64_t>(b) * k;
+    float ut = 0.f;
+    for (int i = tid; i < k && soft; i += blockDim.x) {
+        const int64_t n = static_cast<int64_t>(ix[i]) - row_lo;
+        if (n < 0 || n >= n_loc) continue;
+        float c = 0.f;
+        for (int bb = 0; bb < B; ++bb) c += soft[static_cast<int64_t>(bb) * n_loc + n];
+        ut += c;
+    }
+    ut = aux_block_sum(ut, red);
+    if (tid == 0) ushare[b] = ut;
+    for (int e = tid; e < k * d_k; e += blockDim.x) {
+        const int i = e / d_k, d = e - i * d_k;
+        const int64_t n = static_cast<int64_t>(ix[i]) - row_lo;
+        float acc = 0.f;
+        if (n >= 0 && n < n_loc) {
+            for (int s = 0; s < S; ++s) acc += keys[(static_cast<int64_t>(s) * n_loc + n) * d_k + d];
+            acc /= static_cast<float>(S);
+        }
+        rk_out[static_cast<int64_t>(b) * k * d_k + e] = acc;
+    }
+}
+
+// part[0] = Σ_b ushare[b], part[1] = Σ of the l_norm partials, in order.
+__global__ void aux_local_sums_kernel(const float* __restrict__ ushare, int B, const float* __restrict__ npart,
+                                      int nn, float* __restrict__ part) {
+    pdl_enter();
+    if (threadIdx.x != 0) return;
+    float u = 0.f, nm = 0.f;
+    for (int b = 0; b < B; ++b) u += ushare[b];
+    for (int i = 0; i < nn; ++i) nm += npart[i];
+    part[0] = u;
+    part[1] = nm;
+}
+
+// The losses of a sharded call from the summed part (l_util's sum, l_norm's
+// sum) and the per-query l_div / l_sparse terms of the finish.
+__global__ void aux_finish_sharded_kernel(const float* __restrict__ part_sum, const float* __restrict__ qpart, int B,
+                                          int k, int64_t N, float lu, float ld, float ln, float ls,
+                                          float* __restrict__ losses) {
+    pdl_enter();
+    if (threadIdx.x != 0) return;
+    float dv = 0.f, sp = 0.f;
+    for (int b = 0; b < B; ++b) {
+        dv += qpart[3 * b + 1];
+        sp += qpart[3 * b + 2];
+    }
+    const float fB = static_cast<float>(B);
+    const float l_util = static_cast<float>(N) / (fB * fB * static_cast<float>(k)) * part_sum[0];
+    const float l_div = dv / (static_cast<float>(static_cast<int64_t>(k) * (k - 1) / 2) * fB + 1e-8f);
+    const float l_norm = part_sum[1] / fB;
     const float l_sparse = sp / fB;
     losses[0] = l_util;
     losses[1] = l_div;
@@ -321,10 +400,10 @@ extern "C" int dwa_aux_losses(void* stream, const DwaAuxDims* dims, const DwaAux
     if (g_soft_full) {
         DWA_CUDA_TRY(cudaMemsetAsync(g_soft_full, 0, static_cast<size_t>(d.B) * d.N * sizeof(float), st));
         DWA_CUDA_TRY(cudaMemsetAsync(w.cnt, 0, static_cast<size_t>(d.N) * sizeof(int), st));
-        launch_pdl(aux_count_kernel, (n + 255) / 256, 256, 0, st, indices, n, d.N, w.cnt);
+        launch_pdl(aux_count_kernel, (n + 255) / 256, 256, 0, st, indices, n, int64_t(0), d.N, w.cnt);
         DWA_LAUNCH_CHECK("aux_count_kernel");
         const float fB = static_cast<float>(d.B);
-        launch_pdl(aux_soft_grad_kernel, n, 32, 0, st, indices, n, d.B, d.N, w.cnt,
+        launch_pdl(aux_soft_grad_kernel, n, 32, 0, st, indices, n, d.B, int64_t(0), d.N, w.cnt,
                    lambdas->util * static_cast<float>(d.N) / (fB * fB * static_cast<float>(d.k)), g_soft_full);
         DWA_LAUNCH_CHECK("aux_soft_grad_kernel");
         g_launches_total += 2;
@@ -339,6 +418,95 @@ extern "C" int dwa_aux_losses(void* stream, const DwaAuxDims* dims, const DwaAux
             rc = dwa_pool_grad_scatter(stream, n, d.d_k, indices, w.g_rk, d.N, 0, d.N, DWA_F32,
                                        g_pool_keys + static_cast<int64_t>(s) * d.N * d.d_k, w.scatter_ws,
                                        w.scatter_bytes);
+            if (rc) return rc;
+        }
+    }
+    return DWA_OK;
+}
+
+extern "C" int dwa_aux_losses_local(void* stream, const DwaAuxDims* dims, const DwaAuxShard* shard,
+                                    const DwaAuxWeights* lambdas, const int32_t* indices, const float* local_keys,
+                                    const float* W, const float* W_base, const float* soft_full, float* part,
+                                    float* rk_part, float* g_soft_full, float* g_W, float* g_W_base_part,
+                                    void* workspace, size_t workspace_bytes) {
+    int rc = check_aux(dims);
+    if (rc) return rc;
+    const DwaAuxDims& d = *dims;
+    if (!shard || shard->row_lo < 0 || shard->n_global < shard->row_lo + d.N || shard->w_batch < 0 ||
+        shard->w_batch > d.B)
+        return fail(DWA_ERR_INVALID_ARG, "shard: need row_lo + N <= n_global and 0 <= w_batch <= B");
+    if (!lambdas || !indices || !local_keys || !W_base || !soft_full || !part || !rk_part || (shard->w_batch && !W))
+        return fail(DWA_ERR_INVALID_ARG, "a required pointer is NULL");
+    const AuxWorkspace w = carve_aux(workspace, d);
+    if (!workspace || reinterpret_cast<uintptr_t>(workspace) % 256 != 0 || workspace_bytes < w.bytes)
+        return fail(DWA_ERR_WORKSPACE, "workspace: dwa_aux_losses_workspace_bytes, 256-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    launch_pdl(aux_local_kernel, d.B, kAuxThreads, 0, st, indices, d.k, d.B, d.S, d.d_k, shard->row_lo, d.N,
+               local_keys, soft_full, w.qpart, rk_part);
+    DWA_LAUNCH_CHECK("aux_local_kernel");
+    const int64_t E = static_cast<int64_t>(d.d_B) * d.d_A;
+    if (shard->w_batch > 0) {
+        launch_pdl(aux_norm_kernel, w.nn, kAuxThreads, 0, st, W, W_base, static_cast<int>(shard->w_batch), E,
+                   2.f * lambdas->norm / static_cast<float>(d.B), g_W, g_W_base_part, w.npart);
+        DWA_LAUNCH_CHECK("aux_norm_kernel");
+    } else {
+        DWA_CUDA_TRY(cudaMemsetAsync(w.npart, 0, static_cast<size_t>(w.nn) * sizeof(float), st));
+        if (g_W_base_part) DWA_CUDA_TRY(cudaMemsetAsync(g_W_base_part, 0, static_cast<size_t>(E) * sizeof(float), st));
+    }
+    launch_pdl(aux_local_sums_kernel, 1, 32, 0, st, w.qpart, d.B, w.npart, w.nn, part);
+    DWA_LAUNCH_CHECK("aux_local_sums_kernel");
+    g_launches_total += 3;
+    const int n = d.B * d.k;
+    if (g_soft_full) {
+        DWA_CUDA_TRY(cudaMemsetAsync(g_soft_full, 0, static_cast<size_t>(d.B) * d.N * sizeof(float), st));
+        DWA_CUDA_TRY(cudaMemsetAsync(w.cnt, 0, static_cast<size_t>(d.N) * sizeof(int), st));
+        launch_pdl(aux_count_kernel, (n + 255) / 256, 256, 0, st, indices, n, shard->row_lo, d.N, w.cnt);
+        DWA_LAUNCH_CHECK("aux_count_kernel");
+        const float fB = static_cast<float>(d.B);
+        launch_pdl(aux_soft_grad_kernel, n, 32, 0, st, indices, n, d.B, shard->row_lo, d.N, w.cnt,
+                   lambdas->util * static_cast<float>(shard->n_global) / (fB * fB * static_cast<float>(d.k)),
+                   g_soft_full);
+        DWA_LAUNCH_CHECK("aux_soft_grad_kernel");
+        g_launches_total += 2;
+    }
+    return DWA_OK;
+}
+
+extern "C" int dwa_aux_losses_finish(void* stream, const DwaAuxDims* dims, const DwaAuxShard* shard,
+                                     const DwaAuxWeights* lambdas, const float* alphas, const int32_t* indices,
+                                     const float* part_sum, const float* rk_sum, float* losses, float* g_alphas,
+                                     float* g_pool_keys, void* workspace, size_t workspace_bytes) {
+    int rc = check_aux(dims);
+    if (rc) return rc;
+    const DwaAuxDims& d = *dims;
+    if (!shard || shard->row_lo < 0 || shard->n_global < shard->row_lo + d.N)
+        return fail(DWA_ERR_INVALID_ARG, "shard: need row_lo + N <= n_global");
+    if (!lambdas || !alphas || !indices || !part_sum || !rk_sum || !losses)
+        return fail(DWA_ERR_INVALID_ARG, "a required pointer is NULL");
+    const AuxWorkspace w = carve_aux(workspace, d);
+    if (!workspace || reinterpret_cast<uintptr_t>(workspace) % 256 != 0 || workspace_bytes < w.bytes)
+        return fail(DWA_ERR_WORKSPACE, "workspace: dwa_aux_losses_workspace_bytes, 256-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    AuxQueryArgs qa{};
+    qa.B = d.B; qa.k = d.k; qa.S = d.S; qa.d_k = d.d_k; qa.N = d.N;
+    qa.lam_div = lambdas->div; qa.lam_sparse = lambdas->sparse;
+    qa.alphas = alphas; qa.indices = indices; qa.keys = nullptr; qa.soft = nullptr; qa.rk_in = rk_sum;
+    qa.part = w.qpart; qa.g_alphas = g_alphas; qa.g_rk = g_pool_keys ? w.g_rk : nullptr;
+    qa.status = static_cast<uint32_t*>(workspace);
+    const size_t qsh = (static_cast<size_t>(d.k) * d.d_k + d.d_k + 2 * d.k) * sizeof(float);
+    DWA_CUDA_TRY(cudaFuncSetAttribute(aux_query_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    launch_pdl(aux_query_kernel, d.B, kAuxThreads, qsh, st, qa);
+    DWA_LAUNCH_CHECK("aux_query_kernel");
+    launch_pdl(aux_finish_sharded_kernel, 1, 32, 0, st, part_sum, w.qpart, d.B, d.k, shard->n_global, lambdas->util,
+               lambdas->div, lambdas->norm, lambdas->sparse, losses);
+    DWA_LAUNCH_CHECK("aux_finish_sharded_kernel");
+    g_launches_total += 2;
+    if (g_pool_keys) {
+        const int n = d.B * d.k;
+        for (int s = 0; s < d.S; ++s) {
+            rc = dwa_pool_grad_scatter(stream, n, d.d_k, indices, w.g_rk, shard->n_global, shard->row_lo,
+                                       shard->row_lo + d.N, DWA_F32, g_pool_keys + static_cast<int64_t>(s) * d.N * d.d_k,
+                                       w.scatter_ws, w.scatter_bytes);
             if (rc) return rc;
         }
     }

@@ -104,3 +104,58 @@ def aux_losses_with_grad(alphas, indices, pool_keys, W, W_base, soft_full, **lam
     lam = {**DEFAULT_LAMBDAS, **lambdas}
     total, parts = _AuxLossFunction.apply(alphas, soft_full, W, W_base, pool_keys, indices, lam)
     return total, dict(zip(NAMES[:4], parts.detach().unbind()))
+
+
+def sharded_aux_losses_and_grads(alphas, indices, local_keys, W_local, W_base, soft_local, *, row_lo, n_global,
+                                 group=None, key_grad_into=None, reduce=None, **lambdas):
+    """``aux_losses`` and its gradients over a row-sharded pool: this rank holds
+    the key / soft_full rows ``[row_lo, row_lo + rows)`` and the assembled W of
+    its own sequences.  One all-reduce (``reduce``; default ``dist.all_reduce``
+    over ``group``) sums the ranks' ``l_util`` / ``l_norm`` shares, the winners'
+    aspect-mean keys and ``g_W_base``.  Returns ``(losses, grads)``: the losses
+    and ``g_alphas`` / ``g_W_base`` are the same on every rank; ``g_soft_full``
+    and ``g_W`` are this rank's slices; the key gradient of its rows is added
+    into ``key_grad_into``."""
+    import torch.distributed as dist
+    lam = {**DEFAULT_LAMBDAS, **lambdas}
+    dev = alphas.device
+    B, k = alphas.shape
+    S, n_loc, d_k = local_keys.shape
+    d_B, d_A = W_base.shape
+    w_batch = 0 if W_local is None else W_local.shape[0]
+    dims = _lib.AuxDims(B, k, S, d_k, d_B, d_A, max(n_loc, 1))
+    shard = _lib.AuxShard(int(row_lo), int(n_global), int(w_batch))
+    weights = _lib.AuxWeights(lam["lambda_util"], lam["lambda_div"], lam["lambda_norm"], lam["lambda_sparse"])
+    idx = indices.int().contiguous()
+    f32 = dict(dtype=torch.float32, device=dev)
+    part, rk = torch.zeros(2, **f32), torch.zeros((B, k, d_k), **f32)
+    g = dict(g_alphas=torch.empty((B, k), **f32), g_soft_full=torch.zeros((B, n_loc), **f32),
+             g_W=torch.empty((w_batch, d_B, d_A), **f32), g_W_base=torch.zeros((d_B, d_A), **f32))
+    lib = _lib.load()
+    ws = workspace(dev, "aux_losses_sharded", lib.dwa_aux_losses_workspace_bytes(dims))
+    if n_loc > 0 or w_batch > 0:
+        keys = local_keys if n_loc > 0 else torch.zeros((S, 1, d_k), **f32)
+        soft = soft_local.float().contiguous() if n_loc > 0 else torch.zeros((B, 1), **f32)
+        with torch.cuda.device(dev):
+            rc = lib.dwa_aux_losses_local(stream_of(dev), dims, shard, weights, ptr(idx), ptr(keys.contiguous()),
+                                          ptr(W_local.float().contiguous()) if w_batch else None,
+                                          ptr(W_base.float().contiguous()), ptr(soft), ptr(part), ptr(rk),
+                                          ptr(g["g_soft_full"]) if n_loc > 0 else None,
+                                          ptr(g["g_W"]) if w_batch else None, ptr(g["g_W_base"]), ptr(ws),
+                                          ws.numel())
+        _lib.check(rc, "dwa_aux_losses_local")
+    if reduce is None:
+        world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        if world > 1:
+            for t in (part, rk, g["g_W_base"]):
+                dist.all_reduce(t, group=group)
+    else:
+        part, rk, g["g_W_base"] = reduce(part, rk, g["g_W_base"])
+    losses = torch.empty(5, **f32)
+    with torch.cuda.device(dev):
+        rc = lib.dwa_aux_losses_finish(stream_of(dev), dims, shard, weights, ptr(alphas.float().contiguous()), ptr(idx),
+                                       ptr(part.contiguous()), ptr(rk.contiguous()), ptr(losses), ptr(g["g_alphas"]),
+                                       ptr(key_grad_into) if (key_grad_into is not None and n_loc > 0) else None,
+                                       ptr(ws), ws.numel())
+    _lib.check(rc, "dwa_aux_losses_finish")
+    return dict(zip(NAMES, losses.unbind())), g

@@ -92,3 +92,50 @@ def test_autograd_total_matches_explicit_grads():
     for k_ in ("alphas", "soft_full", "W", "W_base"):
         np.testing.assert_allclose(leaves[k_].grad.cpu().numpy(), 3.0 * g["g_" + k_].cpu().numpy(), rtol=1e-6)
     np.testing.assert_allclose(leaves["pool_keys"].grad.cpu().numpy(), 3.0 * gk.cpu().numpy(), rtol=1e-6)
+
+
+@pytest.mark.parametrize("bounds,seqs", [([0, 9000, 20000], [0, 3, 8]), ([0, 7000, 7000, 20000], [0, 4, 4, 8])])
+def test_sharded_aux_equals_single_call(bounds, seqs):
+    """Ranks emulated on one GPU (rows and sequences split, an empty rank):
+    the losses and g_alphas / g_W_base on every rank, and the ranks' slices of
+    g_soft_full, g_W and the key gradient, equal the single call's."""
+    from matrix_b200.losses import aux_losses_and_grads, sharded_aux_losses_and_grads
+    x = _case(seed=5)
+    d = _dev(x)
+    gk_ref = torch.zeros_like(d["pool_keys"])
+    ref, rg = aux_losses_and_grads(**d, key_grad_into=gk_ref, **LAM)
+    world = len(bounds) - 1
+    parts = [(bounds[r], bounds[r + 1], seqs[r], seqs[r + 1]) for r in range(world)]
+    # phase 1 on every rank, then the sums, then phase 2 on every rank
+    collected = []
+
+    def run(r, reduce):
+        lo, hi, s0, s1 = parts[r]
+        gk = torch.zeros((d["pool_keys"].shape[0], hi - lo, d["pool_keys"].shape[2]), device="cuda")
+        W_loc = d["W"][s0:s1].contiguous() if s1 > s0 else None
+        out = sharded_aux_losses_and_grads(d["alphas"], d["indices"], d["pool_keys"][:, lo:hi].contiguous(), W_loc,
+                                           d["W_base"], d["soft_full"][:, lo:hi].contiguous(), row_lo=lo,
+                                           n_global=d["soft_full"].shape[1], key_grad_into=gk, reduce=reduce, **LAM)
+        return out, gk
+
+    def gather(part, rk, gwb):
+        collected.append((part.clone(), rk.clone(), gwb.clone()))
+        return part, rk, gwb
+
+    for r in range(world):          # phase 1 only: record every rank's partials
+        run(r, gather)
+    sums = [sum(c[i] for c in collected) for i in range(3)]
+    results = [run(r, lambda p, rk, g: tuple(t.clone() for t in sums)) for r in range(world)]
+    torch.cuda.synchronize()
+    for (losses, g), gk in results:
+        for name in ("l_util", "l_div", "l_norm", "l_sparse", "total_aux"):
+            r_ = float(ref[name])
+            assert abs(float(losses[name]) - r_) <= TOL * max(abs(r_), 1e-3), name
+        assert_close(g["g_alphas"].cpu().numpy(), rg["g_alphas"].cpu().numpy(), TOL, name="g_alphas")
+        assert_close(g["g_W_base"].cpu().numpy(), rg["g_W_base"].cpu().numpy(), TOL, name="g_W_base")
+    assert_close(np.concatenate([g["g_soft_full"].cpu().numpy() for (_, g), _ in results], axis=1),
+                 rg["g_soft_full"].cpu().numpy(), TOL, name="g_soft_full")
+    assert_close(np.concatenate([g["g_W"].cpu().numpy() for (_, g), _ in results], axis=0),
+                 rg["g_W"].cpu().numpy(), TOL, name="g_W")
+    assert_close(np.concatenate([gk.cpu().numpy() for _, gk in results], axis=1), gk_ref.cpu().numpy(), TOL,
+                 name="g_pool_keys")
