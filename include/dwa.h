@@ -148,6 +148,24 @@ DWA_API int dwa_assemble_fwd(void* stream, const DwaAssembleDims* dims,
                      void* workspace, size_t workspace_bytes);
 
 /* ---------------------------------------------------------------------------
+ * Assembly apply, h_mid only.  Replaces the Pallas kernel itself
+ * (src/dwa/assembly_pallas.py:85-132 with the pre-factoring of :139-181) when
+ * the caller does not use W (generation, train.py:615-616, where XLA drops the
+ * W recompute of :212-221):
+ *   h_mid[b] = h_A[b] + gamma (h_A[b] W_base^T + (h_A[b] V_s^T) U_f) + pb[b]
+ * Same arguments and meaning as dwa_assemble_fwd without W_out / W_act.  For
+ * T <= 16 rows per sequence it runs the factored form (each gathered row read
+ * once, W never formed); longer sequences take dwa_assemble_fwd's path.
+ * ------------------------------------------------------------------------- */
+DWA_API size_t dwa_assemble_apply_workspace_bytes(const DwaAssembleDims* dims);
+
+DWA_API int dwa_assemble_apply(void* stream, const DwaAssembleDims* dims,
+                     const void* rows, const int32_t* row_index,
+                     const float* alphas, const void* h_A,
+                     const float* W_base, const float* b_base, const float* gamma,
+                     void* h_mid, void* workspace, size_t workspace_bytes);
+
+/* ---------------------------------------------------------------------------
  * Assembly backward.  Replaces _pallas_assemble_bwd
  * (src/dwa/assembly_pallas.py:246-329) for the residuals
  * (rows/row_index, alphas, h_A, W, gamma) and cotangents (g_hmid, g_W_out).

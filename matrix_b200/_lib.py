@@ -83,6 +83,9 @@ _SIGNATURES = {
     "dwa_assemble_workspace_bytes": (C.c_size_t, [C.POINTER(AssembleDims), C.c_int]),
     "dwa_assemble_fwd": (C.c_int, [_P, C.POINTER(AssembleDims), _P, _P, _P, _P, _P, _P, _P,
                                    _P, _P, _P, _P, C.c_size_t]),
+    "dwa_assemble_apply_workspace_bytes": (C.c_size_t, [C.POINTER(AssembleDims)]),
+    "dwa_assemble_apply": (C.c_int, [_P, C.POINTER(AssembleDims), _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                     C.c_size_t]),
     "dwa_assemble_bwd": (C.c_int, [_P, C.POINTER(AssembleDims), _P, _P, _P, _P, _P, _P, _P, _P,
                                    _P, _P, _P, _P, _P, _P, _P, C.c_size_t]),
     "dwa_retrieve_workspace_bytes": (C.c_size_t, [C.POINTER(RetrieveDims), C.c_int, C.c_int]),

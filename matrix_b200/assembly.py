@@ -12,7 +12,8 @@ Drop-in for the reference's ``src/dwa/assembly_pallas.py``:
   and ``gamma`` are summed over the process group in the backward pass.
 * :func:`assemble_forward` / :func:`assemble_backward` expose the two C-ABI
   calls directly, including the fused-gather form that reads pool rows by index
-  instead of a materialised ``gathered`` tensor (model.py:184-195).
+  instead of a materialised ``gathered`` tensor (model.py:184-195);
+  :func:`assemble_apply` is the h_mid-only call (no W) for generation.
 
 Nothing here computes on the CPU: every entry point requires CUDA tensors and
 the built library.
@@ -93,6 +94,33 @@ def assemble_forward(rows, alphas, h_A, W_base, b_base, gamma, d_B, r, d_A, *,
                                   ptr(W), ptr(W_act), ptr(ws), ws.numel())
     _lib.check(rc, "dwa_assemble_fwd")
     return h_mid, W, W_act
+
+
+def assemble_apply(rows, alphas, h_A, W_base, b_base, gamma, d_B, r, d_A, *, row_index=None):
+    """One ``dwa_assemble_apply`` call: ``h_mid`` only, the Pallas kernel's
+    factored form (assembly_pallas.py:85-132) for callers that do not use W
+    (generation, train.py:615-616).  Sequences of at most 16 rows never form W;
+    longer ones take the ``dwa_assemble_fwd`` path.  Same arguments as
+    :func:`assemble_forward`; returns ``h_mid [B,T,d_B]`` in ``h_A``'s dtype.
+    """
+    dev, B, T, k, D, n_rows = _check_common(rows, alphas, h_A, d_B, r, d_A, row_index)
+    act = dtype_code(h_A.dtype, "h_A")
+    rdt = dtype_code(rows.dtype, "rows")
+    alphas, W_base, b_base = _f32(alphas), _f32(W_base), _f32(b_base)
+    gamma = _f32(gamma.reshape(1))
+    for name, t in (("alphas", alphas), ("W_base", W_base), ("b_base", b_base), ("gamma", gamma)):
+        require_cuda(name, t, dev)
+    h_mid = torch.empty((B, T, d_B), dtype=h_A.dtype, device=dev)
+    dims = _dims(B, T, k, D, d_A, d_B, r, act, rdt, n_rows)
+    lib = _lib.load()
+    nbytes = lib.dwa_assemble_apply_workspace_bytes(dims)
+    ws = workspace(dev, "assemble_apply", nbytes)
+    with torch.cuda.device(dev):
+        rc = lib.dwa_assemble_apply(stream_of(dev), dims, ptr(rows), ptr(row_index), ptr(alphas),
+                                    ptr(h_A), ptr(W_base), ptr(b_base), ptr(gamma), ptr(h_mid),
+                                    ptr(ws), ws.numel())
+    _lib.check(rc, "dwa_assemble_apply")
+    return h_mid
 
 
 def assemble_backward(rows, alphas, h_A, W_act, gamma, g_hmid, g_W, d_B, r, d_A, *,

@@ -22,6 +22,7 @@
 //             g_alpha += <V_k, Q_k> = <U_k V_k, gW> (:298) without forming U_k V_k
 //   colsum    g_bias[b] = sum_t g[b];  finalize: g_alpha += <b_k, g_bias>,
 //             g_b = alpha g_bias, pad columns zero, g_b_base, g_gamma.
+#include <algorithm>
 #include <atomic>
 #include <cstdlib>
 #include <cstring>
@@ -389,6 +390,258 @@ __global__ void bias_grad_kernel(const float* __restrict__ gbias, int B, int d,
     g_b_base[j] = acc;
 }
 
+// -------------------------------------------------------- factored apply ---
+// h_mid without W: the Pallas kernel's own factored form
+// (assembly_pallas.py:109-117), h_mid = h_A + gamma (h_A W_base^T + (h_A V_s^T) U_f) + pb,
+// for sequences of a few rows (decode, T <= kFactoredMaxT).  Each gathered row
+// is read once (its V part by factored_hv_kernel, its U and b parts by
+// factored_out_kernel) and the d_B x d_A x k*r product that forming W costs is
+// skipped: at T = 1 that product is ~700x the flops of the apply itself.
+constexpr int kFactoredMaxT = 16;
+
+// hv[b][t][kk*r + rho] = alpha[b,kk] <V_kk[rho], h_A[b][t]>: one warp per (kk, rho),
+// eight per CTA; the warp streams the d_A elements of its V row with 16-byte loads.
+// TMAX: compile-time bound on T (accumulators per lane).
+template <class ACT, class RT, int TMAX>
+__global__ void __launch_bounds__(256) factored_hv_kernel(RowSrc src, const float* __restrict__ alphas,
+                                                          const ACT* __restrict__ hA, int T, int d_A,
+                                                          int64_t s1, int r, bool vec,
+                                                          float* __restrict__ hv, uint32_t* status) {
+    pdl_enter();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b = blockIdx.y, k = src.k;
+    const int kr = k * r;
+    const int p = blockIdx.x * 8 + warp;
+    if (p >= kr) return;
+    const int kk = p / r, rho = p - kk * r;
+    const int64_t off = src.offset(b, kk);
+    float acc[TMAX];
+#pragma unroll
+    for (int t = 0; t < TMAX; ++t) acc[t] = 0.f;
+    if (off < 0) {
+        if (lane == 0 && rho == 0) raise_status(status, DWA_STATUS_BAD_ROW_INDEX);
+    } else {
+        const RT* V = static_cast<const RT*>(src.rows) + off + s1 + static_cast<int64_t>(rho) * d_A;
+        const ACT* h = hA + static_cast<int64_t>(b) * T * d_A;
+        if (vec) {
+#pragma unroll 4
+            for (int i0 = lane * 8; i0 < d_A; i0 += 256) {
+                float v[8];
+                load8(V + i0, v);
+#pragma unroll
+                for (int t = 0; t < TMAX; ++t) {
+                    if (t < T) {
+                        float x[8];
+                        load8(h + static_cast<int64_t>(t) * d_A + i0, x);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) acc[t] = fmaf(v[e], x[e], acc[t]);
+                    }
+                }
+            }
+        } else {
+            for (int i = lane; i < d_A; i += 32) {
+                const float v = Elem<RT>::to_f(V[i]);
+#pragma unroll
+                for (int t = 0; t < TMAX; ++t)
+                    if (t < T) acc[t] = fmaf(v, Elem<ACT>::to_f(h[static_cast<int64_t>(t) * d_A + i]), acc[t]);
+            }
+        }
+    }
+    const float a = off < 0 ? 0.f : __ldg(alphas + static_cast<int64_t>(b) * k + kk);
+#pragma unroll
+    for (int t = 0; t < TMAX; ++t) {
+        if (t < T) {
+            float s = acc[t];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            if (lane == 0) hv[(static_cast<int64_t>(b) * T + t) * kr + p] = a * s;
+        }
+    }
+}
+
+// h_mid[b][t][j] = h_A[b][t][j] + gamma (base[b*T+t][j] + sum_{kk,rho} U_kk[j][rho] hv[b][t][kk*r+rho])
+//                  + b_base[j] + sum_kk alpha[b,kk] b_kk[j]
+// One thread per output column j, 128 per CTA; hv[b], the k row offsets and
+// alphas sit in shared memory; the U factors of (row kk, column j) are r
+// consecutive elements, so a warp reads 32*r contiguous elements per row.
+template <class ACT, class RT, int TMAX>
+__global__ void __launch_bounds__(128) factored_out_kernel(RowSrc src, const float* __restrict__ alphas,
+                                                           const ACT* __restrict__ hA,
+                                                           const float* __restrict__ base,
+                                                           const float* __restrict__ hv,
+                                                           const float* __restrict__ b_base,
+                                                           const float* __restrict__ gamma, int T, int d_B,
+                                                           int r, int64_t s2, bool vec_u,
+                                                           ACT* __restrict__ h_mid) {
+    pdl_enter();
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int b = blockIdx.y, k = src.k, kr = k * r;
+    float* s_hv = reinterpret_cast<float*>(smem_raw);                                // [T][kr]
+    int64_t* s_off = reinterpret_cast<int64_t*>(s_hv + ((T * kr + 1) & ~1));          // [k]
+    float* s_a = reinterpret_cast<float*>(s_off + k);                                // [k]
+    for (int e = threadIdx.x; e < T * kr; e += blockDim.x)
+        s_hv[e] = hv[static_cast<int64_t>(b) * T * kr + e];
+    for (int kk = threadIdx.x; kk < k; kk += blockDim.x) {
+        s_off[kk] = src.offset(b, kk);
+        s_a[kk] = alphas[static_cast<int64_t>(b) * k + kk];
+    }
+    __syncthreads();
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= d_B) return;
+    const RT* rows = static_cast<const RT*>(src.rows);
+    float acc[TMAX];
+#pragma unroll
+    for (int t = 0; t < TMAX; ++t) acc[t] = 0.f;
+    float bias = 0.f;
+#pragma unroll 4
+    for (int kk = 0; kk < k; ++kk) {
+        const int64_t off = s_off[kk];
+        if (off < 0) continue;
+        const RT* U = rows + off + static_cast<int64_t>(j) * r;
+        bias = fmaf(s_a[kk], Elem<RT>::to_f(rows[off + s2 + j]), bias);
+        const float* h = s_hv + kk * r;
+        if (vec_u) {    // r == 8
+            float u[8];
+            load8(U, u);
+#pragma unroll
+            for (int t = 0; t < TMAX; ++t) {
+                if (t < T) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc[t] = fmaf(u[e], h[t * kr + e], acc[t]);
+                }
+            }
+        } else {
+            for (int rho = 0; rho < r; ++rho) {
+                const float u = Elem<RT>::to_f(U[rho]);
+#pragma unroll
+                for (int t = 0; t < TMAX; ++t)
+                    if (t < T) acc[t] = fmaf(u, h[t * kr + rho], acc[t]);
+            }
+        }
+    }
+    const float g = __ldg(gamma);
+    const float pbj = b_base[j] + bias;
+#pragma unroll
+    for (int t = 0; t < TMAX; ++t) {
+        if (t < T) {
+            const int64_t o = (static_cast<int64_t>(b) * T + t) * d_B + j;
+            h_mid[o] = Elem<ACT>::from_f(Elem<ACT>::to_f(hA[o]) + g * (base[o] + acc[t]) + pbj);
+        }
+    }
+}
+
+// 4 consecutive elements as floats (8-byte bf16 / 16-byte f32 access).
+__device__ __forceinline__ void load4(const float* p, float* v) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+}
+__device__ __forceinline__ void load4(const __nv_bfloat16* p, float* v) {
+    const uint2 t = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&t.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&t.y));
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+
+// base[m][j] = <W_base[j], h[m]> for a few rows m (M <= MMAX): W_base is read
+// once, in fp32, straight from the parameter (no cast, no tile padding).  A
+// warp owns 4 rows of W_base so that every h load feeds 4 of them; 4 warps
+// per CTA.
+template <class ACT, int MMAX>
+__global__ void __launch_bounds__(128) base_rows_kernel(const float* __restrict__ W_base,
+                                                        const ACT* __restrict__ hA, int M, int d_A, int d_B,
+                                                        bool vec, float* __restrict__ base) {
+    pdl_enter();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int j0 = (blockIdx.x * 4 + warp) * 4;
+    if (j0 >= d_B) return;
+    const int nj = min(4, d_B - j0);
+    float acc[4][MMAX];
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj)
+#pragma unroll
+        for (int m = 0; m < MMAX; ++m) acc[jj][m] = 0.f;
+    if (vec) {
+#pragma unroll 2
+        for (int i0 = lane * 4; i0 < d_A; i0 += 128) {
+            float4 w[4];
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj)
+                w[jj] = jj < nj ? __ldg(reinterpret_cast<const float4*>(W_base + static_cast<int64_t>(j0 + jj) * d_A + i0))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int m = 0; m < MMAX; ++m) {
+                if (m < M) {
+                    float x[4];
+                    load4(hA + static_cast<int64_t>(m) * d_A + i0, x);
+#pragma unroll
+                    for (int jj = 0; jj < 4; ++jj)
+                        acc[jj][m] = fmaf(w[jj].x, x[0], fmaf(w[jj].y, x[1], fmaf(w[jj].z, x[2],
+                                     fmaf(w[jj].w, x[3], acc[jj][m]))));
+                }
+            }
+        }
+    } else {
+        for (int i = lane; i < d_A; i += 32) {
+            float w[4];
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) w[jj] = jj < nj ? W_base[static_cast<int64_t>(j0 + jj) * d_A + i] : 0.f;
+#pragma unroll
+            for (int m = 0; m < MMAX; ++m) {
+                if (m < M) {
+                    const float x = Elem<ACT>::to_f(hA[static_cast<int64_t>(m) * d_A + i]);
+#pragma unroll
+                    for (int jj = 0; jj < 4; ++jj) acc[jj][m] = fmaf(w[jj], x, acc[jj][m]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+#pragma unroll
+        for (int m = 0; m < MMAX; ++m) {
+            if (m < M) {
+                float v = acc[jj][m];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (lane == 0 && jj < nj) base[static_cast<int64_t>(m) * d_B + j0 + jj] = v;
+            }
+        }
+    }
+}
+
+// W_base in the activation dtype (the B operand of the batched base GEMM).
+__global__ void __launch_bounds__(256) cast_bf16_kernel(const float* __restrict__ x, int64_t n, bool vec,
+                                                        __nv_bfloat16* __restrict__ y) {
+    pdl_enter();
+    const int64_t n8 = vec ? n / 8 : 0;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float v[8];
+        load8(x + i * 8, v);
+        store8(y + i * 8, v);
+    }
+    for (int64_t i = n8 * 8 + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        y[i] = __float2bfloat16_rn(x[i]);
+}
+
+// base[row][j] = acc (row = b*T + t of the batched h_A W_base^T)
+struct EpiStore : NoReduce {
+    float* out; int N; bool vec;
+    struct Frag {};
+    __device__ void load(int, int, int, int, Frag&) const {}
+    __device__ float finish(int, int row, int col0, const float* v, int cnt, const Frag&) const {
+        float* o = out + static_cast<int64_t>(row) * N + col0;
+        if (vec && cnt == 8) {
+            store8(o, v);
+        } else {
+            for (int c = 0; c < cnt; ++c) o[c] = v[c];
+        }
+        return 0.f;
+    }
+    DWA_EPI_CALL
+};
+
 // ------------------------------------------------------------------ host ---
 static bool force_simt() {
     static const bool v = [] {
@@ -753,4 +1006,186 @@ extern "C" int dwa_assemble_bwd(void* stream, const DwaAssembleDims* dims, const
         return bwd_impl<float, __nv_bfloat16>(DWA_BWD_ARGS(float, __nv_bfloat16));
     return bwd_impl<float, float>(DWA_BWD_ARGS(float, float));
 #undef DWA_BWD_ARGS
+}
+
+// ------------------------------------------------- factored apply (host) ---
+namespace dwa {
+
+static size_t factored_smem(const DwaAssembleDims& d) {
+    const size_t kr = static_cast<size_t>(d.k) * d.r;
+    return align_up(static_cast<size_t>(d.T) * kr, 2) * sizeof(float) +
+           static_cast<size_t>(d.k) * (sizeof(int64_t) + sizeof(float));
+}
+
+// The factored kernels hold T accumulators per thread and hv[b] in shared memory.
+static bool factored_ok(const DwaAssembleDims& d) {
+    return d.T <= kFactoredMaxT && factored_smem(d) <= 160 * 1024;
+}
+
+// Rows of the base product up to which base_rows_kernel runs; beyond, a GEMM
+// (bf16: the tensor-core GEMM over h_A padded to whole 128-row tiles).
+constexpr int kBaseRowsMax = 16;
+
+static bool base_on_tensor_cores(const DwaAssembleDims& d) {
+    return d.act_dtype == DWA_BF16 && static_cast<int64_t>(d.B) * d.T > kBaseRowsMax;
+}
+
+struct FactWorkspace {
+    uint32_t* status;
+    void* Wb;       // [d_B, d_A] W_base in the activation dtype (bf16 activations, B*T > 16)
+    void* hpad;     // [Mp, d_A] h_A rows padded with zeros to a whole 128-row tile (same case)
+    float* hv;      // [B, T, k*r]
+    float* base;    // [Mp, d_B] h_A W_base^T
+    size_t bytes;
+};
+
+static FactWorkspace carve_factored(void* base, const DwaAssembleDims& d) {
+    Carver c(base);
+    FactWorkspace w{};
+    w.status = static_cast<uint32_t*>(base);
+    const size_t bt = static_cast<size_t>(d.B) * d.T, kr = static_cast<size_t>(d.k) * d.r;
+    const bool tc = base_on_tensor_cores(d);
+    const size_t mp = tc ? align_up(bt, 128) : bt;
+    w.Wb = c.take<char>(tc ? static_cast<size_t>(d.d_B) * d.d_A * 2 : 0);
+    w.hpad = c.take<char>(tc ? mp * d.d_A * 2 : 0);
+    w.hv = c.take<float>(bt * kr);
+    w.base = c.take<float>(mp * d.d_B);
+    w.bytes = c.bytes();
+    return w;
+}
+
+static bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+template <class ACT, class RT>
+static int factored_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src, const float* alphas,
+                         const ACT* hA, const float* W_base, const float* b_base, const float* gamma,
+                         ACT* h_mid, const FactWorkspace& w) {
+    Lanes lanes(st);
+    int rc = lanes.rc;
+    if (rc) return rc;
+    const int kr = d.k * d.r;
+    const int BT = d.B * d.T;
+    const int64_t s1 = static_cast<int64_t>(d.d_B) * d.r, s2 = s1 + static_cast<int64_t>(d.r) * d.d_A;
+    // aux0: hv = alpha (V h_A), one warp per (row, factor)
+    const bool vec_hv = d.d_A % 8 == 0 && d.D % 8 == 0 && s1 % 8 == 0 && aligned16(src.rows) && aligned16(hA);
+    const dim3 g_hv((kr + 7) / 8, d.B);
+    if (d.T == 1)
+        DWA_TIMED("factored_hv", lanes.aux[0],
+                  launch_pdl(factored_hv_kernel<ACT, RT, 1>, g_hv, 256, 0, lanes.aux[0], src, alphas, hA, d.T,
+                             d.d_A, s1, d.r, vec_hv, w.hv, w.status));
+    else if (d.T <= 4)
+        DWA_TIMED("factored_hv", lanes.aux[0],
+                  launch_pdl(factored_hv_kernel<ACT, RT, 4>, g_hv, 256, 0, lanes.aux[0], src, alphas, hA, d.T,
+                             d.d_A, s1, d.r, vec_hv, w.hv, w.status));
+    else
+        DWA_TIMED("factored_hv", lanes.aux[0],
+                  launch_pdl(factored_hv_kernel<ACT, RT, kFactoredMaxT>, g_hv, 256, 0, lanes.aux[0], src, alphas,
+                             hA, d.T, d.d_A, s1, d.r, vec_hv, w.hv, w.status));
+    DWA_LAUNCH_CHECK("factored_hv_kernel");
+    ++g_launches_total;
+    // main: base = h_A W_base^T over all B*T rows at once (W_base read once)
+    if (BT <= kBaseRowsMax) {
+        const bool vec_b = d.d_A % 4 == 0 && aligned16(W_base) && aligned16(hA);
+        const dim3 g_b((d.d_B + 15) / 16);
+        if (BT <= 4)
+            DWA_TIMED("base_rows", st,
+                      launch_pdl(base_rows_kernel<ACT, 4>, g_b, 128, 0, st, W_base, hA, BT, d.d_A, d.d_B, vec_b,
+                                 w.base));
+        else
+            DWA_TIMED("base_rows", st,
+                      launch_pdl(base_rows_kernel<ACT, kBaseRowsMax>, g_b, 128, 0, st, W_base, hA, BT, d.d_A,
+                                 d.d_B, vec_b, w.base));
+        DWA_LAUNCH_CHECK("base_rows_kernel");
+        ++g_launches_total;
+    } else if (!std::is_same<ACT, __nv_bfloat16>::value) {
+        // float activations, more than 16 rows: the CUDA-core GEMM, fp32 throughout
+        EpiStore es_;
+        es_.out = w.base; es_.N = d.d_B; es_.vec = d.d_B % 8 == 0;
+        rc = gemm<ACT, false, false>("gemm_base", hA, d.d_A, static_cast<int64_t>(BT) * d.d_A, W_base, d.d_A,
+                                     static_cast<int64_t>(d.d_B) * d.d_A, BT, d.d_B, d.d_A, 1, es_, w.status, st);
+        if (rc) return rc;
+        ++g_launches_total;
+    } else {
+        const int64_t n = static_cast<int64_t>(d.d_B) * d.d_A;
+        const int grid = static_cast<int>(std::min<int64_t>((n / 8 + 255) / 256 + 1, 148 * 8));
+        DWA_TIMED("cast_w_base", st,
+                  launch_pdl(cast_bf16_kernel, dim3(grid), 256, 0, st, W_base, n, aligned16(W_base),
+                             static_cast<__nv_bfloat16*>(w.Wb)));
+        DWA_LAUNCH_CHECK("cast_bf16_kernel");
+        ++g_launches_total;
+        const size_t es = sizeof(ACT);
+        const int Mp = static_cast<int>(align_up(static_cast<size_t>(BT), 128));
+        DWA_CUDA_TRY(cudaMemcpyAsync(w.hpad, hA, static_cast<size_t>(BT) * d.d_A * es, cudaMemcpyDeviceToDevice, st));
+        if (Mp > BT)
+            DWA_CUDA_TRY(cudaMemsetAsync(static_cast<char*>(w.hpad) + static_cast<size_t>(BT) * d.d_A * es, 0,
+                                         static_cast<size_t>(Mp - BT) * d.d_A * es, st));
+        EpiStore es_;
+        es_.out = w.base; es_.N = d.d_B; es_.vec = d.d_B % 8 == 0;
+        // A = h_A padded (M=Mp, K=d_A, K-major); B = W_base (N=d_B, K=d_A, K-major)
+        rc = gemm<ACT, false, false>("gemm_base", w.hpad, d.d_A, static_cast<int64_t>(Mp) * d.d_A, w.Wb, d.d_A,
+                                     static_cast<int64_t>(d.d_B) * d.d_A, Mp, d.d_B, d.d_A, 1, es_, w.status, st);
+        if (rc) return rc;
+        ++g_launches_total;
+    }
+    if ((rc = lanes.join())) return rc;
+    const size_t smem = factored_smem(d);
+    const bool vec_u = d.r == 8 && d.D % 8 == 0 && aligned16(src.rows);
+    const dim3 g_out((d.d_B + 127) / 128, d.B);
+#define DWA_FACT_OUT(TM)                                                                                       \
+    do {                                                                                                       \
+        if (smem > 48 * 1024)                                                                                  \
+            DWA_CUDA_TRY(cudaFuncSetAttribute(factored_out_kernel<ACT, RT, TM>,                                \
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem))); \
+        DWA_TIMED("factored_out", st,                                                                          \
+                  launch_pdl(factored_out_kernel<ACT, RT, TM>, g_out, 128, smem, st, src, alphas, hA,           \
+                             static_cast<const float*>(w.base), static_cast<const float*>(w.hv), b_base, gamma, \
+                             d.T, d.d_B, d.r, s2, vec_u, h_mid));                                              \
+    } while (0)
+    if (d.T == 1)
+        DWA_FACT_OUT(1);
+    else if (d.T <= 4)
+        DWA_FACT_OUT(4);
+    else
+        DWA_FACT_OUT(kFactoredMaxT);
+#undef DWA_FACT_OUT
+    DWA_LAUNCH_CHECK("factored_out_kernel");
+    ++g_launches_total;
+    return DWA_OK;
+}
+
+}  // namespace dwa
+
+extern "C" size_t dwa_assemble_apply_workspace_bytes(const DwaAssembleDims* dims) {
+    if (check_dims(dims)) return 0;
+    return factored_ok(*dims) ? carve_factored(nullptr, *dims).bytes : carve(nullptr, *dims, false).bytes;
+}
+
+extern "C" int dwa_assemble_apply(void* stream, const DwaAssembleDims* dims, const void* rows,
+                                  const int32_t* row_index, const float* alphas, const void* h_A,
+                                  const float* W_base, const float* b_base, const float* gamma, void* h_mid,
+                                  void* workspace, size_t workspace_bytes) {
+    int rc = check_dims(dims);
+    if (rc) return rc;
+    const DwaAssembleDims& d = *dims;
+    if (!factored_ok(d))   // long sequences: assembling W first is the cheaper order
+        return dwa_assemble_fwd(stream, dims, rows, row_index, alphas, h_A, W_base, b_base, gamma, h_mid,
+                                nullptr, nullptr, workspace, workspace_bytes);
+    if (!rows || !alphas || !h_A || !W_base || !b_base || !gamma || !h_mid)
+        return fail(DWA_ERR_INVALID_ARG, "a required pointer is NULL");
+    const FactWorkspace w = carve_factored(workspace, d);
+    if ((rc = check_ws(workspace, workspace_bytes, w.bytes))) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const RowSrc src{rows, row_index, row_index ? d.n_rows : static_cast<int64_t>(d.B) * d.k, d.D,
+                     d.k, d.rows_dtype};
+#define DWA_APPLY_ARGS(A)                                                                            \
+    st, d, src, alphas, static_cast<const A*>(h_A), W_base, b_base, gamma, static_cast<A*>(h_mid), w
+    if (d.act_dtype == DWA_BF16) {
+        if (d.rows_dtype == DWA_BF16)
+            return factored_impl<__nv_bfloat16, __nv_bfloat16>(DWA_APPLY_ARGS(__nv_bfloat16));
+        return factored_impl<__nv_bfloat16, float>(DWA_APPLY_ARGS(__nv_bfloat16));
+    }
+    if (d.rows_dtype == DWA_BF16)
+        return factored_impl<float, __nv_bfloat16>(DWA_APPLY_ARGS(float));
+    return factored_impl<float, float>(DWA_APPLY_ARGS(float));
+#undef DWA_APPLY_ARGS
 }

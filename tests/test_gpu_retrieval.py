@@ -201,3 +201,29 @@ def test_negative_lambda_selects_a_valid_top_k_of_raw():
         assert len(set(i[b].tolist())) == cfg.k_max
         assert (sel >= kth * (1 - 1e-5)).all()
         assert_close(a[b], sel / (sel.sum() + 1e-8), TOL, name="alphas")
+
+
+@pytest.mark.parametrize("use_ivf", [True, False])
+def test_decode_batch_and_top_k_match_oracle(use_ivf):
+    """The decode sweep's shapes beyond the specialised scans: 72 queries
+    (more than 32, so the generic scoring kernels) and top-k 128, warmup and
+    gate, IVF over Zipf(1.1) lists and full search."""
+    B = 72
+    cfg = DWAConfig(D=17 * 64, N=41 * 487, use_ivf=use_ivf, C=41, m=5, d_A=64, d_B=64, r=8, k_max=128,
+                    S=4, d_k=64, T=1.0, gamma_init=0.1, bf16_pool=False)
+    x = make_inputs(cfg, B, 1, 41, variant="rich", zipf=1.1)
+    off = x.list_offsets
+    max_list = int(np.diff(off).max())
+    f = np.float64
+    for is_warmup, lam in ((True, 1.0), (False, 5.0)):
+        a, i, sf = _gpu_retrieve(cfg, x, lam, is_warmup, True, use_ivf=use_ivf, offsets=off,
+                                 max_list=max_list)
+        ra, ri, rsf = O.retrieve(
+            x.z.astype(f), x.W_Q.astype(f), x.aspect_weights.astype(f), f(x.tau),
+            x.centroids.astype(f) if use_ivf else None, x.keys.astype(f), k=cfg.k_max, m=cfg.m,
+            T=cfg.T, lambda_val=lam, is_warmup=is_warmup, use_ivf=use_ivf,
+            list_offsets=off if use_ivf else None, tie_break="index")
+        tag = f"ivf={use_ivf} warmup={is_warmup}"
+        np.testing.assert_array_equal(i, ri, err_msg=tag)
+        assert_close(a, ra, TOL, name=f"alphas {tag}")
+        assert_close(sf, rsf, TOL, name=f"soft_full {tag}")
