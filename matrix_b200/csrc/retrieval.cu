@@ -634,6 +634,124 @@ __global__ void fine_kernel(const float* __restrict__ qw, const float* __restric
     scores[static_cast<int64_t>(b) * K_cap + base + r] = sc;
 }
 
+// List-inverted fine scores for batches the key scans do not take (B > 32,
+// d_k = 64, S <= 4, no soft_full).  One CTA per (256 rows of a list, list):
+// it collects, in query order, the probes (b, j) of list c, reads each 64-row
+// chunk of the list's keys once into registers (thread = (aspect, row)) and
+// scores every probing query against it, instead of every query re-reading its
+// probed lists.  Per (row, query) the operations and their order are those of
+// row_scores(), so the scores are bit-identical to fine_kernel's.
+constexpr int kFlRows = 64, kFlChunks = 4, kFlBatch = 16, kFlCap = 1024;
+
+__global__ void __launch_bounds__(256) fine_lists_kernel(
+    const float* __restrict__ qw, const float* __restrict__ keys, int64_t N, int S, int B, int m,
+    const int32_t* __restrict__ top_clusters, const int64_t* __restrict__ probe_lo,
+    const int64_t* __restrict__ cand_base, int64_t K_cap, float* __restrict__ scores) {
+    pdl_enter();
+    __shared__ int s_ent[kFlCap];
+    __shared__ int s_wcnt[8];
+    __shared__ __align__(16) float s_q[kFlBatch][4 * 64];
+    __shared__ float s_part[kFlBatch][4][kFlRows];
+    const int c = blockIdx.y;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int s = tid >> 6, rl = tid & 63;
+    const int BM = B * m;
+    for (int start = 0;; start += kFlCap) {
+        // the probes of list c with ordinal in [start, start + kFlCap), in (b, j) order
+        int seen = 0;
+        for (int w0 = 0; w0 < BM; w0 += 256) {
+            const int e = w0 + tid;
+            bool hit = false;
+            if (e < BM && top_clusters[e] == c) {
+                const int64_t* cb = cand_base + static_cast<int64_t>(e / m) * (m + 1) + (e % m);
+                hit = cb[1] > cb[0];
+            }
+            const unsigned bal = __ballot_sync(0xffffffffu, hit);
+            if (lane == 0) s_wcnt[warp] = __popc(bal);
+            __syncthreads();
+            int before = 0, total = 0;
+            for (int w = 0; w < 8; ++w) {
+                const int v = s_wcnt[w];
+                before += w < warp ? v : 0;
+                total += v;
+            }
+            if (hit) {
+                const int ord = seen + before + __popc(bal & ((1u << lane) - 1u));
+                if (ord >= start && ord < start + kFlCap) s_ent[ord - start] = e;
+            }
+            seen += total;
+            __syncthreads();
+        }
+        const int n = min(seen - start, kFlCap);
+        if (n <= 0) return;                      // same in every thread
+        const int e0 = s_ent[0];
+        const int b0 = e0 / m, j0 = e0 - b0 * m;
+        const int64_t lo = probe_lo[static_cast<int64_t>(b0) * (m + 1) + j0];
+        const int64_t sz = cand_base[static_cast<int64_t>(b0) * (m + 1) + j0 + 1] -
+                           cand_base[static_cast<int64_t>(b0) * (m + 1) + j0];
+        for (int ch = 0; ch < kFlChunks; ++ch) {
+            const int64_t r0 = (static_cast<int64_t>(blockIdx.x) * kFlChunks + ch) * kFlRows;
+            if (r0 >= sz) break;                 // same in every thread
+            const int64_t row = r0 + rl;
+            const bool valid = s < S && row < sz;
+            float4 kv[16];
+            float den = 1.f;
+            if (valid) {
+                const float4* kp = reinterpret_cast<const float4*>(keys + (static_cast<int64_t>(s) * N + lo + row) * 64);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) kv[i] = __ldg(kp + i);
+                float nrm = 0.f;
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    nrm = fmaf(kv[i].x, kv[i].x, nrm);
+                    nrm = fmaf(kv[i].y, kv[i].y, nrm);
+                    nrm = fmaf(kv[i].z, kv[i].z, nrm);
+                    nrm = fmaf(kv[i].w, kv[i].w, nrm);
+                }
+                den = sqrtf(nrm) + 1e-8f;
+            }
+            for (int i0 = 0; i0 < n; i0 += kFlBatch) {
+                const int nb = min(kFlBatch, n - i0);
+                for (int t = tid; t < nb * S * 64; t += 256) {
+                    const int i = t / (S * 64), o = t - i * (S * 64);
+                    const int b = s_ent[i0 + i] / m;
+                    s_q[i][o] = qw[static_cast<int64_t>(b) * S * 64 + o];
+                }
+                __syncthreads();
+                if (valid) {
+                    for (int i = 0; i < nb; ++i) {
+                        const float4* qq = reinterpret_cast<const float4*>(&s_q[i][s * 64]);
+                        float dot = 0.f;
+#pragma unroll
+                        for (int c4 = 0; c4 < 16; ++c4) {
+                            const float4 qv = qq[c4];
+                            dot = fmaf(kv[c4].x, qv.x, dot);
+                            dot = fmaf(kv[c4].y, qv.y, dot);
+                            dot = fmaf(kv[c4].z, qv.z, dot);
+                            dot = fmaf(kv[c4].w, qv.w, dot);
+                        }
+                        s_part[i][s][rl] = dot / den;
+                    }
+                }
+                __syncthreads();
+                for (int t = tid; t < nb * kFlRows; t += 256) {
+                    const int i = t / kFlRows, r2 = t - i * kFlRows;
+                    const int64_t row2 = r0 + r2;
+                    if (row2 < sz) {
+                        const int e = s_ent[i0 + i];
+                        const int b = e / m, j = e - b * m;
+                        float sc = 0.f;
+                        for (int s2 = 0; s2 < S; ++s2) sc += s_part[i][s2][r2];
+                        scores[static_cast<int64_t>(b) * K_cap + cand_base[static_cast<int64_t>(b) * (m + 1) + j] + row2] = sc;
+                    }
+                }
+                __syncthreads();
+            }
+        }
+        if (seen - start <= kFlCap) return;
+    }
+}
+
 // Full-pool scores for up to NB queries at a time; writes raw s_full and per
 // block (max, sum exp) of s*invT (invT = 1/T) for the softmax.
 template <int NB, int DK>
@@ -1420,6 +1538,12 @@ static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaSha
     // 4. fine scores of the probed lists (read from the full pass when it ran)
     if (ivf && !want_sf && (use_tc || use_scan)) {
         if ((rc = launch_scores(1, w.scores, nullptr))) return rc;
+    } else if (ivf && !want_sf && dk64 && d.S <= 4 && d.B > 32) {
+        dim3 gl(static_cast<unsigned>((d.max_list + kFlRows * kFlChunks - 1) / (kFlRows * kFlChunks)), d.C);
+        DWA_TIMED("fine", st, launch_pdl(fine_lists_kernel, gl, 256, 0, st, w.qw, pool_keys, d.N, d.S, d.B,
+                                         w.m_eff, w.topc, w.probe_lo, w.cand_base, w.K_cap, w.scores));
+        DWA_LAUNCH_CHECK("fine_lists_kernel");
+        ++g_launches_total;
     } else if (ivf && !want_sf) {
         dim3 gf(static_cast<unsigned>((d.max_list + 255) / 256), w.m_eff, d.B);
         if (dk64)

@@ -206,8 +206,10 @@ def test_negative_lambda_selects_a_valid_top_k_of_raw():
 @pytest.mark.parametrize("use_ivf", [True, False])
 def test_decode_batch_and_top_k_match_oracle(use_ivf):
     """The decode sweep's shapes beyond the specialised scans: 72 queries
-    (more than 32, so the generic scoring kernels) and top-k 128, warmup and
-    gate, IVF over Zipf(1.1) lists and full search."""
+    (more than 32: the generic full pass, and without soft_full the
+    list-inverted fine pass) and top-k 128, warmup and gate, IVF over
+    Zipf(1.1) lists and full search.  The fine pass selects bit-identically
+    to the full pass."""
     B = 72
     cfg = DWAConfig(D=17 * 64, N=41 * 487, use_ivf=use_ivf, C=41, m=5, d_A=64, d_B=64, r=8, k_max=128,
                     S=4, d_k=64, T=1.0, gamma_init=0.1, bf16_pool=False)
@@ -227,3 +229,7 @@ def test_decode_batch_and_top_k_match_oracle(use_ivf):
         np.testing.assert_array_equal(i, ri, err_msg=tag)
         assert_close(a, ra, TOL, name=f"alphas {tag}")
         assert_close(sf, rsf, TOL, name=f"soft_full {tag}")
+        a2, i2, _ = _gpu_retrieve(cfg, x, lam, is_warmup, False, use_ivf=use_ivf, offsets=off,
+                                  max_list=max_list)
+        np.testing.assert_array_equal(i2, i, err_msg=f"fine pass {tag}")
+        np.testing.assert_array_equal(a2, a, err_msg=f"fine pass {tag}")
