@@ -271,21 +271,22 @@ class ShardedStep:
 
 
 # ------------------------------------------------------------ decode sweep ---
-def decode_sweep(args, dev, flush, peaks, peak_src):
+def decode_sweep(args, w, dev, flush, peaks, peak_src):
     """The decode workload on one GPU holding one rank's share of 8: 2M/8 =
     262144 pool rows x 69632 (d 4096, bf16, 36.5 GB) with their keys and 256
     of the 2048 lists (1024 rows each).  A step is one token for B sequences:
     sequence mean (T = 1), dwa_retrieve over this GPU's rows (gate mode,
     nprobe 16, no soft_full) and dwa_assemble_apply (h_mid only, the winning
-    rows read from the pool by index).  Returns one JSON-ready dict."""
+    rows read from the pool by index).  ``decode_profile``: the same step at
+    batch 256, top-k 128 on its own small pool (for ncu).  Returns one
+    JSON-ready dict."""
     import torch
     from matrix_b200 import _lib, runtime
     from matrix_b200.assembly import assemble_apply, compute_key_cache
     from matrix_b200.retrieval import retrieve
-    from matrix_b200.config import WORKLOADS
-    w = WORKLOADS["decode"]
     c = w.cfg
-    share = 8
+    share = 8 if w.name == "decode" else 1
+    shapes = [(B, k) for B in (1, 8, 64, 256) for k in (16, 128)] if w.name == "decode" else [(w.batch, c.k_max)]
     d, D, S, dk, r = c.d_A, c.D, c.S, c.d_k, c.r
     N, C = c.N // share, c.C // share
     lib = _lib.load()
@@ -306,66 +307,66 @@ def decode_sweep(args, dev, flush, peaks, peak_src):
     gamma = torch.full((1,), c.gamma_init, device=dev)
     lam = torch.full((1,), 5.0, device=dev)
     points = []
-    for B in (1, 8, 64, 256):
-        for k in (16, 128):
-            h_A = torch.randn((B, 1, d), generator=g, device=dev).to(torch.bfloat16)
-            z = torch.empty((B, d), dtype=torch.float32, device=dev)
+    for B, k in shapes:
+        h_A = torch.randn((B, 1, d), generator=g, device=dev).to(torch.bfloat16)
+        z = torch.empty((B, d), dtype=torch.float32, device=dev)
 
-            def step():
-                rc = lib.dwa_sequence_mean(runtime.stream_of(dev), B, 1, d, 1, runtime.ptr(h_A), runtime.ptr(z))
-                _lib.check(rc, "dwa_sequence_mean")
-                al, idx, _ = retrieve(z, W_Q, aw, tau, cent, keys, lam, False, k=k, m=c.m, T=c.T,
-                                      want_soft_full=False)
-                return assemble_apply(pool, al, h_A, W_base, b_base, gamma, d, r, d, row_index=idx)
+        def step():
+            rc = lib.dwa_sequence_mean(runtime.stream_of(dev), B, 1, d, 1, runtime.ptr(h_A), runtime.ptr(z))
+            _lib.check(rc, "dwa_sequence_mean")
+            al, idx, _ = retrieve(z, W_Q, aw, tau, cent, keys, lam, False, k=k, m=c.m, T=c.T,
+                                  want_soft_full=False)
+            return assemble_apply(pool, al, h_A, W_base, b_base, gamma, d, r, d, row_index=idx)
 
+        step()
+        torch.cuda.synchronize()
+        c0 = _lib.launch_counters()[0]
+        step()
+        torch.cuda.synchronize()
+        launches = _lib.launch_counters()[0] - c0
+        kms, _ = profile_kernels(step, flush)
+        s_ = torch.cuda.Stream()
+        s_.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s_):
             step()
-            torch.cuda.synchronize()
-            c0 = _lib.launch_counters()[0]
+        torch.cuda.current_stream().wait_stream(s_)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
             step()
-            torch.cuda.synchronize()
-            launches = _lib.launch_counters()[0] - c0
-            kms, _ = profile_kernels(step, flush)
-            s_ = torch.cuda.Stream()
-            s_.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(s_):
-                step()
-            torch.cuda.current_stream().wait_stream(s_)
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                step()
-            for _ in range(max(args.warmup, 3)):
-                flush()
-                graph.replay()
-            reps = 20
-            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
-            torch.cuda.synchronize()
-            for a, b in ev:
-                flush()
-                a.record()
-                graph.replay()
-                b.record()
-            torch.cuda.synchronize()
-            ms = float(np.mean([a.elapsed_time(b) for a, b in ev]))
-            del graph
-            runtime.raise_on_device_status()
-            row_bytes = B * k * D * 2
-            pt = {"batch": B, "top_k": k, "ms_per_token_step": ms, "tokens_per_s": B / (ms / 1e3),
-                  "kernels_ms": kms, "gpu_launches_per_step": int(launches),
-                  "gathered_row_bytes": row_bytes}
-            # the two row kernels each read their part of every winning row
-            for name, part in (("factored_hv", r * d), ("factored_out", d * r + d)):
-                if kms.get(name):
-                    gbs = B * k * part * 2 / (kms[name] / 1e3) / 1e9
-                    pt[name + "_gbs"] = gbs
-                    pt[name + "_frac"] = gbs / float(peaks["hbm_gbs"])
-            points.append(pt)
+        for _ in range(max(args.warmup, 3)):
+            flush()
+            graph.replay()
+        reps = 20
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        torch.cuda.synchronize()
+        for a, b in ev:
+            flush()
+            a.record()
+            graph.replay()
+            b.record()
+        torch.cuda.synchronize()
+        ms = float(np.mean([a.elapsed_time(b) for a, b in ev]))
+        del graph
+        runtime.raise_on_device_status()
+        row_bytes = B * k * D * 2
+        pt = {"batch": B, "top_k": k, "ms_per_token_step": ms, "tokens_per_s": B / (ms / 1e3),
+              "kernels_ms": kms, "gpu_launches_per_step": int(launches),
+              "gathered_row_bytes": row_bytes}
+        # the two row kernels each read their part of every winning row
+        for name, part in (("factored_hv", r * d), ("factored_out", d * r + d)):
+            if kms.get(name):
+                gbs = B * k * part * 2 / (kms[name] / 1e3) / 1e9
+                pt[name + "_gbs"] = gbs
+                pt[name + "_frac"] = gbs / float(peaks["hbm_gbs"])
+        points.append(pt)
     big = points[-1]
     return {"metric": METRIC, "value": big["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1,
             "steps": 20, "warmup": max(args.warmup, 3), "ms_per_step": big["ms_per_token_step"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": "decode", "note": w.note,
-                       "this_gpu": f"one rank's share of 8: {N} pool rows x {D}, {C} lists, nprobe {c.m}",
+            "config": {"workload": w.name, "note": w.note,
+                       "this_gpu": (f"one rank's share of {share}: " if share > 1 else "") +
+                                   f"{N} pool rows x {D}, {C} lists, nprobe {c.m}",
                        "mode": "gate lambda=5.0, no soft_full, h_mid only (dwa_assemble_apply)",
                        "l2": "flushed between steps (512 MB write, then 256 MB read)",
                        "step": "CUDA graph: seq_mean + dwa_retrieve + dwa_assemble_apply",
@@ -749,12 +750,12 @@ def main():
         flush_buf.zero_()
         flush_sink.copy_(flush_buf[: flush_buf.numel() // 2].sum())
 
-    if w.name == "decode" and not args.sharded:
+    if w.name in ("decode", "decode_profile") and not args.sharded:
         # the decode pool (2M x 69632, 292 GB) needs 8 GPUs; one GPU runs one rank's share
         if world > 1:
             raise SystemExit("the decode sweep runs on one GPU (one rank's share of the pool)")
         peaks, peak_src = load_peaks()
-        print(json.dumps(decode_sweep(args, dev, flush, peaks, peak_src)), flush=True)
+        print(json.dumps(decode_sweep(args, w, dev, flush, peaks, peak_src)), flush=True)
         return
 
     if args.sharded:

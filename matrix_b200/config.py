@@ -97,6 +97,9 @@ WORKLOADS: dict[str, Workload] = {
     "decode": Workload("decode", _cfg(4096, 1 << 21, 2048, 16, 64, "bfloat16"), 64, 1, False,
                        note="bf16, batch 1-256, seq 1, d 4096, pool 2M, 2048 lists, nprobe 16, top-k 16-128"),
     # reduced cases for detailed ncu captures (a few GB on the device)
+    "decode_profile": Workload("decode_profile", _cfg(4096, 1 << 14, 16, 16, 128, "bfloat16"), 256, 1, False,
+                               note="ncu case: decode shapes (d 4096, batch 256, top-k 128) on a 2.3 GB pool "
+                                    "of 16384 rows in 16 lists"),
     "profile_keys": Workload("profile_keys", _cfg(512, 131072, 256, 8, 32, "bfloat16"), 8, 512, True,
                              note="ncu case: key cache 134 MB (> L2), pool 2.3 GB; small shapes otherwise"),
     "profile_gemm": Workload("profile_gemm", _cfg(1024, 16384, 32, 8, 32, "bfloat16"), 8, 512, True,

@@ -203,13 +203,29 @@ def test_negative_lambda_selects_a_valid_top_k_of_raw():
         assert_close(a[b], sel / (sel.sum() + 1e-8), TOL, name="alphas")
 
 
+def _assert_rows_equal_up_to_ties(got, ref, soft_ref, T, tag, gap=1e-5):
+    """Selected rows equal the oracle's position by position, except where the
+    oracle's own scores of the two rows differ by less than ``gap`` (s = T log
+    soft_full + const within a query): there float32 and float64 may order
+    them differently.  Used where 72 queries x 128 ranks of a full search make
+    a seed without such near-ties unlikely."""
+    bad = np.argwhere(got != ref)
+    for b, p in bad:
+        s_got = T * np.log(soft_ref[b, got[b, p]])
+        s_ref = T * np.log(soft_ref[b, ref[b, p]])
+        assert abs(s_got - s_ref) < gap, (f"{tag}: query {b} rank {p}: row {got[b, p]} "
+                                          f"(s {s_got:.9g}) instead of {ref[b, p]} (s {s_ref:.9g})")
+    assert len(bad) <= 0.01 * got.size, f"{tag}: {len(bad)} positions differ"
+
+
 @pytest.mark.parametrize("use_ivf", [True, False])
 def test_decode_batch_and_top_k_match_oracle(use_ivf):
     """The decode sweep's shapes beyond the specialised scans: 72 queries
     (more than 32: the generic full pass, and without soft_full the
     list-inverted fine pass) and top-k 128, warmup and gate, IVF over
-    Zipf(1.1) lists and full search.  The fine pass selects bit-identically
-    to the full pass."""
+    Zipf(1.1) lists and full search.  Rows equal the oracle's except at
+    float32/float64 near-ties (gap < 1e-5); the fine pass selects
+    bit-identically to the full pass."""
     B = 72
     cfg = DWAConfig(D=17 * 64, N=41 * 487, use_ivf=use_ivf, C=41, m=5, d_A=64, d_B=64, r=8, k_max=128,
                     S=4, d_k=64, T=1.0, gamma_init=0.1, bf16_pool=False)
@@ -226,7 +242,7 @@ def test_decode_batch_and_top_k_match_oracle(use_ivf):
             T=cfg.T, lambda_val=lam, is_warmup=is_warmup, use_ivf=use_ivf,
             list_offsets=off if use_ivf else None, tie_break="index")
         tag = f"ivf={use_ivf} warmup={is_warmup}"
-        np.testing.assert_array_equal(i, ri, err_msg=tag)
+        _assert_rows_equal_up_to_ties(i, ri, rsf, cfg.T, tag)
         assert_close(a, ra, TOL, name=f"alphas {tag}")
         assert_close(sf, rsf, TOL, name=f"soft_full {tag}")
         a2, i2, _ = _gpu_retrieve(cfg, x, lam, is_warmup, False, use_ivf=use_ivf, offsets=off,
