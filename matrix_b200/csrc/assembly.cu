@@ -471,11 +471,13 @@ __global__ void __launch_bounds__(128) factored_out_kernel(RowSrc src, const flo
                                                            const float* __restrict__ hv,
                                                            const float* __restrict__ b_base,
                                                            const float* __restrict__ gamma, int T, int d_B,
-                                                           int r, int64_t s2, bool vec_u,
+                                                           int r, int64_t s2, bool vec_u, int kchunk,
+                                                           float* __restrict__ part, float* __restrict__ pbias,
                                                            ACT* __restrict__ h_mid) {
     pdl_enter();
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int b = blockIdx.y, k = src.k, kr = k * r;
+    const int kk0 = blockIdx.z * kchunk, kk1 = min(k, kk0 + kchunk);
     float* s_hv = reinterpret_cast<float*>(smem_raw);                                // [T][kr]
     int64_t* s_off = reinterpret_cast<int64_t*>(s_hv + ((T * kr + 1) & ~1));          // [k]
     float* s_a = reinterpret_cast<float*>(s_off + k);                                // [k]
@@ -494,7 +496,7 @@ __global__ void __launch_bounds__(128) factored_out_kernel(RowSrc src, const flo
     for (int t = 0; t < TMAX; ++t) acc[t] = 0.f;
     float bias = 0.f;
 #pragma unroll 4
-    for (int kk = 0; kk < k; ++kk) {
+    for (int kk = kk0; kk < kk1; ++kk) {
         const int64_t off = s_off[kk];
         if (off < 0) continue;
         const RT* U = rows + off + static_cast<int64_t>(j) * r;
@@ -519,6 +521,14 @@ __global__ void __launch_bounds__(128) factored_out_kernel(RowSrc src, const flo
             }
         }
     }
+    if (gridDim.z > 1) {   // row-split partial sums: factored_combine_kernel finishes
+        const int64_t BT = static_cast<int64_t>(gridDim.y) * T;
+#pragma unroll
+        for (int t = 0; t < TMAX; ++t)
+            if (t < T) part[(blockIdx.z * BT + static_cast<int64_t>(b) * T + t) * d_B + j] = acc[t];
+        pbias[(static_cast<int64_t>(blockIdx.z) * gridDim.y + b) * d_B + j] = bias;
+        return;
+    }
     const float g = __ldg(gamma);
     const float pbj = b_base[j] + bias;
 #pragma unroll
@@ -528,6 +538,31 @@ __global__ void __launch_bounds__(128) factored_out_kernel(RowSrc src, const flo
             h_mid[o] = Elem<ACT>::from_f(Elem<ACT>::to_f(hA[o]) + g * (base[o] + acc[t]) + pbj);
         }
     }
+}
+
+// h_mid from the row-split partial sums of factored_out_kernel, added in split order.
+template <class ACT>
+__global__ void __launch_bounds__(256) factored_combine_kernel(const float* __restrict__ part,
+                                                               const float* __restrict__ pbias, int nsplit,
+                                                               const ACT* __restrict__ hA,
+                                                               const float* __restrict__ base,
+                                                               const float* __restrict__ b_base,
+                                                               const float* __restrict__ gamma, int B, int T,
+                                                               int d_B, ACT* __restrict__ h_mid) {
+    pdl_enter();
+    const int64_t BT = static_cast<int64_t>(B) * T, n = BT * d_B;
+    const int64_t o = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (o >= n) return;
+    const int j = static_cast<int>(o % d_B);
+    const int64_t bt = o / d_B;
+    const int b = static_cast<int>(bt / T);
+    float acc = 0.f, bias = 0.f;
+    for (int z = 0; z < nsplit; ++z) {
+        acc += part[z * n + o];
+        bias += pbias[(static_cast<int64_t>(z) * B + b) * d_B + j];
+    }
+    const float g = __ldg(gamma);
+    h_mid[o] = Elem<ACT>::from_f(Elem<ACT>::to_f(hA[o]) + g * (base[o] + acc) + (b_base[j] + bias));
 }
 
 // 4 consecutive elements as floats (8-byte bf16 / 16-byte f32 access).
@@ -544,16 +579,17 @@ __device__ __forceinline__ void load4(const __nv_bfloat16* p, float* v) {
 
 // base[m][j] = <W_base[j], h[m]> for a few rows m (M <= MMAX): W_base is read
 // once, in fp32, straight from the parameter (no cast, no tile padding).  A
-// warp owns 4 rows of W_base so that every h load feeds 4 of them; 4 warps
-// per CTA.
+// CTA owns 4 rows of W_base (every h load feeds 4 of them) and its 8 warps
+// split the d_A columns, so that 8x more loads are in flight than with one
+// warp per row group; the 8 partial sums are added in warp order.
 template <class ACT, int MMAX>
-__global__ void __launch_bounds__(128) base_rows_kernel(const float* __restrict__ W_base,
+__global__ void __launch_bounds__(256) base_rows_kernel(const float* __restrict__ W_base,
                                                         const ACT* __restrict__ hA, int M, int d_A, int d_B,
                                                         bool vec, float* __restrict__ base) {
     pdl_enter();
+    __shared__ float s_part[8][4][MMAX];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int j0 = (blockIdx.x * 4 + warp) * 4;
-    if (j0 >= d_B) return;
+    const int j0 = blockIdx.x * 4;
     const int nj = min(4, d_B - j0);
     float acc[4][MMAX];
 #pragma unroll
@@ -561,8 +597,10 @@ __global__ void __launch_bounds__(128) base_rows_kernel(const float* __restrict_
 #pragma unroll
         for (int m = 0; m < MMAX; ++m) acc[jj][m] = 0.f;
     if (vec) {
+        const int span = (d_A / 4 + 7) / 8 * 4;          // columns per warp, a multiple of 4
+        const int c0 = warp * span, c1 = min(d_A, c0 + span);
 #pragma unroll 2
-        for (int i0 = lane * 4; i0 < d_A; i0 += 128) {
+        for (int i0 = c0 + lane * 4; i0 < c1; i0 += 128) {
             float4 w[4];
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj)
@@ -581,7 +619,7 @@ __global__ void __launch_bounds__(128) base_rows_kernel(const float* __restrict_
             }
         }
     } else {
-        for (int i = lane; i < d_A; i += 32) {
+        for (int i = threadIdx.x; i < d_A; i += 256) {
             float w[4];
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) w[jj] = jj < nj ? W_base[static_cast<int64_t>(j0 + jj) * d_A + i] : 0.f;
@@ -603,8 +641,17 @@ __global__ void __launch_bounds__(128) base_rows_kernel(const float* __restrict_
                 float v = acc[jj][m];
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (lane == 0 && jj < nj) base[static_cast<int64_t>(m) * d_B + j0 + jj] = v;
+                if (lane == 0) s_part[warp][jj][m] = v;
             }
+        }
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < 4 * MMAX; t += blockDim.x) {
+        const int jj = t / MMAX, m = t - jj * MMAX;
+        if (jj < nj && m < M) {
+            float v = 0.f;
+            for (int w = 0; w < 8; ++w) v += s_part[w][jj][m];
+            base[static_cast<int64_t>(m) * d_B + j0 + jj] = v;
         }
     }
 }
@@ -1036,8 +1083,22 @@ struct FactWorkspace {
     void* hpad;     // [Mp, d_A] h_A rows padded with zeros to a whole 128-row tile (same case)
     float* hv;      // [B, T, k*r]
     float* base;    // [Mp, d_B] h_A W_base^T
+    float* part;    // [nsplit, B*T, d_B] row-split partial sums (nsplit > 1)
+    float* pbias;   // [nsplit, B, d_B]
+    int nsplit, kchunk;
     size_t bytes;
 };
+
+// Splits of the k rows of factored_out_kernel: enough CTAs for two per SM
+// when the batch alone gives fewer, at least 4 rows per split.
+static void factored_split(const DwaAssembleDims& d, int* nsplit, int* kchunk) {
+    const int64_t ctas = static_cast<int64_t>((d.d_B + 127) / 128) * d.B;
+    int ns = static_cast<int>(std::min<int64_t>((2 * 148 + ctas - 1) / ctas, std::max(1, d.k / 4)));
+    ns = std::max(ns, 1);
+    const int kc = (d.k + ns - 1) / ns;
+    *kchunk = kc;
+    *nsplit = (d.k + kc - 1) / kc;
+}
 
 static FactWorkspace carve_factored(void* base, const DwaAssembleDims& d) {
     Carver c(base);
@@ -1050,6 +1111,10 @@ static FactWorkspace carve_factored(void* base, const DwaAssembleDims& d) {
     w.hpad = c.take<char>(tc ? mp * d.d_A * 2 : 0);
     w.hv = c.take<float>(bt * kr);
     w.base = c.take<float>(mp * d.d_B);
+    factored_split(d, &w.nsplit, &w.kchunk);
+    const size_t ns = w.nsplit > 1 ? static_cast<size_t>(w.nsplit) : 0;
+    w.part = c.take<float>(ns * bt * d.d_B);
+    w.pbias = c.take<float>(ns * d.B * d.d_B);
     w.bytes = c.bytes();
     return w;
 }
@@ -1086,14 +1151,18 @@ static int factored_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc
     // main: base = h_A W_base^T over all B*T rows at once (W_base read once)
     if (BT <= kBaseRowsMax) {
         const bool vec_b = d.d_A % 4 == 0 && aligned16(W_base) && aligned16(hA);
-        const dim3 g_b((d.d_B + 15) / 16);
+        const dim3 g_b((d.d_B + 3) / 4);
         if (BT <= 4)
             DWA_TIMED("base_rows", st,
-                      launch_pdl(base_rows_kernel<ACT, 4>, g_b, 128, 0, st, W_base, hA, BT, d.d_A, d.d_B, vec_b,
+                      launch_pdl(base_rows_kernel<ACT, 4>, g_b, 256, 0, st, W_base, hA, BT, d.d_A, d.d_B, vec_b,
+                                 w.base));
+        else if (BT <= 8)
+            DWA_TIMED("base_rows", st,
+                      launch_pdl(base_rows_kernel<ACT, 8>, g_b, 256, 0, st, W_base, hA, BT, d.d_A, d.d_B, vec_b,
                                  w.base));
         else
             DWA_TIMED("base_rows", st,
-                      launch_pdl(base_rows_kernel<ACT, kBaseRowsMax>, g_b, 128, 0, st, W_base, hA, BT, d.d_A,
+                      launch_pdl(base_rows_kernel<ACT, kBaseRowsMax>, g_b, 256, 0, st, W_base, hA, BT, d.d_A,
                                  d.d_B, vec_b, w.base));
         DWA_LAUNCH_CHECK("base_rows_kernel");
         ++g_launches_total;
@@ -1130,7 +1199,7 @@ static int factored_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc
     if ((rc = lanes.join())) return rc;
     const size_t smem = factored_smem(d);
     const bool vec_u = d.r == 8 && d.D % 8 == 0 && aligned16(src.rows);
-    const dim3 g_out((d.d_B + 127) / 128, d.B);
+    const dim3 g_out((d.d_B + 127) / 128, d.B, w.nsplit);
 #define DWA_FACT_OUT(TM)                                                                                       \
     do {                                                                                                       \
         if (smem > 48 * 1024)                                                                                  \
@@ -1139,7 +1208,7 @@ static int factored_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc
         DWA_TIMED("factored_out", st,                                                                          \
                   launch_pdl(factored_out_kernel<ACT, RT, TM>, g_out, 128, smem, st, src, alphas, hA,           \
                              static_cast<const float*>(w.base), static_cast<const float*>(w.hv), b_base, gamma, \
-                             d.T, d.d_B, d.r, s2, vec_u, h_mid));                                              \
+                             d.T, d.d_B, d.r, s2, vec_u, w.kchunk, w.part, w.pbias, h_mid));                   \
     } while (0)
     if (d.T == 1)
         DWA_FACT_OUT(1);
@@ -1150,6 +1219,15 @@ static int factored_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc
 #undef DWA_FACT_OUT
     DWA_LAUNCH_CHECK("factored_out_kernel");
     ++g_launches_total;
+    if (w.nsplit > 1) {
+        const int64_t n = static_cast<int64_t>(BT) * d.d_B;
+        DWA_TIMED("factored_combine", st,
+                  launch_pdl(factored_combine_kernel<ACT>, dim3(static_cast<unsigned>((n + 255) / 256)), 256, 0, st,
+                             static_cast<const float*>(w.part), static_cast<const float*>(w.pbias), w.nsplit, hA,
+                             static_cast<const float*>(w.base), b_base, gamma, d.B, d.T, d.d_B, h_mid));
+        DWA_LAUNCH_CHECK("factored_combine_kernel");
+        ++g_launches_total;
+    }
     return DWA_OK;
 }
 

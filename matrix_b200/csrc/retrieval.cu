@@ -635,18 +635,68 @@ __global__ void fine_kernel(const float* __restrict__ qw, const float* __restric
 }
 
 // List-inverted fine scores for batches the key scans do not take (B > 32,
-// d_k = 64, S <= 4, no soft_full).  One CTA per (256 rows of a list, list):
-// it collects, in query order, the probes (b, j) of list c, reads each 64-row
-// chunk of the list's keys once into registers (thread = (aspect, row)) and
-// scores every probing query against it, instead of every query re-reading its
-// probed lists.  Per (row, query) the operations and their order are those of
+// d_k = 64, S <= 4, no soft_full).  One CTA per (64 rows of a list, list):
+// it takes the probes (b, j) of list c (from the probe CSR, or by scanning all
+// probes when there are too many lists for it), reads its 64-row chunk of the
+// list's keys once into registers (thread = (aspect, row)) and scores every
+// probing query against it, instead of every query re-reading its probed
+// lists.  Per (row, query) the operations and their order are those of
 // row_scores(), so the scores are bit-identical to fine_kernel's.
-constexpr int kFlRows = 64, kFlChunks = 4, kFlBatch = 16, kFlCap = 1024;
+constexpr int kFlRows = 64, kFlChunks = 1, kFlBatch = 16, kFlCap = 1024;
+constexpr int kFlMaxLists = 16384;   // lists up to which probe_lists_kernel builds the CSR
+
+// The probes (b*m + j, with rows) of every list as CSR: list_start [C+1],
+// list_ent [B*m].  One CTA; counts and cursors in shared memory.  Within a list
+// the order is arbitrary (each probe's scores are written independently).
+__global__ void __launch_bounds__(1024) probe_lists_kernel(const int32_t* __restrict__ top_clusters,
+                                                           const int64_t* __restrict__ cand_base, int B, int m,
+                                                           int C, int32_t* __restrict__ list_start,
+                                                           int32_t* __restrict__ list_ent) {
+    pdl_enter();
+    extern __shared__ int sh_lists[];
+    int* cnt = sh_lists;          // [C]
+    int* cur = sh_lists + C;      // [C]
+    __shared__ int s_seg[1024];
+    const int tid = threadIdx.x, BM = B * m;
+    for (int c = tid; c < C; c += 1024) cnt[c] = 0;
+    __syncthreads();
+    for (int e = tid; e < BM; e += 1024) {
+        const int64_t* cb = cand_base + static_cast<int64_t>(e / m) * (m + 1) + (e % m);
+        const int c = top_clusters[e];
+        if (cb[1] > cb[0] && c >= 0 && c < C) atomicAdd(&cnt[c], 1);
+    }
+    __syncthreads();
+    const int seg = (C + 1023) / 1024, c0 = tid * seg, c1 = min(C, c0 + seg);
+    int sum = 0;
+    for (int c = c0; c < c1; ++c) sum += cnt[c];
+    s_seg[tid] = sum;
+    __syncthreads();
+    for (int off = 1; off < 1024; off <<= 1) {
+        const int v = tid >= off ? s_seg[tid - off] : 0;
+        __syncthreads();
+        s_seg[tid] += v;
+        __syncthreads();
+    }
+    int run = s_seg[tid] - sum;
+    for (int c = c0; c < c1; ++c) {
+        list_start[c] = run;
+        cur[c] = run;
+        run += cnt[c];
+    }
+    if (tid == 1023) list_start[C] = s_seg[1023];
+    __syncthreads();
+    for (int e = tid; e < BM; e += 1024) {
+        const int64_t* cb = cand_base + static_cast<int64_t>(e / m) * (m + 1) + (e % m);
+        const int c = top_clusters[e];
+        if (cb[1] > cb[0] && c >= 0 && c < C) list_ent[atomicAdd(&cur[c], 1)] = e;
+    }
+}
 
 __global__ void __launch_bounds__(256) fine_lists_kernel(
     const float* __restrict__ qw, const float* __restrict__ keys, int64_t N, int S, int B, int m,
     const int32_t* __restrict__ top_clusters, const int64_t* __restrict__ probe_lo,
-    const int64_t* __restrict__ cand_base, int64_t K_cap, float* __restrict__ scores) {
+    const int64_t* __restrict__ cand_base, int64_t K_cap, const int32_t* __restrict__ list_start,
+    const int32_t* __restrict__ list_ent, float* __restrict__ scores) {
     pdl_enter();
     __shared__ int s_ent[kFlCap];
     __shared__ int s_wcnt[8];
@@ -657,9 +707,17 @@ __global__ void __launch_bounds__(256) fine_lists_kernel(
     const int s = tid >> 6, rl = tid & 63;
     const int BM = B * m;
     for (int start = 0;; start += kFlCap) {
-        // the probes of list c with ordinal in [start, start + kFlCap), in (b, j) order
+        // the probes of list c with ordinal in [start, start + kFlCap): from the
+        // CSR when it was built, else in (b, j) order from a scan of all probes
         int seen = 0;
-        for (int w0 = 0; w0 < BM; w0 += 256) {
+        if (list_start) {
+            const int a0 = list_start[c];
+            seen = list_start[c + 1] - a0;
+            const int nn = min(seen - start, kFlCap);
+            for (int i = tid; i < nn; i += 256) s_ent[i] = list_ent[a0 + start + i];
+            __syncthreads();
+        }
+        for (int w0 = 0; !list_start && w0 < BM; w0 += 256) {
             const int e = w0 + tid;
             bool hit = false;
             if (e < BM && top_clusters[e] == c) {
@@ -1206,6 +1264,8 @@ struct RetWorkspace {
     float* sfull;
     float* partial;
     float* stats;
+    int32_t* list_start;   // [C+1] probe CSR of the list-inverted fine pass
+    int32_t* list_ent;     // [B*m_eff]
     int m_eff;
     int64_t K_cap;
     int nblk;
@@ -1214,6 +1274,11 @@ struct RetWorkspace {
 
 constexpr int kFullRows = 256;
 constexpr int kMaxScanGrid = 1024;            // CTAs of a key scan
+
+// The list-inverted fine pass: batches above the key scans' 32 queries.
+static bool fine_by_lists(const DwaRetrieveDims& d, bool ivf, bool want_sf) {
+    return ivf && !want_sf && d.d_k == 64 && d.S <= 4 && d.B > 32;
+}
 
 static RetWorkspace carve_ret(void* base, const DwaRetrieveDims& d, bool ivf, bool want_sf) {
     Carver c(base);
@@ -1230,6 +1295,10 @@ static RetWorkspace carve_ret(void* base, const DwaRetrieveDims& d, bool ivf, bo
         w.c_score = c.take<float>(static_cast<size_t>(d.B) * d.C);
         w.topc = c.take<int32_t>(static_cast<size_t>(d.B) * w.m_eff);
         if (!want_sf) w.scores = c.take<float>(static_cast<size_t>(d.B) * w.K_cap);
+        if (fine_by_lists(d, ivf, want_sf) && d.C <= kFlMaxLists) {
+            w.list_start = c.take<int32_t>(static_cast<size_t>(d.C) + 1);
+            w.list_ent = c.take<int32_t>(static_cast<size_t>(d.B) * w.m_eff);
+        }
     }
     const bool full_pass = !ivf || want_sf;
     if (!ivf && !want_sf) w.sfull = c.take<float>(static_cast<size_t>(d.B) * d.N);
@@ -1538,10 +1607,21 @@ static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaSha
     // 4. fine scores of the probed lists (read from the full pass when it ran)
     if (ivf && !want_sf && (use_tc || use_scan)) {
         if ((rc = launch_scores(1, w.scores, nullptr))) return rc;
-    } else if (ivf && !want_sf && dk64 && d.S <= 4 && d.B > 32) {
+    } else if (fine_by_lists(d, ivf, want_sf) && dk64) {
+        if (w.list_start) {
+            const size_t lsm = 2 * static_cast<size_t>(d.C) * sizeof(int);
+            if (lsm > 48 * 1024)
+                DWA_CUDA_TRY(cudaFuncSetAttribute(probe_lists_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  static_cast<int>(lsm)));
+            DWA_TIMED("probe_lists", st, launch_pdl(probe_lists_kernel, 1, 1024, lsm, st, w.topc, w.cand_base, d.B,
+                                                    w.m_eff, d.C, w.list_start, w.list_ent));
+            DWA_LAUNCH_CHECK("probe_lists_kernel");
+            ++g_launches_total;
+        }
         dim3 gl(static_cast<unsigned>((d.max_list + kFlRows * kFlChunks - 1) / (kFlRows * kFlChunks)), d.C);
         DWA_TIMED("fine", st, launch_pdl(fine_lists_kernel, gl, 256, 0, st, w.qw, pool_keys, d.N, d.S, d.B,
-                                         w.m_eff, w.topc, w.probe_lo, w.cand_base, w.K_cap, w.scores));
+                                         w.m_eff, w.topc, w.probe_lo, w.cand_base, w.K_cap, w.list_start,
+                                         w.list_ent, w.scores));
         DWA_LAUNCH_CHECK("fine_lists_kernel");
         ++g_launches_total;
     } else if (ivf && !want_sf) {
