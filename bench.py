@@ -428,7 +428,7 @@ KERNELS = ["seq_mean", "query", "query_norm", "coarse", "topm", "full_scores", "
            "softmax_stats",
            "softmax_apply", "prep_factors", "prep_bias", "gemm_W", "gemm_apply", "gemm_G",
            "gemm_gh", "gemm_P", "gemm_Q", "colsum", "finalize", "bias_grad", "merge", "gather_rows",
-           "factored_hv", "base_rows", "cast_w_base", "gemm_base", "factored_out"]
+           "factored_hv", "base_rows", "cast_w_base", "gemm_base", "factored_out", "factored_combine", "probe_lists"]
 
 
 def profile_kernels(step, flush, n=5):
