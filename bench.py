@@ -55,6 +55,9 @@ def parse_args():
     ap.add_argument("--sharded", action="store_true",
                     help="row-shard the pool over the ranks (the medium / large configs): the "
                          "workload's batch is the global batch, each rank holds 1/N of the rows")
+    ap.add_argument("--emulate-ranks", type=int, default=0,
+                    help="with --sharded on one GPU: run rank 0 of this many ranks (its row share, "
+                         "retrieval for the whole batch over it, assembly of its sequences), no collectives")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip timing the retrieval VJP and the auxiliary losses")
@@ -148,22 +151,30 @@ class Step:
 
 
 # ------------------------------------------------- row-sharded workload ---
-def build_sharded_workload(w, device, rank, world, group, seed):
+def build_sharded_workload(w, device, rank, world, group, seed, emulate=0):
     """Rank ``rank``'s part of a row-sharded pool: the rows ``[lo, hi)`` (whole
     lists, balanced by rows) and their keys; the replicated parameters (same
     seed on every rank, centroids = key rows at random indices, combined by an
-    all-reduce); this rank's ``w.batch / world`` sequences."""
+    all-reduce); this rank's ``w.batch / world`` sequences.  ``emulate = P``
+    (one process): the rank of P with the most rows, whose sequences' queries
+    are joined by the other ranks' (all ``w.batch`` sequences are generated for
+    the query means) and whose centroids of lists held elsewhere are random
+    vectors of the keys' scale."""
+    shares = emulate if emulate else world
     import torch
     from matrix_b200.assembly import compute_key_cache
     from matrix_b200.sharded import shard_rows
     from matrix_b200.synthetic import zipf_list_offsets
     cfg = w.cfg
     d, D, N, S, dk, C = cfg.d_A, cfg.D, cfg.N, cfg.S, cfg.d_k, cfg.C
-    if w.batch % world:
+    if w.batch % shares:
         raise ValueError("the global batch must split evenly over the ranks")
     rng = np.random.default_rng(seed)
     off_np = (zipf_list_offsets(N, C, w.zipf, rng) if w.zipf else np.arange(C + 1, dtype=np.int64) * (N // C))
-    lo, hi = shard_rows(off_np, world)[rank]
+    bounds = shard_rows(off_np, shares)
+    if emulate:   # the rank with the most rows, which sets the step time of the job
+        rank = int(np.argmax([h - l for l, h in bounds]))
+    lo, hi = bounds[rank]
     bf = torch.bfloat16
     g_rows = torch.Generator(device=device).manual_seed(seed + 1 + rank)     # this rank's pool rows
     pool = torch.empty((hi - lo, D), dtype=bf, device=device)
@@ -181,7 +192,14 @@ def build_sharded_workload(w, device, rank, world, group, seed):
     if world > 1:
         import torch.distributed as dist
         dist.all_reduce(cent, group=group)
-    Bp = w.batch // world
+    if emulate:
+        others = np.nonzero((rows_c < lo) | (rows_c >= hi))[0]
+        if others.size:
+            scale = float(keys.std())
+            cent[:, torch.from_numpy(others).to(device)] = torch.randn(
+                (S, others.size, dk), generator=torch.Generator(device=device).manual_seed(seed + 3),
+                device=device) * scale
+    Bp = w.batch // shares
     gs = torch.Generator(device=device).manual_seed(seed + 7919 * (rank + 1))  # this rank's sequences
     t = dict(
         pool=pool, keys=keys, row_lo=lo, row_hi=hi, list_offsets=torch.from_numpy(off_np).to(device),
@@ -194,6 +212,9 @@ def build_sharded_workload(w, device, rank, world, group, seed):
         lam=torch.full((1,), w.lambda_val, device=device),
         h_A=torch.randn((Bp, w.seq, d), generator=gs, device=device).to(bf),
     )
+    if emulate:   # the other ranks' sequences, for the queries only
+        t["h_A_rest"] = torch.randn((w.batch - Bp, w.seq, d), generator=gs, device=device).to(bf)
+        t["rank"] = rank
     if w.backward:
         t["g_hmid"] = (torch.randn((Bp, w.seq, d), generator=gs, device=device) * 0.1).to(bf)
         t["g_W"] = torch.randn((Bp, d, d), generator=gs, device=device) * 1e-3
@@ -209,19 +230,25 @@ class ShardedStep:
     backward, the rows' gradients returned to their owners and the parameter
     gradients all-reduced."""
 
-    def __init__(self, w, t, group, rank, world):
+    def __init__(self, w, t, group, rank, world, emulate=0):
         import torch
         from matrix_b200 import _lib
         from matrix_b200.peer import PeerPool
         self.w, self.t, self.group, self.rank, self.world = w, t, group, rank, world
+        self.emulate = emulate
         self.lib = _lib.load()
         dev = t["h_A"].device
-        Bp = w.batch // world
+        Bp = w.batch // (emulate or world)
+        if emulate:
+            rank = t["rank"]
+            self.z_rest = torch.empty((w.batch - Bp, w.cfg.d_A), dtype=torch.float32, device=dev)
         self.b0, self.b1 = rank * Bp, (rank + 1) * Bp
         self.z_local = torch.empty((Bp, w.cfg.d_A), dtype=torch.float32, device=dev)
         self.z = torch.empty((w.batch, w.cfg.d_A), dtype=torch.float32, device=dev)
         bounds = None
-        if world > 1:
+        if emulate:
+            self.peers = PeerPool.from_shards([t["pool"]], [t["row_lo"], t["row_hi"]])
+        elif world > 1:
             import torch.distributed as dist
             lohi = [None] * world
             dist.all_gather_object(lohi, (t["row_lo"], t["row_hi"]), group=group)
@@ -244,6 +271,16 @@ class ShardedStep:
         if self.world > 1:
             import torch.distributed as dist
             dist.all_gather_into_tensor(self.z, self.z_local, group=self.group)
+            z = self.z
+        elif self.emulate:
+            # the other ranks' query means, in place of the all-gather
+            Bq = w.batch - self.z_local.shape[0]
+            rc = self.lib.dwa_sequence_mean(runtime.stream_of(dev), Bq, w.seq, cfg.d_A, 1,
+                                            runtime.ptr(t["h_A_rest"]), runtime.ptr(self.z_rest))
+            _lib.check(rc, "dwa_sequence_mean")
+            self.z[: self.b0].copy_(self.z_rest[: self.b0])
+            self.z[self.b0: self.b1].copy_(self.z_local)
+            self.z[self.b1:].copy_(self.z_rest[self.b0:])
             z = self.z
         else:
             z = self.z_local
@@ -762,8 +799,10 @@ def main():
         # a manual mode for the configs whose pool is row-sharded; the driver's
         # runs use the data-parallel default
         args.no_e2e = args.no_extras = args.no_key_cache = args.no_cpu_baseline = True
-        t = build_sharded_workload(w, dev, rank, world, group, args.seed)
-        step = ShardedStep(w, t, group, rank, world)
+        if args.emulate_ranks and world > 1:
+            raise SystemExit("--emulate-ranks runs on one GPU")
+        t = build_sharded_workload(w, dev, rank, world, group, args.seed, emulate=args.emulate_ranks)
+        step = ShardedStep(w, t, group, rank, world, emulate=args.emulate_ranks)
     else:
         t = build_device_workload(w, dev, args.seed + rank)
         step = Step(w, t, group)
@@ -846,6 +885,8 @@ def main():
     total_ms = float(tmax.item())
     ms_per_step = total_ms / args.steps
     tokens = w.batch * w.seq
+    if args.emulate_ranks:      # this GPU's sequences: rank 0's share of the batch
+        tokens = w.batch // args.emulate_ranks * w.seq
     # data parallel: w.batch sequences per rank; row-sharded: w.batch in all
     value = tokens * (1 if args.sharded else world) / (ms_per_step / 1e3)
 
@@ -917,7 +958,8 @@ def main():
     # ---- roofline of the dominant kernel ----
     peaks, peak_src = load_peaks()
     if args.sharded:
-        bound, work = kernel_work(w, dominant, n_rows=t["row_hi"] - t["row_lo"], seqs=w.batch // world)
+        bound, work = kernel_work(w, dominant, n_rows=t["row_hi"] - t["row_lo"],
+                                  seqs=w.batch // (args.emulate_ranks or world))
     else:
         bound, work = kernel_work(w, dominant)
     kms = float(np.mean(kern_ms))
@@ -958,6 +1000,14 @@ def main():
             "value_per_gpu": value / world, "roofline": roof,
             "kernels_ms": breakdown, "kernels_start_ms": kstarts, "gpu_launches": int(launches_per_step * args.steps),
             "clocks": clocks, "e2e": e2e}
+    if args.emulate_ranks:
+        P = args.emulate_ranks
+        line["config"]["parallelism"] = f"rows{P}, one rank emulated on one GPU"
+        line["config"]["emulated"] = (
+            f"rank {t['rank']} of {P} (the most rows): pool rows [{t['row_lo']}, {t['row_hi']}) of {w.cfg.N} (whole lists), retrieval of "
+            f"all {w.batch} queries over them, assembly of its {w.batch // P} sequences; the all-gathers, the "
+            f"merge across ranks, peer reads and the row-gradient exchange are not in it")
+        line["value_per_gpu"] = value
     if world == 1 and not args.no_key_cache:
         line["key_cache"] = time_key_cache(t, flush, peaks)
     if world == 1 and not args.no_extras:
