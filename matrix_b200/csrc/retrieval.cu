@@ -702,6 +702,7 @@ __global__ void __launch_bounds__(256) fine_lists_kernel(
     __shared__ int s_wcnt[8];
     __shared__ __align__(16) float s_q[kFlBatch][4 * 64];
     __shared__ float s_part[kFlBatch][4][kFlRows];
+    __shared__ int64_t s_out[kFlBatch];     // scores offset of each probe of the batch
     const int c = blockIdx.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int s = tid >> 6, rl = tid & 63;
@@ -770,10 +771,16 @@ __global__ void __launch_bounds__(256) fine_lists_kernel(
             }
             for (int i0 = 0; i0 < n; i0 += kFlBatch) {
                 const int nb = min(kFlBatch, n - i0);
-                for (int t = tid; t < nb * S * 64; t += 256) {
-                    const int i = t / (S * 64), o = t - i * (S * 64);
+                for (int t = tid; t < nb * S * 16; t += 256) {
+                    const int i = t / (S * 16), o = t - i * (S * 16);
                     const int b = s_ent[i0 + i] / m;
-                    s_q[i][o] = qw[static_cast<int64_t>(b) * S * 64 + o];
+                    reinterpret_cast<float4*>(s_q[i])[o] =
+                        __ldg(reinterpret_cast<const float4*>(qw + static_cast<int64_t>(b) * S * 64) + o);
+                }
+                if (tid < nb) {
+                    const int e = s_ent[i0 + tid];
+                    const int b = e / m, j = e - b * m;
+                    s_out[tid] = static_cast<int64_t>(b) * K_cap + cand_base[static_cast<int64_t>(b) * (m + 1) + j];
                 }
                 __syncthreads();
                 if (valid) {
@@ -796,11 +803,9 @@ __global__ void __launch_bounds__(256) fine_lists_kernel(
                     const int i = t / kFlRows, r2 = t - i * kFlRows;
                     const int64_t row2 = r0 + r2;
                     if (row2 < sz) {
-                        const int e = s_ent[i0 + i];
-                        const int b = e / m, j = e - b * m;
                         float sc = 0.f;
                         for (int s2 = 0; s2 < S; ++s2) sc += s_part[i][s2][r2];
-                        scores[static_cast<int64_t>(b) * K_cap + cand_base[static_cast<int64_t>(b) * (m + 1) + j] + row2] = sc;
+                        scores[s_out[i] + row2] = sc;
                     }
                 }
                 __syncthreads();
