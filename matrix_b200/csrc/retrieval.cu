@@ -277,51 +277,54 @@ __device__ int block_topk(int64_t n, int k, const KeyAt& key_at, uint64_t* sel_k
 // t, t + 256, ... (kProjCols of them per batch of loads in flight), the 256
 // partial dot products of an output are added by warp shuffles, then over the
 // 8 warps in warp order.
+// Larger batches take PR = 8 rows x PQ = 16 queries per CTA (fewer L2 re-reads
+// of z and W_Q); every thread still adds its columns in the same order, so the
+// outputs are bit-identical whichever tile computed them.
 constexpr int kProjRows = 2, kProjQ = 8, kProjThreads = 256, kProjCols = 4;
-template <class ZT>
+template <class ZT, int PR = kProjRows, int PQ = kProjQ, int PC = kProjCols>
 __global__ void __launch_bounds__(kProjThreads) query_proj_kernel(const ZT* __restrict__ z,
                                                                   const float* __restrict__ W_Q, int B,
                                                                   int rows, int d_A, float* __restrict__ q) {
     pdl_enter();
-    constexpr int NO = kProjRows * kProjQ;
+    constexpr int NO = PR * PQ;
     __shared__ float red[kProjThreads / 32][NO];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int o0 = blockIdx.x * kProjRows, b0 = blockIdx.y * kProjQ;
-    const int nr = min(kProjRows, rows - o0), nb = min(kProjQ, B - b0);
-    float acc[kProjRows][kProjQ];
+    const int o0 = blockIdx.x * PR, b0 = blockIdx.y * PQ;
+    const int nr = min(PR, rows - o0), nb = min(PQ, B - b0);
+    float acc[PR][PQ];
 #pragma unroll
-    for (int r = 0; r < kProjRows; ++r)
+    for (int r = 0; r < PR; ++r)
 #pragma unroll
-        for (int j = 0; j < kProjQ; ++j) acc[r][j] = 0.f;
-    for (int c0 = threadIdx.x; c0 < d_A; c0 += kProjThreads * kProjCols) {
-        float wv[kProjCols][kProjRows], zv[kProjCols][kProjQ];
+        for (int j = 0; j < PQ; ++j) acc[r][j] = 0.f;
+    for (int c0 = threadIdx.x; c0 < d_A; c0 += kProjThreads * PC) {
+        float wv[PC][PR], zv[PC][PQ];
 #pragma unroll
-        for (int u = 0; u < kProjCols; ++u) {
+        for (int u = 0; u < PC; ++u) {
             const int c = c0 + u * kProjThreads;
 #pragma unroll
-            for (int r = 0; r < kProjRows; ++r)
+            for (int r = 0; r < PR; ++r)
                 wv[u][r] = (c < d_A && r < nr) ? __ldg(W_Q + static_cast<int64_t>(o0 + r) * d_A + c) : 0.f;
 #pragma unroll
-            for (int j = 0; j < kProjQ; ++j)
+            for (int j = 0; j < PQ; ++j)
                 zv[u][j] = (c < d_A && j < nb) ? Elem<ZT>::to_f(z[static_cast<int64_t>(b0 + j) * d_A + c]) : 0.f;
         }
 #pragma unroll
-        for (int u = 0; u < kProjCols; ++u)
+        for (int u = 0; u < PC; ++u)
 #pragma unroll
-            for (int r = 0; r < kProjRows; ++r)
+            for (int r = 0; r < PR; ++r)
 #pragma unroll
-                for (int j = 0; j < kProjQ; ++j) acc[r][j] = fmaf(wv[u][r], zv[u][j], acc[r][j]);
+                for (int j = 0; j < PQ; ++j) acc[r][j] = fmaf(wv[u][r], zv[u][j], acc[r][j]);
     }
 #pragma unroll
-    for (int r = 0; r < kProjRows; ++r)
+    for (int r = 0; r < PR; ++r)
 #pragma unroll
-        for (int j = 0; j < kProjQ; ++j) {
+        for (int j = 0; j < PQ; ++j) {
             const float v = warp_sum(acc[r][j]);
-            if (lane == 0) red[warp][r * kProjQ + j] = v;
+            if (lane == 0) red[warp][r * PQ + j] = v;
         }
     __syncthreads();
     if (threadIdx.x < NO) {
-        const int r = threadIdx.x / kProjQ, j = threadIdx.x % kProjQ;
+        const int r = threadIdx.x / PQ, j = threadIdx.x % PQ;
         float v = 0.f;
 #pragma unroll
         for (int i = 0; i < kProjThreads / 32; ++i) v += red[i][threadIdx.x];
@@ -1363,7 +1366,14 @@ static int launch_queries_and_probes(cudaStream_t st, const DwaRetrieveDims& d, 
     // 1. raw aspect queries q = W_Q z
     const int rows = d.S * d.d_k;
     const dim3 gq((rows + kProjRows - 1) / kProjRows, (d.B + kProjQ - 1) / kProjQ);
-    if (d.z_dtype == DWA_BF16)
+    const dim3 gq_big((rows + 7) / 8, (d.B + 15) / 16);
+    if (d.B > 16 && d.z_dtype == DWA_BF16)
+        DWA_TIMED("query", st, launch_pdl(query_proj_kernel<__nv_bfloat16, 8, 16, 2>, gq_big, kProjThreads, 0, st,
+                                          static_cast<const __nv_bfloat16*>(z), W_Q, d.B, rows, d.d_A, w.q));
+    else if (d.B > 16)
+        DWA_TIMED("query", st, launch_pdl(query_proj_kernel<float, 8, 16, 2>, gq_big, kProjThreads, 0, st,
+                                          static_cast<const float*>(z), W_Q, d.B, rows, d.d_A, w.q));
+    else if (d.z_dtype == DWA_BF16)
         DWA_TIMED("query", st, launch_pdl(query_proj_kernel<__nv_bfloat16>, gq, kProjThreads, 0, st,
                                           static_cast<const __nv_bfloat16*>(z), W_Q, d.B, rows, d.d_A, w.q));
     else
