@@ -478,8 +478,12 @@ DWA_API int dwa_pool_grad_scatter(void* stream, int n, int D, const int32_t* ind
  *  - Allocates nothing (no cudaMalloc / cudaFree, no allocating library call).
  *  - All calls share the one array: calls that overlap on the GPU (other
  *    streams, other threads) race and must be serialised by the caller.
- *  - The device status word lives in that shared scratch and cannot be read
- *    back; use dwa_retrieve for runs that check it.
+ *  - The device status word (DWA_STATUS_* bits: a bad row index, bad list
+ *    offsets, a bounded wait that ran out) lives in that shared scratch; each
+ *    call clears it first.  dwa_retrieve_noalloc_status reads it back.
+ *  - The cached array address is per CUDA context, so a call from a context
+ *    that has not used the array yet does the look-up again: make the first
+ *    call of every context before any stream capture.
  * ------------------------------------------------------------------------- */
 DWA_API int dwa_retrieve_noalloc(void* stream, const DwaRetrieveDims* dims, int use_ivf,
                                  int is_warmup, const float* lambda_val, const void* z,
@@ -487,6 +491,13 @@ DWA_API int dwa_retrieve_noalloc(void* stream, const DwaRetrieveDims* dims, int 
                                  const float* centroids, const int64_t* list_offsets,
                                  const float* pool_keys, float* alphas, int32_t* indices,
                                  float* soft_full);
+
+/* The status word of the last dwa_retrieve_noalloc call on the current device
+ * and context, as dwa_workspace_status reports it for a workspace: copied on
+ * `stream` after the call's kernels (the stream is synchronised), cleared when
+ * `clear` is non-zero; DWA_ERR_DEVICE when a bit is set.  No counterpart in the
+ * reference (companion of dwa_retrieve_noalloc).  Allocates nothing. */
+DWA_API int dwa_retrieve_noalloc_status(void* stream, uint32_t* status, int clear);
 
 #ifdef __cplusplus
 }

@@ -14,6 +14,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libdwa.so")
 
 DWA_OK = 0
+DWA_ERR_DEVICE = -5
 DWA_F32 = 0
 DWA_BF16 = 1
 
@@ -93,6 +94,7 @@ _SIGNATURES = {
                                _P, _P, _P, _P, _P, _P, _P, C.c_size_t]),
     "dwa_retrieve_noalloc": (C.c_int, [_P, C.POINTER(RetrieveDims), C.c_int, C.c_int, _P, _P, _P,
                                        _P, _P, _P, _P, _P, _P, _P, _P]),
+    "dwa_retrieve_noalloc_status": (C.c_int, [_P, C.POINTER(C.c_uint32), C.c_int]),
     "dwa_retrieve_local": (C.c_int, [_P, C.POINTER(RetrieveDims), C.POINTER(Shard), C.c_int, C.c_int,
                                      _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t]),
     "dwa_retrieve_merge_workspace_bytes": (C.c_size_t, [C.POINTER(RetrieveDims)]),

@@ -20,6 +20,8 @@
 #include <atomic>
 #include <mutex>
 
+#include <cuda.h>
+
 #include "dwa_common.cuh"
 #include "tc_gemm.cuh"
 #include "scores_scan.cuh"
@@ -1821,29 +1823,65 @@ extern "C" int dwa_sequence_mean(void* stream, int B, int T, int d, int dtype, c
 // this file-scope device array instead of a caller workspace.  Every GPU that
 // loads libdwa keeps these 8 MiB until the process exits.  In host code the
 // name g_retrieve_scratch is only a stand-in for the symbol, not a device
-// address: the address a kernel may use comes from cudaGetSymbolAddress, once
-// per device, with that device current.
+// address: the address a kernel may use comes from cudaGetSymbolAddress, with
+// the device current.  The looked-up address is cached per CUDA context (the
+// module, and so the array, is loaded once per context), so a driver-API
+// context other than the primary one, or a primary context re-created after
+// cudaDeviceReset, gets its own lookup instead of a stale address.
 namespace dwa {
 constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
 static __device__ __align__(256) unsigned char g_retrieve_scratch[kNoAllocScratchBytes];
 
+using PFN_ctx_current = CUresult (*)(CUcontext*);
+
+static PFN_ctx_current ctx_current_fn() {
+    static PFN_ctx_current fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_ctx_current>(p);
+    });
+    return fn;
+}
+
+struct ScratchSlot {
+    CUcontext ctx;
+    void* addr;
+};
+constexpr int kScratchSlots = 64;
 static std::mutex g_scratch_mu;
-static void* g_scratch_addr[64];
+static ScratchSlot g_scratch_slots[kScratchSlots];
+static int g_scratch_next = 0;
 
 static int scratch_address(void** out) {
-    int dev = 0;
-    DWA_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) return fail(DWA_ERR_UNSUPPORTED, "device ordinal above 63");
+    PFN_ctx_current cur = ctx_current_fn();
+    if (!cur) return fail(DWA_ERR_CUDA, "cuCtxGetCurrent unavailable");
+    CUcontext ctx = nullptr;
+    if (cur(&ctx) != CUDA_SUCCESS) return fail(DWA_ERR_CUDA, "cuCtxGetCurrent failed");
     std::lock_guard<std::mutex> lk(g_scratch_mu);
-    if (!g_scratch_addr[dev]) {
-        void* p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_retrieve_scratch);
-        if (e != cudaSuccess || p == nullptr)
-            return fail(DWA_ERR_CUDA, std::string("cudaGetSymbolAddress(g_retrieve_scratch): ") +
-                                          cudaGetErrorString(e));
-        g_scratch_addr[dev] = p;
-    }
-    *out = g_scratch_addr[dev];
+    if (ctx)
+        for (int i = 0; i < kScratchSlots; ++i)
+            if (g_scratch_slots[i].ctx == ctx && g_scratch_slots[i].addr) {
+                *out = g_scratch_slots[i].addr;
+                return DWA_OK;
+            }
+    // no context yet (this look-up makes the device's primary context current)
+    // or a context that has not used the array: look its address up
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_retrieve_scratch);
+    if (e != cudaSuccess || p == nullptr)
+        return fail(DWA_ERR_CUDA, std::string("cudaGetSymbolAddress(g_retrieve_scratch): ") +
+                                      cudaGetErrorString(e));
+    if (cur(&ctx) != CUDA_SUCCESS || ctx == nullptr)
+        return fail(DWA_ERR_CUDA, "no current CUDA context after the symbol look-up");
+    // a context handle can be reused after its context is destroyed: the
+    // newest lookup for a handle wins, older slots are recycled round-robin
+    g_scratch_slots[g_scratch_next] = ScratchSlot{ctx, p};
+    g_scratch_next = (g_scratch_next + 1) % kScratchSlots;
+    *out = p;
     return DWA_OK;
 }
 }  // namespace dwa
@@ -1872,5 +1910,11 @@ extern "C" int dwa_retrieve_noalloc(void* stream, const DwaRetrieveDims* dims, i
     return dwa_retrieve(stream, dims, use_ivf, is_warmup, lambda_val, z, W_Q, aspect_weights, tau,
                         centroids, list_offsets, pool_keys, alphas, indices, soft_full, scratch,
                         kNoAllocScratchBytes);
+}
+
+extern "C" int dwa_retrieve_noalloc_status(void* stream, uint32_t* status, int clear) {
+    void* scratch = nullptr;
+    if (int rc = scratch_address(&scratch)) return rc;
+    return dwa_workspace_status(stream, scratch, status, clear);
 }
 #include "retrieval_bwd.cuh"

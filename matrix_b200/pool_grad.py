@@ -23,6 +23,8 @@ import torch
 from . import _lib
 from .runtime import dtype_code, ptr, require_cuda, stream_of, workspace
 
+SCATTER_MAX_N = 8192   # contributions one dwa_pool_grad_scatter call accepts
+
 
 def scatter_pool_grad(g_rows: torch.Tensor, indices: torch.Tensor, g_pool: torch.Tensor, *,
                       row_lo: int = 0, n_global: int | None = None) -> torch.Tensor:
@@ -43,12 +45,17 @@ def scatter_pool_grad(g_rows: torch.Tensor, indices: torch.Tensor, g_pool: torch
     n_global = row_lo + n_rows if n_global is None else n_global
     lib = _lib.load()
     n = idx.numel()
-    ws = workspace(dev, "pool_grad", lib.dwa_pool_grad_scatter_workspace_bytes(n))
+    # one call sorts at most SCATTER_MAX_N contributions; larger batches go in
+    # consecutive calls (each a deterministic sorted scatter-add, in order)
+    chunk = min(n, SCATTER_MAX_N)
+    ws = workspace(dev, "pool_grad", lib.dwa_pool_grad_scatter_workspace_bytes(max(chunk, 1)))
     with torch.cuda.device(dev):
-        rc = lib.dwa_pool_grad_scatter(stream_of(dev), n, D, ptr(idx), ptr(gr), int(n_global), int(row_lo),
-                                       int(row_lo + n_rows), dtype_code(g_pool.dtype, "g_pool"), ptr(g_pool),
-                                       ptr(ws), ws.numel())
-    _lib.check(rc, "dwa_pool_grad_scatter")
+        for i0 in range(0, n, SCATTER_MAX_N):
+            c = min(SCATTER_MAX_N, n - i0)
+            rc = lib.dwa_pool_grad_scatter(stream_of(dev), c, D, ptr(idx[i0:]), ptr(gr[i0:]), int(n_global),
+                                           int(row_lo), int(row_lo + n_rows), dtype_code(g_pool.dtype, "g_pool"),
+                                           ptr(g_pool), ptr(ws), ws.numel())
+            _lib.check(rc, "dwa_pool_grad_scatter")
     return g_pool
 
 

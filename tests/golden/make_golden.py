@@ -2,7 +2,9 @@
 
 Run in a container that has the reference checkout (read-only is fine)::
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <reference checkout>
+
+(or set ``DWA_REFERENCE_DIR`` to the checkout instead of passing ``--reference``).
 
 The reference's ``src/dwa/config.py``, ``src/dwa/retrieval.py`` and
 ``src/dwa/assembly_pallas.py`` are imported unchanged, with JAX / Flax replaced
@@ -98,9 +100,12 @@ def run_case(name, ref_config, ref_retrieval, ref_ap):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("DWA_REFERENCE_DIR"),
+                    help="root of the reference checkout (default: $DWA_REFERENCE_DIR)")
     ap.add_argument("--cases", nargs="*", default=list(CASES))
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("pass --reference <checkout> or set DWA_REFERENCE_DIR")
     ref_config, ref_retrieval, ref_ap = numpy_jax.load_reference_modules(
         os.path.join(args.reference, "src", "dwa"))
     for name in args.cases:

@@ -7,6 +7,10 @@ inside libdwa instead of a workspace.
 The GPU test calls it through the C ABI twice in a row and checks each result
 against the workspace entry point dwa_retrieve on the same inputs: indices
 identical, alphas and soft_full within the retrieval tolerance (rtol 1e-5).
+It then reads the device status word back through dwa_retrieve_noalloc_status:
+clear after the good calls, the list-overflow bit after a call whose max_list
+is shorter than the probed lists (the kernels clip such a list and flag it),
+and clear again after the next good call, since every call starts from zero.
 This file is collected last so a run that stops at the first failure has run
 every other test before it.
 """
@@ -87,3 +91,20 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls():
                 assert_close(a2, a1, TOL, name=f"alphas {tag}")
                 if want_sf:
                     assert_close(s2, s1, TOL, name=f"soft_full {tag}")
+
+    # the status word: clean after the good calls above
+    bits = C.c_uint32(0xFFFFFFFF)
+    assert lib.dwa_retrieve_noalloc_status(st, C.byref(bits), 1) == 0
+    assert bits.value == 0
+    # a max_list shorter than the lists (128 rows each): clipped and flagged
+    short = _lib.RetrieveDims(B, cfg.S, cfg.d_k, cfg.d_A, cfg.C, cfg.m, k, 64, N, cfg.T, _lib.DWA_F32)
+    a = torch.empty((B, k), device=dev)
+    i = torch.empty((B, k), dtype=torch.int32, device=dev)
+    lam = d(np.array([5.0], np.float32))
+    for dims_, expect in ((short, 0x8), (dims, 0)):
+        _lib.check(lib.dwa_retrieve_noalloc(st, dims_, 1, 0, ptr(lam), ptr(z), ptr(W_Q), ptr(aw), ptr(tau),
+                                            ptr(cents), ptr(off), ptr(keys), ptr(a), ptr(i), None),
+                   "noalloc")
+        rc = lib.dwa_retrieve_noalloc_status(st, C.byref(bits), 0)
+        assert bits.value == expect, (bits.value, expect)
+        assert rc == (0 if expect == 0 else _lib.DWA_ERR_DEVICE)
