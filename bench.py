@@ -1,25 +1,32 @@
 #!/usr/bin/env python
-"""Benchmark of the DWA hot path on B200: retrieve + assemble + apply, with the
-custom-VJP backward, on the single-GPU "small" workload
-(bf16, batch 8, seq 512, d 1024, pool 262144 x 17408, 512 lists, nprobe 8,
-top-k 32, gate selection with soft_full, forward + backward).
+"""Benchmark of the DWA hot path on B200: retrieve + gather + assemble, the
+pool and its IVF lists row-sharded over the GPUs of one node.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference]
+                    [--workload medium|small|large|decode]
 
-One JSON line on rank 0.  ``value`` is assembled tokens/s of the whole job
-(all ranks), timed on the device with CUDA events around each step, L2
-flushed (512 MB write, then a 256 MB read) between steps, max over ranks.  One step is replayed
-from a CUDA graph of: z = mean_t h_A -> dwa_retrieve -> dwa_assemble_fwd ->
-dwa_assemble_bwd (+ an NCCL all-reduce of the replicated-parameter gradients
-when N > 1, the shard_map transpose of the reference's batch-sharded path).
-With N GPUs every rank runs its own batch against its own pool replica
-(data parallel, weak scaling).
+Default workload ``medium``: bf16, global batch 16, seq 1024, d 2048, pool
+1M x 34816 rows (73 GB), 1024 lists, nprobe 16, top-k 64, gate selection with
+soft_full, forward.  Rank p of N holds the rows of a contiguous run of whole
+lists and their keys; one step is the sequence means of its sequences, an
+all-gather of z, ``dwa_retrieve_local`` over its rows, an all-gather of the
+[B, 2k+3] summaries, ``dwa_retrieve_merge``, the winning rows of its
+sequences read from their owners by peer loads (``dwa_gather_rows``) and
+``dwa_assemble_fwd`` of its B/N sequences.  Strong scaling: the job is the
+same at every N.  ``value`` is the job's assembled tokens/s: B*T over the step
+time, timed on the device with CUDA events around each step (a barrier before
+every step, L2 flushed between steps, the per-step maximum over ranks).
 
-``e2e`` repeats the step through the public Python API with the step's
-inputs copied from pinned host memory and its results copied back inside the
-timed region.  ``--impl reference`` times the CPU restatement of the
-reference's algorithm (the NumPy oracle; JAX is not installable here) on the
-host cores.
+At N=1 the line also carries ``small_fwd_bwd`` (the single-GPU small workload,
+forward + custom-VJP backward), the key-cache GEMM, the retrieval VJP, the aux
+losses and ``cpu_baseline``.  ``parity`` compares the sharded result with the
+single-device call over the all-gathered key cache and the peer-read rows with
+the masked-psum gather of the reference's model-sharded path.
+
+``--impl reference`` times the reference's algorithm on the host CPU: the
+NumPy restatement of the reference (JAX is not installable here), batched as
+the reference calls it, on all host cores, no GPU and nothing of this
+package.
 """
 
 from __future__ import annotations
@@ -39,26 +46,46 @@ sys.path.insert(0, ROOT)
 
 METRIC = "assembled tokens/sec/GPU (retrieve+assemble+apply) at 1/2/4/8 B200; % HBM/tensor roofline"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+L2_NOTE = "flushed between steps (512 MB write, then 256 MB read)"
+ROWS_WORKLOADS = ("medium", "large")
+
+# The workloads' sizes, restated for the host-only reference arm (which
+# imports nothing of the package); tests/test_bench_cpu.py checks them against
+# matrix_b200.config.WORKLOADS.  sample_B: sequences per reference step.
+HOST_WORKLOADS = {
+    "small": dict(B=8, T=512, d=1024, N=262144, C=512, m=8, k=32, r=8, S=4, dk=64, zipf=None,
+                  backward=True, soft_full=True, lam=5.0, warmup=False, sample_B=4),
+    "medium": dict(B=16, T=1024, d=2048, N=1 << 20, C=1024, m=16, k=64, r=8, S=4, dk=64, zipf=None,
+                   backward=False, soft_full=True, lam=5.0, warmup=False, sample_B=2),
+    "large": dict(B=32, T=2048, d=2048, N=1 << 22, C=4096, m=32, k=64, r=8, S=4, dk=64, zipf=1.1,
+                  backward=True, soft_full=True, lam=5.0, warmup=False, sample_B=1),
+}
+NOTES = {
+    "small": "bf16, batch 8, seq 512, d 1024, pool 262144, 512 lists, nprobe 8, top-k 32, fwd+bwd",
+    "medium": "bf16, batch 16, seq 1024, d 2048, pool 1M, 1024 lists, nprobe 16, top-k 64, fwd",
+    "large": "bf16, batch 32, seq 2048, d 2048, pool 4M, 4096 Zipf(1.1) lists, nprobe 32, top-k 64",
+}
 
 
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="small")
+    ap.add_argument("--workload", default="medium")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-budget-s", type=float, default=20.0,
                     help="CPU seconds for the cpu_baseline sample (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sharded", action="store_true",
-                    help="row-shard the pool over the ranks (the medium / large configs): the "
-                         "workload's batch is the global batch, each rank holds 1/N of the rows")
+                    help="row-shard the pool of the small workload too (medium and large always are)")
     ap.add_argument("--emulate-ranks", type=int, default=0,
-                    help="with --sharded on one GPU: run rank 0 of this many ranks (its row share, "
-                         "retrieval for the whole batch over it, assembly of its sequences), no collectives")
+                    help="row-sharded, one GPU: run the rank of this many that holds the most rows (its row "
+                         "share, retrieval of the whole batch over it, assembly of its sequences), no collectives")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-parity", action="store_true")
+    ap.add_argument("--no-small", action="store_true", help="skip the small fwd+bwd extra at N=1")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip timing the retrieval VJP and the auxiliary losses")
     ap.add_argument("--no-key-cache", action="store_true",
@@ -70,29 +97,199 @@ def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
-            d = json.load(f)
-        return d, "measured"
+            return json.load(f), "measured"
     return FALLBACK_PEAKS, "fallback"
 
 
-# --------------------------------------------------------------- workload ---
+def step_description(name, rows_mode, world, backward, emulate=0):
+    if rows_mode:
+        gather = ("dwa_gather_rows (peer loads of the winning rows)" if world > 1 or emulate else
+                  "winning rows read from the pool by index inside the assembly")
+        s = ("CUDA graph: seq_mean + " + ("all-gather of z + " if world > 1 else "") +
+             "dwa_retrieve_local + " + ("all-gather of summaries + " if world > 1 else "") +
+             "dwa_retrieve_merge + " + gather + " + dwa_assemble_fwd")
+        if backward:
+            s += (" + dwa_assemble_bwd + pool-row gradient exchange and scatter" +
+                  (" + NCCL all_reduce of parameter grads" if world > 1 else ""))
+        return s
+    return ("CUDA graph: seq_mean + dwa_retrieve + dwa_assemble_fwd" + (" + dwa_assemble_bwd" if backward else "")
+            + (" + NCCL all_reduce of parameter grads" if world > 1 and backward else ""))
+
+
+def run_config(name, world, rows_mode, emulate=0, w=None):
+    """The ``config`` object of the JSON line; identical for both arms.  A
+    workload without a host restatement (the ncu cases) takes its sizes from
+    ``w``."""
+    if name in HOST_WORKLOADS:
+        h, note = HOST_WORKLOADS[name], NOTES[name]
+    else:
+        h = dict(B=w.batch, T=w.seq, warmup=w.is_warmup, lam=w.lambda_val, soft_full=w.soft_full,
+                 backward=w.backward)
+        note = w.note
+    cfg = {"workload": name, "note": note,
+           "global_batch": h["B"] if rows_mode else h["B"] * world, "seq_len": h["T"],
+           "parallelism": (f"rows{emulate}, one rank emulated on one GPU" if emulate
+                           else f"rows{world}" if rows_mode else f"dp{world}"),
+           "mode": "warmup" if h["warmup"] else f"gate lambda={h['lam']}",
+           "soft_full": h["soft_full"], "backward": h["backward"], "l2": L2_NOTE,
+           "step": step_description(name, rows_mode, world, h["backward"], emulate)}
+    return cfg
+
+
+# ======================================================================
+# Host reference arm: the reference's algorithm on the CPU (NumPy port)
+# ======================================================================
+def _zipf_offsets(N, C, s, rng):
+    w = 1.0 / np.arange(1, C + 1, dtype=np.float64) ** s
+    sizes = np.floor(w / w.sum() * (N - C)).astype(np.int64) + 1
+    sizes[0] += N - sizes.sum()
+    rng.shuffle(sizes)
+    off = np.zeros(C + 1, dtype=np.int64)
+    np.cumsum(sizes, out=off[1:])
+    return off
+
+
+def host_inputs(name, seed, n_pool_rows=4096):
+    """Seeded host inputs of workload ``name`` for the reference's CPU path:
+    the key cache [S, N, d_k] f32 drawn from N(0, 1/d) (the distribution
+    compute_key_cache gives for pool rows ~ N(0, 1/sqrt d) and key projections
+    ~ N(0, 1/sqrt D); the 73 GB pool itself is not formed on the host),
+    centroids = keys of a random row per list, the retrieval and assembly
+    parameters at their initialisation scales, ``sample_B`` sequences of h_A,
+    and ``n_pool_rows`` pool rows that the gather reads (row i mod n)."""
+    h = HOST_WORKLOADS[name]
+    rng = np.random.default_rng(seed)
+    d, N, S, dk, C, r, Bs, T = h["d"], h["N"], h["S"], h["dk"], h["C"], h["r"], h["sample_B"], h["T"]
+    D = d * (2 * r + 1)
+    f32 = np.float32
+    keys = rng.standard_normal((S, N, dk), dtype=f32)
+    keys *= f32(d ** -0.5)
+    off = (_zipf_offsets(N, C, h["zipf"], rng) if h["zipf"] else np.arange(C + 1, dtype=np.int64) * (N // C))
+    rows_c = off[:-1] + (rng.random(C) * np.diff(off)).astype(np.int64)
+    x = dict(keys=keys, list_offsets=off, centroids=np.ascontiguousarray(keys[:, rows_c, :]),
+             W_Q=rng.standard_normal((S, dk, d), dtype=f32) * f32(d ** -0.5),
+             aspect_weights=np.zeros(S, f32), tau=f32(0.0),
+             W_base=rng.standard_normal((d, d), dtype=f32) * f32(0.01), b_base=np.zeros(d, f32),
+             gamma=f32(0.1), h_A=rng.standard_normal((Bs, T, d), dtype=f32),
+             pool_rows=rng.standard_normal((n_pool_rows, D), dtype=f32) * f32(d ** -0.5))
+    if h["backward"]:
+        x["g_hmid"] = rng.standard_normal((Bs, T, d), dtype=f32) * f32(0.1)
+        x["g_W"] = rng.standard_normal((Bs, d, d), dtype=f32) * f32(1e-3)
+    return x
+
+
+def host_step(name, x):
+    """One batched call of the reference's forward (retrieve + gather + float32
+    cast + assemble_jax) and, when the workload has one, its VJP, over the
+    ``sample_B`` sequences of ``x``, through the NumPy restatement."""
+    from oracle import dwa_oracle as O
+    h = HOST_WORKLOADS[name]
+    z = x["h_A"].mean(axis=1, dtype=np.float32)
+    alphas, idx, _ = O.retrieve(z, x["W_Q"], x["aspect_weights"], x["tau"], x["centroids"], x["keys"],
+                                k=h["k"], m=h["m"], T=1.0, lambda_val=h["lam"], is_warmup=h["warmup"],
+                                list_offsets=x["list_offsets"], want_soft_full=h["soft_full"])
+    gathered = O.gather(x["pool_rows"], idx % x["pool_rows"].shape[0])
+    h_mid, W = O.assemble(gathered, alphas, x["h_A"], x["W_base"], x["b_base"], x["gamma"], h["d"], h["r"], h["d"])
+    if h["backward"]:
+        O.assemble_bwd(gathered, alphas, x["h_A"], W, x["gamma"], x["g_hmid"], x["g_W"], h["d"], h["r"], h["d"])
+    return h_mid
+
+
+def host_threads():
+    """Let every BLAS / OpenMP pool use all host cores (torchrun sets
+    OMP_NUM_THREADS=1 on every rank); returns (os.cpu_count(), threads in use)."""
+    n = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_info, threadpool_limits
+        threadpool_limits(limits=n)
+        used = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:  # noqa: BLE001
+        used = 1
+    return n, used
+
+
+def host_sample_desc(name):
+    h = HOST_WORKLOADS[name]
+    return (f"batched call over {h['sample_B']} of the {h['B']} sequences per step ({h['T']} tokens each): "
+            f"retrieve over all {h['N']} key rows (IVF {h['C']} lists, nprobe {h['m']}, top-k {h['k']}, "
+            f"{'soft_full, ' if h['soft_full'] else ''}gate lambda {h['lam']}), gather + float32 cast, "
+            f"assemble_jax{' + its VJP' if h['backward'] else ''}; NumPy float32 restatement of "
+            f"retrieval.py:48-159, model.py:193-195, assembly_pallas.py:42-75"
+            f"{', 246-329' if h['backward'] else ''}; keys drawn from the compute_key_cache distribution, "
+            f"gathered rows from a 4096-row host pool")
+
+
+def reference_arm(args, rank, world):
+    """--impl reference: rank 0 times the host path; other ranks exit at once."""
+    if rank != 0:
+        return
+    name = args.workload
+    if name not in HOST_WORKLOADS:
+        print(json.dumps({"impl": "reference", "unavailable": f"no host reference for workload {name}"}))
+        return
+    cores, threads = host_threads()
+    h = HOST_WORKLOADS[name]
+    rows_mode = name in ROWS_WORKLOADS or args.sharded
+    x = host_inputs(name, args.seed)
+    for _ in range(args.warmup):
+        host_step(name, x)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        host_step(name, x)
+        times.append(time.perf_counter() - t0)
+    sec = float(np.mean(times))
+    value = h["sample_B"] * h["T"] / sec
+    sample = host_sample_desc(name)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+            "scaling": "strong" if rows_mode else "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": run_config(name, world, rows_mode),
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "threads": threads,
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "host": {"os_cpu_count": cores, "blas_threads": threads}}
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(name, seed, budget_s):
+    """The host path on a bounded sample of workload ``name`` (rank 0, N=1)."""
+    cores, threads = host_threads()
+    h = HOST_WORKLOADS[name]
+    x = host_inputs(name, seed)
+    host_step(name, x)   # warm-up
+    times = []
+    t0 = time.perf_counter()
+    while not times or (time.perf_counter() - t0 < budget_s and len(times) < 20):
+        s = time.perf_counter()
+        host_step(name, x)
+        times.append(time.perf_counter() - s)
+    sec = float(np.mean(times))
+    return {"value": h["sample_B"] * h["T"] / sec, "unit": "tokens/s", "cores": cores, "threads": threads,
+            "kind": "port", "sample": f"{len(times)} steps, each a " + host_sample_desc(name),
+            "sec_per_step": sec}
+
+
+# ======================================================================
+# Device workloads
+# ======================================================================
 def build_device_workload(w, device, seed):
-    """Seeded synthetic inputs generated on the device (the pool is 9 GB)."""
+    """Seeded synthetic inputs of a data-parallel (replicated pool) workload,
+    generated on the device (the small pool is 9.1 GB)."""
     import torch
+    from matrix_b200.assembly import compute_key_cache
     cfg = w.cfg
     g = torch.Generator(device=device).manual_seed(seed)
     d, D, N, S, dk, C = cfg.d_A, cfg.D, cfg.N, cfg.S, cfg.d_k, cfg.C
     bf = torch.bfloat16
     pool = torch.empty((N, D), dtype=bf, device=device)
-    step = 16384
-    for i in range(0, N, step):
-        pool[i:i + step].normal_(0.0, d ** -0.5, generator=g)
+    for i in range(0, N, 16384):
+        pool[i:i + 16384].normal_(0.0, d ** -0.5, generator=g)
     key_proj = (torch.randn((S, D, dk), generator=g, device=device) * D ** -0.5).to(bf)
-    from matrix_b200.assembly import compute_key_cache
     keys = compute_key_cache(pool, key_proj)        # once per window in training (outside the step)
     off = torch.arange(C + 1, dtype=torch.int64, device=device) * (N // C)
     rows = off[:-1] + torch.randint(0, N // C, (C,), generator=g, device=device)
-    t = dict(
+    return dict(
         pool=pool, key_proj=key_proj, keys=keys, list_offsets=off, centroids=keys[:, rows, :].contiguous(),
         W_Q=torch.randn((S, dk, d), generator=g, device=device) * d ** -0.5,
         aspect_weights=torch.zeros(S, device=device), tau=torch.zeros(1, device=device),
@@ -104,11 +301,10 @@ def build_device_workload(w, device, seed):
         g_hmid=(torch.randn((w.batch, w.seq, d), generator=g, device=device) * 0.1).to(bf),
         g_W=torch.randn((w.batch, d, d), generator=g, device=device) * 1e-3,
     )
-    return t
 
 
 class Step:
-    """One hot-path step on device-resident inputs through the C ABI."""
+    """One data-parallel step on device-resident inputs through the C ABI."""
 
     def __init__(self, w, t, group):
         import torch
@@ -116,10 +312,11 @@ class Step:
         self.w, self.t, self.group = w, t, group
         self.lib = _lib.load()
         self.z = torch.empty((w.batch, w.cfg.d_A), dtype=torch.float32, device=t["h_A"].device)
+        self.comm_events = None
 
     def __call__(self, h_A=None, g_hmid=None, g_W=None):
         import torch
-        from matrix_b200 import runtime
+        from matrix_b200 import _lib, runtime
         from matrix_b200.assembly import assemble_backward, assemble_forward
         from matrix_b200.retrieval import retrieve
         w, t, cfg = self.w, self.t, self.w.cfg
@@ -127,10 +324,8 @@ class Step:
         g_hmid = t["g_hmid"] if g_hmid is None else g_hmid
         g_W = t["g_W"] if g_W is None else g_W
         dev = h_A.device
-        rc = self.lib.dwa_sequence_mean(runtime.stream_of(dev), w.batch, w.seq, cfg.d_A, 1,
-                                        runtime.ptr(h_A), runtime.ptr(self.z))
-        from matrix_b200 import _lib
-        _lib.check(rc, "dwa_sequence_mean")
+        _lib.check(self.lib.dwa_sequence_mean(runtime.stream_of(dev), w.batch, w.seq, cfg.d_A, 1,
+                                              runtime.ptr(h_A), runtime.ptr(self.z)), "dwa_sequence_mean")
         alphas, indices, soft_full = retrieve(
             self.z, t["W_Q"], t["aspect_weights"], t["tau"], t["centroids"], t["keys"], t["lam"],
             w.is_warmup, k=cfg.k_max, m=cfg.m, T=cfg.T, list_offsets=t["list_offsets"],
@@ -145,12 +340,29 @@ class Step:
             if self.group is not None:
                 import torch.distributed as dist
                 flat = torch.cat([out["g_W_base"].reshape(-1), out["g_b_base"], out["g_gamma"]])
-                dist.all_reduce(flat, group=self.group)
+                with comm_timer(self.comm_events, "param_allreduce"):
+                    dist.all_reduce(flat, group=self.group)
                 out["g_params"] = flat
         return out
 
 
-# ------------------------------------------------- row-sharded workload ---
+class comm_timer:
+    """Event pair around one collective (recorded into a graph capture as
+    external event nodes) when ``events`` maps its name to a pair."""
+
+    def __init__(self, events, name):
+        self.pair = events.get(name) if events else None
+
+    def __enter__(self):
+        if self.pair:
+            self.pair[0].record()
+
+    def __exit__(self, *exc):
+        if self.pair:
+            self.pair[1].record()
+        return False
+
+
 def build_sharded_workload(w, device, rank, world, group, seed, emulate=0):
     """Rank ``rank``'s part of a row-sharded pool: the rows ``[lo, hi)`` (whole
     lists, balanced by rows) and their keys; the replicated parameters (same
@@ -183,6 +395,7 @@ def build_sharded_workload(w, device, rank, world, group, seed, emulate=0):
     g = torch.Generator(device=device).manual_seed(seed)                    # replicated parameters
     key_proj = (torch.randn((S, D, dk), generator=g, device=device) * D ** -0.5).to(bf)
     keys = compute_key_cache(pool, key_proj)
+    del key_proj
     sizes = np.diff(off_np)
     rows_c = off_np[:-1] + (rng.random(C) * sizes).astype(np.int64)
     cent = torch.zeros((S, C, dk), device=device)
@@ -202,7 +415,7 @@ def build_sharded_workload(w, device, rank, world, group, seed, emulate=0):
     Bp = w.batch // shares
     gs = torch.Generator(device=device).manual_seed(seed + 7919 * (rank + 1))  # this rank's sequences
     t = dict(
-        pool=pool, keys=keys, row_lo=lo, row_hi=hi, list_offsets=torch.from_numpy(off_np).to(device),
+        pool=pool, keys=keys, row_lo=lo, row_hi=hi, bounds=bounds, list_offsets=torch.from_numpy(off_np).to(device),
         max_list=int(sizes.max()), centroids=cent.contiguous(),
         W_Q=torch.randn((S, dk, d), generator=g, device=device) * d ** -0.5,
         aspect_weights=torch.zeros(S, device=device), tau=torch.zeros(1, device=device),
@@ -226,9 +439,10 @@ class ShardedStep:
     """One step of a row-sharded pool on this rank: the sequence means of its
     sequences, one all-gather of z, row-sharded retrieval (local top-k, one
     all-gather of the summaries, merge), the winning rows of its sequences read
-    from the ranks that hold them (peer loads), their assembly and, with the
-    backward, the rows' gradients returned to their owners and the parameter
-    gradients all-reduced."""
+    from the ranks that hold them (peer loads; with one rank the assembly reads
+    them from the pool by index), their assembly and, with the backward, the
+    rows' gradients returned to their owners and the parameter gradients
+    all-reduced."""
 
     def __init__(self, w, t, group, rank, world, emulate=0):
         import torch
@@ -237,6 +451,7 @@ class ShardedStep:
         self.w, self.t, self.group, self.rank, self.world = w, t, group, rank, world
         self.emulate = emulate
         self.lib = _lib.load()
+        self.comm_events = None
         dev = t["h_A"].device
         Bp = w.batch // (emulate or world)
         if emulate:
@@ -245,204 +460,83 @@ class ShardedStep:
         self.b0, self.b1 = rank * Bp, (rank + 1) * Bp
         self.z_local = torch.empty((Bp, w.cfg.d_A), dtype=torch.float32, device=dev)
         self.z = torch.empty((w.batch, w.cfg.d_A), dtype=torch.float32, device=dev)
-        bounds = None
+        self.peers = None
         if emulate:
             self.peers = PeerPool.from_shards([t["pool"]], [t["row_lo"], t["row_hi"]])
         elif world > 1:
-            import torch.distributed as dist
-            lohi = [None] * world
-            dist.all_gather_object(lohi, (t["row_lo"], t["row_hi"]), group=group)
-            bounds = [lohi[0][0]] + [h for _, h in lohi]
+            bounds = [t["bounds"][0][0]] + [h for _, h in t["bounds"]]
             self.peers = PeerPool(t["pool"], bounds, group)
-        else:
-            self.peers = PeerPool.from_shards([t["pool"]], [0, t["row_hi"]])
 
-    def __call__(self):
-        import torch
+    def __call__(self, h_A=None):
         from matrix_b200 import _lib, runtime
         from matrix_b200.assembly import assemble_backward, assemble_forward
         from matrix_b200.pool_grad import scatter_pool_grad_gathered
         from matrix_b200.sharded import RowShard, sharded_retrieve
         w, t, cfg = self.w, self.t, self.w.cfg
-        dev = t["h_A"].device
-        rc = self.lib.dwa_sequence_mean(runtime.stream_of(dev), self.z_local.shape[0], w.seq, cfg.d_A, 1,
-                                        runtime.ptr(t["h_A"]), runtime.ptr(self.z_local))
-        _lib.check(rc, "dwa_sequence_mean")
+        h_A = t["h_A"] if h_A is None else h_A
+        dev = h_A.device
+        _lib.check(self.lib.dwa_sequence_mean(runtime.stream_of(dev), self.z_local.shape[0], w.seq, cfg.d_A, 1,
+                                              runtime.ptr(h_A), runtime.ptr(self.z_local)), "dwa_sequence_mean")
         if self.world > 1:
             import torch.distributed as dist
-            dist.all_gather_into_tensor(self.z, self.z_local, group=self.group)
+            with comm_timer(self.comm_events, "allgather_z"):
+                dist.all_gather_into_tensor(self.z, self.z_local, group=self.group)
             z = self.z
         elif self.emulate:
             # the other ranks' query means, in place of the all-gather
             Bq = w.batch - self.z_local.shape[0]
-            rc = self.lib.dwa_sequence_mean(runtime.stream_of(dev), Bq, w.seq, cfg.d_A, 1,
-                                            runtime.ptr(t["h_A_rest"]), runtime.ptr(self.z_rest))
-            _lib.check(rc, "dwa_sequence_mean")
+            _lib.check(self.lib.dwa_sequence_mean(runtime.stream_of(dev), Bq, w.seq, cfg.d_A, 1,
+                                                  runtime.ptr(t["h_A_rest"]), runtime.ptr(self.z_rest)),
+                       "dwa_sequence_mean")
             self.z[: self.b0].copy_(self.z_rest[: self.b0])
             self.z[self.b0: self.b1].copy_(self.z_local)
             self.z[self.b1:].copy_(self.z_rest[self.b0:])
             z = self.z
         else:
             z = self.z_local
-        alphas, indices, soft = sharded_retrieve(
-            z, t["W_Q"], t["aspect_weights"], t["tau"], t["centroids"], t["keys"], t["list_offsets"], t["lam"],
-            w.is_warmup, RowShard(t["row_lo"], t["row_hi"], cfg.N, self.group), k=cfg.k_max, m=cfg.m, T=cfg.T,
-            max_list=t["max_list"], want_soft_full=w.soft_full)
+        with comm_timer(self.comm_events, "retrieve_sharded"):
+            alphas, indices, soft = sharded_retrieve(
+                z, t["W_Q"], t["aspect_weights"], t["tau"], t["centroids"], t["keys"], t["list_offsets"],
+                t["lam"], w.is_warmup, RowShard(t["row_lo"], t["row_hi"], cfg.N, self.group), k=cfg.k_max,
+                m=cfg.m, T=cfg.T, max_list=t["max_list"], want_soft_full=w.soft_full)
         idx_mine = indices[self.b0:self.b1]
-        rows = self.peers.gather(idx_mine)
-        h_mid, W, W_act = assemble_forward(rows, alphas[self.b0:self.b1], t["h_A"], t["W_base"], t["b_base"],
-                                           t["gamma"], cfg.d_B, cfg.r, cfg.d_A)
-        out = dict(alphas=alphas, indices=indices, soft_full=soft, h_mid=h_mid, W=W)
+        al_mine = alphas[self.b0:self.b1]
+        if self.peers is not None:
+            rows, row_index = self.peers.gather(idx_mine), None
+        else:
+            rows, row_index = t["pool"], idx_mine
+        h_mid, W, W_act = assemble_forward(rows, al_mine, h_A, t["W_base"], t["b_base"], t["gamma"],
+                                           cfg.d_B, cfg.r, cfg.d_A, row_index=row_index)
+        out = dict(alphas=alphas, indices=indices, soft_full=soft, h_mid=h_mid, W=W,
+                   rows=rows if row_index is None else None)
         if w.backward:
-            g = assemble_backward(rows, alphas[self.b0:self.b1], t["h_A"], W_act, t["gamma"], t["g_hmid"],
-                                  t["g_W"], cfg.d_B, cfg.r, cfg.d_A)
+            g = assemble_backward(rows, al_mine, h_A, W_act, t["gamma"], t["g_hmid"], t["g_W"],
+                                  cfg.d_B, cfg.r, cfg.d_A, row_index=row_index)
             out.update(zip(("g_rows", "g_alpha", "g_hA", "g_W_base", "g_b_base", "g_gamma"), g))
-            scatter_pool_grad_gathered(g[0], idx_mine, t["g_pool"], row_lo=t["row_lo"], n_global=cfg.N,
-                                       group=self.group)
+            with comm_timer(self.comm_events, "rowgrad_exchange"):
+                scatter_pool_grad_gathered(g[0], idx_mine, t["g_pool"], row_lo=t["row_lo"], n_global=cfg.N,
+                                           group=self.group if self.world > 1 else None)
             if self.world > 1:
+                import torch
                 import torch.distributed as dist
                 flat = torch.cat([out["g_W_base"].reshape(-1), out["g_b_base"], out["g_gamma"]])
-                dist.all_reduce(flat, group=self.group)
+                with comm_timer(self.comm_events, "param_allreduce"):
+                    dist.all_reduce(flat, group=self.group)
                 out["g_params"] = flat
         return out
 
 
-# ------------------------------------------------------------ decode sweep ---
-def decode_sweep(args, w, dev, flush, peaks, peak_src):
-    """The decode workload on one GPU holding one rank's share of 8: 2M/8 =
-    262144 pool rows x 69632 (d 4096, bf16, 36.5 GB) with their keys and 256
-    of the 2048 lists (1024 rows each).  A step is one token for B sequences:
-    sequence mean (T = 1), dwa_retrieve over this GPU's rows (gate mode,
-    nprobe 16, no soft_full) and dwa_assemble_apply (h_mid only, the winning
-    rows read from the pool by index).  ``decode_profile``: the same step at
-    batch 256, top-k 128 on its own small pool (for ncu).  Returns one
-    JSON-ready dict."""
-    import torch
-    from matrix_b200 import _lib, runtime
-    from matrix_b200.assembly import assemble_apply, compute_key_cache
-    from matrix_b200.retrieval import retrieve
-    c = w.cfg
-    share = 8 if w.name == "decode" else 1
-    shapes = [(B, k) for B in (1, 8, 64, 256) for k in (16, 128)] if w.name == "decode" else [(w.batch, c.k_max)]
-    d, D, S, dk, r = c.d_A, c.D, c.S, c.d_k, c.r
-    N, C = c.N // share, c.C // share
-    lib = _lib.load()
-    g = torch.Generator(device=dev).manual_seed(args.seed)
-    pool = torch.empty((N, D), dtype=torch.bfloat16, device=dev)
-    for i in range(0, N, 8192):
-        pool[i:i + 8192].normal_(0.0, d ** -0.5, generator=g)
-    key_proj = (torch.randn((S, D, dk), generator=g, device=dev) * D ** -0.5).to(torch.bfloat16)
-    keys = compute_key_cache(pool, key_proj)
-    del key_proj
-    rows_c = (torch.arange(C, device=dev) * (N // C) +
-              torch.randint(0, N // C, (C,), generator=g, device=dev))
-    cent = keys[:, rows_c].contiguous()
-    W_Q = torch.randn((S, dk, d), generator=g, device=dev) * d ** -0.5
-    aw, tau = torch.zeros(S, device=dev), torch.zeros(1, device=dev)
-    W_base = torch.randn((d, d), generator=g, device=dev) * 0.01
-    b_base = torch.zeros(d, device=dev)
-    gamma = torch.full((1,), c.gamma_init, device=dev)
-    lam = torch.full((1,), 5.0, device=dev)
-    points = []
-    for B, k in shapes:
-        h_A = torch.randn((B, 1, d), generator=g, device=dev).to(torch.bfloat16)
-        z = torch.empty((B, d), dtype=torch.float32, device=dev)
-
-        def step():
-            rc = lib.dwa_sequence_mean(runtime.stream_of(dev), B, 1, d, 1, runtime.ptr(h_A), runtime.ptr(z))
-            _lib.check(rc, "dwa_sequence_mean")
-            al, idx, _ = retrieve(z, W_Q, aw, tau, cent, keys, lam, False, k=k, m=c.m, T=c.T,
-                                  want_soft_full=False)
-            return assemble_apply(pool, al, h_A, W_base, b_base, gamma, d, r, d, row_index=idx)
-
-        step()
-        torch.cuda.synchronize()
-        c0 = _lib.launch_counters()[0]
-        step()
-        torch.cuda.synchronize()
-        launches = _lib.launch_counters()[0] - c0
-        kms, _ = profile_kernels(step, flush)
-        s_ = torch.cuda.Stream()
-        s_.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s_):
-            step()
-        torch.cuda.current_stream().wait_stream(s_)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            step()
-        for _ in range(max(args.warmup, 3)):
-            flush()
-            graph.replay()
-        reps = 20
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
-        torch.cuda.synchronize()
-        for a, b in ev:
-            flush()
-            a.record()
-            graph.replay()
-            b.record()
-        torch.cuda.synchronize()
-        ms = float(np.mean([a.elapsed_time(b) for a, b in ev]))
-        del graph
-        runtime.raise_on_device_status()
-        row_bytes = B * k * D * 2
-        pt = {"batch": B, "top_k": k, "ms_per_token_step": ms, "tokens_per_s": B / (ms / 1e3),
-              "kernels_ms": kms, "gpu_launches_per_step": int(launches),
-              "gathered_row_bytes": row_bytes}
-        # the two row kernels each read their part of every winning row
-        for name, part in (("factored_hv", r * d), ("factored_out", d * r + d)):
-            if kms.get(name):
-                gbs = B * k * part * 2 / (kms[name] / 1e3) / 1e9
-                pt[name + "_gbs"] = gbs
-                pt[name + "_frac"] = gbs / float(peaks["hbm_gbs"])
-        points.append(pt)
-    big = points[-1]
-    return {"metric": METRIC, "value": big["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1,
-            "steps": 20, "warmup": max(args.warmup, 3), "ms_per_step": big["ms_per_token_step"],
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic",
-            "config": {"workload": w.name, "note": w.note,
-                       "this_gpu": (f"one rank's share of {share}: " if share > 1 else "") +
-                                   f"{N} pool rows x {D}, {C} lists, nprobe {c.m}",
-                       "mode": "gate lambda=5.0, no soft_full, h_mid only (dwa_assemble_apply)",
-                       "l2": "flushed between steps (512 MB write, then 256 MB read)",
-                       "step": "CUDA graph: seq_mean + dwa_retrieve + dwa_assemble_apply",
-                       "headline": "batch 256, top-k 128"},
-            "peak_hbm_gbs": float(peaks["hbm_gbs"]), "peak_source": peak_src, "sweep": points}
-
-
-# ------------------------------------------------------ roofline numbers ---
-def profiled_traffic(kernel, w):
-    """DRAM bytes (read + write) per launch of `kernel` at workload `w`, from
-    the `traffic:` lines of the ncu summaries under profiles/.  A summary
-    captured on a smaller case is scaled by the queries x pool rows it
-    processed (the key stream and the s_full writes both grow with them)."""
-    d = os.path.join(ROOT, "profiles")
-    if not os.path.isdir(d):
-        return None
-    for fn in sorted(os.listdir(d)):
-        if not fn.endswith(".txt"):
-            continue
-        with open(os.path.join(d, fn)) as f:
-            for line in f:
-                if not line.startswith("traffic:"):
-                    continue
-                kv = dict(tok.split("=", 1) for tok in line.split()[1:] if "=" in tok)
-                if kv.get("kernel") != kernel:
-                    continue
-                scale = (w.cfg.N * w.batch) / (float(kv["rows"]) * float(kv["queries"]))
-                return int((int(kv["dram_read_bytes"]) + int(kv["dram_write_bytes"])) * scale)
-    return None
-
-
+# ======================================================================
+# Timing
+# ======================================================================
 def kernel_work(w, name, n_rows=None, seqs=None):
     """Algorithmic bytes (HBM-bound kernels) or flops (tensor kernels) of one
     launch of `name` on workload w; returns (bound, amount).  A rank of a
     row-sharded pool scores ``n_rows`` rows for all ``w.batch`` queries and
     assembles ``seqs`` sequences."""
     c = w.cfg
-    B, T, d, k, r, S, dk, N = w.batch, w.seq, c.d_A, c.k_max, c.r, c.S, c.d_k, c.N
-    N = N if n_rows is None else n_rows
+    B, T, d, k, r, S, dk = w.batch, w.seq, c.d_A, c.k_max, c.r, c.S, c.d_k
+    N = c.N if n_rows is None else n_rows
     Ba = B if seqs is None else seqs
     kr = k * r
     table = {
@@ -461,55 +555,405 @@ def kernel_work(w, name, n_rows=None, seqs=None):
     return table.get(name, ("hbm", None))
 
 
+def profiled_traffic(kernel, n_rows, queries):
+    """DRAM bytes (read + write) per launch of `kernel`, from the `traffic:`
+    lines of the ncu summaries under profiles/ (the one whose query count
+    matches, else any): a summary captured on a smaller case is scaled by the
+    key rows it read (keys and s_full writes both grow with the rows)."""
+    d = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(d):
+        return None
+    best = None
+    for fn in sorted(os.listdir(d)):
+        if not fn.endswith(".txt"):
+            continue
+        with open(os.path.join(d, fn)) as f:
+            for line in f:
+                if not line.startswith("traffic:"):
+                    continue
+                kv = dict(tok.split("=", 1) for tok in line.split()[1:] if "=" in tok)
+                if kv.get("kernel") != kernel:
+                    continue
+                if best is None or int(kv.get("queries", -1)) == queries:
+                    best = kv
+    if best is None:
+        return None
+    q0 = int(best["queries"])
+    bytes0 = int(best["dram_read_bytes"]) + int(best["dram_write_bytes"])
+    rows0 = float(best["rows"])
+    # per row: the key stream (fixed) plus q s_full floats written
+    per_row = bytes0 / rows0
+    return int(per_row * n_rows + 4 * n_rows * (queries - q0))
+
+
 KERNELS = ["seq_mean", "query", "query_norm", "coarse", "topm", "full_scores", "fine", "select",
            "softmax_stats",
            "softmax_apply", "prep_factors", "prep_bias", "gemm_W", "gemm_apply", "gemm_G",
            "gemm_gh", "gemm_P", "gemm_Q", "colsum", "finalize", "bias_grad", "merge", "gather_rows",
-           "factored_hv", "base_rows", "cast_w_base", "gemm_base", "factored_out", "factored_combine", "probe_lists"]
+           "factored_hv", "base_rows", "cast_w_base", "gemm_base", "factored_out", "factored_combine", "probe_lists",
+           "scatter_sort", "scatter_add"]
+COMM = ["allgather_z", "retrieve_sharded", "rowgrad_exchange", "param_allreduce"]
 
 
-def profile_kernels(step, flush, n=5):
-    """Average duration (ms) of every library kernel of one step, and its start
-    relative to the step's first kernel (the sequence mean), from replays of a
-    CUDA graph of the step in which the library records an event pair around
-    each kernel (no host launch gaps inside the measurement).  A kernel the
-    step does not launch keeps its setup record, which precedes the replay."""
+def C_ptr(event):
+    import ctypes
+    return ctypes.c_void_p(event.cuda_event)
+
+
+def capture(step, n_pre=1):
     import torch
-    from matrix_b200 import _lib
-    lib = _lib.load()
-    ev = {k: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for k in KERNELS}
-    for a, b in ev.values():     # torch creates the CUDA event on its first record
-        a.record(); b.record()
-    torch.cuda.synchronize()
-    for k, (a, b) in ev.items():
-        lib.dwa_profile_kernel(k.encode(), C_ptr(a), C_ptr(b))
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
-        step()
+        for _ in range(n_pre):
+            step()
     torch.cuda.current_stream().wait_stream(s)
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
         step()
-    lib.dwa_profile_clear()
-    first = ev[KERNELS[0]][0]
-    acc = {k: [] for k in KERNELS}
-    start = {k: [] for k in KERNELS}
+    return g
+
+
+def profile_kernels(step, flush, group, n=5):
+    """Per-kernel device time (ms) of one step, additive: the step is captured
+    with serialised launches (no programmatic dependent launch, the calls'
+    concurrent lanes on one stream) and an event pair around every library
+    kernel and every collective; averaged over ``n`` replays.  Returns
+    (durations, starts relative to the step's first kernel, serialised step
+    ms)."""
+    import torch
+    from matrix_b200 import _lib
+    lib = _lib.load()
+    mk = lambda: (torch.cuda.Event(enable_timing=True, external=True),  # noqa: E731
+                  torch.cuda.Event(enable_timing=True, external=True))
+    ev = {k: mk() for k in KERNELS}
+    comm = {k: mk() for k in COMM}
+    for a, b in list(ev.values()) + list(comm.values()):   # torch creates the CUDA event on first record
+        a.record(); b.record()
+    torch.cuda.synchronize()
+    for k, (a, b) in ev.items():
+        lib.dwa_profile_kernel(k.encode(), C_ptr(a), C_ptr(b))
+    lib.dwa_profile_serialize(1)
+    step.comm_events = comm
+    try:
+        g = capture(step)
+    finally:
+        step.comm_events = None
+        lib.dwa_profile_serialize(0)
+        lib.dwa_profile_clear()
+    whole = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+    acc = {k: [] for k in KERNELS + COMM}
+    start = {k: [] for k in KERNELS + COMM}
+    total = []
     for _ in range(n):
         flush()
+        sync_ranks(group)
+        whole[0].record()
         g.replay()
+        whole[1].record()
         torch.cuda.synchronize()
-        for k, (a, b) in ev.items():
-            t0 = first.elapsed_time(a)
+        total.append(whole[0].elapsed_time(whole[1]))
+        for k, (a, b) in list(ev.items()) + list(comm.items()):
+            t0 = whole[0].elapsed_time(a)
             if t0 >= 0.0:
                 acc[k].append(a.elapsed_time(b))
                 start[k].append(t0)
     del g
     dur = {k: float(np.mean(v)) for k, v in acc.items() if v}
-    return dur, {k: float(np.mean(start[k])) for k in dur}
+    return dur, {k: float(np.mean(start[k])) for k in dur}, float(np.mean(total))
 
 
+def sync_ranks(group):
+    import torch
+    torch.cuda.synchronize()
+    if group is not None:
+        import torch.distributed as dist
+        dist.barrier(group=group)
+        torch.cuda.synchronize()
+
+
+class ClockSampler:
+    """nvidia-smi samples of the SM clock, power and throttle reasons of the
+    given GPUs (by UUID), 200 ms apart, while the timed region runs."""
+    QUERY = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuids):
+        self.uuids = {u.lower().replace("gpu-", "") for u in uuids}
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, mx, reasons, power = [], None, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9 or f[0].lower().replace("gpu-", "") not in self.uuids:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        out = {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+               "samples": len(sm), "gpus": len(self.uuids)}
+        if power:
+            out["power_w_max"] = float(max(power))
+        return out
+
+
+def device_uuids(dev, group):
+    import torch
+    u = str(torch.cuda.get_device_properties(dev).uuid)
+    if group is None:
+        return [u]
+    import torch.distributed as dist
+    every = [None] * dist.get_world_size(group)
+    dist.all_gather_object(every, u, group=group)
+    return every
+
+
+def measure(step, flush, group, dev, steps, warmup, rank, sample_clocks=True):
+    """Launch count, additive kernel breakdown, then the timed graph replays:
+    ``steps`` replays after ``warmup``, each after an L2 flush and a barrier,
+    CUDA events around each replay, per-step maximum over ranks; the dominant
+    kernel re-timed live inside the timed replays (external event nodes)."""
+    import torch
+    from matrix_b200 import _lib
+    lib = _lib.load()
+    step()                       # first call: workspaces, kernel attributes
+    torch.cuda.synchronize()
+    c0 = _lib.launch_counters()[0]
+    step()
+    torch.cuda.synchronize()
+    launches = _lib.launch_counters()[0] - c0
+    breakdown, kstarts, serial_ms = profile_kernels(step, flush, group)
+    dominant = max((k for k in breakdown if k in KERNELS), key=breakdown.get)
+
+    ka = torch.cuda.Event(enable_timing=True, external=True)
+    kb = torch.cuda.Event(enable_timing=True, external=True)
+    ka.record(); kb.record()
+    torch.cuda.synchronize()
+    lib.dwa_profile_kernel(dominant.encode(), C_ptr(ka), C_ptr(kb))
+    try:
+        graph = capture(step, n_pre=2)
+    finally:
+        lib.dwa_profile_clear()
+    for _ in range(max(warmup, 3)):
+        flush()
+        graph.replay()
+    uuids = device_uuids(dev, group)
+    sampler = ClockSampler(uuids) if (rank == 0 and sample_clocks) else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    stops = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    kern_ms = []
+    sync_ranks(group)
+    for i in range(steps):
+        flush()
+        sync_ranks(group)
+        starts[i].record()
+        graph.replay()
+        stops[i].record()
+        stops[i].synchronize()
+        kern_ms.append(ka.elapsed_time(kb))
+    sync_ranks(group)
+    clocks = sampler.stop() if sampler else None
+    per_step = torch.tensor([a.elapsed_time(b) for a, b in zip(starts, stops)], device=dev, dtype=torch.float64)
+    mine = float(per_step.mean().item())
+    if group is not None:
+        import torch.distributed as dist
+        dist.all_reduce(per_step, op=dist.ReduceOp.MAX, group=group)
+    del graph
+    return dict(ms_per_step=float(per_step.sum().item()) / steps, rank_ms_per_step=mine, launches=int(launches),
+                breakdown=breakdown, starts=kstarts, serial_ms=serial_ms, dominant=dominant,
+                kern_ms=float(np.mean(kern_ms)), clocks=clocks)
+
+
+def roofline(w, m, peaks, peak_src, n_rows=None, seqs=None, queries=None):
+    bound, work = kernel_work(w, m["dominant"], n_rows=n_rows, seqs=seqs)
+    if work is None:
+        return None
+    kms = m["kern_ms"]
+    if bound == "hbm":
+        ach, peak, unit = work / (kms / 1e3) / 1e9, float(peaks["hbm_gbs"]), "GB/s"
+    else:
+        ach, peak, unit = work / (kms / 1e3) / 1e12, float(peaks["bf16_tflops"]), "TFLOP/s"
+    traffic = None
+    if m["dominant"] == "full_scores":
+        traffic = profiled_traffic("full_scores", n_rows if n_rows is not None else w.cfg.N,
+                                   queries if queries is not None else w.batch)
+    return {"kernel": m["dominant"], "bound": bound, "achieved": ach, "peak": peak, "unit": unit,
+            "frac": ach / peak, "traffic": traffic, "peak_source": peak_src,
+            "algorithmic_per_launch": work, "launch_ms": kms,
+            "timed_in": "graph replay of the timed steps (external event nodes)"}
+
+
+# ======================================================================
+# Parity of the row-sharded step
+# ======================================================================
+def rows_parity(w, t, step, group, rank, world):
+    """The sharded retrieval against ``dwa_retrieve`` on one device over the
+    all-gathered key cache (same z): indices equal, alphas and soft_full within
+    rtol 1e-5; and, with several ranks, each rank's peer-read rows against the
+    reference's masked-psum gather (model.py:16-47: every rank contributes the
+    rows it holds, zeros elsewhere, summed over the ranks).  Runs after the
+    timing, outside the timed region."""
+    import torch
+    from matrix_b200.retrieval import retrieve
+    cfg = w.cfg
+    dev = t["keys"].device
+    out = step()
+    torch.cuda.synchronize()
+    S, n_loc, dk = t["keys"].shape
+    z = step.z if (world > 1 or step.emulate) else step.z_local
+    if world > 1:
+        import torch.distributed as dist
+        n_max = max(h - l for l, h in t["bounds"])
+        pad = torch.zeros((S, n_max, dk), device=dev)
+        pad[:, :n_loc] = t["keys"]
+        allk = torch.empty((world, S, n_max, dk), device=dev)
+        dist.all_gather_into_tensor(allk, pad, group=group)
+        keys = torch.cat([allk[p, :, :h - l] for p, (l, h) in enumerate(t["bounds"])], dim=1).contiguous()
+        del allk, pad
+        sf = None
+        if out["soft_full"] is not None:
+            spad = torch.zeros((w.batch, n_max), device=dev)
+            spad[:, :n_loc] = out["soft_full"]
+            alls = torch.empty((world, w.batch, n_max), device=dev)
+            dist.all_gather_into_tensor(alls, spad, group=group)
+            sf = torch.cat([alls[p, :, :h - l] for p, (l, h) in enumerate(t["bounds"])], dim=1)
+            del alls, spad
+    else:
+        keys, sf = t["keys"], out["soft_full"]
+    a1, i1, s1 = retrieve(z, t["W_Q"], t["aspect_weights"], t["tau"], t["centroids"], keys, t["lam"], w.is_warmup,
+                          k=cfg.k_max, m=cfg.m, T=cfg.T, list_offsets=t["list_offsets"], max_list=t["max_list"],
+                          want_soft_full=w.soft_full)
+    res = {"indices_equal": bool(torch.equal(i1, out["indices"])),
+           "alphas_max_rel_err": float(((a1 - out["alphas"]).abs() / a1.abs().clamp_min(1e-30)).max().item())}
+    if s1 is not None and sf is not None:
+        res["soft_full_max_err_rel_to_max"] = float(((s1 - sf).abs().max() / s1.abs().max()).item())
+    del keys
+    if world > 1:
+        import torch.distributed as dist
+        idx = out["indices"].reshape(-1).long()
+        lo, hi = t["row_lo"], t["row_hi"]
+        mask = (idx >= lo) & (idx < hi)
+        full = torch.zeros((idx.numel(), cfg.D), dtype=t["pool"].dtype, device=dev)
+        full[mask] = t["pool"][idx[mask] - lo]
+        dist.all_reduce(full, group=group)
+        Bp = w.batch // world
+        mine = full.reshape(w.batch, cfg.k_max, cfg.D)[rank * Bp:(rank + 1) * Bp]
+        res["rows_equal"] = bool(torch.equal(mine, out["rows"]))
+        del full
+        flags = torch.tensor([float(res["indices_equal"]), float(res["rows_equal"])], device=dev)
+        dist.all_reduce(flags, op=dist.ReduceOp.MIN, group=group)
+        errs = torch.tensor([res["alphas_max_rel_err"], res.get("soft_full_max_err_rel_to_max", 0.0)], device=dev)
+        dist.all_reduce(errs, op=dist.ReduceOp.MAX, group=group)
+        res.update(indices_equal=bool(flags[0] > 0), rows_equal=bool(flags[1] > 0),
+                   alphas_max_rel_err=float(errs[0]), soft_full_max_err_rel_to_max=float(errs[1]),
+                   ranks_checked=world)
+    else:
+        res["rows_equal"] = None
+    res["ok"] = bool(res["indices_equal"] and res["alphas_max_rel_err"] <= 1e-5
+                     and res.get("soft_full_max_err_rel_to_max", 0.0) <= 1e-5
+                     and res["rows_equal"] is not False)
+    res["against"] = ("dwa_retrieve on one device over the all-gathered key cache; rows: the masked-psum "
+                      "gather of the reference's model-sharded path")
+    torch.cuda.synchronize()
+    return res
+
+
+# ======================================================================
+# End to end through the public API with pinned host buffers
+# ======================================================================
+def e2e_pipeline(step_fn, host_inputs_, result_keys, n, group, dev):
+    """A training input pipeline: step i+1's inputs go up on a copy stream while
+    step i computes and step i-1's results come down on another; device inputs
+    and pinned host outputs are double-buffered.  Every step's host->device
+    and device->host copies are inside the timed region.  Returns (ms per
+    step, max over ranks; h2d bytes; d2h bytes)."""
+    import torch
+    dev_bufs = [[torch.empty(h.shape, dtype=h.dtype, device=dev) for h in host_inputs_] for _ in range(2)]
+    for b, h in zip(dev_bufs[0], host_inputs_):
+        b.copy_(h)
+    out = step_fn(*dev_bufs[0])
+    torch.cuda.synchronize()
+    pins = [{k: torch.empty(out[k].shape, dtype=out[k].dtype).pin_memory() for k in result_keys} for _ in range(2)]
+    h2d = sum(h.nbytes for h in host_inputs_)
+    d2h = sum(v.nbytes for v in pins[0].values())
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    main = torch.cuda.current_stream()
+    ev_in = [torch.cuda.Event() for _ in range(n)]
+    ev_used = [torch.cuda.Event() for _ in range(n)]
+    ev_out = [torch.cuda.Event() for _ in range(n)]
+    t_start, t_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sync_ranks(group)
+    ring = [None, None]     # step outputs alive until their copy to the host is done
+    t_start.record(main)
+    s_in.wait_event(t_start)
+    for i in range(n):
+        bufs = dev_bufs[i % 2]
+        with torch.cuda.stream(s_in):
+            if i >= 2:
+                s_in.wait_event(ev_used[i - 2])      # step i-2 has read this buffer
+            for b, h in zip(bufs, host_inputs_):
+                b.copy_(h, non_blocking=True)
+            ev_in[i].record(s_in)
+        main.wait_event(ev_in[i])
+        if i >= 2:
+            main.wait_event(ev_out[i - 2])           # step i-2's outputs reached the host
+            ring[i % 2] = None
+        out = step_fn(*bufs)
+        ev_used[i].record(main)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_used[i])
+            for k in result_keys:
+                pins[i % 2][k].copy_(out[k], non_blocking=True)
+            ev_out[i].record(s_out)
+        ring[i % 2] = out
+    main.wait_event(ev_out[n - 1])
+    t_stop.record(main)
+    t_stop.synchronize()
+    e_ms = torch.tensor([t_start.elapsed_time(t_stop) / n], device=dev, dtype=torch.float64)
+    if group is not None:
+        import torch.distributed as dist
+        dist.all_reduce(e_ms, op=dist.ReduceOp.MAX, group=group)
+    return float(e_ms.item()), int(h2d), int(d2h)
+
+
+# ======================================================================
+# Extras at N=1 (small workload)
+# ======================================================================
 def time_key_cache(t, flush, peaks, reps=3):
     """``compute_key_cache`` on the workload's pool (once per training window,
     not part of the step), timed with CUDA events after a flush, against its
@@ -549,16 +993,10 @@ def time_key_cache(t, flush, peaks, reps=3):
 
 
 def time_training_extras(w, t, flush, peaks, reps=5):
-    """The training-time parts next to the step, on the workload's inputs, timed
-    with CUDA events after a flush (best of ``reps``):
-
-    * ``retrieve_bwd``: the retrieval VJP for the alphas' cotangent alone (the
-      key pass visits only the probed lists' tiles), with the soft_full
-      cotangent as well (the key pass reads every key row), and with the
-      key-cache gradient; the key pass of the full case against the HBM
-      roofline (keys + G read once: 4 (S N d_k + B N) bytes);
-    * ``aux_losses``: the four losses and their gradients.
-    The cotangents are seeded synthetic values of the right shapes."""
+    """The retrieval VJP (alphas' cotangent alone, with soft_full's, with the
+    key-cache gradient; key pass against its HBM roofline) and the aux losses,
+    on the small workload's inputs, timed with CUDA events after a flush (best
+    of ``reps``).  The cotangents are seeded synthetic values."""
     import torch
     from matrix_b200 import _lib
     from matrix_b200.losses import aux_losses_and_grads
@@ -618,163 +1056,133 @@ def time_training_extras(w, t, flush, peaks, reps=5):
     return out
 
 
-def C_ptr(event):
-    import ctypes
-    return ctypes.c_void_p(event.cuda_event)
-
-
-# ---------------------------------------------------------------- clocks ---
-class ClockSampler:
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-
-    def __init__(self, index):
-        self.index = index
-        self.proc = None
-        self.lines = []
-
-    def start(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "50"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except OSError:
-            self.proc = None
-
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
-    def stop(self):
-        if self.proc is None:
-            return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self.thread.join(timeout=2)
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": 0}
-        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
-
-
-# ----------------------------------------------------------- CPU baseline ---
-def cpu_baseline(w, t, budget_s):
-    """The NumPy oracle (the reference's algorithm, float32) on one sequence of
-    the same workload per sample, with the same key cache and pool rows."""
-    from oracle import dwa_oracle as O
+# ======================================================================
+# Decode sweep (manual mode)
+# ======================================================================
+def decode_sweep(args, w, dev, flush, peaks, peak_src):
+    """The decode workload on one GPU holding one rank's share of 8: 2M/8 =
+    262144 pool rows x 69632 (d 4096, bf16, 36.5 GB) with their keys and 256
+    of the 2048 lists (1024 rows each).  A step is one token for B sequences:
+    sequence mean (T = 1), dwa_retrieve over this GPU's rows (gate mode,
+    nprobe 16, no soft_full) and dwa_assemble_apply (h_mid only, the winning
+    rows read from the pool by index).  ``decode_profile``: the same step at
+    batch 256, top-k 128 on its own small pool (for ncu).  Returns one
+    JSON-ready dict."""
     import torch
-    try:
-        from threadpoolctl import threadpool_info
-        threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
-    except Exception:  # noqa: BLE001
-        threads = 1
-    cfg = w.cfg
-    keys = t["keys"].cpu().numpy()
-    cents = t["centroids"].cpu().numpy()
-    W_Q = t["W_Q"].cpu().numpy()
-    aw = t["aspect_weights"].cpu().numpy()
-    W_base = t["W_base"].cpu().numpy()
-    b_base = t["b_base"].cpu().numpy()
-    gamma = np.float32(t["gamma"].item())
-    h_all = t["h_A"].float().cpu().numpy()
-    g_all = t["g_hmid"].float().cpu().numpy()
-    gW_all = t["g_W"].cpu().numpy()
-    pool = t["pool"]
+    from matrix_b200 import _lib, runtime
+    from matrix_b200.assembly import assemble_apply, compute_key_cache
+    from matrix_b200.retrieval import retrieve
+    c = w.cfg
+    share = 8 if w.name == "decode" else 1
+    shapes = [(B, k) for B in (1, 8, 64, 256) for k in (16, 128)] if w.name == "decode" else [(w.batch, c.k_max)]
+    d, D, S, dk, r = c.d_A, c.D, c.S, c.d_k, c.r
+    N, C = c.N // share, c.C // share
+    lib = _lib.load()
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    pool = torch.empty((N, D), dtype=torch.bfloat16, device=dev)
+    for i in range(0, N, 8192):
+        pool[i:i + 8192].normal_(0.0, d ** -0.5, generator=g)
+    key_proj = (torch.randn((S, D, dk), generator=g, device=dev) * D ** -0.5).to(torch.bfloat16)
+    keys = compute_key_cache(pool, key_proj)
+    del key_proj
+    rows_c = (torch.arange(C, device=dev) * (N // C) +
+              torch.randint(0, N // C, (C,), generator=g, device=dev))
+    cent = keys[:, rows_c].contiguous()
+    W_Q = torch.randn((S, dk, d), generator=g, device=dev) * d ** -0.5
+    aw, tau = torch.zeros(S, device=dev), torch.zeros(1, device=dev)
+    W_base = torch.randn((d, d), generator=g, device=dev) * 0.01
+    b_base = torch.zeros(d, device=dev)
+    gamma = torch.full((1,), c.gamma_init, device=dev)
+    lam = torch.full((1,), 5.0, device=dev)
+    points = []
+    for B, k in shapes:
+        h_A = torch.randn((B, 1, d), generator=g, device=dev).to(torch.bfloat16)
+        z = torch.empty((B, d), dtype=torch.float32, device=dev)
 
-    def one(b):
-        h = h_all[b:b + 1]
-        z = h.mean(axis=1, dtype=np.float32)
-        a, idx, sf = O.retrieve(z, W_Q, aw, np.float32(0.0), cents, keys, k=cfg.k_max, m=cfg.m,
-                                T=cfg.T, lambda_val=w.lambda_val, is_warmup=w.is_warmup,
-                                want_soft_full=w.soft_full)
-        gathered = pool[torch.from_numpy(idx).to(pool.device)].float().cpu().numpy()
-        h_mid, W = O.assemble(gathered, a, h, W_base, b_base, gamma, cfg.d_B, cfg.r, cfg.d_A)
-        if w.backward:
-            O.assemble_bwd(gathered, a, h, W, gamma, g_all[b:b + 1], gW_all[b:b + 1],
-                           cfg.d_B, cfg.r, cfg.d_A)
+        class _Step:
+            comm_events = None
 
-    one(0)  # warm-up
-    times, b = [], 0
-    t0 = time.perf_counter()
-    while not times or (time.perf_counter() - t0 < budget_s and len(times) < w.batch):
-        s = time.perf_counter()
-        one(b % w.batch)
-        times.append(time.perf_counter() - s)
-        b += 1
-    sec_per_seq = float(np.mean(times))
-    return {"value": w.seq / sec_per_seq, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{len(times)} of {w.batch} sequences ({w.seq} tokens each): NumPy float32 "
-                      f"oracle of retrieval.py:48-159 + model.py:193-195 + assemble_jax + "
-                      f"_pallas_assemble_bwd, same key cache and pool rows as the GPU run",
-            "sec_per_sequence": sec_per_seq}
+            def __call__(self):
+                _lib.check(lib.dwa_sequence_mean(runtime.stream_of(dev), B, 1, d, 1, runtime.ptr(h_A),
+                                                 runtime.ptr(z)), "dwa_sequence_mean")
+                al, idx, _ = retrieve(z, W_Q, aw, tau, cent, keys, lam, False, k=k, m=c.m, T=c.T,
+                                      want_soft_full=False)
+                return assemble_apply(pool, al, h_A, W_base, b_base, gamma, d, r, d, row_index=idx)
 
-
-def reference_arm(args, w, rank):
-    """--impl reference: the CPU port timed per step on one sequence per step."""
-    if rank != 0:
-        return
-    import torch
-    dev = torch.device("cuda", 0) if torch.cuda.is_available() else None
-    if dev is None:
-        print(json.dumps({"impl": "reference", "unavailable": "needs the device workload builder"}))
-        return
-    t = build_device_workload(w, dev, args.seed)
-    budget = 150.0
-    cb = cpu_baseline(w, t, budget_s=min(budget, 30.0))
-    sec = cb["sec_per_sequence"]
-    steps = int(min(args.steps, max(1, budget // max(sec, 1e-9))))
-    value = cb["value"]
-    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
-            "n_gpus": args.gpus, "steps": steps, "steps_requested": args.steps,
-            "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": w.name, "note": w.note},
-            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
-            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+        m = measure(_Step(), flush, None, dev, 20, args.warmup, 0, sample_clocks=False)
+        runtime.raise_on_device_status()
+        ms = m["ms_per_step"]
+        pt = {"batch": B, "top_k": k, "ms_per_token_step": ms, "tokens_per_s": B / (ms / 1e3),
+              "kernels_ms": m["breakdown"], "gpu_launches_per_step": m["launches"],
+              "gathered_row_bytes": B * k * D * 2}
+        for name, part in (("factored_hv", r * d), ("factored_out", d * r + d)):
+            if m["breakdown"].get(name):
+                gbs = B * k * part * 2 / (m["breakdown"][name] / 1e3) / 1e9
+                pt[name + "_gbs"] = gbs
+                pt[name + "_frac"] = gbs / float(peaks["hbm_gbs"])
+        points.append(pt)
+    big = points[-1]
+    return {"metric": METRIC, "value": big["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1,
+            "steps": 20, "warmup": max(args.warmup, 3), "ms_per_step": big["ms_per_token_step"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": w.name, "note": w.note,
+                       "this_gpu": (f"one rank's share of {share}: " if share > 1 else "") +
+                                   f"{N} pool rows x {D}, {C} lists, nprobe {c.m}",
+                       "mode": "gate lambda=5.0, no soft_full, h_mid only (dwa_assemble_apply)",
+                       "l2": L2_NOTE, "step": "CUDA graph: seq_mean + dwa_retrieve + dwa_assemble_apply",
+                       "headline": "batch 256, top-k 128"},
+            "peak_hbm_gbs": float(peaks["hbm_gbs"]), "peak_source": peak_src, "sweep": points}
 
 
-# ------------------------------------------------------------------- main ---
+# ======================================================================
+# Main
+# ======================================================================
+def small_dp_line(args, w, dev, group, rank, world, flush, peaks, peak_src, full=True):
+    """The data-parallel small workload (fwd + bwd): every rank its own batch
+    against its own pool replica.  ``full``: also e2e, key cache, extras."""
+    t = build_device_workload(w, dev, args.seed + rank)
+    step = Step(w, t, group)
+    m = measure(step, flush, group, dev, args.steps, args.warmup, rank, sample_clocks=full)
+    tokens = w.batch * w.seq * world
+    res = {"value": tokens / (m["ms_per_step"] / 1e3), "ms_per_step": m["ms_per_step"],
+           "roofline": roofline(w, m, peaks, peak_src), "kernels_ms": m["breakdown"],
+           "kernels_start_ms": m["starts"], "serialized_step_ms": m["serial_ms"],
+           "gpu_launches": m["launches"] * args.steps, "clocks": m["clocks"]}
+    if full and not args.no_e2e:
+        from matrix_b200 import runtime  # noqa: F401
+        ins = [t["h_A"].cpu().pin_memory(), t["g_hmid"].cpu().pin_memory(), t["g_W"].cpu().pin_memory()]
+        keys = ["h_mid", "g_hA", "g_rows", "g_alpha", "g_W_base", "g_b_base", "g_gamma", "alphas", "indices"]
+        ms, h2d, d2h = e2e_pipeline(lambda a, b, c: step(a, b, c), ins, keys, min(args.steps, 50), group, dev)
+        res["e2e"] = {"value": tokens / (ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                      "d2h_bytes_per_step": d2h, "ms_per_step": ms,
+                      "mode": "copies overlapped with compute on two copy streams, double-buffered"}
+    if world == 1 and full:
+        if not args.no_key_cache:
+            res["key_cache"] = time_key_cache(t, flush, peaks)
+        if not args.no_extras:
+            res.update(time_training_extras(w, t, flush, peaks))
+    return res
+
+
 def main():
     args = parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
-    from matrix_b200.config import WORKLOADS
-    w = WORKLOADS[args.workload]
     if args.impl == "reference":
-        return reference_arm(args, w, rank)
+        return reference_arm(args, rank, world)
 
     import torch
     import torch.distributed as dist
+    from matrix_b200.config import WORKLOADS
+    w = WORKLOADS[args.workload]
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     group = None
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
         group = dist.group.WORLD
 
     flush_buf = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
@@ -787,237 +1195,87 @@ def main():
         flush_buf.zero_()
         flush_sink.copy_(flush_buf[: flush_buf.numel() // 2].sum())
 
-    if w.name in ("decode", "decode_profile") and not args.sharded:
-        # the decode pool (2M x 69632, 292 GB) needs 8 GPUs; one GPU runs one rank's share
+    peaks, peak_src = load_peaks()
+    if w.name in ("decode", "decode_profile"):
         if world > 1:
             raise SystemExit("the decode sweep runs on one GPU (one rank's share of the pool)")
-        peaks, peak_src = load_peaks()
         print(json.dumps(decode_sweep(args, w, dev, flush, peaks, peak_src)), flush=True)
         return
 
-    if args.sharded:
-        # a manual mode for the configs whose pool is row-sharded; the driver's
-        # runs use the data-parallel default
-        args.no_e2e = args.no_extras = args.no_key_cache = args.no_cpu_baseline = True
-        if args.emulate_ranks and world > 1:
-            raise SystemExit("--emulate-ranks runs on one GPU")
-        t = build_sharded_workload(w, dev, rank, world, group, args.seed, emulate=args.emulate_ranks)
-        step = ShardedStep(w, t, group, rank, world, emulate=args.emulate_ranks)
-    else:
-        t = build_device_workload(w, dev, args.seed + rank)
-        step = Step(w, t, group)
-
-    from matrix_b200 import _lib
-    step()                       # first call: workspaces, kernel attributes
-    torch.cuda.synchronize()
-    c0 = _lib.launch_counters()[0]
-    step()
-    torch.cuda.synchronize()
-    launches_per_step = _lib.launch_counters()[0] - c0
-
-    breakdown, kstarts = profile_kernels(step, flush)
-    dominant = max(breakdown, key=breakdown.get)
-
-    # capture the step in a CUDA graph, with the dominant kernel's events inside
-    lib = _lib.load()
-    ka, kb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ka.record(); kb.record()     # the library re-records both inside every graph replay
-    torch.cuda.synchronize()
-    lib.dwa_profile_kernel(dominant.encode(), C_ptr(ka), C_ptr(kb))
-    s = torch.cuda.Stream()
-    s.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(s):
-        for _ in range(2):
-            step()
-    torch.cuda.current_stream().wait_stream(s)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        step()
-    lib.dwa_profile_clear()
-
-    for _ in range(max(args.warmup, 3)):
-        flush()
-        graph.replay()
-    torch.cuda.synchronize()
-
-    sampler = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
-                           else local)
-    sampler.start()
-    time.sleep(0.2)
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    stops = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    kern_ms = []
-    kern_src = "graph replay (external event nodes)"
-    if group is not None:
-        dist.barrier()
-    torch.cuda.synchronize()
-    for i in range(args.steps):
-        flush()
-        starts[i].record()
-        graph.replay()
-        stops[i].record()
-        stops[i].synchronize()
-        if kern_src is not None:
-            try:
-                kern_ms.append(ka.elapsed_time(kb))
-            except Exception:  # noqa: BLE001  (no timing on graph-recorded events)
-                kern_src, kern_ms = None, []
-    torch.cuda.synchronize()
-    if group is not None:
-        dist.barrier()
-    clocks = sampler.stop()
-    if kern_src is None:
-        # time the dominant kernel's launches in eager steps, same flush discipline
-        kern_src = "eager steps"
-        ka, kb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ka.record(); kb.record()
-        lib.dwa_profile_kernel(dominant.encode(), C_ptr(ka), C_ptr(kb))
-        for i in range(min(args.steps, 50)):
-            flush()
-            step()
-            torch.cuda.synchronize()
-            kern_ms.append(ka.elapsed_time(kb))
-        lib.dwa_profile_clear()
-    step_ms = float(sum(a.elapsed_time(b) for a, b in zip(starts, stops)))
-    tmax = torch.tensor([step_ms], device=dev, dtype=torch.float64)
-    if group is not None:
-        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
-    total_ms = float(tmax.item())
-    ms_per_step = total_ms / args.steps
-    tokens = w.batch * w.seq
-    if args.emulate_ranks:      # this GPU's sequences: rank 0's share of the batch
-        tokens = w.batch // args.emulate_ranks * w.seq
-    # data parallel: w.batch sequences per rank; row-sharded: w.batch in all
-    value = tokens * (1 if args.sharded else world) / (ms_per_step / 1e3)
-
-    # ---- end to end through the public API with pinned host buffers ----
-    e2e = None
-    if not args.no_e2e:
-        hA_h = t["h_A"].cpu().pin_memory()
-        g_h = t["g_hmid"].cpu().pin_memory()
-        gW_h = t["g_W"].cpu().pin_memory()
-        hA_d, g_d, gW_d = torch.empty_like(t["h_A"]), torch.empty_like(t["g_hmid"]), torch.empty_like(t["g_W"])
-        res_keys = ["h_mid", "g_hA", "g_rows", "g_alpha", "g_W_base", "g_b_base", "g_gamma",
-                    "alphas", "indices"]
-        out = step(hA_d.copy_(hA_h), g_d.copy_(g_h), gW_d.copy_(gW_h))
-        pinned = {k: torch.empty(out[k].shape, dtype=out[k].dtype).pin_memory() for k in res_keys}
-        h2d = hA_h.nbytes + g_h.nbytes + gW_h.nbytes
-        d2h = sum(v.nbytes for v in pinned.values())
-        n_e2e = min(args.steps, 50)
-        # A training loop's input pipeline: step i+1's inputs go up on a copy
-        # stream while step i computes and step i-1's results come down on
-        # another; device inputs and pinned host outputs are double-buffered.
-        # Every step's H2D and D2H is inside the timed region; L2 is not flushed
-        # (the pool and key cache are larger than L2).
-        s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
-        main = torch.cuda.current_stream()
-        bufs = [(hA_d, g_d, gW_d), (torch.empty_like(hA_d), torch.empty_like(g_d), torch.empty_like(gW_d))]
-        pins = [pinned, {k: torch.empty_like(v).pin_memory() for k, v in pinned.items()}]
-        ev_in = [torch.cuda.Event() for _ in range(n_e2e)]
-        ev_used = [torch.cuda.Event() for _ in range(n_e2e)]
-        ev_out = [torch.cuda.Event() for _ in range(n_e2e)]
-        t_start, t_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        ring = [None, None]     # step outputs alive until their copy to the host is done
-        t_start.record(main)
-        s_in.wait_event(t_start)
-        for i in range(n_e2e):
-            bh, bg, bw = bufs[i % 2]
-            with torch.cuda.stream(s_in):
-                if i >= 2:
-                    s_in.wait_event(ev_used[i - 2])      # step i-2 has read this buffer
-                bh.copy_(hA_h, non_blocking=True)
-                bg.copy_(g_h, non_blocking=True)
-                bw.copy_(gW_h, non_blocking=True)
-                ev_in[i].record(s_in)
-            main.wait_event(ev_in[i])
-            if i >= 2:
-                # step i-2's outputs reached the host: release them in stream order
-                main.wait_event(ev_out[i - 2])
-                ring[i % 2] = None
-            out = step(bh, bg, bw)
-            ev_used[i].record(main)
-            with torch.cuda.stream(s_out):
-                s_out.wait_event(ev_used[i])
-                for k in res_keys:
-                    pins[i % 2][k].copy_(out[k], non_blocking=True)
-                ev_out[i].record(s_out)
-            ring[i % 2] = out
-        main.wait_event(ev_out[n_e2e - 1])
-        t_stop.record(main)
-        t_stop.synchronize()
-        e_ms = torch.tensor([t_start.elapsed_time(t_stop) / n_e2e], device=dev, dtype=torch.float64)
+    rows_mode = w.name in ROWS_WORKLOADS or args.sharded or args.emulate_ranks
+    if not rows_mode:
+        r = small_dp_line(args, w, dev, group, rank, world, flush, peaks, peak_src)
+        line = {"metric": METRIC, "value": r.pop("value"), "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": r.pop("ms_per_step"),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic", "config": run_config(w.name, world, False, w=w)}
+        line.update(r)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline and w.name in HOST_WORKLOADS:
+            cb = cpu_baseline(w.name, args.seed, args.cpu_budget_s)
+            line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "threads", "kind", "sample")}
+        if rank == 0:
+            print(json.dumps(line), flush=True)
         if group is not None:
-            dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
-        e2e = {"value": tokens * world / (float(e_ms.item()) / 1e3), "unit": "tokens/s",
-               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-               "ms_per_step": float(e_ms.item()), "steps": n_e2e,
-               "mode": "copies overlapped with compute on two copy streams, double-buffered; "
-                       "no L2 flush (inputs larger than L2)"}
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
-    # ---- roofline of the dominant kernel ----
-    peaks, peak_src = load_peaks()
-    if args.sharded:
-        bound, work = kernel_work(w, dominant, n_rows=t["row_hi"] - t["row_lo"],
-                                  seqs=w.batch // (args.emulate_ranks or world))
-    else:
-        bound, work = kernel_work(w, dominant)
-    kms = float(np.mean(kern_ms))
-    roof = None
-    if work is not None:
-        if bound == "hbm":
-            ach = work / (kms / 1e3) / 1e9
-            peak = float(peaks["hbm_gbs"])
-            unit = "GB/s"
-        else:
-            ach = work / (kms / 1e3) / 1e12
-            peak = float(peaks["bf16_tflops"])
-            unit = "TFLOP/s"
-        traffic = None if args.sharded else profiled_traffic(dominant, w)
-        roof = {"kernel": dominant, "bound": bound, "achieved": ach, "peak": peak, "unit": unit,
-                "frac": ach / peak, "traffic": traffic, "peak_source": peak_src,
-                "algorithmic_per_launch": work, "launch_ms": kms, "timed_in": kern_src}
-
-    if args.sharded:
-        step_desc = ("CUDA graph: seq_mean + all-gather of z + dwa_retrieve_local + all-gather of summaries + "
-                     "dwa_retrieve_merge + dwa_gather_rows (peer loads) + dwa_assemble_fwd"
-                     + (" + dwa_assemble_bwd + pool-row gradient all-gather and scatter + NCCL all_reduce of "
-                        "parameter grads" if w.backward else ""))
-    else:
-        step_desc = ("CUDA graph: seq_mean + dwa_retrieve + dwa_assemble_fwd + dwa_assemble_bwd"
-                     + (" + NCCL all_reduce of parameter grads" if world > 1 else ""))
+    # ---------------- row-sharded pool (the default) ----------------
+    if args.emulate_ranks and world > 1:
+        raise SystemExit("--emulate-ranks runs on one GPU")
+    emulate = args.emulate_ranks
+    t = build_sharded_workload(w, dev, rank, world, group, args.seed, emulate=emulate)
+    step = ShardedStep(w, t, group, rank, world, emulate=emulate)
+    m = measure(step, flush, group, dev, args.steps, args.warmup, rank)
+    Bp = w.batch // (emulate or world)
+    n_loc = t["row_hi"] - t["row_lo"]
+    tokens = (Bp if emulate else w.batch) * w.seq
+    value = tokens / (m["ms_per_step"] / 1e3)
+    roof = roofline(w, m, peaks, peak_src, n_rows=n_loc, seqs=Bp, queries=w.batch)
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "strong" if args.sharded else "weak", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": w.name, "note": w.note,
-                       "global_batch": w.batch if args.sharded else w.batch * world,
-                       "seq_len": w.seq, "parallelism": f"rows{world}" if args.sharded else f"dp{world}",
-                       "mode": "warmup" if w.is_warmup else f"gate lambda={w.lambda_val}",
-                       "soft_full": w.soft_full, "backward": w.backward,
-                       "l2": "flushed between steps (512 MB write, then 256 MB read)",
-                       "step": step_desc},
-            "value_per_gpu": value / world, "roofline": roof,
-            "kernels_ms": breakdown, "kernels_start_ms": kstarts, "gpu_launches": int(launches_per_step * args.steps),
-            "clocks": clocks, "e2e": e2e}
-    if args.emulate_ranks:
-        P = args.emulate_ranks
-        line["config"]["parallelism"] = f"rows{P}, one rank emulated on one GPU"
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": m["ms_per_step"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": run_config(w.name, world, True, emulate, w=w),
+            "value_per_gpu": value / (1 if emulate else world), "roofline": roof,
+            "kernels_ms": m["breakdown"], "kernels_start_ms": m["starts"], "serialized_step_ms": m["serial_ms"],
+            "gpu_launches": m["launches"] * args.steps, "clocks": m["clocks"],
+            "rows_per_rank": n_loc, "seqs_per_rank": Bp}
+    if group is not None:
+        every = [None] * world
+        dist.all_gather_object(every, {"ms_per_step": m["rank_ms_per_step"], "kernels_ms": m["breakdown"],
+                                       "rows": n_loc}, group=group)
+        line["per_rank"] = every
+    if emulate:
         line["config"]["emulated"] = (
-            f"rank {t['rank']} of {P} (the most rows): pool rows [{t['row_lo']}, {t['row_hi']}) of {w.cfg.N} (whole lists), retrieval of "
-            f"all {w.batch} queries over them, assembly of its {w.batch // P} sequences; the all-gathers, the "
-            f"merge across ranks, peer reads and the row-gradient exchange are not in it")
-        line["value_per_gpu"] = value
-    if world == 1 and not args.no_key_cache:
-        line["key_cache"] = time_key_cache(t, flush, peaks)
-    if world == 1 and not args.no_extras:
-        line.update(time_training_extras(w, t, flush, peaks))
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cb = cpu_baseline(w, t, args.cpu_budget_s)
-        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            f"rank {t['rank']} of {emulate} (the most rows): pool rows [{t['row_lo']}, {t['row_hi']}) of "
+            f"{w.cfg.N} (whole lists), retrieval of all {w.batch} queries over them, assembly of its {Bp} "
+            f"sequences; the all-gathers, the merge across ranks, peer reads and the row-gradient exchange are "
+            f"not in it")
+    if not args.no_parity and not emulate:
+        line["parity"] = rows_parity(w, t, step, group, rank, world)
+    if not args.no_e2e and not emulate and not w.backward:
+        hA_h = t["h_A"].cpu().pin_memory()
+        ms, h2d, d2h = e2e_pipeline(lambda a: step(a), [hA_h], ["h_mid", "alphas", "indices"],
+                                    min(args.steps, 20), group, dev)
+        line["e2e"] = {"value": tokens / (ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d * world,
+                       "d2h_bytes_per_step": d2h * world, "ms_per_step": ms,
+                       "mode": "every rank copies its sequences' h_A up and their h_mid, alphas and indices "
+                               "down each step (bytes summed over ranks); copies overlapped with compute on "
+                               "two copy streams, double-buffered"}
+    from matrix_b200 import runtime
+    runtime.raise_on_device_status()
+    del step
+    t.clear()
+    torch.cuda.empty_cache()
+    if world == 1 and not emulate and not args.no_small and w.name != "small":
+        sm = small_dp_line(args, WORKLOADS["small"], dev, None, 0, 1, flush, peaks, peak_src)
+        sm["config"] = run_config("small", 1, False)
+        line["small_fwd_bwd"] = sm
+    if rank == 0 and world == 1 and not emulate and not args.no_cpu_baseline and w.name in HOST_WORKLOADS:
+        cb = cpu_baseline(w.name, args.seed, args.cpu_budget_s)
+        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "threads", "kind", "sample")}
     if rank == 0:
         print(json.dumps(line), flush=True)
-    del graph
     if group is not None:
         dist.barrier()
         dist.destroy_process_group()

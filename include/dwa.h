@@ -116,6 +116,14 @@ DWA_API void dwa_launch_counters(uint64_t* total, uint64_t* tensor_core_gemms, u
 DWA_API int  dwa_profile_kernel(const char* kernel, void* start_event, void* stop_event);
 DWA_API void dwa_profile_clear(void);
 
+/* Profiling control: with on != 0, launches that follow use no programmatic
+ * dependent launch and the calls' concurrent lanes collapse onto the caller's
+ * stream, so each kernel runs alone and the event pairs of dwa_profile_kernel
+ * add up to the step.  Off by default; affects launches (and graph captures)
+ * made while it is set.  Not thread-scoped: set it only around a profiling
+ * pass. */
+DWA_API void dwa_profile_serialize(int on);
+
 /* z[b,:] = mean over t of h_A[b,t,:] in float32 (the retrieval query of
  * src/dwa/model.py:171).  h_A [B,T,d] in dtype; z [B,d] f32. */
 DWA_API int dwa_sequence_mean(void* stream, int B, int T, int d, int dtype, const void* h_A,

@@ -80,6 +80,7 @@ _SIGNATURES = {
     "dwa_launch_counters": (None, [C.POINTER(C.c_uint64)] * 3),
     "dwa_profile_kernel": (C.c_int, [C.c_char_p, _P, _P]),
     "dwa_profile_clear": (None, []),
+    "dwa_profile_serialize": (None, [C.c_int]),
     "dwa_sequence_mean": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int, _P, _P]),
     "dwa_assemble_workspace_bytes": (C.c_size_t, [C.POINTER(AssembleDims), C.c_int]),
     "dwa_assemble_fwd": (C.c_int, [_P, C.POINTER(AssembleDims), _P, _P, _P, _P, _P, _P, _P,

@@ -13,12 +13,19 @@ namespace dwa {
 
 std::atomic<uint64_t> g_launches_total{0}, g_launches_tc{0}, g_launches_simt{0};
 
+// Serialised launches (dwa_profile_serialize): no programmatic dependent
+// launch and no concurrent lanes, so that an event pair around one kernel
+// measures that kernel alone and per-kernel times add up to the step.
+static std::atomic<int> g_serialize{0};
+
+bool serialized() { return g_serialize.load(std::memory_order_relaxed) != 0; }
+
 bool pdl_enabled() {
     static const bool on = [] {
         const char* v = std::getenv("DWA_PDL");
         return !(v && std::strcmp(v, "0") == 0);
     }();
-    return on;
+    return on && !serialized();
 }
 
 static thread_local std::string t_last_error;
@@ -93,9 +100,13 @@ Lanes::Lanes(cudaStream_t st) : main(st) {
         }
         L.ready = true;
     }
+    for (int i = 0; i < 8; ++i) ev[i] = L.ev[i];
+    if (serialized()) {   // every lane is the main stream: kernels run one after another
+        aux[0] = aux[1] = main;
+        return;
+    }
     aux[0] = L.aux[0];
     aux[1] = L.aux[1];
-    for (int i = 0; i < 8; ++i) ev[i] = L.ev[i];
     if ((rc = depend(aux[0], main, 0))) return;
     rc = depend(aux[1], main, 0);
 }
@@ -105,6 +116,7 @@ Lanes::~Lanes() {
 }
 
 int Lanes::depend(cudaStream_t to, cudaStream_t from, int slot) {
+    if (to == from) return DWA_OK;
     if (cudaEventRecord(ev[slot], from) != cudaSuccess || cudaStreamWaitEvent(to, ev[slot], 0) != cudaSuccess)
         return fail(DWA_ERR_CUDA, "Lanes: event record/wait failed");
     return DWA_OK;
@@ -222,6 +234,8 @@ extern "C" void dwa_launch_counters(uint64_t* total, uint64_t* tensor_core_gemms
     if (tensor_core_gemms) *tensor_core_gemms = dwa::g_launches_tc.load();
     if (simt_gemms) *simt_gemms = dwa::g_launches_simt.load();
 }
+
+extern "C" void dwa_profile_serialize(int on) { dwa::g_serialize.store(on ? 1 : 0); }
 
 extern "C" int dwa_profile_kernel(const char* kernel, void* start_event, void* stop_event) {
     if (!kernel || std::strlen(kernel) >= sizeof(dwa::ProfEntry::name))

@@ -48,6 +48,7 @@ __device__ __forceinline__ void pdl_enter() {
 }
 
 bool pdl_enabled();
+bool serialized();   // dwa_profile_serialize is on
 
 // Split cluster barrier: arrive early, wait just before the first access to
 // another CTA's shared memory (every CTA of the cluster has then started).

@@ -128,7 +128,7 @@ def fine_scores(q_norm, w, pool_keys, cand):
 def full_scores(q_norm, w, pool_keys):
     """``s_full[b,n]`` over every pool row (retrieval.py:114-118, 123-125)."""
     p_norm = l2_normalize(pool_keys)
-    sim_all = np.einsum("bsk,snk->bsn", q_norm, p_norm)
+    sim_all = np.einsum("bsk,snk->bsn", q_norm, p_norm, optimize=True)
     return np.einsum("s,bsn->bn", w, sim_all)
 
 
@@ -567,8 +567,8 @@ def assemble_bwd(gathered, alphas, h_A, W, gamma, g_hmid, g_W_out, d_B, r, d_A,
     g_gamma = np.sum(g_hmid * h_res)                                   # :275
     g_bias = g_hmid.sum(axis=1)                                        # :276
     g_h_res = gamma * g_hmid                                           # :277
-    g_W_hres = np.einsum("btj,bti->bji", g_h_res, h_A)                 # :281
-    g_hA_hres = np.einsum("btj,bji->bti", g_h_res, W)                  # :283
+    g_W_hres = np.einsum("btj,bti->bji", g_h_res, h_A, optimize=True)  # :281
+    g_hA_hres = np.einsum("btj,bji->bti", g_h_res, W, optimize=True)   # :283
     g_hA = g_hmid + g_hA_hres                                          # :285
     g_W_total = g_W_hres + g_W_out                                     # :288
     g_W_base = g_W_total.sum(0)                                        # :289
@@ -580,7 +580,7 @@ def assemble_bwd(gathered, alphas, h_A, W, gamma, g_hmid, g_W_out, d_B, r, d_A,
         nb = b1 - b0
         UV = np.matmul(U[b0:b1].reshape(nb * k, d_B, r),
                        V[b0:b1].reshape(nb * k, r, d_A)).reshape(nb, k, d_B, d_A)  # :293-295
-        g_alpha_dW[b0:b1] = np.einsum("bkji,bji->bk", UV, g_delta_W[b0:b1])    # :298
+        g_alpha_dW[b0:b1] = np.einsum("bkji,bji->bk", UV, g_delta_W[b0:b1], optimize=True)  # :298
     g_U = alphas[:, :, None, None] * np.matmul(g_delta_W[:, None, :, :],
                                                V.transpose(0, 1, 3, 2))          # :303-305
     g_V = alphas[:, :, None, None] * np.matmul(U.transpose(0, 1, 3, 2),
