@@ -129,6 +129,28 @@ int Lanes::join() {
 
 namespace tc {
 
+// Streaming multiprocessors of the current device (cached per device).
+int sm_count() {
+    static int cache[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!cache[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
+// DWA_GEMM=classic selects the one-tile-per-CTA GEMM instead of the persistent one.
+bool persistent_gemm() {
+    static const bool on = [] {
+        const char* v = std::getenv("DWA_GEMM");
+        return !(v && std::strcmp(v, "classic") == 0);
+    }();
+    return on;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;

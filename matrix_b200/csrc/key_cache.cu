@@ -22,6 +22,8 @@
 #include <atomic>
 #include <cstdlib>
 
+#include <cstring>
+
 #include "dwa_common.cuh"
 #include "epilogue.cuh"
 #include "simt_gemm.cuh"
@@ -147,13 +149,16 @@ extern "C" int dwa_key_cache(void* stream, const DwaKeyCacheDims* dims, const vo
     epi.keys = keys;
     epi.N = d.N;
     epi.d_k = d.d_k;
-    if (d.dtype == DWA_BF16 && std::getenv("DWA_GEMM") == nullptr) {
+    const char* gsel = std::getenv("DWA_GEMM");
+    if (d.dtype == DWA_BF16 && !(gsel && std::strcmp(gsel, "simt") == 0)) {
+        const bool pers = tc::persistent_gemm();
         const tc::Operand A{pool_vectors, false, K, 0}, B{bt, false, K, 0};
         const int64_t ctas256 = static_cast<int64_t>((M + 127) / 128) * ((Ng + 255) / 256);
         if (Ng >= 256 && ctas256 >= 120 && tc::tc_operand_ok(A, M, K, 128) && tc::tc_operand_ok(B, Ng, K, 256)) {
             ++g_launches_tc;
             prof_begin("key_cache", st);
-            rc = tc::launch_gemm_bf16<256, 4, false, false>(A, B, M, Ng, K, 1, epi, status, st);
+            rc = pers ? tc::launch_gemm_bf16_persistent<256, 3, false, false>(A, B, M, Ng, K, 1, epi, status, st)
+                      : tc::launch_gemm_bf16<256, 4, false, false>(A, B, M, Ng, K, 1, epi, status, st);
             prof_end("key_cache", st);
             ++g_launches_total;
             return rc;
@@ -161,7 +166,8 @@ extern "C" int dwa_key_cache(void* stream, const DwaKeyCacheDims* dims, const vo
         if (Ng >= 128 && tc::tc_operand_ok(A, M, K, 128) && tc::tc_operand_ok(B, Ng, K, 128)) {
             ++g_launches_tc;
             prof_begin("key_cache", st);
-            rc = tc::launch_gemm_bf16<128, 6, false, false>(A, B, M, Ng, K, 1, epi, status, st);
+            rc = pers ? tc::launch_gemm_bf16_persistent<128, 4, false, false>(A, B, M, Ng, K, 1, epi, status, st)
+                      : tc::launch_gemm_bf16<128, 6, false, false>(A, B, M, Ng, K, 1, epi, status, st);
             prof_end("key_cache", st);
             ++g_launches_total;
             return rc;

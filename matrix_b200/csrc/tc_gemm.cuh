@@ -60,6 +60,10 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                  : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -393,6 +397,249 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), EW == 8 ? 2 : 1)
     }
 }
 
+// --------------------------------------------------- persistent variant ---
+// One CTA per SM loops over the output tiles (tile t = blockIdx.x + i *
+// gridDim.x, column block fastest, then row block, then batch item, so the
+// CTAs running at once share their operands in L2).  Two TMEM accumulators
+// (2 x BN columns): while the epilogue warps drain tile i from one, the MMA
+// warp accumulates tile i+1 into the other, and the producer keeps the TMA
+// ring full across tile boundaries.  The epilogue stages half a tile (BN/2
+// columns) at a time in its own shared buffer, so the ring stays in use.
+//   acc_full[buf]   MMA commit: tile accumulated in buffer buf
+//   acc_empty[buf]  one arrive per epilogue warp: buffer buf read out
+template <int BN, int STAGES>
+struct PSmem {
+    static constexpr int HB = BN / 2 < 128 ? BN : BN / 2;   // columns staged per epilogue pass
+    static constexpr uint32_t A_STAGE = BM * BK * 2;
+    static constexpr uint32_t B_STAGE = BN * BK * 2;
+    static constexpr uint32_t RING = STAGES * (A_STAGE + B_STAGE);
+    static constexpr uint32_t STAGE_LD = HB + 4;             // floats per staged row
+    static constexpr uint32_t EPI_OFF = RING;
+    static constexpr uint32_t BAR_OFF = EPI_OFF + BM * STAGE_LD * 4;
+    static constexpr uint32_t NBAR = 2 * STAGES + 5;        // full, empty, acc_full[2], acc_empty[2], drain
+    static constexpr uint32_t BYTES = 1024 + BAR_OFF + NBAR * 8 + 16;
+    static_assert(BYTES <= 227 * 1024, "persistent GEMM shared memory above the per-CTA limit");
+};
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EW = kEpiWarps>
+__global__ void __launch_bounds__(gemm_threads<EW>(), 1)
+    gemm_bf16_persistent(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                         int M, int N, int K, int batch, int a_batched, int b_batched, Epi epi,
+                         uint32_t* status) {
+    using L = PSmem<BN, STAGES>;
+    constexpr int HB = L::HB;
+    constexpr int NH = BN / HB;                 // epilogue passes per tile
+    constexpr uint32_t TMEM_COLS = 2 * BN;
+    extern __shared__ uint8_t dyn_smem[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * L::A_STAGE;
+    float* stage_tile = reinterpret_cast<float*>(smem + L::EPI_OFF);
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+    uint64_t* empty_bar = full_bar + STAGES;
+    uint64_t* acc_full = empty_bar + STAGES;
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* drain_bar = acc_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+    __shared__ float s_red[EW];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles_n = (N + BN - 1) / BN, tiles_m = (M + BM - 1) / BM;
+    const int tiles = tiles_n * tiles_m * batch;
+    const int nkb = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], EW);
+        }
+        mbar_init(drain_bar, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, TMEM_COLS);
+        tmem_relinquish();
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    pdl_enter();   // operands and epilogue inputs come from earlier kernels
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                const int n0 = (t % tiles_n) * BN, m0 = ((t / tiles_n) % tiles_m) * BM;
+                const int bz = t / (tiles_n * tiles_m);
+                const int za = a_batched ? bz : 0, zb = b_batched ? bz : 0;
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    if (it >= STAGES && !mbar_wait_bounded(&empty_bar[s], ((it / STAGES) - 1) & 1)) {
+                        raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full_bar[s], L::A_STAGE + L::B_STAGE);
+                    const int k0 = kb * BK;
+                    uint8_t* a = sA + s * L::A_STAGE;
+                    uint8_t* b = sB + s * L::B_STAGE;
+                    if (A_MN) {
+#pragma unroll
+                        for (int h = 0; h < BM / 64; ++h)
+                            tma_load_3d(a + h * 8192, &tmA, &full_bar[s], m0 + 64 * h, k0, za);
+                    } else {
+                        tma_load_3d(a, &tmA, &full_bar[s], k0, m0, za);
+                    }
+                    if (B_MN) {
+#pragma unroll
+                        for (int h = 0; h < BN / 64; ++h)
+                            tma_load_3d(b + h * 8192, &tmB, &full_bar[s], n0 + 64 * h, k0, zb);
+                    } else {
+                        tma_load_3d(b, &tmB, &full_bar[s], k0, n0, zb);
+                    }
+                }
+            }
+            // every issued copy must have landed before the CTA may exit
+            for (int i = (it > STAGES ? it - STAGES : 0); i < it; ++i)
+                if (!mbar_wait_bounded(&full_bar[i % STAGES], (i / STAGES) & 1)) {
+                    raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
+                    break;
+                }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = instr_desc_bf16<BN, A_MN, B_MN>();
+            int it = 0, li = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++li) {
+                const int buf = li & 1;
+                if (li >= 2 && !mbar_wait_bounded(&acc_empty[buf], ((li >> 1) - 1) & 1)) {
+                    raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + static_cast<uint32_t>(buf * BN);
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    if (!mbar_wait_bounded(&full_bar[s], (it / STAGES) & 1)) {
+                        raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_base = smem_u32(sA + s * L::A_STAGE);
+                    const uint32_t b_base = smem_u32(sB + s * L::B_STAGE);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        mma_bf16_ss(d_tmem, operand_desc<A_MN>(a_base, kk), operand_desc<B_MN>(b_base, kk),
+                                    idesc, (kb | kk) != 0 ? 1u : 0u);
+                    mma_commit(&empty_bar[s]);
+                }
+                if (ok) mma_commit(&acc_full[buf]);
+            }
+            // every MMA this thread issued has completed before TMEM is released
+            mma_commit(drain_bar);
+            if (!mbar_wait_bounded(drain_bar, 0)) raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
+        }
+        __syncwarp();
+    } else {
+        const int q = warp & 3;        // TMEM lane quarter this warp may read
+        const int e = warp - 2;        // epilogue warp 0..EW-1
+        const int grp = e >> 2;        // column group 0..EW/4-1
+        constexpr int LD = L::STAGE_LD;
+        constexpr int LPR = HB / 8, RPW = 32 / LPR, PF = 4;
+        constexpr int STEP = EW * RPW;
+        const int sub = lane / LPR, lic = lane % LPR;
+        int li = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++li) {
+            const int n0 = (t % tiles_n) * BN, m0 = ((t / tiles_n) % tiles_m) * BM;
+            const int bz = t / (tiles_n * tiles_m);
+            const int buf = li & 1;
+            const bool ok = mbar_wait_bounded(&acc_full[buf], (li >> 1) & 1);
+            if (!ok) {
+                if (lane == 0) raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
+                break;
+            }
+            tc_fence_after();
+            float cta_acc = 0.f;
+#pragma unroll 1
+            for (int h = 0; h < NH; ++h) {
+                asm volatile("bar.sync 1, %0;" ::"n"(32 * EW) : "memory");   // staging buffer free
+                const int r_local = q * 32 + lane;
+                for (int c = grp; c < HB / 32; c += EW / 4) {
+                    if (n0 + h * HB + c * 32 >= N) break;
+                    float v[32];
+                    tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) +
+                                  static_cast<uint32_t>(buf * BN + h * HB + c * 32), v);
+                    float4* dst = reinterpret_cast<float4*>(stage_tile + r_local * LD + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                }
+                if (h == NH - 1) {             // accumulator read out: the MMA may reuse it
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[buf]);
+                }
+                asm volatile("bar.sync 1, %0;" ::"n"(32 * EW) : "memory");   // staging buffer full
+                const int col0 = n0 + h * HB + lic * 8;
+                const int cnt = min(8, N - col0);
+                for (int base = e * RPW + sub; base < BM; base += STEP * PF) {
+                    typename Epi::Frag frag[PF];
+#pragma unroll
+                    for (int u = 0; u < PF; ++u) {
+                        const int rr = base + u * STEP, row = m0 + rr;
+                        if (rr < BM && row < M && cnt > 0) epi.load(bz, row, col0, cnt, frag[u]);
+                    }
+#pragma unroll
+                    for (int u = 0; u < PF; ++u) {
+                        const int rr = base + u * STEP, row = m0 + rr;
+                        float part = 0.f;
+                        if (rr < BM && row < M && cnt > 0) {
+                            const float4* src = reinterpret_cast<const float4*>(stage_tile + rr * LD + lic * 8);
+                            const float4 a = src[0], b = src[1];
+                            const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+                            part = epi.finish(bz, row, col0, v, cnt, frag[u]);
+                        }
+                        if (Epi::kReduce == 1) {
+#pragma unroll
+                            for (int o = LPR / 2; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+                            if (lic == 0 && rr < BM && row < M) epi.row_done(bz, row, part);
+                        } else if (Epi::kReduce == 2) {
+                            cta_acc += part;
+                        }
+                    }
+                }
+            }
+            if (Epi::kReduce == 2) {
+                cta_acc = warp_sum(cta_acc);
+                if (lane == 0) s_red[e] = cta_acc;
+                asm volatile("bar.sync 1, %0;" ::"n"(32 * EW) : "memory");
+                if (e == 0 && lane == 0) {
+                    float tsum = 0.f;
+                    for (int i = 0; i < EW; ++i) tsum += s_red[i];
+                    epi.cta_done(bz, tsum);
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
 // ------------------------------------------------------------------ host ---
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
@@ -429,6 +676,37 @@ int launch_gemm_bf16(const Operand& A, const Operand& B, int M, int N, int K, in
     launch_pdl(kern, grid, gemm_threads<EW>(), L::BYTES, stream, ta, tb, M, N, K, A.bstride != 0, B.bstride != 0,
                                                    epi, status);
     DWA_LAUNCH_CHECK("gemm_bf16_kernel");
+    return DWA_OK;
+}
+
+
+int sm_count();
+bool persistent_gemm();
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EW = kEpiWarps>
+int launch_gemm_bf16_persistent(const Operand& A, const Operand& B, int M, int N, int K, int batch,
+                                const Epi& epi, uint32_t* status, cudaStream_t stream) {
+    static_assert(BN == 128 || BN == 256, "persistent GEMM: BN 128 or 256");
+    CUtensorMap ta, tb;
+    std::string why;
+    if (!make_operand_map(&ta, A, M, K, batch, BM, &why) ||
+        !make_operand_map(&tb, B, N, K, batch, BN, &why))
+        return fail(DWA_ERR_INVALID_ARG, "tensor map: " + why);
+    using L = PSmem<BN, STAGES>;
+    auto kern = gemm_bf16_persistent<BN, STAGES, A_MN, B_MN, Epi, EW>;
+    static bool attr_set[64] = {};  // per instantiation and device
+    int dev = 0;
+    DWA_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        DWA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(L::BYTES)));
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+    const int64_t tiles = static_cast<int64_t>((N + BN - 1) / BN) * ((M + BM - 1) / BM) * batch;
+    const int grid = static_cast<int>(std::min<int64_t>(tiles, sm_count()));
+    launch_pdl(kern, dim3(grid), gemm_threads<EW>(), L::BYTES, stream, ta, tb, M, N, K, batch,
+               A.bstride != 0, B.bstride != 0, epi, status);
+    DWA_LAUNCH_CHECK("gemm_bf16_persistent");
     return DWA_OK;
 }
 

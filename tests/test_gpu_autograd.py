@@ -40,7 +40,7 @@ def _grads(fn, cfg, x, idx, alphas):
     loss = (h_mid.float() * _dev(x.g_hmid, act).float()).sum() + (W * _dev(x.g_W)).sum()
     loss.backward()
     torch.cuda.synchronize()
-    return h_mid, W, [t.grad for t in leaves]
+    return h_mid.detach(), W.detach(), [t.grad for t in leaves]
 
 
 @pytest.mark.parametrize("name", ["f32_ragged", "bf16_tc", "bf16_small_like"])
