@@ -421,6 +421,21 @@ struct PSmem {
     static_assert(BYTES <= 227 * 1024, "persistent GEMM shared memory above the per-CTA limit");
 };
 
+// True on every epilogue thread when `ok` holds on all of them (named barrier 1).
+template <int EW>
+__device__ __forceinline__ bool epi_all(bool ok) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.and.pred p, 1, %2, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(ok)), "n"(32 * EW)
+        : "memory");
+    return r != 0;
+}
+
 template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EW = kEpiWarps>
 __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
     gemm_bf16_persistent(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -566,7 +581,9 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
             const int bz = t / (tiles_n * tiles_m);
             const int buf = li & 1;
             const bool ok = mbar_wait_bounded(&acc_full[buf], (li >> 1) & 1);
-            if (!ok) {
+            // every epilogue thread leaves together, or none does (the named
+            // barriers below must be reached by all of them)
+            if (!epi_all<EW>(ok)) {
                 if (lane == 0) raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
                 break;
             }
