@@ -109,7 +109,8 @@ def step_description(name, rows_mode, world, backward, emulate=0):
              "dwa_retrieve_local + " + ("all-gather of summaries + " if world > 1 else "") +
              "dwa_retrieve_merge + " + gather + " + dwa_assemble_fwd")
         if backward:
-            s += (" + dwa_assemble_bwd + pool-row gradient exchange and scatter" +
+            s += (" + dwa_assemble_bwd + pool-row gradients to their owners (peer stores of bf16 rows) and "
+                  "scatter" +
                   (" + NCCL all_reduce of parameter grads" if world > 1 else ""))
         return s
     return ("CUDA graph: seq_mean + dwa_retrieve + dwa_assemble_fwd" + (" + dwa_assemble_bwd" if backward else "")
@@ -466,6 +467,10 @@ class ShardedStep:
         elif world > 1:
             bounds = [t["bounds"][0][0]] + [h for _, h in t["bounds"]]
             self.peers = PeerPool(t["pool"], bounds, group)
+        self.exchange = None
+        if w.backward and world > 1 and not emulate:
+            from matrix_b200.pool_grad import PoolGradExchange
+            self.exchange = PoolGradExchange(bounds, Bp * w.cfg.k_max, w.cfg.D, dev, group)
 
     def __call__(self, h_A=None):
         from matrix_b200 import _lib, runtime
@@ -514,8 +519,11 @@ class ShardedStep:
                                   cfg.d_B, cfg.r, cfg.d_A, row_index=row_index)
             out.update(zip(("g_rows", "g_alpha", "g_hA", "g_W_base", "g_b_base", "g_gamma"), g))
             with comm_timer(self.comm_events, "rowgrad_exchange"):
-                scatter_pool_grad_gathered(g[0], idx_mine, t["g_pool"], row_lo=t["row_lo"], n_global=cfg.N,
-                                           group=self.group if self.world > 1 else None)
+                if self.exchange is not None:     # bf16 rows stored into their owners' receive areas
+                    self.exchange(g[0], idx_mine, t["g_pool"])
+                else:
+                    scatter_pool_grad_gathered(g[0], idx_mine, t["g_pool"], row_lo=t["row_lo"], n_global=cfg.N,
+                                               group=None)
             if self.world > 1:
                 import torch
                 import torch.distributed as dist

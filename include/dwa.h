@@ -466,9 +466,45 @@ DWA_API int dwa_rmsnorm_bwd(void* stream, int64_t rows, int d, int x_dtype, int 
  * ------------------------------------------------------------------------- */
 DWA_API size_t dwa_pool_grad_scatter_workspace_bytes(int n);
 
+/* Index value of an empty slot: skipped by the scatter without a status bit. */
+#define DWA_PAD_INDEX (-2147483647 - 1)
+
 DWA_API int dwa_pool_grad_scatter(void* stream, int n, int D, const int32_t* indices, const float* g_rows,
                                   int64_t n_global, int64_t row_lo, int64_t row_hi, int g_dtype,
                                   void* g_pool, void* workspace, size_t workspace_bytes);
+
+/* The same scatter with the contributions in rows_dtype (DWA_F32 or DWA_BF16),
+ * e.g. the bf16 rows a receive area of dwa_pool_grad_send holds. */
+DWA_API int dwa_pool_grad_scatter_typed(void* stream, int n, int D, const int32_t* indices, int rows_dtype,
+                                        const void* g_rows, int64_t n_global, int64_t row_lo, int64_t row_hi,
+                                        int g_dtype, void* g_pool, void* workspace, size_t workspace_bytes);
+
+/* ---------------------------------------------------------------------------
+ * Returning row gradients to the ranks that own the rows (row-sharded pool).
+ * Replaces the transpose of _distributed_gather (src/dwa/model.py:16-47), whose
+ * autodiff reduces a dense [B,k,D] cotangent over the model axis, and the
+ * all-gather of every rank's rows: rank `rank` stores each of its n <= slot
+ * contributions (g_rows [n, D] f32, pool rows indices [n]) straight into the
+ * receive area of the rank that owns the row, converted to rows_dtype (bf16,
+ * the pool's dtype, halves the bytes that cross NVLink).
+ *  - recv: bases[q] = rank q's receive area mapped on this GPU (CUDA IPC;
+ *    dwa_pool_grad_recv_bytes each, 256-byte aligned), row_lo = the owners' row
+ *    bounds; world * slot <= 8192.
+ *  - Area layout: idx [world * slot] int32 (padded to 256 bytes), then rows
+ *    [world * slot, D].  Slot rank * slot + i holds contribution i of `rank`;
+ *    the slots of rows owned elsewhere, and slots i >= n, hold DWA_PAD_INDEX.
+ *  - After every rank's send, a collective (any; it orders the stores before
+ *    the reads), then each owner calls dwa_pool_grad_scatter_typed on its own
+ *    area (n = world * slot, rows_dtype) into its rows [row_lo, row_hi).
+ *  - An area is overwritten by the next send into it: alternate two areas
+ *    between calls, so that a rank one call ahead never writes into an area
+ *    its owner is still reading.
+ *  - Indices outside every owner set DWA_STATUS_BAD_ROW_INDEX (workspace).
+ * ------------------------------------------------------------------------- */
+DWA_API size_t dwa_pool_grad_recv_bytes(int world, int slot, int64_t D, int rows_dtype);
+DWA_API int dwa_pool_grad_send(void* stream, int rank, int n, int slot, int64_t D, const int32_t* indices,
+                               const float* g_rows, int rows_dtype, const DwaPoolShards* recv, void* workspace,
+                               size_t workspace_bytes);
 
 /* ---------------------------------------------------------------------------
  * Retrieval without a workspace.  No counterpart in the reference: it exists for

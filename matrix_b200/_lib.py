@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(HERE, "libdwa.so")
 
 DWA_OK = 0
 DWA_ERR_DEVICE = -5
+DWA_PAD_INDEX = -(2 ** 31)
 DWA_F32 = 0
 DWA_BF16 = 1
 
@@ -105,6 +106,11 @@ _SIGNATURES = {
     "dwa_pool_grad_scatter_workspace_bytes": (C.c_size_t, [C.c_int]),
     "dwa_pool_grad_scatter": (C.c_int, [_P, C.c_int, C.c_int, _P, _P, C.c_int64, C.c_int64, C.c_int64,
                                         C.c_int, _P, _P, C.c_size_t]),
+    "dwa_pool_grad_scatter_typed": (C.c_int, [_P, C.c_int, C.c_int, _P, C.c_int, _P, C.c_int64, C.c_int64,
+                                              C.c_int64, C.c_int, _P, _P, C.c_size_t]),
+    "dwa_pool_grad_recv_bytes": (C.c_size_t, [C.c_int, C.c_int, C.c_int64, C.c_int]),
+    "dwa_pool_grad_send": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int64, _P, _P, C.c_int,
+                                     C.POINTER(PoolShards), _P, C.c_size_t]),
     "dwa_rmsnorm_bwd": (C.c_int, [_P, C.c_int64, C.c_int, C.c_int, C.c_int, _P, _P, _P, _P, _P, _P, _P,
                                   C.c_size_t]),
     "dwa_key_cache": (C.c_int, [_P, C.POINTER(KeyCacheDims), _P, _P, _P, _P, C.c_size_t]),

@@ -729,12 +729,13 @@ static int gemm(const char* name, const void* a, int64_t lda, int64_t bsa, const
             return rc;
         }
         const int64_t ctas256 = static_cast<int64_t>((M + 127) / 128) * ((N + 255) / 256) * batch;
-        const bool pers = tc::persistent_gemm();
+        // persistent only when CTAs get several tiles (a single wave gains nothing from it)
+        const bool pers = tc::persistent_gemm() && ctas256 > tc::sm_count();
         if (N >= 256 && ctas256 >= 120 && tc::tc_operand_ok(A, M, K, 128) &&
             tc::tc_operand_ok(B, N, K, 256)) {
             ++g_launches_tc;
             prof_begin(name, st);
-            const int rc = pers ? tc::launch_gemm_bf16_persistent<256, 3, A_MN, B_MN>(A, B, M, N, K, batch, epi, status, st)
+            const int rc = pers ? tc::launch_gemm_bf16_persistent<256, 4, A_MN, B_MN>(A, B, M, N, K, batch, epi, status, st)
                                 : tc::launch_gemm_bf16<256, 4, A_MN, B_MN>(A, B, M, N, K, batch, epi, status, st);
             prof_end(name, st);
             return rc;
@@ -742,7 +743,7 @@ static int gemm(const char* name, const void* a, int64_t lda, int64_t bsa, const
         if (N >= 128 && tc::tc_operand_ok(A, M, K, 128) && tc::tc_operand_ok(B, N, K, 128)) {
             ++g_launches_tc;
             prof_begin(name, st);
-            const int rc = pers ? tc::launch_gemm_bf16_persistent<128, 4, A_MN, B_MN>(A, B, M, N, K, batch, epi, status, st)
+            const int rc = pers ? tc::launch_gemm_bf16_persistent<128, 6, A_MN, B_MN>(A, B, M, N, K, batch, epi, status, st)
                                 : tc::launch_gemm_bf16<128, 6, A_MN, B_MN>(A, B, M, N, K, batch, epi, status, st);
             prof_end(name, st);
             return rc;

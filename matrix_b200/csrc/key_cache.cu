@@ -157,7 +157,7 @@ extern "C" int dwa_key_cache(void* stream, const DwaKeyCacheDims* dims, const vo
         if (Ng >= 256 && ctas256 >= 120 && tc::tc_operand_ok(A, M, K, 128) && tc::tc_operand_ok(B, Ng, K, 256)) {
             ++g_launches_tc;
             prof_begin("key_cache", st);
-            rc = pers ? tc::launch_gemm_bf16_persistent<256, 3, false, false>(A, B, M, Ng, K, 1, epi, status, st)
+            rc = pers ? tc::launch_gemm_bf16_persistent<256, 4, false, false>(A, B, M, Ng, K, 1, epi, status, st)
                       : tc::launch_gemm_bf16<256, 4, false, false>(A, B, M, Ng, K, 1, epi, status, st);
             prof_end("key_cache", st);
             ++g_launches_total;
@@ -166,7 +166,7 @@ extern "C" int dwa_key_cache(void* stream, const DwaKeyCacheDims* dims, const vo
         if (Ng >= 128 && tc::tc_operand_ok(A, M, K, 128) && tc::tc_operand_ok(B, Ng, K, 128)) {
             ++g_launches_tc;
             prof_begin("key_cache", st);
-            rc = pers ? tc::launch_gemm_bf16_persistent<128, 4, false, false>(A, B, M, Ng, K, 1, epi, status, st)
+            rc = pers ? tc::launch_gemm_bf16_persistent<128, 6, false, false>(A, B, M, Ng, K, 1, epi, status, st)
                       : tc::launch_gemm_bf16<128, 6, false, false>(A, B, M, Ng, K, 1, epi, status, st);
             prof_end("key_cache", st);
             ++g_launches_total;

@@ -53,11 +53,32 @@ template <int QB> constexpr int rows_per_thread() { return 4; }
 template <int QB> constexpr int tile_rows() { return 32 * rows_per_thread<QB>() * CONSUMER_WARPS; }
 template <int QB> constexpr uint32_t slot_bytes() { return tile_rows<QB>() * KQ * 4; }
 
-// Dynamic shared memory for `stages` slots and nq x S query vectors.
+// With 16 query chains the dot products run as packed pairs of queries
+// (fma.rn.f32x2: lane h of a pair is exactly fmaf(k, q_{2p+h}, dot), so the
+// scores are bit-identical to scalar FMAs in the same order), which halves the
+// FMA instructions of the loop.
+template <int QB> constexpr bool paired() { return QB > 8; }
+
+// Dynamic shared memory for `stages` slots and nq x S query vectors (and,
+// for paired queries, the same vectors interleaved by query pair).
 template <int QB>
 inline size_t smem_bytes(int stages, int nq, int S) {
     return 1024 + static_cast<size_t>(stages) * slot_bytes<QB>() +
-           static_cast<size_t>(nq) * S * 64 * sizeof(float) + 2 * static_cast<size_t>(stages) * 8;
+           static_cast<size_t>(nq) * S * 64 * sizeof(float) * (paired<QB>() ? 2 : 1) +
+           2 * static_cast<size_t>(stages) * 8;
+}
+
+__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void unpack2(unsigned long long v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+// d.lo = fma(a.lo, b.lo, d.lo), d.hi = fma(a.hi, b.hi, d.hi), round to nearest
+__device__ __forceinline__ void ffma2(unsigned long long& d, unsigned long long a, unsigned long long b) {
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(a), "l"(b));
 }
 
 // QB: queries scored per row (full pass, B <= QB, padded with zero queries);
@@ -69,12 +90,15 @@ __global__ void __launch_bounds__(THREADS, 1) key_scan_kernel(const __grid_const
     constexpr int ROWS = tile_rows<QB>();
     constexpr uint32_t SLOT = slot_bytes<QB>();
     constexpr int J = FINE ? 1 : QB;   // query chains per row
+    constexpr bool PAIRED = !FINE && paired<QB>();
     extern __shared__ uint8_t dyn[];
     const int stages = a.stages, S = a.S;
     uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn) + 1023) & ~uintptr_t(1023));
     const int nq = FINE ? a.B : QB;    // query vectors staged
     float* qs = reinterpret_cast<float*>(ring + static_cast<size_t>(stages) * SLOT);   // [nq][S][64]
-    uint64_t* full = reinterpret_cast<uint64_t*>(qs + nq * S * 64);
+    // paired queries: [S][32 element pairs][QB/2 query pairs][2 elements][2 queries]
+    float* qp = qs + nq * S * 64;
+    uint64_t* full = reinterpret_cast<uint64_t*>(qp + (PAIRED ? nq * S * 64 : 0));
     uint64_t* empty = full + stages;
     __shared__ float red_m[CONSUMER_WARPS][32], red_z[CONSUMER_WARPS][32];
 
@@ -136,6 +160,15 @@ __global__ void __launch_bounds__(THREADS, 1) key_scan_kernel(const __grid_const
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (qb < a.B) v = reinterpret_cast<const float4*>(a.qw)[i];
         reinterpret_cast<float4*>(qs)[i] = v;
+        if constexpr (PAIRED) {
+            const int rem = i - qb * S * 16, s4 = rem >> 4, e0 = (rem & 15) * 4;   // aspect, first element
+            const float x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int e = e0 + u;
+                qp[((s4 * 32 + (e >> 1)) * (QB / 2) + (qb >> 1)) * 4 + (e & 1) * 2 + (qb & 1)] = x[u];
+            }
+        }
     }
     asm volatile("bar.sync 2, %0;" ::"r"(CONSUMER_WARPS * 32) : "memory");
     const int cw = warp - 1;
@@ -149,12 +182,19 @@ __global__ void __launch_bounds__(THREADS, 1) key_scan_kernel(const __grid_const
         if (!t.valid) continue;
         const bool warp_active = cw * 32 * R < t.rows;
         const float* qt = FINE ? qs + t.b * S * 64 : qs;
-        float sc[R][J], dot[R][J], nrm[R];
+        constexpr int JD = PAIRED ? 1 : J;     // scalar dot chains (the paired ones live in dot2)
+        constexpr int JP = PAIRED ? J / 2 : 1;
+        float sc[R][J], dot[R][JD], nrm[R];
+        unsigned long long dot2[R][JP];
 #pragma unroll
         for (int i = 0; i < R; ++i) {
             nrm[i] = 0.f;
 #pragma unroll
-            for (int j = 0; j < J; ++j) { sc[i][j] = 0.f; dot[i][j] = 0.f; }
+            for (int j = 0; j < J; ++j) sc[i][j] = 0.f;
+#pragma unroll
+            for (int j = 0; j < JD; ++j) dot[i][j] = 0.f;
+#pragma unroll
+            for (int p = 0; p < JP; ++p) dot2[i][p] = 0ull;
         }
         for (int s = 0; s < S && ok; ++s) {
             for (int kq = 0; kq < 4; ++kq, ++it) {
@@ -171,7 +211,41 @@ __global__ void __launch_bounds__(THREADS, 1) key_scan_kernel(const __grid_const
                 }
                 const uint8_t* sp = ring + static_cast<size_t>(slot) * SLOT;
                 const float* qa = qt + s * 64 + kq * KQ;   // query j of this quarter: qa + j*S*64
-                if constexpr (J > 8) {
+                if constexpr (PAIRED) {
+                    // query pair p of element pair ep: qp + ((s*32 + ep)*(J/2) + p)*4
+                    const float* qpa = qp + (s * 32 + kq * (KQ / 2)) * (J / 2) * 4;
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        float4 kc[R];
+#pragma unroll
+                        for (int i = 0; i < R; ++i) {
+                            const int rr = rbase + 32 * i;
+                            kc[i] = *reinterpret_cast<const float4*>(sp + rr * (KQ * 4) + ((c ^ ((rr >> 1) & 3)) << 4));
+                        }
+#pragma unroll
+                        for (int i = 0; i < R; ++i) {
+                            nrm[i] = fmaf(kc[i].x, kc[i].x, nrm[i]);
+                            nrm[i] = fmaf(kc[i].y, kc[i].y, nrm[i]);
+                            nrm[i] = fmaf(kc[i].z, kc[i].z, nrm[i]);
+                            nrm[i] = fmaf(kc[i].w, kc[i].w, nrm[i]);
+                        }
+#pragma unroll
+                        for (int p = 0; p < J / 2; ++p) {
+                            // (q_2p, q_2p+1) of elements 4c, 4c+1 and of 4c+2, 4c+3
+                            const ulonglong2 b01 = *reinterpret_cast<const ulonglong2*>(qpa + ((2 * c) * (J / 2) + p) * 4);
+                            const ulonglong2 b23 = *reinterpret_cast<const ulonglong2*>(qpa + ((2 * c + 1) * (J / 2) + p) * 4);
+#pragma unroll
+                            for (int i = 0; i < R; ++i) {
+                                ffma2(dot2[i][p], pack2(kc[i].x, kc[i].x), b01.x);
+                                ffma2(dot2[i][p], pack2(kc[i].y, kc[i].y), b01.y);
+                                ffma2(dot2[i][p], pack2(kc[i].z, kc[i].z), b23.x);
+                                ffma2(dot2[i][p], pack2(kc[i].w, kc[i].w), b23.y);
+                            }
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) kt::mbar_arrive(&empty[slot]);
+                } else if constexpr (J > 8) {
                     // 16 query chains: the key registers hold one float4 chunk of
                     // the R rows at a time (the accumulators take the rest), and
                     // the slot is released after the last chunk
@@ -241,8 +315,19 @@ __global__ void __launch_bounds__(THREADS, 1) key_scan_kernel(const __grid_const
 #pragma unroll
                     for (int i = 0; i < R; ++i) {
                         const float inv = 1.f / (sqrtf(nrm[i]) + 1e-8f);
+                        if constexpr (PAIRED) {
 #pragma unroll
-                        for (int j = 0; j < J; ++j) { sc[i][j] = fmaf(dot[i][j], inv, sc[i][j]); dot[i][j] = 0.f; }
+                            for (int p = 0; p < JP; ++p) {
+                                float lo, hi;
+                                unpack2(dot2[i][p], lo, hi);
+                                sc[i][2 * p] = fmaf(lo, inv, sc[i][2 * p]);
+                                sc[i][2 * p + 1] = fmaf(hi, inv, sc[i][2 * p + 1]);
+                                dot2[i][p] = 0ull;
+                            }
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < J; ++j) { sc[i][j] = fmaf(dot[i][j], inv, sc[i][j]); dot[i][j] = 0.f; }
+                        }
                         nrm[i] = 0.f;
                     }
                 }

@@ -409,7 +409,7 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), EW == 8 ? 2 : 1)
 //   acc_empty[buf]  one arrive per epilogue warp: buffer buf read out
 template <int BN, int STAGES>
 struct PSmem {
-    static constexpr int HB = BN / 2 < 128 ? BN : BN / 2;   // columns staged per epilogue pass
+    static constexpr int HB = 32;                            // columns staged per epilogue pass
     static constexpr uint32_t A_STAGE = BM * BK * 2;
     static constexpr uint32_t B_STAGE = BN * BK * 2;
     static constexpr uint32_t RING = STAGES * (A_STAGE + B_STAGE);
@@ -572,8 +572,9 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
         const int e = warp - 2;        // epilogue warp 0..EW-1
         const int grp = e >> 2;        // column group 0..EW/4-1
         constexpr int LD = L::STAGE_LD;
-        constexpr int LPR = HB / 8, RPW = 32 / LPR, PF = 4;
+        constexpr int LPR = HB / 8, RPW = 32 / LPR;
         constexpr int STEP = EW * RPW;
+        constexpr int PF = BM / STEP > 4 ? 4 : (BM / STEP < 1 ? 1 : BM / STEP);
         const int sub = lane / LPR, lic = lane % LPR;
         int li = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++li) {

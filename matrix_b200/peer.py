@@ -21,6 +21,46 @@ from . import _lib
 from .runtime import dtype_code, ptr, require_cuda, stream_of, workspace
 
 
+def map_peer_buffers(local: torch.Tensor, group=None):
+    """Every rank's ``local`` buffer, readable and writable from this GPU:
+    ``(bases, opened)`` with ``bases[r]`` the device address of rank r's buffer
+    here (this rank's own for r == rank) and ``opened`` the mappings to close.
+    Collective: every rank of ``group`` calls it at the same point with
+    buffers of the same size."""
+    import torch.distributed as dist
+    require_cuda("local", local)
+    lib = _lib.load()
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    handle = (C.c_char * lib.dwa_ipc_handle_bytes())()
+    off = C.c_int64()
+    with torch.cuda.device(local.device):
+        _lib.check(lib.dwa_ipc_handle(ptr(local), handle, C.byref(off)), "dwa_ipc_handle")
+    mine = (bytes(handle), off.value, int(local.numel() * local.element_size()))
+    every = [None] * world
+    dist.all_gather_object(every, mine, group=group)
+    if any(e[2] != mine[2] for e in every):
+        raise ValueError("every rank's buffer needs the same size")
+    bases, opened = [], []
+    with torch.cuda.device(local.device):
+        for r, (h, o, _) in enumerate(every):
+            if r == rank:
+                bases.append(local.data_ptr())
+                continue
+            p = C.c_void_p()
+            _lib.check(lib.dwa_ipc_open(h, o, C.byref(p)), "dwa_ipc_open")
+            opened.append((p.value, o))
+            bases.append(p.value)
+    return bases, opened
+
+
+def close_peer_buffers(device, opened) -> None:
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        torch.cuda.synchronize(device)
+        for p, o in opened:
+            _lib.check(lib.dwa_ipc_close(C.c_void_p(p), o), "dwa_ipc_close")
+
+
 class PeerPool:
     """Every rank's pool rows, readable from this GPU.
 

@@ -122,3 +122,46 @@ def test_out_of_range_row_sets_status_and_is_skipped():
     m = keep.reshape(-1) >= 0
     np.add.at(ref, keep.reshape(-1)[m], g.reshape(-1, g.shape[-1])[m].astype(np.float64))
     assert_close(gp.cpu().numpy(), ref, 1e-6, name="skipped")
+
+
+def _bf16(x):
+    from matrix_b200.synthetic import bf16_round
+    return bf16_round(np.asarray(x, np.float32))
+
+
+@pytest.mark.parametrize("bounds", [[0, 5000], [0, 1700, 1700, 5000], [0, 900, 2600, 4100, 5000]])
+def test_owner_exchange_equals_sorted_scatter(bounds):
+    """Emulated ranks on one GPU return their rows' gradients to the owners
+    through receive areas (dwa_pool_grad_send: bf16 rows, pad slots
+    elsewhere; then each owner's dwa_pool_grad_scatter_typed).  Every owner's
+    rows equal np.add.at of the bf16-rounded contributions in float64 (rtol
+    1e-5 on the f32 sums); a second call into the other areas with fewer
+    contributions adds only those (the pad slots of the earlier call are
+    not replayed); no status bit is set by the pad slots."""
+    from matrix_b200.pool_grad import PoolGradExchange
+    from matrix_b200.runtime import raise_on_device_status
+    world = len(bounds) - 1
+    idx, g, _ = _case(seed=9)
+    D = g.shape[-1]
+    per = idx.shape[0] // world if world > 1 else idx.shape[0]
+    sends = [(idx[r * per:(r + 1) * per], g[r * per:(r + 1) * per]) for r in range(world)]
+    slot = per * idx.shape[1]
+    nbytes = PoolGradExchange.area_size(world, slot, D)
+    areas = [[torch.zeros(nbytes, dtype=torch.uint8, device="cuda") for _ in range(world)] for _ in range(2)]
+    ex = [PoolGradExchange.from_areas(world, r, bounds, slot, D, areas) for r in range(world)]
+    pools = [torch.zeros((bounds[r + 1] - bounds[r], D), dtype=torch.float32, device="cuda") for r in range(world)]
+    n_global = bounds[-1]
+    expect = np.zeros((n_global, D))
+    for call, take in enumerate((slot, slot // 3)):
+        parity = call & 1
+        for r in range(world):
+            i_r, g_r = sends[r]
+            i_r, g_r = i_r.reshape(-1)[:take], g_r.reshape(-1, D)[:take]
+            ex[r].send(torch.from_numpy(g_r).cuda(), torch.from_numpy(i_r).cuda(), parity)
+            np.add.at(expect, i_r, _bf16(g_r).astype(np.float64))
+        for r in range(world):
+            ex[r].scatter(pools[r], parity)
+        torch.cuda.synchronize()
+        got = np.concatenate([p.cpu().numpy() for p in pools])
+        assert_close(got, expect, 1e-5, name=f"call {call}")
+    raise_on_device_status()

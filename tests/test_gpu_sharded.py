@@ -183,12 +183,13 @@ def test_two_nccl_ranks(tmp_path):
 def _peer_rank(rank, world, port, out_dir):
     """One rank of a row-sharded pool: map the peer's shard by IPC, gather the
     winning rows of this rank's sequences from both shards, assemble them, and
-    return the rows' gradients to their owners (all-gather + sorted scatter)."""
+    return the rows' gradients to their owners (all-gather + sorted scatter,
+    and peer stores into the owners' receive areas + each owner's scatter)."""
     import torch.distributed as dist
     from datetime import timedelta
     from matrix_b200.assembly import assemble_backward, assemble_forward
     from matrix_b200.peer import PeerPool
-    from matrix_b200.pool_grad import scatter_pool_grad_gathered
+    from matrix_b200.pool_grad import PoolGradExchange, scatter_pool_grad_gathered
     from test_gpu_assembly import _setup
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -219,9 +220,18 @@ def _peer_rank(rank, world, port, out_dir):
                                    d(x.g_W[b0:b1]), cfg.d_B, cfg.r, cfg.d_A)[0]
         g_pool = torch.zeros((hi - lo, x.pool.shape[1]), dtype=torch.float32, device=dev)
         scatter_pool_grad_gathered(g_rows, d(idx[b0:b1]), g_pool, row_lo=lo, n_global=N)
+        # the same gradients returned to their owners by peer stores (bf16
+        # rows), twice: the second call goes through the other receive areas
+        ex = PoolGradExchange(bounds, (b1 - b0) * idx.shape[1], x.pool.shape[1], dev)
+        g_pool2 = torch.zeros_like(g_pool)
+        ex(g_rows, d(idx[b0:b1]), g_pool2)
+        once = g_pool2.clone()
+        ex(g_rows, d(idx[b0:b1]), g_pool2)
         torch.cuda.synchronize(dev)
+        ex.close()
         np.savez(os.path.join(out_dir, f"peer{rank}.npz"), rows=rows.float().cpu().numpy(),
-                 h_mid=h_mid.float().cpu().numpy(), W=W.cpu().numpy(), g_pool=g_pool.cpu().numpy())
+                 h_mid=h_mid.float().cpu().numpy(), W=W.cpu().numpy(), g_pool=g_pool.cpu().numpy(),
+                 g_pool_owner=once.cpu().numpy(), g_pool_owner2=g_pool2.cpu().numpy())
         dist.barrier()
     finally:
         if pp is not None:
@@ -261,6 +271,10 @@ def test_two_ranks_peer_gather_and_sharded_assembly(tmp_path):
     np.testing.assert_array_equal(np.concatenate([g["h_mid"] for g in got]), h_mid.float().cpu().numpy())
     np.testing.assert_array_equal(np.concatenate([g["W"] for g in got]), W.cpu().numpy())
     assert_close(np.concatenate([g["g_pool"] for g in got]), g_pool.cpu().numpy(), TOL, name="g_pool")
+    # bf16 transport of the row gradients: the bf16 tolerance
+    owner = np.concatenate([g["g_pool_owner"] for g in got])
+    assert_close(owner, g_pool.cpu().numpy(), 2e-2, name="g_pool by owner exchange")
+    np.testing.assert_array_equal(np.concatenate([g["g_pool_owner2"] for g in got]), 2 * owner)
 
 
 # ---------------------------------------------------------------------------
