@@ -253,10 +253,10 @@ __global__ void __launch_bounds__(512, 2) column_sum8_kernel(const T* __restrict
     const T* p = x + static_cast<int64_t>(b) * T_ * d;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (c < d) {
-        for (int t0 = t_lo + w; t0 < t_hi; t0 += 16 * 4) {
-            float v[4][8];
+        for (int t0 = t_lo + w; t0 < t_hi; t0 += 16 * 8) {
+            float v[8][8];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < 8; ++u) {
                 const int t = t0 + 16 * u;
                 const T* q = p + static_cast<int64_t>(t) * d + c;
                 if (t < t_hi) {
@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(512, 2) column_sum8_kernel(const T* __restrict
                 }
             }
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
+            for (int u = 0; u < 8; ++u)
 #pragma unroll
                 for (int j = 0; j < 8; ++j) acc[j] += v[u][j];
         }
@@ -311,11 +311,16 @@ __global__ void __launch_bounds__(512, 2) column_sum8_kernel(const T* __restrict
     }
 }
 
-// Launch of column_sum8_kernel over x [B, T, d]: about 64 rows per CTA, at most
-// 8 CTAs (one cluster) per (column block, b).
+// Launch of column_sum8_kernel over x [B, T, d]: the rows of a (column block,
+// b) are split over up to 8 CTAs (one cluster) only as far as needed to give
+// the GPU about 4 CTAs per SM: at least 128 rows per CTA (8 per warp, all 8
+// loads of a thread in flight at once).
 template <class T>
 inline cudaError_t launch_column_sum8(cudaStream_t st, const T* x, int B, int T_, int d, int mean, float* out) {
-    int split = (T_ + 63) / 64;
+    const int64_t blocks = static_cast<int64_t>((d + 255) / 256) * B;
+    int split = static_cast<int>((592 + blocks - 1) / blocks);                 // ~4 CTAs per SM
+    const int by_rows = (T_ + 127) / 128;
+    split = split > by_rows ? by_rows : split;
     split = split < 1 ? 1 : split > 8 ? 8 : split;
     return launch_pdl_cluster(column_sum8_kernel<T>, dim3((d + 255) / 256, B, split), dim3(512), 0, st,
                               dim3(1, 1, split), x, T_, d, mean, out);
