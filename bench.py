@@ -105,9 +105,9 @@ def step_description(name, rows_mode, world, backward, emulate=0):
     if rows_mode:
         gather = ("dwa_gather_rows (peer loads of the winning rows)" if world > 1 or emulate else
                   "winning rows read from the pool by index inside the assembly")
-        s = ("CUDA graph: seq_mean + " + ("all-gather of z + " if world > 1 else "") +
-             "dwa_retrieve_local + " + ("all-gather of summaries + " if world > 1 else "") +
-             "dwa_retrieve_merge + " + gather + " + dwa_assemble_fwd")
+        retr = ("all-gather of z + dwa_retrieve_local + all-gather of summaries + dwa_retrieve_merge"
+                if world > 1 else "dwa_retrieve_local + dwa_retrieve_merge" if emulate else "dwa_retrieve")
+        s = "CUDA graph: seq_mean + " + retr + " + " + gather + " + dwa_assemble_fwd"
         if backward:
             s += (" + dwa_assemble_bwd + pool-row gradients to their owners (peer stores of bf16 rows) and "
                   "scatter" +
@@ -500,10 +500,17 @@ class ShardedStep:
         else:
             z = self.z_local
         with comm_timer(self.comm_events, "retrieve_sharded"):
-            alphas, indices, soft = sharded_retrieve(
-                z, t["W_Q"], t["aspect_weights"], t["tau"], t["centroids"], t["keys"], t["list_offsets"],
-                t["lam"], w.is_warmup, RowShard(t["row_lo"], t["row_hi"], cfg.N, self.group), k=cfg.k_max,
-                m=cfg.m, T=cfg.T, max_list=t["max_list"], want_soft_full=w.soft_full)
+            if self.world == 1 and not self.emulate:     # every row here: the single-device call
+                from matrix_b200.retrieval import retrieve
+                alphas, indices, soft = retrieve(
+                    z, t["W_Q"], t["aspect_weights"], t["tau"], t["centroids"], t["keys"], t["lam"], w.is_warmup,
+                    k=cfg.k_max, m=cfg.m, T=cfg.T, list_offsets=t["list_offsets"], max_list=t["max_list"],
+                    want_soft_full=w.soft_full)
+            else:
+                alphas, indices, soft = sharded_retrieve(
+                    z, t["W_Q"], t["aspect_weights"], t["tau"], t["centroids"], t["keys"], t["list_offsets"],
+                    t["lam"], w.is_warmup, RowShard(t["row_lo"], t["row_hi"], cfg.N, self.group), k=cfg.k_max,
+                    m=cfg.m, T=cfg.T, max_list=t["max_list"], want_soft_full=w.soft_full)
         idx_mine = indices[self.b0:self.b1]
         al_mine = alphas[self.b0:self.b1]
         if self.peers is not None:

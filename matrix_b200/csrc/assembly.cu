@@ -324,28 +324,36 @@ __global__ void __launch_bounds__(256) prep_factors_bf16_r8_kernel(
     }
 }
 
-// pb[b][j] = b_base[j] + sum_k alpha[b,k] b_k[j].  A CTA owns 8*64 = 512
-// columns of one sequence: its 4 warp pairs (64 threads, 8 columns each, one
-// 16-byte load per row for bf16 rows) take a quarter of the k rows each, all
-// loads in flight at once, and the quarters' partial sums are added in order.
+// pb[b][j] = b_base[j] + sum_k alpha[b,k] b_k[j].  A CTA owns 8*32 = 256
+// columns of one sequence: the k row offsets and weights are staged in shared
+// memory first, then each of its 4 warps (8 columns per lane, one 16-byte
+// load per row for bf16 rows) takes a quarter of the k rows with all loads
+// independent, and the quarters' partial sums are added in order.
 template <class RT>
-__global__ void __launch_bounds__(256) prep_bias_kernel(RowSrc src, const float* __restrict__ alphas,
+__global__ void __launch_bounds__(128) prep_bias_kernel(RowSrc src, const float* __restrict__ alphas,
                                                         const float* __restrict__ b_base, int64_t s2,
                                                         int d_B, float* __restrict__ pb) {
     pdl_enter();
-    __shared__ float part[4][512];
-    const int b = blockIdx.y, q = threadIdx.x >> 6, t = threadIdx.x & 63;
-    const int j0 = blockIdx.x * 512 + t * 8;
+    __shared__ float part[4][256];
+    extern __shared__ int64_t offs[];                 // [k] row offsets, then [k] weights (as float)
+    float* wts = reinterpret_cast<float*>(offs + src.k);
+    const int b = blockIdx.y, q = threadIdx.x >> 5, t = threadIdx.x & 31;
+    for (int kk = threadIdx.x; kk < src.k; kk += blockDim.x) {
+        offs[kk] = src.offset(b, kk);
+        wts[kk] = alphas[static_cast<int64_t>(b) * src.k + kk];
+    }
+    __syncthreads();
+    const int j0 = blockIdx.x * 256 + t * 8;
     const RT* rows = static_cast<const RT*>(src.rows);
-    const float* a = alphas + static_cast<int64_t>(b) * src.k;
     const int kq = (src.k + 3) / 4, k_lo = q * kq, k_hi = min(src.k, k_lo + kq);
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     const bool vec = (s2 % 8 == 0) && (src.D % 8 == 0) && j0 + 8 <= d_B &&
                      reinterpret_cast<uintptr_t>(rows) % 16 == 0;
+#pragma unroll 8
     for (int kk = k_lo; kk < k_hi; ++kk) {
-        const int64_t off = src.offset(b, kk);
+        const int64_t off = offs[kk];
         if (off < 0) continue;
-        const float w = a[kk];
+        const float w = wts[kk];
         if (vec) {
             float x[8];
             load8(rows + off + s2 + j0, x);
@@ -359,8 +367,8 @@ __global__ void __launch_bounds__(256) prep_bias_kernel(RowSrc src, const float*
 #pragma unroll
     for (int i = 0; i < 8; ++i) part[q][t * 8 + i] = acc[i];
     __syncthreads();
-    for (int c = threadIdx.x; c < 512; c += blockDim.x) {
-        const int j = blockIdx.x * 512 + c;
+    for (int c = threadIdx.x; c < 256; c += blockDim.x) {
+        const int j = blockIdx.x * 256 + c;
         if (j < d_B) pb[static_cast<int64_t>(b) * d_B + j] = b_base[j] + (((part[0][c] + part[1][c]) + part[2][c]) + part[3][c]);
     }
 }
@@ -857,9 +865,10 @@ static int prep(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src, co
     if (with_factors) ++g_launches_total;
     if (with_bias) {
         const int64_t s2 = static_cast<int64_t>(d.d_B) * d.r + static_cast<int64_t>(d.r) * d.d_A;
-        dim3 g2((d.d_B + 511) / 512, d.B);
+        dim3 g2((d.d_B + 255) / 256, d.B);
         DWA_TIMED("prep_bias", st,
-                  launch_pdl(prep_bias_kernel<RT>, g2, 256, 0, st, src, alphas, b_base, s2, d.d_B, w.pb));
+                  launch_pdl(prep_bias_kernel<RT>, g2, 128, static_cast<size_t>(d.k) * 12, st, src, alphas, b_base,
+                             s2, d.d_B, w.pb));
         DWA_LAUNCH_CHECK("prep_bias_kernel");
         ++g_launches_total;
     }

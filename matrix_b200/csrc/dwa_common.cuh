@@ -311,16 +311,12 @@ __global__ void __launch_bounds__(512, 2) column_sum8_kernel(const T* __restrict
     }
 }
 
-// Launch of column_sum8_kernel over x [B, T, d]: the rows of a (column block,
-// b) are split over up to 8 CTAs (one cluster) only as far as needed to give
-// the GPU about 4 CTAs per SM: at least 128 rows per CTA (8 per warp, all 8
-// loads of a thread in flight at once).
+// Launch of column_sum8_kernel over x [B, T, d]: about 64 rows per CTA, at most
+// 8 CTAs (one cluster) per (column block, b); short CTAs finish sooner than
+// long ones saturate the memory system, so the split is as wide as it goes.
 template <class T>
 inline cudaError_t launch_column_sum8(cudaStream_t st, const T* x, int B, int T_, int d, int mean, float* out) {
-    const int64_t blocks = static_cast<int64_t>((d + 255) / 256) * B;
-    int split = static_cast<int>((592 + blocks - 1) / blocks);                 // ~4 CTAs per SM
-    const int by_rows = (T_ + 127) / 128;
-    split = split > by_rows ? by_rows : split;
+    int split = (T_ + 63) / 64;
     split = split < 1 ? 1 : split > 8 ? 8 : split;
     return launch_pdl_cluster(column_sum8_kernel<T>, dim3((d + 255) / 256, B, split), dim3(512), 0, st,
                               dim3(1, 1, split), x, T_, d, mean, out);
