@@ -90,6 +90,9 @@ def parse_args():
                     help="skip timing the retrieval VJP and the auxiliary losses")
     ap.add_argument("--no-key-cache", action="store_true",
                     help="skip timing compute_key_cache (once per window, not part of the step)")
+    ap.add_argument("--ncu-steps", type=int, default=0,
+                    help="for an ncu launch list: after one warm-up step, run this many eager steps, each "
+                         "inside an NVTX range 'dwa_step' (an L2 flush before each, outside it), then exit")
     return ap.parse_args()
 
 
@@ -606,7 +609,7 @@ KERNELS = ["seq_mean", "query", "query_norm", "coarse", "topm", "full_scores", "
            "softmax_apply", "prep_factors", "prep_bias", "gemm_W", "gemm_apply", "gemm_G",
            "gemm_gh", "gemm_P", "gemm_Q", "colsum", "finalize", "bias_grad", "merge", "gather_rows",
            "factored_hv", "base_rows", "cast_w_base", "gemm_base", "factored_out", "factored_combine", "probe_lists",
-           "scatter_sort", "scatter_add"]
+           "scatter_sort", "scatter_add", "grad_send"]
 COMM = ["allgather_z", "retrieve_sharded", "rowgrad_exchange", "param_allreduce"]
 
 
@@ -676,6 +679,12 @@ def profile_kernels(step, flush, group, n=5):
     del g
     dur = {k: float(np.mean(v)) for k, v in acc.items() if v}
     return dur, {k: float(np.mean(start[k])) for k in dur}, float(np.mean(total))
+
+
+def split_breakdown(dur):
+    """(library kernels, collectives / wrapped phases) of a profile_kernels
+    result; the kernels alone add up to the serialised step on one GPU."""
+    return ({k: v for k, v in dur.items() if k in KERNELS}, {k: v for k, v in dur.items() if k in COMM})
 
 
 def sync_ranks(group):
@@ -1128,7 +1137,7 @@ def decode_sweep(args, w, dev, flush, peaks, peak_src):
         runtime.raise_on_device_status()
         ms = m["ms_per_step"]
         pt = {"batch": B, "top_k": k, "ms_per_token_step": ms, "tokens_per_s": B / (ms / 1e3),
-              "kernels_ms": m["breakdown"], "gpu_launches_per_step": m["launches"],
+              "kernels_ms": split_breakdown(m["breakdown"])[0], "gpu_launches_per_step": m["launches"],
               "gathered_row_bytes": B * k * D * 2}
         for name, part in (("factored_hv", r * d), ("factored_out", d * r + d)):
             if m["breakdown"].get(name):
@@ -1153,6 +1162,26 @@ def decode_sweep(args, w, dev, flush, peaks, peak_src):
 # ======================================================================
 # Main
 # ======================================================================
+def ncu_steps(step, flush, group, n):
+    """Eager steps inside NVTX ranges 'dwa_step', for an ncu launch list
+    filtered with --nvtx --nvtx-include 'dwa_step/'."""
+    import torch
+    step()
+    sync_ranks(group)
+    for _ in range(n):
+        flush()
+        sync_ranks(group)
+        torch.cuda.nvtx.range_push("dwa_step")
+        step()
+        torch.cuda.nvtx.range_pop()
+    sync_ranks(group)
+    print(json.dumps({"ncu_steps": n}), flush=True)
+    if group is not None:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def small_dp_line(args, w, dev, group, rank, world, flush, peaks, peak_src, full=True):
     """The data-parallel small workload (fwd + bwd): every rank its own batch
     against its own pool replica.  ``full``: also e2e, key cache, extras."""
@@ -1160,8 +1189,10 @@ def small_dp_line(args, w, dev, group, rank, world, flush, peaks, peak_src, full
     step = Step(w, t, group)
     m = measure(step, flush, group, dev, args.steps, args.warmup, rank, sample_clocks=full)
     tokens = w.batch * w.seq * world
+    kern, comm = split_breakdown(m["breakdown"])
     res = {"value": tokens / (m["ms_per_step"] / 1e3), "ms_per_step": m["ms_per_step"],
-           "roofline": roofline(w, m, peaks, peak_src), "kernels_ms": m["breakdown"],
+           "roofline": roofline(w, m, peaks, peak_src), "kernels_ms": kern, "comm_ms": comm,
+           "kernels_sum_ms": float(sum(kern.values())),
            "kernels_start_ms": m["starts"], "serialized_step_ms": m["serial_ms"],
            "gpu_launches": m["launches"] * args.steps, "clocks": m["clocks"]}
     if full and not args.no_e2e:
@@ -1218,6 +1249,9 @@ def main():
         return
 
     rows_mode = w.name in ROWS_WORKLOADS or args.sharded or args.emulate_ranks
+    if not rows_mode and args.ncu_steps:
+        return ncu_steps(Step(w, build_device_workload(w, dev, args.seed + rank), group), flush, group,
+                         args.ncu_steps)
     if not rows_mode:
         r = small_dp_line(args, w, dev, group, rank, world, flush, peaks, peak_src)
         line = {"metric": METRIC, "value": r.pop("value"), "unit": "tokens/s", "n_gpus": world,
@@ -1241,6 +1275,8 @@ def main():
     emulate = args.emulate_ranks
     t = build_sharded_workload(w, dev, rank, world, group, args.seed, emulate=emulate)
     step = ShardedStep(w, t, group, rank, world, emulate=emulate)
+    if args.ncu_steps:
+        return ncu_steps(step, flush, group, args.ncu_steps)
     m = measure(step, flush, group, dev, args.steps, args.warmup, rank)
     Bp = w.batch // (emulate or world)
     n_loc = t["row_hi"] - t["row_lo"]
@@ -1252,7 +1288,9 @@ def main():
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic", "config": run_config(w.name, world, True, emulate, w=w),
             "value_per_gpu": value / (1 if emulate else world), "roofline": roof,
-            "kernels_ms": m["breakdown"], "kernels_start_ms": m["starts"], "serialized_step_ms": m["serial_ms"],
+            "kernels_ms": split_breakdown(m["breakdown"])[0], "comm_ms": split_breakdown(m["breakdown"])[1],
+            "kernels_sum_ms": float(sum(split_breakdown(m["breakdown"])[0].values())),
+            "kernels_start_ms": m["starts"], "serialized_step_ms": m["serial_ms"],
             "gpu_launches": m["launches"] * args.steps, "clocks": m["clocks"],
             "rows_per_rank": n_loc, "seqs_per_rank": Bp}
     if group is not None:

@@ -111,8 +111,11 @@ DWA_API void dwa_launch_counters(uint64_t* total, uint64_t* tensor_core_gemms, u
  * "prep_bias", "gemm_W", "gemm_apply", "gemm_G", "gemm_gh", "gemm_P",
  * "gemm_Q", "colsum", "finalize", "bias_grad", "seq_mean", "merge",
  * "key_cache", "centroid_ema", "rmsnorm_fwd", "rmsnorm_bwd", "scatter_sort",
- * "scatter_add".  Passing NULL
- * events removes the entry; dwa_profile_clear() removes all. */
+ * "scatter_add", "grad_send", "gather_rows", "key_grad", "sel_grad",
+ * "aux_query", "aux_norm", the decode kernels ("factored_hv", "factored_out",
+ * "factored_combine", "base_rows", "cast_w_base", "gemm_base") and
+ * "probe_lists"; up to 64 entries.  Passing NULL events removes the entry;
+ * dwa_profile_clear() removes all. */
 DWA_API int  dwa_profile_kernel(const char* kernel, void* start_event, void* stop_event);
 DWA_API void dwa_profile_clear(void);
 

@@ -42,7 +42,7 @@ struct ProfEntry {
     cudaEvent_t start, stop;
 };
 static std::mutex g_prof_mu;
-static ProfEntry g_prof[32];
+static ProfEntry g_prof[64];
 static int g_prof_n = 0;
 static std::atomic<int> g_prof_active{0};
 
@@ -271,7 +271,7 @@ extern "C" int dwa_profile_kernel(const char* kernel, void* start_event, void* s
         }
     } else {
         if (!e) {
-            if (dwa::g_prof_n >= 32) return dwa::fail(DWA_ERR_UNSUPPORTED, "too many timed kernels");
+            if (dwa::g_prof_n >= 64) return dwa::fail(DWA_ERR_UNSUPPORTED, "too many timed kernels");
             e = &dwa::g_prof[dwa::g_prof_n++];
             std::snprintf(e->name, sizeof(e->name), "%s", kernel);
         }

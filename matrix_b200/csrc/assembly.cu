@@ -74,8 +74,8 @@ struct EpiW : NoReduce {
             float w[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) w[i] = f.wb[i] + v[i];
-            if (W_out) store8(W_out + o, w);
-            if (W_act) store8(W_act + o, w);
+            if (W_out) store8_stream(W_out + o, w);     // the API's W: not read again in this call
+            if (W_act) store8(W_act + o, w);            // the apply GEMM's operand, read next
         } else {
             const float* wb = W_base + static_cast<int64_t>(row) * d_A + col0;
             for (int c = 0; c < cnt; ++c) {

@@ -28,6 +28,12 @@ __device__ __forceinline__ void store8(float* p, const float* v) {
     reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
     reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
 }
+// Streaming store (st.global.cs): for outputs no kernel of the same call reads
+// again, so they do not evict operands that are still being re-read from L2.
+__device__ __forceinline__ void store8_stream(float* p, const float* v) {
+    __stcs(reinterpret_cast<float4*>(p), make_float4(v[0], v[1], v[2], v[3]));
+    __stcs(reinterpret_cast<float4*>(p) + 1, make_float4(v[4], v[5], v[6], v[7]));
+}
 __device__ __forceinline__ void store8(__nv_bfloat16* p, const float* v) {
     uint4 t;
     __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&t);

@@ -58,7 +58,7 @@ struct EpiKeys : NoReduce {
     __device__ float finish(int, int row, int col0, const float* v, int cnt, const Frag&) const {
         if (cnt == 8 && d_k % 8 == 0) {
             // eight columns inside one aspect (col0 is a multiple of 8)
-            store8(keys + (static_cast<int64_t>(col0 / d_k) * N + row) * d_k + col0 % d_k, v);
+            store8_stream(keys + (static_cast<int64_t>(col0 / d_k) * N + row) * d_k + col0 % d_k, v);
         } else {
             for (int c = 0; c < cnt; ++c) {
                 const int j = col0 + c;

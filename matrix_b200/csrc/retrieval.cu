@@ -514,8 +514,16 @@ constexpr int kCoarseCluster = 8;
 
 __host__ __device__ inline size_t coarse_topm_keys_bytes(int C) { return (static_cast<size_t>(C) * 8 + 15) / 16 * 16; }
 __host__ __device__ inline int coarse_topm_chunk(int C, int CL) { return (C + CL - 1) / CL; }
-__host__ __device__ inline size_t coarse_topm_smem(int C, int S, int d_k) {
-    return coarse_topm_keys_bytes(C) + (static_cast<size_t>(S) * d_k + static_cast<size_t>(S) * 64) * sizeof(float);
+// Centroids scored per pass by one CTA of the fused coarse kernel: its chunk of
+// the lists, rounded up to a warp, as far as S * cpp threads fit in 1024.
+__host__ __device__ inline int coarse_topm_cpp(int C, int CL, int S) {
+    int cpp = (coarse_topm_chunk(C, CL) + 31) / 32 * 32;
+    const int cap = (1024 / S) / 32 * 32;
+    cpp = cpp > cap ? cap : cpp;
+    return cpp < 32 ? 32 : cpp;
+}
+__host__ __device__ inline size_t coarse_topm_smem(int C, int S, int d_k, int cpp) {
+    return coarse_topm_keys_bytes(C) + (static_cast<size_t>(S) * d_k + static_cast<size_t>(S) * cpp) * sizeof(float);
 }
 
 template <int DK>
@@ -530,7 +538,8 @@ __global__ void __launch_bounds__(1024) coarse_topm_kernel(CoarseTopmArgs a) {
     const int CL = static_cast<int>(cl.num_blocks()), rank = static_cast<int>(cl.block_rank());
     const int b = blockIdx.y, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     const int cpc = coarse_topm_chunk(C, CL), c_lo = rank * cpc, c_hi = min(C, c_lo + cpc);
-    const int cl_i = threadIdx.x & 63, s = threadIdx.x >> 6;
+    const int cpp = blockDim.x / S;             // centroids per pass (coarse_topm_cpp)
+    const int cl_i = threadIdx.x % cpp, s = threadIdx.x / cpp;
     // The preceding kernel (the query projection) does not write the
     // centroids: the first chunk's rows and their squared norms are read
     // before waiting for it.
@@ -562,7 +571,7 @@ __global__ void __launch_bounds__(1024) coarse_topm_kernel(CoarseTopmArgs a) {
     if (rank == 0)
         for (int i = threadIdx.x; i < S * d_k; i += blockDim.x) a.qw[static_cast<int64_t>(b) * S * d_k + i] = qs[i];
     cluster_wait();   // rank 0 is running: its key array takes remote stores
-    for (int cb = c_lo; cb < c_hi; cb += 64) {
+    for (int cb = c_lo; cb < c_hi; cb += cpp) {
         const int c = cb + cl_i;
         if (c < c_hi) {
             const float* kp = a.centroids + (static_cast<int64_t>(s) * C + c) * d_k;
@@ -600,12 +609,12 @@ __global__ void __launch_bounds__(1024) coarse_topm_kernel(CoarseTopmArgs a) {
                     dot = fmaf(x, qq[d], dot);
                 }
             }
-            terms[s * 64 + cl_i] = dot / (sqrtf(nrm) + 1e-8f);
+            terms[s * cpp + cl_i] = dot / (sqrtf(nrm) + 1e-8f);
         }
         __syncthreads();
         if (s == 0 && c < c_hi) {
             float sc = 0.f;
-            for (int t = 0; t < S; ++t) sc += terms[t * 64 + cl_i];
+            for (int t = 0; t < S; ++t) sc += terms[t * cpp + cl_i];
             keys0[c] = make_key(sc, static_cast<uint32_t>(c));
         }
         __syncthreads();
@@ -1388,7 +1397,8 @@ static int launch_queries_and_probes(cudaStream_t st, const DwaRetrieveDims& d, 
     //    and their candidate ranges: one cluster per query when the C list keys
     //    fit in shared memory, else three kernels
     const int CL = ivf ? std::min(kCoarseCluster, (d.C + 63) / 64) : 1;
-    const size_t ct_smem = coarse_topm_smem(d.C, d.S, d.d_k);
+    const int cpp = coarse_topm_cpp(d.C, CL, d.S);
+    const size_t ct_smem = coarse_topm_smem(d.C, d.S, d.d_k, cpp);
     const bool fused_coarse = ivf && d.C <= kStageKeys && ct_smem <= 200 * 1024;
     if (!fused_coarse) {
         DWA_TIMED("query_norm", st, launch_pdl(query_norm_kernel, d.B, 32 * d.S, 0, st, w.q, aspect_weights,
@@ -1414,7 +1424,7 @@ static int launch_queries_and_probes(cudaStream_t st, const DwaRetrieveDims& d, 
                 if (dv >= 0 && dv < 64) ct_attr[dk64][dv] = true;
             }
         }
-        DWA_TIMED("coarse", st, launch_pdl_cluster(fn, dim3(CL, d.B), dim3(64 * d.S), sm, st, dim3(CL, 1, 1), ca));
+        DWA_TIMED("coarse", st, launch_pdl_cluster(fn, dim3(CL, d.B), dim3(cpp * d.S), sm, st, dim3(CL, 1, 1), ca));
         DWA_LAUNCH_CHECK("coarse_topm_kernel");
         ++g_launches_total;
     } else if (ivf) {
