@@ -253,10 +253,10 @@ __global__ void __launch_bounds__(512, 2) column_sum8_kernel(const T* __restrict
     const T* p = x + static_cast<int64_t>(b) * T_ * d;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (c < d) {
-        for (int t0 = t_lo + w; t0 < t_hi; t0 += 16 * 8) {
-            float v[8][8];
+        for (int t0 = t_lo + w; t0 < t_hi; t0 += 16 * 4) {
+            float v[4][8];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < 4; ++u) {
                 const int t = t0 + 16 * u;
                 const T* q = p + static_cast<int64_t>(t) * d + c;
                 if (t < t_hi) {
@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(512, 2) column_sum8_kernel(const T* __restrict
                 }
             }
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
+            for (int u = 0; u < 4; ++u)
 #pragma unroll
                 for (int j = 0; j < 8; ++j) acc[j] += v[u][j];
         }
@@ -314,6 +314,8 @@ __global__ void __launch_bounds__(512, 2) column_sum8_kernel(const T* __restrict
 // Launch of column_sum8_kernel over x [B, T, d]: about 64 rows per CTA, at most
 // 8 CTAs (one cluster) per (column block, b); short CTAs finish sooner than
 // long ones saturate the memory system, so the split is as wide as it goes.
+// Four rows in flight per thread: at two 512-thread CTAs per SM a thread has
+// 64 registers, and eight rows of eight floats would spill.
 template <class T>
 inline cudaError_t launch_column_sum8(cudaStream_t st, const T* x, int B, int T_, int d, int mean, float* out) {
     int split = (T_ + 63) / 64;

@@ -83,11 +83,19 @@ __device__ __forceinline__ void ffma2(unsigned long long& d, unsigned long long 
 
 // QB: queries scored per row (full pass, B <= QB, padded with zero queries);
 // FINE: the fine pass (one query per tile, chains of query t.b only).
-template <int QB, bool FINE>
-__global__ void __launch_bounds__(THREADS, 1) key_scan_kernel(const __grid_constant__ CUtensorMap tm,
-                                                              kt::Args a) {
-    constexpr int R = rows_per_thread<QB>();
-    constexpr int ROWS = tile_rows<QB>();
+// CW: consumer warps.  CW = 7 with 4 rows per thread (the default); CW = 14
+// with 2 rows per thread (WIDE_WARPS, twice the warps to hide latency, half
+// the registers per thread): the same 896-row tile and ring either way.
+constexpr int WIDE_WARPS = 14;
+template <int CW> constexpr int scan_threads() { return 32 + 32 * CW; }
+
+template <int QB, bool FINE, int CW = CONSUMER_WARPS>
+__global__ void __launch_bounds__(scan_threads<CW>(), 1) key_scan_kernel(const __grid_constant__ CUtensorMap tm,
+                                                                         kt::Args a) {
+    static_assert(CW == CONSUMER_WARPS || CW == WIDE_WARPS, "consumer warps: 7 or 14");
+    constexpr int R = CW == WIDE_WARPS ? 2 : rows_per_thread<QB>();
+    constexpr int ROWS = 32 * R * CW;
+    static_assert(ROWS == tile_rows<QB>(), "both layouts use the same tile");
     constexpr uint32_t SLOT = slot_bytes<QB>();
     constexpr int J = FINE ? 1 : QB;   // query chains per row
     constexpr bool PAIRED = !FINE && paired<QB>();
@@ -100,14 +108,14 @@ __global__ void __launch_bounds__(THREADS, 1) key_scan_kernel(const __grid_const
     float* qp = qs + nq * S * 64;
     uint64_t* full = reinterpret_cast<uint64_t*>(qp + (PAIRED ? nq * S * 64 : 0));
     uint64_t* empty = full + stages;
-    __shared__ float red_m[CONSUMER_WARPS][32], red_z[CONSUMER_WARPS][32];
+    __shared__ float red_m[CW][32], red_z[CW][32];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         tc::prefetch_tmap(&tm);
         for (int i = 0; i < stages; ++i) {
             tc::mbar_init(&full[i], 1);
-            tc::mbar_init(&empty[i], CONSUMER_WARPS);
+            tc::mbar_init(&empty[i], CW);
         }
         tc::fence_barrier_init();
     }
@@ -155,7 +163,7 @@ __global__ void __launch_bounds__(THREADS, 1) key_scan_kernel(const __grid_const
 
     // ----------------------------------------------------------- consumers
     // the queries are staged while the producer's first loads are in flight
-    for (int i = threadIdx.x - 32; i < nq * S * 16; i += 32 * CONSUMER_WARPS) {
+    for (int i = threadIdx.x - 32; i < nq * S * 16; i += 32 * CW) {
         const int qb = i / (S * 16);
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (qb < a.B) v = reinterpret_cast<const float4*>(a.qw)[i];
@@ -170,7 +178,7 @@ __global__ void __launch_bounds__(THREADS, 1) key_scan_kernel(const __grid_const
             }
         }
     }
-    asm volatile("bar.sync 2, %0;" ::"r"(CONSUMER_WARPS * 32) : "memory");
+    asm volatile("bar.sync 2, %0;" ::"r"(CW * 32) : "memory");
     const int cw = warp - 1;
     const int rbase = cw * 32 * R + lane;   // tile row of chain i: rbase + 32*i
     const float invT = a.invT;
@@ -229,18 +237,29 @@ __global__ void __launch_bounds__(THREADS, 1) key_scan_kernel(const __grid_const
                             nrm[i] = fmaf(kc[i].z, kc[i].z, nrm[i]);
                             nrm[i] = fmaf(kc[i].w, kc[i].w, nrm[i]);
                         }
+                        unsigned long long kx[R], ky[R], kz[R], kw[R];
+#pragma unroll
+                        for (int i = 0; i < R; ++i) {
+                            kx[i] = pack2(kc[i].x, kc[i].x);
+                            ky[i] = pack2(kc[i].y, kc[i].y);
+                            kz[i] = pack2(kc[i].z, kc[i].z);
+                            kw[i] = pack2(kc[i].w, kc[i].w);
+                        }
 #pragma unroll
                         for (int p = 0; p < J / 2; ++p) {
                             // (q_2p, q_2p+1) of elements 4c, 4c+1 and of 4c+2, 4c+3
                             const ulonglong2 b01 = *reinterpret_cast<const ulonglong2*>(qpa + ((2 * c) * (J / 2) + p) * 4);
                             const ulonglong2 b23 = *reinterpret_cast<const ulonglong2*>(qpa + ((2 * c + 1) * (J / 2) + p) * 4);
+                            // component-major: the R rows' chains are independent, so a
+                            // chain's next FMA is R instructions after its last
 #pragma unroll
-                            for (int i = 0; i < R; ++i) {
-                                ffma2(dot2[i][p], pack2(kc[i].x, kc[i].x), b01.x);
-                                ffma2(dot2[i][p], pack2(kc[i].y, kc[i].y), b01.y);
-                                ffma2(dot2[i][p], pack2(kc[i].z, kc[i].z), b23.x);
-                                ffma2(dot2[i][p], pack2(kc[i].w, kc[i].w), b23.y);
-                            }
+                            for (int i = 0; i < R; ++i) ffma2(dot2[i][p], kx[i], b01.x);
+#pragma unroll
+                            for (int i = 0; i < R; ++i) ffma2(dot2[i][p], ky[i], b01.y);
+#pragma unroll
+                            for (int i = 0; i < R; ++i) ffma2(dot2[i][p], kz[i], b23.x);
+#pragma unroll
+                            for (int i = 0; i < R; ++i) ffma2(dot2[i][p], kw[i], b23.y);
                         }
                     }
                     __syncwarp();
@@ -373,13 +392,13 @@ __global__ void __launch_bounds__(THREADS, 1) key_scan_kernel(const __grid_const
         // CTA reduction of the online statistics (consumer warps only)
         red_m[cw][lane] = m_run;
         red_z[cw][lane] = z_run;
-        asm volatile("bar.sync 1, %0;" ::"r"(CONSUMER_WARPS * 32) : "memory");
+        asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
         if (cw == 0 && lane < a.B && lane < QB) {
             const int j = lane;
             float M = -INFINITY;
-            for (int w = 0; w < CONSUMER_WARPS; ++w) M = fmaxf(M, red_m[w][j]);
+            for (int w = 0; w < CW; ++w) M = fmaxf(M, red_m[w][j]);
             float Z = 0.f;
-            for (int w = 0; w < CONSUMER_WARPS; ++w)
+            for (int w = 0; w < CW; ++w)
                 if (red_m[w][j] != -INFINITY) Z += red_z[w][j] * expf(red_m[w][j] - M);
             a.partial[(static_cast<int64_t>(j) * gridDim.x + blockIdx.x) * 2] = M;
             a.partial[(static_cast<int64_t>(j) * gridDim.x + blockIdx.x) * 2 + 1] = Z;
