@@ -1064,12 +1064,13 @@ def time_training_extras(w, t, flush, peaks, reps=5):
 
     probed_ms, _ = timed(lambda: bwd(None, False))
     full_ms, kp_ms = timed(lambda: bwd(g_sf, False), name="key_grad")
-    keys_ms, _ = timed(lambda: bwd(g_sf, True))
+    keys_ms, kp_keys_ms = timed(lambda: bwd(g_sf, True), name="key_grad")
     S, N, dk = t["keys"].shape
     B = z.shape[0]
     kp_bytes = 4.0 * (S * N * dk + B * N)
     out = {"retrieve_bwd": {
         "alphas_only_ms": probed_ms, "alphas_and_soft_full_ms": full_ms, "with_key_grad_ms": keys_ms,
+        "key_pass_with_key_grad_ms": kp_keys_ms,
         "key_pass": {"kernel": "key_grad", "ms": kp_ms, "algorithmic_bytes": kp_bytes,
                      "hbm_gbs": kp_bytes / (kp_ms * 1e-3) / 1e9 if kp_ms else None,
                      "frac": (kp_bytes / (kp_ms * 1e-3) / 1e9) / float(peaks["hbm_gbs"]) if kp_ms else None},

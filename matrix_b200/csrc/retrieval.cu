@@ -1553,18 +1553,12 @@ static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaSha
                                           static_cast<int>(sc::kSmemLimit)));
         if (dev >= 0 && dev < 64) tc_attr[ti][dev] = true;
     }
-    // 16 queries: 7 consumer warps of 4 rows, or (DWA_SCAN16=wide) 14 warps of 2 rows
-    static const bool scan16_wide = [] {
-        const char* v = std::getenv("DWA_SCAN16");
-        return v && std::strcmp(v, "wide") == 0;
-    }();
     const int qi = qb == 4 ? 0 : qb == 8 ? 1 : 2;
     if (use_scan && (dev < 0 || dev >= 64 || !scan_attr[qi][dev] || !scan_attr[3][dev])) {
         const void* fns[2] = {
             qb == 4   ? reinterpret_cast<const void*>(ks::key_scan_kernel<4, false>)
             : qb == 8 ? reinterpret_cast<const void*>(ks::key_scan_kernel<8, false>)
-            : scan16_wide ? reinterpret_cast<const void*>(ks::key_scan_kernel<16, false, ks::WIDE_WARPS>)
-                          : reinterpret_cast<const void*>(ks::key_scan_kernel<16, false>),
+                      : reinterpret_cast<const void*>(ks::key_scan_kernel<16, false>),
             reinterpret_cast<const void*>(ks::key_scan_kernel<8, true>)};
         for (const void* fn : fns)
             DWA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1611,9 +1605,6 @@ static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaSha
                 DWA_TIMED(name, st, (launch_pdl(ks::key_scan_kernel<4, false>, blocks, ks::THREADS, smem, st, tm_scores, ka)));
             else if (qb == 8)
                 DWA_TIMED(name, st, (launch_pdl(ks::key_scan_kernel<8, false>, blocks, ks::THREADS, smem, st, tm_scores, ka)));
-            else if (scan16_wide)
-                DWA_TIMED(name, st, (launch_pdl(ks::key_scan_kernel<16, false, ks::WIDE_WARPS>, blocks,
-                                                ks::scan_threads<ks::WIDE_WARPS>(), smem, st, tm_scores, ka)));
             else
                 DWA_TIMED(name, st, (launch_pdl(ks::key_scan_kernel<16, false>, blocks, ks::THREADS, smem, st, tm_scores, ka)));
             DWA_LAUNCH_CHECK("key_scan_kernel");

@@ -83,19 +83,12 @@ __device__ __forceinline__ void ffma2(unsigned long long& d, unsigned long long 
 
 // QB: queries scored per row (full pass, B <= QB, padded with zero queries);
 // FINE: the fine pass (one query per tile, chains of query t.b only).
-// CW: consumer warps.  CW = 7 with 4 rows per thread (the default); CW = 14
-// with 2 rows per thread (WIDE_WARPS, twice the warps to hide latency, half
-// the registers per thread): the same 896-row tile and ring either way.
-constexpr int WIDE_WARPS = 14;
-template <int CW> constexpr int scan_threads() { return 32 + 32 * CW; }
-
-template <int QB, bool FINE, int CW = CONSUMER_WARPS>
-__global__ void __launch_bounds__(scan_threads<CW>(), 1) key_scan_kernel(const __grid_constant__ CUtensorMap tm,
-                                                                         kt::Args a) {
-    static_assert(CW == CONSUMER_WARPS || CW == WIDE_WARPS, "consumer warps: 7 or 14");
-    constexpr int R = CW == WIDE_WARPS ? 2 : rows_per_thread<QB>();
-    constexpr int ROWS = 32 * R * CW;
-    static_assert(ROWS == tile_rows<QB>(), "both layouts use the same tile");
+template <int QB, bool FINE>
+__global__ void __launch_bounds__(THREADS, 1) key_scan_kernel(const __grid_constant__ CUtensorMap tm,
+                                                              kt::Args a) {
+    constexpr int CW = CONSUMER_WARPS;
+    constexpr int R = rows_per_thread<QB>();
+    constexpr int ROWS = tile_rows<QB>();
     constexpr uint32_t SLOT = slot_bytes<QB>();
     constexpr int J = FINE ? 1 : QB;   // query chains per row
     constexpr bool PAIRED = !FINE && paired<QB>();
