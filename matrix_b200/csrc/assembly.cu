@@ -61,45 +61,25 @@ struct RowSrc {
 // 8 consecutive elements through 16-byte accesses (the pointer must be 16-byte
 // aligned for bf16, 16-byte aligned for fp32 pairs of float4).
 // W[b](j,i) = W_base(j,i) + acc   -> fp32 W_out and/or act-typed W_act
-// With `preloaded` (set by the tensor-core GEMM when it has put W_base into
-// the accumulator before the first MMA) acc already is W.
 template <class ACT>
 struct EpiW : NoReduce {
-    static constexpr bool kAccInit = true;
     const float* W_base; float* W_out; ACT* W_act; int d_B, d_A; bool vec;
-    bool preloaded = false;
-    __device__ bool can_preload() const { return vec; }
-    // 32 accumulator columns of row `row` from col0: W_base, zero past the edges
-    __device__ void init_row(int, int row, int col0, uint32_t* v) const {
-        const float* p = W_base + static_cast<int64_t>(row) * d_A + col0;
-        if (row < d_B && col0 + 32 <= d_A) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float4 x = __ldg(reinterpret_cast<const float4*>(p) + i);
-                v[4 * i] = __float_as_uint(x.x); v[4 * i + 1] = __float_as_uint(x.y);
-                v[4 * i + 2] = __float_as_uint(x.z); v[4 * i + 3] = __float_as_uint(x.w);
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = (row < d_B && col0 + i < d_A) ? __float_as_uint(p[i]) : 0u;
-        }
-    }
     struct Frag { float wb[8]; };
     __device__ void load(int, int row, int col0, int cnt, Frag& f) const {
-        if (vec && cnt == 8 && !preloaded) load8(W_base + static_cast<int64_t>(row) * d_A + col0, f.wb);
+        if (vec && cnt == 8) load8(W_base + static_cast<int64_t>(row) * d_A + col0, f.wb);
     }
     __device__ float finish(int b, int row, int col0, const float* v, int cnt, const Frag& f) const {
         const int64_t o = (static_cast<int64_t>(b) * d_B + row) * d_A + col0;
         if (vec && cnt == 8) {
             float w[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) w[i] = preloaded ? v[i] : f.wb[i] + v[i];
+            for (int i = 0; i < 8; ++i) w[i] = f.wb[i] + v[i];
             if (W_out) store8_stream(W_out + o, w);     // the API's W: not read again in this call
             if (W_act) store8(W_act + o, w);            // the apply GEMM's operand, read next
         } else {
             const float* wb = W_base + static_cast<int64_t>(row) * d_A + col0;
             for (int c = 0; c < cnt; ++c) {
-                const float w = preloaded ? v[c] : wb[c] + v[c];
+                const float w = wb[c] + v[c];
                 if (W_out) W_out[o + c] = w;
                 if (W_act) W_act[o + c] = Elem<ACT>::from_f(w);
             }
@@ -142,7 +122,6 @@ struct EpiApply : NoReduce {
 template <class ACT>
 struct EpiG {
     static constexpr int kReduce = 2;
-    static constexpr bool kAccInit = false;
     const float* gamma; const float* gWo; ACT* gW; float* gWbase; const ACT* Wact;
     float* gamma_acc; int d_B, d_A; bool vec;
     struct Frag { float w[8], x[8]; };
@@ -233,7 +212,6 @@ struct EpiP : NoReduce {
 template <class RT>
 struct EpiQ {
     static constexpr int kReduce = 1;
-    static constexpr bool kAccInit = false;
     RowSrc src; const float* alphas; float* g_rows; float* dW_acc; int64_t s1; int d_A, r; bool vec;
     struct Frag { float vv[8]; float a; bool has; };
     __device__ void load(int b, int row, int col0, int cnt, Frag& f) const {

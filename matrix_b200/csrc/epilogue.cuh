@@ -55,10 +55,6 @@ __device__ __forceinline__ void red_add4(float* p, float a, float b, float c, fl
 // starting at a multiple of 8; other segments take the scalar path in finish().
 struct NoReduce {
     static constexpr int kReduce = 0;
-    // kAccInit: the epilogue can provide initial accumulator rows
-    // (init_row), which the tensor-core GEMM preloads into TMEM while the
-    // mainloop runs, so that the MMAs accumulate onto them.
-    static constexpr bool kAccInit = false;
     __device__ void row_done(int, int, float) const {}
     __device__ void cta_done(int, float) const {}
 };

@@ -157,20 +157,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// 32 consecutive 32-bit columns of this thread's TMEM lane, from registers.
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
-        "%29, %30, %31, %32};" ::"r"(taddr),
-        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
-        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
-        "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]),
-        "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
-        : "memory");
-}
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
 // Shared-memory matrix descriptor, 128-byte swizzle, sm_100 format:
 // start>>4 [0,14), LBO>>4 [16,30), SBO>>4 [32,46), version=1 [46,48),
 // base offset 0 [49,52), layout SWIZZLE_128B = 2 [61,64).
@@ -246,20 +232,10 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), EW == 8 ? 2 : 1)
     uint64_t* done_bar = empty_bar + STAGES;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
     __shared__ float s_red[EW];
-    __shared__ uint64_t init_bar;   // one arrive per epilogue warp: accumulator preloaded
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, bz = blockIdx.z;
     const int nkb = (K + BK - 1) / BK;
-    // Epilogues with initial accumulator rows (kAccInit): the epilogue warps,
-    // idle during the mainloop, store them into TMEM and the first MMA
-    // accumulates onto them instead of overwriting.
-    Epi ep = epi;
-    bool preload = false;
-    if constexpr (Epi::kAccInit) {
-        preload = epi.can_preload();
-        ep.preloaded = preload;
-    }
 
     if (threadIdx.x == 0) {
         prefetch_tmap(&tmA);
@@ -269,7 +245,6 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), EW == 8 ? 2 : 1)
             mbar_init(&empty_bar[s], 1);
         }
         mbar_init(done_bar, 1);
-        mbar_init(&init_bar, EW);
         fence_barrier_init();
     }
     if (warp == 1) {
@@ -323,13 +298,7 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), EW == 8 ? 2 : 1)
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = instr_desc_bf16<BN, A_MN, B_MN>();
-            bool ok = true;
-            if (preload && !mbar_wait_bounded(&init_bar, 0)) {
-                raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
-                ok = false;
-            }
-            tc_fence_after();
-            for (int kb = 0; kb < nkb && ok; ++kb) {
+            for (int kb = 0; kb < nkb; ++kb) {
                 const int s = kb % STAGES;
                 if (!mbar_wait_bounded(&full_bar[s], (kb / STAGES) & 1)) {
                     raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
@@ -341,7 +310,7 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), EW == 8 ? 2 : 1)
 #pragma unroll
                 for (int kk = 0; kk < BK / 16; ++kk)
                     mma_bf16_ss(tmem, operand_desc<A_MN>(a_base, kk), operand_desc<B_MN>(b_base, kk),
-                                idesc, ((kb | kk) != 0 || preload) ? 1u : 0u);
+                                idesc, (kb | kk) != 0 ? 1u : 0u);
                 mma_commit(&empty_bar[s]);
             }
             mma_commit(done_bar);
@@ -356,20 +325,6 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), EW == 8 ? 2 : 1)
         const int q = warp & 3;
         const int e = warp - 2;        // epilogue warp 0..EW-1
         const int grp = e >> 2;        // column group 0..EW/4-1
-        if constexpr (Epi::kAccInit) {
-            if (preload) {             // this warp's lane quarter, its column group's chunks
-                const int row = m0 + q * 32 + lane;
-                for (int c = grp; c < BN / 32; c += EW / 4) {
-                    uint32_t v[32];
-                    epi.init_row(bz, row, n0 + c * 32, v);
-                    tmem_st32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c * 32, v);
-                }
-                tmem_wait_st();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&init_bar);
-            }
-        }
         const bool ok = mbar_wait_bounded(done_bar, 0);
         if (!ok && lane == 0) raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
         tc_fence_after();
@@ -403,7 +358,7 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), EW == 8 ? 2 : 1)
 #pragma unroll
                 for (int u = 0; u < PF; ++u) {
                     const int rr = base + u * STEP, row = m0 + rr;
-                    if (rr < BM && row < M && cnt > 0) ep.load(bz, row, col0, cnt, frag[u]);
+                    if (rr < BM && row < M && cnt > 0) epi.load(bz, row, col0, cnt, frag[u]);
                 }
 #pragma unroll
                 for (int u = 0; u < PF; ++u) {
@@ -413,12 +368,12 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), EW == 8 ? 2 : 1)
                         const float4* src = reinterpret_cast<const float4*>(tile + rr * LD + li * 8);
                         const float4 a = src[0], b = src[1];
                         const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-                        part = ep.finish(bz, row, col0, v, cnt, frag[u]);
+                        part = epi.finish(bz, row, col0, v, cnt, frag[u]);
                     }
                     if (Epi::kReduce == 1) {
 #pragma unroll
                         for (int o = LPR / 2; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-                        if (li == 0 && rr < BM && row < M) ep.row_done(bz, row, part);
+                        if (li == 0 && rr < BM && row < M) epi.row_done(bz, row, part);
                     } else if (Epi::kReduce == 2) {
                         cta_acc += part;
                     }
@@ -434,7 +389,7 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), EW == 8 ? 2 : 1)
     if (Epi::kReduce == 2 && threadIdx.x == 0) {
         float t = 0.f;
         for (int i = 0; i < EW; ++i) t += s_red[i];
-        ep.cta_done(bz, t);
+        epi.cta_done(bz, t);
     }
     if (warp == 1) {
         tc_fence_after();
