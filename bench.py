@@ -110,7 +110,8 @@ def step_description(name, rows_mode, world, backward, emulate=0):
                   "winning rows read from the pool by index inside the assembly")
         retr = ("all-gather of z + dwa_retrieve_local + all-gather of summaries + dwa_retrieve_merge"
                 if world > 1 else "dwa_retrieve_local + dwa_retrieve_merge" if emulate else "dwa_retrieve")
-        s = "CUDA graph: seq_mean + " + retr + " + " + gather + " + dwa_assemble_fwd"
+        s = "CUDA graph: seq_mean + " + retr + " + " + gather + (
+            " + dwa_assemble_apply (h_mid only)" if name == "decode" else " + dwa_assemble_fwd")
         if backward:
             s += (" + dwa_assemble_bwd + pool-row gradients to their owners (peer stores of bf16 rows) and "
                   "scatter" +
@@ -454,6 +455,7 @@ class ShardedStep:
         from matrix_b200.peer import PeerPool
         self.w, self.t, self.group, self.rank, self.world = w, t, group, rank, world
         self.emulate = emulate
+        self.apply_only = w.seq == 1 and not w.backward
         self.lib = _lib.load()
         self.comm_events = None
         dev = t["h_A"].device
@@ -520,8 +522,13 @@ class ShardedStep:
             rows, row_index = self.peers.gather(idx_mine), None
         else:
             rows, row_index = t["pool"], idx_mine
-        h_mid, W, W_act = assemble_forward(rows, al_mine, h_A, t["W_base"], t["b_base"], t["gamma"],
-                                           cfg.d_B, cfg.r, cfg.d_A, row_index=row_index)
+        if self.apply_only:     # generation: h_mid only, W never formed (dwa_assemble_apply)
+            from matrix_b200.assembly import assemble_apply
+            h_mid, W = assemble_apply(rows, al_mine, h_A, t["W_base"], t["b_base"], t["gamma"], cfg.d_B, cfg.r,
+                                      cfg.d_A, row_index=row_index), None
+        else:
+            h_mid, W, W_act = assemble_forward(rows, al_mine, h_A, t["W_base"], t["b_base"], t["gamma"],
+                                               cfg.d_B, cfg.r, cfg.d_A, row_index=row_index)
         out = dict(alphas=alphas, indices=indices, soft_full=soft, h_mid=h_mid, W=W,
                    rows=rows if row_index is None else None)
         if w.backward:
@@ -569,6 +576,9 @@ def kernel_work(w, name, n_rows=None, seqs=None):
         "gemm_P": ("tensor", 2 * Ba * d * d * kr),
         "gemm_Q": ("tensor", 2 * Ba * d * d * kr),
         "gather_rows": ("hbm", 2 * Ba * k * c.D * (2 if c.bf16_pool else 4)),
+        # h_mid-only apply: the V part, then the U and b parts of every winning row
+        "factored_hv": ("hbm", Ba * k * r * d * 2),
+        "factored_out": ("hbm", Ba * k * (d * r + d) * 2),
     }
     return table.get(name, ("hbm", None))
 
@@ -1243,13 +1253,16 @@ def main():
         flush_sink.copy_(flush_buf[: flush_buf.numel() // 2].sum())
 
     peaks, peak_src = load_peaks()
-    if w.name in ("decode", "decode_profile"):
-        if world > 1:
-            raise SystemExit("the decode sweep runs on one GPU (one rank's share of the pool)")
+    if w.name in ("decode", "decode_profile") and world == 1 and not args.sharded:
         print(json.dumps(decode_sweep(args, w, dev, flush, peaks, peak_src)), flush=True)
         return
+    if w.name == "decode":
+        # several GPUs: the whole 2M-row pool row-sharded over them, one token of
+        # 256 sequences with top-k 128 (the sweep's headline point), no soft_full
+        from matrix_b200.config import scaled
+        w = scaled(w, batch=256, k_max=128, soft_full=False, name="decode")
 
-    rows_mode = w.name in ROWS_WORKLOADS or args.sharded or args.emulate_ranks
+    rows_mode = w.name in ROWS_WORKLOADS or w.name == "decode" or args.sharded or args.emulate_ranks
     if not rows_mode and args.ncu_steps:
         return ncu_steps(Step(w, build_device_workload(w, dev, args.seed + rank), group), flush, group,
                          args.ncu_steps)

@@ -1068,7 +1068,7 @@ __global__ void __launch_bounds__(1024) select_kernel(SelectArgs a) {
 // in rank order and selects the top k of the CL*k pushed slots; the keys order
 // (score or gate term, then pool row) is the single-block selection's, so the
 // winners are the same.  The last rank also writes the soft_full statistics.
-constexpr int kSelThreads = 256;
+constexpr int kSelThreads = 512;
 constexpr int kSelCluster = 8;
 constexpr int kSelLocalKeys = 14336;   // candidates a CTA stages (168 KB of keys and scores)
 

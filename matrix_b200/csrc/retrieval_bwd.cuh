@@ -60,7 +60,7 @@ __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_g
 // and issues QB FMAs per column and row.  With g_keys, also writes the key
 // gradient of its rows.  Partial sums per CTA; added in CTA order afterwards.
 // Needs d_k % 4 == 0 and d_k dividing 1024.
-template <int CPT, int QB>
+template <int CPT, int QB, bool FUSED = false>
 __global__ void __launch_bounds__(kKeyThreads) key_grad_pass_kernel(KeyGradArgs a) {
     pdl_enter();
     extern __shared__ __align__(16) float kg_sm[];
@@ -73,9 +73,28 @@ __global__ void __launch_bounds__(kKeyThreads) key_grad_pass_kernel(KeyGradArgs 
     float* dotk = inv + kKeyTile * S;                 // [kKeyTile][S]
     float* qs = dotk + kKeyTile * S;                  // [QB][cols] (g_keys only)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nwarps = blockDim.x >> 5;
-    if (a.g_keys)
+    // Key gradient folded into the row loop when every warp's 32 columns lie in
+    // one aspect (d_k % 32 == 0): a thread keeps its columns' weighted queries
+    // in registers, forms g_k̂ from the G values the row loop already holds,
+    // and one warp sum per row gives its part of k·g_k̂ (the normalisation VJP's
+    // dot); the row's gradient is written after the tile.
+    constexpr bool fused = FUSED;                     // launched only with g_keys and d_k % 32 == 0
+    float* part = qs;                                 // fused: [kKeyTile][cols / 32] warp partials
+    float qsr[CPT][FUSED ? QB : 1];
+    if constexpr (FUSED) {
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) {
+            const int col = tid + c * kKeyThreads;
+#pragma unroll
+            for (int b = 0; b < QB; ++b)
+                qsr[c][b] = (col < cols && b < a.nb)
+                                ? a.qh[static_cast<int64_t>(a.b0 + b) * cols + col] * a.w[col / d_k] : 0.f;
+        }
+    }
+    if (!FUSED && a.g_keys) {
         for (int i = tid; i < a.nb * cols; i += blockDim.x)
             qs[i] = a.qh[static_cast<int64_t>(a.b0) * cols + i] * a.w[(i % cols) / d_k];
+    }
     // this thread's part of a tile load: float4 c4 of rows r0, r0 + rstep, ...
     const int q4 = d_k / 4;
     const int c4 = tid % q4, r0 = tid / q4, rstep = kKeyThreads / q4;
@@ -145,7 +164,9 @@ __global__ void __launch_bounds__(kKeyThreads) key_grad_pass_kernel(KeyGradArgs 
             for (int c = 0; c < CPT; ++c) {
                 const int col = tid + c * kKeyThreads;
                 if (CPT == 1 || col < cols) {
-                    const float kh = kt[r * cols + col] * inv[r * S + col_s[c]];
+                    const float kr = kt[r * cols + col];
+                    const float kh = kr * inv[r * S + col_s[c]];
+                    float gkv = 0.f;
 #pragma unroll
                     for (int q = 0; q < QB / 4; ++q) {
                         const float4 g = gr[q];
@@ -153,11 +174,39 @@ __global__ void __launch_bounds__(kKeyThreads) key_grad_pass_kernel(KeyGradArgs 
                         acc[c][4 * q + 1] = fmaf(g.y, kh, acc[c][4 * q + 1]);
                         acc[c][4 * q + 2] = fmaf(g.z, kh, acc[c][4 * q + 2]);
                         acc[c][4 * q + 3] = fmaf(g.w, kh, acc[c][4 * q + 3]);
+                        if constexpr (FUSED) {
+                            gkv = fmaf(g.x, qsr[c][4 * q], gkv);
+                            gkv = fmaf(g.y, qsr[c][4 * q + 1], gkv);
+                            gkv = fmaf(g.z, qsr[c][4 * q + 2], gkv);
+                            gkv = fmaf(g.w, qsr[c][4 * q + 3], gkv);
+                        }
+                    }
+                    if constexpr (FUSED) {
+                        gk[r * cols + col] = gkv;
+                        const float pd = warp_sum(kr * gkv);   // the warp's 32 columns: one aspect
+                        if (lane == 0) part[r * (cols / 32) + col / 32] = pd;
                     }
                 }
             }
         }
-        if (a.g_keys) {
+        if constexpr (FUSED) {
+            __syncthreads();   // every warp's partials of this tile
+            const int nseg = d_k / 32;
+#pragma unroll
+            for (int c = 0; c < CPT; ++c) {
+                const int col = tid + c * kKeyThreads;
+                if (CPT > 1 && col >= cols) continue;
+                const int s = col_s[c], d = col - s * d_k;
+                float* dst = a.g_keys + (static_cast<int64_t>(s) * a.N + row0) * d_k + d;
+                for (int r = 0; r < rows; ++r) {
+                    const float iv = inv[r * S + s], n = nrm[r * S + s];
+                    float dt = 0.f;
+                    for (int w = 0; w < nseg; ++w) dt += part[r * (cols / 32) + s * nseg + w];
+                    const float coef = n > 0.f ? dt * iv * iv / n : 0.f;
+                    dst[static_cast<int64_t>(r) * d_k] = gk[r * cols + col] * iv - kt[r * cols + col] * coef;
+                }
+            }
+        } else if (a.g_keys) {
             // g_k̂[r, col] = w_s Σ_b G[b, r] q̂[b, col]; then the normalisation VJP
             for (int i = tid; i < rows * cols; i += blockDim.x) {
                 const int r = i / cols, col = i - r * cols;
@@ -638,7 +687,12 @@ static int run_key_pass(cudaStream_t st, const DwaRetrieveDims& d, const BwdWork
         const size_t sm = key_grad_smem(d.S, d.d_k, qb, g_pool_keys != nullptr);
         if (sm > 200 * 1024) return fail(DWA_ERR_UNSUPPORTED, "retrieval VJP: S*d_k too large for the key tile");
         void (*fn)(KeyGradArgs) = nullptr;
-        if (cpt == 1) fn = qb == 8 ? key_grad_pass_kernel<1, 8> : qb == 16 ? key_grad_pass_kernel<1, 16> : key_grad_pass_kernel<1, 32>;
+        const bool fused = g_pool_keys != nullptr && d.d_k % 32 == 0;
+        if (fused) {
+            if (cpt == 1) fn = qb == 8 ? key_grad_pass_kernel<1, 8, true> : qb == 16 ? key_grad_pass_kernel<1, 16, true> : key_grad_pass_kernel<1, 32, true>;
+            else if (cpt == 2) fn = qb == 8 ? key_grad_pass_kernel<2, 8, true> : qb == 16 ? key_grad_pass_kernel<2, 16, true> : key_grad_pass_kernel<2, 32, true>;
+            else fn = qb == 8 ? key_grad_pass_kernel<4, 8, true> : key_grad_pass_kernel<4, 16, true>;
+        } else if (cpt == 1) fn = qb == 8 ? key_grad_pass_kernel<1, 8> : qb == 16 ? key_grad_pass_kernel<1, 16> : key_grad_pass_kernel<1, 32>;
         else if (cpt == 2) fn = qb == 8 ? key_grad_pass_kernel<2, 8> : qb == 16 ? key_grad_pass_kernel<2, 16> : key_grad_pass_kernel<2, 32>;
         else fn = qb == 8 ? key_grad_pass_kernel<4, 8> : key_grad_pass_kernel<4, 16>;
         DWA_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm)));
