@@ -18,6 +18,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <atomic>
+#include <memory>
 #include <mutex>
 
 #include <cuda.h>
@@ -568,7 +569,7 @@ __global__ void __launch_bounds__(1024) coarse_topm_kernel(CoarseTopmArgs a) {
     __syncthreads();
     for (int t = warp; t < S; t += nwarps) normalize_aspect(qs + t * d_k, a.aspect_w, S, t, d_k);
     __syncthreads();
-    if (rank == 0)
+    if (rank == 0 && a.qw)   // qw == nullptr: query_norm_kernel has written it already
         for (int i = threadIdx.x; i < S * d_k; i += blockDim.x) a.qw[static_cast<int64_t>(b) * S * d_k + i] = qs[i];
     cluster_wait();   // rank 0 is running: its key array takes remote stores
     for (int cb = c_lo; cb < c_hi; cb += cpp) {
@@ -1369,10 +1370,14 @@ extern "C" size_t dwa_retrieve_workspace_bytes(const DwaRetrieveDims* dims, int 
 // queries q = W_Q z into w.q; normalised queries into w.qw; with IVF the top-m
 // lists of every query and their candidate ranges (probe_lo, cand_base) clipped
 // to the key rows [row_lo, row_lo + N); without IVF one range of all N rows.
+// lanes != nullptr (soft_full on, so the full key scan needs only qw): the
+// normalised queries come from query_norm_kernel on `st`, and the coarse
+// scores + top-m run on lanes->aux[0], concurrently with the scan the caller
+// launches next on `st`; the caller joins the lanes before the selection.
 static int launch_queries_and_probes(cudaStream_t st, const DwaRetrieveDims& d, bool ivf, bool dk64,
                                      const void* z, const float* W_Q, const float* aspect_weights,
                                      const float* centroids, const int64_t* list_offsets, int64_t row_lo,
-                                     int64_t n_global, const RetWorkspace& w) {
+                                     int64_t n_global, const RetWorkspace& w, Lanes* lanes = nullptr) {
     const size_t qsh = static_cast<size_t>(d.S) * d.d_k * sizeof(float);
     // 1. raw aspect queries q = W_Q z
     const int rows = d.S * d.d_k;
@@ -1400,11 +1405,18 @@ static int launch_queries_and_probes(cudaStream_t st, const DwaRetrieveDims& d, 
     const int cpp = coarse_topm_cpp(d.C, CL, d.S);
     const size_t ct_smem = coarse_topm_smem(d.C, d.S, d.d_k, cpp);
     const bool fused_coarse = ivf && d.C <= kStageKeys && ct_smem <= 200 * 1024;
-    if (!fused_coarse) {
+    const bool overlap = fused_coarse && lanes != nullptr;
+    if (!fused_coarse || overlap) {
         DWA_TIMED("query_norm", st, launch_pdl(query_norm_kernel, d.B, 32 * d.S, 0, st, w.q, aspect_weights,
                                                d.S, d.d_k, w.qw));
         DWA_LAUNCH_CHECK("query_norm_kernel");
         ++g_launches_total;
+    }
+    cudaStream_t cst = st;
+    if (overlap) {
+        int rc = lanes->depend(lanes->aux[0], st, 1);   // the coarse lane starts after the raw queries
+        if (rc) return rc;
+        cst = lanes->aux[0];
     }
     if (fused_coarse) {
         const size_t sm = ct_smem;
@@ -1412,8 +1424,8 @@ static int launch_queries_and_probes(cudaStream_t st, const DwaRetrieveDims& d, 
         ca.q = w.q; ca.aspect_w = aspect_weights; ca.centroids = centroids;
         ca.S = d.S; ca.d_k = d.d_k; ca.C = d.C; ca.m = w.m_eff;
         ca.list_off = list_offsets; ca.n_global = n_global; ca.row_lo = row_lo; ca.row_hi = row_lo + d.N;
-        ca.max_list = d.max_list; ca.qw = w.qw; ca.top_clusters = w.topc; ca.probe_lo = w.probe_lo;
-        ca.cand_base = w.cand_base; ca.status = w.status;
+        ca.max_list = d.max_list; ca.qw = overlap ? nullptr : w.qw; ca.top_clusters = w.topc;
+        ca.probe_lo = w.probe_lo; ca.cand_base = w.cand_base; ca.status = w.status;
         auto fn = dk64 ? coarse_topm_kernel<64> : coarse_topm_kernel<0>;
         {   // static + dynamic shared memory may pass 48 KB at any size
             int dv = 0;
@@ -1424,7 +1436,7 @@ static int launch_queries_and_probes(cudaStream_t st, const DwaRetrieveDims& d, 
                 if (dv >= 0 && dv < 64) ct_attr[dk64][dv] = true;
             }
         }
-        DWA_TIMED("coarse", st, launch_pdl_cluster(fn, dim3(CL, d.B), dim3(cpp * d.S), sm, st, dim3(CL, 1, 1), ca));
+        DWA_TIMED("coarse", cst, launch_pdl_cluster(fn, dim3(CL, d.B), dim3(cpp * d.S), sm, cst, dim3(CL, 1, 1), ca));
         DWA_LAUNCH_CHECK("coarse_topm_kernel");
         ++g_launches_total;
     } else if (ivf) {
@@ -1495,8 +1507,15 @@ static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaSha
     const bool dk64 = d.d_k == 64 && reinterpret_cast<uintptr_t>(pool_keys) % 16 == 0 &&
                       (!ivf || reinterpret_cast<uintptr_t>(centroids) % 16 == 0);
 
+    // with soft_full the full scan needs only the normalised queries: the coarse
+    // top-m runs beside it on a lane that the selection waits for
+    std::unique_ptr<Lanes> lanes;
+    if (ivf && want_sf) {
+        lanes.reset(new Lanes(st));
+        if ((rc = lanes->rc)) return rc;
+    }
     if ((rc = launch_queries_and_probes(st, d, ivf, dk64, z, W_Q, aspect_weights, centroids, list_offsets,
-                                        row_lo, n_global, w)))
+                                        row_lo, n_global, w, lanes.get())))
         return rc;
     float* sfull = want_sf ? soft_full : w.sfull;
     // Scoring variant, the same for the full and the fine pass so both give
@@ -1631,6 +1650,7 @@ static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaSha
         DWA_LAUNCH_CHECK("full_scores_kernel");
         ++g_launches_total;
     }
+    if (lanes && (rc = lanes->join())) return rc;   // the probed lists are known from here on
     // 4. fine scores of the probed lists (read from the full pass when it ran)
     if (ivf && !want_sf && (use_tc || use_scan)) {
         if ((rc = launch_scores(1, w.scores, nullptr))) return rc;

@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(kKeyThreads) key_grad_pass_kernel(KeyGradArgs 
     // in registers, forms g_k̂ from the G values the row loop already holds,
     // and one warp sum per row gives its part of k·g_k̂ (the normalisation VJP's
     // dot); the row's gradient is written after the tile.
-    constexpr bool fused = FUSED;                     // launched only with g_keys and d_k % 32 == 0
+    // FUSED: launched only with g_keys and d_k % 32 == 0
     float* part = qs;                                 // fused: [kKeyTile][cols / 32] warp partials
     float qsr[CPT][FUSED ? QB : 1];
     if constexpr (FUSED) {

@@ -119,6 +119,26 @@ def test_without_soft_full_and_full_search():
     _check(cfg, x, shards, True, 1.0, use_ivf=False)
 
 
+@pytest.mark.parametrize("k", [24, 128])
+def test_many_queries_without_soft_full(k):
+    """The decode shape over emulated ranks: 40 queries (more than the key
+    scans take: the list-inverted fine pass in each rank's window), no
+    soft_full, top-k up to 128; every rank's merge equals the single call."""
+    from dataclasses import replace
+    from matrix_b200.runtime import raise_on_device_status
+    from matrix_b200.sharded import shard_rows
+    cfg, x = _case(B=40, seed=35)
+    cfg = replace(cfg, k_max=k)
+    shards = shard_rows(x.list_offsets, 3)
+    outs, _ = _emulated(cfg, x, shards, False, 5.0, want_sf=False)
+    ra, ri, _ = _single(cfg, x, False, 5.0, want_sf=False)
+    for p, (a, i) in enumerate(outs):
+        # every row's score is the same computation in both calls: bit-equal ranking
+        np.testing.assert_array_equal(i, ri, err_msg=f"rank {p} vs single call")
+        assert_close(a, ra, TOL, name=f"alphas rank {p}")
+    raise_on_device_status()
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
