@@ -217,8 +217,7 @@ template <int EW> constexpr int gemm_threads() { return 64 + 32 * EW; }   // + T
 constexpr int kGemmThreads = gemm_threads<kEpiWarps>();
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EW = kEpiWarps>
-// (a register cap instead of launch bounds: at 576 threads a thread may hold 112)
-__global__ void __maxnreg__(EW == 8 ? 96 : 112)
+__global__ void __launch_bounds__(gemm_threads<EW>(), EW == 8 ? 2 : 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      int M, int N, int K, int a_batched, int b_batched, Epi epi, uint32_t* status) {
     using L = SmemLayout<BN, STAGES>;
@@ -347,10 +346,7 @@ __global__ void __maxnreg__(EW == 8 ? 96 : 112)
         asm volatile("bar.sync 1, %0;" ::"n"(32 * EW) : "memory");
         // Phase 2: coalesced.  LPR lanes cover one row (8 columns each); each
         // warp first loads the epilogue operands of PF rows, then finishes them.
-        // rows whose epilogue operands are loaded before any is finished: 8
-        // for fragments of at most 8 floats (the W_base reads of the W GEMM
-        // are its stall), 4 for larger ones (register budget)
-        constexpr int LPR = BN / 8, RPW = 32 / LPR, PF = sizeof(typename Epi::Frag) <= 32 ? 8 : 4;
+        constexpr int LPR = BN / 8, RPW = 32 / LPR, PF = 4;
         constexpr int STEP = EW * RPW;
         const int sub = lane / LPR, li = lane % LPR;
         const int col0 = n0 + li * 8;
