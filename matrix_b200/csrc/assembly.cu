@@ -755,10 +755,10 @@ static int gemm(const char* name, const void* a, int64_t lda, int64_t bsa, const
         }
         const int64_t ctas256 = static_cast<int64_t>((M + 127) / 128) * ((N + 255) / 256) * batch;
         // persistent only when CTAs get several tiles (a single wave gains nothing
-        // from it) and the mainloop is long enough to hide the previous tile's
-        // epilogue (K >= 1024); short-K, store-heavy epilogues (W) run faster
-        // one tile per CTA
-        const bool pers = tc::persistent_gemm() && ctas256 > tc::sm_count() && K >= 1024;
+        // from it), and for short K (the store-heavy W epilogue) only from four
+        // waves on: below that one tile per CTA is as fast
+        const bool pers = tc::persistent_gemm() && ctas256 > tc::sm_count() &&
+                          (K >= 1024 || ctas256 >= 4 * static_cast<int64_t>(tc::sm_count()));
         if (N >= 256 && ctas256 >= 120 && tc::tc_operand_ok(A, M, K, 128) &&
             tc::tc_operand_ok(B, N, K, 256)) {
             ++g_launches_tc;

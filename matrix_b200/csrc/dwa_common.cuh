@@ -235,14 +235,18 @@ __global__ void __launch_bounds__(1024) column_sum_kernel(const T* __restrict__ 
 // Same sums with 8 consecutive columns per lane (16-byte loads for bf16, two
 // for fp32): grid (ceil(d/256), B, split) launched as clusters of (1, 1, split)
 // CTAs, 512 threads.  CTA z of a cluster sums the rows
-// [T*z/split, T*(z+1)/split) (warp w takes rows w, w+16, ..., 4 loads in flight
-// per lane), adds its 16 warp partials in warp order, and cluster rank 0 adds
+// [T*z/split, T*(z+1)/split) (warp w takes rows w, w+16, ...; U = 8 rows in
+// flight per lane for bf16, held as raw 16-byte words until they land, 4 for
+// fp32), adds its 16 warp partials in warp order, and cluster rank 0 adds
 // the split CTAs' sums in rank order out of their shared memory: deterministic
 // for a given split.  d % 8 == 0 and a 16-byte aligned x required.
+template <class T> constexpr int column_sum8_rows() { return sizeof(T) == 2 ? 8 : 4; }
+
 template <class T>
 __global__ void __launch_bounds__(512, 2) column_sum8_kernel(const T* __restrict__ x, int T_, int d,
                                                           int mean, float* __restrict__ out) {
     pdl_enter();
+    constexpr int U = column_sum8_rows<T>();
     __shared__ float part[16][257];
     __shared__ float tot[256];
     const int b = blockIdx.y, lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -253,37 +257,34 @@ __global__ void __launch_bounds__(512, 2) column_sum8_kernel(const T* __restrict
     const T* p = x + static_cast<int64_t>(b) * T_ * d;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (c < d) {
-        for (int t0 = t_lo + w; t0 < t_hi; t0 += 16 * 4) {
-            float v[4][8];
+        for (int t0 = t_lo + w; t0 < t_hi; t0 += 16 * U) {
+            uint4 r[U], r2[sizeof(T) == 2 ? 1 : U];
+            const T* q0 = p + static_cast<int64_t>(t0) * d + c;
+            const int64_t step = 16 * static_cast<int64_t>(d);
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int t = t0 + 16 * u;
-                const T* q = p + static_cast<int64_t>(t) * d + c;
-                if (t < t_hi) {
-                    if constexpr (sizeof(T) == 2) {
-                        const uint4 r = *reinterpret_cast<const uint4*>(q);
-                        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r);
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const float2 f = __bfloat1622float2(h[j]);
-                            v[u][2 * j] = f.x;
-                            v[u][2 * j + 1] = f.y;
-                        }
-                    } else {
-                        const float4 a = reinterpret_cast<const float4*>(q)[0];
-                        const float4 e = reinterpret_cast<const float4*>(q)[1];
-                        v[u][0] = a.x; v[u][1] = a.y; v[u][2] = a.z; v[u][3] = a.w;
-                        v[u][4] = e.x; v[u][5] = e.y; v[u][6] = e.z; v[u][7] = e.w;
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) v[u][j] = 0.f;
-                }
+            for (int u = 0; u < U; ++u) {
+                const uint4* q = reinterpret_cast<const uint4*>(q0 + u * step);
+                const bool in = t0 + 16 * u < t_hi;
+                r[u] = in ? q[0] : make_uint4(0u, 0u, 0u, 0u);
+                if constexpr (sizeof(T) == 4) r2[u] = in ? q[1] : make_uint4(0u, 0u, 0u, 0u);
             }
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
+            for (int u = 0; u < U; ++u) {
+                if constexpr (sizeof(T) == 2) {
+                    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r[u]);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) acc[j] += v[u][j];
+                    for (int j = 0; j < 4; ++j) {
+                        const float2 f = __bfloat1622float2(h[j]);
+                        acc[2 * j] += f.x;
+                        acc[2 * j + 1] += f.y;
+                    }
+                } else {
+                    acc[0] += __uint_as_float(r[u].x); acc[1] += __uint_as_float(r[u].y);
+                    acc[2] += __uint_as_float(r[u].z); acc[3] += __uint_as_float(r[u].w);
+                    acc[4] += __uint_as_float(r2[u].x); acc[5] += __uint_as_float(r2[u].y);
+                    acc[6] += __uint_as_float(r2[u].z); acc[7] += __uint_as_float(r2[u].w);
+                }
+            }
         }
     }
 #pragma unroll
@@ -311,14 +312,16 @@ __global__ void __launch_bounds__(512, 2) column_sum8_kernel(const T* __restrict
     }
 }
 
-// Launch of column_sum8_kernel over x [B, T, d]: about 64 rows per CTA, at most
-// 8 CTAs (one cluster) per (column block, b); short CTAs finish sooner than
-// long ones saturate the memory system, so the split is as wide as it goes.
-// Four rows in flight per thread: at two 512-thread CTAs per SM a thread has
-// 64 registers, and eight rows of eight floats would spill.
+// Launch of column_sum8_kernel over x [B, T, d]: one round of loads (16 warps x
+// U rows) per CTA where T allows, at most 8 CTAs (one cluster) per (column
+// block, b); short CTAs finish sooner than long ones saturate the memory
+// system, so the split is as wide as it goes.  At two 512-thread CTAs per SM a
+// thread has 64 registers: eight raw bf16 rows (32 registers) fit, eight fp32
+// rows would spill.
 template <class T>
 inline cudaError_t launch_column_sum8(cudaStream_t st, const T* x, int B, int T_, int d, int mean, float* out) {
-    int split = (T_ + 63) / 64;
+    const int rows = 16 * column_sum8_rows<T>();
+    int split = (T_ + rows - 1) / rows;
     split = split < 1 ? 1 : split > 8 ? 8 : split;
     return launch_pdl_cluster(column_sum8_kernel<T>, dim3((d + 255) / 256, B, split), dim3(512), 0, st,
                               dim3(1, 1, split), x, T_, d, mean, out);

@@ -403,19 +403,21 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), EW == 8 ? 2 : 1)
 // CTAs running at once share their operands in L2).  Two TMEM accumulators
 // (2 x BN columns): while the epilogue warps drain tile i from one, the MMA
 // warp accumulates tile i+1 into the other, and the producer keeps the TMA
-// ring full across tile boundaries.  The epilogue stages half a tile (BN/2
-// columns) at a time in its own shared buffer, so the ring stays in use.
+// ring full across tile boundaries.  Eight epilogue warps (320 threads, so a
+// thread may hold 168 registers) each drain 32 x 32 chunks through their own
+// 4 KB staging area beside the ring, with no block-wide barrier inside a tile.
 //   acc_full[buf]   MMA commit: tile accumulated in buffer buf
 //   acc_empty[buf]  one arrive per epilogue warp: buffer buf read out
-template <int BN, int STAGES>
+constexpr int kPersEpiWarps = 8;
+template <int BN, int STAGES, int EW = kPersEpiWarps>
 struct PSmem {
-    static constexpr int HB = 32;                            // columns staged per epilogue pass
     static constexpr uint32_t A_STAGE = BM * BK * 2;
     static constexpr uint32_t B_STAGE = BN * BK * 2;
     static constexpr uint32_t RING = STAGES * (A_STAGE + B_STAGE);
-    static constexpr uint32_t STAGE_LD = HB + 4;             // floats per staged row
+    static constexpr uint32_t STAGE_LD = 33;                 // floats per staged row: conflict-free scalar access
+    static constexpr uint32_t WARP_STAGE = 32 * STAGE_LD * 4;  // one warp's 32 x 32 chunk
     static constexpr uint32_t EPI_OFF = RING;
-    static constexpr uint32_t BAR_OFF = EPI_OFF + BM * STAGE_LD * 4;
+    static constexpr uint32_t BAR_OFF = EPI_OFF + EW * WARP_STAGE;
     static constexpr uint32_t NBAR = 2 * STAGES + 5;        // full, empty, acc_full[2], acc_empty[2], drain
     static constexpr uint32_t BYTES = 1024 + BAR_OFF + NBAR * 8 + 16;
     static_assert(BYTES <= 227 * 1024, "persistent GEMM shared memory above the per-CTA limit");
@@ -436,21 +438,18 @@ __device__ __forceinline__ bool epi_all(bool ok) {
     return r != 0;
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EW = kEpiWarps>
+template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EW = kPersEpiWarps>
 __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
     gemm_bf16_persistent(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          int M, int N, int K, int batch, int a_batched, int b_batched, Epi epi,
                          uint32_t* status) {
-    using L = PSmem<BN, STAGES>;
-    constexpr int HB = L::HB;
-    constexpr int NH = BN / HB;                 // epilogue passes per tile
+    using L = PSmem<BN, STAGES, EW>;
     constexpr uint32_t TMEM_COLS = 2 * BN;
     extern __shared__ uint8_t dyn_smem[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~static_cast<uintptr_t>(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * L::A_STAGE;
-    float* stage_tile = reinterpret_cast<float*>(smem + L::EPI_OFF);
     uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
     uint64_t* empty_bar = full_bar + STAGES;
     uint64_t* acc_full = empty_bar + STAGES;
@@ -568,14 +567,37 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
         }
         __syncwarp();
     } else {
+        // Each epilogue warp drains its own 32 x 32 chunks: TMEM lane quarter
+        // q = warp % 4 (the lanes it may read), chunks grp, grp + EW/4, ... of
+        // the tile's BN/32 column chunks.  A chunk goes TMEM -> registers (row
+        // per lane) -> the warp's own staging area -> registers again with
+        // four lanes per row and eight columns each, so the epilogue's global
+        // loads and stores are coalesced; only __syncwarp orders the staging,
+        // and the warps proceed independently within a tile.  The epilogue
+        // operands of the warp's next chunk (this tile's, or its next tile's
+        // first) are loaded before the current chunk is drained.
         const int q = warp & 3;        // TMEM lane quarter this warp may read
         const int e = warp - 2;        // epilogue warp 0..EW-1
         const int grp = e >> 2;        // column group 0..EW/4-1
         constexpr int LD = L::STAGE_LD;
-        constexpr int LPR = HB / 8, RPW = 32 / LPR;
-        constexpr int STEP = EW * RPW;
-        constexpr int PF = BM / STEP > 4 ? 4 : (BM / STEP < 1 ? 1 : BM / STEP);
-        const int sub = lane / LPR, lic = lane % LPR;
+        constexpr int CPW = BN / 32 / (EW / 4);     // chunks per warp and tile
+        static_assert(CPW >= 1 && (BN / 32) % (EW / 4) == 0, "column chunks split evenly over the groups");
+        constexpr bool PRE = sizeof(typename Epi::Frag) <= 40;   // registers for two chunks' operands
+        float* stg = reinterpret_cast<float*>(smem + L::EPI_OFF + e * L::WARP_STAGE);
+        const int fr_row = lane >> 2, fr_col = (lane & 3) * 8;   // fragment: row within 8, first column
+        typename Epi::Frag nxt[4];
+        auto load_chunk = [&](int t, int ci, typename Epi::Frag* f) {
+            if (t >= tiles) return;
+            const int n0 = (t % tiles_n) * BN, m0 = ((t / tiles_n) % tiles_m) * BM;
+            const int bz = t / (tiles_n * tiles_m);
+            const int col0 = n0 + (grp + ci * (EW / 4)) * 32 + fr_col, cnt = min(8, N - col0);
+#pragma unroll
+            for (int it = 0; it < 4; ++it) {
+                const int row = m0 + q * 32 + it * 8 + fr_row;
+                if (row < M && cnt > 0) epi.load(bz, row, col0, cnt, f[it]);
+            }
+        };
+        if (PRE) load_chunk(blockIdx.x, 0, nxt);
         int li = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++li) {
             const int n0 = (t % tiles_n) * BN, m0 = ((t / tiles_n) % tiles_m) * BM;
@@ -583,7 +605,7 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
             const int buf = li & 1;
             const bool ok = mbar_wait_bounded(&acc_full[buf], (li >> 1) & 1);
             // every epilogue thread leaves together, or none does (the named
-            // barriers below must be reached by all of them)
+            // barrier of the per-CTA reduction must be reached by all of them)
             if (!epi_all<EW>(ok)) {
                 if (lane == 0) raise_status(status, DWA_STATUS_WAIT_TIMEOUT);
                 break;
@@ -591,51 +613,45 @@ __global__ void __launch_bounds__(gemm_threads<EW>(), 1)
             tc_fence_after();
             float cta_acc = 0.f;
 #pragma unroll 1
-            for (int h = 0; h < NH; ++h) {
-                asm volatile("bar.sync 1, %0;" ::"n"(32 * EW) : "memory");   // staging buffer free
-                const int r_local = q * 32 + lane;
-                for (int c = grp; c < HB / 32; c += EW / 4) {
-                    if (n0 + h * HB + c * 32 >= N) break;
-                    float v[32];
-                    tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) +
-                                  static_cast<uint32_t>(buf * BN + h * HB + c * 32), v);
-                    float4* dst = reinterpret_cast<float4*>(stage_tile + r_local * LD + c * 32);
+            for (int ci = 0; ci < CPW; ++ci) {
+                const int c = grp + ci * (EW / 4);
+                const int col0 = n0 + c * 32 + fr_col, cnt = min(8, N - col0);
+                typename Epi::Frag frag[4];
+                if constexpr (PRE) {
 #pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                    for (int it = 0; it < 4; ++it) frag[it] = nxt[it];
+                    if (ci + 1 < CPW) load_chunk(t, ci + 1, nxt);
+                    else load_chunk(t + gridDim.x, 0, nxt);
+                } else {
+                    load_chunk(t, ci, frag);
                 }
-                if (h == NH - 1) {             // accumulator read out: the MMA may reuse it
+                float v[32];
+                tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN + c * 32), v);
+                if (ci == CPW - 1) {           // this warp's part of the accumulator read out
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&acc_empty[buf]);
                 }
-                asm volatile("bar.sync 1, %0;" ::"n"(32 * EW) : "memory");   // staging buffer full
-                const int col0 = n0 + h * HB + lic * 8;
-                const int cnt = min(8, N - col0);
-                for (int base = e * RPW + sub; base < BM; base += STEP * PF) {
-                    typename Epi::Frag frag[PF];
+                __syncwarp();                  // the previous chunk's staging reads are done
 #pragma unroll
-                    for (int u = 0; u < PF; ++u) {
-                        const int rr = base + u * STEP, row = m0 + rr;
-                        if (rr < BM && row < M && cnt > 0) epi.load(bz, row, col0, cnt, frag[u]);
+                for (int i = 0; i < 32; ++i) stg[lane * LD + i] = v[i];
+                __syncwarp();
+#pragma unroll
+                for (int it = 0; it < 4; ++it) {
+                    const int rr = it * 8 + fr_row, row = m0 + q * 32 + rr;
+                    float part = 0.f;
+                    if (row < M && cnt > 0) {
+                        float w8[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) w8[i] = stg[rr * LD + fr_col + i];
+                        part = epi.finish(bz, row, col0, w8, cnt, frag[it]);
                     }
-#pragma unroll
-                    for (int u = 0; u < PF; ++u) {
-                        const int rr = base + u * STEP, row = m0 + rr;
-                        float part = 0.f;
-                        if (rr < BM && row < M && cnt > 0) {
-                            const float4* src = reinterpret_cast<const float4*>(stage_tile + rr * LD + lic * 8);
-                            const float4 a = src[0], b = src[1];
-                            const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-                            part = epi.finish(bz, row, col0, v, cnt, frag[u]);
-                        }
-                        if (Epi::kReduce == 1) {
-#pragma unroll
-                            for (int o = LPR / 2; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-                            if (lic == 0 && rr < BM && row < M) epi.row_done(bz, row, part);
-                        } else if (Epi::kReduce == 2) {
-                            cta_acc += part;
-                        }
+                    if (Epi::kReduce == 1) {
+                        part += __shfl_xor_sync(0xffffffffu, part, 1);
+                        part += __shfl_xor_sync(0xffffffffu, part, 2);
+                        if ((lane & 3) == 0 && row < M && cnt > 0) epi.row_done(bz, row, part);
+                    } else if (Epi::kReduce == 2) {
+                        cta_acc += part;
                     }
                 }
             }
@@ -701,7 +717,7 @@ int launch_gemm_bf16(const Operand& A, const Operand& B, int M, int N, int K, in
 int sm_count();
 bool persistent_gemm();
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EW = kEpiWarps>
+template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EW = kPersEpiWarps>
 int launch_gemm_bf16_persistent(const Operand& A, const Operand& B, int M, int N, int K, int batch,
                                 const Epi& epi, uint32_t* status, cudaStream_t stream) {
     static_assert(BN == 128 || BN == 256, "persistent GEMM: BN 128 or 256");
@@ -710,7 +726,7 @@ int launch_gemm_bf16_persistent(const Operand& A, const Operand& B, int M, int N
     if (!make_operand_map(&ta, A, M, K, batch, BM, &why) ||
         !make_operand_map(&tb, B, N, K, batch, BN, &why))
         return fail(DWA_ERR_INVALID_ARG, "tensor map: " + why);
-    using L = PSmem<BN, STAGES>;
+    using L = PSmem<BN, STAGES, EW>;
     auto kern = gemm_bf16_persistent<BN, STAGES, A_MN, B_MN, Epi, EW>;
     static bool attr_set[64] = {};  // per instantiation and device
     int dev = 0;
