@@ -476,6 +476,11 @@ class ShardedStep:
         if w.backward and world > 1 and not emulate:
             from matrix_b200.pool_grad import PoolGradExchange
             self.exchange = PoolGradExchange(bounds, Bp * w.cfg.k_max, w.cfg.D, dev, group)
+        # the query means through peer-mapped buffers (NCCL all-gather if off)
+        self.z_gather = None
+        if world > 1 and not emulate:
+            from matrix_b200.sharded import peer_gather
+            self.z_gather = peer_gather(self.z_local.numel() * 4, dev, group)
 
     def __call__(self, h_A=None):
         from matrix_b200 import _lib, runtime
@@ -490,7 +495,10 @@ class ShardedStep:
         if self.world > 1:
             import torch.distributed as dist
             with comm_timer(self.comm_events, "allgather_z"):
-                dist.all_gather_into_tensor(self.z, self.z_local, group=self.group)
+                if self.z_gather is not None:
+                    self.z_gather(self.z_local, self.z)
+                else:
+                    dist.all_gather_into_tensor(self.z, self.z_local, group=self.group)
             z = self.z
         elif self.emulate:
             # the other ranks' query means, in place of the all-gather
@@ -1330,7 +1338,16 @@ def main():
                                "down each step (bytes summed over ranks); copies overlapped with compute on "
                                "two copy streams, double-buffered"}
     from matrix_b200 import runtime
-    runtime.raise_on_device_status()
+    if emulate:
+        # one rank alone: its merge sees only its own candidates (fewer than k
+        # for some queries) and the rows of the other ranks are not there to
+        # gather, so those two status bits are expected; any other is an error
+        expected = {"retrieve_merge": 0x10, "gather_rows": 0x1}
+        bad = {k: v & ~expected.get(k[1], 0) for k, v in runtime.workspace_status(clear=True).items()}
+        if any(bad.values()):
+            raise RuntimeError(f"device status in the emulated rank: {bad}")
+    else:
+        runtime.raise_on_device_status()
     del step
     t.clear()
     torch.cuda.empty_cache()

@@ -111,7 +111,7 @@ DWA_API void dwa_launch_counters(uint64_t* total, uint64_t* tensor_core_gemms, u
  * "prep_bias", "gemm_W", "gemm_apply", "gemm_G", "gemm_gh", "gemm_P",
  * "gemm_Q", "colsum", "finalize", "bias_grad", "seq_mean", "merge",
  * "key_cache", "centroid_ema", "rmsnorm_fwd", "rmsnorm_bwd", "scatter_sort",
- * "scatter_add", "grad_send", "gather_rows", "key_grad", "sel_grad",
+ * "scatter_add", "grad_send", "gather_rows", "peer_allgather", "key_grad", "sel_grad",
  * "aux_query", "aux_norm", the decode kernels ("factored_hv", "factored_out",
  * "factored_combine", "base_rows", "cast_w_base", "gemm_base") and
  * "probe_lists"; up to 64 entries.  Passing NULL events removes the entry;
@@ -508,6 +508,30 @@ DWA_API size_t dwa_pool_grad_recv_bytes(int world, int slot, int64_t D, int rows
 DWA_API int dwa_pool_grad_send(void* stream, int rank, int n, int slot, int64_t D, const int32_t* indices,
                                const float* g_rows, int rows_dtype, const DwaPoolShards* recv, void* workspace,
                                size_t workspace_bytes);
+
+/* ---------------------------------------------------------------------------
+ * All-gather of a few kilobytes per rank among the ranks of one node (one
+ * process per GPU), for the two small exchanges of a row-sharded step: the
+ * query means z and the retrieval summaries (gather_summaries, in place of an
+ * NCCL all-gather whose fixed cost is tens of microseconds).
+ *  - Every rank allocates one exchange buffer of
+ *    dwa_peer_allgather_buffer_bytes(world, bytes), zero-filled, 256-byte
+ *    aligned, and maps every other rank's (CUDA IPC); peer_buffers[r] is rank
+ *    r's buffer on this GPU (this rank's own at r == rank).
+ *  - Each call copies `bytes` (a multiple of 16) from src into every rank's
+ *    buffer, signals each peer, waits for every peer's data of the same call
+ *    and writes out[world * bytes] in rank order.  Every rank makes the same
+ *    sequence of calls on the same buffers; a call's buffers alternate
+ *    between two halves, so a rank one call ahead never overwrites data its
+ *    owner is still reading.  Capturable in a CUDA graph.
+ *  - Waits are bounded (about 1 s); a wait that gives up sets
+ *    DWA_STATUS_WAIT_TIMEOUT in the buffer's status word, read (and cleared)
+ *    with dwa_peer_allgather_status.  Ranks must run on distinct GPUs.
+ * ------------------------------------------------------------------------- */
+DWA_API size_t dwa_peer_allgather_buffer_bytes(int world, size_t bytes);
+DWA_API int dwa_peer_allgather(void* stream, int rank, int world, const void* src, size_t bytes,
+                               void* const* peer_buffers, void* out);
+DWA_API int dwa_peer_allgather_status(void* stream, const void* buffer, uint32_t* status, int clear);
 
 /* ---------------------------------------------------------------------------
  * Retrieval without a workspace.  No counterpart in the reference: it exists for

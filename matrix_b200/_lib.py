@@ -111,6 +111,9 @@ _SIGNATURES = {
     "dwa_pool_grad_recv_bytes": (C.c_size_t, [C.c_int, C.c_int, C.c_int64, C.c_int]),
     "dwa_pool_grad_send": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int64, _P, _P, C.c_int,
                                      C.POINTER(PoolShards), _P, C.c_size_t]),
+    "dwa_peer_allgather_buffer_bytes": (C.c_size_t, [C.c_int, C.c_size_t]),
+    "dwa_peer_allgather": (C.c_int, [_P, C.c_int, C.c_int, _P, C.c_size_t, C.POINTER(_P), _P]),
+    "dwa_peer_allgather_status": (C.c_int, [_P, _P, C.POINTER(C.c_uint32), C.c_int]),
     "dwa_rmsnorm_bwd": (C.c_int, [_P, C.c_int64, C.c_int, C.c_int, C.c_int, _P, _P, _P, _P, _P, _P, _P,
                                   C.c_size_t]),
     "dwa_key_cache": (C.c_int, [_P, C.POINTER(KeyCacheDims), _P, _P, _P, _P, C.c_size_t]),

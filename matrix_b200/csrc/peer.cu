@@ -144,3 +144,125 @@ extern "C" int dwa_gather_rows(void* stream, int n, int64_t D, int dtype, const 
     ++g_launches_total;
     return DWA_OK;
 }
+
+// ---------------------------------------------------------------------------
+// All-gather among the ranks of one node through exchange buffers every rank
+// has mapped (dwa_peer_allgather).  Layout of a rank's exchange buffer:
+//   [0, 4096)        flags: word 32*q holds the last call rank q has finished
+//                    writing into this buffer (one 128-byte line per source)
+//   [4096, 4100)     this rank's call counter (never written by peers)
+//   [4100, 4104)     this rank's status bits (DWA_STATUS_WAIT_TIMEOUT)
+//   [8192, ...)      two halves of world slots of `bytes`; call e writes half
+//                    e % 2, so a rank one call ahead never overwrites a slot
+//                    its owner is still reading
+// One CTA per call: it copies the input into slot `rank` of every rank's
+// half (16-byte stores, over NVLink for peers), fences at system scope,
+// stores its flag into every peer with release semantics, waits (bounded,
+// kWaitLimitNs) for every peer's flag of this call, and copies the gathered
+// half to `out`.  Replaces an NCCL all-gather of a few kilobytes per rank,
+// whose fixed cost is tens of microseconds per call.
+// ---------------------------------------------------------------------------
+namespace dwa {
+
+constexpr int kMaxGatherRanks = 16;
+constexpr int64_t kGatherFlagBytes = 4096, kGatherCounter = 4096, kGatherStatus = 4100, kGatherData = 8192;
+
+struct GatherPeers {
+    char* buf[kMaxGatherRanks];
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__global__ void __launch_bounds__(512) peer_allgather_kernel(GatherPeers peers, int rank, int world,
+                                                             const uint4* __restrict__ src, int64_t n16,
+                                                             uint4* __restrict__ out) {
+    __shared__ uint32_t s_call;
+    __shared__ int s_fail;
+    char* mine = peers.buf[rank];
+    uint32_t* counter = reinterpret_cast<uint32_t*>(mine + kGatherCounter);
+    uint32_t* status = reinterpret_cast<uint32_t*>(mine + kGatherStatus);
+    pdl_enter();
+    if (threadIdx.x == 0) {
+        s_call = *counter + 1u;
+        s_fail = 0;
+    }
+    __syncthreads();
+    const uint32_t e = s_call;
+    const int64_t half = static_cast<int64_t>(e & 1u) * world * n16;
+    for (int d = 0; d < world; ++d) {
+        uint4* dst = reinterpret_cast<uint4*>(peers.buf[d] + kGatherData) + half + static_cast<int64_t>(rank) * n16;
+        for (int64_t i = threadIdx.x; i < n16; i += blockDim.x) dst[i] = src[i];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        for (int d = 0; d < world; ++d)
+            if (d != rank) st_release_sys(reinterpret_cast<uint32_t*>(peers.buf[d]) + 32 * rank, e);
+    }
+    if (threadIdx.x < world && static_cast<int>(threadIdx.x) != rank) {
+        const uint32_t* flag = reinterpret_cast<const uint32_t*>(mine) + 32 * threadIdx.x;
+        if (static_cast<int32_t>(ld_acquire_sys(flag) - e) < 0) {
+            const uint64_t t0 = global_timer_ns();
+            while (static_cast<int32_t>(ld_acquire_sys(flag) - e) < 0) {
+                if (global_timer_ns() - t0 > kWaitLimitNs) {
+                    atomicOr(status, DWA_STATUS_WAIT_TIMEOUT);
+                    s_fail = 1;
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    const uint4* got = reinterpret_cast<const uint4*>(mine + kGatherData) + half;
+    for (int64_t i = threadIdx.x; i < world * n16; i += blockDim.x) out[i] = got[i];
+    if (threadIdx.x == 0 && !s_fail) *counter = e;
+}
+
+}  // namespace dwa
+
+extern "C" size_t dwa_peer_allgather_buffer_bytes(int world, size_t bytes) {
+    if (world <= 0 || world > dwa::kMaxGatherRanks) return 0;
+    return static_cast<size_t>(dwa::kGatherData) + 2 * static_cast<size_t>(world) * bytes;
+}
+
+extern "C" int dwa_peer_allgather(void* stream, int rank, int world, const void* src, size_t bytes,
+                                  void* const* peer_buffers, void* out) {
+    using namespace dwa;
+    if (world <= 0 || world > kMaxGatherRanks || rank < 0 || rank >= world)
+        return fail(DWA_ERR_INVALID_ARG, "peer all-gather: 1..16 ranks and 0 <= rank < world");
+    if (!src || !out || !peer_buffers) return fail(DWA_ERR_INVALID_ARG, "a required pointer is NULL");
+    if (bytes == 0 || bytes % 16 != 0 || reinterpret_cast<uintptr_t>(src) % 16 != 0 ||
+        reinterpret_cast<uintptr_t>(out) % 16 != 0)
+        return fail(DWA_ERR_UNSUPPORTED, "peer all-gather: bytes a non-zero multiple of 16, 16-byte aligned src/out");
+    GatherPeers pe{};
+    for (int r = 0; r < world; ++r) {
+        pe.buf[r] = static_cast<char*>(peer_buffers[r]);
+        if (!pe.buf[r] || reinterpret_cast<uintptr_t>(pe.buf[r]) % 256 != 0)
+            return fail(DWA_ERR_INVALID_ARG, "peer all-gather: every exchange buffer 256-byte aligned");
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    DWA_TIMED("peer_allgather", st,
+              launch_pdl(peer_allgather_kernel, 1, 512, 0, st, pe, rank, world, static_cast<const uint4*>(src),
+                         static_cast<int64_t>(bytes / 16), static_cast<uint4*>(out)));
+    DWA_LAUNCH_CHECK("peer_allgather_kernel");
+    ++g_launches_total;
+    return DWA_OK;
+}
+
+extern "C" int dwa_peer_allgather_status(void* stream, const void* buffer, uint32_t* status, int clear) {
+    using namespace dwa;
+    if (!buffer || !status) return fail(DWA_ERR_INVALID_ARG, "a required pointer is NULL");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    char* p = static_cast<char*>(const_cast<void*>(buffer)) + kGatherStatus;
+    DWA_CUDA_TRY(cudaMemcpyAsync(status, p, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+    DWA_CUDA_TRY(cudaStreamSynchronize(st));
+    if (clear) DWA_CUDA_TRY(cudaMemsetAsync(p, 0, sizeof(uint32_t), st));
+    return DWA_OK;
+}

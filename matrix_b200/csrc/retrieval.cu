@@ -998,72 +998,10 @@ __device__ void emit_selection(const SelectArgs& a, int b, int got, bool gate, f
     }
 }
 
-// One block per query, for candidate sets larger than a cluster stages: every
-// radix pass recomputes the keys from the scores in global memory.
-__global__ void __launch_bounds__(1024) select_kernel(SelectArgs a) {
-    pdl_enter();
-    __shared__ uint64_t sel_key[kMaxK];
-    __shared__ int64_t sel_pos[kMaxK];
-    __shared__ int64_t s_lo[kMaxK + 1], s_base[kMaxK + 1];
-    __shared__ float red[33];
-    const int b = blockIdx.x;
-    for (int j = threadIdx.x; j <= a.m; j += blockDim.x) {
-        s_lo[j] = a.probe_lo[static_cast<int64_t>(b) * (a.m + 1) + j];
-        s_base[j] = a.cand_base[static_cast<int64_t>(b) * (a.m + 1) + j];
-    }
-    if (a.sf_stats) write_softmax_stats(a, b, red);
-    __syncthreads();
-    const int64_t n = s_base[a.m];
-    const float lam = __ldg(a.lambda_val), tau = __ldg(a.tau), T = a.T;
-    const bool gate = !a.is_warmup;
-    const bool rank_raw = gate && lam < 0.f;  // raw is monotone in s only for lambda >= 0
-    auto locate = [&](int64_t pos, int64_t* row) {
-        int lo = 0, hi = a.m - 1;
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (s_base[mid] <= pos) lo = mid; else hi = mid - 1;
-        }
-        *row = s_lo[lo] + (pos - s_base[lo]);
-        return a.sfull ? a.sfull[static_cast<int64_t>(b) * a.N + *row]
-                       : a.scores[static_cast<int64_t>(b) * a.K_cap + pos];
-    };
-    auto key_of = [&](int64_t pos, float* raw_out) {
-        int64_t row;
-        const float s = locate(pos, &row);
-        const float raw = gate ? gate_raw(s, lam, tau, T) : 0.f;
-        *raw_out = raw;
-        return make_key(rank_raw ? raw : s, static_cast<uint32_t>(row + a.row_lo));
-    };
-    float Z = 0.f;
-    int got;
-    {
-        if (gate) {
-            float acc = 0.f;
-            for (int64_t p = threadIdx.x; p < n; p += blockDim.x) {
-                float raw;
-                key_of(p, &raw);
-                acc += raw;
-            }
-            Z = block_reduce(acc, false, red);
-        }
-        auto key_at = [&](int64_t pos) { float raw; return key_of(pos, &raw); };
-        got = block_topk(n, a.k, key_at, sel_key, sel_pos);
-    }
-    // winners' scores and global rows, one thread each
-    __shared__ float s_sv[kMaxK];
-    for (int i = threadIdx.x; i < got; i += blockDim.x) {
-        int64_t row;
-        s_sv[i] = locate(sel_pos[i], &row);
-        sel_pos[i] = row + a.row_lo;
-    }
-    __syncthreads();
-    emit_selection(a, b, got, gate, lam, tau, Z, s_sv, sel_pos);
-}
-
 // Selection of one query by a cluster of CL CTAs (grid (CL, B), clusters
-// (CL, 1, 1), kSelThreads threads), for candidate sets that fit in the
-// cluster's shared memory.  CTA r stages the candidate positions
-// [n*r/CL, n*(r+1)/CL): score, gate term and key, adds its share of the gate
+// (CL, 1, 1), kSelThreads threads).  CTA r takes the candidate positions
+// [n*r/CL, n*(r+1)/CL): score, gate term and key staged in shared memory (in
+// passes of up to local_cap when there are more), adds its share of the gate
 // sum Z, selects its local top k and stores it, with its Z share, into cluster
 // rank 0's shared memory.  After one cluster barrier rank 0 adds the Z shares
 // in rank order and selects the top k of the CL*k pushed slots; the keys order
@@ -1112,43 +1050,72 @@ __global__ void __launch_bounds__(kSelThreads) select_cluster_kernel(SelectArgs 
     const bool gate = !a.is_warmup;
     const bool rank_raw = gate && lam < 0.f;
     float zacc = 0.f;
-    if (p_hi - p_lo > local_cap) raise_status(a.status, DWA_STATUS_LIST_OVERFLOW);
-    const int64_t p_end = p_hi - p_lo > local_cap ? p_lo + local_cap : p_hi;
+    // Candidates beyond the staging capacity are taken in passes: the running
+    // winners stay at the front of the staging arrays and each pass stages up
+    // to local_cap - carried new candidates behind them.  Keys are unique
+    // (score or gate term, then pool row), so the winners do not depend on
+    // the passes.
+    auto key_at = [&](int64_t i) { return skeys[i]; };
+    int carried = 0, got = 0;
     constexpr int U = 4;
-    for (int64_t p0 = p_lo; p0 < p_end; p0 += kSelThreads * U) {
-        float sv[U];
-        int64_t rowv[U];
+    for (int64_t q0 = p_lo;;) {
+        const int64_t room = cap - carried;     // cap >= k >= carried
+        if (room <= 0) {
+            raise_status(a.status, DWA_STATUS_LIST_OVERFLOW);
+            break;
+        }
+        const int64_t q1 = p_hi - q0 > room ? q0 + room : p_hi;
+        for (int64_t p0 = q0; p0 < q1; p0 += kSelThreads * U) {
+            float sv[U];
+            int64_t rowv[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int64_t p = p0 + u * kSelThreads + tid;
-            sv[u] = 0.f;
-            rowv[u] = 0;
-            if (p < p_end) {
-                int lo = 0, hi = a.m - 1;
-                while (lo < hi) {
-                    const int mid = (lo + hi + 1) >> 1;
-                    if (s_base[mid] <= p) lo = mid; else hi = mid - 1;
+            for (int u = 0; u < U; ++u) {
+                const int64_t p = p0 + u * kSelThreads + tid;
+                sv[u] = 0.f;
+                rowv[u] = 0;
+                if (p < q1) {
+                    int lo = 0, hi = a.m - 1;
+                    while (lo < hi) {
+                        const int mid = (lo + hi + 1) >> 1;
+                        if (s_base[mid] <= p) lo = mid; else hi = mid - 1;
+                    }
+                    rowv[u] = s_lo[lo] + (p - s_base[lo]);
+                    sv[u] = a.sfull ? a.sfull[static_cast<int64_t>(b) * a.N + rowv[u]]
+                                    : a.scores[static_cast<int64_t>(b) * a.K_cap + p];
                 }
-                rowv[u] = s_lo[lo] + (p - s_base[lo]);
-                sv[u] = a.sfull ? a.sfull[static_cast<int64_t>(b) * a.N + rowv[u]]
-                                : a.scores[static_cast<int64_t>(b) * a.K_cap + p];
             }
-        }
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int64_t p = p0 + u * kSelThreads + tid;
-            if (p < p_end) {
-                const float raw = gate ? gate_raw(sv[u], lam, tau, T) : 0.f;
-                zacc += raw;
-                skeys[p - p_lo] = make_key(rank_raw ? raw : sv[u], static_cast<uint32_t>(rowv[u] + a.row_lo));
-                sscore[p - p_lo] = sv[u];
+            for (int u = 0; u < U; ++u) {
+                const int64_t p = p0 + u * kSelThreads + tid;
+                if (p < q1) {
+                    const float raw = gate ? gate_raw(sv[u], lam, tau, T) : 0.f;
+                    zacc += raw;
+                    skeys[carried + (p - q0)] = make_key(rank_raw ? raw : sv[u], static_cast<uint32_t>(rowv[u] + a.row_lo));
+                    sscore[carried + (p - q0)] = sv[u];
+                }
             }
         }
+        __syncthreads();
+        got = block_topk(carried + (q1 - q0), k, key_at, sel_key, sel_pos);
+        q0 = q1;
+        if (q0 >= p_hi) break;
+        // carry this pass's winners to the front (k <= kMaxK <= kSelThreads)
+        uint64_t kw = 0;
+        float sw = 0.f;
+        if (tid < got) {
+            kw = sel_key[tid];
+            sw = sscore[sel_pos[tid]];
+        }
+        __syncthreads();
+        if (tid < got) {
+            skeys[tid] = kw;
+            sscore[tid] = sw;
+        }
+        carried = got;
+        __syncthreads();
     }
     const float zshare = gate ? block_reduce(zacc, false, red) : 0.f;
     __syncthreads();
-    auto key_at = [&](int64_t i) { return skeys[i]; };
-    const int got = block_topk(p_end - p_lo, k, key_at, sel_key, sel_pos);
     // push the local winners (slots past got: key 0, below every real key)
     // and the Z share into rank 0
     cluster_wait();
@@ -1709,9 +1676,10 @@ static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaSha
     sa.sf_stride = shard ? summary_width(d.k) : 2;
     // one cluster of CL CTAs per query stages the candidates (about 512 per
     // CTA) when they fit, else one block per query re-reads them every pass
+    // (candidate sets beyond the cluster's staging capacity are taken in passes)
     int sel_cl = static_cast<int>(std::min<int64_t>(kSelCluster, std::max<int64_t>(1, (w.K_cap + 511) / 512)));
-    int64_t local_cap = (w.K_cap + sel_cl - 1) / sel_cl;
-    if (local_cap <= kSelLocalKeys) {
+    int64_t local_cap = std::min<int64_t>((w.K_cap + sel_cl - 1) / sel_cl, kSelLocalKeys);
+    {
         const size_t ssh = select_cluster_smem(local_cap, sel_cl, d.k);
         {
             // static + dynamic shared memory may pass 48 KB at any size
@@ -1726,10 +1694,8 @@ static int retrieve_impl(void* stream, const DwaRetrieveDims* dims, const DwaSha
         }
         DWA_TIMED("select", st, launch_pdl_cluster(select_cluster_kernel, dim3(sel_cl, d.B), dim3(kSelThreads), ssh, st,
                                                    dim3(sel_cl, 1, 1), sa, static_cast<int>(local_cap)));
-    } else {
-        DWA_TIMED("select", st, launch_pdl(select_kernel, d.B, 1024, 0, st, sa));
     }
-    DWA_LAUNCH_CHECK("select_kernel");
+    DWA_LAUNCH_CHECK("select_cluster_kernel");
     ++g_launches_total;
     // 6. normalise soft_full in place with the statistics the selection wrote
     //    (a rank of a sharded call only writes them into its summary; the merge

@@ -70,16 +70,13 @@ __global__ void __launch_bounds__(kKeyThreads) key_grad_pass_kernel(KeyGradArgs 
     float* gk = gtb + 2 * QB * kKeyTile;              // [kKeyTile][cols] (g_keys only)
     float* nrm = gk + (a.g_keys ? kKeyTile * cols : 0);// [kKeyTile][S]
     float* inv = nrm + kKeyTile * S;                  // [kKeyTile][S]
-    float* dotk = inv + kKeyTile * S;                 // [kKeyTile][S]
-    float* qs = dotk + kKeyTile * S;                  // [QB][cols] (g_keys only)
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nwarps = blockDim.x >> 5;
-    // Key gradient folded into the row loop when every warp's 32 columns lie in
-    // one aspect (d_k % 32 == 0): a thread keeps its columns' weighted queries
-    // in registers, forms g_k̂ from the G values the row loop already holds,
-    // and one warp sum per row gives its part of k·g_k̂ (the normalisation VJP's
-    // dot); the row's gradient is written after the tile.
-    // FUSED: launched only with g_keys and d_k % 32 == 0
-    float* part = qs;                                 // fused: [kKeyTile][cols / 32] warp partials
+    float* dotk = inv + kKeyTile * S;                 // [kKeyTile][S] (g_keys: the normalisation VJP's coefficient)
+    const int tid = threadIdx.x;
+    // Key gradient folded into the row loop (FUSED, launched with g_keys): a
+    // thread keeps its columns' weighted queries in registers and forms g_k̂
+    // from the G values the row loop already holds, into shared memory; then
+    // one thread per (row, aspect) takes the normalisation VJP's dot k·g_k̂
+    // and its coefficient, and the tile's gradient rows are written.
     float qsr[CPT][FUSED ? QB : 1];
     if constexpr (FUSED) {
 #pragma unroll
@@ -90,10 +87,6 @@ __global__ void __launch_bounds__(kKeyThreads) key_grad_pass_kernel(KeyGradArgs 
                 qsr[c][b] = (col < cols && b < a.nb)
                                 ? a.qh[static_cast<int64_t>(a.b0 + b) * cols + col] * a.w[col / d_k] : 0.f;
         }
-    }
-    if (!FUSED && a.g_keys) {
-        for (int i = tid; i < a.nb * cols; i += blockDim.x)
-            qs[i] = a.qh[static_cast<int64_t>(a.b0) * cols + i] * a.w[(i % cols) / d_k];
     }
     // this thread's part of a tile load: float4 c4 of rows r0, r0 + rstep, ...
     const int q4 = d_k / 4;
@@ -181,54 +174,42 @@ __global__ void __launch_bounds__(kKeyThreads) key_grad_pass_kernel(KeyGradArgs 
                             gkv = fmaf(g.w, qsr[c][4 * q + 3], gkv);
                         }
                     }
-                    if constexpr (FUSED) {
-                        gk[r * cols + col] = gkv;
-                        const float pd = warp_sum(kr * gkv);   // the warp's 32 columns: one aspect
-                        if (lane == 0) part[r * (cols / 32) + col / 32] = pd;
-                    }
+                    if constexpr (FUSED) gk[r * cols + col] = gkv;
                 }
             }
         }
         if constexpr (FUSED) {
-            __syncthreads();   // every warp's partials of this tile
-            const int nseg = d_k / 32;
+            __syncthreads();   // the tile's g_k̂
+            // coefficient of the normalisation VJP per (row, aspect):
+            // (k·g_k̂) / (|k| (|k| + eps)^2); four partial chains over float4s,
+            // each thread starting at a different float4 (spread over the banks)
+            for (int p = tid; p < rows * S; p += blockDim.x) {
+                const int r = p / S, s = p - r * S;
+                const float4* kr4 = reinterpret_cast<const float4*>(kt + r * cols + s * d_k);
+                const float4* gr4 = reinterpret_cast<const float4*>(gk + r * cols + s * d_k);
+                float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
+                for (int i = 0; i < q4; ++i) {
+                    const int j = (i + p) % q4;
+                    const float4 u = kr4[j], v = gr4[j];
+                    t0 = fmaf(u.x, v.x, t0);
+                    t1 = fmaf(u.y, v.y, t1);
+                    t2 = fmaf(u.z, v.z, t2);
+                    t3 = fmaf(u.w, v.w, t3);
+                }
+                const float dt = (t0 + t1) + (t2 + t3), iv = inv[p], n = nrm[p];
+                dotk[p] = n > 0.f ? dt * iv * iv / n : 0.f;
+            }
+            __syncthreads();
 #pragma unroll
             for (int c = 0; c < CPT; ++c) {
                 const int col = tid + c * kKeyThreads;
                 if (CPT > 1 && col >= cols) continue;
                 const int s = col_s[c], d = col - s * d_k;
                 float* dst = a.g_keys + (static_cast<int64_t>(s) * a.N + row0) * d_k + d;
-                for (int r = 0; r < rows; ++r) {
-                    const float iv = inv[r * S + s], n = nrm[r * S + s];
-                    float dt = 0.f;
-                    for (int w = 0; w < nseg; ++w) dt += part[r * (cols / 32) + s * nseg + w];
-                    const float coef = n > 0.f ? dt * iv * iv / n : 0.f;
-                    dst[static_cast<int64_t>(r) * d_k] = gk[r * cols + col] * iv - kt[r * cols + col] * coef;
-                }
-            }
-        } else if (a.g_keys) {
-            // g_k̂[r, col] = w_s Σ_b G[b, r] q̂[b, col]; then the normalisation VJP
-            for (int i = tid; i < rows * cols; i += blockDim.x) {
-                const int r = i / cols, col = i - r * cols;
-                float g = 0.f;
-                for (int b = 0; b < a.nb; ++b) g = fmaf(gt[r * QB + b], qs[b * cols + col], g);
-                gk[i] = g;
-            }
-            __syncthreads();
-            for (int p = warp; p < rows * S; p += nwarps) {
-                const int r = p / S, s = p - r * S;
-                float dt = 0.f;
-                for (int d = lane; d < d_k; d += 32)
-                    dt = fmaf(kt[r * cols + s * d_k + d], gk[r * cols + s * d_k + d], dt);
-                dt = warp_sum(dt);
-                if (lane == 0) dotk[r * S + s] = dt;
-            }
-            __syncthreads();
-            for (int i = tid; i < rows * cols; i += blockDim.x) {
-                const int r = i / cols, col = i - r * cols, s = col / d_k, d = col - s * d_k;
-                const float iv = inv[r * S + s], n = nrm[r * S + s];
-                const float coef = n > 0.f ? dotk[r * S + s] * iv * iv / n : 0.f;
-                a.g_keys[(static_cast<int64_t>(s) * a.N + row0 + r) * d_k + d] = gk[i] * iv - kt[i] * coef;
+#pragma unroll 4
+                for (int r = 0; r < rows; ++r)
+                    dst[static_cast<int64_t>(r) * d_k] =
+                        gk[r * cols + col] * inv[r * S + s] - kt[r * cols + col] * dotk[r * S + s];
             }
         }
         __syncthreads();           // buffer cur is free for the tile after next
@@ -248,8 +229,8 @@ __global__ void __launch_bounds__(kKeyThreads) key_grad_pass_kernel(KeyGradArgs 
 
 __host__ inline size_t key_grad_smem(int S, int d_k, int QB, bool g_keys) {
     const size_t cols = static_cast<size_t>(S) * d_k;
-    return (kKeyTile * cols * (g_keys ? 3 : 2) + 2 * static_cast<size_t>(QB) * kKeyTile + 3 * kKeyTile * S +
-            (g_keys ? static_cast<size_t>(QB) * cols : 0)) * sizeof(float);
+    return (kKeyTile * cols * (g_keys ? 3 : 2) + 2 * static_cast<size_t>(QB) * kKeyTile + 3 * kKeyTile * S) *
+           sizeof(float);
 }
 
 // Tiles of the key pass that hold a probed list's rows: tile_on[t] = 1 when
@@ -508,7 +489,6 @@ __global__ void query_grad_kernel(const float* __restrict__ partial, int nparts,
     pdl_enter();
     __shared__ float red[33];
     const int bl = blockIdx.x, s = blockIdx.y, b = b0 + bl, d = threadIdx.x;
-    const int cols = S * d_k;
     float A = 0.f, qv = 0.f;
     if (d < d_k) {
         for (int p = 0; p < nparts; ++p) A += partial[(static_cast<int64_t>(p) * nb + bl) * rstride + s * d_k + d];
@@ -687,7 +667,7 @@ static int run_key_pass(cudaStream_t st, const DwaRetrieveDims& d, const BwdWork
         const size_t sm = key_grad_smem(d.S, d.d_k, qb, g_pool_keys != nullptr);
         if (sm > 200 * 1024) return fail(DWA_ERR_UNSUPPORTED, "retrieval VJP: S*d_k too large for the key tile");
         void (*fn)(KeyGradArgs) = nullptr;
-        const bool fused = g_pool_keys != nullptr && d.d_k % 32 == 0;
+        const bool fused = g_pool_keys != nullptr;   // the key gradient is always the fused pass
         if (fused) {
             if (cpt == 1) fn = qb == 8 ? key_grad_pass_kernel<1, 8, true> : qb == 16 ? key_grad_pass_kernel<1, 16, true> : key_grad_pass_kernel<1, 32, true>;
             else if (cpt == 2) fn = qb == 8 ? key_grad_pass_kernel<2, 8, true> : qb == 16 ? key_grad_pass_kernel<2, 16, true> : key_grad_pass_kernel<2, 32, true>;

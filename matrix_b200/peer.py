@@ -144,3 +144,55 @@ class PeerPool:
             for p, o in self._opened:
                 _lib.check(lib.dwa_ipc_close(C.c_void_p(p), o), "dwa_ipc_close")
         self._opened = []
+
+
+class PeerAllGather:
+    """All-gather of ``nbytes`` per rank through exchange buffers mapped on
+    every GPU of the group (``dwa_peer_allgather``): for the few-kilobyte
+    exchanges of a row-sharded step, whose NCCL all-gather costs tens of
+    microseconds each.  ``__call__(src)`` returns ``out`` ``[world, *src.shape]``
+    in rank order, the same values ``dist.all_gather_into_tensor`` gives.
+
+    Collective: every rank of ``group`` constructs it at the same point, and
+    every rank makes the same sequence of calls.  The ranks must be on
+    distinct GPUs (a rank waits, bounded, for its peers' data)."""
+
+    def __init__(self, nbytes: int, device, group=None):
+        import torch.distributed as dist
+        lib = _lib.load()
+        self.world, self.rank, self.nbytes = dist.get_world_size(group), dist.get_rank(group), int(nbytes)
+        if self.nbytes <= 0 or self.nbytes % 16:
+            raise ValueError("nbytes must be a positive multiple of 16")
+        size = int(lib.dwa_peer_allgather_buffer_bytes(self.world, self.nbytes))
+        if size == 0:
+            raise ValueError(f"dwa_peer_allgather supports 1..16 ranks, not {self.world}")
+        self.device = torch.device(device)
+        self.buffer = torch.zeros(size, dtype=torch.uint8, device=self.device)
+        torch.cuda.synchronize(self.device)      # zeroed before any peer writes into it
+        bases, self._opened = map_peer_buffers(self.buffer, group)
+        self._bases = (C.c_void_p * self.world)(*bases)
+        dist.barrier(group)                      # every rank's buffer is mapped and zero
+
+    def __call__(self, src: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        require_cuda("src", src)
+        if src.numel() * src.element_size() != self.nbytes or not src.is_contiguous():
+            raise ValueError(f"src must be a contiguous tensor of {self.nbytes} bytes")
+        if out is None:
+            out = torch.empty((self.world,) + tuple(src.shape), dtype=src.dtype, device=src.device)
+        lib = _lib.load()
+        _lib.check(lib.dwa_peer_allgather(stream_of(src.device), self.rank, self.world, ptr(src), self.nbytes,
+                                          self._bases, ptr(out)), "dwa_peer_allgather")
+        return out
+
+    def status(self, clear: bool = True) -> int:
+        """The buffer's status bits (DWA_STATUS_WAIT_TIMEOUT when a wait gave
+        up); synchronises the current stream."""
+        s = C.c_uint32()
+        _lib.check(_lib.load().dwa_peer_allgather_status(stream_of(self.device), ptr(self.buffer), C.byref(s),
+                                                          int(clear)), "dwa_peer_allgather_status")
+        return int(s.value)
+
+    def close(self) -> None:
+        if self._opened:
+            close_peer_buffers(self.device, self._opened)
+            self._opened = []

@@ -11,7 +11,8 @@ IVF stays on and only k candidates per query cross the interconnect:
    picks the same top-m lists and scores the part of them it holds.  Output:
    a summary ``[B, 2k+3]`` per rank (see ``summary_width``) and, with
    soft_full, the raw scores of the rank's rows.
-2. ``gather_summaries``: one all-gather of ``B*(2k+3)*4`` bytes per rank.
+2. ``gather_summaries``: one all-gather of ``B*(2k+3)*4`` bytes per rank
+   (peer-mapped buffers, ``dwa_peer_allgather``, on an NCCL group).
 3. ``retrieve_merge`` on every rank (``dwa_retrieve_merge``): the global top-k
    (ties to the lower pool row), alphas as the single-device call defines
    them, and the rank's soft_full slice normalised with the merged softmax
@@ -70,20 +71,50 @@ def shard_rows(list_offsets, world: int) -> list[tuple[int, int]]:
     return [(bounds[p], bounds[p + 1]) for p in range(world)]
 
 
+_peer_gathers: dict = {}
+
+
+def peer_gather(nbytes: int, device, group=None):
+    """The ``PeerAllGather`` of ``nbytes`` per rank for ``group`` on ``device``,
+    made on first use (a collective: every rank reaches it at the same call),
+    or ``None`` where it does not apply: no NCCL group of two or more ranks, or
+    ``DWA_PEER_GATHER=0`` (then the callers use NCCL's all-gather)."""
+    import os
+    import torch.distributed as dist
+    if os.environ.get("DWA_PEER_GATHER", "1") == "0" or nbytes % 16:
+        return None
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_backend(group) != "nccl":
+        return None
+    if dist.get_world_size(group) < 2:
+        return None
+    key = (id(group), int(nbytes), torch.device(device).index)
+    pg = _peer_gathers.get(key)
+    if pg is None:
+        from .peer import PeerAllGather
+        pg = _peer_gathers[key] = PeerAllGather(nbytes, device, group)
+    return pg
+
+
 def gather_summaries(summary: torch.Tensor, group=None) -> torch.Tensor:
     """All-gather every rank's ``[B, 2k+3]`` summary into ``[P, B, 2k+3]`` (rank
-    order).  One collective; with no process group, the summary alone."""
+    order).  One exchange: through peer-mapped buffers on an NCCL group
+    (``peer_gather``), else one NCCL / gloo all-gather; with no process group,
+    the summary alone."""
     import torch.distributed as dist
     if group is None and not (dist.is_available() and dist.is_initialized()):
         return summary.unsqueeze(0)
     world = dist.get_world_size(group)
     if world == 1:
         return summary.unsqueeze(0)
+    summary = summary.contiguous()
+    pg = peer_gather(summary.numel() * summary.element_size(), summary.device, group)
+    if pg is not None:
+        return pg(summary)
     out = torch.empty((world,) + tuple(summary.shape), dtype=summary.dtype, device=summary.device)
     if dist.get_backend(group) == "nccl":
-        dist.all_gather_into_tensor(out, summary.contiguous(), group=group)
+        dist.all_gather_into_tensor(out, summary, group=group)
     else:
-        dist.all_gather(list(out.unbind(0)), summary.contiguous(), group=group)
+        dist.all_gather(list(out.unbind(0)), summary, group=group)
     return out
 
 

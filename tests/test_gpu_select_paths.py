@@ -10,7 +10,8 @@ sizes the golden-vector cases do not reach, against the oracle in float64:
 * 6200 lists: more list keys than shared memory holds, so normalisation,
   coarse scores and top-m run as three kernels; top-k 128;
 * 15 probes of 8000-row lists: 120000 candidates, more than a cluster
-  stages, so one block per query selects them from global memory.
+  stages at once, so each CTA takes its share in two passes and carries its
+  running winners from the first into the second.
 
 Each case runs with and without soft_full (selection from the full pass and
 from the fine pass).  Indices equal the oracle's (seed 40 leaves a gap above

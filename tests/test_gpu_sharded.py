@@ -398,3 +398,71 @@ def test_emulated_vjp_with_empty_rank_and_alphas_only():
     torch.cuda.synchronize()
     for name in ("g_z", "g_W_Q", "g_aspect_weights"):
         assert_close(got[name].cpu().numpy(), ref[name].cpu().numpy(), TOL, name=name)
+
+
+def _allgather_rank(rank, world, port, out_dir):
+    """``PeerAllGather`` against NCCL's all-gather on the same data: eager calls
+    back to back (the two buffer halves alternate), then calls captured in a
+    CUDA graph and replayed with new inputs."""
+    import torch.distributed as dist
+    from datetime import timedelta
+    from matrix_b200.peer import PeerAllGather
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=dev)
+    pg = None
+    try:
+        shape = (7, 131)                       # a summary's shape: 7 queries, top-k 64
+        pg = PeerAllGather(7 * 131 * 4, dev)
+        g = torch.Generator(device=dev).manual_seed(100 + rank)
+        ok = []
+        for _ in range(5):
+            src = torch.randn(shape, generator=g, device=dev)
+            got = pg(src)
+            ref = torch.empty((world,) + shape, device=dev)
+            dist.all_gather_into_tensor(ref, src)
+            ok.append(bool(torch.equal(got, ref)))
+        src = torch.empty(shape, device=dev)
+        out1 = torch.empty((world,) + shape, device=dev)
+        out2 = torch.empty((world,) + shape, device=dev)
+        src.normal_(generator=g)
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            pg(src, out1)                       # warm-up outside the graph
+            torch.cuda.synchronize(dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s):
+                pg(src, out1)
+                pg(src * 2, out2)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        for rep in range(3):
+            src.normal_(generator=g)
+            graph.replay()
+            ref = torch.empty((world,) + shape, device=dev)
+            dist.all_gather_into_tensor(ref, src)
+            ok.append(bool(torch.equal(out1, ref)) and bool(torch.equal(out2, ref * 2)))
+        torch.cuda.synchronize(dev)
+        del graph
+        ok.append(pg.status() == 0)
+        np.save(os.path.join(out_dir, f"ag{rank}.npy"), np.array(ok))
+    finally:
+        if pg is not None:
+            pg.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_two_ranks_peer_allgather_equals_nccl(tmp_path):
+    import torch.multiprocessing as mp
+    world = 2
+    mp.start_processes(_allgather_rank, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    for rank in range(world):
+        ok = np.load(tmp_path / f"ag{rank}.npy")
+        assert ok.all(), f"rank {rank}: {ok}"
