@@ -416,8 +416,8 @@ def _allgather_rank(rank, world, port, out_dir):
                             device_id=dev)
     pg = None
     try:
-        shape = (7, 131)                       # a summary's shape: 7 queries, top-k 64
-        pg = PeerAllGather(7 * 131 * 4, dev)
+        shape = (8, 131)                       # a summary's shape: 8 queries, top-k 64
+        pg = PeerAllGather(8 * 131 * 4, dev)
         g = torch.Generator(device=dev).manual_seed(100 + rank)
         ok = []
         for _ in range(5):
