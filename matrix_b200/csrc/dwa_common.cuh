@@ -240,6 +240,10 @@ __global__ void __launch_bounds__(1024) column_sum_kernel(const T* __restrict__ 
 // fp32), adds its 16 warp partials in warp order, and cluster rank 0 adds
 // the split CTAs' sums in rank order out of their shared memory: deterministic
 // for a given split.  d % 8 == 0 and a 16-byte aligned x required.
+namespace tc {
+int sm_count();   // streaming multiprocessors of the current device (abi.cu)
+}
+
 template <class T> constexpr int column_sum8_rows() { return sizeof(T) == 2 ? 8 : 4; }
 
 template <class T>
@@ -312,16 +316,19 @@ __global__ void __launch_bounds__(512, 2) column_sum8_kernel(const T* __restrict
     }
 }
 
-// Launch of column_sum8_kernel over x [B, T, d]: one round of loads (16 warps x
-// U rows) per CTA where T allows, at most 8 CTAs (one cluster) per (column
-// block, b); short CTAs finish sooner than long ones saturate the memory
-// system, so the split is as wide as it goes.  At two 512-thread CTAs per SM a
-// thread has 64 registers: eight raw bf16 rows (32 registers) fit, eight fp32
-// rows would spill.
+// Launch of column_sum8_kernel over x [B, T, d]: at most 8 CTAs (one cluster)
+// per (column block, b), at least one round of loads (16 warps x U rows) each,
+// and no more CTAs than one wave at two per SM (measured on B 16 x T 1024 x
+// d 2048 bf16: 22 us with two CTAs per column block, 31 us with eight).  At
+// two 512-thread CTAs per SM a thread has 64 registers: eight raw bf16 rows
+// (32 registers) fit, eight fp32 rows would spill.
 template <class T>
 inline cudaError_t launch_column_sum8(cudaStream_t st, const T* x, int B, int T_, int d, int mean, float* out) {
     const int rows = 16 * column_sum8_rows<T>();
     int split = (T_ + rows - 1) / rows;
+    const int units = B * ((d + 255) / 256);
+    const int wave = 2 * tc::sm_count() / (units > 0 ? units : 1);
+    if (split > wave) split = wave;
     split = split < 1 ? 1 : split > 8 ? 8 : split;
     return launch_pdl_cluster(column_sum8_kernel<T>, dim3((d + 255) / 256, B, split), dim3(512), 0, st,
                               dim3(1, 1, split), x, T_, d, mean, out);
