@@ -336,7 +336,7 @@ DWA_API int dwa_retrieve_bwd_finish(void* stream, const DwaRetrieveDims* dims, i
  *     shard that holds it (plain 16-byte loads, NVLink for peers' rows); rows
  *     outside [row_lo[0], row_lo[world]) set DWA_STATUS_BAD_ROW_INDEX in the
  *     workspace's status word and come out as zeros.  D * element size must be
- *     a multiple of 16 bytes.
+ *     a multiple of 16 bytes; n <= 65535 per call.
  * ------------------------------------------------------------------------- */
 typedef struct DwaPoolShards {
     int32_t world;               /* <= 16 */

@@ -41,37 +41,45 @@ static PFN_addr_range addr_range_fn() {
     return fn;
 }
 
-// One CTA per gathered row: the owner is the last shard whose first row is
-// <= the global row; 16-byte loads, four in flight per thread.
-__global__ void __launch_bounds__(256) gather_rows_kernel(GatherShards sh, const int32_t* __restrict__ idx,
-                                                          char* __restrict__ out, uint32_t* status) {
+// One CTA per (16 KB chunk, gathered row): the owner is the last shard whose
+// first row is <= the global row; 16-byte loads, four in flight per thread,
+// so each CTA makes one round trip (over NVLink for a peer's row) and the
+// chunks of a row are fetched at once.
+constexpr int kGatherThreads = 256, kGatherUnroll = 4;
+constexpr int64_t kGatherChunkVecs = kGatherThreads * kGatherUnroll;
+
+__global__ void __launch_bounds__(kGatherThreads) gather_rows_kernel(GatherShards sh, const int32_t* __restrict__ idx,
+                                                                     char* __restrict__ out, uint32_t* status) {
     pdl_enter();
-    const int i = blockIdx.x;
+    const int i = blockIdx.y;
     const int64_t r = idx[i];
     const int64_t nvec = sh.row_bytes / 16;
+    const int64_t v0 = static_cast<int64_t>(blockIdx.x) * kGatherChunkVecs + threadIdx.x;
     uint4* dst = reinterpret_cast<uint4*>(out + static_cast<int64_t>(i) * sh.row_bytes);
     int p = -1;
     if (r >= sh.row_lo[0] && r < sh.row_lo[sh.world])
         for (int q = 0; q < sh.world; ++q)
             if (r >= sh.row_lo[q] && r < sh.row_lo[q + 1]) p = q;
     if (p < 0) {
-        if (threadIdx.x == 0) raise_status(status, DWA_STATUS_BAD_ROW_INDEX);
-        for (int64_t v = threadIdx.x; v < nvec; v += blockDim.x) dst[v] = make_uint4(0, 0, 0, 0);
+        if (threadIdx.x == 0 && blockIdx.x == 0) raise_status(status, DWA_STATUS_BAD_ROW_INDEX);
+#pragma unroll
+        for (int u = 0; u < kGatherUnroll; ++u) {
+            const int64_t v = v0 + u * kGatherThreads;
+            if (v < nvec) dst[v] = make_uint4(0, 0, 0, 0);
+        }
         return;
     }
     const uint4* src = reinterpret_cast<const uint4*>(sh.base[p] + (r - sh.row_lo[p]) * sh.row_bytes);
-    for (int64_t v0 = threadIdx.x; v0 < nvec; v0 += 4 * blockDim.x) {
-        uint4 t[4];
+    uint4 t[kGatherUnroll];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int64_t v = v0 + u * blockDim.x;
-            if (v < nvec) t[u] = src[v];
-        }
+    for (int u = 0; u < kGatherUnroll; ++u) {
+        const int64_t v = v0 + u * kGatherThreads;
+        if (v < nvec) t[u] = src[v];
+    }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int64_t v = v0 + u * blockDim.x;
-            if (v < nvec) dst[v] = t[u];
-        }
+    for (int u = 0; u < kGatherUnroll; ++u) {
+        const int64_t v = v0 + u * kGatherThreads;
+        if (v < nvec) dst[v] = t[u];
     }
 }
 
@@ -138,7 +146,10 @@ extern "C" int dwa_gather_rows(void* stream, int n, int64_t D, int dtype, const 
     }
     if (n == 0) return DWA_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    DWA_TIMED("gather_rows", st, launch_pdl(gather_rows_kernel, n, 256, 0, st, sh, indices, static_cast<char*>(out),
+    if (n > 65535) return fail(DWA_ERR_UNSUPPORTED, "dwa_gather_rows: at most 65535 rows per call");
+    const int64_t chunks = (sh.row_bytes / 16 + kGatherChunkVecs - 1) / kGatherChunkVecs;
+    DWA_TIMED("gather_rows", st, launch_pdl(gather_rows_kernel, dim3(static_cast<unsigned>(chunks), n),
+                                            kGatherThreads, 0, st, sh, indices, static_cast<char*>(out),
                                             static_cast<uint32_t*>(workspace)));
     DWA_LAUNCH_CHECK("gather_rows_kernel");
     ++g_launches_total;
