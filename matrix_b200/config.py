@@ -104,9 +104,10 @@ WORKLOADS: dict[str, Workload] = {
                              note="ncu case: key cache 134 MB (> L2), pool 2.3 GB; small shapes otherwise"),
     "profile_scan16": Workload("profile_scan16", _cfg(512, 131072, 256, 8, 32, "bfloat16"), 16, 256, False,
                                note="ncu case: the 16-query key scan over a 134 MB key cache (> L2), forward"),
-    "profile_gemm2k": Workload("profile_gemm2k", _cfg(2048, 16384, 16, 8, 64, "bfloat16"), 4, 1024, False,
+    "profile_gemm2k": Workload("profile_gemm2k", _cfg(2048, 16384, 16, 8, 64, "bfloat16"), 8, 1024, False,
                                note="ncu case: the medium workload's assembly GEMM shapes (d 2048, top-k 64, "
-                                    "seq 1024) for 4 sequences on a 1.1 GB pool"),
+                                    "seq 1024) for 8 sequences on a 1.1 GB pool (the W GEMM's grid is multi-wave "
+                                    "enough for the persistent kernel, as on the medium batch)"),
     "profile_gemm": Workload("profile_gemm", _cfg(1024, 16384, 32, 8, 32, "bfloat16"), 8, 512, True,
                              note="ncu case: the small workload's GEMM shapes with a 0.57 GB pool"),
 }

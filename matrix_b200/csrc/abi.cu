@@ -142,6 +142,15 @@ int sm_count() {
     return cache[dev];
 }
 
+// DWA_GEMM=classic or DWA_GEMM=single keeps GEMMs off the CTA-pair kernel.
+bool pair_gemm() {
+    static const bool on = [] {
+        const char* v = std::getenv("DWA_GEMM");
+        return !(v && (std::strcmp(v, "classic") == 0 || std::strcmp(v, "single") == 0));
+    }();
+    return on;
+}
+
 // DWA_GEMM=classic selects the one-tile-per-CTA GEMM instead of the persistent one.
 bool persistent_gemm() {
     static const bool on = [] {

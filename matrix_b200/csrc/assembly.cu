@@ -32,6 +32,7 @@
 #include "epilogue.cuh"
 #include "simt_gemm.cuh"
 #include "tc_gemm.cuh"
+#include "tc_gemm_pair.cuh"
 
 namespace dwa {
 
@@ -759,6 +760,16 @@ static int gemm(const char* name, const void* a, int64_t lda, int64_t bsa, const
         // waves on: below that one tile per CTA is as fast
         const bool pers = tc::persistent_gemm() && ctas256 > tc::sm_count() &&
                           (K >= 1024 || ctas256 >= 4 * static_cast<int64_t>(tc::sm_count()));
+        // long-K multi-wave GEMMs (the apply product) on CTA pairs: 256-row tiles
+        // whose two CTAs stage half of B each
+        if (pers && K >= 1024 && tc::pair_gemm() && N >= 256 && M >= 256 && tc::tc_operand_ok(A, M, K, 128) &&
+            tc::tc_operand_ok(B, N, K, 128)) {
+            ++g_launches_tc;
+            prof_begin(name, st);
+            const int rc = tc::launch_gemm_bf16_pair<256, 6, A_MN, B_MN>(A, B, M, N, K, batch, epi, status, st);
+            prof_end(name, st);
+            return rc;
+        }
         if (N >= 256 && ctas256 >= 120 && tc::tc_operand_ok(A, M, K, 128) &&
             tc::tc_operand_ok(B, N, K, 256)) {
             ++g_launches_tc;

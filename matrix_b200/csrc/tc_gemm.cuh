@@ -715,6 +715,7 @@ int launch_gemm_bf16(const Operand& A, const Operand& B, int M, int N, int K, in
 
 
 int sm_count();
+bool pair_gemm();   // CTA-pair kernel allowed (DWA_GEMM not classic / single)
 bool persistent_gemm();
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EW = kPersEpiWarps>
