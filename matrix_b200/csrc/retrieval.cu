@@ -878,25 +878,35 @@ __global__ void empty_summary_kernel(float* summary, int k) {
 }
 
 // soft_full[b, n] = exp(s*invT - M_b) * (1 / Z_b) in place (invT = 1/T, the
-// factor the full pass used for M and Z); 8 elements per thread.
+// factor the full pass used for M and Z); 8 elements per thread with 16-byte
+// accesses from the first 16-byte boundary of the row on (a rank's slice of
+// a row-sharded pool can have any row count, so rows need not start aligned),
+// and the at most 3 + 7 elements before and after that body one per thread.
 __global__ void __launch_bounds__(256) softmax_apply_kernel(float* __restrict__ sfull, int64_t N,
                                                             float invT, const float* __restrict__ stats) {
     pdl_enter();
     const int b = blockIdx.y;
     const float mx = stats[2 * b], rz = 1.f / stats[2 * b + 1];
     float* p = sfull + static_cast<int64_t>(b) * N;
+    const int64_t lead = ((16 - (reinterpret_cast<uintptr_t>(p) & 15)) & 15) >> 2;
+    const int64_t head = lead < N ? lead : N;
+    const int64_t body = (N - head) & ~static_cast<int64_t>(7);
     const int64_t i0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
-    if (i0 + 8 <= N && (reinterpret_cast<uintptr_t>(p) & 15) == 0 && (N & 3) == 0) {
-        float4 a = reinterpret_cast<const float4*>(p + i0)[0];
-        float4 c = reinterpret_cast<const float4*>(p + i0)[1];
+    if (i0 < body) {
+        float4* q = reinterpret_cast<float4*>(p + head + i0);
+        float4 a = q[0];
+        float4 c = q[1];
         a.x = expf(a.x * invT - mx) * rz; a.y = expf(a.y * invT - mx) * rz;
         a.z = expf(a.z * invT - mx) * rz; a.w = expf(a.w * invT - mx) * rz;
         c.x = expf(c.x * invT - mx) * rz; c.y = expf(c.y * invT - mx) * rz;
         c.z = expf(c.z * invT - mx) * rz; c.w = expf(c.w * invT - mx) * rz;
-        reinterpret_cast<float4*>(p + i0)[0] = a;
-        reinterpret_cast<float4*>(p + i0)[1] = c;
-    } else {
-        for (int64_t i = i0; i < i0 + 8 && i < N; ++i) p[i] = expf(p[i] * invT - mx) * rz;
+        q[0] = a;
+        q[1] = c;
+    }
+    if (blockIdx.x == 0 && threadIdx.x < 16) {
+        const int64_t t = threadIdx.x;
+        const int64_t i = t < head ? t : head + body + (t - head);
+        if (i < N) p[i] = expf(p[i] * invT - mx) * rz;
     }
 }
 
