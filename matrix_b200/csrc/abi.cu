@@ -174,6 +174,37 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
+// W_base [d_B, d_A] fp32, W [batch, d_B, d_A] fp32 (128-byte swizzle) and
+// W_act [batch, d_B, d_A] bf16 (64-byte swizzle), 32 x 32 boxes: the TMA maps
+// of the W GEMM's epilogue.
+bool make_w_epilogue_maps(CUtensorMap* wb, CUtensorMap* wo, CUtensorMap* wa, const float* W_base, float* W_out,
+                          void* W_act, int d_B, int d_A, int batch, std::string* why) {
+    auto enc = tensor_map_encoder();
+    if (!enc) {
+        *why = "cuTensorMapEncodeTiled unavailable";
+        return false;
+    }
+    const cuuint64_t A = static_cast<cuuint64_t>(d_A), Bd = static_cast<cuuint64_t>(d_B);
+    const cuuint32_t box[3] = {32, 32, 1}, es[3] = {1, 1, 1};
+    const cuuint64_t dims2[2] = {A, Bd}, str2[1] = {A * 4};
+    const cuuint64_t dims3[3] = {A, Bd, static_cast<cuuint64_t>(batch)};
+    const cuuint64_t strf[2] = {A * 4, A * Bd * 4}, strh[2] = {A * 2, A * Bd * 2};
+    CUresult r = enc(wb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(W_base), dims2, str2, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r == CUDA_SUCCESS)
+        r = enc(wo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, W_out, dims3, strf, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r == CUDA_SUCCESS)
+        r = enc(wa, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, W_act, dims3, strh, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        *why = "cuTensorMapEncodeTiled error " + std::to_string(static_cast<int>(r)) + " (W epilogue maps)";
+        return false;
+    }
+    return true;
+}
+
 bool tc_operand_ok(const Operand& op, int64_t mn_extent, int64_t k_extent, int box_mn) {
     const int64_t es = 2;
     if (reinterpret_cast<uintptr_t>(op.ptr) % 16 != 0) return false;

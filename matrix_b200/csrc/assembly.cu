@@ -33,6 +33,7 @@
 #include "simt_gemm.cuh"
 #include "tc_gemm.cuh"
 #include "tc_gemm_pair.cuh"
+#include "tc_gemm_w.cuh"
 
 namespace dwa {
 
@@ -849,6 +850,31 @@ static AsmWorkspace carve(void* base, const DwaAssembleDims& d, bool bwd) {
     return w;
 }
 
+// The W GEMM with the TMA epilogue (tc_gemm_w.cuh): bf16 activations, both
+// W (fp32) and W_act (bf16) written, 16-byte aligned buffers and rows, and a
+// grid of four waves or more (as for the persistent kernel); DWA_W_EPILOGUE=lsu
+// keeps the per-thread epilogue.
+template <class ACT>
+static bool w_tma_epilogue(const DwaAssembleDims& d, const float* W_base, const float* W_out, const void* W_act,
+                           const AsmWorkspace& w, int64_t kr) {
+    if constexpr (!std::is_same<ACT, __nv_bfloat16>::value) {
+        return false;
+    } else {
+        static const bool lsu = [] {
+            const char* v = std::getenv("DWA_W_EPILOGUE");
+            return v && std::strcmp(v, "lsu") == 0;
+        }();
+        if (lsu || force_simt() || !tc::persistent_gemm() || !W_base || !W_out || !W_act) return false;
+        if (d.d_A % 8 != 0 || d.d_A < 256 || kr < 64) return false;
+        const auto al16 = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+        if (!al16(W_base) || !al16(W_out) || !al16(W_act)) return false;
+        const int64_t ctas256 = static_cast<int64_t>((d.d_B + 127) / 128) * ((d.d_A + 255) / 256) * d.B;
+        if (ctas256 < 4 * static_cast<int64_t>(tc::sm_count())) return false;
+        const tc::Operand A{w.Ug, false, w.ldu, static_cast<int64_t>(d.d_B) * w.ldu}, B{w.Vs, true, d.d_A, kr * d.d_A};
+        return tc::tc_operand_ok(A, d.d_B, kr, 128) && tc::tc_operand_ok(B, d.d_A, kr, 256);
+    }
+}
+
 static bool vec_ok(const void* p, int64_t ld, size_t es) {
     return p == nullptr ||
            ((reinterpret_cast<uintptr_t>(p) % 16 == 0) && ((ld * static_cast<int64_t>(es)) % 16 == 0));
@@ -909,8 +935,17 @@ static int fwd_impl(cudaStream_t st, const DwaAssembleDims& d, const RowSrc& src
     ew.W_base = W_base; ew.W_out = W_out; ew.W_act = Wact_store; ew.d_B = d.d_B; ew.d_A = d.d_A;
     ew.vec = vec_ok(W_base, d.d_A, 4) && vec_ok(W_out, d.d_A, 4) && vec_ok(Wact_store, d.d_A, es);
     // A = Ug (M=d_B, K=kr, K-major); B = Vs (N=d_A, K=kr, MN-major)
-    rc = gemm<ACT, false, true>("gemm_W", w.Ug, w.ldu, static_cast<int64_t>(d.d_B) * w.ldu, w.Vs, d.d_A,
-                                kr * d.d_A, d.d_B, d.d_A, static_cast<int>(kr), d.B, ew, w.status, st);
+    if (w_tma_epilogue<ACT>(d, W_base, W_out, Wact_store, w, kr)) {
+        const tc::Operand A{w.Ug, false, w.ldu, static_cast<int64_t>(d.d_B) * w.ldu}, B{w.Vs, true, d.d_A, kr * d.d_A};
+        ++g_launches_tc;
+        prof_begin("gemm_W", st);
+        rc = tc::launch_gemm_w_tma(A, B, d.d_B, d.d_A, static_cast<int>(kr), d.B, W_base, W_out, Wact_store, w.status,
+                                   st);
+        prof_end("gemm_W", st);
+    } else {
+        rc = gemm<ACT, false, true>("gemm_W", w.Ug, w.ldu, static_cast<int64_t>(d.d_B) * w.ldu, w.Vs, d.d_A,
+                                    kr * d.d_A, d.d_B, d.d_A, static_cast<int>(kr), d.B, ew, w.status, st);
+    }
     if (rc) return rc;
     ++g_launches_total;
 

@@ -35,6 +35,11 @@ CASES = {
     "bf16_tc": (_cfg(256, 8, 16, 512, "bfloat16"), 3, 200),
     "bf16_small_like": (_cfg(1024, 8, 32, 512, "bfloat16"), 8, 256),
     "bf16_ragged": (_cfg(96, 8, 12, 600, "bfloat16", C=24, D=1640), 5, 40),
+    # 19 x 32 tiles of W (four waves and more on 148 SMs): the W GEMM whose
+    # epilogue moves W_base, W and W_act by TMA; square, then with partial
+    # 32 x 32 boxes at the edges (d 1000)
+    "bf16_w_tma": (_cfg(1024, 8, 8, 64, "bfloat16"), 19, 32),
+    "bf16_w_tma_edges": (_cfg(1000, 8, 8, 64, "bfloat16"), 19, 24),
 }
 
 
